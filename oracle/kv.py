@@ -1,0 +1,111 @@
+"""Q8 KV cache codec, gathers and decode attention core (oracle, test infrastructure).
+
+Restates ``kaggle/qwen38_tpu/attention_cache.py``:
+
+* ``quantize`` ``:15-23`` - per ``group`` channels, ``s = bf16(max|x| / 127)``,
+  codes ``clip(rint(x / (s == 0 ? 1 : s)), -127, 127)``;
+* ``write_quantized`` ``:26-43`` - codes row at ``[b, t]``, scales into the time-minor
+  plane ``[B * G, T]`` (``G = kv_heads * head_dim / group``), inactive rows unchanged;
+* ``gather_scale_plane`` ``:46-68`` with the index rule of the reference's own oracle
+  (``tests/test_qwen38_kv_gather.py:22-32``: negative indices wrap once, then clamp);
+* ``read_quantized`` ``:71-81`` - ``compute_cast(code * scale, dtype)``;
+* ``attention`` ``:159-170`` - GQA scores, BF16 boundaries, masked softmax, PV and the
+  sigmoid output gate.
+"""
+
+import numpy as np
+
+from .precision import bf16_round, divide, sigmoid, softmax
+
+
+def quantize(x, group):
+    """``attention_cache.py:15-23``: returns ``(int8 codes [..., D], BF16-valued scales [..., D/group])``."""
+    x = np.asarray(x, np.float32)
+    grouped = x.reshape(x.shape[:-1] + (-1, group))
+    rounded = bf16_round((np.max(np.abs(grouped), -1) / np.float32(127)).astype(np.float32))
+    divisor = np.where(rounded == 0, np.float32(1), rounded)
+    codes = np.clip(np.rint(divide(grouped, divisor[..., None])), -127, 127).astype(np.int8)
+    return codes.reshape(x.shape), rounded
+
+
+def write_quantized(cache, key, value, indices, active, kv_heads, head_dim, group=32):
+    """``attention_cache.py:26-43``, in place on NumPy arrays.
+
+    ``cache`` holds ``k``, ``v``: int8 ``[B, T, kv*hd]``; ``k_scale``, ``v_scale``:
+    BF16-valued FP32 ``[B * G, T]``. ``key``/``value``: ``[B, kv, hd]``.
+    """
+    batch = key.shape[0]
+    groups = kv_heads * (head_dim // group)
+    for name, token in (("k", key), ("v", value)):
+        codes, scale = quantize(token, group)
+        codes = codes.reshape(batch, -1)
+        scale = scale.reshape(batch, groups)
+        for b in range(batch):
+            if not active[b]:
+                continue
+            t = int(indices[b])
+            cache[name][b, t] = codes[b]
+            cache[name + "_scale"][b * groups : (b + 1) * groups, t] = scale[b]
+    return cache
+
+
+def _time_index(t, size):
+    """Index rule of ``test_qwen38_kv_gather.py:26-29``."""
+    t = int(t)
+    if t < 0:
+        t += size
+    return min(max(t, 0), size - 1)
+
+
+def gather_scale_plane(plane, indices, groups):
+    """``attention_cache.py:46-68`` -> ``[B, S, groups]``."""
+    plane = np.asarray(plane)
+    indices = np.asarray(indices)
+    if indices.ndim != 2 or plane.ndim != 2 or plane.shape[0] != indices.shape[0] * groups:
+        raise ValueError("Scale plane must be [batch * groups, time] for [batch, selected] indices")
+    out = np.empty(indices.shape + (groups,), plane.dtype)
+    for b in range(indices.shape[0]):
+        for s in range(indices.shape[1]):
+            t = _time_index(indices[b, s], plane.shape[1])
+            out[b, s] = plane[b * groups : (b + 1) * groups, t]
+    return out
+
+
+def read_quantized(codes, plane, indices, kv_heads, head_dim, group=32, dtype="bf16"):
+    """``attention_cache.py:71-81`` -> ``[B, S, kv, hd]`` (BF16-valued unless ``dtype='f32'``)."""
+    codes = np.asarray(codes)
+    indices = np.asarray(indices)
+    batch, selected = indices.shape
+    groups = kv_heads * (head_dim // group)
+    scale = gather_scale_plane(plane, indices, groups).astype(np.float32)
+    rows = np.empty((batch, selected, codes.shape[2]), np.float32)
+    for b in range(batch):
+        for s in range(selected):
+            rows[b, s] = codes[b, _time_index(indices[b, s], codes.shape[1])]
+    values = rows.reshape(batch, selected, groups, group) * scale[..., None]
+    values = values.reshape(batch, selected, kv_heads, head_dim).astype(np.float32)
+    return bf16_round(values) if dtype == "bf16" else values
+
+
+def attention(q, keys, values, mask, gate=None):
+    """Decode attention core, ``attention_cache.py:159-170``.
+
+    ``q``: BF16-valued ``[B, hq, hd]``; ``keys``/``values``: BF16-valued
+    ``[B, S, kv, hd]``; ``mask``: bool ``[B, S]``; ``gate``: optional ``[B, hq, hd]``.
+    Returns BF16-valued ``[B, hq, hd]`` (before the output projection).
+    """
+    batch, hq, hd = q.shape
+    kv = keys.shape[2]
+    r = hq // kv
+    qg = q.reshape(batch, kv, r, hd).astype(np.float64)
+    raw = np.einsum("bkrd,btkd->bkrt", qg, keys.astype(np.float64)).astype(np.float32)
+    raw = bf16_round(raw)
+    score = bf16_round((raw / np.float32(np.sqrt(hd))).astype(np.float32))
+    score = np.where(mask[:, None, None, :], score, np.float32(-np.inf)).astype(np.float32)
+    with np.errstate(invalid="ignore"):
+        prob = bf16_round(softmax(score, axis=-1))
+    out = np.einsum("bkrt,btkd->bkrd", prob.astype(np.float64), values.astype(np.float64))
+    out = bf16_round(out.astype(np.float32)).reshape(batch, hq, hd)
+    if gate is not None:
+        out = bf16_round((out * bf16_round(sigmoid(gate))).astype(np.float32))
+    return out
