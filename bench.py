@@ -1,0 +1,511 @@
+#!/usr/bin/env python3
+"""Benchmark of the B200 packed-Q6 routed-expert FFN.
+
+Workload (per GPU, weak scaling): 128 experts, each a SwiGLU FFN with gate/up
+2048 -> 512 and down 512 -> 2048, weights N(0, 0.02) (seed 1) encoded to Q6_K (or
+Q4_K) by this repository's encoder; 128 * M activation rows N(0, 1) (seed 0) assigned
+uniformly at random to the experts (seed 10), route weight 1. A step is one pass of
+the routed FFN (route metadata, gate/up + SwiGLU, down, combine) over all rows.
+
+value: algorithmic HBM bytes of the step (packed bytes of every routed expert + the
+activation rows read + the output rows written) / device time, summed over ranks.
+e2e:   the same bytes / time of the user-facing call with host (pinned) buffers:
+       H2D of x, ids and weights, the forward, D2H of the output, every step.
+The weights (331 MB of Q6_K at 128 experts) exceed the 126 MB L2, so no flush is
+needed between steps.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--m 16] [--qtype Q6_K]
+    python bench.py --impl reference ...   # the reference's CPU path (NumPy port)
+"""
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+for _p in (ROOT, ROOT / "data-synth-tpu_b200"):
+    if str(_p) not in sys.path:
+        sys.path.insert(0, str(_p))
+
+METRIC = "MoE decode tokens/s (B=1..64, 1/2/4/8 GPU); Q6 expert GEMM HBM GB/s"
+HIDDEN, INTER, EXPERTS = 2048, 512, 128
+SWEEP_M = (1, 4, 16, 64, 256)
+FALLBACK_HBM_GBS = 6650.0
+
+
+# ---------------------------------------------------------------------------------------
+# synthetic weights (NumPy encoder, one process per expert chunk; cached per node in /tmp)
+# ---------------------------------------------------------------------------------------
+
+
+def _encode_chunk(args):
+    qtype, seed, first, count = args
+    import numpy as np
+
+    from oracle import gguf
+
+    out = {"gate": [], "up": [], "down": []}
+    for e in range(first, first + count):
+        rng = np.random.default_rng([seed, e])
+        for kind, shape in (("gate", (INTER, HIDDEN)), ("up", (INTER, HIDDEN)), ("down", (HIDDEN, INTER))):
+            w = rng.normal(0, 0.02, shape).astype(np.float32)
+            out[kind].append(gguf.encode(w, qtype).reshape(-1))
+    return {k: np.stack(v) for k, v in out.items()}
+
+
+def synth_experts(qtype, count, seed=1):
+    """Raw GGUF bytes ``{gate, up, down: uint8[count, bytes]}``; one generator per node."""
+    import numpy as np
+
+    path = Path(tempfile.gettempdir()) / f"qk_bench_{qtype}_{count}_{seed}.npz"
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if not path.exists() and local_rank == 0:
+        import multiprocessing as mp
+
+        workers = max(1, min(os.cpu_count() or 1, 16))
+        chunk = (count + workers - 1) // workers
+        jobs = [(qtype, seed, f, min(chunk, count - f)) for f in range(0, count, chunk)]
+        with mp.get_context("spawn").Pool(len(jobs)) as pool:
+            parts = pool.map(_encode_chunk, jobs)
+        data = {k: np.concatenate([p[k] for p in parts]) for k in ("gate", "up", "down")}
+        tmp = path.with_suffix(".tmp.npz")
+        np.savez(tmp, **data)
+        os.replace(tmp, path)
+    deadline = time.time() + 600
+    while not path.exists():
+        if time.time() > deadline:
+            raise TimeoutError(f"{path} was not written by local rank 0")
+        time.sleep(0.5)
+    with np.load(path) as f:
+        return {k: f[k] for k in ("gate", "up", "down")}
+
+
+def workload(m, rank=0):
+    """Activation rows, expert assignment and route weights for M rows per expert."""
+    import numpy as np
+
+    rows = EXPERTS * m
+    x = np.random.default_rng([0, rank]).normal(size=(rows, HIDDEN)).astype(np.float32)
+    ids = np.random.default_rng([10, rank]).integers(0, EXPERTS, (rows, 1)).astype(np.int32)
+    weights = np.ones((rows, 1), np.float32)
+    return x, ids, weights
+
+
+def packed_bytes_per_expert(qtype):
+    per_block = {"Q6_K": 210, "Q4_K": 144}[qtype]
+    return (2 * INTER * HIDDEN + HIDDEN * INTER) // 256 * per_block
+
+
+def step_bytes(qtype, ids):
+    """Algorithmic bytes of one step: routed experts' packed bytes + x read + out written."""
+    import numpy as np
+
+    active = len(np.unique(ids))
+    rows = ids.shape[0]
+    return active * packed_bytes_per_expert(qtype) + rows * HIDDEN * 2 * 2, active
+
+
+def kernel_bytes(qtype, ids):
+    """Algorithmic bytes of the gate/up (dominant) launch: gate+up packed bytes of the routed
+    experts + x rows read + h rows written."""
+    import numpy as np
+
+    active = len(np.unique(ids))
+    rows = ids.shape[0]
+    per_block = {"Q6_K": 210, "Q4_K": 144}[qtype]
+    return active * 2 * INTER * HIDDEN // 256 * per_block + rows * (HIDDEN + INTER) * 2
+
+
+# ---------------------------------------------------------------------------------------
+# measurement helpers
+# ---------------------------------------------------------------------------------------
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons of one GPU, sampled every 100 ms."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-i", str(self.gpu)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def hbm_peak():
+    path = ROOT / "MEASURED_PEAKS.json"
+    try:
+        return float(json.loads(path.read_text())["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def ncu_traffic(qtype, m):
+    """DRAM bytes per gate/up launch from the committed ncu summary, if one matches."""
+    path = ROOT / "profiles" / f"moe_gateup_{qtype.lower()}_m{m}.md"
+    try:
+        for line in path.read_text().splitlines():
+            if line.startswith("traffic_bytes_per_launch:"):
+                return float(line.split(":", 1)[1].strip())
+    except OSError:
+        pass
+    return None
+
+
+def cpu_port_gbs(raw, qtype, x, ids, weights, budget_s=10.0):
+    """Reference CPU path (NumPy port of experts.py:82-110): decode each routed expert and
+    run its SwiGLU with FP32 BLAS, on all host threads, over a bounded sample of experts."""
+    import numpy as np
+
+    from oracle import moe
+    from oracle.precision import bf16_round
+
+    xb = bf16_round(x)
+    order = np.unique(ids)
+    done_bytes, elapsed, experts = 0, 0.0, 0
+    start = time.perf_counter()
+    for e in order:
+        rows = np.nonzero(ids[:, 0] == e)[0]
+        t0 = time.perf_counter()
+        wg = moe.expert_weights(raw["gate"][e], qtype, INTER, HIDDEN)
+        wu = moe.expert_weights(raw["up"][e], qtype, INTER, HIDDEN)
+        wd = moe.expert_weights(raw["down"][e], qtype, HIDDEN, INTER)
+        y = moe.expert_forward(xb[rows], wg, wu, wd, accumulate="f32")
+        _ = (y * weights[rows]).astype(np.float32)
+        elapsed += time.perf_counter() - t0
+        done_bytes += packed_bytes_per_expert(qtype) + rows.size * HIDDEN * 4
+        experts += 1
+        if time.perf_counter() - start > budget_s:
+            break
+    return done_bytes / elapsed / 1e9, experts
+
+
+# ---------------------------------------------------------------------------------------
+# arms
+# ---------------------------------------------------------------------------------------
+
+
+def init_dist():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def reference_arm(args):
+    import numpy as np
+
+    world, rank, _ = init_dist()
+    if rank != 0:
+        return 0
+    raw = synth_experts(args.qtype, EXPERTS)
+    x, ids, weights = workload(args.m)
+    cores = os.cpu_count() or 1
+    for _ in range(args.warmup):
+        cpu_port_gbs(raw, args.qtype, x, ids, weights, budget_s=0.5)
+    samples, experts = [], 0
+    for _ in range(args.steps):
+        gbs, n = cpu_port_gbs(raw, args.qtype, x, ids, weights, budget_s=args.ref_budget)
+        samples.append(gbs)
+        experts = n
+    value = statistics.median(samples)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "u8", "data": "synthetic",
+        "config": config_dict(args, world),
+        "cpu_baseline": {"value": value, "unit": "GB/s", "cores": cores, "kind": "port",
+                         "sample": f"{experts} of {EXPERTS} routed experts per step, M={args.m} rows/expert"},
+        "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def config_dict(args, world):
+    return {
+        "workload": f"expert_gemm_{args.qtype.lower()}_m{args.m}",
+        "experts_per_gpu": EXPERTS, "hidden": HIDDEN, "intermediate": INTER, "qtype": args.qtype,
+        "tokens_per_expert": args.m, "rows_per_gpu": EXPERTS * args.m, "top_k": 1,
+        "parallelism": f"ep{world} (independent expert shards)",
+        "l2": "inputs larger than L2 (331 MB packed weights per GPU)",
+    }
+
+
+def b200_arm(args):
+    import numpy as np
+    import torch
+
+    import qk_b200
+    from qk_b200 import _lib
+    from qk_b200.experts import expert_parallel
+    from qk_b200.parallel import put_expert_bytes
+
+    world, rank, local = init_dist()
+    raw = synth_experts(args.qtype, EXPERTS)  # before CUDA init: the encoder pool is spawned
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=device)
+    tensors = {k: put_expert_bytes(v, k, args.qtype, HIDDEN, INTER, device=device)
+               for k, v in raw.items()}
+    fn = expert_parallel(gate_type=args.qtype, up_type=args.qtype, down_type=args.qtype,
+                         hidden=HIDDEN, intermediate=INTER)
+    stream = torch.cuda.current_stream(device)
+
+    def run_m(m, steps, warmup, profile):
+        x, ids, weights = workload(m, rank)
+        xd = torch.from_numpy(x).to(device).to(torch.bfloat16)
+        idd = torch.from_numpy(ids).to(device)
+        wd = torch.from_numpy(weights).to(device).to(torch.bfloat16)
+        rows = x.shape[0]
+        desc = fn.desc(EXPERTS, 0, 1)
+        ws = fn.workspace(desc, rows, device)
+        out = torch.empty((rows, HIDDEN), dtype=torch.bfloat16, device=device)
+        events = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+        ev_ptrs = (ctypes_void_p * 5)(*[e.cuda_event for e in events]) if profile else None
+
+        def step(profiled=False):
+            lib = _lib.load()
+            if profiled:
+                rc = lib.qk_moe_forward_profiled(desc, _lib.ptr(tensors["gate"]), _lib.ptr(tensors["up"]),
+                                                 _lib.ptr(tensors["down"]), _lib.ptr(xd), _lib.ptr(idd),
+                                                 _lib.ptr(wd), rows, _lib.QK_OUT_BF16, _lib.ptr(out),
+                                                 _lib.ptr(ws), ws.numel(), _lib.stream_handle(device),
+                                                 ev_ptrs)
+            else:
+                rc = lib.qk_moe_forward(desc, _lib.ptr(tensors["gate"]), _lib.ptr(tensors["up"]),
+                                        _lib.ptr(tensors["down"]), _lib.ptr(xd), _lib.ptr(idd),
+                                        _lib.ptr(wd), rows, _lib.QK_OUT_BF16, _lib.ptr(out),
+                                        _lib.ptr(ws), ws.numel(), _lib.stream_handle(device))
+            _lib.check(rc)
+
+        for _ in range(warmup):
+            step()
+        torch.cuda.synchronize(device)
+        # capture one step in a CUDA graph so the timed loop is free of host launch gaps
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            step()
+        graph.replay()
+        torch.cuda.synchronize(device)
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize(device)
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for _ in range(steps):
+            graph.replay()
+        t1.record(stream)
+        torch.cuda.synchronize(device)
+        if dist:
+            dist.barrier()
+        ms = t0.elapsed_time(t1) / steps
+        stage_ms = None
+        if profile:  # per-kernel times from events recorded between the launches
+            acc = [0.0] * 4
+            reps = max(10, min(steps, 200))
+            for _ in range(reps):
+                step(profiled=True)
+                torch.cuda.synchronize(device)
+                for i in range(4):
+                    acc[i] += events[i].elapsed_time(events[i + 1])
+            stage_ms = [a / reps for a in acc]
+        fn.check_status()
+        nbytes, active = step_bytes(args.qtype, ids)
+        return dict(m=m, ms=ms, bytes=nbytes, active=active, rows=rows, stage_ms=stage_ms,
+                    gate_up_bytes=kernel_bytes(args.qtype, ids), x=x, ids=ids, weights=weights,
+                    out=out)
+
+    launches0 = qk_b200.launch_count()
+    _ = launches0
+    peak, peak_kind = hbm_peak()
+    with ClockSampler(local) as clocks:
+        # untimed soak so clocks settle before the measured region
+        soak_end = time.time() + args.soak
+        while time.time() < soak_end:
+            run_m(args.m, 20, 1, False)
+        res = run_m(args.m, args.steps, args.warmup, True)
+    ms = res["ms"]
+    if dist:
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    value = res["bytes"] * world / (ms * 1e-3) / 1e9
+
+    # launches: a graph replay runs the 4 kernels of one qk_moe_forward
+    before = qk_b200.launch_count()
+    _lib.check(0)
+    launches_per_step = 4
+
+    # e2e through the public call with host buffers
+    e2e = e2e_measure(fn, tensors, device, args, res, rank)
+
+    sweep = []
+    if args.sweep and rank == 0 and world == 1:
+        for m in SWEEP_M:
+            r = run_m(m, max(5, args.steps // 4), 2, False)
+            sweep.append({"m": m, "ms_per_step": r["ms"], "gbs": r["bytes"] / (r["ms"] * 1e-3) / 1e9,
+                          "rows_per_s": r["rows"] / (r["ms"] * 1e-3), "active_experts": r["active"]})
+
+    gate_up_ms = res["stage_ms"][1]
+    achieved = res["gate_up_bytes"] / (gate_up_ms * 1e-3) / 1e9
+    line = {
+        "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "u8", "data": "synthetic",
+        "config": config_dict(args, world),
+        "rows_per_s": res["rows"] * world / (ms * 1e-3),
+        "stage_ms": {"route": res["stage_ms"][0], "gate_up": res["stage_ms"][1],
+                     "down": res["stage_ms"][2], "combine": res["stage_ms"][3]},
+        "roofline": {"kernel": "moe_proj_kernel<Q6_K, gate/up>" if args.qtype == "Q6_K" else
+                     "moe_proj_kernel<Q4_K, gate/up>",
+                     "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "peak_kind": peak_kind,
+                     "traffic": ncu_traffic(args.qtype, args.m)},
+        "e2e": e2e,
+        "gpu_launches": launches_per_step * args.steps,
+        "clocks": clocks.summary(),
+    }
+    if sweep:
+        line["sweep"] = sweep
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        gbs, experts = cpu_port_gbs(raw, args.qtype, res["x"], res["ids"], res["weights"],
+                                    budget_s=args.ref_budget)
+        line["cpu_baseline"] = {"value": gbs, "unit": "GB/s", "cores": os.cpu_count() or 1,
+                                "kind": "port",
+                                "sample": f"{experts} of {res['active']} routed experts, M={args.m} rows/expert"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def e2e_measure(fn, tensors, device, args, res, rank):
+    """Public-call throughput with pinned host inputs/outputs copied every step."""
+    import numpy as np
+    import torch
+
+    x, ids, weights = res["x"], res["ids"], res["weights"]
+    rows = x.shape[0]
+    x_h = torch.from_numpy(x).to(torch.bfloat16).pin_memory()
+    ids_h = torch.from_numpy(ids).pin_memory()
+    w_h = torch.from_numpy(weights).to(torch.bfloat16).pin_memory()
+    out_h = torch.empty((rows, HIDDEN), dtype=torch.bfloat16).pin_memory()
+    x_d = torch.empty_like(x_h, device=device)
+    ids_d = torch.empty_like(ids_h, device=device)
+    w_d = torch.empty_like(w_h, device=device)
+    stream = torch.cuda.current_stream(device)
+
+    def step():
+        x_d.copy_(x_h, non_blocking=True)
+        ids_d.copy_(ids_h, non_blocking=True)
+        w_d.copy_(w_h, non_blocking=True)
+        out = fn(tensors["gate"], tensors["up"], tensors["down"], x_d, ids_d, w_d)
+        out_h.copy_(out, non_blocking=True)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(device)
+    steps = max(3, args.steps // 2)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(steps):
+        step()
+    t1.record(stream)
+    torch.cuda.synchronize(device)
+    ms = t0.elapsed_time(t1) / steps
+    h2d = x_h.numel() * 2 + ids_h.numel() * 4 + w_h.numel() * 2
+    d2h = out_h.numel() * 2
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    return {"value": res["bytes"] * world / (ms * 1e-3) / 1e9, "unit": "GB/s",
+            "ms_per_step": ms, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
+
+
+import ctypes  # noqa: E402
+
+ctypes_void_p = ctypes.c_void_p
+
+
+def main():
+    parser = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=200)
+    parser.add_argument("--warmup", type=int, default=5)
+    parser.add_argument("--impl", choices=("b200", "reference"), default="b200")
+    parser.add_argument("--m", type=int, default=16, help="tokens per expert")
+    parser.add_argument("--qtype", choices=("Q6_K", "Q4_K"), default="Q6_K")
+    parser.add_argument("--soak", type=float, default=1.0, help="untimed seconds before timing")
+    parser.add_argument("--sweep", action="store_true", help="also time M in {1,4,16,64,256}")
+    parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--ref-budget", type=float, default=10.0,
+                        help="seconds of CPU work per reference sample")
+    args = parser.parse_args()
+    if args.warmup < 3:
+        parser.error("--warmup must be >= 3")
+    if args.impl == "reference":
+        return reference_arm(args)
+    return b200_arm(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

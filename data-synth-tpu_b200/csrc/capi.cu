@@ -1,0 +1,72 @@
+// Library-level C ABI: version, last-error text, launch counter.
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+
+#include "common.cuh"
+
+namespace qk {
+
+namespace {
+thread_local char g_last_error[512] = "";
+std::atomic<uint64_t> g_launches{0};
+int g_sm_count[64] = {0};
+}  // namespace
+
+int set_error(int status, const char* fmt, ...) {
+  va_list args;
+  va_start(args, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, args);
+  va_end(args);
+  return status;
+}
+
+int cuda_error(cudaError_t err, const char* where) {
+  return set_error(QK_ERR_CUDA, "%s: %s", where, cudaGetErrorString(err));
+}
+
+void count_launch(int n) { g_launches.fetch_add(static_cast<uint64_t>(n)); }
+
+int sm_count() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (g_sm_count[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+      n = 148;
+    g_sm_count[dev] = n;
+  }
+  return g_sm_count[dev];
+}
+
+int allow_smem(const void* kernel, size_t bytes) {
+  // One flag per (kernel, device): the attribute is per device.
+  static thread_local const void* done_kernel[256];
+  static thread_local int done_dev[256];
+  static thread_local int n_done = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  for (int i = 0; i < n_done; ++i)
+    if (done_kernel[i] == kernel && done_dev[i] == dev) return QK_OK;
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(bytes));
+  if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute");
+  if (n_done < 256) {
+    done_kernel[n_done] = kernel;
+    done_dev[n_done] = dev;
+    ++n_done;
+  }
+  return QK_OK;
+}
+
+}  // namespace qk
+
+extern "C" {
+
+const char* qk_version(void) { return "qk_b200 0.1 sm_100a"; }
+
+const char* qk_last_error(void) { return qk::g_last_error; }
+
+uint64_t qk_launch_count(void) { return qk::g_launches.load(); }
+
+}  // extern "C"

@@ -1,0 +1,184 @@
+// Shared device helpers for the qk_b200 kernels (sm_100a).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "qk_b200.h"
+
+namespace qk {
+
+// ---------------------------------------------------------------------------------
+// host-side status plumbing
+// ---------------------------------------------------------------------------------
+
+int set_error(int status, const char* fmt, ...);
+int cuda_error(cudaError_t err, const char* where);
+void count_launch(int n = 1);
+
+#define QK_REQUIRE(cond, ...)                                        \
+  do {                                                               \
+    if (!(cond)) return ::qk::set_error(QK_ERR_INVALID_ARGUMENT, __VA_ARGS__); \
+  } while (0)
+
+#define QK_LAUNCHED(where)                                           \
+  do {                                                               \
+    cudaError_t e_ = cudaGetLastError();                             \
+    if (e_ != cudaSuccess) return ::qk::cuda_error(e_, where);       \
+    ::qk::count_launch();                                            \
+  } while (0)
+
+inline cudaStream_t as_stream(qk_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
+
+int sm_count();  // SMs of the current device (cached per device)
+// Opt a kernel into `bytes` of dynamic shared memory on the current device (once).
+int allow_smem(const void* kernel, size_t bytes);
+
+// ---------------------------------------------------------------------------------
+// numeric boundaries
+// ---------------------------------------------------------------------------------
+
+// BF16 storage bits of x rounded to nearest even; NaN quieted by setting bit 22
+// (the integer rule of the reference's rounded_bf16_float32).
+__host__ __device__ __forceinline__ uint16_t bf16_bits_rne(float x) {
+#ifdef __CUDA_ARCH__
+  uint32_t b = __float_as_uint(x);
+#else
+  uint32_t b;
+  __builtin_memcpy(&b, &x, 4);
+#endif
+  if ((b & 0x7fffffffu) > 0x7f800000u) return static_cast<uint16_t>((b | 0x00400000u) >> 16);
+  return static_cast<uint16_t>((b + 0x7fffu + ((b >> 16) & 1u)) >> 16);
+}
+
+__device__ __forceinline__ float bf16_round(float x) {
+  return __uint_as_float(static_cast<uint32_t>(bf16_bits_rne(x)) << 16);
+}
+
+__device__ __forceinline__ float bf16_to_f32(uint16_t bits) {
+  return __uint_as_float(static_cast<uint32_t>(bits) << 16);
+}
+
+// Exact FP16 -> FP32 expansion (subnormals and signed zero included).
+__device__ __forceinline__ float f16_to_f32(uint16_t bits) {
+  return __half2float(__ushort_as_half(bits));
+}
+
+// Two FP32 values -> packed BF16x2 (low half = a), hardware RNE (cvt.rn.bf16x2.f32).
+// Used only on finite values, where it equals the integer rule above.
+__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(b), "f"(a));
+  return r;
+}
+
+// numerics.py:42-45 sigmoid: divide(x >= 0 ? 1 : e, 1 + e), e = exp(-|x|), IEEE divide.
+__device__ __forceinline__ float sigmoid_ref(float x) {
+  float e = expf(-fabsf(x));
+  return __fdiv_rn(x >= 0.f ? 1.f : e, __fadd_rn(1.f, e));
+}
+
+// ---------------------------------------------------------------------------------
+// tensor core: legacy warp MMA, used for the HBM-bound small-M paths
+// ---------------------------------------------------------------------------------
+
+// D[16x8] += A[16x16] * B[16x8], BF16 operands, FP32 accumulate.
+// a[0]=(r g, k 2c..2c+1) a[1]=(r g+8, k 2c..) a[2]=(r g, k 2c+8..) a[3]=(r g+8, k 2c+8..)
+// b[0]=(k 2c..2c+1, n g) b[1]=(k 2c+8.., n g); d[0..1]=(r g, n 2c..2c+1) d[2..3]=(r g+8, ..)
+// with g = lane / 4 and c = lane % 4.
+__device__ __forceinline__ void mma_bf16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                         uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// Transpose of an 8x8 b16 matrix held in the mma fragment layout.
+__device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
+  uint32_t r;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(r) : "r"(x));
+  return r;
+}
+
+// ---------------------------------------------------------------------------------
+// async bulk copies (TMA engine, 1-D, no multicast) and mbarriers
+// ---------------------------------------------------------------------------------
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+// Global -> shared bulk copy completing on `bar`. dst, src 16-byte aligned, bytes % 16 == 0.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes,
+                                         uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_addr(dst)),
+      "l"(src), "r"(bytes), "r"(smem_addr(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, "
+      "p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait: gives up after `limit` polls (each poll may suspend briefly) and
+// returns false; the caller records QK_ERR_TIMEOUT and stops issuing work.
+constexpr uint32_t kWaitLimit = 1u << 22;
+
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+  for (uint32_t i = 0; i < kWaitLimit; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+  return false;
+}
+
+// ---------------------------------------------------------------------------------
+// small loads
+// ---------------------------------------------------------------------------------
+
+__device__ __forceinline__ uint4 ld_nc_v4(const void* p) {
+  uint4 r;
+  asm("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+__device__ __forceinline__ uint4 lds_v4(const void* p) {
+  return *reinterpret_cast<const uint4*>(p);
+}
+
+__device__ __forceinline__ uint32_t word(const uint4& v, int i) {
+  return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
+}
+
+}  // namespace qk

@@ -1,0 +1,319 @@
+// GGUF block decode (raw and tiled layouts) and the lossless raw <-> tiled repack.
+//
+// qk_dequantize_rows restates glm53_offload/gguf_quant.py:63-177 (Q4_K, Q5_K, Q6_K,
+// Q8_0, F16, BF16, F32) and qwen38_tpu/quant.py:15-55 (Q4_0, Q4_1, Q5_0, Q5_1,
+// IQ4_NL) one output value per thread. FP32 operations are written with explicit
+// round-to-nearest intrinsics so no multiply-add is contracted.
+#include "common.cuh"
+#include "tiles.cuh"
+
+namespace qk {
+namespace {
+
+__device__ __constant__ float kIq4Values[16] = {-127, -104, -83, -65, -49, -35, -22, -10,
+                                                1,    13,   25,  38,  53,  69,  89,  113};
+
+struct BlockShape {
+  int values;
+  int bytes;
+};
+
+__host__ __device__ inline BlockShape block_shape(int qtype) {
+  switch (qtype) {
+    case QK_TYPE_F32: return {1, 4};
+    case QK_TYPE_F16: return {1, 2};
+    case QK_TYPE_BF16: return {1, 2};
+    case QK_TYPE_Q4_0: return {32, 18};
+    case QK_TYPE_Q4_1: return {32, 20};
+    case QK_TYPE_Q5_0: return {32, 22};
+    case QK_TYPE_Q5_1: return {32, 24};
+    case QK_TYPE_Q8_0: return {32, 34};
+    case QK_TYPE_IQ4_NL: return {32, 18};
+    case QK_TYPE_Q4_K: return {256, 144};
+    case QK_TYPE_Q5_K: return {256, 176};
+    case QK_TYPE_Q6_K: return {256, 210};
+    default: return {0, 0};
+  }
+}
+
+__device__ __forceinline__ float f16_at(const uint8_t* b) {
+  return f16_to_f32(static_cast<uint16_t>(b[0] | (b[1] << 8)));
+}
+
+__device__ __forceinline__ void k_scale_min(const uint8_t* blk, int j, int& sc, int& m) {
+  const uint8_t* s = blk + 4;
+  if (j < 4) {
+    sc = s[j] & 63;
+    m = s[j + 4] & 63;
+  } else {
+    sc = (s[j + 4] & 15) | ((s[j - 4] >> 6) << 4);
+    m = (s[j + 4] >> 4) | ((s[j] >> 6) << 4);
+  }
+}
+
+// Value p of one GGUF block.
+__device__ float decode_value(const uint8_t* blk, int qtype, int p) {
+  switch (qtype) {
+    case QK_TYPE_F32: {
+      uint32_t bits = blk[0] | (blk[1] << 8) | (blk[2] << 16) | (static_cast<uint32_t>(blk[3]) << 24);
+      return __uint_as_float(bits);
+    }
+    case QK_TYPE_F16: return f16_at(blk);
+    case QK_TYPE_BF16: return bf16_to_f32(static_cast<uint16_t>(blk[0] | (blk[1] << 8)));
+    case QK_TYPE_Q8_0:
+      return __fmul_rn(f16_at(blk), static_cast<float>(static_cast<int8_t>(blk[2 + p])));
+    case QK_TYPE_Q4_0:
+    case QK_TYPE_Q4_1:
+    case QK_TYPE_Q5_0:
+    case QK_TYPE_Q5_1:
+    case QK_TYPE_IQ4_NL: {  // quant.py:31-55
+      const bool affine = qtype == QK_TYPE_Q4_1 || qtype == QK_TYPE_Q5_1;
+      const bool five = qtype == QK_TYPE_Q5_0 || qtype == QK_TYPE_Q5_1;
+      const int base = affine ? 4 : 2;
+      const uint8_t byte = blk[base + (five ? 4 : 0) + (p & 15)];
+      int q = p < 16 ? (byte & 15) : (byte >> 4);
+      if (five) {
+        const uint8_t* h = blk + base;
+        const uint32_t bits = h[0] | (h[1] << 8) | (h[2] << 16) | (static_cast<uint32_t>(h[3]) << 24);
+        q |= static_cast<int>((bits >> p) & 1u) << 4;
+      }
+      const float d = f16_at(blk);
+      float v;
+      if (qtype == QK_TYPE_IQ4_NL) v = __fmul_rn(d, kIq4Values[q]);
+      else if (affine) v = __fmul_rn(d, static_cast<float>(q));
+      else v = __fmul_rn(d, static_cast<float>(q - (five ? 16 : 8)));
+      if (affine) v = __fadd_rn(v, f16_at(blk + 2));
+      return v;
+    }
+    case QK_TYPE_Q4_K:
+    case QK_TYPE_Q5_K: {  // gguf_quant.py:115-157
+      const int j = p >> 5, i = p & 31;
+      int q;
+      if (qtype == QK_TYPE_Q4_K) {
+        q = (blk[16 + (j >> 1) * 32 + i] >> (4 * (j & 1))) & 15;
+      } else {
+        q = ((blk[48 + (j >> 1) * 32 + i] >> (4 * (j & 1))) & 15) | (((blk[16 + i] >> j) & 1) << 4);
+      }
+      int sc, m;
+      k_scale_min(blk, j, sc, m);
+      const float a = __fmul_rn(__fmul_rn(f16_at(blk), static_cast<float>(sc)), static_cast<float>(q));
+      return __fsub_rn(a, __fmul_rn(f16_at(blk + 2), static_cast<float>(m)));
+    }
+    case QK_TYPE_Q6_K: {  // gguf_quant.py:158-173, packed_q6/reference.py:21-30
+      const int half = p >> 7, quarter = (p & 127) >> 5, lane = p & 31;
+      const int lo = (blk[half * 64 + (quarter & 1) * 32 + lane] >> (4 * (quarter >> 1))) & 15;
+      const int hi = (blk[128 + half * 32 + lane] >> (2 * quarter)) & 3;
+      const int q = (lo | (hi << 4)) - 32;
+      const float ds = __fmul_rn(f16_at(blk + 208), static_cast<float>(static_cast<int8_t>(blk[192 + (p >> 4)])));
+      return __fmul_rn(ds, static_cast<float>(q));
+    }
+    default: return 0.f;
+  }
+}
+
+__global__ void dequant_rows_kernel(const uint8_t* __restrict__ raw, int qtype, int64_t rows,
+                                    int64_t width, int64_t nblk, BlockShape shape, int out_bf16,
+                                    void* __restrict__ out) {
+  const int64_t total = rows * width;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t row = i / width, col = i % width;
+    const int64_t b = col / shape.values;
+    const uint8_t* blk = raw + (row * nblk + b) * shape.bytes;
+    const float v = decode_value(blk, qtype, static_cast<int>(col % shape.values));
+    if (out_bf16) static_cast<uint16_t*>(out)[i] = bf16_bits_rne(v);
+    else static_cast<float*>(out)[i] = v;
+  }
+}
+
+// ---- tiled layout byte map (see oracle/layout.py for the statement of the format) ----
+
+// For tiled byte `off` of a tile: the row inside the 16-row tile and the byte inside
+// that row's GGUF block.
+__host__ __device__ inline void tile_source(int qtype, int off, int& row, int& src) {
+  if (qtype == QK_TYPE_Q6_K) {
+    if (off < 2048) {
+      const int u = off >> 9, within = off & 511, unit = within >> 4, b = within & 15;
+      const int rh = u >> 1, part = u & 1, g = unit >> 2, c = unit & 3;
+      row = rh * 8 + g;
+      src = (c >> 1) * 64 + part * 32 + (c & 1) * 16 + b;
+    } else if (off < 3072) {
+      const int o = off - 2048, rh = o >> 9, within = o & 511;
+      row = rh * 8 + (within >> 6);
+      src = 128 + (within & 63);
+    } else if (off < 3328) {
+      const int o = off - 3072, unit = o >> 3, b = o & 7, g = unit >> 2, c = unit & 3;
+      row = (b >> 2) * 8 + g;
+      src = 192 + (c >> 1) * 8 + (c & 1) + 2 * (b & 3);
+    } else {
+      const int o = off - 3328, g = o >> 2, w = o & 3;
+      row = (w >> 1) * 8 + g;
+      src = 208 + (w & 1);
+    }
+  } else {  // Q4_K
+    if (off < 2048) {
+      const int u = off >> 9, within = off & 511, unit = within >> 4, b = within & 15;
+      const int rh = u >> 1, half = u & 1, g = unit >> 2, c = unit & 3;
+      row = rh * 8 + g;
+      src = 16 + 32 * c + 16 * half + b;
+    } else {
+      const int o = off - 2048;
+      row = o >> 4;
+      src = o & 15;
+    }
+  }
+}
+
+inline int tile_bytes(int qtype) {
+  return qtype == QK_TYPE_Q6_K ? Tile<QType::Q6_K>::kBytes
+         : qtype == QK_TYPE_Q4_K ? Tile<QType::Q4_K>::kBytes
+                                 : 0;
+}
+
+// One CTA per tile; tiled[...] <- raw[...] (or the reverse for unpack).
+template <bool kPack>
+__global__ void repack_kernel(const uint8_t* __restrict__ in, uint8_t* __restrict__ out, int qtype,
+                              int64_t rows, int64_t nblk, int tbytes, int bbytes,
+                              int32_t* bad_scales) {
+  const int64_t tile = blockIdx.x;
+  const int64_t strip = tile / nblk, kb = tile % nblk;
+  for (int off = threadIdx.x; off < tbytes; off += blockDim.x) {
+    int r, src;
+    tile_source(qtype, off, r, src);
+    const int64_t row = strip * 16 + r;
+    const int64_t raw_off = (row * nblk + kb) * bbytes + src;
+    const int64_t tiled_off = tile * tbytes + off;
+    if (kPack) {
+      uint8_t v = 0;
+      if (row < rows) {
+        v = in[raw_off];
+        // Non-finite FP16 block scale (exponent all ones): count once per scale.
+        const bool scale_hi = qtype == QK_TYPE_Q6_K ? src == 209 : (src == 1 || src == 3);
+        if (bad_scales && scale_hi && (v & 0x7c) == 0x7c) atomicAdd(bad_scales, 1);
+      }
+      out[tiled_off] = v;
+    } else if (row < rows) {
+      out[raw_off] = in[tiled_off];
+    }
+  }
+}
+
+// Decode of the tiled layout through the same fragment decoders the GEMM kernels use.
+template <QType QT>
+__global__ void dequant_tiled_kernel(const uint8_t* __restrict__ tiled, int64_t rows,
+                                     int64_t width, int64_t nblk, int out_bf16,
+                                     void* __restrict__ out) {
+  using T = Tile<QT>;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t tile = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + warp;
+  const int64_t strips = (rows + 15) / 16;
+  if (tile >= strips * nblk) return;
+  const int64_t strip = tile / nblk, kb = tile % nblk;
+  typename T::Regs r;
+  T::load(r, tiled + tile * T::kBytes, lane);
+  ScaleState<QT> st;
+  const int g = lane >> 2, c = lane & 3;
+  auto emit = [&](int rh, int p, uint32_t pair) {
+    const int64_t row = strip * 16 + rh * 8 + g;
+    const int64_t col = kb * 256 + p;
+    if (row >= rows) return;
+    for (int i = 0; i < 2; ++i) {
+      if (col + i >= width) break;
+      const uint16_t bits = static_cast<uint16_t>(pair >> (16 * i));
+      if (out_bf16) static_cast<uint16_t*>(out)[row * width + col + i] = bits;
+      else static_cast<float*>(out)[row * width + col + i] = bf16_to_f32(bits);
+    }
+  };
+#pragma unroll
+  for (int s = 0; s < 16; ++s) {
+    st.update(r, c, s);
+    uint32_t a[4];
+    tile_fragment<QT>(r, st, s, a);
+    const int p = T::p0(c, s);
+    emit(0, p, a[0]);
+    emit(0, p + 2, a[2]);
+    emit(1, p, a[1]);
+    emit(1, p + 2, a[3]);
+  }
+}
+
+int grid_for(int64_t total, int block) {
+  int64_t g = (total + block - 1) / block;
+  const int64_t cap = static_cast<int64_t>(sm_count()) * 32;
+  return static_cast<int>(g < 1 ? 1 : (g > cap ? cap : g));
+}
+
+}  // namespace
+}  // namespace qk
+
+using namespace qk;
+
+extern "C" {
+
+int qk_dequantize_rows(const uint8_t* raw, int qtype, int64_t rows, int64_t row_width,
+                       int out_dtype, void* out, qk_stream_t stream) {
+  const BlockShape shape = block_shape(qtype);
+  if (shape.values == 0) return set_error(QK_ERR_UNSUPPORTED_TYPE, "unsupported GGUF quantization type: %d", qtype);
+  QK_REQUIRE(rows >= 0 && row_width > 0, "row_width must be a positive integer");
+  QK_REQUIRE(out_dtype == QK_OUT_F32 || out_dtype == QK_OUT_BF16, "out_dtype must be F32 or BF16");
+  if (rows == 0) return QK_OK;
+  QK_REQUIRE(raw && out, "null pointer");
+  const int64_t nblk = (row_width + shape.values - 1) / shape.values;
+  dequant_rows_kernel<<<grid_for(rows * row_width, 256), 256, 0, as_stream(stream)>>>(
+      raw, qtype, rows, row_width, nblk, shape, out_dtype == QK_OUT_BF16, out);
+  QK_LAUNCHED("dequant_rows_kernel");
+  return QK_OK;
+}
+
+int64_t qk_tiled_bytes(int qtype, int64_t rows, int64_t row_width) {
+  const int tb = tile_bytes(qtype);
+  if (tb == 0 || rows < 0 || row_width <= 0) return -1;
+  return (rows + 15) / 16 * ((row_width + 255) / 256) * tb;
+}
+
+static int repack_common(const uint8_t* in, int qtype, int64_t rows, int64_t row_width,
+                         uint8_t* out, int32_t* bad, qk_stream_t stream, bool pack) {
+  const int tb = tile_bytes(qtype);
+  if (tb == 0) return set_error(QK_ERR_UNSUPPORTED_TYPE, "tiled layout supports Q6_K and Q4_K; got %d", qtype);
+  QK_REQUIRE(rows > 0 && row_width > 0, "Expected [output_features, ceil(input_features / 256), bytes]");
+  QK_REQUIRE(in && out, "null pointer");
+  const int64_t nblk = (row_width + 255) / 256;
+  const int64_t tiles = (rows + 15) / 16 * nblk;
+  QK_REQUIRE(tiles < (1ll << 31), "too many tiles");
+  const int bb = block_shape(qtype).bytes;
+  if (pack)
+    repack_kernel<true><<<static_cast<unsigned>(tiles), 256, 0, as_stream(stream)>>>(in, out, qtype, rows, nblk, tb, bb, bad);
+  else
+    repack_kernel<false><<<static_cast<unsigned>(tiles), 256, 0, as_stream(stream)>>>(in, out, qtype, rows, nblk, tb, bb, nullptr);
+  QK_LAUNCHED("repack_kernel");
+  return QK_OK;
+}
+
+int qk_repack_rows(const uint8_t* raw, int qtype, int64_t rows, int64_t row_width,
+                   uint8_t* tiled, int32_t* bad_scales, qk_stream_t stream) {
+  return repack_common(raw, qtype, rows, row_width, tiled, bad_scales, stream, true);
+}
+
+int qk_unpack_rows(const uint8_t* tiled, int qtype, int64_t rows, int64_t row_width, uint8_t* raw,
+                   qk_stream_t stream) {
+  return repack_common(tiled, qtype, rows, row_width, raw, nullptr, stream, false);
+}
+
+int qk_dequantize_tiled(const uint8_t* tiled, int qtype, int64_t rows, int64_t row_width,
+                        int out_dtype, void* out, qk_stream_t stream) {
+  if (tile_bytes(qtype) == 0) return set_error(QK_ERR_UNSUPPORTED_TYPE, "tiled layout supports Q6_K and Q4_K; got %d", qtype);
+  QK_REQUIRE(rows > 0 && row_width > 0, "rows and row_width must be positive");
+  QK_REQUIRE(out_dtype == QK_OUT_F32 || out_dtype == QK_OUT_BF16, "out_dtype must be F32 or BF16");
+  QK_REQUIRE(tiled && out, "null pointer");
+  const int64_t nblk = (row_width + 255) / 256;
+  const int64_t tiles = (rows + 15) / 16 * nblk;
+  const unsigned grid = static_cast<unsigned>((tiles + 3) / 4);
+  if (qtype == QK_TYPE_Q6_K)
+    dequant_tiled_kernel<QType::Q6_K><<<grid, 128, 0, as_stream(stream)>>>(tiled, rows, row_width, nblk, out_dtype == QK_OUT_BF16, out);
+  else
+    dequant_tiled_kernel<QType::Q4_K><<<grid, 128, 0, as_stream(stream)>>>(tiled, rows, row_width, nblk, out_dtype == QK_OUT_BF16, out);
+  QK_LAUNCHED("dequant_tiled_kernel");
+  return QK_OK;
+}
+
+}  // extern "C"

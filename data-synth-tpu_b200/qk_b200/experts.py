@@ -1,0 +1,151 @@
+"""Routed expert FFN over packed expert weights (replaces ``qwen38_tpu/experts.py:17-140``).
+
+``expert_parallel(group, *, gate_type, up_type, down_type, hidden, intermediate, ...)``
+returns ``fn(gate, up, down, x, ids, weights) -> bf16[B, hidden]`` with the reference's
+positional order (``engine.py:199-201``). ``gate``/``up``/``down`` are this rank's
+device-resident tiled expert tensors from :func:`parallel.put_expert_bytes`; ``x`` is
+BF16 ``[B, hidden]``, ``ids`` int32 ``[B, k]``, ``weights`` BF16 ``[B, k]``, all replicated
+across ranks as in the reference's ``P()`` in_specs.
+
+Single GPU: one ``qk_moe_forward`` call writes the BF16 output. Expert parallel over a
+``torch.distributed`` group (NCCL): each rank writes the FP32 sum over its own experts,
+an all-reduce adds the ranks (``experts.py:130-131``, ``psum(out, "expert")``) and
+``qk_cast_f32_bf16`` casts the sum to BF16.
+"""
+
+import torch
+
+from . import _lib
+from .parallel import expert_shape
+from .quant import GGML_TYPE, normalize_qtype
+
+EXPERT_ROW_TILE = 128
+
+
+class ExpertFFN:
+    def __init__(self, group, gate_type, up_type, down_type, hidden, intermediate):
+        self.group = group
+        self.types = tuple(normalize_qtype(t) for t in (gate_type, up_type, down_type))
+        self.hidden = hidden
+        self.intermediate = intermediate
+        self._workspace = {}
+
+    def _rank_world(self):
+        if self.group is None:
+            return 0, 1
+        import torch.distributed as dist
+
+        return dist.get_rank(self.group), dist.get_world_size(self.group)
+
+    def desc(self, num_experts, first_expert, top_k):
+        return _lib.MoeDesc(
+            GGML_TYPE[self.types[0]], GGML_TYPE[self.types[1]], GGML_TYPE[self.types[2]],
+            self.hidden, self.intermediate, num_experts, first_expert, top_k,
+        )
+
+    def workspace(self, desc, batch, device):
+        need = int(_lib.load().qk_moe_workspace_bytes(desc, batch))
+        key = (device.index, desc.num_experts, desc.top_k)
+        buf = self._workspace.get(key)
+        if buf is None or buf.numel() < need:
+            buf = torch.empty(max(need, 1), dtype=torch.uint8, device=device)
+            self._workspace[key] = buf
+        return buf
+
+    def _check(self, gate, up, down, x, ids, weights):
+        if x.dtype != torch.bfloat16 or x.dim() != 2 or x.shape[1] != self.hidden:
+            raise TypeError("x must be a BF16 [B, hidden] tensor")
+        if ids.dim() != 2 or ids.shape[0] != x.shape[0] or weights.shape != ids.shape:
+            raise ValueError("ids and weights must be [B, top_k]")
+        count = gate.shape[0]
+        if up.shape[0] != count or down.shape[0] != count:
+            raise ValueError("gate, up and down must hold the same experts")
+
+    def partial(self, gate, up, down, x, ids, weights, first_expert=None):
+        """FP32 ``[B, hidden]`` sum over this rank's experts (before the all-reduce)."""
+        return self._run(gate, up, down, x, ids, weights, first_expert, torch.float32)
+
+    def _run(self, gate, up, down, x, ids, weights, first_expert, out_dtype):
+        self._check(gate, up, down, x, ids, weights)
+        rank, _ = self._rank_world()
+        count = gate.shape[0]
+        first = rank * count if first_expert is None else first_expert
+        batch, top_k = ids.shape
+        desc = self.desc(count, first, top_k)
+        device = x.device
+        ws = self.workspace(desc, batch, device)
+        x = x.contiguous()
+        ids = ids.to(torch.int32).contiguous()
+        weights = weights.to(torch.bfloat16).contiguous()
+        out = torch.empty((batch, self.hidden), dtype=out_dtype, device=device)
+        with torch.cuda.device(device):
+            _lib.call(
+                "qk_moe_forward", desc, _lib.ptr(gate), _lib.ptr(up), _lib.ptr(down),
+                _lib.ptr(x), _lib.ptr(ids), _lib.ptr(weights), batch,
+                _lib.QK_OUT_BF16 if out_dtype == torch.bfloat16 else _lib.QK_OUT_F32,
+                _lib.ptr(out), _lib.ptr(ws), ws.numel(), _lib.stream_handle(device),
+            )
+        self.last_workspace = ws
+        return out
+
+    def __call__(self, gate, up, down, x, ids, weights):
+        rank, world = self._rank_world()
+        if world == 1:
+            return self._run(gate, up, down, x, ids, weights, None, torch.bfloat16)
+        import torch.distributed as dist
+
+        partial = self._run(gate, up, down, x, ids, weights, None, torch.float32)
+        dist.all_reduce(partial, group=self.group)
+        out = torch.empty(partial.shape, dtype=torch.bfloat16, device=partial.device)
+        with torch.cuda.device(partial.device):
+            _lib.call("qk_cast_f32_bf16", _lib.ptr(partial), _lib.ptr(out), partial.numel(),
+                      _lib.stream_handle(partial.device))
+        return out
+
+    def check_status(self):
+        """Raise if a bounded device wait of the last call gave up (synchronises)."""
+        ws = getattr(self, "last_workspace", None)
+        if ws is not None:
+            with torch.cuda.device(ws.device):
+                _lib.call("qk_moe_check", _lib.ptr(ws), _lib.stream_handle(ws.device))
+
+
+def expert_parallel(
+    group=None,
+    *,
+    gate_type,
+    up_type,
+    down_type,
+    hidden,
+    intermediate,
+    compute="bf16",
+    row_tile=EXPERT_ROW_TILE,
+    group_size=1,
+    tensor_parallel=1,
+):
+    """Return the routed FFN for this process's experts; see the module docstring.
+
+    ``compute`` "int8_q8" only changes Q8_0 projections in the reference; with the
+    Q6_K/Q4_K types this library takes it computes exactly like "bf16". ``row_tile`` and
+    ``group_size`` shape the reference's XLA loops and do not change results; they are
+    validated and otherwise unused (the kernels tile rows by 32 and stream experts).
+    """
+    if compute not in {"bf16", "int8_q8"}:
+        raise ValueError("Unknown expert compute policy")
+    if row_tile is not None and (type(row_tile) is not int or row_tile < 1):
+        raise ValueError("Expert row tile must be a positive integer or None")
+    if type(group_size) is not int or group_size < 1:
+        raise ValueError("Expert group size must be a positive integer")
+    if type(tensor_parallel) is not int or tensor_parallel < 1:
+        raise ValueError("Tensor parallel size must divide the device count")
+    if tensor_parallel != 1:
+        raise NotImplementedError("tensor-parallel experts are not built in this library")
+    types = tuple(normalize_qtype(t) for t in (gate_type, up_type, down_type))
+    if len(set(types)) != 1 or types[0] not in ("Q6_K", "Q4_K"):
+        raise ValueError("expert kernels take gate/up/down all Q6_K or all Q4_K")
+    if hidden % 256 or intermediate % 256:
+        raise ValueError("hidden and intermediate must be multiples of 256")
+    return ExpertFFN(group, *types, hidden, intermediate)
+
+
+__all__ = ["ExpertFFN", "expert_parallel", "expert_shape", "EXPERT_ROW_TILE"]

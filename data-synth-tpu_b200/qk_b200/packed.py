@@ -1,0 +1,147 @@
+"""Lossless tiled repack and the packed-weight projection.
+
+Mirrors ``kaggle/packed_q6``: ``pack_q6``/``unpack_q6`` (``layout.py:49-108``) and
+``q6_matmul`` (``kernel.py:98-148``), with this build's tile layout (16 rows x 256
+values per tile, see ``csrc/tiles.cuh``) instead of the TPU SoA tiles. ``pack_rows``
+and ``quant_matmul`` are the type-generic forms (Q6_K, Q4_K).
+"""
+
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from . import _lib
+from .quant import BLOCK_LAYOUTS, GGML_TYPE, normalize_qtype
+
+TILED_TYPES = ("Q6_K", "Q4_K")
+
+
+@dataclass(frozen=True)
+class PackedWeights:
+    data: torch.Tensor  # uint8 [tiled_bytes] on the device
+    qtype: str
+    input_features: int
+    output_features: int
+
+    @property
+    def input_blocks(self):
+        return (self.input_features + 255) // 256
+
+    def storage(self):
+        original = self.output_features * self.input_blocks * BLOCK_LAYOUTS[self.qtype][1]
+        size = self.data.numel()
+        return dict(
+            original_bytes=original,
+            packed_bytes=size,
+            padding_bytes=size - original,
+            padding_ratio=size / original - 1,
+            layout="qk_b200_tile16x256_v1",
+        )
+
+
+def tiled_bytes(qtype, rows, row_width):
+    n = _lib.load().qk_tiled_bytes(GGML_TYPE[normalize_qtype(qtype)], rows, row_width)
+    if n < 0:
+        raise ValueError(f"no tiled layout for {qtype}")
+    return int(n)
+
+
+def _device_raw(raw, device):
+    if isinstance(raw, np.ndarray):
+        if raw.dtype != np.uint8:
+            raise TypeError(f"GGUF input must have dtype uint8; got {raw.dtype}")
+        return torch.from_numpy(np.ascontiguousarray(raw)).to(device)
+    if not isinstance(raw, torch.Tensor) or raw.dtype != torch.uint8:
+        raise TypeError("GGUF input must have dtype uint8")
+    return raw.to(device).contiguous()
+
+
+def pack_rows(raw, input_features, qtype="Q6_K", device=None):
+    """Repack ``uint8[N, ceil(K/256), bpb]`` GGUF rows into device tiles (no arithmetic)."""
+    name = normalize_qtype(qtype)
+    if name not in TILED_TYPES:
+        raise ValueError(f"tiled layout supports {TILED_TYPES}; got {name}")
+    if type(input_features) is not int or input_features < 1:
+        raise ValueError("input_features must be a positive integer")
+    device = torch.device(device or "cuda")
+    if isinstance(raw, np.ndarray) and raw.dtype != np.uint8:
+        raise TypeError(f"GGUF {name} input must have dtype uint8")
+    if isinstance(raw, torch.Tensor) and raw.dtype != torch.uint8:
+        raise TypeError(f"GGUF {name} input must have dtype uint8")
+    blocks = (input_features + 255) // 256
+    size = BLOCK_LAYOUTS[name][1]
+    if raw.ndim != 3 or raw.shape[0] < 1 or tuple(raw.shape[1:]) != (blocks, size):
+        raise ValueError("Expected [output_features, ceil(input_features / 256), bytes_per_block]")
+    src = _device_raw(raw, device)
+    rows = int(src.shape[0])
+    out = torch.empty(tiled_bytes(name, rows, input_features), dtype=torch.uint8, device=device)
+    bad = torch.zeros(1, dtype=torch.int32, device=device)
+    with torch.cuda.device(device):
+        _lib.call("qk_repack_rows", _lib.ptr(src), GGML_TYPE[name], rows, input_features,
+                  _lib.ptr(out), _lib.ptr(bad), _lib.stream_handle(device))
+    if int(bad.item()):
+        raise ValueError(f"{name} block scales must be finite")
+    return PackedWeights(out, name, input_features, rows)
+
+
+def pack_q6(raw, input_features, device=None):
+    """``packed_q6.layout.pack_q6`` with the B200 tile layout."""
+    return pack_rows(raw, input_features, "Q6_K", device)
+
+
+def unpack_rows(packed):
+    """Inverse byte transform -> ``uint8[N, ceil(K/256), bpb]`` on the device."""
+    size = BLOCK_LAYOUTS[packed.qtype][1]
+    out = torch.empty((packed.output_features, packed.input_blocks, size), dtype=torch.uint8,
+                      device=packed.data.device)
+    with torch.cuda.device(packed.data.device):
+        _lib.call("qk_unpack_rows", _lib.ptr(packed.data), GGML_TYPE[packed.qtype],
+                  packed.output_features, packed.input_features, _lib.ptr(out),
+                  _lib.stream_handle(packed.data.device))
+    return out
+
+
+unpack_q6 = unpack_rows
+
+
+def dequantize_packed(packed, dtype=torch.bfloat16):
+    """Decode tiles through the GEMM kernels' fragment decoder -> ``[N, K]``."""
+    out = torch.empty((packed.output_features, packed.input_features), dtype=dtype,
+                      device=packed.data.device)
+    with torch.cuda.device(packed.data.device):
+        _lib.call("qk_dequantize_tiled", _lib.ptr(packed.data), GGML_TYPE[packed.qtype],
+                  packed.output_features, packed.input_features,
+                  _lib.QK_OUT_BF16 if dtype == torch.bfloat16 else _lib.QK_OUT_F32,
+                  _lib.ptr(out), _lib.stream_handle(packed.data.device))
+    return out
+
+
+def quant_matmul(x, packed):
+    """FP32 ``x @ bf16(decode(W)).T`` with the weights kept packed."""
+    if not isinstance(x, torch.Tensor) or x.dim() != 2 or min(x.shape) < 1 or x.dtype != torch.bfloat16:
+        raise ValueError("x must be a nonempty [M,K] BF16 array")
+    if x.shape[1] != packed.input_features:
+        raise ValueError("Packed dtype/shape does not match projection dimensions")
+    x = x.contiguous()
+    out = torch.empty((x.shape[0], packed.output_features), dtype=torch.float32, device=x.device)
+    with torch.cuda.device(x.device):
+        _lib.call("qk_quant_gemm", _lib.ptr(x), x.shape[0], x.shape[1], _lib.ptr(packed.data),
+                  GGML_TYPE[packed.qtype], packed.output_features, _lib.ptr(out),
+                  _lib.stream_handle(x.device))
+    return out
+
+
+def q6_matmul(x, packed, *, output_features, batch_tile=8):
+    """``packed_q6.kernel.q6_matmul`` contract: FP32 ``[M, N]``; validates like the reference."""
+    if not isinstance(x, torch.Tensor) or x.dim() != 2 or min(x.shape) < 1 or x.dtype != torch.bfloat16:
+        raise ValueError("x must be a nonempty [M,K] BF16 array")
+    if type(output_features) is not int or output_features < 1:
+        raise ValueError("output_features must be positive")
+    if type(batch_tile) is not int or batch_tile < 8 or batch_tile % 8:
+        raise ValueError("batch_tile must be a positive multiple of 8")
+    if packed.qtype != "Q6_K" or packed.output_features != output_features or (
+        packed.input_features != x.shape[1]
+    ):
+        raise ValueError("Packed Q6 dtype/shape does not match projection dimensions")
+    return quant_matmul(x, packed)

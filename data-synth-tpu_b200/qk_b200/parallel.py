@@ -1,0 +1,82 @@
+"""Expert placement: byte-exact EP/TP splits and device-resident tiled expert tensors.
+
+``split_expert_bytes`` keeps the reference's contract (``qwen38_tpu/parallel.py:40-61``):
+raw GGUF expert bytes ``[E, bytes]`` -> ``[tensor_rank, local_expert, bytes]`` without
+splitting a quantisation block. ``put_expert_bytes`` replaces ``parallel.py:64-87``: it
+takes this rank's contiguous expert range (EP: experts are partitioned, tokens are
+replicated) and repacks each expert into the B200 tile layout on the device.
+"""
+
+import numpy as np
+import torch
+
+from . import _lib
+from .packed import TILED_TYPES, tiled_bytes
+from .quant import BLOCK_LAYOUTS, GGML_TYPE, normalize_qtype
+
+
+def split_expert_bytes(raw, kind, qtype, hidden, intermediate, tensor_parallel):
+    if kind not in {"gate", "up", "down"}:
+        raise ValueError("Unknown expert projection")
+    block, size = BLOCK_LAYOUTS[normalize_qtype(qtype)]
+    if intermediate % tensor_parallel:
+        raise ValueError("Intermediate channels must divide tensor parallel size")
+    local = intermediate // tensor_parallel
+    count = len(raw)
+    if kind == "down":
+        if local % block:
+            raise ValueError("Tensor slices must contain whole down quantization blocks")
+        rows = np.asarray(raw).reshape(count, hidden, tensor_parallel, local // block, size)
+        return rows.transpose(2, 0, 1, 3, 4).reshape(tensor_parallel, count, -1).copy()
+    if hidden % block:
+        raise ValueError("Hidden channels must contain whole quantization blocks")
+    rows = np.asarray(raw).reshape(count, tensor_parallel, local, hidden // block, size)
+    return rows.transpose(1, 0, 2, 3, 4).reshape(tensor_parallel, count, -1).copy()
+
+
+def expert_shape(kind, hidden, intermediate):
+    """(rows, row_width) of one expert's projection matrix."""
+    return (hidden, intermediate) if kind == "down" else (intermediate, hidden)
+
+
+def local_range(num_experts, rank, world):
+    if num_experts % world:
+        raise ValueError("Expert count must divide expert parallel size")
+    per = num_experts // world
+    return rank * per, per
+
+
+def put_expert_bytes(raw, kind, qtype, hidden, intermediate, *, rank=0, world=1, device=None):
+    """This rank's experts as a device tensor ``uint8[E_local, tiled_bytes_per_expert]``."""
+    name = normalize_qtype(qtype)
+    if name not in TILED_TYPES:
+        raise ValueError(f"expert kernels take {TILED_TYPES}; got {name}")
+    rows, width = expert_shape(kind, hidden, intermediate)
+    values, size = BLOCK_LAYOUTS[name]
+    first, count = local_range(len(raw), rank, world)
+    device = torch.device(device or "cuda")
+    per_raw = rows * ((width + values - 1) // values) * size
+    part = raw[first : first + count]
+    if isinstance(part, np.ndarray):
+        if part.dtype != np.uint8:
+            raise TypeError("GGUF expert bytes must have dtype uint8")
+        src = torch.from_numpy(np.ascontiguousarray(part.reshape(count, -1))).to(device)
+    else:
+        src = part.reshape(count, -1).to(device).contiguous()
+    if src.shape[1] != per_raw:
+        raise ValueError(f"{kind} expert must hold {per_raw} bytes; got {src.shape[1]}")
+    per_tiled = tiled_bytes(name, rows, width)
+    out = torch.empty((count, per_tiled), dtype=torch.uint8, device=device)
+    bad = torch.zeros(1, dtype=torch.int32, device=device)
+    stream = _lib.stream_handle(device)
+    with torch.cuda.device(device):
+        if rows % 16 == 0:  # experts never share a 16-row strip: one launch for all
+            _lib.call("qk_repack_rows", _lib.ptr(src), GGML_TYPE[name], count * rows, width,
+                      _lib.ptr(out), _lib.ptr(bad), stream)
+        else:
+            for e in range(count):
+                _lib.call("qk_repack_rows", _lib.ptr(src[e]), GGML_TYPE[name], rows, width,
+                          _lib.ptr(out[e]), _lib.ptr(bad), stream)
+    if int(bad.item()):
+        raise ValueError(f"{name} block scales must be finite")
+    return out

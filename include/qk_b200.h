@@ -1,0 +1,187 @@
+/*
+ * qk_b200.h - C ABI of the B200 (sm_100a) packed-quant MoE and Q8 KV-cache kernels.
+ *
+ * Plain pointers and sizes only. All device pointers refer to memory of the CUDA
+ * device that is current on the calling thread; every call is asynchronous on
+ * `stream` and returns a qk_status. No call allocates device memory: scratch space
+ * is passed in as `workspace` (size from the matching *_workspace_bytes query).
+ *
+ * Reference interfaces (AhmadSaeedZaidi/data-synth-tpu, paths under kaggle/) are
+ * cited beside each entry point. BF16 values are passed as uint16_t storage bits.
+ *
+ * Quantisation type codes are GGML's type numbers (QK_TYPE_*), the numbering the
+ * reference's GGUF reader uses (glm53_offload/gguf_quant.py:31-39).
+ */
+#ifndef QK_B200_H
+#define QK_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef void* qk_stream_t; /* a cudaStream_t; NULL = legacy default stream */
+
+typedef enum qk_status {
+  QK_OK = 0,
+  QK_ERR_INVALID_ARGUMENT = 1, /* bad shape, size, stride or null pointer   */
+  QK_ERR_UNSUPPORTED_TYPE = 2, /* quantisation type not handled by the call */
+  QK_ERR_NONFINITE_SCALE = 3,  /* a block scale is inf/NaN (repack refuses) */
+  QK_ERR_CUDA = 4,             /* a CUDA runtime call or launch failed       */
+  QK_ERR_TIMEOUT = 5,          /* a bounded device wait gave up              */
+  QK_ERR_WORKSPACE = 6         /* workspace pointer missing or too small     */
+} qk_status;
+
+enum {
+  QK_TYPE_F32 = 0,
+  QK_TYPE_F16 = 1,
+  QK_TYPE_Q4_0 = 2,
+  QK_TYPE_Q4_1 = 3,
+  QK_TYPE_Q5_0 = 6,
+  QK_TYPE_Q5_1 = 7,
+  QK_TYPE_Q8_0 = 8,
+  QK_TYPE_Q4_K = 12,
+  QK_TYPE_Q5_K = 13,
+  QK_TYPE_Q6_K = 14,
+  QK_TYPE_IQ4_NL = 20,
+  QK_TYPE_BF16 = 30
+};
+
+enum { QK_OUT_F32 = 0, QK_OUT_BF16 = 1 };
+
+/* ---- library ---------------------------------------------------------------- */
+
+/* Version string "qk_b200 <major>.<minor> sm_100a". */
+const char* qk_version(void);
+/* Human-readable text of the last error set on this host thread (or ""). */
+const char* qk_last_error(void);
+/* Number of kernels this library has launched in this process (all devices). */
+uint64_t qk_launch_count(void);
+
+/* ---- GGUF block decode -------------------------------------------------------
+ * Replaces glm53_offload/gguf_quant.py:180-216 dequantize_rows(raw, qtype,
+ * row_width, dtype) and qwen38_tpu/quant.py:15-55 (Q4_0/Q4_1/Q5_0/Q5_1/IQ4_NL).
+ * raw: uint8 [rows, ceil(row_width / values_per_block), bytes_per_block].
+ * out: [rows, row_width] FP32 or BF16 (RNE, precision.py:7-23). Bit-exact. */
+int qk_dequantize_rows(const uint8_t* raw, int qtype, int64_t rows, int64_t row_width,
+                       int out_dtype, void* out, qk_stream_t stream);
+
+/* ---- tiled repack (lossless) -------------------------------------------------
+ * Replaces packed_q6/layout.py:49-108 pack_q6 / unpack_q6: a byte-only repack of raw
+ * GGUF rows into the B200 tile layout (16 rows x 256 values per tile, rows padded to
+ * 16) read by qk_quant_gemm and qk_moe_forward. Q6_K and Q4_K.
+ * bad_scales (device int32, may be NULL): receives the count of non-finite FP16 block
+ * scales (pack_q6 rejects those, layout.py:67-69); the host wrapper raises on > 0. */
+int64_t qk_tiled_bytes(int qtype, int64_t rows, int64_t row_width);
+int qk_repack_rows(const uint8_t* raw, int qtype, int64_t rows, int64_t row_width,
+                   uint8_t* tiled, int32_t* bad_scales, qk_stream_t stream);
+int qk_unpack_rows(const uint8_t* tiled, int qtype, int64_t rows, int64_t row_width,
+                   uint8_t* raw, qk_stream_t stream);
+/* Decode of the tiled layout (same values as qk_dequantize_rows on the raw rows). */
+int qk_dequantize_tiled(const uint8_t* tiled, int qtype, int64_t rows, int64_t row_width,
+                        int out_dtype, void* out, qk_stream_t stream);
+
+/* ---- packed projection -------------------------------------------------------
+ * Replaces packed_q6/kernel.py:98-148 q6_matmul(x, packed, scales, output_features):
+ * out[M, N] (FP32) = bf16 x[M, K] @ bf16(decode(W))[N, K]^T, FP32 accumulation.
+ * w_tiled: qk_repack_rows output for W (Q6_K or Q4_K). Ragged M, N and K allowed. */
+int qk_quant_gemm(const uint16_t* x, int64_t M, int64_t K, const uint8_t* w_tiled, int qtype,
+                  int64_t N, float* out, qk_stream_t stream);
+
+/* ---- router ------------------------------------------------------------------
+ * Replaces the router of qwen38_tpu/math.py:277-281 (routes_and_shared):
+ * probs = softmax(f32(x) @ f32(Wr)^T); (w, ids) = top_k(probs, k) (ties: lower index);
+ * w = w / sum(w); w = bf16(active ? w : 0).
+ * x: BF16 [T, H]; router_w: FP32 [E, H]; active: uint8 [T] or NULL (all active).
+ * ids: int32 [T, k]; weights: BF16 [T, k]; probs (FP32 [T, E], may be NULL). */
+int qk_router_topk(const uint16_t* x, const float* router_w, const uint8_t* active, int T, int H,
+                   int E, int k, int32_t* ids, uint16_t* weights, float* probs, qk_stream_t stream);
+/* Same selection from precomputed FP32 logits [T, E]. */
+int qk_router_topk_logits(const float* logits, const uint8_t* active, int T, int E, int k,
+                          int32_t* ids, uint16_t* weights, float* probs, qk_stream_t stream);
+
+/* ---- routed expert FFN -------------------------------------------------------
+ * Replaces the function returned by qwen38_tpu/experts.py:17-140 expert_parallel(mesh,
+ * gate_type, up_type, down_type, hidden, intermediate, ...) and
+ * qwen38_tpu/grouped_experts.py:21-163, called as fn(gate, up, down, x, ids, weights)
+ * (engine.py:199-201), for this rank's experts [first_expert, first_expert + num_experts).
+ * gate/up: tiled bytes [num_experts, qk_tiled_bytes(type, intermediate, hidden)];
+ * down: tiled bytes [num_experts, qk_tiled_bytes(type, hidden, intermediate)].
+ * x: BF16 [B, hidden]; ids: int32 [B, top_k]; weights: BF16 [B, top_k].
+ * out: BF16 [B, hidden] (out_dtype QK_OUT_BF16), or the FP32 sum over this rank's
+ * experts (QK_OUT_F32) that an expert-parallel all-reduce adds (experts.py:130-131). */
+typedef struct qk_moe_desc {
+  int gate_type, up_type, down_type; /* QK_TYPE_Q6_K or QK_TYPE_Q4_K (all equal) */
+  int hidden, intermediate;          /* multiples of 256                         */
+  int num_experts;                   /* experts held by this rank                */
+  int first_expert;                  /* global id of this rank's first expert    */
+  int top_k;                         /* routes per token                         */
+} qk_moe_desc;
+
+size_t qk_moe_workspace_bytes(const qk_moe_desc* desc, int max_tokens);
+int qk_moe_forward(const qk_moe_desc* desc, const uint8_t* gate, const uint8_t* up,
+                   const uint8_t* down, const uint16_t* x, const int32_t* ids,
+                   const uint16_t* weights, int B, int out_dtype, void* out, void* workspace,
+                   size_t workspace_bytes, qk_stream_t stream);
+/* qk_moe_forward that also records cudaEvent_t events[0..4] on `stream` before the
+ * route, gate/up, down and combine launches and after the last one (NULL entries are
+ * skipped): the per-kernel timing the benchmark reports. */
+int qk_moe_forward_profiled(const qk_moe_desc* desc, const uint8_t* gate, const uint8_t* up,
+                            const uint8_t* down, const uint16_t* x, const int32_t* ids,
+                            const uint16_t* weights, int B, int out_dtype, void* out,
+                            void* workspace, size_t workspace_bytes, qk_stream_t stream,
+                            void* const* events);
+/* BF16 (RNE) of an FP32 array: the cast after the expert-parallel all-reduce
+ * (experts.py:131, psum(out).astype(x.dtype)). */
+int qk_cast_f32_bf16(const float* in, uint16_t* out, int64_t n, qk_stream_t stream);
+/* Status word the kernels of the last qk_moe_forward on `workspace` left behind:
+ * 0, or QK_ERR_TIMEOUT when a bounded wait gave up. Synchronises `stream`. */
+int qk_moe_check(const void* workspace, qk_stream_t stream);
+
+/* ---- Q8 KV cache -------------------------------------------------------------
+ * Cache layout is the reference's (attention_cache.py:26-43, engine.py:350-369):
+ * codes int8 [B, T, kv_heads * head_dim]; scale planes BF16 [B * G, T] with
+ * G = kv_heads * head_dim / group and group = min(32, head_dim) (config.py:91-93). */
+
+/* attention_cache.py:15-23 quantize(x, group): x [rows, width] (BF16 or FP32 by
+ * in_dtype QK_OUT_*); codes int8 [rows, width]; scales BF16 [rows, width / group]. */
+int qk_kv_q8_quantize(const void* x, int in_dtype, int64_t rows, int width, int group,
+                      int8_t* codes, uint16_t* scales, qk_stream_t stream);
+/* attention_cache.py:26-43 write_quantized(cache, key, value, indices, active, c):
+ * key/value [B, kv_heads, head_dim] (BF16 or FP32 by in_dtype); time [B] int32;
+ * active uint8 [B] or NULL. In place. Negative times wrap once; out-of-range drop. */
+int qk_kv_q8_append(const void* key, const void* value, int in_dtype, const int32_t* time,
+                    const uint8_t* active, int8_t* k_codes, int8_t* v_codes, uint16_t* k_scale,
+                    uint16_t* v_scale, int B, int T, int kv_heads, int head_dim,
+                    qk_stream_t stream);
+/* attention_cache.py:46-68 gather_scale_plane(plane, indices, groups): out BF16
+ * [B, S, groups]; negative indices wrap once, then clamp (test_qwen38_kv_gather.py:22-32). */
+int qk_kv_q8_gather_scales(const uint16_t* plane, const int32_t* indices, int B, int S,
+                           int groups, int T, uint16_t* out, qk_stream_t stream);
+/* attention_cache.py:71-81 read_quantized(cache, name, indices, c, dtype): out
+ * [B, S, kv_heads, head_dim] FP32 or BF16 = compute_cast(code * scale). */
+int qk_kv_q8_read(const int8_t* codes, const uint16_t* plane, const int32_t* indices, int B,
+                  int S, int T, int kv_heads, int head_dim, int out_dtype, void* out,
+                  qk_stream_t stream);
+
+/* Decode attention over the Q8 cache, attention_cache.py:152-170 (step after the
+ * cache write): GQA scores bf16(q.k), bf16(/sqrt(hd)), masked softmax, PV with FP32
+ * accumulation, bf16, then bf16(o * bf16(sigmoid(gate))) when gate != NULL.
+ * q: BF16 [B, hq, hd]; indices: int32 [B, S] cache times of the S slots (a page table
+ * expands to indices[b, s] = page[b, s / P] * P + s % P); valid: uint8 [B, S] or NULL,
+ * in which case slot s is valid iff s <= lengths[b]; out: BF16 [B, hq, hd].
+ * Split-KV: the workspace holds per-split partial (max, sum, out) for an LSE merge. */
+size_t qk_kv_q8_attention_workspace_bytes(int B, int S, int hq, int kv_heads, int head_dim);
+int qk_kv_q8_decode_attention(const uint16_t* q, const int8_t* k_codes, const int8_t* v_codes,
+                              const uint16_t* k_scale, const uint16_t* v_scale,
+                              const int32_t* indices, const uint8_t* valid,
+                              const int32_t* lengths, const uint16_t* gate, int B, int S, int T,
+                              int hq, int kv_heads, int head_dim, uint16_t* out, void* workspace,
+                              size_t workspace_bytes, qk_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* QK_B200_H */

@@ -1,0 +1,148 @@
+"""GGUF decode, tiled repack and packed projection on the GPU against the pinned oracle."""
+
+import hashlib
+
+import numpy as np
+import pytest
+
+from oracle import gguf, layout, moe
+from oracle.precision import bf16_round
+from util import bf16_tensor, to_f32
+
+pytestmark = pytest.mark.gpu
+
+TYPES = ["Q4_K", "Q5_K", "Q6_K", "Q8_0", "F16", "BF16", "F32", "Q4_0", "Q4_1", "Q5_0", "Q5_1", "IQ4_NL"]
+
+
+@pytest.mark.parametrize("qtype", TYPES)
+def test_dequantize_rows_bit_exact_against_reference_golden(golden, cuda_device, qtype):
+    import torch
+
+    from qk_b200.quant import dequantize_rows
+
+    data = golden("gguf_decode.npz")
+    raw, width = data[f"{qtype}_raw"], int(data[f"{qtype}_width"])
+    expected = data[f"{qtype}_expected"]
+    dev = torch.from_numpy(raw).to(cuda_device)
+    got = dequantize_rows(dev, qtype, width).cpu().numpy()
+    np.testing.assert_array_equal(got.view(np.uint32), expected.view(np.uint32))
+    got16 = to_f32(dequantize_rows(dev, qtype, width, dtype=torch.bfloat16))
+    np.testing.assert_array_equal(got16.view(np.uint32), bf16_round(expected).view(np.uint32))
+
+
+def test_q6_k_extreme_scales_every_sub_scale_bf16(golden, cuda_device):
+    import torch
+
+    from qk_b200.packed import dequantize_packed, pack_q6
+    from qk_b200.quant import dequantize_rows
+
+    data = golden("q6_projection.npz")
+    raw = data["extremes_raw"]
+    expected = data["extremes_bf16"]
+    got = to_f32(dequantize_rows(torch.from_numpy(raw).to(cuda_device), "Q6_K", 256, torch.bfloat16))
+    np.testing.assert_array_equal(got.view(np.uint32), expected.view(np.uint32))
+    # the GEMM kernels' in-register fragment decoder gives the same bits
+    tiled = to_f32(dequantize_packed(pack_q6(raw, 256, cuda_device)))
+    np.testing.assert_array_equal(tiled.view(np.uint32), expected.view(np.uint32))
+
+
+@pytest.mark.parametrize("qtype", ["Q6_K", "Q4_K"])
+@pytest.mark.parametrize("rows,width", [(1, 256), (17, 512), (65, 263), (512, 2048), (2048, 512)])
+def test_repack_is_lossless_and_fragment_decode_is_bit_exact(cuda_device, qtype, rows, width):
+    import torch
+
+    from qk_b200.packed import dequantize_packed, pack_rows, unpack_rows
+
+    rng = np.random.default_rng(rows * 7 + width)
+    size = layout.BLOCK_BYTES[qtype]
+    raw = rng.integers(0, 256, (rows, (width + 255) // 256, size), dtype=np.uint8)
+    offs = (208,) if qtype == "Q6_K" else (0, 2)
+    for off in offs:
+        raw[..., off : off + 2] = rng.uniform(-0.05, 0.05, raw.shape[:2]).astype("<f2").view(
+            np.uint8).reshape(*raw.shape[:2], 2)
+    packed = pack_rows(raw, width, qtype, cuda_device)
+    assert packed.data.numel() == layout.tiled_bytes(qtype, rows, width)
+    np.testing.assert_array_equal(packed.data.cpu().numpy(), layout.tile(raw, qtype))
+    np.testing.assert_array_equal(unpack_rows(packed).cpu().numpy(), raw)
+    expected = bf16_round(gguf.dequantize_rows(raw, qtype, width))
+    got = to_f32(dequantize_packed(packed, torch.bfloat16))
+    np.testing.assert_array_equal(got.view(np.uint32), expected.view(np.uint32))
+
+
+@pytest.mark.parametrize("scale", [np.inf, -np.inf, np.nan])
+def test_nonfinite_block_scale_rejected(cuda_device, scale):
+    from qk_b200.packed import pack_q6
+
+    raw = gguf.legal_q6_k_fixture(1, 256)
+    raw[0, 0, 208:] = np.array([scale], dtype="<f2").view(np.uint8)
+    with pytest.raises(ValueError, match="finite"):
+        pack_q6(raw, 256, cuda_device)
+
+
+def test_invalid_layout_or_projection_contract_rejected(cuda_device):
+    import torch
+
+    from qk_b200.packed import pack_q6, q6_matmul
+
+    with pytest.raises(TypeError, match="uint8"):
+        pack_q6(np.zeros((64, 1, 210)), 256, cuda_device)
+    with pytest.raises(ValueError, match="Expected"):
+        pack_q6(np.zeros((64, 1, 211), np.uint8), 256, cuda_device)
+    packed = pack_q6(gguf.legal_q6_k_fixture(64, 256), 256, cuda_device)
+    with pytest.raises(ValueError, match="BF16"):
+        q6_matmul(torch.ones((1, 256), device=cuda_device), packed, output_features=64)
+    with pytest.raises(ValueError, match="multiple of 8"):
+        q6_matmul(torch.ones((1, 256), dtype=torch.bfloat16, device=cuda_device), packed,
+                  output_features=64, batch_tile=1)
+    with pytest.raises(ValueError, match="dtype/shape"):
+        q6_matmul(torch.ones((1, 257), dtype=torch.bfloat16, device=cuda_device), packed,
+                  output_features=64)
+
+
+def test_packed_projection_matches_reference_fp64_dot(golden, cuda_device):
+    from qk_b200.packed import pack_q6, q6_matmul
+
+    data = golden("q6_projection.npz")
+    for batch, outputs, inputs in data["cases"]:
+        batch, outputs, inputs = int(batch), int(outputs), int(inputs)
+        key = f"{batch}_{outputs}_{inputs}"
+        raw = gguf.legal_q6_k_fixture(outputs, inputs)
+        assert hashlib.sha256(raw.tobytes()).digest() == bytes(data[f"raw_sha256_{key}"])
+        packed = pack_q6(raw, inputs, cuda_device)
+        x = bf16_tensor(data[f"x_{key}"], cuda_device)
+        got = q6_matmul(x, packed, output_features=outputs).cpu().numpy()
+        assert got.dtype == np.float32 and got.shape == (batch, outputs)
+        assert np.isfinite(got).all()
+        # tests/test_packed_q6.py:81 tolerance
+        np.testing.assert_allclose(got, data[f"expected_{key}"], rtol=2e-5, atol=2e-4)
+
+
+@pytest.mark.parametrize("qtype", ["Q6_K", "Q4_K"])
+@pytest.mark.parametrize("m", [1, 5, 33, 70])
+def test_quant_matmul_against_oracle(cuda_device, qtype, m):
+    from qk_b200.packed import pack_rows, quant_matmul
+
+    rng = np.random.default_rng(11 + m)
+    w = rng.normal(0, 0.02, (96, 512)).astype(np.float32)
+    raw = gguf.encode(w, qtype)
+    x = rng.normal(size=(m, 512)).astype(np.float32)
+    packed = pack_rows(raw, 512, qtype, cuda_device)
+    got = quant_matmul(bf16_tensor(x, cuda_device), packed).cpu().numpy()
+    wb = bf16_round(gguf.dequantize_rows(raw, qtype, 512))
+    expected = (bf16_round(x).astype(np.float64) @ wb.astype(np.float64).T).astype(np.float32)
+    np.testing.assert_allclose(got, expected, rtol=2e-5, atol=2e-4)
+
+
+def test_accumulator_is_reset_between_row_and_token_tiles(cuda_device):
+    import torch
+
+    from qk_b200.packed import pack_q6, q6_matmul
+
+    raw = gguf.legal_q6_k_fixture(128, 512)
+    raw[64:] = raw[:64]
+    packed = pack_q6(raw, 512, cuda_device)
+    x = torch.ones((40, 512), dtype=torch.bfloat16, device=cuda_device)
+    x[20:] = -1
+    result = q6_matmul(x, packed, output_features=128).cpu().numpy()
+    np.testing.assert_array_equal(result[:, :64], result[:, 64:])
+    np.testing.assert_array_equal(result[:20], -result[20:])

@@ -1,0 +1,155 @@
+"""Routed expert FFN on the GPU against the pinned oracle and the reference's own golden."""
+
+import numpy as np
+import pytest
+
+from oracle import gguf, moe
+from oracle.precision import bf16_round
+from util import bf16_tensor, rel_err, to_f32
+
+pytestmark = pytest.mark.gpu
+
+# North-star layer tolerance: max relative error 1e-2 (BF16 with FP32 accumulation).
+LAYER_TOL = 1e-2
+
+
+def make_experts(rng, count, hidden, intermediate, qtype):
+    raw = {}
+    for kind, (rows, width) in (("gate", (intermediate, hidden)), ("up", (intermediate, hidden)),
+                                ("down", (hidden, intermediate))):
+        w = rng.normal(0, 0.02, (count, rows, width)).astype(np.float32)
+        raw[kind] = gguf.encode(w, qtype).reshape(count, -1)
+    return raw
+
+
+def run_layer(device, raw, qtype, hidden, intermediate, x, ids, weights):
+    import torch
+
+    from qk_b200.experts import expert_parallel
+    from qk_b200.parallel import put_expert_bytes
+
+    dev = {k: put_expert_bytes(v, k, qtype, hidden, intermediate, device=device) for k, v in raw.items()}
+    fn = expert_parallel(gate_type=qtype, up_type=qtype, down_type=qtype, hidden=hidden,
+                         intermediate=intermediate)
+    out = fn(dev["gate"], dev["up"], dev["down"], bf16_tensor(x, device),
+             torch.from_numpy(np.asarray(ids, np.int32)).to(device), bf16_tensor(weights, device))
+    fn.check_status()
+    return to_f32(out), fn, dev
+
+
+def test_routed_ffn_matches_reference_numpy_oracle_golden(golden, cuda_device):
+    from make_golden import ROUTING_BATCHES, routing_inputs
+
+    data = golden("routing_ffn.npz")
+    packed, batches, down_type, hidden, intermediate, count = routing_inputs("q6", gguf.encode_q8_0)
+    flat = {k: v.reshape(count, -1) for k, v in packed.items()}
+    for batch in ROUTING_BATCHES:
+        ids, weights, source = batches[batch]
+        got, _, _ = run_layer(cuda_device, flat, "Q6_K", hidden, intermediate, source, ids, weights)
+        expected = (data[f"q6_b{batch}_bf16_bits"].astype(np.uint32) << 16).view(np.float32)
+        # routing_validation.py:262 BF16 tolerance
+        np.testing.assert_allclose(got, expected, atol=3e-3, rtol=3e-3)
+        np.testing.assert_array_equal(got[np.all(weights == 0, axis=-1)], 0)
+
+
+@pytest.mark.parametrize("qtype", ["Q6_K", "Q4_K"])
+def test_config1_layer_t8_top4_of_64(cuda_device, qtype):
+    """T=8, H=2048, I=512, 64 experts, router top-4 (smaller E keeps the oracle fast)."""
+    import torch
+
+    from qk_b200.routing import routes
+
+    hidden, intermediate, count, k = 2048, 512, 64, 4
+    raw = make_experts(np.random.default_rng(1), count, hidden, intermediate, qtype)
+    x = np.random.default_rng(0).normal(size=(8, hidden)).astype(np.float32)
+    router = np.random.default_rng(2).normal(0, 0.02, (count, hidden)).astype(np.float32)
+    ids, weights = routes(bf16_tensor(x, cuda_device), torch.from_numpy(router).to(cuda_device), k)
+    ids, weights = ids.cpu().numpy(), to_f32(weights)
+    got, _, _ = run_layer(cuda_device, raw, qtype, hidden, intermediate, x, ids, weights)
+    expected = moe.expert_ffn(raw["gate"], raw["up"], raw["down"], x, ids, weights, gate_type=qtype,
+                              up_type=qtype, down_type=qtype, hidden=hidden, intermediate=intermediate)
+    mx, l2 = rel_err(got, expected)
+    assert mx < LAYER_TOL and l2 < 2e-3, (mx, l2)
+
+
+@pytest.mark.parametrize("tokens_per_expert", [1, 9, 33, 70])
+def test_many_tokens_per_expert_duplicates_and_finished_rows(cuda_device, tokens_per_expert):
+    hidden, intermediate, count, k = 512, 256, 6, 2
+    rng = np.random.default_rng(tokens_per_expert)
+    raw = make_experts(rng, count, hidden, intermediate, "Q6_K")
+    batch = tokens_per_expert * count // k + 1
+    ids = rng.integers(0, count, (batch, k)).astype(np.int32)
+    ids[:3, 1] = ids[:3, 0]  # duplicate routes of one token merge into one entry
+    weights = bf16_round(rng.uniform(0.05, 1.0, (batch, k)).astype(np.float32))
+    weights[::7] = 0  # finished rows contribute exactly zero
+    x = rng.normal(size=(batch, hidden)).astype(np.float32)
+    got, _, _ = run_layer(cuda_device, raw, "Q6_K", hidden, intermediate, x, ids, weights)
+    expected = moe.expert_ffn(raw["gate"], raw["up"], raw["down"], x, ids, weights, gate_type="Q6_K",
+                              up_type="Q6_K", down_type="Q6_K", hidden=hidden,
+                              intermediate=intermediate)
+    mx, l2 = rel_err(got, expected)
+    assert mx < LAYER_TOL and l2 < 2e-3, (mx, l2)
+    np.testing.assert_array_equal(got[::7], 0)
+
+
+def test_zero_weights_give_zero_and_ids_outside_rank_are_ignored(cuda_device):
+    hidden, intermediate, count = 256, 256, 4
+    rng = np.random.default_rng(3)
+    raw = make_experts(rng, count, hidden, intermediate, "Q6_K")
+    x = rng.normal(size=(5, hidden)).astype(np.float32)
+    ids = np.array([[0, 1]] * 5, np.int32)
+    got, _, _ = run_layer(cuda_device, raw, "Q6_K", hidden, intermediate, x, ids,
+                          np.zeros((5, 2), np.float32))
+    np.testing.assert_array_equal(got, 0)
+    ids = np.array([[7, 9]] * 5, np.int32)  # experts another rank would own
+    got, _, _ = run_layer(cuda_device, raw, "Q6_K", hidden, intermediate, x, ids,
+                          np.full((5, 2), 0.5, np.float32))
+    np.testing.assert_array_equal(got, 0)
+
+
+def test_partial_sums_over_two_expert_ranges_add_up_to_the_layer(cuda_device):
+    """The expert-parallel decomposition (per-rank FP32 partial + all-reduce) on one GPU."""
+    import torch
+
+    from qk_b200.experts import expert_parallel
+    from qk_b200.parallel import put_expert_bytes
+
+    hidden, intermediate, count, k = 512, 256, 8, 3
+    rng = np.random.default_rng(9)
+    raw = make_experts(rng, count, hidden, intermediate, "Q6_K")
+    x = rng.normal(size=(11, hidden)).astype(np.float32)
+    ids = np.stack([rng.permutation(count)[:k] for _ in range(11)]).astype(np.int32)
+    weights = bf16_round(rng.uniform(0.1, 1, (11, k)).astype(np.float32))
+    fn = expert_parallel(gate_type="Q6_K", up_type="Q6_K", down_type="Q6_K", hidden=hidden,
+                         intermediate=intermediate)
+    xs, ids_t, w_t = bf16_tensor(x, cuda_device), torch.from_numpy(ids).to(cuda_device), bf16_tensor(weights, cuda_device)
+    total = None
+    for rank in range(2):
+        dev = {kd: put_expert_bytes(v, kd, "Q6_K", hidden, intermediate, rank=rank, world=2,
+                                    device=cuda_device) for kd, v in raw.items()}
+        part = fn.partial(dev["gate"], dev["up"], dev["down"], xs, ids_t, w_t, first_expert=rank * 4)
+        expected = moe.expert_ffn(raw["gate"][rank * 4:(rank + 1) * 4], raw["up"][rank * 4:(rank + 1) * 4],
+                                  raw["down"][rank * 4:(rank + 1) * 4], x, ids, weights,
+                                  gate_type="Q6_K", up_type="Q6_K", down_type="Q6_K", hidden=hidden,
+                                  intermediate=intermediate, first_expert=rank * 4, partial=True)
+        mx, _ = rel_err(part.cpu().numpy(), expected)
+        assert mx < LAYER_TOL
+        total = part if total is None else total + part
+    full = moe.expert_ffn(raw["gate"], raw["up"], raw["down"], x, ids, weights, gate_type="Q6_K",
+                          up_type="Q6_K", down_type="Q6_K", hidden=hidden, intermediate=intermediate)
+    mx, _ = rel_err(bf16_round(total.cpu().numpy()), full)
+    assert mx < LAYER_TOL
+
+
+def test_contract_errors(cuda_device):
+    from qk_b200.experts import expert_parallel
+
+    with pytest.raises(ValueError, match="compute policy"):
+        expert_parallel(gate_type="Q6_K", up_type="Q6_K", down_type="Q6_K", hidden=256,
+                        intermediate=256, compute="fp8")
+    with pytest.raises(ValueError, match="row tile"):
+        expert_parallel(gate_type="Q6_K", up_type="Q6_K", down_type="Q6_K", hidden=256,
+                        intermediate=256, row_tile=0)
+    with pytest.raises(ValueError):
+        expert_parallel(gate_type="Q6_K", up_type="Q6_K", down_type="Q8_0", hidden=256,
+                        intermediate=256)
