@@ -320,6 +320,9 @@ def b200_arm(args):
         ws = fn.workspace(desc, rows, device)
         out = torch.empty((rows, HIDDEN), dtype=torch.bfloat16, device=device)
         events = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+        for e in events:  # torch creates the CUDA event on its first record
+            e.record(stream)
+        torch.cuda.synchronize(device)
         ev_ptrs = (ctypes_void_p * 5)(*[e.cuda_event for e in events]) if profile else None
 
         def step(profiled=False):

@@ -40,21 +40,29 @@ int sm_count() {
 }
 
 int allow_smem(const void* kernel, size_t bytes) {
-  // One flag per (kernel, device): the attribute is per device.
+  // The attribute is per (kernel, device) and is a ceiling: remember the largest value
+  // set so far and raise it when a launch needs more (never lower it).
   static thread_local const void* done_kernel[256];
   static thread_local int done_dev[256];
+  static thread_local size_t done_bytes[256];
   static thread_local int n_done = 0;
+  if (bytes <= 48 * 1024) return QK_OK;  // below the default limit: nothing to opt into
   int dev = 0;
   cudaGetDevice(&dev);
+  int slot = -1;
   for (int i = 0; i < n_done; ++i)
-    if (done_kernel[i] == kernel && done_dev[i] == dev) return QK_OK;
+    if (done_kernel[i] == kernel && done_dev[i] == dev) {
+      if (done_bytes[i] >= bytes) return QK_OK;
+      slot = i;
+    }
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(bytes));
   if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute");
-  if (n_done < 256) {
-    done_kernel[n_done] = kernel;
-    done_dev[n_done] = dev;
-    ++n_done;
+  if (slot < 0 && n_done < 256) slot = n_done++;
+  if (slot >= 0) {
+    done_kernel[slot] = kernel;
+    done_dev[slot] = dev;
+    done_bytes[slot] = bytes;
   }
   return QK_OK;
 }

@@ -198,8 +198,10 @@ __global__ void repack_kernel(const uint8_t* __restrict__ in, uint8_t* __restric
   }
 }
 
-// Decode of the tiled layout through the same fragment decoders the GEMM kernels use.
-template <QType QT>
+// Decode of the tiled layout through the fragment decoders of the GEMM kernels: kExact
+// selects the reference-exact form (signed zeros included), otherwise the fused form the
+// GEMM kernels run (equal values; a zero may carry the other sign).
+template <QType QT, bool kExact>
 __global__ void dequant_tiled_kernel(const uint8_t* __restrict__ tiled, int64_t rows,
                                      int64_t width, int64_t nblk, int out_bf16,
                                      void* __restrict__ out) {
@@ -228,7 +230,7 @@ __global__ void dequant_tiled_kernel(const uint8_t* __restrict__ tiled, int64_t 
   for (int s = 0; s < 16; ++s) {
     st.update(r, c, s);
     uint32_t a[4];
-    tile_fragment<QT>(r, st, s, a);
+    tile_fragment<QT, kExact>(r, st, s, a);
     const int p = T::p0(c, s);
     emit(0, p, a[0]);
     emit(0, p + 2, a[2]);
@@ -303,15 +305,22 @@ int qk_dequantize_tiled(const uint8_t* tiled, int qtype, int64_t rows, int64_t r
                         int out_dtype, void* out, qk_stream_t stream) {
   if (tile_bytes(qtype) == 0) return set_error(QK_ERR_UNSUPPORTED_TYPE, "tiled layout supports Q6_K and Q4_K; got %d", qtype);
   QK_REQUIRE(rows > 0 && row_width > 0, "rows and row_width must be positive");
+  const bool fused = (out_dtype & QK_DECODE_FUSED) != 0;
+  out_dtype &= ~QK_DECODE_FUSED;
   QK_REQUIRE(out_dtype == QK_OUT_F32 || out_dtype == QK_OUT_BF16, "out_dtype must be F32 or BF16");
   QK_REQUIRE(tiled && out, "null pointer");
   const int64_t nblk = (row_width + 255) / 256;
   const int64_t tiles = (rows + 15) / 16 * nblk;
   const unsigned grid = static_cast<unsigned>((tiles + 3) / 4);
-  if (qtype == QK_TYPE_Q6_K)
-    dequant_tiled_kernel<QType::Q6_K><<<grid, 128, 0, as_stream(stream)>>>(tiled, rows, row_width, nblk, out_dtype == QK_OUT_BF16, out);
-  else
-    dequant_tiled_kernel<QType::Q4_K><<<grid, 128, 0, as_stream(stream)>>>(tiled, rows, row_width, nblk, out_dtype == QK_OUT_BF16, out);
+  const int bf = out_dtype == QK_OUT_BF16;
+  cudaStream_t st = as_stream(stream);
+  if (qtype == QK_TYPE_Q6_K) {
+    if (fused) dequant_tiled_kernel<QType::Q6_K, false><<<grid, 128, 0, st>>>(tiled, rows, row_width, nblk, bf, out);
+    else dequant_tiled_kernel<QType::Q6_K, true><<<grid, 128, 0, st>>>(tiled, rows, row_width, nblk, bf, out);
+  } else {
+    if (fused) dequant_tiled_kernel<QType::Q4_K, false><<<grid, 128, 0, st>>>(tiled, rows, row_width, nblk, bf, out);
+    else dequant_tiled_kernel<QType::Q4_K, true><<<grid, 128, 0, st>>>(tiled, rows, row_width, nblk, bf, out);
+  }
   QK_LAUNCHED("dequant_tiled_kernel");
   return QK_OK;
 }

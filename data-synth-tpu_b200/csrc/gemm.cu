@@ -67,8 +67,11 @@ __global__ void __launch_bounds__(kWarps * 32, 1) quant_gemm_kernel(const uint16
       const int m = chunk * kChunk + 8 * j + g;
       rows[j] = (8 * j + g < ntok) ? x + static_cast<int64_t>(m) * K : nullptr;
     }
+    // One fresh FP32 partial sum per 256-value block, added to the running total: keeps
+    // the accumulator small while the MMAs sum, as the reference's per-block dot does.
     float acc[4][4] = {}, unused[4][4];
     for (int kb = 0; kb < nkb; ++kb) {
+      float blk[4][4] = {};
       const uint32_t slot = tc % R;
       if (!mbar_wait_bounded(&bars[slot], (tc / R) & 1)) {
         ok = false;
@@ -77,14 +80,18 @@ __global__ void __launch_bounds__(kWarps * 32, 1) quant_gemm_kernel(const uint16
       const uint8_t* stage = ring + slot * Cfg::kStage;
       const bool safe = ragged && kb == nkb - 1;
       if (safe || (K & 7)) {
-        if (J == 1) proj_stage<QT, false, 1, true>(stage, lane, kb * 256, K, rows, acc, unused);
-        else if (J == 2) proj_stage<QT, false, 2, true>(stage, lane, kb * 256, K, rows, acc, unused);
-        else proj_stage<QT, false, 4, true>(stage, lane, kb * 256, K, rows, acc, unused);
+        if (J == 1) proj_stage<QT, false, 1, true>(stage, lane, kb * 256, K, rows, blk, unused);
+        else if (J == 2) proj_stage<QT, false, 2, true>(stage, lane, kb * 256, K, rows, blk, unused);
+        else proj_stage<QT, false, 4, true>(stage, lane, kb * 256, K, rows, blk, unused);
       } else {
-        if (J == 1) proj_stage<QT, false, 1, false>(stage, lane, kb * 256, K, rows, acc, unused);
-        else if (J == 2) proj_stage<QT, false, 2, false>(stage, lane, kb * 256, K, rows, acc, unused);
-        else proj_stage<QT, false, 4, false>(stage, lane, kb * 256, K, rows, acc, unused);
+        if (J == 1) proj_stage<QT, false, 1, false>(stage, lane, kb * 256, K, rows, blk, unused);
+        else if (J == 2) proj_stage<QT, false, 2, false>(stage, lane, kb * 256, K, rows, blk, unused);
+        else proj_stage<QT, false, 4, false>(stage, lane, kb * 256, K, rows, blk, unused);
       }
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[j][i] = __fadd_rn(acc[j][i], blk[j][i]);
       ++tc;
       __syncwarp();
       if (lane == 0) fence_proxy_async_smem();

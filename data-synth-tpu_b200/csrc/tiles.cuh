@@ -18,6 +18,11 @@
 //   Q6_K: u = 128 + code (built by byte permute into FP32 bits 0x43000000 | code << 16),
 //         w = fma(u, ds, -160 * ds) = (code - 32) * ds, exact;
 //   Q4_K: w = fma(u, ds, -128 * ds) - dm, the multiply exact, one rounding in the sub.
+// These fused forms give +0 where the reference's (d * sc) * 0 keeps the sign of d * sc;
+// a signed zero cannot change a dot product, so the GEMM kernels use them. The kExact
+// variant (qk_dequantize_tiled) subtracts first and then multiplies, which reproduces
+// the reference bit for bit, signed zeros included: w = (u - 160) * ds for Q6_K and
+// w = (u - 128) * ds - dm for Q4_K.
 #pragma once
 
 #include "common.cuh"
@@ -77,24 +82,36 @@ struct Tile<QType::Q6_K> {
 
   // Four BF16 values of row half rh at k-step s -> two packed pairs.
   // s must fold to a constant (callers fully unroll their k-step loops).
+  template <bool kExact>
   __device__ __forceinline__ static void pairs(const Regs& r, int rh, float2 sc, int s,
                                                uint32_t& lo, uint32_t& hi) {
     const int Q = s >> 2, J4 = s & 3;
     const uint32_t l = (word(r.ql[rh][Q & 1], J4) >> (4 * (Q >> 1))) & 0x0f0f0f0fu;
     const uint32_t h = (word(r.qh[rh], J4) >> (2 * Q)) & 0x03030303u;
     const uint32_t code = l | (h << 4);
-    const float2 ds = make_float2(sc.x, sc.x), nk = make_float2(sc.y, sc.y);
-    const float2 w01 = __ffma2_rn(make_float2(magic128<0>(code), magic128<1>(code)), ds, nk);
-    const float2 w23 = __ffma2_rn(make_float2(magic128<2>(code), magic128<3>(code)), ds, nk);
+    const float2 ds = make_float2(sc.x, sc.x);
+    const float2 u01 = make_float2(magic128<0>(code), magic128<1>(code));
+    const float2 u23 = make_float2(magic128<2>(code), magic128<3>(code));
+    float2 w01, w23;
+    if (kExact) {
+      const float2 off = make_float2(-160.f, -160.f);
+      w01 = __fmul2_rn(__fadd2_rn(u01, off), ds);
+      w23 = __fmul2_rn(__fadd2_rn(u23, off), ds);
+    } else {
+      const float2 nk = make_float2(sc.y, sc.y);
+      w01 = __ffma2_rn(u01, ds, nk);
+      w23 = __ffma2_rn(u23, ds, nk);
+    }
     lo = pack_bf16x2(w01.x, w01.y);
     hi = pack_bf16x2(w23.x, w23.y);
   }
 
   // A fragment of k-step s. `sc[rh]` must hold scale(r, rh, s >> 2).
+  template <bool kExact = false>
   __device__ __forceinline__ static void fragment(const Regs& r, const float2 (&sc)[2], int s,
                                                   uint32_t (&a)[4]) {
-    pairs(r, 0, sc[0], s, a[0], a[2]);
-    pairs(r, 1, sc[1], s, a[1], a[3]);
+    pairs<kExact>(r, 0, sc[0], s, a[0], a[2]);
+    pairs<kExact>(r, 1, sc[1], s, a[1], a[3]);
   }
 
 };
@@ -153,24 +170,36 @@ struct Tile<QType::Q4_K> {
     return make_float4(ds, __fmul_rn(ds, -128.f), __fmul_rn(dmin, static_cast<float>(m)), 0.f);
   }
 
+  template <bool kExact>
   __device__ __forceinline__ static void pairs(const Regs& r, int rh, float4 sc, int s,
                                                uint32_t& lo, uint32_t& hi) {
     const int NIB = s >> 3, HALF = (s >> 2) & 1, J4 = s & 3;
     const uint32_t code = (word(r.qs[rh][HALF], J4) >> (4 * NIB)) & 0x0f0f0f0fu;
-    const float2 ds = make_float2(sc.x, sc.x), nk = make_float2(sc.y, sc.y);
+    const float2 ds = make_float2(sc.x, sc.x);
     const float2 dm = make_float2(-sc.z, -sc.z);
-    float2 w01 = __ffma2_rn(make_float2(magic128<0>(code), magic128<1>(code)), ds, nk);
-    float2 w23 = __ffma2_rn(make_float2(magic128<2>(code), magic128<3>(code)), ds, nk);
+    const float2 u01 = make_float2(magic128<0>(code), magic128<1>(code));
+    const float2 u23 = make_float2(magic128<2>(code), magic128<3>(code));
+    float2 w01, w23;
+    if (kExact) {
+      const float2 off = make_float2(-128.f, -128.f);
+      w01 = __fmul2_rn(__fadd2_rn(u01, off), ds);
+      w23 = __fmul2_rn(__fadd2_rn(u23, off), ds);
+    } else {
+      const float2 nk = make_float2(sc.y, sc.y);
+      w01 = __ffma2_rn(u01, ds, nk);
+      w23 = __ffma2_rn(u23, ds, nk);
+    }
     w01 = __fadd2_rn(w01, dm);
     w23 = __fadd2_rn(w23, dm);
     lo = pack_bf16x2(w01.x, w01.y);
     hi = pack_bf16x2(w23.x, w23.y);
   }
 
+  template <bool kExact = false>
   __device__ __forceinline__ static void fragment(const Regs& r, const float4 (&sc)[2], int s,
                                                   uint32_t (&a)[4]) {
-    pairs(r, 0, sc[0], s, a[0], a[2]);
-    pairs(r, 1, sc[1], s, a[1], a[3]);
+    pairs<kExact>(r, 0, sc[0], s, a[0], a[2]);
+    pairs<kExact>(r, 1, sc[1], s, a[1], a[3]);
   }
 };
 
@@ -200,10 +229,10 @@ struct ScaleState<QType::Q4_K> {
 };
 
 // Decode the A fragment of k-step s with a scale state already updated for s.
-template <QType QT>
+template <QType QT, bool kExact = false>
 __device__ __forceinline__ void tile_fragment(const typename Tile<QT>::Regs& r,
                                               const ScaleState<QT>& st, int s, uint32_t (&a)[4]) {
-  Tile<QT>::fragment(r, st.v, s, a);
+  Tile<QT>::template fragment<kExact>(r, st.v, s, a);
 }
 
 }  // namespace qk

@@ -23,6 +23,7 @@ QK_ERR_WORKSPACE = 6
 
 QK_OUT_F32 = 0
 QK_OUT_BF16 = 1
+QK_DECODE_FUSED = 0x100
 
 _p = ctypes.c_void_p
 _i = ctypes.c_int

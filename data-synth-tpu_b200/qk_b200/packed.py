@@ -105,14 +105,19 @@ def unpack_rows(packed):
 unpack_q6 = unpack_rows
 
 
-def dequantize_packed(packed, dtype=torch.bfloat16):
-    """Decode tiles through the GEMM kernels' fragment decoder -> ``[N, K]``."""
+def dequantize_packed(packed, dtype=torch.bfloat16, *, fused=False):
+    """Decode tiles through the GEMM kernels' fragment decoder -> ``[N, K]``.
+
+    ``fused=False`` reproduces the reference bit for bit (signed zeros included);
+    ``fused=True`` runs the fused multiply-add form of the GEMM kernels (same values, a
+    zero may carry the other sign)."""
     out = torch.empty((packed.output_features, packed.input_features), dtype=dtype,
                       device=packed.data.device)
     with torch.cuda.device(packed.data.device):
         _lib.call("qk_dequantize_tiled", _lib.ptr(packed.data), GGML_TYPE[packed.qtype],
                   packed.output_features, packed.input_features,
-                  _lib.QK_OUT_BF16 if dtype == torch.bfloat16 else _lib.QK_OUT_F32,
+                  (_lib.QK_OUT_BF16 if dtype == torch.bfloat16 else _lib.QK_OUT_F32)
+                  | (_lib.QK_DECODE_FUSED if fused else 0),
                   _lib.ptr(out), _lib.stream_handle(packed.data.device))
     return out
 

@@ -50,6 +50,9 @@ enum {
 };
 
 enum { QK_OUT_F32 = 0, QK_OUT_BF16 = 1 };
+/* Flag for qk_dequantize_tiled's out_dtype: decode with the fused multiply-add form the
+ * GEMM kernels run (same values; a zero may carry the other sign). */
+enum { QK_DECODE_FUSED = 0x100 };
 
 /* ---- library ---------------------------------------------------------------- */
 
@@ -79,7 +82,9 @@ int qk_repack_rows(const uint8_t* raw, int qtype, int64_t rows, int64_t row_widt
                    uint8_t* tiled, int32_t* bad_scales, qk_stream_t stream);
 int qk_unpack_rows(const uint8_t* tiled, int qtype, int64_t rows, int64_t row_width,
                    uint8_t* raw, qk_stream_t stream);
-/* Decode of the tiled layout (same values as qk_dequantize_rows on the raw rows). */
+/* Decode of the tiled layout through the GEMM kernels' in-register fragment decoder:
+ * bit-identical to qk_dequantize_rows on the raw rows (signed zeros included), or with
+ * out_dtype | QK_DECODE_FUSED the exact arithmetic the GEMM kernels run. */
 int qk_dequantize_tiled(const uint8_t* tiled, int qtype, int64_t rows, int64_t row_width,
                         int out_dtype, void* out, qk_stream_t stream);
 

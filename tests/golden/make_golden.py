@@ -51,7 +51,9 @@ def load_reference(root):
         raise KeyError(name)
 
     compute = kaggle / "qwen38_tpu" / "compute.py"
+    parallel = kaggle / "qwen38_tpu" / "parallel.py"
     funcs = {
+        "split_expert_bytes": extract(parallel, "split_expert_bytes"),
         "pack_q8": extract(compute, "pack_q8"),
         "numpy_q8_matmul": extract(compute, "numpy_q8_matmul"),
         "scale_oracle": extract(kaggle / "tests" / "test_qwen38_kv_gather.py", "scale_oracle"),
@@ -269,6 +271,32 @@ def q8_golden(funcs):
     np.savez_compressed(HERE / "q8_kv.npz", **out)
 
 
+SPLIT_CASES = (("Q6_K", 256, 512, 2), ("Q8_0", 64, 64, 2), ("Q4_K", 512, 256, 1))
+
+
+def split_inputs(qtype, kind, hidden, inter, block):
+    """Raw expert bytes [3, bytes] for one split case (seeded per case)."""
+    values, size = block
+    rows, width = (hidden, inter) if kind == "down" else (inter, hidden)
+    seed = [101, hidden, inter, ("gate", "up", "down").index(kind), size]
+    return np.random.default_rng(seed).integers(0, 256, (3, rows * (width // values) * size), dtype=np.uint8)
+
+
+def split_golden(quant, funcs):
+    """parallel.py:40-61 split_expert_bytes (its block_layout is quant's): sha256 + shape."""
+    split = funcs["split_expert_bytes"]
+    split.__globals__["block_layout"] = quant.block_layout
+    out = {}
+    for qtype, hidden, inter, tp in SPLIT_CASES:
+        for kind in ("gate", "up", "down"):
+            raw = split_inputs(qtype, kind, hidden, inter, quant.block_layout(qtype))
+            result = np.ascontiguousarray(split(raw, kind, qtype, hidden, inter, tp))
+            tag = f"{qtype}_{kind}_{tp}"
+            out[f"{tag}_shape"] = np.array(result.shape, np.int64)
+            out[f"{tag}_sha256"] = np.frombuffer(hashlib.sha256(result.tobytes()).digest(), np.uint8)
+    np.savez_compressed(HERE / "split_experts.npz", **out)
+
+
 def main():
     root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
     gguf_quant, quant, q6ref, funcs = load_reference(root)
@@ -276,6 +304,7 @@ def main():
     q6_golden(q6ref)
     routing_golden(quant, funcs)
     q8_golden(funcs)
+    split_golden(quant, funcs)
     for path in sorted(HERE.glob("*.npz")):
         print(f"{path.name}: {path.stat().st_size} bytes")
 

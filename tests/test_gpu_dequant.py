@@ -67,6 +67,9 @@ def test_repack_is_lossless_and_fragment_decode_is_bit_exact(cuda_device, qtype,
     expected = bf16_round(gguf.dequantize_rows(raw, qtype, width))
     got = to_f32(dequantize_packed(packed, torch.bfloat16))
     np.testing.assert_array_equal(got.view(np.uint32), expected.view(np.uint32))
+    # the fused form the GEMM kernels run: equal values (a zero may be -0 vs +0)
+    fused = to_f32(dequantize_packed(packed, torch.bfloat16, fused=True))
+    np.testing.assert_array_equal(fused, expected)
 
 
 @pytest.mark.parametrize("scale", [np.inf, -np.inf, np.nan])

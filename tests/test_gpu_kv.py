@@ -42,6 +42,8 @@ def test_write_then_read_matches_reference_and_leaves_inactive_rows(golden, cuda
         got = to_f32(read_quantized(cache, "k", indices, c, dtype))
         expected = np.zeros((2, 4, 2, 256), np.float32)
         expected[0, [0, 2]] = data["read_reconstructed"]
+        if dtype == torch.bfloat16:  # test_qwen38_kv_gather.py:94 expected.astype(dtype)
+            expected = bf16_round(expected)
         np.testing.assert_array_equal(got, expected)
     for name in ("k", "v", "k_scale", "v_scale"):
         assert (cache[name].reshape(2, -1)[1] == 0).all()
