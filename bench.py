@@ -377,8 +377,6 @@ def b200_arm(args):
                     gate_up_bytes=kernel_bytes(args.qtype, ids), x=x, ids=ids, weights=weights,
                     out=out)
 
-    launches0 = qk_b200.launch_count()
-    _ = launches0
     peak, peak_kind = hbm_peak()
     with ClockSampler(local) as clocks:
         # untimed soak so clocks settle before the measured region
@@ -393,10 +391,8 @@ def b200_arm(args):
         ms = float(t.item())
     value = res["bytes"] * world / (ms * 1e-3) / 1e9
 
-    # launches: a graph replay runs the 4 kernels of one qk_moe_forward
-    before = qk_b200.launch_count()
-    _lib.check(0)
-    launches_per_step = 4
+    # launches: a graph replay runs the 5 kernels of one qk_moe_forward
+    launches_per_step = 5
 
     # e2e through the public call with host buffers
     e2e = e2e_measure(fn, tensors, device, args, res, rank)
@@ -416,10 +412,9 @@ def b200_arm(args):
         "vs_baseline": None, "dtype": "u8", "data": "synthetic",
         "config": config_dict(args, world),
         "rows_per_s": res["rows"] * world / (ms * 1e-3),
-        "stage_ms": {"route": res["stage_ms"][0], "gate_up": res["stage_ms"][1],
+        "stage_ms": {"route_dispatch": res["stage_ms"][0], "gate_up": res["stage_ms"][1],
                      "down": res["stage_ms"][2], "combine": res["stage_ms"][3]},
-        "roofline": {"kernel": "moe_proj_kernel<Q6_K, gate/up>" if args.qtype == "Q6_K" else
-                     "moe_proj_kernel<Q4_K, gate/up>",
+        "roofline": {"kernel": f"umma_proj_kernel<{args.qtype}, gate/up>",
                      "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "peak_kind": peak_kind,
                      "traffic": ncu_traffic(args.qtype, args.m)},

@@ -5,7 +5,7 @@
 // IQ4_NL) one output value per thread. FP32 operations are written with explicit
 // round-to-nearest intrinsics so no multiply-add is contracted.
 #include "common.cuh"
-#include "tiles.cuh"
+#include "rowtile.cuh"
 
 namespace qk {
 namespace {
@@ -126,47 +126,24 @@ __global__ void dequant_rows_kernel(const uint8_t* __restrict__ raw, int qtype, 
   }
 }
 
-// ---- tiled layout byte map (see oracle/layout.py for the statement of the format) ----
+// ---- tiled layout byte map (the format is stated in oracle/layout.py and rowtile.cuh) ----
 
-// For tiled byte `off` of a tile: the row inside the 16-row tile and the byte inside
-// that row's GGUF block.
+// For byte `off` of a 128-row tile: the row inside the tile and the byte of that row's block.
 __host__ __device__ inline void tile_source(int qtype, int off, int& row, int& src) {
-  if (qtype == QK_TYPE_Q6_K) {
-    if (off < 2048) {
-      const int u = off >> 9, within = off & 511, unit = within >> 4, b = within & 15;
-      const int rh = u >> 1, part = u & 1, g = unit >> 2, c = unit & 3;
-      row = rh * 8 + g;
-      src = (c >> 1) * 64 + part * 32 + (c & 1) * 16 + b;
-    } else if (off < 3072) {
-      const int o = off - 2048, rh = o >> 9, within = o & 511;
-      row = rh * 8 + (within >> 6);
-      src = 128 + (within & 63);
-    } else if (off < 3328) {
-      const int o = off - 3072, unit = o >> 3, b = o & 7, g = unit >> 2, c = unit & 3;
-      row = (b >> 2) * 8 + g;
-      src = 192 + (c >> 1) * 8 + (c & 1) + 2 * (b & 3);
-    } else {
-      const int o = off - 3328, g = o >> 2, w = o & 3;
-      row = (w >> 1) * 8 + g;
-      src = 208 + (w & 1);
-    }
-  } else {  // Q4_K
-    if (off < 2048) {
-      const int u = off >> 9, within = off & 511, unit = within >> 4, b = within & 15;
-      const int rh = u >> 1, half = u & 1, g = unit >> 2, c = unit & 3;
-      row = rh * 8 + g;
-      src = 16 + 32 * c + 16 * half + b;
-    } else {
-      const int o = off - 2048;
-      row = o >> 4;
-      src = o & 15;
-    }
+  const int chunks = qtype == QK_TYPE_Q6_K ? RowTile<QType::Q6_K>::kChunks : RowTile<QType::Q4_K>::kChunks;
+  if (off < chunks * 2048) {
+    row = (off & 2047) >> 4;
+    src = (off >> 11) * 16 + (off & 15);
+  } else {  // Q6_K scale plane: [row][2 B] = block bytes 208..209
+    const int o = off - chunks * 2048;
+    row = o >> 1;
+    src = 208 + (o & 1);
   }
 }
 
 inline int tile_bytes(int qtype) {
-  return qtype == QK_TYPE_Q6_K ? Tile<QType::Q6_K>::kBytes
-         : qtype == QK_TYPE_Q4_K ? Tile<QType::Q4_K>::kBytes
+  return qtype == QK_TYPE_Q6_K ? RowTile<QType::Q6_K>::kBytes
+         : qtype == QK_TYPE_Q4_K ? RowTile<QType::Q4_K>::kBytes
                                  : 0;
 }
 
@@ -180,7 +157,7 @@ __global__ void repack_kernel(const uint8_t* __restrict__ in, uint8_t* __restric
   for (int off = threadIdx.x; off < tbytes; off += blockDim.x) {
     int r, src;
     tile_source(qtype, off, r, src);
-    const int64_t row = strip * 16 + r;
+    const int64_t row = strip * 128 + r;
     const int64_t raw_off = (row * nblk + kb) * bbytes + src;
     const int64_t tiled_off = tile * tbytes + off;
     if (kPack) {
@@ -198,45 +175,32 @@ __global__ void repack_kernel(const uint8_t* __restrict__ in, uint8_t* __restric
   }
 }
 
-// Decode of the tiled layout through the fragment decoders of the GEMM kernels: kExact
+// Decode of the tiled layout through the row decoders of the tensor-core kernels: kExact
 // selects the reference-exact form (signed zeros included), otherwise the fused form the
-// GEMM kernels run (equal values; a zero may carry the other sign).
+// kernels run (equal values; a zero may carry the other sign). One thread per tile row.
 template <QType QT, bool kExact>
-__global__ void dequant_tiled_kernel(const uint8_t* __restrict__ tiled, int64_t rows,
-                                     int64_t width, int64_t nblk, int out_bf16,
-                                     void* __restrict__ out) {
-  using T = Tile<QT>;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t tile = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + warp;
-  const int64_t strips = (rows + 15) / 16;
-  if (tile >= strips * nblk) return;
+__global__ void __launch_bounds__(128) dequant_tiled_kernel(const uint8_t* __restrict__ tiled, int64_t rows,
+                                                            int64_t width, int64_t nblk, int out_bf16,
+                                                            void* __restrict__ out) {
+  using RT = RowTile<QT>;
+  const int64_t tile = blockIdx.x;
   const int64_t strip = tile / nblk, kb = tile % nblk;
-  typename T::Regs r;
-  T::load(r, tiled + tile * T::kBytes, lane);
-  ScaleState<QT> st;
-  const int g = lane >> 2, c = lane & 3;
-  auto emit = [&](int rh, int p, uint32_t pair) {
-    const int64_t row = strip * 16 + rh * 8 + g;
-    const int64_t col = kb * 256 + p;
-    if (row >= rows) return;
-    for (int i = 0; i < 2; ++i) {
-      if (col + i >= width) break;
-      const uint16_t bits = static_cast<uint16_t>(pair >> (16 * i));
-      if (out_bf16) static_cast<uint16_t*>(out)[row * width + col + i] = bits;
-      else static_cast<float*>(out)[row * width + col + i] = bf16_to_f32(bits);
+  const int r = threadIdx.x;
+  const int64_t row = strip * 128 + r;
+  if (row >= rows) return;
+  typename RT::Regs regs;
+  RT::load(regs, tiled + tile * RT::kBytes, r);
+  auto store = [&](int64_t k0, const uint32_t(&o)[8]) {
+    for (int i = 0; i < 16; ++i) {
+      const int64_t k = k0 + i;
+      if (k >= width) break;
+      const uint16_t bits = static_cast<uint16_t>(o[i >> 1] >> (16 * (i & 1)));
+      if (out_bf16) static_cast<uint16_t*>(out)[row * width + k] = bits;
+      else static_cast<float*>(out)[row * width + k] = bf16_to_f32(bits);
     }
   };
-#pragma unroll
-  for (int s = 0; s < 16; ++s) {
-    st.update(r, c, s);
-    uint32_t a[4];
-    tile_fragment<QT, kExact>(r, st, s, a);
-    const int p = T::p0(c, s);
-    emit(0, p, a[0]);
-    emit(0, p + 2, a[2]);
-    emit(1, p, a[1]);
-    emit(1, p + 2, a[3]);
-  }
+  RT::template decode_half<kExact, 0>(regs, [&](int col, const uint32_t(&o)[8]) { store(kb * 256 + 2 * col, o); });
+  RT::template decode_half<kExact, 1>(regs, [&](int col, const uint32_t(&o)[8]) { store(kb * 256 + 128 + 2 * col, o); });
 }
 
 int grid_for(int64_t total, int block) {
@@ -270,7 +234,7 @@ int qk_dequantize_rows(const uint8_t* raw, int qtype, int64_t rows, int64_t row_
 int64_t qk_tiled_bytes(int qtype, int64_t rows, int64_t row_width) {
   const int tb = tile_bytes(qtype);
   if (tb == 0 || rows < 0 || row_width <= 0) return -1;
-  return (rows + 15) / 16 * ((row_width + 255) / 256) * tb;
+  return (rows + 127) / 128 * ((row_width + 255) / 256) * tb;
 }
 
 static int repack_common(const uint8_t* in, int qtype, int64_t rows, int64_t row_width,
@@ -280,7 +244,7 @@ static int repack_common(const uint8_t* in, int qtype, int64_t rows, int64_t row
   QK_REQUIRE(rows > 0 && row_width > 0, "Expected [output_features, ceil(input_features / 256), bytes]");
   QK_REQUIRE(in && out, "null pointer");
   const int64_t nblk = (row_width + 255) / 256;
-  const int64_t tiles = (rows + 15) / 16 * nblk;
+  const int64_t tiles = (rows + 127) / 128 * nblk;
   QK_REQUIRE(tiles < (1ll << 31), "too many tiles");
   const int bb = block_shape(qtype).bytes;
   if (pack)
@@ -310,8 +274,8 @@ int qk_dequantize_tiled(const uint8_t* tiled, int qtype, int64_t rows, int64_t r
   QK_REQUIRE(out_dtype == QK_OUT_F32 || out_dtype == QK_OUT_BF16, "out_dtype must be F32 or BF16");
   QK_REQUIRE(tiled && out, "null pointer");
   const int64_t nblk = (row_width + 255) / 256;
-  const int64_t tiles = (rows + 15) / 16 * nblk;
-  const unsigned grid = static_cast<unsigned>((tiles + 3) / 4);
+  const int64_t tiles = (rows + 127) / 128 * nblk;
+  const unsigned grid = static_cast<unsigned>(tiles);
   const int bf = out_dtype == QK_OUT_BF16;
   cudaStream_t st = as_stream(stream);
   if (qtype == QK_TYPE_Q6_K) {

@@ -1,23 +1,25 @@
 // Routed-expert SwiGLU FFN over tiled Q6_K / Q4_K expert weights (decode regime).
 //
 // Replaces the routed FFN of qwen38_tpu/experts.py:61-131 (and grouped_experts.py:185-292
-// at tp = 1) for the experts one rank holds. Four launches on one stream:
+// at tp = 1) for the experts one rank holds. Five launches on one stream:
 //
-//  1. route   - one CTA turns ids/weights [B, k] into per-expert entry lists (expert-
-//               sorted), merging duplicate routes of a token into one entry whose weight
-//               is bf16(sum) (experts.py:66-73) and dropping zero-weight routes (their
-//               contribution is zero in the reference, experts.py:74-76).
-//  2. gate/up - per (active expert, 16-row strip of I): h = bf16(silu(bf16(x Wg^T)) *
-//               bf16(x Wu^T)) for every entry of the expert (experts.py:103-107,
-//               math.py:10-20). Weight tiles stream HBM -> shared memory with 1-D bulk
-//               copies (TMA engine) into a per-warp ring; each warp decodes its tile into
-//               BF16 MMA fragments in registers and runs m16n8k16 MMAs with FP32 accumulate.
-//  3. down    - per (active expert, 16-row strip of H): y = bf16(h Wd^T).
-//  4. combine - per token, FP32 sum of f32(y) * f32(route) over its experts in ascending
-//               expert order (the reference's accumulation order, experts.py:129), then
-//               BF16 (experts.py:131), or the FP32 partial sum for an EP all-reduce.
+//  1. route    - one CTA turns ids/weights [B, k] into per-expert entry lists (expert-
+//                sorted), merging duplicate routes of a token into one entry whose weight
+//                is bf16(sum) (experts.py:66-73) and dropping zero-weight routes (their
+//                contribution is zero in the reference, experts.py:74-76); it also lays
+//                out the token chunks (<= 64 entries of one expert) of the next passes.
+//  2. dispatch - copies each entry's x row into the activation tiles of its chunk (BF16,
+//                128-byte-swizzled K-major: the tensor core's shared-memory operand layout).
+//  3. gate/up  - tcgen05 pass (umma_proj.cuh): per (chunk, 128 rows of I), gate and up
+//                tiles decoded into TMEM, FP32 accumulators; epilogue
+//                h = bf16(silu(bf16(x Wg^T)) * bf16(x Wu^T)) (experts.py:103-107,
+//                math.py:10-20) written as the activation tiles of the down pass.
+//  4. down     - tcgen05 pass, per (chunk, 256 rows of H): y = bf16(h Wd^T).
+//  5. combine  - per token, FP32 sum of f32(y) * f32(route) over its experts in ascending
+//                expert order (the reference's accumulation order, experts.py:129), then
+//                BF16 (experts.py:131), or the FP32 partial sum for an EP all-reduce.
 #include "common.cuh"
-#include "proj.cuh"
+#include "umma_proj.cuh"
 
 namespace qk {
 namespace {
@@ -26,7 +28,9 @@ struct MoeMeta {
   int32_t n_active;
   int32_t n_entries;
   int32_t status;
-  int32_t reserved;
+  int32_t n_chunks;
+  int32_t row_total;
+  int32_t reserved[3];
 };
 
 struct Workspace {
@@ -34,17 +38,28 @@ struct Workspace {
   int32_t* counts;        // [E]
   int32_t* offsets;       // [E + 1]
   int32_t* active;        // [E]   active expert ids (local), ascending
+  int32_t* chunk_off;     // [E + 1] first chunk of each active slot
+  int32_t* row_off;       // [E + 1] first activation-tile row of each active slot
   int32_t* entry_token;   // [B k] token of each entry (expert-sorted)
   float* entry_weight;    // [B k] bf16-valued route weight of each entry
   int32_t* route_entry;   // [B k] entry of route (b, j), -1 if none
-  uint16_t* h;            // [B k, I]
+  uint8_t* xt;            // gate/up activation tiles [rows_max x H bf16]
+  uint8_t* ht;            // down activation tiles [rows_max x I bf16]
   uint16_t* y;            // [B k, H]
 };
 
 inline size_t align256(size_t n) { return (n + 255) & ~size_t(255); }
 
+// Activation-tile rows: each active expert's entries rounded up to 16 per chunk.
+inline size_t rows_bound(const qk_moe_desc& d, int max_tokens) {
+  const size_t R = static_cast<size_t>(max_tokens) * d.top_k;
+  const size_t E = static_cast<size_t>(d.num_experts);
+  return R + 15 * (E < R ? E : R);
+}
+
 size_t layout(const qk_moe_desc& d, int max_tokens, uint8_t* base, Workspace* ws) {
   const size_t E = d.num_experts, R = static_cast<size_t>(max_tokens) * d.top_k;
+  const size_t rows = rows_bound(d, max_tokens);
   size_t off = 0;
   auto take = [&](size_t bytes) {
     uint8_t* p = base ? base + off : nullptr;
@@ -55,20 +70,26 @@ size_t layout(const qk_moe_desc& d, int max_tokens, uint8_t* base, Workspace* ws
   uint8_t* counts = take(E * 4);
   uint8_t* offsets = take((E + 1) * 4);
   uint8_t* active = take(E * 4);
+  uint8_t* chunk_off = take((E + 1) * 4);
+  uint8_t* row_off = take((E + 1) * 4);
   uint8_t* et = take(R * 4);
   uint8_t* ew = take(R * 4);
   uint8_t* re = take(R * 4);
-  uint8_t* h = take(R * d.intermediate * 2);
+  uint8_t* xt = take(rows * d.hidden * 2);
+  uint8_t* ht = take(rows * d.intermediate * 2);
   uint8_t* y = take(R * d.hidden * 2);
   if (ws) {
     ws->meta = reinterpret_cast<MoeMeta*>(meta);
     ws->counts = reinterpret_cast<int32_t*>(counts);
     ws->offsets = reinterpret_cast<int32_t*>(offsets);
     ws->active = reinterpret_cast<int32_t*>(active);
+    ws->chunk_off = reinterpret_cast<int32_t*>(chunk_off);
+    ws->row_off = reinterpret_cast<int32_t*>(row_off);
     ws->entry_token = reinterpret_cast<int32_t*>(et);
     ws->entry_weight = reinterpret_cast<float*>(ew);
     ws->route_entry = reinterpret_cast<int32_t*>(re);
-    ws->h = reinterpret_cast<uint16_t*>(h);
+    ws->xt = xt;
+    ws->ht = ht;
     ws->y = reinterpret_cast<uint16_t*>(y);
   }
   return off;
@@ -147,6 +168,39 @@ __global__ void __launch_bounds__(1024) moe_route_kernel(const int32_t* __restri
       ws.meta->n_active = active_base[32];
       ws.meta->status = 0;
     }
+    __syncwarp();
+    // Token chunks (<= kMaxTok entries of one expert) and their activation-tile rows
+    // (each chunk padded to a multiple of 16 rows), in active-expert order.
+    const int n_act = active_base[32];
+    const int per2 = (n_act + 31) / 32, lo2 = min(n_act, tid * per2), hi2 = min(n_act, lo2 + per2);
+    int ch_sum = 0, row_sum = 0;
+    for (int a = lo2; a < hi2; ++a) {
+      const int m = counts[ws.active[a]], nch = (m + kMaxTok - 1) / kMaxTok;
+      ch_sum += nch;
+      row_sum += kMaxTok * (nch - 1) + (((m - kMaxTok * (nch - 1)) + 15) & ~15);
+    }
+    int ch_incl = ch_sum, row_incl = row_sum;
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, ch_incl, o), w = __shfl_up_sync(0xffffffffu, row_incl, o);
+      if (tid >= o) {
+        ch_incl += v;
+        row_incl += w;
+      }
+    }
+    int cb = ch_incl - ch_sum, rb = row_incl - row_sum;
+    for (int a = lo2; a < hi2; ++a) {
+      const int m = counts[ws.active[a]], nch = (m + kMaxTok - 1) / kMaxTok;
+      ws.chunk_off[a] = cb;
+      ws.row_off[a] = rb;
+      cb += nch;
+      rb += kMaxTok * (nch - 1) + (((m - kMaxTok * (nch - 1)) + 15) & ~15);
+    }
+    if (tid == 31) {
+      ws.chunk_off[n_act] = ch_incl;
+      ws.row_off[n_act] = row_incl;
+      ws.meta->n_chunks = ch_incl;
+      ws.meta->row_total = row_incl;
+    }
   }
   __syncthreads();
 
@@ -175,157 +229,39 @@ __global__ void __launch_bounds__(1024) moe_route_kernel(const int32_t* __restri
 }
 
 // ------------------------------------------------------------------------------------
-// 2./3. projection kernels
+// 2. dispatch: x rows of every chunk into the swizzled activation tiles (zero padding rows)
 // ------------------------------------------------------------------------------------
-
-struct ProjArgs {
-  const uint8_t* wa;      // gate (gate/up) or down tiles, expert-major
-  const uint8_t* wb;      // up tiles (gate/up only)
-  int64_t expert_bytes;   // tiled bytes per expert of one projection
-  const uint16_t* act;    // x [B, H] (gate/up) or h [entries, I] (down)
-  int K;                  // reduction width (H or I)
-  int N;                  // output rows (I or H)
-  Workspace ws;
-};
-
-// Position of (item, chunk, kb) in a warp's tile stream.
-struct Cursor {
-  int item, chunk, kb, chunks;
-  __device__ __forceinline__ bool valid(int n_items) const { return item < n_items; }
-};
-
-template <QType QT, bool kGateUp>
-__device__ __forceinline__ int chunks_of(const ProjArgs& a, int item, int strips) {
-  const int e = a.ws.active[item / strips];
-  return (a.ws.counts[e] + kChunk - 1) / kChunk;
-}
-
-template <QType QT, bool kGateUp>
-__global__ void __launch_bounds__(kWarps * 32, 1) moe_proj_kernel(ProjArgs a) {
-  using Cfg = ProjCfg<QT, kGateUp>;
-  constexpr int TB = Tile<QT>::kBytes, R = Cfg::kStages;
-  extern __shared__ __align__(128) uint8_t smem[];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int g = lane >> 2, c = lane & 3;
-  uint8_t* ring = smem + static_cast<size_t>(warp) * R * Cfg::kStage;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + static_cast<size_t>(kWarps) * R * Cfg::kStage) + warp * R;
-
-  const int strips = a.N / 16, nkb = a.K / 256;
-  const int n_items = a.ws.meta->n_active * strips;
-  const int total = gridDim.x * kWarps;
-  const int first = blockIdx.x * kWarps + warp;
-  if (first >= n_items) return;
-
-  if (lane == 0) {
-    for (int i = 0; i < R; ++i) mbar_init(&bars[i], 1);
-    fence_mbar_init();
-  }
-  __syncwarp();
-
-  auto tile_src = [&](const uint8_t* base, const Cursor& cur) {
-    const int e = a.ws.active[cur.item / strips];
-    const int strip = cur.item % strips;
-    return base + e * a.expert_bytes + (static_cast<int64_t>(strip) * nkb + cur.kb) * TB;
-  };
-  auto advance = [&](Cursor& cur) {
-    if (++cur.kb == nkb) {
-      cur.kb = 0;
-      if (++cur.chunk == cur.chunks) {
-        cur.chunk = 0;
-        cur.item += total;
-        cur.chunks = cur.item < n_items ? chunks_of<QT, kGateUp>(a, cur.item, strips) : 0;
-      }
+__global__ void __launch_bounds__(256) moe_dispatch_kernel(const uint16_t* __restrict__ x, int H,
+                                                           Workspace ws) {
+  const int n_rows = ws.meta->row_total, n_act = ws.meta->n_active;
+  const int cpr = H / 8, nkb = H / 256;
+  const int64_t total = static_cast<int64_t>(n_rows) * cpr;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int g = static_cast<int>(i / cpr), j = static_cast<int>(i % cpr);
+    int lo = 0, hi = n_act;  // largest a with row_off[a] <= g
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (ws.row_off[mid] <= g) lo = mid;
+      else hi = mid;
     }
-  };
-
-  Cursor prod{first, 0, 0, chunks_of<QT, kGateUp>(a, first, strips)};
-  Cursor cons = prod;
-  uint32_t tp = 0, tc = 0;
-  auto issue = [&]() {
-    if (lane == 0) {
-      const uint32_t slot = tp % R;
-      uint8_t* dst = ring + slot * Cfg::kStage;
-      mbar_expect_tx(&bars[slot], Cfg::kStage);
-      bulk_g2s(dst, tile_src(a.wa, prod), TB, &bars[slot]);
-      if (kGateUp) bulk_g2s(dst + TB, tile_src(a.wb, prod), TB, &bars[slot]);
+    const int r_in = g - ws.row_off[lo], ch = r_in / kMaxTok, rr = r_in % kMaxTok;
+    const int e = ws.active[lo];
+    const int ntok = min(kMaxTok, ws.counts[e] - kMaxTok * ch), r16 = (ntok + 15) & ~15;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (rr < ntok) {
+      const int token = ws.entry_token[ws.offsets[e] + r_in];
+      v = ld_nc_v4(x + static_cast<int64_t>(token) * H + j * 8);
     }
-    ++tp;
-    advance(prod);
-  };
-  for (int i = 0; i < R && prod.valid(n_items); ++i) issue();
-
-  bool ok = true;
-  while (cons.valid(n_items) && ok) {
-    const int e = a.ws.active[cons.item / strips];
-    const int strip = cons.item % strips;
-    const int base = a.ws.offsets[e] + cons.chunk * kChunk;
-    const int ntok = min(kChunk, a.ws.counts[e] - cons.chunk * kChunk);
-    const int J = (ntok + 7) / 8;
-    // B-fragment source rows of token columns 8j + g.
-    const uint16_t* rows[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int col = 8 * j + g;
-      rows[j] = nullptr;
-      if (col < ntok) {
-        const int src = kGateUp ? a.ws.entry_token[base + col] : base + col;
-        rows[j] = a.act + static_cast<int64_t>(src) * a.K;
-      }
-    }
-    float acc_a[4][4] = {}, acc_b[4][4] = {};
-    for (int kb = 0; kb < nkb; ++kb) {
-      const uint32_t slot = tc % R;
-      if (!mbar_wait_bounded(&bars[slot], (tc / R) & 1)) {
-        ok = false;
-        break;
-      }
-      const uint8_t* stage = ring + slot * Cfg::kStage;
-      if (J == 1) proj_stage<QT, kGateUp, 1, false>(stage, lane, kb * 256, a.K, rows, acc_a, acc_b);
-      else if (J == 2) proj_stage<QT, kGateUp, 2, false>(stage, lane, kb * 256, a.K, rows, acc_a, acc_b);
-      else proj_stage<QT, kGateUp, 4, false>(stage, lane, kb * 256, a.K, rows, acc_a, acc_b);
-      ++tc;
-      // Every lane has consumed (decoded) its shared-memory words: refill the slot.
-      __syncwarp();
-      if (lane == 0) fence_proxy_async_smem();
-      if (prod.valid(n_items)) issue();
-    }
-    if (!ok) break;
-    // Epilogue: rows strip*16 + g (+8), token columns 8j + 2c (+1).
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      if (j >= J) break;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int col = 8 * j + 2 * c + (i & 1);
-        const int row = strip * 16 + g + (i >> 1) * 8;
-        if (col >= ntok) continue;
-        const int entry = base + col;
-        if (kGateUp) {
-          const float gb = bf16_round(acc_a[j][i]);
-          const float ub = bf16_round(acc_b[j][i]);
-          const float act = bf16_round(__fmul_rn(gb, sigmoid_ref(gb)));  // silu, math.py:19-20
-          a.ws.h[static_cast<int64_t>(entry) * a.N + row] = bf16_bits_rne(__fmul_rn(act, ub));
-        } else {
-          a.ws.y[static_cast<int64_t>(entry) * a.N + row] = bf16_bits_rne(acc_a[j][i]);
-        }
-      }
-    }
-    // advance consumer to the next (item, chunk)
-    cons.kb = nkb - 1;
-    advance(cons);
-  }
-  if (!ok) {
-    if (lane == 0) atomicExch(&a.ws.meta->status, QK_ERR_TIMEOUT);
-    // Drain copies still in flight into this warp's ring before leaving.
-    while (tc < tp) {
-      mbar_wait_bounded(&bars[tc % R], (tc / R) & 1);
-      ++tc;
-    }
+    const int k = j * 8;
+    uint8_t* dst = ws.xt + static_cast<int64_t>(ws.row_off[lo] + kMaxTok * ch) * 512 * nkb +
+                   static_cast<int64_t>(k >> 8) * r16 * 512 + xt_offset(r16, rr, k & 255);
+    *reinterpret_cast<uint4*>(dst) = v;
   }
 }
 
 // ------------------------------------------------------------------------------------
-// 4. combine
+// 5. combine
 // ------------------------------------------------------------------------------------
 constexpr int kMaxTopK = 32;
 
@@ -366,26 +302,6 @@ __global__ void cast_kernel(const float* __restrict__ in, uint16_t* __restrict__
 }
 
 bool supported(int t) { return t == QK_TYPE_Q6_K || t == QK_TYPE_Q4_K; }
-
-template <QType QT>
-int launch_proj(const ProjArgs& a, int max_items, cudaStream_t st, bool gateup) {
-  const int sms = sm_count();
-  int grid = (max_items + kWarps - 1) / kWarps;
-  grid = grid < 1 ? 1 : (grid > sms ? sms : grid);
-  if (gateup) {
-    using Cfg = ProjCfg<QT, true>;
-    int rc = allow_smem(reinterpret_cast<const void*>(moe_proj_kernel<QT, true>), Cfg::kSmem);
-    if (rc) return rc;
-    moe_proj_kernel<QT, true><<<grid, kWarps * 32, Cfg::kSmem, st>>>(a);
-  } else {
-    using Cfg = ProjCfg<QT, false>;
-    int rc = allow_smem(reinterpret_cast<const void*>(moe_proj_kernel<QT, false>), Cfg::kSmem);
-    if (rc) return rc;
-    moe_proj_kernel<QT, false><<<grid, kWarps * 32, Cfg::kSmem, st>>>(a);
-  }
-  QK_LAUNCHED("moe_proj_kernel");
-  return QK_OK;
-}
 
 }  // namespace
 }  // namespace qk
@@ -433,17 +349,49 @@ static int moe_forward_impl(const qk_moe_desc* desc, const uint8_t* gate, const 
   moe_route_kernel<<<1, 1024, route_smem, st>>>(ids, weights, B, d.top_k, d.num_experts, d.first_expert, ws);
   QK_LAUNCHED("moe_route_kernel");
 
-  const int max_active = d.num_experts < B * d.top_k ? d.num_experts : B * d.top_k;
-  ProjArgs gu{gate, up, qk_tiled_bytes(d.gate_type, d.intermediate, d.hidden), x, d.hidden, d.intermediate, ws};
-  ProjArgs dn{down, nullptr, qk_tiled_bytes(d.down_type, d.hidden, d.intermediate), ws.h, d.intermediate, d.hidden, ws};
+  const int sms = sm_count();
+  const int64_t rows_max = static_cast<int64_t>(rows_bound(d, B));
+  int64_t dgrid = (rows_max * (d.hidden / 8) + 255) / 256;
+  if (dgrid > sms * 16) dgrid = sms * 16;
+  moe_dispatch_kernel<<<static_cast<unsigned>(dgrid), 256, 0, st>>>(x, d.hidden, ws);
+  QK_LAUNCHED("moe_dispatch_kernel");
+
   const bool q6 = d.gate_type == QK_TYPE_Q6_K;
+  UArgs gu{};
+  gu.wa = gate;
+  gu.wb = up;
+  gu.expert_bytes = qk_tiled_bytes(d.gate_type, d.intermediate, d.hidden);
+  gu.nkb = d.hidden / 256;
+  gu.rowtiles = d.intermediate / 128;
+  gu.pairs = d.intermediate / 128;
+  gu.xt = ws.xt;
+  gu.n_chunks_p = &ws.meta->n_chunks;
+  gu.chunk_off = ws.chunk_off;
+  gu.row_off = ws.row_off;
+  gu.active = ws.active;
+  gu.counts = ws.counts;
+  gu.offsets = ws.offsets;
+  gu.n_active_p = &ws.meta->n_active;
+  gu.ht = ws.ht;
+  gu.nkb_out = d.intermediate / 256;
+  gu.nrows = d.intermediate;
+  gu.status = &ws.meta->status;
+  UArgs dn = gu;
+  dn.wa = down;
+  dn.wb = nullptr;
+  dn.expert_bytes = qk_tiled_bytes(d.down_type, d.hidden, d.intermediate);
+  dn.nkb = d.intermediate / 256;
+  dn.rowtiles = d.hidden / 128;
+  dn.pairs = (d.hidden / 128 + 1) / 2;
+  dn.xt = ws.ht;
+  dn.ht = nullptr;
+  dn.y = ws.y;
+  dn.nrows = d.hidden;
   mark(1);
-  rc = q6 ? launch_proj<QType::Q6_K>(gu, max_active * (d.intermediate / 16), st, true)
-          : launch_proj<QType::Q4_K>(gu, max_active * (d.intermediate / 16), st, true);
+  rc = q6 ? launch_umma<QType::Q6_K, kModeGateUp>(gu, sms, st) : launch_umma<QType::Q4_K, kModeGateUp>(gu, sms, st);
   if (rc) return rc;
   mark(2);
-  rc = q6 ? launch_proj<QType::Q6_K>(dn, max_active * (d.hidden / 16), st, false)
-          : launch_proj<QType::Q4_K>(dn, max_active * (d.hidden / 16), st, false);
+  rc = q6 ? launch_umma<QType::Q6_K, kModeDown>(dn, sms, st) : launch_umma<QType::Q4_K, kModeDown>(dn, sms, st);
   if (rc) return rc;
   mark(3);
   moe_combine_kernel<<<B, 256, 0, st>>>(ids, B, d.top_k, d.hidden, out_dtype == QK_OUT_BF16, out, ws);

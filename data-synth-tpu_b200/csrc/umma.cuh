@@ -1,0 +1,96 @@
+// tcgen05 (5th-generation tensor core) helpers: tensor-memory allocation, TMEM loads and
+// stores, the kind::f16 MMA with A in TMEM and B in shared memory, commits and fences.
+// Single-CTA forms only (cta_group::1), no multicast anywhere.
+#pragma once
+
+#include "common.cuh"
+
+namespace qk {
+
+// ---- tensor memory ------------------------------------------------------------------
+
+// Allocate `ncols` TMEM columns (power of two >= 32) for this CTA; the base address is
+// written to shared memory at `dst`. One full warp executes it.
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(dst)),
+               "r"(ncols));
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t base, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(base), "r"(ncols));
+}
+
+// TMEM address: lane in bits 31..16, column in bits 15..0.
+__device__ __forceinline__ uint32_t tmem_addr(uint32_t base, uint32_t lane, uint32_t col) {
+  return base + (lane << 16) + col;
+}
+
+// Each thread of the warp writes 8 consecutive 32-bit columns of its own lane.
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr),
+               "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+               : "memory");
+}
+
+// Each thread of the warp reads 8 consecutive 32-bit columns of its own lane.
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+                 "=r"(r[7])
+               : "r"(taddr)
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// ---- MMA ----------------------------------------------------------------------------
+
+// Instruction descriptor of kind::f16: BF16 A and B, FP32 D, both K-major, M = 128, N.
+__device__ __forceinline__ uint32_t idesc_bf16_m128(uint32_t n) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((n >> 3) << 17) | ((128u >> 4) << 24);
+}
+
+// Shared-memory matrix descriptor, K-major, 128-byte swizzle: 8-row x 128-byte atoms,
+// row groups `sbo` bytes apart, start address 16-byte granular (K offset inside the atom
+// row is added to the start address, 32 bytes per 16 BF16 values).
+__device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr, uint32_t sbo) {
+  return static_cast<uint64_t>((saddr >> 4) & 0x3fffu) | (1ull << 16) |
+         (static_cast<uint64_t>((sbo >> 4) & 0x3fffu) << 32) | (1ull << 46) | (2ull << 61);
+}
+
+// D[tmem] (+)= A[tmem] * B[smem], M = 128, N from the descriptor, K = 16. One thread issues.
+__device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                        uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive once on `bar` when all tcgen05 operations issued so far by this thread complete.
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_addr(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+// ---- activation tiles ("xt" layout) --------------------------------------------------
+// The B operand of one stage (R rows = tokens, R % 16 == 0, 256 K values) is stored, in
+// global memory as in shared memory, as [k atom (4)][row group (R/8)][8 rows x 128 B] with
+// the 128-byte swizzle (16-byte chunk index XOR row % 8). Byte offset of element (row, k):
+__host__ __device__ __forceinline__ uint32_t xt_offset(uint32_t rows16, uint32_t row, uint32_t k) {
+  const uint32_t atom = k >> 6, kin = k & 63, chunk = kin >> 3;
+  return atom * (rows16 >> 3) * 1024u + (row >> 3) * 1024u + (row & 7) * 128u +
+         ((chunk ^ (row & 7)) << 4) + (kin & 7) * 2u;
+}
+
+}  // namespace qk

@@ -1,8 +1,8 @@
 """Lossless tiled repack and the packed-weight projection.
 
 Mirrors ``kaggle/packed_q6``: ``pack_q6``/``unpack_q6`` (``layout.py:49-108``) and
-``q6_matmul`` (``kernel.py:98-148``), with this build's tile layout (16 rows x 256
-values per tile, see ``csrc/tiles.cuh``) instead of the TPU SoA tiles. ``pack_rows``
+``q6_matmul`` (``kernel.py:98-148``), with this build's tile layout (128 rows x 256
+values per tile, see ``csrc/rowtile.cuh``) instead of the TPU SoA tiles. ``pack_rows``
 and ``quant_matmul`` are the type-generic forms (Q6_K, Q4_K).
 """
 
@@ -122,18 +122,33 @@ def dequantize_packed(packed, dtype=torch.bfloat16, *, fused=False):
     return out
 
 
+_workspaces = {}
+
+
+def _workspace(device, nbytes):
+    """Per-device scratch for the activation tiles (grown on demand, never shrunk)."""
+    key = device.index
+    buf = _workspaces.get(key)
+    if buf is None or buf.numel() < nbytes:
+        buf = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=device)
+        _workspaces[key] = buf
+    return buf
+
+
 def quant_matmul(x, packed):
-    """FP32 ``x @ bf16(decode(W)).T`` with the weights kept packed."""
+    """FP32 ``x @ bf16(decode(W)).T`` with the weights kept packed (tcgen05 tensor core)."""
     if not isinstance(x, torch.Tensor) or x.dim() != 2 or min(x.shape) < 1 or x.dtype != torch.bfloat16:
         raise ValueError("x must be a nonempty [M,K] BF16 array")
     if x.shape[1] != packed.input_features:
         raise ValueError("Packed dtype/shape does not match projection dimensions")
     x = x.contiguous()
     out = torch.empty((x.shape[0], packed.output_features), dtype=torch.float32, device=x.device)
+    need = int(_lib.load().qk_quant_gemm_workspace_bytes(x.shape[0], x.shape[1]))
+    ws = _workspace(x.device, need)
     with torch.cuda.device(x.device):
         _lib.call("qk_quant_gemm", _lib.ptr(x), x.shape[0], x.shape[1], _lib.ptr(packed.data),
-                  GGML_TYPE[packed.qtype], packed.output_features, _lib.ptr(out),
-                  _lib.stream_handle(x.device))
+                  GGML_TYPE[packed.qtype], packed.output_features, _lib.ptr(out), _lib.ptr(ws),
+                  ws.numel(), _lib.stream_handle(x.device))
     return out
 
 

@@ -73,8 +73,8 @@ int qk_dequantize_rows(const uint8_t* raw, int qtype, int64_t rows, int64_t row_
 
 /* ---- tiled repack (lossless) -------------------------------------------------
  * Replaces packed_q6/layout.py:49-108 pack_q6 / unpack_q6: a byte-only repack of raw
- * GGUF rows into the B200 tile layout (16 rows x 256 values per tile, rows padded to
- * 16) read by qk_quant_gemm and qk_moe_forward. Q6_K and Q4_K.
+ * GGUF rows into the B200 tile layout (128 rows x 256 values per tile, rows padded to
+ * 128) read by qk_quant_gemm and qk_moe_forward. Q6_K and Q4_K.
  * bad_scales (device int32, may be NULL): receives the count of non-finite FP16 block
  * scales (pack_q6 rejects those, layout.py:67-69); the host wrapper raises on > 0. */
 int64_t qk_tiled_bytes(int qtype, int64_t rows, int64_t row_width);
@@ -90,10 +90,13 @@ int qk_dequantize_tiled(const uint8_t* tiled, int qtype, int64_t rows, int64_t r
 
 /* ---- packed projection -------------------------------------------------------
  * Replaces packed_q6/kernel.py:98-148 q6_matmul(x, packed, scales, output_features):
- * out[M, N] (FP32) = bf16 x[M, K] @ bf16(decode(W))[N, K]^T, FP32 accumulation.
- * w_tiled: qk_repack_rows output for W (Q6_K or Q4_K). Ragged M, N and K allowed. */
+ * out[M, N] (FP32) = bf16 x[M, K] @ bf16(decode(W))[N, K]^T, FP32 accumulation on the
+ * tcgen05 tensor core. w_tiled: qk_repack_rows output for W (Q6_K or Q4_K). Ragged M, N
+ * and K allowed. The workspace holds x repacked into the tensor core's operand tiles. */
+size_t qk_quant_gemm_workspace_bytes(int64_t M, int64_t K);
 int qk_quant_gemm(const uint16_t* x, int64_t M, int64_t K, const uint8_t* w_tiled, int qtype,
-                  int64_t N, float* out, qk_stream_t stream);
+                  int64_t N, float* out, void* workspace, size_t workspace_bytes,
+                  qk_stream_t stream);
 
 /* ---- router ------------------------------------------------------------------
  * Replaces the router of qwen38_tpu/math.py:277-281 (routes_and_shared):
