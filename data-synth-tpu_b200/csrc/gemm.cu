@@ -48,6 +48,20 @@ __global__ void __launch_bounds__(256) pack_x_kernel(const uint16_t* __restrict_
   }
 }
 
+// out[m, n] = sum over K blocks, in K order, of the block partials [nkb, M, N].
+__global__ void reduce_blocks_kernel(const float* __restrict__ part, int64_t mn, int nkb, float* __restrict__ out) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < mn;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    float acc = part[i];
+    for (int kb = 1; kb < nkb; ++kb) acc = __fadd_rn(acc, part[kb * mn + i]);
+    out[i] = acc;
+  }
+}
+
+size_t xt_bytes(int64_t M, int64_t K) {
+  return static_cast<size_t>(dense_tile_rows(M)) * 512 * static_cast<size_t>((K + 255) / 256);
+}
+
 }  // namespace
 }  // namespace qk
 
@@ -55,9 +69,10 @@ using namespace qk;
 
 extern "C" {
 
-size_t qk_quant_gemm_workspace_bytes(int64_t M, int64_t K) {
-  if (M <= 0 || K <= 0) return 0;
-  return static_cast<size_t>(dense_tile_rows(M)) * 512 * static_cast<size_t>((K + 255) / 256);
+size_t qk_quant_gemm_workspace_bytes(int64_t M, int64_t K, int64_t N) {
+  if (M <= 0 || K <= 0 || N <= 0) return 0;
+  const int64_t nkb = (K + 255) / 256;
+  return xt_bytes(M, K) + (nkb > 1 ? static_cast<size_t>(nkb * M * N) * 4 : 0);
 }
 
 int qk_quant_gemm(const uint16_t* x, int64_t M, int64_t K, const uint8_t* w_tiled, int qtype,
@@ -68,7 +83,7 @@ int qk_quant_gemm(const uint16_t* x, int64_t M, int64_t K, const uint8_t* w_tile
   QK_REQUIRE(M < (1 << 30) && K < (1 << 30) && N < (1 << 30), "dimension too large");
   if (M == 0) return QK_OK;
   QK_REQUIRE(x && w_tiled && out, "null pointer");
-  const size_t need = qk_quant_gemm_workspace_bytes(M, K);
+  const size_t need = qk_quant_gemm_workspace_bytes(M, K, N);
   if (!workspace || workspace_bytes < need)
     return set_error(QK_ERR_WORKSPACE, "workspace needs %zu bytes, got %zu", need, workspace_bytes);
   cudaStream_t st = as_stream(stream);
@@ -89,12 +104,22 @@ int qk_quant_gemm(const uint16_t* x, int64_t M, int64_t K, const uint8_t* w_tile
   a.xt = static_cast<const uint8_t*>(workspace);
   a.n_chunks_dense = static_cast<int>((M + kMaxTok - 1) / kMaxTok);
   a.m_dense = static_cast<int>(M);
-  a.out = out;
   a.nrows = static_cast<int>(N);
-  const int64_t items = static_cast<int64_t>(a.n_chunks_dense) * a.pairs;
+  // Split K: one item per 256-value block writes its FP32 partial sum; the partials are
+  // then added in K order (the per-block accumulation of packed_q6/kernel.py:95-107).
+  a.ksplit = nkb > 1;
+  a.out = a.ksplit ? reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + xt_bytes(M, K)) : out;
+  const int64_t items = static_cast<int64_t>(a.n_chunks_dense) * a.pairs * (a.ksplit ? nkb : 1);
   const int grid = static_cast<int>(items < sms ? items : sms);
-  return qtype == QK_TYPE_Q6_K ? launch_umma<QType::Q6_K, kModeDense>(a, grid, st)
-                               : launch_umma<QType::Q4_K, kModeDense>(a, grid, st);
+  int rc = qtype == QK_TYPE_Q6_K ? launch_umma<QType::Q6_K, kModeDense>(a, grid, st)
+                                 : launch_umma<QType::Q4_K, kModeDense>(a, grid, st);
+  if (rc || !a.ksplit) return rc;
+  const int64_t mn = M * N;
+  int64_t rgrid = (mn + 255) / 256;
+  if (rgrid > sms * 8) rgrid = sms * 8;
+  reduce_blocks_kernel<<<static_cast<unsigned>(rgrid), 256, 0, st>>>(a.out, mn, nkb, out);
+  QK_LAUNCHED("reduce_blocks_kernel");
+  return QK_OK;
 }
 
 }  // extern "C"

@@ -63,8 +63,9 @@ struct UArgs {
   uint8_t* ht;       // gate/up: activation tiles of the down pass
   int nkb_out;       // gate/up: K blocks of the down pass
   uint16_t* y;       // down: y [entries, nrows]
-  float* out;        // dense: out [M, nrows]
+  float* out;        // dense: out [M, nrows], or with ksplit the block partials [nkb, M, nrows]
   int nrows;         // output rows of the matrix (I, H or N)
+  int ksplit;        // dense: one work item per K block (partial sums, reduced in K order)
   int32_t* status;
 };
 
@@ -121,6 +122,26 @@ __device__ __forceinline__ int item_tiles(const UArgs& A, int e, int p, const ui
   return (2 * p + 1 < A.rowtiles) ? 2 : 1;
 }
 
+// Work item -> (token chunk, tile pair, K-block range).
+struct ItemInfo {
+  int ci, p, kb0, kb1;
+};
+
+__device__ __forceinline__ ItemInfo item_info(const UArgs& A, int item) {
+  ItemInfo it;
+  if (A.ksplit) {
+    it.kb0 = item % A.nkb;
+    it.kb1 = it.kb0 + 1;
+    item /= A.nkb;
+  } else {
+    it.kb0 = 0;
+    it.kb1 = A.nkb;
+  }
+  it.ci = item / A.pairs;
+  it.p = item % A.pairs;
+  return it;
+}
+
 template <QType QT, int MODE>
 __global__ void __launch_bounds__(kUmmaThreads, 1) umma_proj_kernel(const UArgs A) {
   using Cfg = UCfg<QT>;
@@ -139,7 +160,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) umma_proj_kernel(const UArgs 
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_chunks = MODE == kModeDense ? A.n_chunks_dense : *A.n_chunks_p;
-  const int n_items = n_chunks * A.pairs;
+  const int n_items = n_chunks * A.pairs * (A.ksplit ? A.nkb : 1);
   if (static_cast<int>(blockIdx.x) >= n_items) return;
 
   if (threadIdx.x == 0) {
@@ -166,15 +187,15 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) umma_proj_kernel(const UArgs 
     if (lane == 0) {
       uint32_t sc = 0;
       for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
-        const int ci = item / A.pairs, p = item % A.pairs;
-        const ChunkInfo c = chunk_info<MODE>(A, ci);
+        const ItemInfo it = item_info(A, item);
+        const ChunkInfo c = chunk_info<MODE>(A, it.ci);
         const uint8_t *w0, *w1;
         int rt0;
-        const int nt = item_tiles<MODE>(A, c.e, p, w0, w1, rt0);
+        const int nt = item_tiles<MODE>(A, c.e, it.p, w0, w1, rt0);
         const int rtb = MODE == kModeGateUp ? rt0 : rt0 + 1;
         const uint32_t xbytes = static_cast<uint32_t>(c.r16) * 512u;
         const uint8_t* xsrc = A.xt + c.xrow * 512 * A.nkb;
-        for (int kb = 0; kb < A.nkb; ++kb, ++sc) {
+        for (int kb = it.kb0; kb < it.kb1; ++kb, ++sc) {
           const int s = sc % S;
           if (sc >= S && !mbar_wait_bounded(&empty[s], ((sc / S) - 1) & 1)) {
             ok = false;
@@ -192,11 +213,11 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) umma_proj_kernel(const UArgs 
     if (lane == 0) {
       uint32_t sc = 0, ac = 0, ic = 0;
       for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
-        const int ci = item / A.pairs, p = item % A.pairs;
-        const ChunkInfo c = chunk_info<MODE>(A, ci);
+        const ItemInfo it = item_info(A, item);
+        const ChunkInfo c = chunk_info<MODE>(A, it.ci);
         const uint8_t *w0, *w1;
         int rt0;
-        const int nt = item_tiles<MODE>(A, c.e, p, w0, w1, rt0);
+        const int nt = item_tiles<MODE>(A, c.e, it.p, w0, w1, rt0);
         const uint32_t idesc = idesc_bf16_m128(static_cast<uint32_t>(c.r16));
         const uint32_t d = ic & 1;
         if (ic >= 2 && !mbar_wait_bounded(&dempty[d], ((ic >> 1) - 1) & 1)) {
@@ -204,7 +225,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) umma_proj_kernel(const UArgs 
           break;
         }
         tc_fence_after();
-        for (int kb = 0; kb < A.nkb && ok; ++kb, ++sc) {
+        for (int kb = it.kb0; kb < it.kb1 && ok; ++kb, ++sc) {
           const int s = sc % S;
           if (!mbar_wait_bounded(&full[s], (sc / S) & 1)) {
             ok = false;
@@ -225,7 +246,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) umma_proj_kernel(const UArgs 
                 const uint64_t desc =
                     sdesc_sw128(xs + (k >> 6) * (static_cast<uint32_t>(c.r16) >> 3) * 1024u + (k & 63) * 2u, 1024u);
                 umma_ts(tbase + 256 + d * 128 + t * 64, tbase + aa * 128 + t * 64 + ks * 8, desc, idesc,
-                        (kb | h | ks) != 0);
+                        ((kb - it.kb0) | h | ks) != 0);
               }
             }
             umma_commit(&aempty[aa]);
@@ -242,13 +263,13 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) umma_proj_kernel(const UArgs 
     const int t = warp >> 2, q = warp & 3, row = 32 * q + lane;
     uint32_t sc = 0, ac = 0, ic = 0;
     for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
-      const int ci = item / A.pairs, p = item % A.pairs;
-      const ChunkInfo c = chunk_info<MODE>(A, ci);
+      const ItemInfo it = item_info(A, item);
+      const ChunkInfo c = chunk_info<MODE>(A, it.ci);
       const uint8_t *w0, *w1;
       int rt0;
-      const int nt = item_tiles<MODE>(A, c.e, p, w0, w1, rt0);
+      const int nt = item_tiles<MODE>(A, c.e, it.p, w0, w1, rt0);
       const bool mine = t < nt;
-      for (int kb = 0; kb < A.nkb && ok; ++kb, ++sc) {
+      for (int kb = it.kb0; kb < it.kb1 && ok; ++kb, ++sc) {
         const int s = sc % S;
         if (!mbar_wait_bounded(&full[s], (sc / S) & 1)) {
           ok = false;
@@ -324,7 +345,8 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) umma_proj_kernel(const UArgs 
             if (MODE == kModeDown) {
               A.y[orow * A.nrows + R] = bf16_bits_rne(__uint_as_float(v[j]));
             } else if (R < A.nrows) {
-              A.out[orow * A.nrows + R] = __uint_as_float(v[j]);
+              float* o = A.ksplit ? A.out + static_cast<int64_t>(it.kb0) * A.m_dense * A.nrows : A.out;
+              o[orow * A.nrows + R] = __uint_as_float(v[j]);
             }
           }
         }

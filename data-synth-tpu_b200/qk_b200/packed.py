@@ -143,7 +143,8 @@ def quant_matmul(x, packed):
         raise ValueError("Packed dtype/shape does not match projection dimensions")
     x = x.contiguous()
     out = torch.empty((x.shape[0], packed.output_features), dtype=torch.float32, device=x.device)
-    need = int(_lib.load().qk_quant_gemm_workspace_bytes(x.shape[0], x.shape[1]))
+    need = int(_lib.load().qk_quant_gemm_workspace_bytes(x.shape[0], x.shape[1],
+                                                        packed.output_features))
     ws = _workspace(x.device, need)
     with torch.cuda.device(x.device):
         _lib.call("qk_quant_gemm", _lib.ptr(x), x.shape[0], x.shape[1], _lib.ptr(packed.data),

@@ -92,8 +92,9 @@ int qk_dequantize_tiled(const uint8_t* tiled, int qtype, int64_t rows, int64_t r
  * Replaces packed_q6/kernel.py:98-148 q6_matmul(x, packed, scales, output_features):
  * out[M, N] (FP32) = bf16 x[M, K] @ bf16(decode(W))[N, K]^T, FP32 accumulation on the
  * tcgen05 tensor core. w_tiled: qk_repack_rows output for W (Q6_K or Q4_K). Ragged M, N
- * and K allowed. The workspace holds x repacked into the tensor core's operand tiles. */
-size_t qk_quant_gemm_workspace_bytes(int64_t M, int64_t K);
+ * and K allowed. The workspace holds x repacked into the tensor core's operand tiles and
+ * the FP32 partial sum of every 256-value K block, added in K order at the end. */
+size_t qk_quant_gemm_workspace_bytes(int64_t M, int64_t K, int64_t N);
 int qk_quant_gemm(const uint16_t* x, int64_t M, int64_t K, const uint8_t* w_tiled, int qtype,
                   int64_t N, float* out, void* workspace, size_t workspace_bytes,
                   qk_stream_t stream);

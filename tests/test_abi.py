@@ -53,7 +53,7 @@ def test_argument_validation_happens_before_any_launch():
     assert lib.qk_dequantize_rows(null, 14, 1, 0, 0, null, null) == _lib.QK_ERR_INVALID_ARGUMENT
     assert lib.qk_quant_gemm(null, 1, 256, null, 8, 16, null, null, 0, null) == _lib.QK_ERR_UNSUPPORTED_TYPE
     assert lib.qk_quant_gemm(ctypes.c_void_p(16), 4, 256, ctypes.c_void_p(16), 14, 16, ctypes.c_void_p(16), null, 0, null) == _lib.QK_ERR_WORKSPACE
-    assert lib.qk_quant_gemm_workspace_bytes(65, 263) == 80 * 512 * 2
+    assert lib.qk_quant_gemm_workspace_bytes(65, 263, 7) == 80 * 512 * 2 + 2 * 65 * 7 * 4
     assert lib.qk_router_topk_logits(null, null, 1, 4, 5, null, null, null, null) == _lib.QK_ERR_INVALID_ARGUMENT
     desc = _lib.MoeDesc(14, 14, 8, 2048, 512, 64, 0, 4)
     assert lib.qk_moe_forward(ctypes.byref(desc), *([null] * 6), 1, 1, null, null, 0, null) == _lib.QK_ERR_UNSUPPORTED_TYPE
