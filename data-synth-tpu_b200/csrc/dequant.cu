@@ -126,20 +126,7 @@ __global__ void dequant_rows_kernel(const uint8_t* __restrict__ raw, int qtype, 
   }
 }
 
-// ---- tiled layout byte map (the format is stated in oracle/layout.py and rowtile.cuh) ----
-
-// For byte `off` of a 128-row tile: the row inside the tile and the byte of that row's block.
-__host__ __device__ inline void tile_source(int qtype, int off, int& row, int& src) {
-  const int chunks = qtype == QK_TYPE_Q6_K ? RowTile<QType::Q6_K>::kChunks : RowTile<QType::Q4_K>::kChunks;
-  if (off < chunks * 2048) {
-    row = (off & 2047) >> 4;
-    src = (off >> 11) * 16 + (off & 15);
-  } else {  // Q6_K scale plane: [row][2 B] = block bytes 208..209
-    const int o = off - chunks * 2048;
-    row = o >> 1;
-    src = 208 + (o & 1);
-  }
-}
+// ---- tiled layout (the format is stated in oracle/layout.py and rowtile.cuh) ----
 
 inline int tile_bytes(int qtype) {
   return qtype == QK_TYPE_Q6_K ? RowTile<QType::Q6_K>::kBytes
@@ -147,26 +134,106 @@ inline int tile_bytes(int qtype) {
                                  : 0;
 }
 
-// One CTA per tile; tiled[...] <- raw[...] (or the reverse for unpack).
+// Byte offset, inside a 128-row tile, of 32-bit word w of row r.
+__device__ __forceinline__ int tile_word(int r, int w) { return ((w >> 2) * 128 + r) * 16 + (w & 3) * 4; }
+
+// Q6_K code of position p of a GGUF block (packed_q6/reference.py:21-27 position rule).
+__device__ __forceinline__ uint32_t q6_code(const uint8_t* blk, int p) {
+  const int half = p >> 7, quarter = (p & 127) >> 5, lane = p & 31;
+  const uint32_t lo = (blk[half * 64 + (quarter & 1) * 32 + lane] >> (4 * (quarter >> 1))) & 15u;
+  const uint32_t hi = (blk[128 + half * 32 + lane] >> (2 * quarter)) & 3u;
+  return lo | (hi << 4);
+}
+
+// One thread per (tile row, sub-block j) - 16 codes -> 3 words; j == 16 copies the
+// sub-scale words and d. kPack: raw -> tiled, else tiled -> raw.
 template <bool kPack>
-__global__ void repack_kernel(const uint8_t* __restrict__ in, uint8_t* __restrict__ out, int qtype,
-                              int64_t rows, int64_t nblk, int tbytes, int bbytes,
-                              int32_t* bad_scales) {
+__global__ void __launch_bounds__(128) repack_q6_kernel(const uint8_t* __restrict__ in, uint8_t* __restrict__ out,
+                                                        int64_t rows, int64_t nblk, int32_t* bad_scales) {
+  constexpr int TB = RowTile<QType::Q6_K>::kBytes;
   const int64_t tile = blockIdx.x;
   const int64_t strip = tile / nblk, kb = tile % nblk;
-  for (int off = threadIdx.x; off < tbytes; off += blockDim.x) {
-    int r, src;
-    tile_source(qtype, off, r, src);
+  const int r = threadIdx.x;
+  const int64_t row = strip * 128 + r;
+  const bool real = row < rows;
+  uint8_t* traw_out = nullptr;
+  const uint8_t* blk = nullptr;
+  uint8_t* t = nullptr;
+  const uint8_t* tin = nullptr;
+  if (kPack) {
+    blk = real ? in + (row * nblk + kb) * 210 : nullptr;
+    t = out + tile * TB;
+  } else {
+    tin = in + tile * TB;
+    traw_out = real ? out + (row * nblk + kb) * 210 : nullptr;
+  }
+  if (kPack) {
+    for (int j = 0; j < 16; ++j) {
+      uint32_t u[16];
+      for (int i = 0; i < 16; ++i) u[i] = real ? q6_code(blk, 16 * j + i) : 0u;
+      uint32_t w[3] = {0, 0, 0};
+      for (int n = 0; n < 3; ++n)
+        for (int i = 0; i < 4; ++i)
+          w[n] |= (u[4 * n + i] | (((u[12 + i] >> (2 * n)) & 3u) << 6)) << (8 * i);
+      for (int n = 0; n < 3; ++n) *reinterpret_cast<uint32_t*>(t + tile_word(r, 3 * j + n)) = w[n];
+    }
+    for (int n = 0; n < 4; ++n) {  // sub-scales: block bytes 192..207
+      uint32_t v = 0;
+      if (real)
+        for (int i = 0; i < 4; ++i) v |= static_cast<uint32_t>(blk[192 + 4 * n + i]) << (8 * i);
+      *reinterpret_cast<uint32_t*>(t + tile_word(r, 48 + n)) = v;
+    }
+    const uint16_t d = real ? static_cast<uint16_t>(blk[208] | (blk[209] << 8)) : 0;
+    *reinterpret_cast<uint16_t*>(t + 13 * 2048 + r * 2) = d;
+    if (bad_scales && (d & 0x7c00) == 0x7c00) atomicAdd(bad_scales, 1);
+  } else if (real) {
+    uint8_t b[208];
+    for (int i = 0; i < 192; ++i) b[i] = 0;
+    for (int j = 0; j < 16; ++j) {
+      uint32_t w[3];
+      for (int n = 0; n < 3; ++n) w[n] = *reinterpret_cast<const uint32_t*>(tin + tile_word(r, 3 * j + n));
+      for (int i = 0; i < 16; ++i) {
+        uint32_t u;
+        if (i < 12) {
+          u = (w[i >> 2] >> (8 * (i & 3))) & 63u;
+        } else {
+          const int m = i - 12;
+          u = 0;
+          for (int n = 0; n < 3; ++n) u |= ((w[n] >> (8 * m + 6)) & 3u) << (2 * n);
+        }
+        const int p = 16 * j + i, half = p >> 7, quarter = (p & 127) >> 5, lane = p & 31;
+        b[half * 64 + (quarter & 1) * 32 + lane] |= static_cast<uint8_t>((u & 15u) << (4 * (quarter >> 1)));
+        b[128 + half * 32 + lane] |= static_cast<uint8_t>((u >> 4) << (2 * quarter));
+      }
+    }
+    for (int n = 0; n < 4; ++n) {
+      const uint32_t v = *reinterpret_cast<const uint32_t*>(tin + tile_word(r, 48 + n));
+      for (int i = 0; i < 4; ++i) b[192 + 4 * n + i] = static_cast<uint8_t>(v >> (8 * i));
+    }
+    for (int i = 0; i < 208; ++i) traw_out[i] = b[i];
+    const uint16_t d = *reinterpret_cast<const uint16_t*>(tin + 13 * 2048 + r * 2);
+    traw_out[208] = static_cast<uint8_t>(d & 0xff);
+    traw_out[209] = static_cast<uint8_t>(d >> 8);
+  }
+}
+
+// Q4_K: a byte transpose. One CTA per tile; tiled[...] <- raw[...] (or the reverse).
+template <bool kPack>
+__global__ void repack_q4_kernel(const uint8_t* __restrict__ in, uint8_t* __restrict__ out, int64_t rows,
+                                 int64_t nblk, int32_t* bad_scales) {
+  constexpr int TB = RowTile<QType::Q4_K>::kBytes;
+  const int64_t tile = blockIdx.x;
+  const int64_t strip = tile / nblk, kb = tile % nblk;
+  for (int off = threadIdx.x; off < TB; off += blockDim.x) {
+    const int r = (off & 2047) >> 4, src = (off >> 11) * 16 + (off & 15);
     const int64_t row = strip * 128 + r;
-    const int64_t raw_off = (row * nblk + kb) * bbytes + src;
-    const int64_t tiled_off = tile * tbytes + off;
+    const int64_t raw_off = (row * nblk + kb) * 144 + src;
+    const int64_t tiled_off = tile * TB + off;
     if (kPack) {
       uint8_t v = 0;
       if (row < rows) {
         v = in[raw_off];
-        // Non-finite FP16 block scale (exponent all ones): count once per scale.
-        const bool scale_hi = qtype == QK_TYPE_Q6_K ? src == 209 : (src == 1 || src == 3);
-        if (bad_scales && scale_hi && (v & 0x7c) == 0x7c) atomicAdd(bad_scales, 1);
+        if (bad_scales && (src == 1 || src == 3) && (v & 0x7c) == 0x7c) atomicAdd(bad_scales, 1);
       }
       out[tiled_off] = v;
     } else if (row < rows) {
@@ -246,11 +313,15 @@ static int repack_common(const uint8_t* in, int qtype, int64_t rows, int64_t row
   const int64_t nblk = (row_width + 255) / 256;
   const int64_t tiles = (rows + 127) / 128 * nblk;
   QK_REQUIRE(tiles < (1ll << 31), "too many tiles");
-  const int bb = block_shape(qtype).bytes;
-  if (pack)
-    repack_kernel<true><<<static_cast<unsigned>(tiles), 256, 0, as_stream(stream)>>>(in, out, qtype, rows, nblk, tb, bb, bad);
-  else
-    repack_kernel<false><<<static_cast<unsigned>(tiles), 256, 0, as_stream(stream)>>>(in, out, qtype, rows, nblk, tb, bb, nullptr);
+  const unsigned g = static_cast<unsigned>(tiles);
+  cudaStream_t st = as_stream(stream);
+  if (qtype == QK_TYPE_Q6_K) {
+    if (pack) repack_q6_kernel<true><<<g, 128, 0, st>>>(in, out, rows, nblk, bad);
+    else repack_q6_kernel<false><<<g, 128, 0, st>>>(in, out, rows, nblk, nullptr);
+  } else {
+    if (pack) repack_q4_kernel<true><<<g, 256, 0, st>>>(in, out, rows, nblk, bad);
+    else repack_q4_kernel<false><<<g, 256, 0, st>>>(in, out, rows, nblk, nullptr);
+  }
   QK_LAUNCHED("repack_kernel");
   return QK_OK;
 }

@@ -233,12 +233,12 @@ __global__ void __launch_bounds__(1024) moe_route_kernel(const int32_t* __restri
 // ------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) moe_dispatch_kernel(const uint16_t* __restrict__ x, int H,
                                                            Workspace ws) {
+  // One warp per activation-tile row: the owning expert chunk is looked up once per row,
+  // then the lanes copy the row's 16-byte chunks (H / 8 of them) into the swizzled tile.
   const int n_rows = ws.meta->row_total, n_act = ws.meta->n_active;
-  const int cpr = H / 8, nkb = H / 256;
-  const int64_t total = static_cast<int64_t>(n_rows) * cpr;
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int g = static_cast<int>(i / cpr), j = static_cast<int>(i % cpr);
+  const int lane = threadIdx.x & 31, cpr = H / 8, nkb = H / 256;
+  const int warps = gridDim.x * (blockDim.x >> 5);
+  for (int g = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); g < n_rows; g += warps) {
     int lo = 0, hi = n_act;  // largest a with row_off[a] <= g
     while (hi - lo > 1) {
       const int mid = (lo + hi) >> 1;
@@ -248,15 +248,13 @@ __global__ void __launch_bounds__(256) moe_dispatch_kernel(const uint16_t* __res
     const int r_in = g - ws.row_off[lo], ch = r_in / kMaxTok, rr = r_in % kMaxTok;
     const int e = ws.active[lo];
     const int ntok = min(kMaxTok, ws.counts[e] - kMaxTok * ch), r16 = (ntok + 15) & ~15;
-    uint4 v = make_uint4(0, 0, 0, 0);
-    if (rr < ntok) {
-      const int token = ws.entry_token[ws.offsets[e] + r_in];
-      v = ld_nc_v4(x + static_cast<int64_t>(token) * H + j * 8);
+    const uint16_t* src = rr < ntok ? x + static_cast<int64_t>(ws.entry_token[ws.offsets[e] + r_in]) * H : nullptr;
+    uint8_t* base = ws.xt + static_cast<int64_t>(ws.row_off[lo] + kMaxTok * ch) * 512 * nkb;
+    for (int j = lane; j < cpr; j += 32) {
+      const uint4 v = src ? ld_nc_v4(src + j * 8) : make_uint4(0, 0, 0, 0);
+      const int k = j * 8;
+      *reinterpret_cast<uint4*>(base + static_cast<int64_t>(k >> 8) * r16 * 512 + xt_offset(r16, rr, k & 255)) = v;
     }
-    const int k = j * 8;
-    uint8_t* dst = ws.xt + static_cast<int64_t>(ws.row_off[lo] + kMaxTok * ch) * 512 * nkb +
-                   static_cast<int64_t>(k >> 8) * r16 * 512 + xt_offset(r16, rr, k & 255);
-    *reinterpret_cast<uint4*>(dst) = v;
   }
 }
 
@@ -265,33 +263,51 @@ __global__ void __launch_bounds__(256) moe_dispatch_kernel(const uint16_t* __res
 // ------------------------------------------------------------------------------------
 constexpr int kMaxTopK = 32;
 
+// One warp per token: lane j holds route j's entry; ranks by expert id give the reference's
+// ascending-expert accumulation order; each lane then sums 8 columns at a time in FP32.
 __global__ void __launch_bounds__(256) moe_combine_kernel(const int32_t* __restrict__ ids, int B,
                                                           int k, int H, int out_bf16, void* out,
                                                           Workspace ws) {
-  const int b = blockIdx.x;
-  int ent[kMaxTopK], eid[kMaxTopK];
-  int n = 0;
+  const int lane = threadIdx.x & 31;
+  const int b = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (b >= B) return;
+  const int entry = lane < k ? ws.route_entry[b * k + lane] : -1;
+  const int eid = entry >= 0 ? ids[b * k + lane] : 0x7fffffff;
+  const float w = entry >= 0 ? ws.entry_weight[entry] : 0.f;
+  int rank = 0, n = 0;
   for (int j = 0; j < k; ++j) {
-    const int entry = ws.route_entry[b * k + j];
-    if (entry < 0) continue;
-    const int e = ids[b * k + j];
-    int pos = n++;
-    while (pos > 0 && eid[pos - 1] > e) {  // insertion sort by expert id
-      eid[pos] = eid[pos - 1];
-      ent[pos] = ent[pos - 1];
-      --pos;
-    }
-    eid[pos] = e;
-    ent[pos] = entry;
+    const int ej = __shfl_sync(0xffffffffu, eid, j);
+    const int vj = __shfl_sync(0xffffffffu, entry, j) >= 0;
+    n += vj;
+    rank += vj && (ej < eid);  // entries of a token name distinct experts
   }
-  for (int col = threadIdx.x; col < H; col += blockDim.x) {
-    float acc = 0.f;
+  for (int c0 = lane * 8; c0 < H; c0 += 256) {
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     for (int i = 0; i < n; ++i) {
-      const float y = bf16_to_f32(ws.y[static_cast<int64_t>(ent[i]) * H + col]);
-      acc = __fadd_rn(acc, __fmul_rn(y, ws.entry_weight[ent[i]]));
+      const unsigned who = __ballot_sync(0xffffffffu, entry >= 0 && rank == i);
+      const int src = __ffs(who) - 1;
+      const int ent = __shfl_sync(0xffffffffu, entry, src);
+      const float wi = __shfl_sync(0xffffffffu, w, src);
+      const uint4 v = ld_nc_v4(ws.y + static_cast<int64_t>(ent) * H + c0);
+      const uint32_t p[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int t = 0; t < 8; ++t) {
+        const float y = bf16_to_f32(static_cast<uint16_t>(p[t >> 1] >> (16 * (t & 1))));
+        acc[t] = __fadd_rn(acc[t], __fmul_rn(y, wi));
+      }
     }
-    if (out_bf16) static_cast<uint16_t*>(out)[static_cast<int64_t>(b) * H + col] = bf16_bits_rne(acc);
-    else static_cast<float*>(out)[static_cast<int64_t>(b) * H + col] = acc;
+    const int64_t o = static_cast<int64_t>(b) * H + c0;
+    if (out_bf16) {
+      uint32_t q[4];
+#pragma unroll
+      for (int t = 0; t < 4; ++t)
+        q[t] = static_cast<uint32_t>(bf16_bits_rne(acc[2 * t])) | (static_cast<uint32_t>(bf16_bits_rne(acc[2 * t + 1])) << 16);
+      *reinterpret_cast<uint4*>(static_cast<uint16_t*>(out) + o) = make_uint4(q[0], q[1], q[2], q[3]);
+    } else {
+      float4* f = reinterpret_cast<float4*>(static_cast<float*>(out) + o);
+      f[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+      f[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+    }
   }
 }
 
@@ -351,8 +367,8 @@ static int moe_forward_impl(const qk_moe_desc* desc, const uint8_t* gate, const 
 
   const int sms = sm_count();
   const int64_t rows_max = static_cast<int64_t>(rows_bound(d, B));
-  int64_t dgrid = (rows_max * (d.hidden / 8) + 255) / 256;
-  if (dgrid > sms * 16) dgrid = sms * 16;
+  int64_t dgrid = (rows_max + 7) / 8;  // 8 rows (warps) per CTA
+  if (dgrid > sms * 8) dgrid = sms * 8;
   moe_dispatch_kernel<<<static_cast<unsigned>(dgrid), 256, 0, st>>>(x, d.hidden, ws);
   QK_LAUNCHED("moe_dispatch_kernel");
 
@@ -394,7 +410,7 @@ static int moe_forward_impl(const qk_moe_desc* desc, const uint8_t* gate, const 
   rc = q6 ? launch_umma<QType::Q6_K, kModeDown>(dn, sms, st) : launch_umma<QType::Q4_K, kModeDown>(dn, sms, st);
   if (rc) return rc;
   mark(3);
-  moe_combine_kernel<<<B, 256, 0, st>>>(ids, B, d.top_k, d.hidden, out_dtype == QK_OUT_BF16, out, ws);
+  moe_combine_kernel<<<(B + 7) / 8, 256, 0, st>>>(ids, B, d.top_k, d.hidden, out_dtype == QK_OUT_BF16, out, ws);
   QK_LAUNCHED("moe_combine_kernel");
   mark(4);
   return QK_OK;

@@ -3,17 +3,24 @@
 // Layout of one matrix W[rows, K] (rows zero-padded to a multiple of 128): tiles of 128
 // rows x one 256-value GGUF block, ordered [row tile][k block]. Inside a tile the first
 // 16 * C bytes of every row's block are stored as [chunk c][row r][16 B] (C = 13 for Q6_K,
-// covering block bytes 0..207; C = 9 for Q4_K, the whole 144-byte block); Q6_K then holds
-// the rows' FP16 scale d as [row][2 B]. Thread r of the decode warps reads chunk c of its
-// row at (c * 128 + r) * 16 - consecutive rows are consecutive 16-byte words, so the
-// shared-memory reads are conflict free - and decodes the row in natural K order.
+// C = 9 for Q4_K); Q6_K then holds the rows' FP16 scale d as [row][2 B]. Thread r of the
+// decode warps reads chunk c of its row at (c * 128 + r) * 16 - consecutive rows are
+// consecutive 16-byte words, so the shared-memory reads are conflict free - and decodes
+// the row in natural K order.
+//
+// Q4_K rows keep the GGUF block bytes. Q6_K rows re-pack the 6-bit codes (a lossless bit
+// permutation, still 192 bytes per block): sub-block j (values 16j .. 16j + 15, one int8
+// sub-scale) is three words W0, W1, W2 at bytes 12j .. 12j + 11, where byte i of Wn holds
+// code 4n + i in bits 0..5 and bits 2m..2m+1 of code 12 + i in bits 6..7 (m = n). Codes
+// 0..11 then need one AND per four codes, codes 12..15 a shift-and-or of the three words.
+// Bytes 192..207 are the int8 sub-scales and the FP16 d follows in the scale plane.
 //
 // Values: the reference decodes (d * sc) * q (Q6_K) and (d * sc) * q - dmin * m (Q4_K)
 // in FP32 and rounds to BF16 (glm53_offload/gguf_quant.py:154-157,171). The products are
 // exact in FP32, so one fused multiply-add per element reproduces them:
-//   Q6_K: u = 128 + code (byte permute into FP32 bits 0x43000000 | code << 16),
-//         w = fma(u, ds, -160 ds) = (code - 32) ds;
-//   Q4_K: w = fma(u, ds, -128 ds) - dmin m.
+//   code -> FP16 1024 + code (byte permute, two codes per instruction) -> FP32;
+//   Q6_K: w = fma(v, ds, -1056 ds) = (code - 32) ds (1056 ds is exact: 33 ds needs <= 24 bits);
+//   Q4_K: w = fma(v, ds, -1024 ds) - dmin m.
 // The fused form turns a (d * sc) * 0 of negative sign into +0, which no dot product can
 // see; kExact (the dequantisation entry points) subtracts before multiplying and so
 // reproduces the reference bit for bit, signed zeros included.
@@ -27,50 +34,34 @@ namespace qk {
 
 enum class QType { Q6_K = 14, Q4_K = 12 };
 
-// 128 + byte I of `codes` as FP32.
-template <int I>
-__device__ __forceinline__ float magic128(uint32_t codes) {
-  return __uint_as_float(__byte_perm(codes, 0x43u, 0x4055u | (I << 8)));
+// Two codes (bytes 2P and 2P + 1 of `codes`) as FP32 1024 + code, via an FP16 pair.
+template <int P>
+__device__ __forceinline__ float2 magic1024(uint32_t codes) {
+  const uint32_t h2 = __byte_perm(codes, 0x6464u, P == 0 ? 0x5140u : 0x5342u);
+  return __half22float2(*reinterpret_cast<const __half2*>(&h2));
 }
 
-// Four codes (bytes of `code`) -> two packed BF16 pairs.
-template <bool kExact>
-__device__ __forceinline__ void code4_q6(uint32_t code, float ds, float nk, uint32_t& lo, uint32_t& hi) {
-  const float2 u01 = make_float2(magic128<0>(code), magic128<1>(code));
-  const float2 u23 = make_float2(magic128<2>(code), magic128<3>(code));
+// Four codes (bytes of `code`) -> two packed BF16 pairs: w = (code - off) * ds [- dm].
+template <bool kExact, bool kMin>
+__device__ __forceinline__ void code4(uint32_t code, float ds, float nk, float off, float dm,
+                                      uint32_t& lo, uint32_t& hi) {
+  const float2 u01 = magic1024<0>(code), u23 = magic1024<1>(code);
   const float2 s = make_float2(ds, ds);
   float2 w01, w23;
   if (kExact) {
-    const float2 off = make_float2(-160.f, -160.f);
-    w01 = __fmul2_rn(__fadd2_rn(u01, off), s);
-    w23 = __fmul2_rn(__fadd2_rn(u23, off), s);
+    const float2 o = make_float2(-off, -off);
+    w01 = __fmul2_rn(__fadd2_rn(u01, o), s);
+    w23 = __fmul2_rn(__fadd2_rn(u23, o), s);
   } else {
     const float2 k = make_float2(nk, nk);
     w01 = __ffma2_rn(u01, s, k);
     w23 = __ffma2_rn(u23, s, k);
   }
-  lo = pack_bf16x2(w01.x, w01.y);
-  hi = pack_bf16x2(w23.x, w23.y);
-}
-
-template <bool kExact>
-__device__ __forceinline__ void code4_q4(uint32_t code, float ds, float nk, float dm, uint32_t& lo,
-                                         uint32_t& hi) {
-  const float2 u01 = make_float2(magic128<0>(code), magic128<1>(code));
-  const float2 u23 = make_float2(magic128<2>(code), magic128<3>(code));
-  const float2 s = make_float2(ds, ds), m = make_float2(-dm, -dm);
-  float2 w01, w23;
-  if (kExact) {
-    const float2 off = make_float2(-128.f, -128.f);
-    w01 = __fmul2_rn(__fadd2_rn(u01, off), s);
-    w23 = __fmul2_rn(__fadd2_rn(u23, off), s);
-  } else {
-    const float2 k = make_float2(nk, nk);
-    w01 = __ffma2_rn(u01, s, k);
-    w23 = __ffma2_rn(u23, s, k);
+  if (kMin) {
+    const float2 m = make_float2(-dm, -dm);
+    w01 = __fadd2_rn(w01, m);
+    w23 = __fadd2_rn(w23, m);
   }
-  w01 = __fadd2_rn(w01, m);
-  w23 = __fadd2_rn(w23, m);
   lo = pack_bf16x2(w01.x, w01.y);
   hi = pack_bf16x2(w23.x, w23.y);
 }
@@ -85,7 +76,7 @@ struct RowTile<QType::Q6_K> {
   static constexpr int kBytes = 128 * kBlockBytes;  // 26880
 
   struct Regs {
-    uint32_t w[52];  // block bytes 0..207: ql (words 0..31), qh (32..47), sub-scales (48..51)
+    uint32_t w[52];  // block bytes 0..207: re-packed codes (words 0..47), sub-scales (48..51)
     float d;
   };
 
@@ -108,23 +99,19 @@ struct RowTile<QType::Q6_K> {
   template <bool kExact, int h, typename Emit>
   __device__ __forceinline__ static void decode_half(const Regs& r, Emit&& emit) {
 #pragma unroll
-    for (int lg = 0; lg < 2; ++lg) {
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const int j = 8 * h + 2 * q + lg;  // sub-block of 16 positions
-        const int sc = static_cast<int8_t>((r.w[48 + (j >> 2)] >> (8 * (j & 3))) & 0xffu);
-        const float ds = __fmul_rn(r.d, static_cast<float>(sc));
-        const float nk = __fmul_rn(ds, -160.f);
-        uint32_t out[8];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const uint32_t ql = r.w[16 * h + 8 * (q & 1) + 4 * lg + i];
-          const uint32_t qh = r.w[32 + 8 * h + 4 * lg + i];
-          const uint32_t code = ((ql >> (4 * (q >> 1))) & 0x0f0f0f0fu) | (((qh >> (2 * q)) & 0x03030303u) << 4);
-          code4_q6<kExact>(code, ds, nk, out[2 * i], out[2 * i + 1]);
-        }
-        emit(q * 16 + lg * 8, out);
-      }
+    for (int jj = 0; jj < 8; ++jj) {
+      const int j = 8 * h + jj;  // sub-block of 16 positions
+      const int sc = static_cast<int8_t>((r.w[48 + (j >> 2)] >> (8 * (j & 3))) & 0xffu);
+      const float ds = __fmul_rn(r.d, static_cast<float>(sc));
+      const float nk = __fmul_rn(ds, -1056.f);
+      const uint32_t w0 = r.w[3 * j], w1 = r.w[3 * j + 1], w2 = r.w[3 * j + 2];
+      const uint32_t c3 = ((w0 >> 6) & 0x03030303u) | ((w1 >> 4) & 0x0c0c0c0cu) | ((w2 >> 2) & 0x30303030u);
+      uint32_t out[8];
+      code4<kExact, false>(w0 & 0x3f3f3f3fu, ds, nk, 1056.f, 0.f, out[0], out[1]);
+      code4<kExact, false>(w1 & 0x3f3f3f3fu, ds, nk, 1056.f, 0.f, out[2], out[3]);
+      code4<kExact, false>(w2 & 0x3f3f3f3fu, ds, nk, 1056.f, 0.f, out[4], out[5]);
+      code4<kExact, false>(c3, ds, nk, 1056.f, 0.f, out[6], out[7]);
+      emit(jj * 8, out);
     }
   }
 };
@@ -170,7 +157,7 @@ struct RowTile<QType::Q4_K> {
         m = (scale_byte(r, j + 4) >> 4) | ((scale_byte(r, j) >> 6) << 4);
       }
       const float ds = __fmul_rn(d, static_cast<float>(sc));
-      const float nk = __fmul_rn(ds, -128.f);
+      const float nk = __fmul_rn(ds, -1024.f);
       const float dm = __fmul_rn(dmin, static_cast<float>(m));
 #pragma unroll
       for (int half16 = 0; half16 < 2; ++half16) {
@@ -179,7 +166,7 @@ struct RowTile<QType::Q4_K> {
         for (int i = 0; i < 4; ++i) {
           const uint32_t word = r.w[4 + 8 * (j >> 1) + 4 * half16 + i];
           const uint32_t code = (word >> (4 * (j & 1))) & 0x0f0f0f0fu;
-          code4_q4<kExact>(code, ds, nk, dm, out[2 * i], out[2 * i + 1]);
+          code4<kExact, true>(code, ds, nk, 1024.f, dm, out[2 * i], out[2 * i + 1]);
         }
         emit(jj * 16 + half16 * 8, out);
       }

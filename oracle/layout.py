@@ -4,10 +4,15 @@ This is the build's own lossless byte layout (the reference's analogue is the TP
 repack ``kaggle/packed_q6/layout.py:49-108``, which groups 64 rows x 256 values into
 separate ql/qh/scale/d regions). Here a tile is 128 rows x one 256-value block, tiles are
 ordered ``[row_tile][k_block]`` and rows are zero-padded to a multiple of 128. Inside a
-tile the first ``16 * C`` bytes of every row's block are stored as ``[chunk c][row r][16 B]``
-(``C = 13`` for Q6_K: block bytes 0..207; ``C = 9`` for Q4_K: the whole 144-byte block), and
-Q6_K appends the rows' FP16 scales as ``[row][2 B]`` (block bytes 208..209). Thread ``r`` of
-the tensor-core kernels' decode warps reads chunk ``c`` of its row at ``(c*128 + r)*16``.
+tile the first ``16 * C`` bytes of every row's (re-packed) block are stored as
+``[chunk c][row r][16 B]`` (``C = 13`` for Q6_K, ``C = 9`` for Q4_K), and Q6_K appends the
+rows' FP16 scales as ``[row][2 B]`` (block bytes 208..209). Thread ``r`` of the tensor-core
+kernels' decode warps reads chunk ``c`` of its row at ``(c*128 + r)*16``.
+
+Q4_K blocks keep their GGUF bytes. Q6_K blocks re-pack the 6-bit codes losslessly: sub-block
+``j`` (values ``16j .. 16j+15``) becomes three little-endian words ``W0, W1, W2`` at bytes
+``12j .. 12j+11``; byte ``i`` of ``Wn`` holds code ``4n + i`` in bits 0..5 and bits
+``2n .. 2n+1`` of code ``12 + i`` in bits 6..7. Bytes 192..207 are the sub-scales.
 """
 
 import numpy as np
@@ -27,12 +32,61 @@ def tiled_bytes(qtype, rows, row_width):
     return padded_rows(rows) // TILE_ROWS * nblk * TILE_BYTES[qtype]
 
 
+def _q6_codes(raw):
+    """6-bit codes ``[..., 256]`` of Q6_K blocks (position rule of packed_q6/reference.py:21-27)."""
+    p = np.arange(256)
+    half, quarter, lane = p // 128, (p % 128) // 32, p % 32
+    lo = (raw[..., half * 64 + (quarter % 2) * 32 + lane] >> (4 * (quarter // 2))) & 15
+    hi = (raw[..., 128 + half * 32 + lane] >> (2 * quarter)) & 3
+    return (lo | (hi << 4)).astype(np.uint8)
+
+
+def _q6_from_codes(u):
+    """Inverse of :func:`_q6_codes` -> ql/qh bytes ``[..., 192]``."""
+    p = np.arange(256)
+    half, quarter, lane = p // 128, (p % 128) // 32, p % 32
+    out = np.zeros(u.shape[:-1] + (192,), np.uint8)
+    lo_idx = half * 64 + (quarter % 2) * 32 + lane
+    hi_idx = 128 + half * 32 + lane
+    for pos in range(256):  # small fixtures only
+        out[..., lo_idx[pos]] |= ((u[..., pos] & 15) << (4 * (quarter[pos] // 2))).astype(np.uint8)
+        out[..., hi_idx[pos]] |= ((u[..., pos] >> 4) << (2 * quarter[pos])).astype(np.uint8)
+    return out
+
+
+def repack_q6_codes(raw):
+    """GGUF Q6_K bytes ``[..., 210]`` -> re-packed bytes ``[..., 210]`` (codes, sub-scales, d)."""
+    raw = np.asarray(raw, np.uint8)
+    u = _q6_codes(raw).reshape(raw.shape[:-1] + (16, 16))  # [..., sub-block, value]
+    words = np.zeros(raw.shape[:-1] + (16, 3, 4), np.uint8)
+    for n in range(3):
+        words[..., n, :] = u[..., 4 * n : 4 * n + 4] | (((u[..., 12:16] >> (2 * n)) & 3) << 6)
+    out = raw.copy()
+    out[..., :192] = words.reshape(raw.shape[:-1] + (192,))
+    return out
+
+
+def unrepack_q6_codes(packed):
+    """Inverse of :func:`repack_q6_codes`."""
+    packed = np.asarray(packed, np.uint8)
+    words = packed[..., :192].reshape(packed.shape[:-1] + (16, 3, 4))
+    u = np.zeros(packed.shape[:-1] + (16, 16), np.uint8)
+    for n in range(3):
+        u[..., 4 * n : 4 * n + 4] = words[..., n, :] & 63
+        u[..., 12:16] |= ((words[..., n, :] >> 6) & 3) << (2 * n)
+    out = packed.copy()
+    out[..., :192] = _q6_from_codes(u.reshape(packed.shape[:-1] + (256,)))
+    return out
+
+
 def tile(raw, qtype):
     """``uint8[rows, nblk, bpb]`` -> flat tiled bytes."""
     raw = np.asarray(raw, np.uint8)
     rows, nblk, size = raw.shape
     if size != BLOCK_BYTES[qtype]:
         raise ValueError(f"{qtype} blocks contain {BLOCK_BYTES[qtype]} bytes")
+    if qtype == "Q6_K":
+        raw = repack_q6_codes(raw)
     full = np.zeros((padded_rows(rows), nblk, size), np.uint8)
     full[:rows] = raw
     t = full.reshape(-1, TILE_ROWS, nblk, size).transpose(0, 2, 1, 3)  # [G, kb, row, B]
@@ -56,4 +110,5 @@ def untile(tiled, qtype, rows, row_width):
     out[..., : 16 * c] = body.reshape(g, nblk, TILE_ROWS, 16 * c)
     if qtype == "Q6_K":
         out[..., 208:210] = t[..., 16 * c * TILE_ROWS :].reshape(g, nblk, TILE_ROWS, 2)
-    return out.transpose(0, 2, 1, 3).reshape(-1, nblk, size)[:rows]
+    raw = out.transpose(0, 2, 1, 3).reshape(-1, nblk, size)[:rows]
+    return unrepack_q6_codes(raw) if qtype == "Q6_K" else raw
