@@ -80,6 +80,10 @@ SIGNATURES = {
         _i,
         [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _i, _p, _p, _sz, _p],
     ),
+    "qk_kv_q8_decode_attention_noalloc": (
+        _i,
+        [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _i, _p, _p],
+    ),
 }
 
 _lib = None

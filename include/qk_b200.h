@@ -190,6 +190,22 @@ int qk_kv_q8_decode_attention(const uint16_t* q, const int8_t* k_codes, const in
                               int hq, int kv_heads, int head_dim, uint16_t* out, void* workspace,
                               size_t workspace_bytes, qk_stream_t stream);
 
+/* No counterpart in the reference. qk_kv_q8_decode_attention without a workspace, for
+ * callers that cannot provide device memory at the call. The split scratch is a fixed
+ * 4 MiB array in the library's device image (QK_ATTN_STATIC_SCRATCH_BYTES). A geometry
+ * whose qk_kv_q8_attention_workspace_bytes() exceeds it returns QK_ERR_WORKSPACE and
+ * runs nothing. The first call on a device looks up the array's address, so make it
+ * before any stream capture. The scratch is shared per device, so overlapping calls
+ * (other streams or threads) race on it; calls in order on one stream are safe. */
+#define QK_ATTN_STATIC_SCRATCH_BYTES (4u << 20)
+int qk_kv_q8_decode_attention_noalloc(const uint16_t* q, const int8_t* k_codes,
+                                      const int8_t* v_codes, const uint16_t* k_scale,
+                                      const uint16_t* v_scale, const int32_t* indices,
+                                      const uint8_t* valid, const int32_t* lengths,
+                                      const uint16_t* gate, int B, int S, int T, int hq,
+                                      int kv_heads, int head_dim, uint16_t* out,
+                                      qk_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif
