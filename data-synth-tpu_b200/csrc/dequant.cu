@@ -129,13 +129,13 @@ __global__ void dequant_rows_kernel(const uint8_t* __restrict__ raw, int qtype, 
 // ---- tiled layout (the format is stated in oracle/layout.py and rowtile.cuh) ----
 
 inline int tile_bytes(int qtype) {
-  return qtype == QK_TYPE_Q6_K ? RowTile<QType::Q6_K>::kBytes
-         : qtype == QK_TYPE_Q4_K ? RowTile<QType::Q4_K>::kBytes
+  return qtype == QK_TYPE_Q6_K ? HalfTile<QType::Q6_K>::kBytes
+         : qtype == QK_TYPE_Q4_K ? HalfTile<QType::Q4_K>::kBytes
                                  : 0;
 }
 
-// Byte offset, inside a 128-row tile, of 32-bit word w of row r.
-__device__ __forceinline__ int tile_word(int r, int w) { return ((w >> 2) * 128 + r) * 16 + (w & 3) * 4; }
+// Byte offset, inside a 64-row tile, of 32-bit word w of row r.
+__device__ __forceinline__ int tile_word(int r, int w) { return ((w >> 2) * kTileRows + r) * 16 + (w & 3) * 4; }
 
 // Q6_K code of position p of a GGUF block (packed_q6/reference.py:21-27 position rule).
 __device__ __forceinline__ uint32_t q6_code(const uint8_t* blk, int p) {
@@ -148,13 +148,14 @@ __device__ __forceinline__ uint32_t q6_code(const uint8_t* blk, int p) {
 // One thread per (tile row, sub-block j) - 16 codes -> 3 words; j == 16 copies the
 // sub-scale words and d. kPack: raw -> tiled, else tiled -> raw.
 template <bool kPack>
-__global__ void __launch_bounds__(128) repack_q6_kernel(const uint8_t* __restrict__ in, uint8_t* __restrict__ out,
-                                                        int64_t rows, int64_t nblk, int32_t* bad_scales) {
-  constexpr int TB = RowTile<QType::Q6_K>::kBytes;
+__global__ void __launch_bounds__(kTileRows) repack_q6_kernel(const uint8_t* __restrict__ in, uint8_t* __restrict__ out,
+                                                              int64_t rows, int64_t nblk, int32_t* bad_scales) {
+  constexpr int TB = HalfTile<QType::Q6_K>::kBytes;
+  constexpr int kScaleOff = HalfTile<QType::Q6_K>::kScaleOff;
   const int64_t tile = blockIdx.x;
   const int64_t strip = tile / nblk, kb = tile % nblk;
   const int r = threadIdx.x;
-  const int64_t row = strip * 128 + r;
+  const int64_t row = strip * kTileRows + r;
   const bool real = row < rows;
   uint8_t* traw_out = nullptr;
   const uint8_t* blk = nullptr;
@@ -184,7 +185,7 @@ __global__ void __launch_bounds__(128) repack_q6_kernel(const uint8_t* __restric
       *reinterpret_cast<uint32_t*>(t + tile_word(r, 48 + n)) = v;
     }
     const uint16_t d = real ? static_cast<uint16_t>(blk[208] | (blk[209] << 8)) : 0;
-    *reinterpret_cast<uint16_t*>(t + 13 * 2048 + r * 2) = d;
+    *reinterpret_cast<uint16_t*>(t + kScaleOff + r * 2) = d;
     if (bad_scales && (d & 0x7c00) == 0x7c00) atomicAdd(bad_scales, 1);
   } else if (real) {
     uint8_t b[208];
@@ -211,7 +212,7 @@ __global__ void __launch_bounds__(128) repack_q6_kernel(const uint8_t* __restric
       for (int i = 0; i < 4; ++i) b[192 + 4 * n + i] = static_cast<uint8_t>(v >> (8 * i));
     }
     for (int i = 0; i < 208; ++i) traw_out[i] = b[i];
-    const uint16_t d = *reinterpret_cast<const uint16_t*>(tin + 13 * 2048 + r * 2);
+    const uint16_t d = *reinterpret_cast<const uint16_t*>(tin + kScaleOff + r * 2);
     traw_out[208] = static_cast<uint8_t>(d & 0xff);
     traw_out[209] = static_cast<uint8_t>(d >> 8);
   }
@@ -221,12 +222,12 @@ __global__ void __launch_bounds__(128) repack_q6_kernel(const uint8_t* __restric
 template <bool kPack>
 __global__ void repack_q4_kernel(const uint8_t* __restrict__ in, uint8_t* __restrict__ out, int64_t rows,
                                  int64_t nblk, int32_t* bad_scales) {
-  constexpr int TB = RowTile<QType::Q4_K>::kBytes;
+  constexpr int TB = HalfTile<QType::Q4_K>::kBytes;
   const int64_t tile = blockIdx.x;
   const int64_t strip = tile / nblk, kb = tile % nblk;
   for (int off = threadIdx.x; off < TB; off += blockDim.x) {
-    const int r = (off & 2047) >> 4, src = (off >> 11) * 16 + (off & 15);
-    const int64_t row = strip * 128 + r;
+    const int r = (off & 1023) >> 4, src = (off >> 10) * 16 + (off & 15);
+    const int64_t row = strip * kTileRows + r;
     const int64_t raw_off = (row * nblk + kb) * 144 + src;
     const int64_t tiled_off = tile * TB + off;
     if (kPack) {
@@ -242,21 +243,21 @@ __global__ void repack_q4_kernel(const uint8_t* __restrict__ in, uint8_t* __rest
   }
 }
 
-// Decode of the tiled layout through the row decoders of the tensor-core kernels: kExact
-// selects the reference-exact form (signed zeros included), otherwise the fused form the
-// kernels run (equal values; a zero may carry the other sign). One thread per tile row.
+// Decode of the tiled layout through the half-block decoders of the tensor-core kernels:
+// kExact selects the reference-exact form (signed zeros included), otherwise the fused
+// form the kernels run (equal values; a zero may carry the other sign). One thread per
+// (tile row, half block).
 template <QType QT, bool kExact>
-__global__ void __launch_bounds__(128) dequant_tiled_kernel(const uint8_t* __restrict__ tiled, int64_t rows,
-                                                            int64_t width, int64_t nblk, int out_bf16,
-                                                            void* __restrict__ out) {
-  using RT = RowTile<QT>;
+__global__ void __launch_bounds__(2 * kTileRows) dequant_tiled_kernel(const uint8_t* __restrict__ tiled, int64_t rows,
+                                                                      int64_t width, int64_t nblk, int out_bf16,
+                                                                      void* __restrict__ out) {
+  using HT = HalfTile<QT>;
   const int64_t tile = blockIdx.x;
   const int64_t strip = tile / nblk, kb = tile % nblk;
-  const int r = threadIdx.x;
-  const int64_t row = strip * 128 + r;
+  const int r = threadIdx.x % kTileRows, h = threadIdx.x / kTileRows;
+  const int64_t row = strip * kTileRows + r;
   if (row >= rows) return;
-  typename RT::Regs regs;
-  RT::load(regs, tiled + tile * RT::kBytes, r);
+  const uint8_t* t = tiled + tile * HT::kBytes;
   auto store = [&](int64_t k0, const uint32_t(&o)[8]) {
     for (int i = 0; i < 16; ++i) {
       const int64_t k = k0 + i;
@@ -266,8 +267,14 @@ __global__ void __launch_bounds__(128) dequant_tiled_kernel(const uint8_t* __res
       else static_cast<float*>(out)[row * width + k] = bf16_to_f32(bits);
     }
   };
-  RT::template decode_half<kExact, 0>(regs, [&](int col, const uint32_t(&o)[8]) { store(kb * 256 + 2 * col, o); });
-  RT::template decode_half<kExact, 1>(regs, [&](int col, const uint32_t(&o)[8]) { store(kb * 256 + 128 + 2 * col, o); });
+  typename HT::Regs regs;
+  if (h == 0) {
+    HT::template load<0>(regs, t, r);
+    HT::template decode<kExact, 0>(regs, [&](int col, const uint32_t(&o)[8]) { store(kb * 256 + 2 * col, o); });
+  } else {
+    HT::template load<1>(regs, t, r);
+    HT::template decode<kExact, 1>(regs, [&](int col, const uint32_t(&o)[8]) { store(kb * 256 + 128 + 2 * col, o); });
+  }
 }
 
 int grid_for(int64_t total, int block) {
@@ -301,7 +308,7 @@ int qk_dequantize_rows(const uint8_t* raw, int qtype, int64_t rows, int64_t row_
 int64_t qk_tiled_bytes(int qtype, int64_t rows, int64_t row_width) {
   const int tb = tile_bytes(qtype);
   if (tb == 0 || rows < 0 || row_width <= 0) return -1;
-  return (rows + 127) / 128 * ((row_width + 255) / 256) * tb;
+  return (rows + kTileRows - 1) / kTileRows * ((row_width + 255) / 256) * tb;
 }
 
 static int repack_common(const uint8_t* in, int qtype, int64_t rows, int64_t row_width,
@@ -311,13 +318,13 @@ static int repack_common(const uint8_t* in, int qtype, int64_t rows, int64_t row
   QK_REQUIRE(rows > 0 && row_width > 0, "Expected [output_features, ceil(input_features / 256), bytes]");
   QK_REQUIRE(in && out, "null pointer");
   const int64_t nblk = (row_width + 255) / 256;
-  const int64_t tiles = (rows + 127) / 128 * nblk;
+  const int64_t tiles = (rows + kTileRows - 1) / kTileRows * nblk;
   QK_REQUIRE(tiles < (1ll << 31), "too many tiles");
   const unsigned g = static_cast<unsigned>(tiles);
   cudaStream_t st = as_stream(stream);
   if (qtype == QK_TYPE_Q6_K) {
-    if (pack) repack_q6_kernel<true><<<g, 128, 0, st>>>(in, out, rows, nblk, bad);
-    else repack_q6_kernel<false><<<g, 128, 0, st>>>(in, out, rows, nblk, nullptr);
+    if (pack) repack_q6_kernel<true><<<g, kTileRows, 0, st>>>(in, out, rows, nblk, bad);
+    else repack_q6_kernel<false><<<g, kTileRows, 0, st>>>(in, out, rows, nblk, nullptr);
   } else {
     if (pack) repack_q4_kernel<true><<<g, 256, 0, st>>>(in, out, rows, nblk, bad);
     else repack_q4_kernel<false><<<g, 256, 0, st>>>(in, out, rows, nblk, nullptr);
@@ -345,16 +352,17 @@ int qk_dequantize_tiled(const uint8_t* tiled, int qtype, int64_t rows, int64_t r
   QK_REQUIRE(out_dtype == QK_OUT_F32 || out_dtype == QK_OUT_BF16, "out_dtype must be F32 or BF16");
   QK_REQUIRE(tiled && out, "null pointer");
   const int64_t nblk = (row_width + 255) / 256;
-  const int64_t tiles = (rows + 127) / 128 * nblk;
+  const int64_t tiles = (rows + kTileRows - 1) / kTileRows * nblk;
+  QK_REQUIRE(tiles < (1ll << 31), "too many tiles");
   const unsigned grid = static_cast<unsigned>(tiles);
   const int bf = out_dtype == QK_OUT_BF16;
   cudaStream_t st = as_stream(stream);
   if (qtype == QK_TYPE_Q6_K) {
-    if (fused) dequant_tiled_kernel<QType::Q6_K, false><<<grid, 128, 0, st>>>(tiled, rows, row_width, nblk, bf, out);
-    else dequant_tiled_kernel<QType::Q6_K, true><<<grid, 128, 0, st>>>(tiled, rows, row_width, nblk, bf, out);
+    if (fused) dequant_tiled_kernel<QType::Q6_K, false><<<grid, 2 * kTileRows, 0, st>>>(tiled, rows, row_width, nblk, bf, out);
+    else dequant_tiled_kernel<QType::Q6_K, true><<<grid, 2 * kTileRows, 0, st>>>(tiled, rows, row_width, nblk, bf, out);
   } else {
-    if (fused) dequant_tiled_kernel<QType::Q4_K, false><<<grid, 128, 0, st>>>(tiled, rows, row_width, nblk, bf, out);
-    else dequant_tiled_kernel<QType::Q4_K, true><<<grid, 128, 0, st>>>(tiled, rows, row_width, nblk, bf, out);
+    if (fused) dequant_tiled_kernel<QType::Q4_K, false><<<grid, 2 * kTileRows, 0, st>>>(tiled, rows, row_width, nblk, bf, out);
+    else dequant_tiled_kernel<QType::Q4_K, true><<<grid, 2 * kTileRows, 0, st>>>(tiled, rows, row_width, nblk, bf, out);
   }
   QK_LAUNCHED("dequant_tiled_kernel");
   return QK_OK;

@@ -1,10 +1,10 @@
 // Packed-weight projection: out[M, N] (FP32) = bf16 x[M, K] @ bf16(decode(W))[N, K]^T.
 //
 // Replaces packed_q6/kernel.py:98-148 (q6_matmul) and its XLA baseline
-// packed_q6/baselines.py:33-39. The weights stay packed in HBM (128-row Q6_K / Q4_K tiles);
+// packed_q6/baselines.py:33-39. The weights stay packed in HBM (64-row Q6_K / Q4_K tiles);
 // the tcgen05 pass of umma_proj.cuh decodes them into TMEM and multiplies with FP32
 // accumulation. x is first packed into the tensor core's activation-tile layout (chunks of
-// 64 rows, zero padding for ragged M and K, as the reference zero-pads, kernel.py:139-140);
+// 32 rows, zero padding for ragged M and K, as the reference zero-pads, kernel.py:139-140);
 // rows at or beyond N are not stored.
 #include "common.cuh"
 #include "umma_proj.cuh"
@@ -99,8 +99,8 @@ int qk_quant_gemm(const uint16_t* x, int64_t M, int64_t K, const uint8_t* w_tile
   a.wa = w_tiled;
   a.expert_bytes = 0;
   a.nkb = nkb;
-  a.rowtiles = static_cast<int>((N + 127) / 128);
-  a.pairs = (a.rowtiles + 1) / 2;
+  a.tiles64 = static_cast<int>((N + kTileRows - 1) / kTileRows);
+  a.items_per_chunk = static_cast<int>((N + 2 * kTileRows - 1) / (2 * kTileRows));
   a.xt = static_cast<const uint8_t*>(workspace);
   a.n_chunks_dense = static_cast<int>((M + kMaxTok - 1) / kMaxTok);
   a.m_dense = static_cast<int>(M);
@@ -109,7 +109,7 @@ int qk_quant_gemm(const uint16_t* x, int64_t M, int64_t K, const uint8_t* w_tile
   // then added in K order (the per-block accumulation of packed_q6/kernel.py:95-107).
   a.ksplit = nkb > 1;
   a.out = a.ksplit ? reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + xt_bytes(M, K)) : out;
-  const int64_t items = static_cast<int64_t>(a.n_chunks_dense) * a.pairs * (a.ksplit ? nkb : 1);
+  const int64_t items = static_cast<int64_t>(a.n_chunks_dense) * a.items_per_chunk * (a.ksplit ? nkb : 1);
   const int grid = static_cast<int>(items < sms ? items : sms);
   int rc = qtype == QK_TYPE_Q6_K ? launch_umma<QType::Q6_K, kModeDense>(a, grid, st)
                                  : launch_umma<QType::Q4_K, kModeDense>(a, grid, st);

@@ -10,11 +10,11 @@
 //                out the token chunks (<= 64 entries of one expert) of the next passes.
 //  2. dispatch - copies each entry's x row into the activation tiles of its chunk (BF16,
 //                128-byte-swizzled K-major: the tensor core's shared-memory operand layout).
-//  3. gate/up  - tcgen05 pass (umma_proj.cuh): per (chunk, 128 rows of I), gate and up
-//                tiles decoded into TMEM, FP32 accumulators; epilogue
+//  3. gate/up  - tcgen05 pass (umma_proj.cuh): per (chunk, 64 rows of I), gate and up
+//                rows decoded into one 128-lane TMEM operand, FP32 accumulators; epilogue
 //                h = bf16(silu(bf16(x Wg^T)) * bf16(x Wu^T)) (experts.py:103-107,
 //                math.py:10-20) written as the activation tiles of the down pass.
-//  4. down     - tcgen05 pass, per (chunk, 256 rows of H): y = bf16(h Wd^T).
+//  4. down     - tcgen05 pass, per (chunk, 128 rows of H): y = bf16(h Wd^T).
 //  5. combine  - per token, FP32 sum of f32(y) * f32(route) over its experts in ascending
 //                expert order (the reference's accumulation order, experts.py:129), then
 //                BF16 (experts.py:131), or the FP32 partial sum for an EP all-reduce.
@@ -378,8 +378,8 @@ static int moe_forward_impl(const qk_moe_desc* desc, const uint8_t* gate, const 
   gu.wb = up;
   gu.expert_bytes = qk_tiled_bytes(d.gate_type, d.intermediate, d.hidden);
   gu.nkb = d.hidden / 256;
-  gu.rowtiles = d.intermediate / 128;
-  gu.pairs = d.intermediate / 128;
+  gu.tiles64 = d.intermediate / kTileRows;
+  gu.items_per_chunk = d.intermediate / kTileRows;  // 64 rows of I (gate + up) per MMA tile
   gu.xt = ws.xt;
   gu.n_chunks_p = &ws.meta->n_chunks;
   gu.chunk_off = ws.chunk_off;
@@ -397,8 +397,8 @@ static int moe_forward_impl(const qk_moe_desc* desc, const uint8_t* gate, const 
   dn.wb = nullptr;
   dn.expert_bytes = qk_tiled_bytes(d.down_type, d.hidden, d.intermediate);
   dn.nkb = d.intermediate / 256;
-  dn.rowtiles = d.hidden / 128;
-  dn.pairs = (d.hidden / 128 + 1) / 2;
+  dn.tiles64 = d.hidden / kTileRows;
+  dn.items_per_chunk = d.hidden / (2 * kTileRows);
   dn.xt = ws.ht;
   dn.ht = nullptr;
   dn.y = ws.y;

@@ -1,26 +1,31 @@
-// 128-row weight tiles and their thread-per-row decode into BF16 TMEM columns.
+// 64-row weight tiles and their half-block decode into BF16 TMEM columns.
 //
-// Layout of one matrix W[rows, K] (rows zero-padded to a multiple of 128): tiles of 128
-// rows x one 256-value GGUF block, ordered [row tile][k block]. Inside a tile the first
-// 16 * C bytes of every row's block are stored as [chunk c][row r][16 B] (C = 13 for Q6_K,
-// C = 9 for Q4_K); Q6_K then holds the rows' FP16 scale d as [row][2 B]. Thread r of the
-// decode warps reads chunk c of its row at (c * 128 + r) * 16 - consecutive rows are
-// consecutive 16-byte words, so the shared-memory reads are conflict free - and decodes
-// the row in natural K order.
+// Layout of one matrix W[rows, K] (rows zero-padded to a multiple of 64): tiles of 64 rows x
+// one 256-value GGUF block, ordered [row tile][k block]. Inside a tile the first 16 * C
+// bytes of every row's block are stored as [chunk c][row r][16 B] (C = 13 for Q6_K, C = 9
+// for Q4_K); Q6_K then holds the rows' FP16 scale d as [row][2 B]. A decode thread owning
+// row r reads chunk c at (c * 64 + r) * 16 - consecutive rows are consecutive 16-byte
+// words, so the shared-memory reads of a warp are conflict free.
+//
+// Each block is decoded as two halves (values 0..127 and 128..255) by two different
+// threads; a half needs only its own chunks:
+//   Q6_K half h: code chunks 6h .. 6h + 5, the sub-scale chunk 12 (8 bytes of it) and d;
+//   Q4_K half h: chunk 0 (d, dmin, packed scales) and quant chunks 1 + 4h .. 4 + 4h.
 //
 // Q4_K rows keep the GGUF block bytes. Q6_K rows re-pack the 6-bit codes (a lossless bit
 // permutation, still 192 bytes per block): sub-block j (values 16j .. 16j + 15, one int8
 // sub-scale) is three words W0, W1, W2 at bytes 12j .. 12j + 11, where byte i of Wn holds
-// code 4n + i in bits 0..5 and bits 2m..2m+1 of code 12 + i in bits 6..7 (m = n). Codes
-// 0..11 then need one AND per four codes, codes 12..15 a shift-and-or of the three words.
+// code 4n + i in bits 0..5 and bits 2n..2n+1 of code 12 + i in bits 6..7. Codes 0..11
+// then need one AND per four codes, codes 12..15 a shift-and-or of the three words.
 // Bytes 192..207 are the int8 sub-scales and the FP16 d follows in the scale plane.
 //
 // Values: the reference decodes (d * sc) * q (Q6_K) and (d * sc) * q - dmin * m (Q4_K)
 // in FP32 and rounds to BF16 (glm53_offload/gguf_quant.py:154-157,171). The products are
-// exact in FP32, so one fused multiply-add per element reproduces them:
-//   code -> FP16 1024 + code (byte permute, two codes per instruction) -> FP32;
-//   Q6_K: w = fma(v, ds, -1056 ds) = (code - 32) ds (1056 ds is exact: 33 ds needs <= 24 bits);
-//   Q4_K: w = fma(v, ds, -1024 ds) - dmin m.
+// exact in FP32 (d * sc needs at most 18 significant bits, the code 6), so one fused
+// multiply-add per element reproduces them. The code enters as the FP32 number
+// f = 0.5 + code / 256, built by one byte permute (exponent byte 0x3F, code in bits 16..23):
+//   Q6_K: w = fma(f, 256 ds, -160 ds) = (code - 32) ds   (160 ds is exact);
+//   Q4_K: w = fma(f, 256 ds, -128 ds) - dmin m.
 // The fused form turns a (d * sc) * 0 of negative sign into +0, which no dot product can
 // see; kExact (the dequantisation entry points) subtracts before multiplying and so
 // reproduces the reference bit for bit, signed zeros included.
@@ -34,6 +39,8 @@ namespace qk {
 
 enum class QType { Q6_K = 14, Q4_K = 12 };
 
+constexpr int kTileRows = 64;
+
 // Two codes (bytes 2P and 2P + 1 of `codes`) as FP32 1024 + code, via an FP16 pair.
 template <int P>
 __device__ __forceinline__ float2 magic1024(uint32_t codes) {
@@ -41,21 +48,28 @@ __device__ __forceinline__ float2 magic1024(uint32_t codes) {
   return __half22float2(*reinterpret_cast<const __half2*>(&h2));
 }
 
+// Code byte I of `codes` (a value below 128) as the FP32 number 0.5 + code / 256.
+template <int I>
+__device__ __forceinline__ float half_plus_code(uint32_t codes) {
+  return __uint_as_float(__byte_perm(codes, 0x3F000000u, 0x7044u | (I << 8)));
+}
+
 // Four codes (bytes of `code`) -> two packed BF16 pairs: w = (code - off) * ds [- dm].
+// s256 = 256 ds and k = -(128 + off) ds feed the fused form; the exact form uses ds, off.
 template <bool kExact, bool kMin>
-__device__ __forceinline__ void code4(uint32_t code, float ds, float nk, float off, float dm,
-                                      uint32_t& lo, uint32_t& hi) {
-  const float2 u01 = magic1024<0>(code), u23 = magic1024<1>(code);
-  const float2 s = make_float2(ds, ds);
+__device__ __forceinline__ void code4(uint32_t code, float ds, float s256, float k, float off,
+                                      float dm, uint32_t& lo, uint32_t& hi) {
   float2 w01, w23;
   if (kExact) {
-    const float2 o = make_float2(-off, -off);
+    const float2 u01 = magic1024<0>(code), u23 = magic1024<1>(code);
+    const float2 o = make_float2(-(1024.f + off), -(1024.f + off));
+    const float2 s = make_float2(ds, ds);
     w01 = __fmul2_rn(__fadd2_rn(u01, o), s);
     w23 = __fmul2_rn(__fadd2_rn(u23, o), s);
   } else {
-    const float2 k = make_float2(nk, nk);
-    w01 = __ffma2_rn(u01, s, k);
-    w23 = __ffma2_rn(u23, s, k);
+    const float2 s2 = make_float2(s256, s256), k2 = make_float2(k, k);
+    w01 = __ffma2_rn(make_float2(half_plus_code<0>(code), half_plus_code<1>(code)), s2, k2);
+    w23 = __ffma2_rn(make_float2(half_plus_code<2>(code), half_plus_code<3>(code)), s2, k2);
   }
   if (kMin) {
     const float2 m = make_float2(-dm, -dm);
@@ -66,85 +80,113 @@ __device__ __forceinline__ void code4(uint32_t code, float ds, float nk, float o
   hi = pack_bf16x2(w23.x, w23.y);
 }
 
+__device__ __forceinline__ uint4 lds128(const uint8_t* p) { return *reinterpret_cast<const uint4*>(p); }
+
 template <QType QT>
-struct RowTile;
+struct HalfTile;
 
 template <>
-struct RowTile<QType::Q6_K> {
+struct HalfTile<QType::Q6_K> {
   static constexpr int kBlockBytes = 210;
   static constexpr int kChunks = 13;
-  static constexpr int kBytes = 128 * kBlockBytes;  // 26880
+  static constexpr int kBytes = kTileRows * kBlockBytes;  // 13440
+  static constexpr int kScaleOff = kChunks * kTileRows * 16;
 
   struct Regs {
-    uint32_t w[52];  // block bytes 0..207: re-packed codes (words 0..47), sub-scales (48..51)
+    uint32_t w[24];  // re-packed codes of sub-blocks 8h .. 8h + 7
+    uint32_t sc[2];  // their int8 sub-scales
     float d;
   };
 
+  // A row that does not exist: decodes to zeros.
+  __device__ __forceinline__ static void clear(Regs& r) {
+#pragma unroll
+    for (int i = 0; i < 24; ++i) r.w[i] = 0;
+    r.sc[0] = r.sc[1] = 0;
+    r.d = 0.f;
+  }
+
+  template <int h>
   __device__ __forceinline__ static void load(Regs& r, const uint8_t* tile, int row) {
 #pragma unroll
-    for (int c = 0; c < kChunks; ++c) {
-      const uint4 v = *reinterpret_cast<const uint4*>(tile + (c * 128 + row) * 16);
+    for (int c = 0; c < 6; ++c) {
+      const uint4 v = lds128(tile + ((6 * h + c) * kTileRows + row) * 16);
       r.w[4 * c] = v.x;
       r.w[4 * c + 1] = v.y;
       r.w[4 * c + 2] = v.z;
       r.w[4 * c + 3] = v.w;
     }
-    r.d = f16_to_f32(*reinterpret_cast<const uint16_t*>(tile + kChunks * 128 * 16 + row * 2));
+    const uint2 s = *reinterpret_cast<const uint2*>(tile + (12 * kTileRows + row) * 16 + 8 * h);
+    r.sc[0] = s.x;
+    r.sc[1] = s.y;
+    r.d = f16_to_f32(*reinterpret_cast<const uint16_t*>(tile + kScaleOff + row * 2));
   }
 
-  // Decode positions 128 h .. 128 h + 127 of the block (h compile-time, so the word
-  // indices are constants and the row stays in registers); emit(col, regs[8]) receives the
-  // 8 packed BF16 pairs of the 16 positions starting at column `col` (= position / 2
-  // inside the half).
+  // emit(col, regs[8]) receives the 8 packed BF16 pairs of the 16 positions starting at
+  // column `col` of the half (column = position / 2 inside the half).
   template <bool kExact, int h, typename Emit>
-  __device__ __forceinline__ static void decode_half(const Regs& r, Emit&& emit) {
+  __device__ __forceinline__ static void decode(const Regs& r, Emit&& emit) {
 #pragma unroll
     for (int jj = 0; jj < 8; ++jj) {
-      const int j = 8 * h + jj;  // sub-block of 16 positions
-      const int sc = static_cast<int8_t>((r.w[48 + (j >> 2)] >> (8 * (j & 3))) & 0xffu);
+      const int sc = static_cast<int8_t>((r.sc[jj >> 2] >> (8 * (jj & 3))) & 0xffu);
       const float ds = __fmul_rn(r.d, static_cast<float>(sc));
-      const float nk = __fmul_rn(ds, -1056.f);
-      const uint32_t w0 = r.w[3 * j], w1 = r.w[3 * j + 1], w2 = r.w[3 * j + 2];
+      const float s256 = __fmul_rn(ds, 256.f), k = __fmul_rn(ds, -160.f);
+      const uint32_t w0 = r.w[3 * jj], w1 = r.w[3 * jj + 1], w2 = r.w[3 * jj + 2];
       const uint32_t c3 = ((w0 >> 6) & 0x03030303u) | ((w1 >> 4) & 0x0c0c0c0cu) | ((w2 >> 2) & 0x30303030u);
       uint32_t out[8];
-      code4<kExact, false>(w0 & 0x3f3f3f3fu, ds, nk, 1056.f, 0.f, out[0], out[1]);
-      code4<kExact, false>(w1 & 0x3f3f3f3fu, ds, nk, 1056.f, 0.f, out[2], out[3]);
-      code4<kExact, false>(w2 & 0x3f3f3f3fu, ds, nk, 1056.f, 0.f, out[4], out[5]);
-      code4<kExact, false>(c3, ds, nk, 1056.f, 0.f, out[6], out[7]);
+      code4<kExact, false>(w0 & 0x3f3f3f3fu, ds, s256, k, 32.f, 0.f, out[0], out[1]);
+      code4<kExact, false>(w1 & 0x3f3f3f3fu, ds, s256, k, 32.f, 0.f, out[2], out[3]);
+      code4<kExact, false>(w2 & 0x3f3f3f3fu, ds, s256, k, 32.f, 0.f, out[4], out[5]);
+      code4<kExact, false>(c3, ds, s256, k, 32.f, 0.f, out[6], out[7]);
       emit(jj * 8, out);
     }
   }
 };
 
 template <>
-struct RowTile<QType::Q4_K> {
+struct HalfTile<QType::Q4_K> {
   static constexpr int kBlockBytes = 144;
   static constexpr int kChunks = 9;
-  static constexpr int kBytes = 128 * kBlockBytes;  // 18432
+  static constexpr int kBytes = kTileRows * kBlockBytes;  // 9216
 
   struct Regs {
-    uint32_t w[36];  // d | dmin << 16 (word 0), 12 scale bytes (1..3), qs (4..35)
+    uint32_t hd[4];  // d | dmin << 16, then the 12 packed scale bytes
+    uint32_t w[16];  // quant bytes of sub-blocks 4h .. 4h + 3
   };
 
-  __device__ __forceinline__ static void load(Regs& r, const uint8_t* tile, int row) {
+  // A row that does not exist: decodes to zeros.
+  __device__ __forceinline__ static void clear(Regs& r) {
 #pragma unroll
-    for (int c = 0; c < kChunks; ++c) {
-      const uint4 v = *reinterpret_cast<const uint4*>(tile + (c * 128 + row) * 16);
-      r.w[4 * c] = v.x;
-      r.w[4 * c + 1] = v.y;
-      r.w[4 * c + 2] = v.z;
-      r.w[4 * c + 3] = v.w;
+    for (int i = 0; i < 4; ++i) r.hd[i] = 0;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) r.w[i] = 0;
+  }
+
+  template <int h>
+  __device__ __forceinline__ static void load(Regs& r, const uint8_t* tile, int row) {
+    const uint4 v = lds128(tile + row * 16);
+    r.hd[0] = v.x;
+    r.hd[1] = v.y;
+    r.hd[2] = v.z;
+    r.hd[3] = v.w;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const uint4 u = lds128(tile + ((1 + 4 * h + c) * kTileRows + row) * 16);
+      r.w[4 * c] = u.x;
+      r.w[4 * c + 1] = u.y;
+      r.w[4 * c + 2] = u.z;
+      r.w[4 * c + 3] = u.w;
     }
   }
 
   __device__ __forceinline__ static int scale_byte(const Regs& r, int i) {
-    return static_cast<int>((r.w[1 + (i >> 2)] >> (8 * (i & 3))) & 0xffu);
+    return static_cast<int>((r.hd[1 + (i >> 2)] >> (8 * (i & 3))) & 0xffu);
   }
 
   template <bool kExact, int h, typename Emit>
-  __device__ __forceinline__ static void decode_half(const Regs& r, Emit&& emit) {
-    const float d = f16_to_f32(static_cast<uint16_t>(r.w[0] & 0xffffu));
-    const float dmin = f16_to_f32(static_cast<uint16_t>(r.w[0] >> 16));
+  __device__ __forceinline__ static void decode(const Regs& r, Emit&& emit) {
+    const float d = f16_to_f32(static_cast<uint16_t>(r.hd[0] & 0xffffu));
+    const float dmin = f16_to_f32(static_cast<uint16_t>(r.hd[0] >> 16));
 #pragma unroll
     for (int jj = 0; jj < 4; ++jj) {
       const int j = 4 * h + jj;  // sub-block of 32 positions (gguf_quant.py:118-135)
@@ -157,16 +199,16 @@ struct RowTile<QType::Q4_K> {
         m = (scale_byte(r, j + 4) >> 4) | ((scale_byte(r, j) >> 6) << 4);
       }
       const float ds = __fmul_rn(d, static_cast<float>(sc));
-      const float nk = __fmul_rn(ds, -1024.f);
+      const float s256 = __fmul_rn(ds, 256.f), k = __fmul_rn(ds, -128.f);
       const float dm = __fmul_rn(dmin, static_cast<float>(m));
 #pragma unroll
       for (int half16 = 0; half16 < 2; ++half16) {
         uint32_t out[8];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          const uint32_t word = r.w[4 + 8 * (j >> 1) + 4 * half16 + i];
+          const uint32_t word = r.w[8 * (jj >> 1) + 4 * half16 + i];
           const uint32_t code = (word >> (4 * (j & 1))) & 0x0f0f0f0fu;
-          code4<kExact, true>(code, ds, nk, 1024.f, dm, out[2 * i], out[2 * i + 1]);
+          code4<kExact, true>(code, ds, s256, k, 0.f, dm, out[2 * i], out[2 * i + 1]);
         }
         emit(jj * 16 + half16 * 8, out);
       }

@@ -1,7 +1,7 @@
 """Lossless tiled repack and the packed-weight projection.
 
 Mirrors ``kaggle/packed_q6``: ``pack_q6``/``unpack_q6`` (``layout.py:49-108``) and
-``q6_matmul`` (``kernel.py:98-148``), with this build's tile layout (128 rows x 256
+``q6_matmul`` (``kernel.py:98-148``), with this build's tile layout (64 rows x 256
 values per tile, see ``csrc/rowtile.cuh``) instead of the TPU SoA tiles. ``pack_rows``
 and ``quant_matmul`` are the type-generic forms (Q6_K, Q4_K).
 """

@@ -2,12 +2,12 @@
 
 This is the build's own lossless byte layout (the reference's analogue is the TPU SoA
 repack ``kaggle/packed_q6/layout.py:49-108``, which groups 64 rows x 256 values into
-separate ql/qh/scale/d regions). Here a tile is 128 rows x one 256-value block, tiles are
-ordered ``[row_tile][k_block]`` and rows are zero-padded to a multiple of 128. Inside a
+separate ql/qh/scale/d regions). Here a tile is 64 rows x one 256-value block, tiles are
+ordered ``[row_tile][k_block]`` and rows are zero-padded to a multiple of 64. Inside a
 tile the first ``16 * C`` bytes of every row's (re-packed) block are stored as
 ``[chunk c][row r][16 B]`` (``C = 13`` for Q6_K, ``C = 9`` for Q4_K), and Q6_K appends the
-rows' FP16 scales as ``[row][2 B]`` (block bytes 208..209). Thread ``r`` of the tensor-core
-kernels' decode warps reads chunk ``c`` of its row at ``(c*128 + r)*16``.
+rows' FP16 scales as ``[row][2 B]`` (block bytes 208..209). A decode thread of the
+tensor-core kernels reads chunk ``c`` of its row ``r`` at ``(c*64 + r)*16``.
 
 Q4_K blocks keep their GGUF bytes. Q6_K blocks re-pack the 6-bit codes losslessly: sub-block
 ``j`` (values ``16j .. 16j+15``) becomes three little-endian words ``W0, W1, W2`` at bytes
@@ -17,7 +17,7 @@ Q4_K blocks keep their GGUF bytes. Q6_K blocks re-pack the 6-bit codes losslessl
 
 import numpy as np
 
-TILE_ROWS = 128
+TILE_ROWS = 64
 BLOCK_BYTES = {"Q6_K": 210, "Q4_K": 144}
 CHUNKS = {"Q6_K": 13, "Q4_K": 9}
 TILE_BYTES = {q: TILE_ROWS * b for q, b in BLOCK_BYTES.items()}
