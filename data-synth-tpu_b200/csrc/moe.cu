@@ -39,6 +39,7 @@ struct Workspace {
   int32_t* offsets;       // [E + 1]
   int32_t* active;        // [E]   active expert ids (local), ascending
   int32_t* chunk_off;     // [E + 1] first chunk of each active slot
+  int4* chunk_rec;        // [chunks_max] per chunk: {expert, tokens, first entry, first tile row}
   int32_t* row_off;       // [E + 1] first activation-tile row of each active slot
   int32_t* entry_token;   // [B k] token of each entry (expert-sorted)
   float* entry_weight;    // [B k] bf16-valued route weight of each entry
@@ -51,6 +52,13 @@ struct Workspace {
 inline size_t align256(size_t n) { return (n + 255) & ~size_t(255); }
 
 // Activation-tile rows: each active expert's entries rounded up to 16 per chunk.
+// Token chunks: each active expert's entries in runs of kMaxTok.
+inline size_t chunks_bound(const qk_moe_desc& d, int max_tokens) {
+  const size_t R = static_cast<size_t>(max_tokens) * d.top_k;
+  const size_t E = static_cast<size_t>(d.num_experts);
+  return (R + kMaxTok - 1) / kMaxTok + (E < R ? E : R);
+}
+
 inline size_t rows_bound(const qk_moe_desc& d, int max_tokens) {
   const size_t R = static_cast<size_t>(max_tokens) * d.top_k;
   const size_t E = static_cast<size_t>(d.num_experts);
@@ -71,6 +79,7 @@ size_t layout(const qk_moe_desc& d, int max_tokens, uint8_t* base, Workspace* ws
   uint8_t* offsets = take((E + 1) * 4);
   uint8_t* active = take(E * 4);
   uint8_t* chunk_off = take((E + 1) * 4);
+  uint8_t* chunk_rec = take(chunks_bound(d, max_tokens) * sizeof(int4));
   uint8_t* row_off = take((E + 1) * 4);
   uint8_t* et = take(R * 4);
   uint8_t* ew = take(R * 4);
@@ -84,6 +93,7 @@ size_t layout(const qk_moe_desc& d, int max_tokens, uint8_t* base, Workspace* ws
     ws->offsets = reinterpret_cast<int32_t*>(offsets);
     ws->active = reinterpret_cast<int32_t*>(active);
     ws->chunk_off = reinterpret_cast<int32_t*>(chunk_off);
+    ws->chunk_rec = reinterpret_cast<int4*>(chunk_rec);
     ws->row_off = reinterpret_cast<int32_t*>(row_off);
     ws->entry_token = reinterpret_cast<int32_t*>(et);
     ws->entry_weight = reinterpret_cast<float*>(ew);
@@ -203,6 +213,18 @@ __global__ void __launch_bounds__(1024) moe_route_kernel(const int32_t* __restri
     }
   }
   __syncthreads();
+
+  // Chunk records: the tensor-core passes read one record per token chunk instead of
+  // searching the chunk tables.
+  {
+    const int n_act = ws.meta->n_active;
+    for (int a = tid; a < n_act; a += nt) {
+      const int e = ws.active[a], m = counts[e], nch = (m + kMaxTok - 1) / kMaxTok;
+      const int c0 = ws.chunk_off[a], r0 = ws.row_off[a], e0 = offsets[e];
+      for (int ch = 0; ch < nch; ++ch)
+        ws.chunk_rec[c0 + ch] = make_int4(e, min(kMaxTok, m - kMaxTok * ch), e0 + kMaxTok * ch, r0 + kMaxTok * ch);
+    }
+  }
 
   // Pass 2: place entries.
   for (int b = tid; b < B; b += nt) {
@@ -383,6 +405,7 @@ static int moe_forward_impl(const qk_moe_desc* desc, const uint8_t* gate, const 
   gu.xt = ws.xt;
   gu.n_chunks_p = &ws.meta->n_chunks;
   gu.chunk_off = ws.chunk_off;
+  gu.chunk_rec = ws.chunk_rec;
   gu.row_off = ws.row_off;
   gu.active = ws.active;
   gu.counts = ws.counts;

@@ -22,10 +22,9 @@
 // Values: the reference decodes (d * sc) * q (Q6_K) and (d * sc) * q - dmin * m (Q4_K)
 // in FP32 and rounds to BF16 (glm53_offload/gguf_quant.py:154-157,171). The products are
 // exact in FP32 (d * sc needs at most 18 significant bits, the code 6), so one fused
-// multiply-add per element reproduces them. The code enters as the FP32 number
-// f = 0.5 + code / 256, built by one byte permute (exponent byte 0x3F, code in bits 16..23):
-//   Q6_K: w = fma(f, 256 ds, -160 ds) = (code - 32) ds   (160 ds is exact);
-//   Q4_K: w = fma(f, 256 ds, -128 ds) - dmin m.
+// multiply-add per element reproduces them (see code4):
+//   Q6_K: w = fma(1024 + code, ds, -1056 ds) = (code - 32) ds   (1056 ds is exact);
+//   Q4_K: w = fma(1024 + code, ds, -1024 ds) - dmin m.
 // The fused form turns a (d * sc) * 0 of negative sign into +0, which no dot product can
 // see; kExact (the dequantisation entry points) subtracts before multiplying and so
 // reproduces the reference bit for bit, signed zeros included.
@@ -55,10 +54,17 @@ __device__ __forceinline__ float half_plus_code(uint32_t codes) {
 }
 
 // Four codes (bytes of `code`) -> two packed BF16 pairs: w = (code - off) * ds [- dm].
-// s256 = 256 ds and k = -(128 + off) ds feed the fused form; the exact form uses ds, off.
+// The fused forms (kExact false) build the code as a float with byte permutes and apply
+// the scale in one multiply-add; the offsets below keep every product exact:
+//   kDecodeViaHalf: u = 1024 + code via an FP16 pair (one permute per two codes, the
+//                   FP16 -> FP32 conversions run on the FMA pipe): w = fma(u, ds, -(1024 + off) ds);
+//   otherwise:      f = 0.5 + code / 256 (one permute per code): w = fma(f, 256 ds, -(128 + off) ds).
+// Both constants are exact: (1024 + off) and (128 + off) have at most 6 significant bits.
+constexpr bool kDecodeViaHalf = true;
+
 template <bool kExact, bool kMin>
-__device__ __forceinline__ void code4(uint32_t code, float ds, float s256, float k, float off,
-                                      float dm, uint32_t& lo, uint32_t& hi) {
+__device__ __forceinline__ void code4(uint32_t code, float ds, float off, float dm, uint32_t& lo,
+                                      uint32_t& hi) {
   float2 w01, w23;
   if (kExact) {
     const float2 u01 = magic1024<0>(code), u23 = magic1024<1>(code);
@@ -66,7 +72,13 @@ __device__ __forceinline__ void code4(uint32_t code, float ds, float s256, float
     const float2 s = make_float2(ds, ds);
     w01 = __fmul2_rn(__fadd2_rn(u01, o), s);
     w23 = __fmul2_rn(__fadd2_rn(u23, o), s);
+  } else if (kDecodeViaHalf) {
+    const float k = __fmul_rn(ds, -(1024.f + off));
+    const float2 s2 = make_float2(ds, ds), k2 = make_float2(k, k);
+    w01 = __ffma2_rn(magic1024<0>(code), s2, k2);
+    w23 = __ffma2_rn(magic1024<1>(code), s2, k2);
   } else {
+    const float s256 = __fmul_rn(ds, 256.f), k = __fmul_rn(ds, -(128.f + off));
     const float2 s2 = make_float2(s256, s256), k2 = make_float2(k, k);
     w01 = __ffma2_rn(make_float2(half_plus_code<0>(code), half_plus_code<1>(code)), s2, k2);
     w23 = __ffma2_rn(make_float2(half_plus_code<2>(code), half_plus_code<3>(code)), s2, k2);
@@ -130,14 +142,13 @@ struct HalfTile<QType::Q6_K> {
     for (int jj = 0; jj < 8; ++jj) {
       const int sc = static_cast<int8_t>((r.sc[jj >> 2] >> (8 * (jj & 3))) & 0xffu);
       const float ds = __fmul_rn(r.d, static_cast<float>(sc));
-      const float s256 = __fmul_rn(ds, 256.f), k = __fmul_rn(ds, -160.f);
       const uint32_t w0 = r.w[3 * jj], w1 = r.w[3 * jj + 1], w2 = r.w[3 * jj + 2];
       const uint32_t c3 = ((w0 >> 6) & 0x03030303u) | ((w1 >> 4) & 0x0c0c0c0cu) | ((w2 >> 2) & 0x30303030u);
       uint32_t out[8];
-      code4<kExact, false>(w0 & 0x3f3f3f3fu, ds, s256, k, 32.f, 0.f, out[0], out[1]);
-      code4<kExact, false>(w1 & 0x3f3f3f3fu, ds, s256, k, 32.f, 0.f, out[2], out[3]);
-      code4<kExact, false>(w2 & 0x3f3f3f3fu, ds, s256, k, 32.f, 0.f, out[4], out[5]);
-      code4<kExact, false>(c3, ds, s256, k, 32.f, 0.f, out[6], out[7]);
+      code4<kExact, false>(w0 & 0x3f3f3f3fu, ds, 32.f, 0.f, out[0], out[1]);
+      code4<kExact, false>(w1 & 0x3f3f3f3fu, ds, 32.f, 0.f, out[2], out[3]);
+      code4<kExact, false>(w2 & 0x3f3f3f3fu, ds, 32.f, 0.f, out[4], out[5]);
+      code4<kExact, false>(c3, ds, 32.f, 0.f, out[6], out[7]);
       emit(jj * 8, out);
     }
   }
@@ -199,7 +210,6 @@ struct HalfTile<QType::Q4_K> {
         m = (scale_byte(r, j + 4) >> 4) | ((scale_byte(r, j) >> 6) << 4);
       }
       const float ds = __fmul_rn(d, static_cast<float>(sc));
-      const float s256 = __fmul_rn(ds, 256.f), k = __fmul_rn(ds, -128.f);
       const float dm = __fmul_rn(dmin, static_cast<float>(m));
 #pragma unroll
       for (int half16 = 0; half16 < 2; ++half16) {
@@ -208,7 +218,7 @@ struct HalfTile<QType::Q4_K> {
         for (int i = 0; i < 4; ++i) {
           const uint32_t word = r.w[8 * (jj >> 1) + 4 * half16 + i];
           const uint32_t code = (word >> (4 * (j & 1))) & 0x0f0f0f0fu;
-          code4<kExact, true>(code, ds, s256, k, 0.f, dm, out[2 * i], out[2 * i + 1]);
+          code4<kExact, true>(code, ds, 0.f, dm, out[2 * i], out[2 * i + 1]);
         }
         emit(jj * 16 + half16 * 8, out);
       }

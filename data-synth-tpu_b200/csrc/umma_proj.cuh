@@ -9,25 +9,33 @@
 //
 // One persistent CTA per SM, 25 warps:
 //   warps 0-15  decode, in two groups of 8 that take alternate K-block stages (group g =
-//               warp / 8 decodes stage counter sc with sc % 2 == g into A buffer g). In a
+//               warp / 8 decodes the stages sc with sc % 2 == g, into A buffer sc % 3). In a
 //               group, warp w decodes half h = (w / 4) % 2 of the block for TMEM lanes
 //               32 (w % 4) .. + 31: it reads its row's half block from the shared-memory
-//               stage, frees the stage, decodes 128 values into BF16 and stores them with
-//               tcgen05.st into its lane (64 columns).
-//   warp 16     producer: one lane streams each stage's two weight tiles and the chunk's
-//               activation tile (already in the 128-byte-swizzled K-major layout) into a
-//               shared-memory ring with 1-D bulk copies (TMA engine, no multicast).
+//               weight ring into registers, frees the slot, decodes 128 values into BF16
+//               and stores them with tcgen05.st into its lane (64 columns).
+//   warp 16     producer: one lane issues, per stage, the activation tile (already in the
+//               128-byte-swizzled K-major layout) and then the two weight tiles as 1-D bulk
+//               copies (TMA engine, no multicast). Issued together they land together: the
+//               SM's copy queue is kept deep by the weight stream, and an activation tile
+//               requested later would arrive microseconds after the decoded weights.
+//               Weight slots are freed by the decode (right after its register load), so
+//               the stream runs ahead by the whole weight ring; activation tiles live in a
+//               64 KB ring of 8 KB granules (16 tokens x one K block each) until their MMAs
+//               complete.
 //   warps 17-20 MMA: lane 0 of issuer i issues, per stage, the 4 tcgen05.mma kind::f16
 //               (M = 128, N = chunk tokens rounded to 16, K = 16) of K atom i (values
 //               64i .. 64i + 63 of the block) with A from TMEM and B from shared memory
 //               into its own FP32 accumulator, and signals with tcgen05.commit. One thread
-//               issues an MMA only every ~60 cycles whatever N is, so four issuers (one
-//               per scheduler) keep the tensor core fed at N = 16.
-//   warps 21-24 epilogue: read the four accumulators (tcgen05.ld), release them, add
-//               them, and write h = SwiGLU (gate/up), y (down) or the FP32 output (dense).
-// TMEM: A buffers [0, 256) (2 x 128 columns = 256 BF16 of K per lane), accumulators
-// [256, 512) (2 buffers x 4 issuers x kMaxTok columns). Every wait is bounded; on
-// give-up the CTA records QK_ERR_TIMEOUT in `status` and leaves its loops.
+//               issues an MMA only every ~60 cycles (more when the decode warps saturate
+//               the schedulers) whatever N is, so four issuers - one per scheduler - share
+//               the stage.
+//   warps 21-24 epilogue: read the four accumulators (tcgen05.ld), add them, release them,
+//               and write h = SwiGLU (gate/up), y (down) or the FP32 output (dense).
+// TMEM: A buffers [0, 384) (3 x 128 columns = 256 BF16 of K per lane; three, so a decode
+// group never waits for the MMA of the stage it decoded last), accumulators [384, 512)
+// (4 issuers x kMaxTok columns). Every wait is bounded; on give-up the CTA records
+// QK_ERR_TIMEOUT in `status` and leaves its loops.
 #pragma once
 
 #include "rowtile.cuh"
@@ -38,13 +46,18 @@ namespace qk {
 constexpr int kDecodeWarps = 16;
 constexpr int kProducerWarp = 16;
 constexpr int kMmaWarp0 = 17;
-constexpr int kMmaIssuers = 4;  // one per 64-value K atom of a block
+constexpr int kMmaIssuers = 4;  // each takes 16 / kMmaIssuers of a block's 16 K steps
+constexpr int kABuffers = 3;
+constexpr int kDBuffers = 1;
+static_assert(kABuffers * 128 + kDBuffers * kMmaIssuers * 32 <= 512, "TMEM columns");
 constexpr int kEpilogueWarp0 = kMmaWarp0 + kMmaIssuers;
 constexpr int kUmmaThreads = (kEpilogueWarp0 + 4) * 32;
-constexpr int kMaxTok = 32;                   // tokens per chunk (MMA N <= 32)
-constexpr int kXtStageBytes = kMaxTok * 512;  // activation tile of one K block
+constexpr int kMaxTok = 32;           // tokens per chunk (MMA N <= 32)
+constexpr int kXGranule = 16 * 512;   // activation tile of 16 tokens x one K block
+constexpr int kXGranules = 8;         // activation ring: 64 KB
+constexpr int kXSlots = 8;            // stages that can hold activation granules at once
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kAccCol = 256;
+constexpr uint32_t kAccCol = kABuffers * 128;
 
 enum { kModeGateUp = 0, kModeDown = 1, kModeDense = 2 };
 
@@ -54,10 +67,15 @@ struct UCfg {
   // The second tile starts 64 bytes past a 128-byte boundary, so the two 16-row halves a
   // warp reads (even lanes tile 0, odd lanes tile 1) fall on different banks.
   static constexpr int kTile1 = (kTile + 127) / 128 * 128 + 64;
-  static constexpr int kWBytes = (kTile1 + kTile + 1023) / 1024 * 1024;
-  static constexpr int kStageBytes = kWBytes + kXtStageBytes;
-  static constexpr int kStages = (225 * 1024) / kStageBytes;  // 5 (Q6_K), 6 (Q4_K)
-  static constexpr size_t kSmem = 1024 + static_cast<size_t>(kStages) * kStageBytes + 512;
+  static constexpr int kWStageBytes = (kTile1 + kTile + 127) / 128 * 128;
+  // Activation ring (1024-aligned granules at the start) and weight ring. The weight ring
+  // gets the rest: at ~2.7 us loaded HBM latency an SM needs ~130 KB of weights in flight
+  // to take its share of the HBM bandwidth, besides the two stages being decoded.
+  static constexpr int kXBytes = kXGranules * kXGranule;
+  static constexpr int kWStages = (225 * 1024 - kXBytes) / kWStageBytes;  // 6 (Q6_K), 8 (Q4_K)
+  static constexpr size_t kWOff = kXBytes;
+  static constexpr size_t kBarOff = kWOff + static_cast<size_t>(kWStages) * kWStageBytes;
+  static constexpr size_t kSmem = 1024 + kBarOff + 512;
 };
 
 struct UArgs {
@@ -73,6 +91,7 @@ struct UArgs {
   int n_chunks_dense;
   int m_dense;
   const int32_t* chunk_off;  // [n_active + 1]
+  const int4* chunk_rec;     // [n_chunks] {expert, tokens, first entry, first tile row}
   const int32_t* row_off;    // [n_active + 1]
   const int32_t* active;
   const int32_t* counts;
@@ -105,25 +124,27 @@ __device__ __forceinline__ ChunkInfo chunk_info(const UArgs& A, int ci) {
     c.xrow = kMaxTok * ci;
     c.ntok = min(kMaxTok, A.m_dense - kMaxTok * ci);
   } else {
-    int lo = 0, hi = *A.n_active_p;  // largest a with chunk_off[a] <= ci
-    while (hi - lo > 1) {
-      const int mid = (lo + hi) >> 1;
-      if (A.chunk_off[mid] <= ci) lo = mid;
-      else hi = mid;
-    }
-    const int ch = ci - A.chunk_off[lo];
-    c.e = A.active[lo];
-    c.ntok = min(kMaxTok, A.counts[c.e] - kMaxTok * ch);
-    c.entry0 = A.offsets[c.e] + kMaxTok * ch;
-    c.xrow = A.row_off[lo] + kMaxTok * ch;
+    const int4 rec = A.chunk_rec[ci];
+    c.e = rec.x;
+    c.ntok = rec.y;
+    c.entry0 = rec.z;
+    c.xrow = rec.w;
   }
   c.r16 = (c.ntok + 15) & ~15;
   return c;
 }
 
-// Work item -> (token chunk, MMA tile p, K-block range).
+// Work item -> (token chunk, MMA tile p, K-block range). The items of one chunk run on
+// neighbouring CTAs at the same time; each walks its K blocks starting at a different one
+// (block kb0 + (i + p) % n at step i), so they do not all fetch the same activation tile
+// from the same L2 lines at once. The FP32 accumulation order over K blocks is the only
+// thing that changes.
 struct ItemInfo {
   int ci, p, kb0, kb1;
+  __device__ __forceinline__ int kblock(int i) const {
+    const int n = kb1 - kb0;
+    return kb0 + (i + p) % n;
+  }
 };
 
 __device__ __forceinline__ ItemInfo item_info(const UArgs& A, int item) {
@@ -163,17 +184,22 @@ template <QType QT, int MODE>
 __global__ void __launch_bounds__(kUmmaThreads, 1) umma_proj_kernel(const UArgs A) {
   using Cfg = UCfg<QT>;
   using HT = HalfTile<QT>;
-  constexpr int S = Cfg::kStages;
+  constexpr int SW = Cfg::kWStages;
   constexpr int TB = Cfg::kTile;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + static_cast<size_t>(S) * Cfg::kStageBytes);
-  uint64_t* empty = full + S;
-  uint64_t* afull = empty + S;
-  uint64_t* aempty = afull + 2;
-  uint64_t* dfull = aempty + 2;
-  uint64_t* dempty = dfull + 2;
-  uint32_t* tmem_sh = reinterpret_cast<uint32_t*>(dempty + 2);
+  uint8_t* xring = smem;
+  uint8_t* wring = smem + Cfg::kWOff;
+  uint64_t* wfull = reinterpret_cast<uint64_t*>(smem + Cfg::kBarOff);
+  uint64_t* wempty = wfull + SW;
+  uint64_t* xfull = wempty + SW;
+  uint64_t* xempty = xfull + kXSlots;
+  uint64_t* afull = xempty + kXSlots;
+  uint64_t* aempty = afull + kABuffers;
+  uint64_t* dfull = aempty + kABuffers;
+  uint64_t* dempty = dfull + kDBuffers;
+  volatile uint32_t* xoff = reinterpret_cast<volatile uint32_t*>(dempty + kDBuffers);  // [kXSlots] granule of each stage
+  uint32_t* tmem_sh = const_cast<uint32_t*>(xoff + kXSlots);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_chunks = MODE == kModeDense ? A.n_chunks_dense : *A.n_chunks_p;
@@ -181,13 +207,19 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) umma_proj_kernel(const UArgs 
   if (static_cast<int>(blockIdx.x) >= n_items) return;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < S; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kDecodeWarps / 2 + kMmaIssuers);  // the stage's decode group + the MMA commits
+    for (int s = 0; s < SW; ++s) {
+      mbar_init(&wfull[s], 1);
+      mbar_init(&wempty[s], kDecodeWarps / 2);  // the stage's decode group
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int s = 0; s < kXSlots; ++s) {
+      mbar_init(&xfull[s], 1);
+      mbar_init(&xempty[s], kMmaIssuers);  // the MMA commits
+    }
+    for (int i = 0; i < kABuffers; ++i) {
       mbar_init(&afull[i], kDecodeWarps / 2);
       mbar_init(&aempty[i], kMmaIssuers);
+    }
+    for (int i = 0; i < kDBuffers; ++i) {
       mbar_init(&dfull[i], kMmaIssuers);
       mbar_init(&dempty[i], 4);
     }
@@ -202,61 +234,84 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) umma_proj_kernel(const UArgs 
 
   if (warp == kProducerWarp) {
     if (lane == 0) {
+      const uint64_t wpol = l2_evict_first_policy(), xpol = l2_evict_last_policy();
       uint32_t sc = 0;
+      uint32_t xlo = 0, xused = 0, xhead = 0, xcnt = 0;  // granule ring: oldest live stage, granules
+                                                          // held, next free granule, 2-bit counts
       for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
         const ItemInfo it = item_info(A, item);
         const ChunkInfo c = chunk_info<MODE>(A, it.ci);
         const uint8_t *w0, *w1;
         int rt0, rt1;
         const int nt = item_tiles<MODE>(A, c.e, it.p, w0, w1, rt0, rt1);
-        const uint32_t xbytes = static_cast<uint32_t>(c.r16) * 512u;
+        const uint32_t g = static_cast<uint32_t>(c.r16) / 16;  // granules per activation tile
+        const uint32_t xbytes = g * kXGranule;
         const uint8_t* xsrc = A.xt + c.xrow * 512 * A.nkb;
-        for (int kb = it.kb0; kb < it.kb1; ++kb, ++sc) {
-          const int s = sc % S;
-          if (sc >= S && !mbar_wait_bounded(&empty[s], ((sc / S) - 1) & 1)) {
+        for (int i = 0; i < it.kb1 - it.kb0 && ok; ++i, ++sc) {
+          const int kb = it.kblock(i);
+          // activation granules: contiguous, skipping a tail granule too short for the tile
+          const uint32_t off = xhead + g > kXGranules ? 0u : xhead;
+          const uint32_t need = g + (off == 0u && xhead != 0u ? kXGranules - xhead : 0u);
+          while (xused + need > kXGranules || sc - xlo >= kXSlots) {
+            if (!mbar_wait_bounded(&xempty[xlo % kXSlots], (xlo / kXSlots) & 1)) {
+              ok = false;
+              break;
+            }
+            xused -= (xcnt >> (2 * (xlo % kXSlots))) & 3u;
+            ++xlo;
+          }
+          const int s = sc % SW;
+          if (!ok || (sc >= SW && !mbar_wait_bounded(&wempty[s], ((sc / SW) - 1) & 1))) {
             ok = false;
             break;
           }
-          uint8_t* st = smem + static_cast<size_t>(s) * Cfg::kStageBytes;
-          mbar_expect_tx(&full[s], static_cast<uint32_t>(TB * nt) + xbytes);
-          bulk_g2s(st, w0 + (static_cast<int64_t>(rt0) * A.nkb + kb) * TB, TB, &full[s]);
-          if (nt == 2) bulk_g2s(st + Cfg::kTile1, w1 + (static_cast<int64_t>(rt1) * A.nkb + kb) * TB, TB, &full[s]);
-          bulk_g2s(st + Cfg::kWBytes, xsrc + static_cast<int64_t>(kb) * xbytes, xbytes, &full[s]);
+          const uint32_t j = sc % kXSlots;
+          xcnt = (xcnt & ~(3u << (2 * j))) | (need << (2 * j));
+          xused += need;
+          xhead = (off + g) % kXGranules;
+          xoff[j] = off;
+          mbar_expect_tx(&xfull[j], xbytes);
+          bulk_g2s_hint(xring + off * kXGranule, xsrc + static_cast<int64_t>(kb) * xbytes, xbytes, &xfull[j], xpol);
+          uint8_t* st = wring + static_cast<size_t>(s) * Cfg::kWStageBytes;
+          mbar_expect_tx(&wfull[s], static_cast<uint32_t>(TB * nt));
+          bulk_g2s_hint(st, w0 + (static_cast<int64_t>(rt0) * A.nkb + kb) * TB, TB, &wfull[s], wpol);
+          if (nt == 2)
+            bulk_g2s_hint(st + Cfg::kTile1, w1 + (static_cast<int64_t>(rt1) * A.nkb + kb) * TB, TB, &wfull[s], wpol);
         }
       }
     }
   } else if (warp >= kMmaWarp0 && warp < kEpilogueWarp0) {
     if (lane == 0) {
-      const uint32_t atom_i = static_cast<uint32_t>(warp - kMmaWarp0);
+      const uint32_t mi = static_cast<uint32_t>(warp - kMmaWarp0);
       uint32_t sc = 0, ic = 0;
       for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
         const ItemInfo it = item_info(A, item);
         const ChunkInfo c = chunk_info<MODE>(A, it.ci);
         const uint32_t idesc = idesc_bf16_m128(static_cast<uint32_t>(c.r16));
         const uint32_t atom = static_cast<uint32_t>(c.r16 >> 3) * 1024u;  // bytes per 64-value K atom
-        const uint32_t d = ic & 1;
-        const uint32_t dcol = tbase + kAccCol + (d * kMmaIssuers + atom_i) * kMaxTok;
-        if (ic >= 2 && !mbar_wait_bounded(&dempty[d], ((ic >> 1) - 1) & 1)) {
+        const uint32_t d = ic % kDBuffers;
+        const uint32_t dcol = tbase + kAccCol + (d * kMmaIssuers + mi) * kMaxTok;
+        if (ic >= kDBuffers && !mbar_wait_bounded(&dempty[d], ((ic / kDBuffers) - 1) & 1)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        for (int kb = it.kb0; kb < it.kb1; ++kb, ++sc) {
-          const int s = sc % S;
-          const uint32_t g = sc & 1;
-          if (!mbar_wait_bounded(&full[s], (sc / S) & 1) || !mbar_wait_bounded(&afull[g], (sc >> 1) & 1)) {
+        for (int i = 0; i < it.kb1 - it.kb0; ++i, ++sc) {
+          const uint32_t j = sc % kXSlots, b = sc % kABuffers;
+          if (!mbar_wait_bounded(&xfull[j], (sc / kXSlots) & 1) || !mbar_wait_bounded(&afull[b], (sc / kABuffers) & 1)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint64_t b0 = sdesc_sw128(
-              smem_addr(smem + static_cast<size_t>(s) * Cfg::kStageBytes + Cfg::kWBytes + atom_i * atom), 1024u);
-          const uint32_t acol = tbase + g * 128 + atom_i * 32;
+          constexpr int kSteps = 16 / kMmaIssuers;  // K steps of 16 values per issuer
+          const uint32_t xs = smem_addr(xring + xoff[j] * kXGranule);
+          const uint64_t bd = sdesc_sw128(xs + (mi * kSteps / 4) * atom, 1024u);
+          const uint32_t acol = tbase + b * 128 + mi * kSteps * 8;
 #pragma unroll
-          for (int ks = 0; ks < 4; ++ks)
-            umma_ts(dcol, acol + ks * 8, b0 + ks * 2, idesc, (kb != it.kb0) || (ks != 0));
-          umma_commit(&aempty[g]);
-          umma_commit(&empty[s]);
+          for (int ks = 0; ks < kSteps; ++ks)
+            umma_ts(dcol, acol + ks * 8, bd + (((ks >> 2) * atom) >> 4) + (ks & 3) * 2, idesc, (i != 0) || (ks != 0));
+          umma_commit(&aempty[b]);
+          umma_commit(&xempty[j]);
         }
         if (!ok) break;
         umma_commit(&dfull[d]);
@@ -270,23 +325,16 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) umma_proj_kernel(const UArgs 
     for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++ic) {
       const ItemInfo it = item_info(A, item);
       const ChunkInfo c = chunk_info<MODE>(A, it.ci);
-      const uint32_t d = ic & 1;
-      if (!mbar_wait_bounded(&dfull[d], (ic >> 1) & 1)) {
+      const uint32_t d = ic % kDBuffers;
+      if (!mbar_wait_bounded(&dfull[d], (ic / kDBuffers) & 1)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      // Eight token columns at a time: acc = ((D0 + D1) + D2) + D3 over the four issuers'
-      // accumulators, then the mode's output for those columns.
+      // acc = ((D0 + D1) + D2) + D3 over the issuers' accumulators, eight columns at a time;
+      // the accumulators are released before the outputs are computed.
       const uint32_t dcol = tbase + (static_cast<uint32_t>(32 * q) << 16) + kAccCol + d * kMmaIssuers * kMaxTok;
-      const int t = L & 1, r = L >> 1;
-      const int R = MODE == kModeGateUp ? 64 * it.p + r : 128 * it.p + 64 * t + r;
-      uint8_t* hbase = MODE == kModeGateUp
-                           ? A.ht + c.xrow * 512 * A.nkb_out + static_cast<int64_t>(R >> 8) * c.r16 * 512
-                           : nullptr;
-      float* obase = MODE == kModeDense
-                         ? (A.ksplit ? A.out + static_cast<int64_t>(it.kb0) * A.m_dense * A.nrows : A.out)
-                         : nullptr;
+      float acc[kMaxTok];
 #pragma unroll
       for (int cg = 0; cg < kMaxTok / 8; ++cg) {
         if (8 * cg >= c.r16) break;
@@ -294,42 +342,50 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) umma_proj_kernel(const UArgs 
 #pragma unroll
         for (int i = 0; i < kMmaIssuers; ++i) tmem_ld8(dcol + i * kMaxTok + 8 * cg, v[i]);
         tmem_wait_ld();
-        float acc[8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          acc[j] = __uint_as_float(v[0][j]);
+        for (int jj = 0; jj < 8; ++jj) {
+          float a = __uint_as_float(v[0][jj]);
 #pragma unroll
-          for (int i = 1; i < kMmaIssuers; ++i) acc[j] = __fadd_rn(acc[j], __uint_as_float(v[i][j]));
-        }
-        if (MODE == kModeGateUp) {
-          // lane pair (gate row r, up row r): the even lane takes the first half of the
-          // token columns, the odd lane the second; each gets its partner's value by shuffle.
-          const int half = c.r16 >> 1;
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const int col = 8 * cg + j;
-            const float other = __shfl_xor_sync(0xffffffffu, acc[j], 1);
-            if ((col < half) == (t == 0)) {
-              const float gb = bf16_round(t == 0 ? acc[j] : other);
-              const float ub = bf16_round(t == 0 ? other : acc[j]);
-              const float act = bf16_round(__fmul_rn(gb, sigmoid_ref(gb)));  // silu, math.py:19-20
-              *reinterpret_cast<uint16_t*>(hbase + xt_offset(c.r16, col, R & 255)) = bf16_bits_rne(__fmul_rn(act, ub));
-            }
-          }
-        } else if (R < A.nrows) {
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const int col = 8 * cg + j;
-            if (col >= c.ntok) break;
-            const int64_t orow = c.entry0 + col;
-            if (MODE == kModeDown) A.y[orow * A.nrows + R] = bf16_bits_rne(acc[j]);
-            else obase[orow * A.nrows + R] = acc[j];
-          }
+          for (int i = 1; i < kMmaIssuers; ++i) a = __fadd_rn(a, __uint_as_float(v[i][jj]));
+          acc[8 * cg + jj] = a;
         }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&dempty[d]);
+      const int t = L & 1, r = L >> 1;
+      if (MODE == kModeGateUp) {
+        // lane pair (gate row r, up row r): the even lane takes the first half of the token
+        // columns, the odd lane the second; each gets its partner's value by shuffle.
+        const int R = 64 * it.p + r;  // row of I = K index of the down pass
+        uint8_t* hbase = A.ht + c.xrow * 512 * A.nkb_out + static_cast<int64_t>(R >> 8) * c.r16 * 512;
+        const int half = c.r16 >> 1;
+#pragma unroll
+        for (int col = 0; col < kMaxTok; ++col) {
+          if (col >= c.r16) break;
+          const float other = __shfl_xor_sync(0xffffffffu, acc[col], 1);
+          if ((col < half) == (t == 0)) {
+            const float gb = bf16_round(t == 0 ? acc[col] : other);
+            const float ub = bf16_round(t == 0 ? other : acc[col]);
+            const float act = bf16_round(__fmul_rn(gb, sigmoid_ref(gb)));  // silu, math.py:19-20
+            *reinterpret_cast<uint16_t*>(hbase + xt_offset(c.r16, col, R & 255)) = bf16_bits_rne(__fmul_rn(act, ub));
+          }
+        }
+      } else {
+        const int R = 128 * it.p + 64 * t + r;
+        if (R < A.nrows) {
+          float* obase = MODE == kModeDense
+                             ? (A.ksplit ? A.out + static_cast<int64_t>(it.kb0) * A.m_dense * A.nrows : A.out)
+                             : nullptr;
+#pragma unroll
+          for (int col = 0; col < kMaxTok; ++col) {
+            if (col >= c.ntok) break;
+            const int64_t orow = c.entry0 + col;
+            if (MODE == kModeDown) A.y[orow * A.nrows + R] = bf16_bits_rne(acc[col]);
+            else obase[orow * A.nrows + R] = acc[col];
+          }
+        }
+      }
     }
   } else {
     // ---------------- decode warps ----------------
@@ -337,17 +393,15 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) umma_proj_kernel(const UArgs 
     const int t = L & 1, r = L >> 1;
     auto run = [&](auto hc) {
       constexpr int h = decltype(hc)::value;
-      uint32_t sc = 0, j = 0;
+      uint32_t sc = 0;
       for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
+        // The decode needs no chunk metadata: only whether its tile exists.
         const ItemInfo it = item_info(A, item);
-        const ChunkInfo c = chunk_info<MODE>(A, it.ci);
-        const uint8_t *w0, *w1;
-        int rt0, rt1;
-        const bool mine = t < item_tiles<MODE>(A, c.e, it.p, w0, w1, rt0, rt1);
-        for (int kb = it.kb0; kb < it.kb1; ++kb, ++sc) {
+        const bool mine = MODE == kModeGateUp || t == 0 || 2 * it.p + 1 < A.tiles64;
+        for (int i = 0; i < it.kb1 - it.kb0; ++i, ++sc) {
           if ((sc & 1) != static_cast<uint32_t>(g)) continue;
-          const int s = sc % S;
-          if (!mbar_wait_bounded(&full[s], (sc / S) & 1)) {
+          const int s = sc % SW;
+          if (!mbar_wait_bounded(&wfull[s], (sc / SW) & 1)) {
             ok = false;
             break;
           }
@@ -355,22 +409,22 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) umma_proj_kernel(const UArgs 
           // tile) decode zeros: tcgen05.st / wait::st are warp-collective, so every lane
           // of the warp must run them.
           typename HT::Regs regs;
-          if (mine) HT::template load<h>(regs, smem + static_cast<size_t>(s) * Cfg::kStageBytes + t * Cfg::kTile1, r);
+          if (mine) HT::template load<h>(regs, wring + static_cast<size_t>(s) * Cfg::kWStageBytes + t * Cfg::kTile1, r);
           else HT::clear(regs);
           __syncwarp();
-          if (lane == 0) mbar_arrive(&empty[s]);
-          if (j >= 1 && !mbar_wait_bounded(&aempty[g], (j - 1) & 1)) {
+          if (lane == 0) mbar_arrive(&wempty[s]);
+          const uint32_t b = sc % kABuffers;
+          if (sc >= kABuffers && !mbar_wait_bounded(&aempty[b], ((sc / kABuffers) - 1) & 1)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t col0 = tbase + (static_cast<uint32_t>(32 * q) << 16) + g * 128 + h * 64;
+          const uint32_t col0 = tbase + (static_cast<uint32_t>(32 * q) << 16) + b * 128 + h * 64;
           HT::template decode<false, h>(regs, [&](int col, const uint32_t(&o)[8]) { tmem_st8(col0 + col, o); });
           tmem_wait_st();
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&afull[g]);
-          ++j;
+          if (lane == 0) mbar_arrive(&afull[b]);
         }
       }
     };
