@@ -14,6 +14,10 @@ e2e:   the same bytes / time of the user-facing call with host (pinned) buffers:
 The weights (331 MB of Q6_K at 128 experts) exceed the 126 MB L2, so no flush is
 needed between steps.
 
+The line also carries the Q8 KV decode-attention sweep of configs[2] (B in {1, 8, 32},
+context 4096 and 32768, 16 q / 2 kv heads, head dim 256, page-table indices) as GB/s of
+codes + scales per call, unless --no-attention.
+
     python bench.py [--gpus N] [--steps K] [--warmup W] [--m 16] [--qtype Q6_K]
     python bench.py --impl reference ...   # the reference's CPU path (NumPy port)
 """
@@ -424,6 +428,14 @@ def b200_arm(args):
     }
     if sweep:
         line["sweep"] = sweep
+    if rank == 0 and not args.no_attention:
+        peak_gbs, _ = hbm_peak()
+        attn = attention_sweep(device)
+        for r in attn:
+            r["frac"] = r["gbs"] / peak_gbs
+        line["attention"] = {"kernel": "attn_split_kernel + attn_merge_kernel (Q8 KV, 16q/2kv, hd 256)",
+                             "bytes_per_slot": ATTN_SLOT_BYTES, "l2": "flushed before every call",
+                             "configs": attn}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         gbs, experts = cpu_port_gbs(raw, args.qtype, res["x"], res["ids"], res["weights"],
                                     budget_s=args.ref_budget)
@@ -436,6 +448,68 @@ def b200_arm(args):
         dist.barrier()
         dist.destroy_process_group()
     return 0
+
+
+ATTN_CONFIGS = ((1, 4096), (8, 4096), (32, 4096), (1, 32768), (8, 32768), (32, 32768))
+ATTN_SLOT_BYTES = 2 * 512 + 2 * 16 * 2  # K + V codes (2 kv heads x 256) + BF16 scales (16 groups)
+
+
+def attention_sweep(device, reps=20):
+    """Q8 KV decode attention: 16 q / 2 kv heads, head dim 256,
+    one query token per sequence, every slot of the context attended through a page table
+    that is a random permutation (seed 0) of 256-token pages. K/V codes and BF16 scales
+    are synthetic (uniform codes, scales in [0.001, 0.021)); the kernel's cost does not
+    depend on their values. Bytes per step = B * ctx * 1088 (codes + scales); each timed
+    call follows an L2 flush."""
+    import numpy as np
+    import torch
+
+    from qk_b200 import _lib
+
+    lib = _lib.load()
+    stream = torch.cuda.current_stream(device)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+    results = []
+    for batch, ctx in ATTN_CONFIGS:
+        g = torch.Generator(device=device).manual_seed(batch * 7 + ctx)
+        k = torch.randint(-127, 128, (batch, ctx, 512), dtype=torch.int8, device=device, generator=g)
+        v = torch.randint(-127, 128, (batch, ctx, 512), dtype=torch.int8, device=device, generator=g)
+        ks = (torch.rand((batch * 16, ctx), device=device, generator=g) * 0.02 + 0.001).to(torch.bfloat16)
+        vs = (torch.rand((batch * 16, ctx), device=device, generator=g) * 0.02 + 0.001).to(torch.bfloat16)
+        rng = np.random.default_rng(0)
+        pages = ctx // 256
+        table = np.stack([rng.permutation(pages) for _ in range(batch)])
+        slots = np.arange(ctx)
+        idx = torch.from_numpy((table[:, slots // 256] * 256 + slots % 256).astype(np.int32)).to(device)
+        lengths = torch.full((batch,), ctx - 1, dtype=torch.int32, device=device)
+        q = torch.randn((batch, 16, 256), device=device, generator=g).to(torch.bfloat16)
+        out = torch.empty((batch, 16, 256), dtype=torch.bfloat16, device=device)
+        need = int(lib.qk_kv_q8_attention_workspace_bytes(batch, ctx, 16, 2, 256))
+        ws = torch.empty(max(need, 1), dtype=torch.uint8, device=device)
+
+        def call():
+            _lib.check(lib.qk_kv_q8_decode_attention(
+                _lib.ptr(q), _lib.ptr(k), _lib.ptr(v), _lib.ptr(ks), _lib.ptr(vs), _lib.ptr(idx), None,
+                _lib.ptr(lengths), None, batch, ctx, ctx, 16, 2, 256, _lib.ptr(out),
+                _lib.ptr(ws) if need else None, need, _lib.stream_handle(device)))
+
+        for _ in range(3):
+            call()
+        times = []
+        for _ in range(reps):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            call()
+            e1.record(stream)
+            torch.cuda.synchronize(device)
+            times.append(e0.elapsed_time(e1))
+        ms = statistics.median(times)
+        nbytes = batch * ctx * ATTN_SLOT_BYTES
+        results.append({"batch": batch, "ctx": ctx, "us": ms * 1e3, "gbs": nbytes / (ms * 1e-3) / 1e9,
+                        "tokens_per_s": batch / (ms * 1e-3)})
+        del k, v, ks, vs
+    return results
 
 
 def e2e_measure(fn, tensors, device, args, res, rank):
@@ -495,6 +569,7 @@ def main():
     parser.add_argument("--soak", type=float, default=1.0, help="untimed seconds before timing")
     parser.add_argument("--sweep", action="store_true", help="also time M in {1,4,16,64,256}")
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--no-attention", action="store_true", help="skip the Q8 KV attention sweep")
     parser.add_argument("--ref-budget", type=float, default=10.0,
                         help="seconds of CPU work per reference sample")
     args = parser.parse_args()

@@ -32,6 +32,30 @@ void count_launch(int n = 1);
 
 inline cudaStream_t as_stream(qk_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
 
+// Programmatic dependent launch: a kernel started with launch_dependent may begin (and run
+// its prologue) while the previous kernel of the stream is still running; it must call
+// pdl_wait() before touching anything that kernel (or an earlier one) writes or reads.
+// pdl_trigger() lets the next dependent kernel be launched early. Both are no-ops when the
+// kernel was launched normally.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_dependent(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                             Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 int sm_count();  // SMs of the current device (cached per device)
 // Opt a kernel into `bytes` of dynamic shared memory on the current device (once).
 int allow_smem(const void* kernel, size_t bytes);

@@ -20,6 +20,7 @@ __host__ __device__ inline int64_t dense_tile_rows(int64_t M) {
 // x [M, K] (any K, any alignment) -> activation tiles [chunk][kb][r16 x 512 B].
 __global__ void __launch_bounds__(256) pack_x_kernel(const uint16_t* __restrict__ x, int M, int K,
                                                      int nkb, uint8_t* __restrict__ xt) {
+  pdl_trigger();
   const int64_t rows = dense_tile_rows(M);
   const int cpr = nkb * 32;  // 16-byte chunks of one padded row
   const int64_t total = rows * cpr;
@@ -50,6 +51,7 @@ __global__ void __launch_bounds__(256) pack_x_kernel(const uint16_t* __restrict_
 
 // out[m, n] = sum over K blocks, in K order, of the block partials [nkb, M, N].
 __global__ void reduce_blocks_kernel(const float* __restrict__ part, int64_t mn, int nkb, float* __restrict__ out) {
+  pdl_wait();
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < mn;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     float acc = part[i];
@@ -117,8 +119,10 @@ int qk_quant_gemm(const uint16_t* x, int64_t M, int64_t K, const uint8_t* w_tile
   const int64_t mn = M * N;
   int64_t rgrid = (mn + 255) / 256;
   if (rgrid > sms * 8) rgrid = sms * 8;
-  reduce_blocks_kernel<<<static_cast<unsigned>(rgrid), 256, 0, st>>>(a.out, mn, nkb, out);
-  QK_LAUNCHED("reduce_blocks_kernel");
+  const cudaError_t e = launch_dependent(reduce_blocks_kernel, dim3(static_cast<unsigned>(rgrid)), dim3(256), 0, st,
+                                         static_cast<const float*>(a.out), mn, nkb, out);
+  if (e != cudaSuccess) return cuda_error(e, "reduce_blocks_kernel");
+  count_launch(1);
   return QK_OK;
 }
 

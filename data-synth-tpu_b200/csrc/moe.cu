@@ -113,6 +113,7 @@ __global__ void __launch_bounds__(1024) moe_route_kernel(const int32_t* __restri
                                                          int B, int k, int E, int first,
                                                          Workspace ws) {
   extern __shared__ int32_t sh[];
+  pdl_trigger();  // the dispatch may launch now (it waits for this kernel before reading)
   int32_t* counts = sh;            // [E]
   int32_t* cursor = sh + E;        // [E]
   int32_t* offsets = sh + 2 * E;   // [E + 1]
@@ -255,27 +256,35 @@ __global__ void __launch_bounds__(1024) moe_route_kernel(const int32_t* __restri
 // ------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) moe_dispatch_kernel(const uint16_t* __restrict__ x, int H,
                                                            Workspace ws) {
-  // One warp per activation-tile row: the owning expert chunk is looked up once per row,
-  // then the lanes copy the row's 16-byte chunks (H / 8 of them) into the swizzled tile.
-  const int n_rows = ws.meta->row_total, n_act = ws.meta->n_active;
+  // One warp per (token chunk, tile row): the chunk's record gives the row's place; the
+  // lanes load the row's 16-byte pieces (H / 8 of them) eight at a time before storing them
+  // into the swizzled tile. Rows past the chunk's tokens (up to the 16-row padding) are zero.
+  constexpr int kU = 8;
+  pdl_trigger();
+  pdl_wait();
+  const int n_rows = ws.meta->n_chunks * kMaxTok;
   const int lane = threadIdx.x & 31, cpr = H / 8, nkb = H / 256;
   const int warps = gridDim.x * (blockDim.x >> 5);
   for (int g = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); g < n_rows; g += warps) {
-    int lo = 0, hi = n_act;  // largest a with row_off[a] <= g
-    while (hi - lo > 1) {
-      const int mid = (lo + hi) >> 1;
-      if (ws.row_off[mid] <= g) lo = mid;
-      else hi = mid;
-    }
-    const int r_in = g - ws.row_off[lo], ch = r_in / kMaxTok, rr = r_in % kMaxTok;
-    const int e = ws.active[lo];
-    const int ntok = min(kMaxTok, ws.counts[e] - kMaxTok * ch), r16 = (ntok + 15) & ~15;
-    const uint16_t* src = rr < ntok ? x + static_cast<int64_t>(ws.entry_token[ws.offsets[e] + r_in]) * H : nullptr;
-    uint8_t* base = ws.xt + static_cast<int64_t>(ws.row_off[lo] + kMaxTok * ch) * 512 * nkb;
-    for (int j = lane; j < cpr; j += 32) {
-      const uint4 v = src ? ld_nc_v4(src + j * 8) : make_uint4(0, 0, 0, 0);
-      const int k = j * 8;
-      *reinterpret_cast<uint4*>(base + static_cast<int64_t>(k >> 8) * r16 * 512 + xt_offset(r16, rr, k & 255)) = v;
+    const int ci = g / kMaxTok, rr = g % kMaxTok;
+    const int4 rec = ws.chunk_rec[ci];  // {expert, tokens, first entry, first tile row}
+    const int ntok = rec.y, r16 = (ntok + 15) & ~15;
+    if (rr >= r16) continue;
+    const uint16_t* src = rr < ntok ? x + static_cast<int64_t>(ws.entry_token[rec.z + rr]) * H : nullptr;
+    uint8_t* base = ws.xt + static_cast<int64_t>(rec.w) * 512 * nkb;
+    for (int j0 = lane; j0 < cpr; j0 += 32 * kU) {
+      uint4 v[kU];
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int j = j0 + 32 * u;
+        v[u] = src && j < cpr ? ld_nc_v4(src + j * 8) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int j = j0 + 32 * u, k = j * 8;
+        if (j < cpr)
+          *reinterpret_cast<uint4*>(base + static_cast<int64_t>(k >> 8) * r16 * 512 + xt_offset(r16, rr, k & 255)) = v[u];
+      }
     }
   }
 }
@@ -286,10 +295,14 @@ __global__ void __launch_bounds__(256) moe_dispatch_kernel(const uint16_t* __res
 constexpr int kMaxTopK = 32;
 
 // One warp per token: lane j holds route j's entry; ranks by expert id give the reference's
-// ascending-expert accumulation order; each lane then sums 8 columns at a time in FP32.
+// ascending-expert accumulation order. Each lane owns 8 columns of each 256-column block
+// and, per entry, loads all its blocks of a 2048-column group before accumulating them in
+// FP32, so a token's loads are in flight together.
 __global__ void __launch_bounds__(256) moe_combine_kernel(const int32_t* __restrict__ ids, int B,
                                                           int k, int H, int out_bf16, void* out,
                                                           Workspace ws) {
+  constexpr int kBlocks = 8;  // 256-column blocks per group
+  pdl_wait();
   const int lane = threadIdx.x & 31;
   const int b = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (b >= B) return;
@@ -303,32 +316,49 @@ __global__ void __launch_bounds__(256) moe_combine_kernel(const int32_t* __restr
     n += vj;
     rank += vj && (ej < eid);  // entries of a token name distinct experts
   }
-  for (int c0 = lane * 8; c0 < H; c0 += 256) {
-    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  for (int g0 = 0; g0 < H; g0 += kBlocks * 256) {
+    float acc[kBlocks][8];
+#pragma unroll
+    for (int cb = 0; cb < kBlocks; ++cb)
+#pragma unroll
+      for (int t = 0; t < 8; ++t) acc[cb][t] = 0.f;
     for (int i = 0; i < n; ++i) {
       const unsigned who = __ballot_sync(0xffffffffu, entry >= 0 && rank == i);
       const int src = __ffs(who) - 1;
       const int ent = __shfl_sync(0xffffffffu, entry, src);
       const float wi = __shfl_sync(0xffffffffu, w, src);
-      const uint4 v = ld_nc_v4(ws.y + static_cast<int64_t>(ent) * H + c0);
-      const uint32_t p[4] = {v.x, v.y, v.z, v.w};
+      const uint16_t* yrow = ws.y + static_cast<int64_t>(ent) * H + g0 + lane * 8;
+      uint4 v[kBlocks];
 #pragma unroll
-      for (int t = 0; t < 8; ++t) {
-        const float y = bf16_to_f32(static_cast<uint16_t>(p[t >> 1] >> (16 * (t & 1))));
-        acc[t] = __fadd_rn(acc[t], __fmul_rn(y, wi));
+      for (int cb = 0; cb < kBlocks; ++cb)
+        v[cb] = g0 + cb * 256 < H ? ld_nc_v4(yrow + cb * 256) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+      for (int cb = 0; cb < kBlocks; ++cb) {
+        const uint32_t p[4] = {v[cb].x, v[cb].y, v[cb].z, v[cb].w};
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+          const float y = bf16_to_f32(static_cast<uint16_t>(p[t >> 1] >> (16 * (t & 1))));
+          acc[cb][t] = __fadd_rn(acc[cb][t], __fmul_rn(y, wi));
+        }
       }
     }
-    const int64_t o = static_cast<int64_t>(b) * H + c0;
-    if (out_bf16) {
-      uint32_t q[4];
 #pragma unroll
-      for (int t = 0; t < 4; ++t)
-        q[t] = static_cast<uint32_t>(bf16_bits_rne(acc[2 * t])) | (static_cast<uint32_t>(bf16_bits_rne(acc[2 * t + 1])) << 16);
-      *reinterpret_cast<uint4*>(static_cast<uint16_t*>(out) + o) = make_uint4(q[0], q[1], q[2], q[3]);
-    } else {
-      float4* f = reinterpret_cast<float4*>(static_cast<float*>(out) + o);
-      f[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
-      f[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+    for (int cb = 0; cb < kBlocks; ++cb) {
+      const int c0 = g0 + cb * 256 + lane * 8;
+      if (c0 >= H) break;
+      const int64_t o = static_cast<int64_t>(b) * H + c0;
+      if (out_bf16) {
+        uint32_t q[4];
+#pragma unroll
+        for (int t = 0; t < 4; ++t)
+          q[t] = static_cast<uint32_t>(bf16_bits_rne(acc[cb][2 * t])) |
+                 (static_cast<uint32_t>(bf16_bits_rne(acc[cb][2 * t + 1])) << 16);
+        *reinterpret_cast<uint4*>(static_cast<uint16_t*>(out) + o) = make_uint4(q[0], q[1], q[2], q[3]);
+      } else {
+        float4* f = reinterpret_cast<float4*>(static_cast<float*>(out) + o);
+        f[0] = make_float4(acc[cb][0], acc[cb][1], acc[cb][2], acc[cb][3]);
+        f[1] = make_float4(acc[cb][4], acc[cb][5], acc[cb][6], acc[cb][7]);
+      }
     }
   }
 }
@@ -388,11 +418,15 @@ static int moe_forward_impl(const qk_moe_desc* desc, const uint8_t* gate, const 
   QK_LAUNCHED("moe_route_kernel");
 
   const int sms = sm_count();
-  const int64_t rows_max = static_cast<int64_t>(rows_bound(d, B));
+  const int64_t rows_max = static_cast<int64_t>(chunks_bound(d, B)) * kMaxTok;
   int64_t dgrid = (rows_max + 7) / 8;  // 8 rows (warps) per CTA
   if (dgrid > sms * 8) dgrid = sms * 8;
-  moe_dispatch_kernel<<<static_cast<unsigned>(dgrid), 256, 0, st>>>(x, d.hidden, ws);
-  QK_LAUNCHED("moe_dispatch_kernel");
+  {
+    const cudaError_t e = launch_dependent(moe_dispatch_kernel, dim3(static_cast<unsigned>(dgrid)), dim3(256), 0, st,
+                                           x, d.hidden, ws);
+    if (e != cudaSuccess) return cuda_error(e, "moe_dispatch_kernel");
+    count_launch(1);
+  }
 
   const bool q6 = d.gate_type == QK_TYPE_Q6_K;
   UArgs gu{};
@@ -433,8 +467,12 @@ static int moe_forward_impl(const qk_moe_desc* desc, const uint8_t* gate, const 
   rc = q6 ? launch_umma<QType::Q6_K, kModeDown>(dn, sms, st) : launch_umma<QType::Q4_K, kModeDown>(dn, sms, st);
   if (rc) return rc;
   mark(3);
-  moe_combine_kernel<<<(B + 7) / 8, 256, 0, st>>>(ids, B, d.top_k, d.hidden, out_dtype == QK_OUT_BF16, out, ws);
-  QK_LAUNCHED("moe_combine_kernel");
+  {
+    const cudaError_t e = launch_dependent(moe_combine_kernel, dim3((B + 7) / 8), dim3(256), 0, st, ids, B, d.top_k,
+                                           d.hidden, static_cast<int>(out_dtype == QK_OUT_BF16), out, ws);
+    if (e != cudaSuccess) return cuda_error(e, "moe_combine_kernel");
+    count_launch(1);
+  }
   mark(4);
   return QK_OK;
 }

@@ -202,9 +202,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) umma_proj_kernel(const UArgs 
   uint32_t* tmem_sh = const_cast<uint32_t*>(xoff + kXSlots);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n_chunks = MODE == kModeDense ? A.n_chunks_dense : *A.n_chunks_p;
-  const int n_items = n_chunks * A.items_per_chunk * (A.ksplit ? A.nkb : 1);
-  if (static_cast<int>(blockIdx.x) >= n_items) return;
+  pdl_trigger();  // the next pass may be launched now; its CTAs start as these ones leave
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < SW; ++s) {
@@ -230,9 +228,15 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) umma_proj_kernel(const UArgs 
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = *tmem_sh;
+  pdl_wait();  // everything above is this CTA's own set-up; from here on, earlier kernels' data
+  const int n_chunks = MODE == kModeDense ? A.n_chunks_dense : *A.n_chunks_p;
+  const int n_items = n_chunks * A.items_per_chunk * (A.ksplit ? A.nkb : 1);
   bool ok = true;
+  const bool idle = static_cast<int>(blockIdx.x) >= n_items;  // no item for this CTA
 
-  if (warp == kProducerWarp) {
+  if (idle) {
+    // nothing to do: fall through to the teardown
+  } else if (warp == kProducerWarp) {
     if (lane == 0) {
       const uint64_t wpol = l2_evict_first_policy(), xpol = l2_evict_last_policy();
       uint32_t sc = 0;
@@ -446,8 +450,9 @@ int launch_umma(const UArgs& A, int grid, cudaStream_t st) {
   using Cfg = UCfg<QT>;
   int rc = allow_smem(reinterpret_cast<const void*>(umma_proj_kernel<QT, MODE>), Cfg::kSmem);
   if (rc) return rc;
-  umma_proj_kernel<QT, MODE><<<grid, kUmmaThreads, Cfg::kSmem, st>>>(A);
-  QK_LAUNCHED("umma_proj_kernel");
+  const cudaError_t e = launch_dependent(umma_proj_kernel<QT, MODE>, dim3(grid), dim3(kUmmaThreads), Cfg::kSmem, st, A);
+  if (e != cudaSuccess) return cuda_error(e, "umma_proj_kernel");
+  count_launch(1);
   return QK_OK;
 }
 

@@ -73,8 +73,8 @@ int qk_dequantize_rows(const uint8_t* raw, int qtype, int64_t rows, int64_t row_
 
 /* ---- tiled repack (lossless) -------------------------------------------------
  * Replaces packed_q6/layout.py:49-108 pack_q6 / unpack_q6: a byte-only repack of raw
- * GGUF rows into the B200 tile layout (128 rows x 256 values per tile, rows padded to
- * 128) read by qk_quant_gemm and qk_moe_forward. Q6_K and Q4_K.
+ * GGUF rows into the B200 tile layout (64 rows x 256 values per tile, rows padded to
+ * 64) read by qk_quant_gemm and qk_moe_forward. Q6_K and Q4_K.
  * bad_scales (device int32, may be NULL): receives the count of non-finite FP16 block
  * scales (pack_q6 rejects those, layout.py:67-69); the host wrapper raises on > 0. */
 int64_t qk_tiled_bytes(int qtype, int64_t rows, int64_t row_width);
@@ -148,6 +148,29 @@ int qk_cast_f32_bf16(const float* in, uint16_t* out, int64_t n, qk_stream_t stre
 /* Status word the kernels of the last qk_moe_forward on `workspace` left behind:
  * 0, or QK_ERR_TIMEOUT when a bounded wait gave up. Synchronises `stream`. */
 int qk_moe_check(const void* workspace, qk_stream_t stream);
+
+/* ---- expert parallel with token dispatch ---------------------------------------
+ * The dispatch / combine form of the expert-parallel layer that the reference expresses as
+ * replicated tokens plus psum (qwen38_tpu/experts.py:130-131; placement parallel.py:64-87):
+ * rank r owns experts [r * experts_per_rank, (r + 1) * experts_per_rank) and sends each
+ * route's token row to the owning rank, which returns bf16(h Wd^T) for it.
+ * qk_ep_plan: per token, routes naming the same expert merge into the first one with weight
+ * bf16(sum) and zero-weight routes drop (experts.py:66-76); surviving routes are counting-
+ * sorted by owning rank: send_counts [world], send_rows / send_expert [B * k] (token and
+ * global expert of each send slot, rank-major), route_slot [B * k] (slot of route (b, j)
+ * or -1), route_weight [B * k] (merged FP32 weight, 0 when dropped). */
+int qk_ep_plan(const int32_t* ids, const uint16_t* weights, int B, int k, int experts_per_rank,
+               int world, int32_t* send_counts, int32_t* send_rows, int32_t* send_expert,
+               int32_t* route_slot, float* route_weight, qk_stream_t stream);
+/* dst[i, :] = src[rows[i], :] for BF16 rows of `width` values (16-byte aligned). */
+int qk_gather_rows(const uint16_t* src, const int32_t* rows, int64_t n, int64_t width, uint16_t* dst,
+                   qk_stream_t stream);
+/* out[b] = bf16 (or FP32 with QK_OUT_F32) of the FP32 sum over token b's surviving routes,
+ * in ascending expert order, of f32(y[route_slot[b, j]]) * route_weight[b, j]
+ * (experts.py:129-131). y: BF16 [slots, H], the returned expert outputs in send-slot order. */
+int qk_ep_combine(const uint16_t* y, const int32_t* route_slot, const int32_t* ids,
+                  const float* route_weight, int B, int k, int H, int out_dtype, void* out,
+                  qk_stream_t stream);
 
 /* ---- Q8 KV cache -------------------------------------------------------------
  * Cache layout is the reference's (attention_cache.py:26-43, engine.py:350-369):

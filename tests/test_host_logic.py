@@ -108,3 +108,117 @@ def test_expert_parallel_partials_all_reduce_to_the_layer_gloo(tmp_path):
     mp.start_processes(_ep_rank, args=(2, port, str(result)), nprocs=2, start_method="spawn")
     got, full = np.load(result)
     assert np.max(np.abs(got - full)) <= 1e-2 * np.max(np.abs(full))
+
+
+# ---- expert parallel with token dispatch (all-to-all), orchestration on gloo ----
+
+
+class _NumpyOps:
+    """The four local steps of ExpertAllToAll restated with the oracle (CPU, test only)."""
+
+    def __init__(self, qtype, hidden, intermediate):
+        self.qtype, self.hidden, self.intermediate = qtype, hidden, intermediate
+
+    def plan(self, ids, weights, experts_per_rank, world):
+        import torch
+
+        from qk_b200.ep import Plan
+
+        ids_n = ids.numpy()
+        w_n = weights.float().numpy()
+        B, k = ids_n.shape
+        n_exp = experts_per_rank * world
+        route_weight = np.zeros((B, k), np.float32)
+        for b in range(B):
+            for j in range(k):
+                e = ids_n[b, j]
+                if e < 0 or e >= n_exp or e in ids_n[b, :j]:
+                    continue
+                route_weight[b, j] = bf16_round(np.float32(w_n[b, j:][ids_n[b, j:] == e].sum(dtype=np.float32)))
+        live = [(b, j) for b in range(B) for j in range(k) if route_weight[b, j] != 0]
+        live.sort(key=lambda bj: ids_n[bj] // experts_per_rank)  # stable: token order per rank
+        counts = np.bincount([ids_n[bj] // experts_per_rank for bj in live], minlength=world)
+        slot = np.full((B, k), -1, np.int32)
+        rows = np.zeros(max(B * k, 1), np.int32)
+        expert = np.zeros(max(B * k, 1), np.int32)
+        for s, (b, j) in enumerate(live):
+            slot[b, j], rows[s], expert[s] = s, b, ids_n[b, j]
+        return Plan(torch.from_numpy(counts.astype(np.int64)), torch.from_numpy(rows),
+                    torch.from_numpy(expert), torch.from_numpy(slot), torch.from_numpy(route_weight))
+
+    def gather(self, x, rows):
+        return x[rows.long()]
+
+    def local_ffn(self, gate, up, down, x, experts, first_expert):
+        import torch
+
+        xs = x.float().numpy()
+        out = np.zeros((xs.shape[0], self.hidden), np.float32)
+        for i, e in enumerate(experts.numpy()):
+            le = int(e) - first_expert
+            wg = moe.expert_weights(gate[le], self.qtype, self.intermediate, self.hidden)
+            wu = moe.expert_weights(up[le], self.qtype, self.intermediate, self.hidden)
+            wd = moe.expert_weights(down[le], self.qtype, self.hidden, self.intermediate)
+            out[i] = moe.expert_forward(xs[i:i + 1], wg, wu, wd)[0]
+        return torch.from_numpy(out)
+
+    def combine(self, y, plan, ids, hidden):
+        import torch
+
+        ys = y.float().numpy()
+        slot, w, ids_n = plan.route_slot.numpy(), plan.route_weight.numpy(), ids.numpy()
+        out = np.zeros((ids_n.shape[0], hidden), np.float32)
+        for b in range(ids_n.shape[0]):
+            for j in np.argsort(np.where(slot[b] >= 0, ids_n[b], np.iinfo(np.int32).max), kind="stable"):
+                if slot[b, j] >= 0:
+                    out[b] = (out[b] + (ys[slot[b, j]] * w[b, j]).astype(np.float32)).astype(np.float32)
+        return torch.from_numpy(bf16_round(out))
+
+
+def _a2a_rank(rank, world, port, result_path):
+    import torch
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from qk_b200.ep import ExpertAllToAll
+
+        hidden, inter, per, k = 256, 256, 3, 3
+        count = per * world
+        rng = np.random.default_rng(7)  # same experts on every rank
+        raw = {n: gguf.encode_q6_k(rng.normal(0, 0.05, (count,) + shape)).reshape(count, -1)
+               for n, shape in (("gate", (inter, hidden)), ("up", (inter, hidden)), ("down", (hidden, inter)))}
+        trng = np.random.default_rng(100 + rank)  # this rank's own tokens
+        B = 5 + rank
+        x = bf16_round(trng.normal(size=(B, hidden)).astype(np.float32))
+        ids = trng.integers(0, count, (B, k)).astype(np.int32)
+        ids[0, 1] = ids[0, 0]  # a repeated expert: one route of weight bf16(w0 + w1)
+        weights = bf16_round(trng.uniform(0.1, 1, (B, k)).astype(np.float32))
+        weights[1, 2] = 0.0    # a dropped route
+        mine = slice(rank * per, (rank + 1) * per)
+        fn = ExpertAllToAll(dist.group.WORLD, gate_type="Q6_K", up_type="Q6_K", down_type="Q6_K",
+                            hidden=hidden, intermediate=inter, experts_per_rank=per,
+                            ops=_NumpyOps("Q6_K", hidden, inter))
+        got = fn(raw["gate"][mine], raw["up"][mine], raw["down"][mine], torch.from_numpy(x),
+                 torch.from_numpy(ids), torch.from_numpy(weights)).numpy()
+        expected = moe.expert_ffn(raw["gate"], raw["up"], raw["down"], x, ids, weights, gate_type="Q6_K",
+                                  up_type="Q6_K", down_type="Q6_K", hidden=hidden, intermediate=inter)
+        np.save(f"{result_path}.{rank}.npy", np.stack([got, expected]))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_expert_all_to_all_dispatch_matches_single_device_layer_gloo(tmp_path):
+    import socket
+
+    import torch.multiprocessing as mp
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    result = tmp_path / "a2a"
+    mp.start_processes(_a2a_rank, args=(2, port, str(result)), nprocs=2, start_method="spawn")
+    for rank in range(2):
+        got, expected = np.load(f"{result}.{rank}.npy")
+        np.testing.assert_array_equal(got, expected)
