@@ -260,7 +260,6 @@ __global__ void __launch_bounds__(256) moe_dispatch_kernel(const uint16_t* __res
   // lanes load the row's 16-byte pieces (H / 8 of them) eight at a time before storing them
   // into the swizzled tile. Rows past the chunk's tokens (up to the 16-row padding) are zero.
   constexpr int kU = 8;
-  pdl_trigger();
   pdl_wait();
   const int n_rows = ws.meta->n_chunks * kMaxTok;
   const int lane = threadIdx.x & 31, cpr = H / 8, nkb = H / 256;
@@ -287,6 +286,9 @@ __global__ void __launch_bounds__(256) moe_dispatch_kernel(const uint16_t* __res
       }
     }
   }
+  // Only now may the projection be launched: its CTAs take a whole SM each and would
+  // otherwise crowd out the rest of this grid.
+  pdl_trigger();
 }
 
 // ------------------------------------------------------------------------------------
