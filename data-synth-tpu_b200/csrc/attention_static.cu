@@ -9,9 +9,11 @@
 // partial (max, sum, output) rows. This entry point takes that scratch from
 // `g_attn_scratch` instead.
 //
-// Limit: kStaticScratchBytes (4 MiB). That covers every geometry whose workspace query is
-// at most 4 MiB, for example B <= 32 sequences of 2 KV heads at head_dim 256 on a 148-SM
-// B200 (3.7 MB). Larger requests are refused with QK_ERR_WORKSPACE before anything runs.
+// Limit: kStaticScratchBytes (4 MiB). The split kernel runs one CTA per SM and each CTA
+// leaves at most two partial rows, so the workspace query never exceeds
+// 2 * SMs * (16 + 8 * head_dim) * 4 bytes whatever B and S are: 2.4 MB at head_dim 256 on
+// a 148-SM B200. A device whose query exceeds the array is refused with QK_ERR_WORKSPACE
+// before anything runs.
 //
 // Set-up: the first call on each device (the device current on the calling thread) looks
 // up the array's device address with cudaGetSymbolAddress and caches it. That first call

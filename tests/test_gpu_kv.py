@@ -157,3 +157,76 @@ def test_decode_attention_valid_mask_and_sparse_indices(cuda_device):
     expected = kv.attention(q, keys, values, valid)
     mx, l2 = rel_err(got, expected)
     assert mx < 1e-2 and l2 < 5e-3, (mx, l2)
+
+
+def _random_cache(torch, device, rng, batch, T, kv_heads, hd):
+    """Cache tensors filled directly (random codes, scales in [0.001, 0.021)): long contexts
+    without T single-token appends."""
+    groups = kv_heads * hd // 32
+    codes = {n: rng.integers(-127, 128, (batch, T, kv_heads * hd)).astype(np.int8) for n in ("k", "v")}
+    planes = {n: bf16_round(rng.uniform(0.001, 0.021, (batch * groups, T)).astype(np.float32))
+              for n in ("k", "v")}
+    cache = {n: torch.from_numpy(codes[n]).to(device) for n in ("k", "v")}
+    cache.update({n + "_scale": bf16_tensor(planes[n], device) for n in ("k", "v")})
+    return cache, codes, planes
+
+
+@pytest.mark.parametrize("batch,S,hq,kv_heads,hd,pages", [
+    (1, 8192, 16, 2, 256, True),     # two pairs, each cut across dozens of CTAs
+    (3, 2000, 16, 2, 256, False),    # ragged last tile (2000 = 125 * 16), contiguous slots
+    (5, 777, 16, 2, 256, True),      # ragged tile inside the CTA ranges, 16-slot pages
+    (2, 300, 8, 2, 128, False),      # head_dim 128, 4 query heads per KV head
+    (4, 1500, 32, 4, 128, True),     # head_dim 128, 8 query heads per KV head, 4 KV heads
+])
+def test_decode_attention_stream_split_matches_oracle(cuda_device, batch, S, hq, kv_heads, hd, pages):
+    import torch
+
+    from qk_b200.attention_cache import CacheConfig, decode_attention
+
+    rng = np.random.default_rng(batch * 131 + S)
+    T = S + 48
+    c = CacheConfig(max_context=T, query_heads=hq, kv_heads=kv_heads, head_dim=hd)
+    cache, codes, planes = _random_cache(torch, cuda_device, rng, batch, T, kv_heads, hd)
+    if pages:
+        P = 16
+        table = np.stack([rng.permutation(T // P) for _ in range(batch)])
+        slots = np.arange(S)
+        indices = (table[:, slots // P] * P + slots % P).astype(np.int32)
+    else:
+        indices = np.tile(np.arange(S, dtype=np.int32), (batch, 1))
+    lengths = rng.integers(S // 2, S, batch).astype(np.int32)
+    q = bf16_round(rng.normal(size=(batch, hq, hd)).astype(np.float32))
+    gate = bf16_round(rng.normal(size=(batch, hq, hd)).astype(np.float32))
+    got = to_f32(decode_attention(bf16_tensor(q, cuda_device), cache, torch.from_numpy(indices), c,
+                                  lengths=torch.from_numpy(lengths), gate=bf16_tensor(gate, cuda_device)))
+    keys = kv.read_quantized(codes["k"], planes["k"], indices, kv_heads, hd)
+    values = kv.read_quantized(codes["v"], planes["v"], indices, kv_heads, hd)
+    mask = np.arange(S)[None, :] <= lengths[:, None]
+    expected = kv.attention(q, keys, values, mask, gate)
+    mx, l2 = rel_err(got, expected)
+    assert mx < 1e-2 and l2 < 5e-3, (mx, l2)
+
+
+def test_decode_attention_wrapped_and_clamped_indices(cuda_device):
+    """Negative cache times wrap once, out-of-range times clamp (the scale gather rule), and
+    runs that are consecutive but not 8-aligned take the per-scale path."""
+    import torch
+
+    from qk_b200.attention_cache import CacheConfig, decode_attention
+
+    rng = np.random.default_rng(17)
+    batch, S, T = 2, 700, 640
+    c = CacheConfig(max_context=T, query_heads=16, kv_heads=2, head_dim=256)
+    cache, codes, planes = _random_cache(torch, cuda_device, rng, batch, T, 2, 256)
+    indices = np.tile((np.arange(S) + 3).astype(np.int32), (batch, 1))  # consecutive, offset 3
+    indices[0, :40] = rng.integers(-2 * T, 0, 40)     # negative: wrap (then clamp to 0)
+    indices[1, 100:140] = rng.integers(T, 3 * T, 40)  # past the end: clamp to T - 1
+    valid = rng.random((batch, S)) < 0.8
+    q = bf16_round(rng.normal(size=(batch, 16, 256)).astype(np.float32))
+    got = to_f32(decode_attention(bf16_tensor(q, cuda_device), cache, torch.from_numpy(indices), c,
+                                  valid=torch.from_numpy(valid)))
+    keys = kv.read_quantized(codes["k"], planes["k"], indices, 2, 256)
+    values = kv.read_quantized(codes["v"], planes["v"], indices, 2, 256)
+    expected = kv.attention(q, keys, values, valid)
+    mx, l2 = rel_err(got, expected)
+    assert mx < 1e-2 and l2 < 5e-3, (mx, l2)

@@ -40,7 +40,7 @@ def _args(_lib, cache, q, gate, idx, lengths, batch, S, T, out):
             batch, S, T, HQ, KV, HD, _lib.ptr(out))
 
 
-@pytest.mark.parametrize("batch,S", [(4, 512), (32, 1024), (1, 40)])
+@pytest.mark.parametrize("batch,S", [(4, 512), (32, 1024), (1, 40), (1, 8192), (150, 512)])
 def test_noalloc_matches_workspace_entry_point_twice_in_a_row(cuda_device, batch, S):
     import torch
 
@@ -76,14 +76,32 @@ def test_noalloc_matches_workspace_entry_point_twice_in_a_row(cuda_device, batch
     assert not torch.equal(outs[0], outs[1])
 
 
-def test_noalloc_refuses_geometry_above_the_fixed_scratch(cuda_device):
+def test_workspace_is_bounded_by_the_sm_count_whatever_the_batch(cuda_device):
+    """One CTA per SM, at most two partial rows each: the workspace (and so the fixed
+    scratch the no-alloc entry point needs) does not grow with B or S."""
+    import torch
+
+    from qk_b200 import _lib
+
+    lib = _lib.load()
+    sms = torch.cuda.get_device_properties(cuda_device).multi_processor_count
+    bound = 2 * sms * (16 + 8 * HD) * 4
+    for batch, S in ((1, 40), (1, 32768), (32, 32768), (150, 512), (1024, 4096)):
+        need = int(lib.qk_kv_q8_attention_workspace_bytes(batch, S, HQ, KV, HD))
+        assert need <= bound, (batch, S, need, bound)
+    assert bound <= STATIC_SCRATCH_BYTES
+
+
+def test_noalloc_refuses_a_workspace_above_the_fixed_scratch_unrun(cuda_device):
+    """The refusal path, driven through a geometry the kernel accepts but whose scratch
+    would not fit: checked against the query, so it only runs where the query exceeds it."""
     from qk_b200 import _lib
 
     lib = _lib.load()
     batch, S, T = 150, 512, 512
     need = int(lib.qk_kv_q8_attention_workspace_bytes(batch, S, HQ, KV, HD))
     if need <= STATIC_SCRATCH_BYTES:
-        pytest.skip(f"this device splits {batch}x{S} into {need} bytes, within the fixed scratch")
+        pytest.skip(f"this device needs {need} bytes for {batch}x{S}, within the fixed scratch")
     launches = _lib.launch_count()
     dummy = ctypes.c_void_p(256)
     rc = lib.qk_kv_q8_decode_attention_noalloc(*([dummy] * 6), None, dummy, None, batch, S, T, HQ,
