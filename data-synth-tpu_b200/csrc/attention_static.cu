@@ -9,11 +9,12 @@
 // partial (max, sum, output) rows. This entry point takes that scratch from
 // `g_attn_scratch` instead.
 //
-// Limit: kStaticScratchBytes (4 MiB). The split kernel runs one CTA per SM and each CTA
-// leaves at most two partial rows, so the workspace query never exceeds
-// 2 * SMs * (16 + 8 * head_dim) * 4 bytes whatever B and S are: 2.4 MB at head_dim 256 on
-// a 148-SM B200. A device whose query exceeds the array is refused with QK_ERR_WORKSPACE
-// before anything runs.
+// Limit: kStaticScratchBytes (16 MiB). The split kernel runs one CTA per SM and each CTA
+// leaves at most two partial rows per KV head, so the workspace query never exceeds
+// 2 * SMs * kv_heads * (16 + 8 * head_dim) * 4 bytes whatever B and S are: 4.9 MB for 2 KV
+// heads at head_dim 256 and 9.9 MB for 8 KV heads at head_dim 128 on a 148-SM B200. A
+// geometry whose query exceeds the array is refused with QK_ERR_WORKSPACE before anything
+// runs.
 //
 // Set-up: the first call on each device (the device current on the calling thread) looks
 // up the array's device address with cudaGetSymbolAddress and caches it. That first call
@@ -30,7 +31,7 @@
 namespace qk {
 namespace {
 
-constexpr size_t kStaticScratchBytes = size_t(4) << 20;
+constexpr size_t kStaticScratchBytes = size_t(16) << 20;
 constexpr int kMaxDevices = 64;
 
 __device__ __align__(256) unsigned char g_attn_scratch[kStaticScratchBytes];

@@ -83,6 +83,7 @@ SIGNATURES = {
     "qk_ep_plan": (_i, [_p, _p, _i, _i, _i, _i, _p, _p, _p, _p, _p, _p]),
     "qk_gather_rows": (_i, [_p, _p, _i64, _i64, _p, _p]),
     "qk_ep_combine": (_i, [_p, _p, _p, _p, _i, _i, _i, _i, _p, _p]),
+    "qk_kv_q8_attention_check": (_i, [_p]),
     "qk_kv_q8_decode_attention_noalloc": (
         _i,
         [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _i, _p, _p],

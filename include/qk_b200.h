@@ -206,7 +206,7 @@ int qk_kv_q8_read(const int8_t* codes, const uint16_t* plane, const int32_t* ind
  * in which case slot s is valid iff s <= lengths[b]; out: BF16 [B, hq, hd].
  * Split-KV: one CTA per SM takes an equal, contiguous range of all pairs' 16-slot tiles; a
  * (b, kv head) pair cut by CTA boundaries leaves one partial (max, sum, out) per CTA in the
- * workspace for an LSE merge. The workspace is at most 2 * SMs * (16 + 8 * hd) * 4 bytes. */
+ * workspace for an LSE merge. The workspace is at most 2 * SMs * kv * (16 + 8 * hd) * 4 bytes. */
 size_t qk_kv_q8_attention_workspace_bytes(int B, int S, int hq, int kv_heads, int head_dim);
 int qk_kv_q8_decode_attention(const uint16_t* q, const int8_t* k_codes, const int8_t* v_codes,
                               const uint16_t* k_scale, const uint16_t* v_scale,
@@ -215,14 +215,19 @@ int qk_kv_q8_decode_attention(const uint16_t* q, const int8_t* k_codes, const in
                               int hq, int kv_heads, int head_dim, uint16_t* out, void* workspace,
                               size_t workspace_bytes, qk_stream_t stream);
 
+/* No counterpart in the reference. QK_ERR_TIMEOUT if a bounded device wait of an earlier
+ * qk_kv_q8_decode_attention on this device gave up (its output is then not valid), else
+ * QK_OK; clears the flag. Synchronises `stream`. */
+int qk_kv_q8_attention_check(qk_stream_t stream);
+
 /* No counterpart in the reference. qk_kv_q8_decode_attention without a workspace, for
  * callers that cannot provide device memory at the call. The split scratch is a fixed
- * 4 MiB array in the library's device image (QK_ATTN_STATIC_SCRATCH_BYTES). A geometry
+ * 16 MiB array in the library's device image (QK_ATTN_STATIC_SCRATCH_BYTES). A geometry
  * whose qk_kv_q8_attention_workspace_bytes() exceeds it returns QK_ERR_WORKSPACE and
  * runs nothing. The first call on a device looks up the array's address, so make it
  * before any stream capture. The scratch is shared per device, so overlapping calls
  * (other streams or threads) race on it; calls in order on one stream are safe. */
-#define QK_ATTN_STATIC_SCRATCH_BYTES (4u << 20)
+#define QK_ATTN_STATIC_SCRATCH_BYTES (16u << 20)
 int qk_kv_q8_decode_attention_noalloc(const uint16_t* q, const int8_t* k_codes,
                                       const int8_t* v_codes, const uint16_t* k_scale,
                                       const uint16_t* v_scale, const int32_t* indices,
