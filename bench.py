@@ -480,7 +480,7 @@ def attention_sweep(device, reps=20):
         pages = ctx // 256
         table = np.stack([rng.permutation(pages) for _ in range(batch)])
         slots = np.arange(ctx)
-        idx = torch.from_numpy((table[:, slots // 256] * 256 + slots % 256).astype(np.int32)).to(device)
+        idx = torch.from_numpy(np.ascontiguousarray((table[:, slots // 256] * 256 + slots % 256).astype(np.int32))).to(device)
         lengths = torch.full((batch,), ctx - 1, dtype=torch.int32, device=device)
         q = torch.randn((batch, 16, 256), device=device, generator=g).to(torch.bfloat16)
         out = torch.empty((batch, 16, 256), dtype=torch.bfloat16, device=device)

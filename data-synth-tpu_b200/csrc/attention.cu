@@ -4,34 +4,34 @@
 // cache write): per batch row b and KV head h (a "pair"), the r = hq / kv query heads of
 // the group attend over S gathered slots.
 //
-// Work split (stream-K): a pair's slots form tiles of 16. The B * kv * ceil(S/16) tiles of
-// all pairs are ordered (b, tile, h) when kv divides the CTA's 8 warps (else (b, h, tile))
-// and cut into one contiguous, equal range per CTA, one CTA per SM, so the grid is
-// balanced whatever B and S are. The 8 warps take the tiles of their CTA's range round
-// robin; with the (b, tile, h) order each warp keeps one KV head, and the warps of the
-// different heads fetch the same cache rows at the same moment (a row holds all heads).
-// Per tile, a warp
-//   - has the tile's cache times (indices) copied by cp.async into a small ring several
-//     tiles ahead, so address generation never waits on a load;
-//   - copies its K and V codes into a two-stage ring completing on one mbarrier per stage:
-//     when the 16 times are consecutive, as 2D tensor copies (TMA) of 16 rows x 128 bytes
-//     with the 128-byte shared-memory swizzle (two boxes per plane at head_dim 256), and
-//     the BF16 scale tiles as 2D tensor copies when the first time is 8-aligned; else one
-//     bulk copy per 128-byte row piece and one load per scale;
-//   - loads the tile's K and V fragments into registers and refills the stage with the
-//     tile two ahead, so two tiles stay in flight while it computes;
+// Work unit: 128 / kg consecutive slots of one batch row for a group of kg KV heads (kg the
+// largest power of two dividing kv, at most 2 at head_dim 256 and 8 at head_dim 128), i.e.
+// eight (16-slot tile, KV head) items - one per warp of the CTA. When the unit's cache
+// times are consecutive (any page table of 128-slot-multiple pages), its K and V codes
+// arrive as 2D tensor copies (TMA) of [unit rows x 128 bytes] boxes with the 128-byte
+// shared-memory swizzle (each box 8 KB at head_dim 256, large enough that the copy engine
+// streams at HBM speed) and its BF16 scales as one 2D box per plane; otherwise as one bulk
+// copy per 128-byte row piece and one load per scale. The units of all batch rows and head
+// groups are cut into one contiguous, equal range per CTA (stream-K, one CTA per SM).
+//
+// Pipeline (no producer warp): the CTA has a two-stage ring of units. Each warp waits for
+// the stage, loads its item's K and V fragments into registers and arrives on the stage's
+// "empty" barrier; warp k % 8 waits for that barrier, refills the stage with unit k + 2 and
+// starts the index copy of unit k + 4 (a four-slot ring of cache times and valid flags, so
+// address generation never waits on a load) - the refill work rotates over the warps.
+// Then each warp
 //   - dequantises K in registers to bf16(code * scale) (read_quantized, :71-81; the
 //     product is exact so the only rounding is BF16 RNE) for QK^T as m16n8k16 MMAs (16
-//     slots x 8 heads, FP32 accumulate); score = bf16(bf16(qk) / sqrt(hd)) (:160-165),
-//     masked, feeds an online softmax (running max / sum per head, FP32); V is dequantised
-//     into the transposed A operand for O^T[d, head] += V^T P^T with
+//     slots x 8 query heads, FP32 accumulate); score = bf16(bf16(qk) / sqrt(hd))
+//     (:160-165), masked, feeds an online softmax (running max / sum per head, FP32);
+//   - dequantises V into the transposed A operand for O^T[d, head] += V^T P^T with
 //     P = bf16(exp(score - running max)).
-// At the end of each batch row (or pair) the CTA merges the warps of each KV head with the
-// log-sum-exp rule in warp order. A pair that lies inside one CTA's range is finished
-// there: divide by the sum, then bf16(bf16(o) * bf16(sigmoid(gate))) (:170). A pair cut by
-// CTA boundaries leaves one partial (max, sum, out) per CTA in the workspace, and the merge
-// kernel (launched as a programmatic dependent of the split kernel, so it is resident when
-// the split kernel ends) combines them in CTA order.
+// At the end of a (batch row, head group) segment the CTA merges the warps of each KV head
+// with the log-sum-exp rule in warp order. A pair that lies inside one CTA's range is
+// finished there: divide by the sum, then bf16(bf16(o) * bf16(sigmoid(gate))) (:170). A
+// pair cut by CTA boundaries leaves one partial (max, sum, out) per CTA in the workspace,
+// and the merge kernel (launched as a programmatic dependent of the split kernel, so it is
+// resident when the split kernel ends) combines them in CTA order.
 // Deviation from the reference, inside the 1e-2 layer tolerance: the reference rounds the
 // normalised probability to BF16 before PV; here the unnormalised exp(score - max) is
 // rounded (normalisation happens after the FP32 sum).
@@ -42,37 +42,35 @@
 namespace qk {
 namespace {
 
-constexpr int kAttnWarps = 8;   // warps per CTA (one CTA per SM)
+constexpr int kAttnWarps = 8;   // warps per CTA (one CTA per SM); one (tile, head) item each
 constexpr int kHeads = 8;       // query heads per KV head handled by the MMA column block
-constexpr int kStages = 2;      // per-warp copy ring depth (the stage is refilled on read)
-constexpr int kMetaLead = 3;    // tiles between a tile's index copy and its code copies
-constexpr int kMetaSlots = 6;   // index ring slots per warp (> kStages + kMetaLead)
-constexpr int kMinTilesPerCta = 2 * kAttnWarps;
+constexpr int kStages = 2;      // unit ring depth
+constexpr int kMetaSlots = 4;   // cache-time ring: unit n's times are copied at unit n-4's release
+constexpr int kUnitRows = 128;  // slots x heads of a unit (16 slots x 8 warps)
 constexpr int kMergeThreads = 256;
 constexpr int kBox = 128;       // bytes of one tensor-copy box row (the 128-byte swizzle span)
+constexpr int kMetaBytes = kUnitRows * 4 + kUnitRows;  // cache times (int32), valid flags (uint8)
 
 template <int HD>
 struct Geo {
-  static constexpr int kGroups = HD / 32;                 // scale groups per slot row
-  static constexpr int kBoxes = HD / kBox;                // boxes per 16-row code tile
-  static constexpr int kTile = 16 * HD;                   // one plane's codes: [box][16 rows][128 B]
-  static constexpr int kScale = kGroups * 16 * 2;         // one scale tile [group][slot] BF16
-  static constexpr int kStage = (2 * kTile + 2 * kScale + 1023) / 1024 * 1024;  // swizzle atoms stay aligned
-  static constexpr int kRing = kStages * kStage;
+  static constexpr int kGroups = HD / 32;                 // scale groups per head row
+  static constexpr int kCodes = kUnitRows * HD;           // one plane of a unit: [box][rows][128 B]
+  static constexpr int kScales = 8 * HD;                  // one scale plane: [kg * groups][rows] BF16
+  static constexpr int kStage = 2 * kCodes + 2 * kScales; // a multiple of 1024 (swizzle atoms)
   static constexpr int kOP = HD == 256 ? 274 : 146;       // o_buf row (floats): conflict-free writes
-  static constexpr int kMeta = 16 * 4 + 16;               // index ring slot: 16 times, 16 valid flags
-  static constexpr int kOOff = kAttnWarps * kRing;        // float o_buf[warps][kHeads][kOP]
+  static constexpr int kOOff = kStages * kStage;          // float o_buf[warps][kHeads][kOP]
   static constexpr int kMOff = kOOff + kAttnWarps * kHeads * kOP * 4;  // float m_s, l_s, f_s [warps][kHeads]
-  static constexpr int kIdxOff = kMOff + 3 * kAttnWarps * kHeads * 4;  // [warps][kMetaSlots][kMeta]
-  static constexpr int kFlagOff = kIdxOff + kAttnWarps * kMetaSlots * kMeta;  // uint32 [warps][stages]
-  static constexpr int kBarOff = kFlagOff + kAttnWarps * kStages * 4;         // uint64 [warps][stages]
-  static constexpr int kQOff = kBarOff + kAttnWarps * kStages * 8;  // bf16 q_s[heads][kHeads][HD], then L
-  static constexpr int kSlotFloats = 2 * kHeads + kHeads * HD;      // partial: m, l, o
-  // dynamic shared memory for `nh` KV heads per segment (plus slack to align to 1024)
-  static constexpr size_t smem(int nh) { return kQOff + static_cast<size_t>(nh) * kHeads * (HD * 2 + 4) + 1024; }
-  // byte of (row, 16-byte chunk) in a plane tile; swizzled when written by a tensor copy
-  __device__ static int at(int row, int chunk, bool swz) {
-    return (chunk >> 3) * (16 * kBox) + row * kBox + (((chunk & 7) ^ (swz ? (row & 7) : 0)) << 4);
+  static constexpr int kIdxOff = kMOff + 3 * kAttnWarps * kHeads * 4;  // [kMetaSlots][kMetaBytes]
+  static constexpr int kBarOff = kIdxOff + kMetaSlots * kMetaBytes;    // uint64 full[stages], meta[slots], empty[stages]
+  static constexpr int kCtlOff = kBarOff + (2 * kStages + kMetaSlots) * 8; // uint32 swz[stages], abort
+  static constexpr int kQOff = kCtlOff + 64;                           // bf16 q_s[kg][kHeads][HD], then float L
+  static constexpr int kSlotFloats = 2 * kHeads + kHeads * HD;         // partial: m, l, o
+  static_assert(kStage % 1024 == 0, "stage size");
+  // dynamic shared memory for kg KV heads per unit (plus slack to align to 1024)
+  static constexpr size_t smem(int kg) { return kQOff + static_cast<size_t>(kg) * kHeads * (HD * 2 + 4) + 1024; }
+  // byte offset of (row, 16-byte chunk of the kg-head row) in a code plane of `rows` rows
+  __device__ static int at(int rows, int row, int chunk, bool swz) {
+    return (chunk >> 3) * (rows * kBox) + row * kBox + (((chunk & 7) ^ (swz ? (row & 7) : 0)) << 4);
   }
   // o_buf column of output dim d (a gap every 32 floats)
   __device__ static int oc(int d) { return d + d / 32; }
@@ -90,14 +88,16 @@ struct AttnArgs {
   const uint16_t* gate;
   uint16_t* out;
   float* part;       // [2 * ctas][kv][kSlotFloats]: CTA c's first (2c) and last (2c + 1) segment
-  long long units;   // B * kv * nt tiles
-  int B, S, T, hq, kv, r, nt, ctas;
-  int hfast;         // tiles ordered (b, tile, h); else (b, h, tile)
-  int seg_units;     // tiles per segment: nt * kv (a batch row) or nt (a pair)
+  long long units;   // B * groups * nch
+  int B, S, T, hq, kv, r, ctas;
+  int kg;            // KV heads per unit
+  int rows;          // slots per unit = kUnitRows / kg
+  int groups;        // kv / kg head groups
+  int nch;           // units per segment (batch row, head group) = ceil(S / rows)
   int tma_codes;     // code tiles of consecutive times use the tensor maps
   int tma_scales;    // ... and the scale tiles too (T % 8 == 0, aligned planes)
-  int idx16;         // indices rows start 16-byte aligned (S % 4 == 0): 4-index copies
-  int flag16;        // valid rows start 16-byte aligned (S % 16 == 0): 16-flag copies
+  int idx16;         // cache-time rows 16-byte aligned (S % 4 == 0): the time ring is used
+  int flag16;        // valid rows 16-byte aligned (S % 16 == 0): flags ride in the time ring
   float div;         // f32(sqrt(hd))
 };
 
@@ -108,7 +108,7 @@ __device__ int g_attn_status;
 __host__ __device__ __forceinline__ long long cta_start(long long c, long long units, int ctas) {
   return c * units / ctas;
 }
-// The CTA whose range holds tile u: the largest c with cta_start(c) <= u.
+// The CTA whose range holds unit u: the largest c with cta_start(c) <= u.
 __device__ __forceinline__ int cta_of(long long u, long long units, int ctas) {
   return static_cast<int>(((u + 1) * ctas - 1) / units);
 }
@@ -146,129 +146,151 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
       : "memory");
 }
 
-// cp.async of 4 bytes (L1-allocating form; the 16-byte form is cp_async16).
-__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+// Expected transaction bytes without an arrival, and a plain arrival (release): the
+// issuing warp registers the copies' bytes, issues them, makes its own stores, then arrives.
+__device__ __forceinline__ void mbar_expect_only(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.expect_tx.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_release(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
 }
 
-// A warp's position in its tile sequence, advanced by kAttnWarps tiles without divisions.
-struct Cursor {
-  int b, h, tile;
-  __device__ void init(long long u, const AttnArgs& a) {
-    const long long per_b = static_cast<long long>(a.nt) * a.kv;
-    b = static_cast<int>(u / per_b);
-    const int rem = static_cast<int>(u - b * per_b);
-    if (a.hfast) {
-      tile = rem / a.kv;
-      h = rem - tile * a.kv;
-    } else {
-      h = rem / a.nt;
-      tile = rem - h * a.nt;
-    }
+// Bounded wait that also gives up at once when another warp has aborted (*abort != 0).
+__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, volatile uint32_t* abort) {
+  if (mbar_try_wait(bar, parity)) return true;
+  for (uint32_t i = 0; i < kWaitLimit; ++i) {
+    if (*abort) return false;
+    if (mbar_try_wait_suspend(bar, parity, kWaitHintNs)) return true;
   }
-  __device__ void advance(const AttnArgs& a) {
-    if (a.hfast) {  // kv divides kAttnWarps: the head stays
-      tile += kAttnWarps / a.kv;
-      while (tile >= a.nt) {
-        tile -= a.nt;
-        ++b;
-      }
-    } else {
-      tile += kAttnWarps;
-      while (tile >= a.nt) {
-        tile -= a.nt;
-        if (++h == a.kv) {
-          h = 0;
-          ++b;
-        }
-      }
-    }
+  return false;
+}
+
+// Unit n of the CTA order: segment (batch row, head group) and chunk of rows slots.
+struct Unit {
+  int b, hg, s0, nvalid;
+  __device__ Unit(long long n, const AttnArgs& a) {
+    const int seg = static_cast<int>(n / a.nch);
+    const int chunk = static_cast<int>(n - static_cast<long long>(seg) * a.nch);
+    b = seg / a.groups;
+    hg = seg - b * a.groups;
+    s0 = chunk * a.rows;
+    nvalid = min(a.rows, a.S - s0);
   }
-  __device__ int seg(const AttnArgs& a) const { return a.hfast ? b : b * a.kv + h; }
 };
 
-// Copy the cache times (and valid flags) of the tile at `at` into index ring slot `slot`.
-// Times of slots past S are not read; their entries are never used.
-__device__ __forceinline__ void copy_meta(const AttnArgs& a, uint8_t* slot, const Cursor& at, int lane) {
-  const int s0 = at.tile * 16;
-  const int64_t row = static_cast<int64_t>(at.b) * a.S + s0;
-  const bool full = s0 + 16 <= a.S;
-  if (a.idx16 && full) {
-    if (lane < 4) cp_async16(slot + 16 * lane, a.indices + row + 4 * lane);
-  } else if (lane < 16 && s0 + lane < a.S) {
-    cp_async4(slot + 4 * lane, a.indices + row + lane);
-  }
-  if (a.valid && a.flag16 && full && lane == 16) cp_async16(slot + 64, a.valid + row);
+// Start the copy of unit n's cache times (and valid flags) into a time-ring slot (one
+// thread; only when the rows are 16-byte aligned).
+__device__ __forceinline__ void issue_meta(const AttnArgs& a, uint8_t* slot, uint64_t* bar, long long n) {
+  const Unit u(n, a);
+  const int64_t row = static_cast<int64_t>(u.b) * a.S + u.s0;
+  const uint32_t flags = a.flag16 ? static_cast<uint32_t>(u.nvalid) : 0u;
+  mbar_expect_tx(bar, static_cast<uint32_t>(u.nvalid) * 4u + flags);
+  bulk_g2s(slot, a.indices + row, static_cast<uint32_t>(u.nvalid) * 4u, bar);
+  if (flags) bulk_g2s(slot + kUnitRows * 4, a.valid + row, flags, bar);
 }
 
-// Issue the code and scale copies of the tile at `at` into `stage`, completing on `bar`,
-// and record in *flag whether the code tiles are swizzled (tensor copies).
+// Issue unit n's code and scale copies into `stage` (one warp), completing on `full`.
+// `swz` records whether the code planes are swizzled (tensor copies). Returns false when
+// the wait for the unit's cache times gave up.
 template <int HD>
-__device__ __forceinline__ void issue_tile(const AttnArgs& a, const CUtensorMap* tm_k, const CUtensorMap* tm_v,
+__device__ __forceinline__ bool issue_unit(const AttnArgs& a, const CUtensorMap* tm_k, const CUtensorMap* tm_v,
                                            const CUtensorMap* tm_ks, const CUtensorMap* tm_vs, uint8_t* stage,
-                                           uint64_t* bar, uint32_t* flag, const int32_t* times, const Cursor& at,
-                                           int lane, uint64_t pol) {
+                                           uint64_t* full, uint32_t* swz, const uint8_t* mslot, uint64_t* mbar,
+                                           uint32_t mparity, volatile uint32_t* abort, long long n, int lane,
+                                           uint64_t pol) {
   using G = Geo<HD>;
-  const int slot = lane & 15;
-  const bool in = at.tile * 16 + slot < a.S;
-  const int t = in ? wrap_clamp(times[slot], a.T) : 0;
-  const uint32_t inmask = __ballot_sync(0xffffffffu, in) & 0xffffu;
-  const int t0 = __shfl_sync(0xffffffffu, t, 0);
-  const bool run = __ballot_sync(0xffffffffu, lane >= 16 || t == t0 + lane) == 0xffffffffu;
-  const bool tma = a.tma_codes && run && inmask == 0xffffu;  // times t0 .. t0+15, all < T
+  const Unit u(n, a);
+  const int rows = a.rows, kg = a.kg;
+  bool ok = true;
+  if (a.idx16) ok = wait_or_abort(mbar, mparity, abort);
+  if (!__all_sync(0xffffffffu, ok)) return false;
+  const int32_t* times = reinterpret_cast<const int32_t*>(mslot);
+  const int64_t trow = static_cast<int64_t>(u.b) * a.S + u.s0;
+  // lane l holds the times of slots l, l + 32, ... (rows <= 128)
+  int t[kUnitRows / 32];
+  bool run = true;
+#pragma unroll
+  for (int q = 0; q < kUnitRows / 32; ++q) t[q] = 0;
+  if (a.idx16) {
+#pragma unroll
+    for (int q = 0; q < kUnitRows / 32; ++q) {
+      const int s = lane + 32 * q;
+      if (s < u.nvalid) t[q] = wrap_clamp(times[s], a.T);
+    }
+  } else {
+#pragma unroll
+    for (int q = 0; q < kUnitRows / 32; ++q) {
+      const int s = lane + 32 * q;
+      if (s < u.nvalid) t[q] = wrap_clamp(a.indices[trow + s], a.T);
+    }
+  }
+  const int t0 = __shfl_sync(0xffffffffu, t[0], 0);
+#pragma unroll
+  for (int q = 0; q < kUnitRows / 32; ++q) {
+    const int s = lane + 32 * q;
+    if (s < u.nvalid && t[q] != t0 + s) run = false;
+  }
+  run = __all_sync(0xffffffffu, run) && u.nvalid == rows;
+  const bool tma = a.tma_codes && run;  // times t0 .. t0 + rows - 1, all < T
   const bool tma_s = tma && a.tma_scales && (t0 & 7) == 0;
-  const uint32_t bytes = (tma ? 2u * G::kTile : __popc(inmask) * 2u * HD) + (tma_s ? 2u * G::kScale : 0u);
+  const int nbox = kg * HD / kBox;
+  const uint32_t bytes = (tma ? 2u * G::kCodes : static_cast<uint32_t>(u.nvalid) * 2u * kg * HD) +
+                         (tma_s ? 2u * G::kScales : 0u);
   if (lane == 0) {
-    *flag = tma ? 1u : 0u;
-    mbar_expect_tx(bar, bytes);
+    fence_proxy_async_smem();  // the warps' reads of the stage come before the new copies
+    *swz = tma ? 1u : 0u;
+    mbar_expect_only(full, bytes);
   }
   __syncwarp();
 
   bool generic = false;
+  const int col0 = u.hg * kg * HD;  // first code byte of the head group in a cache row
   if (tma) {
-    if (lane < 2 * G::kBoxes) {
-      const int plane = lane / G::kBoxes, e = lane % G::kBoxes;
-      tma_load_2d(stage + plane * G::kTile + e * 16 * kBox, plane ? tm_v : tm_k, at.h * HD + e * kBox,
-                  at.b * a.T + t0, bar, pol);
+    if (lane < 2 * nbox) {
+      const int plane = lane / nbox, e = lane % nbox;
+      tma_load_2d(stage + plane * G::kCodes + e * rows * kBox, plane ? tm_v : tm_k, col0 + e * kBox,
+                  u.b * a.T + t0, full, pol);
     }
   } else {
-    // lane l: plane l >> 4 (K, V), row l & 15, as kBoxes linear 128-byte pieces
-    const int plane = lane >> 4;
-    uint8_t* dst = stage + plane * G::kTile + slot * kBox;
-    if (in) {
-      const int64_t off = (static_cast<int64_t>(at.b) * a.T + t) * a.kv * HD + static_cast<int64_t>(at.h) * HD;
-      const int8_t* src = (plane ? a.v_codes : a.k_codes) + off;
+    // one bulk copy per (row, plane, 128-byte piece); rows past S are zero
+    for (int item = lane; item < rows * 2 * nbox; item += 32) {
+      const int s = item % rows, pe = item / rows, plane = pe / nbox, e = pe % nbox;
+      uint8_t* dst = stage + plane * G::kCodes + e * rows * kBox + s * kBox;
+      if (s < u.nvalid) {
+        const int ts = wrap_clamp(a.idx16 ? times[s] : a.indices[trow + s], a.T);
+        const int64_t off = (static_cast<int64_t>(u.b) * a.T + ts) * a.kv * HD + col0 + e * kBox;
+        bulk_g2s_hint(dst, (plane ? a.v_codes : a.k_codes) + off, kBox, full, pol);
+      } else {
 #pragma unroll
-      for (int e = 0; e < G::kBoxes; ++e) bulk_g2s_hint(dst + e * 16 * kBox, src + e * kBox, kBox, bar, pol);
-    } else {  // past the end of the pair: zero codes (and zero scales below)
-#pragma unroll
-      for (int e = 0; e < G::kBoxes; ++e)
-#pragma unroll
-        for (int i = 0; i < kBox / 16; ++i)
-          reinterpret_cast<uint4*>(dst + e * 16 * kBox)[i] = make_uint4(0u, 0u, 0u, 0u);
-      generic = true;
+        for (int i = 0; i < kBox / 16; ++i) reinterpret_cast<uint4*>(dst)[i] = make_uint4(0u, 0u, 0u, 0u);
+        generic = true;
+      }
     }
   }
-  uint8_t* kss = stage + 2 * G::kTile;
-  const int grp0 = (at.b * a.kv + at.h) * G::kGroups;  // first scale row of the pair
+  uint8_t* sc = stage + 2 * G::kCodes;
+  const int grp0 = (u.b * a.kv + u.hg * kg) * G::kGroups;  // first scale row of the head group
   if (tma_s) {
-    if (lane < 2) tma_load_2d(kss + lane * G::kScale, lane ? tm_vs : tm_ks, t0, grp0, bar, pol);
+    if (lane < 2) tma_load_2d(sc + lane * G::kScales, lane ? tm_vs : tm_ks, t0, grp0, full, pol);
   } else {
-#pragma unroll
-    for (int m = 0; m < G::kGroups / 2; ++m) {
-      const int gi = (lane >> 4) + 2 * m;
-      uint16_t sk = 0, sv = 0;
-      if (in) {
-        sk = a.k_scale[static_cast<int64_t>(grp0 + gi) * a.T + t];
-        sv = a.v_scale[static_cast<int64_t>(grp0 + gi) * a.T + t];
+    // [kg * groups][rows] per plane; rows past S are zero
+    for (int item = lane; item < rows * kg * G::kGroups * 2; item += 32) {
+      const int s = item % rows, rg = (item / rows) % (kg * G::kGroups), plane = item / (rows * kg * G::kGroups);
+      uint16_t v = 0;
+      if (s < u.nvalid) {
+        const int ts = wrap_clamp(a.idx16 ? times[s] : a.indices[trow + s], a.T);
+        v = (plane ? a.v_scale : a.k_scale)[static_cast<int64_t>(grp0 + rg) * a.T + ts];
       }
-      reinterpret_cast<uint16_t*>(kss)[gi * 16 + slot] = sk;
-      reinterpret_cast<uint16_t*>(kss + G::kScale)[gi * 16 + slot] = sv;
+      reinterpret_cast<uint16_t*>(sc + plane * G::kScales)[rg * rows + s] = v;
     }
     generic = true;
   }
   // generic stores into the stage come before any later asynchronous copy into it
   if (__any_sync(0xffffffffu, generic)) fence_proxy_async_smem();
+  __syncwarp();
+  // the stage's one arrival, after every lane's stores (the phase completes once the
+  // copies' bytes have landed as well)
+  if (lane == 0) mbar_arrive_release(full);
+  return true;
 }
 
 template <int HD>
@@ -290,149 +312,155 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
   uint8_t* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
   const int tid = threadIdx.x;
-  uint8_t* ring = smem + warp * G::kRing;
   float* o_buf = reinterpret_cast<float*>(smem + G::kOOff);
   float* m_s = reinterpret_cast<float*>(smem + G::kMOff);
   float* l_s = m_s + kAttnWarps * kHeads;
   float* f_s = l_s + kAttnWarps * kHeads;
-  uint8_t* meta = smem + G::kIdxOff + warp * kMetaSlots * G::kMeta;
-  uint32_t* flags = reinterpret_cast<uint32_t*>(smem + G::kFlagOff) + warp * kStages;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + G::kBarOff) + warp * kStages;
+  uint8_t* meta = smem + G::kIdxOff;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + G::kBarOff);
+  uint64_t* mbar = full + kStages;
+  uint64_t* empty = mbar + kMetaSlots;
+  uint32_t* swz = reinterpret_cast<uint32_t*>(smem + G::kCtlOff);
+  volatile uint32_t* abort = swz + kStages;
   uint16_t* q_s = reinterpret_cast<uint16_t*>(smem + G::kQOff);
-  const int nh_max = a.hfast ? a.kv : 1;
-  float* hl_s = reinterpret_cast<float*>(smem + G::kQOff + nh_max * kHeads * HD * 2);  // [nh][kHeads]
+  float* hl_s = reinterpret_cast<float*>(smem + G::kQOff + a.kg * kHeads * HD * 2);  // [kg][kHeads]
 
-  if (lane == 0)
-    for (int i = 0; i < kStages; ++i) mbar_init(bars + i, 1);
-  fence_mbar_init();
+  const int kg = a.kg, rows = a.rows;
+  const int item_tile = warp / kg, hl_w = warp % kg;  // this warp's (tile, head) in every unit
+
+  if (tid == 0) {
+    for (int i = 0; i < kStages + kMetaSlots; ++i) mbar_init(full + i, 1);
+    for (int i = 0; i < kStages; ++i) mbar_init(empty + i, kAttnWarps);
+    *abort = 0;
+    fence_mbar_init();
+  }
   __syncthreads();
   pdl_trigger();  // the merge kernel may take its place now; it waits for this grid to end
 
   const int cta = blockIdx.x;
   const long long u0 = cta_start(cta, a.units, a.ctas), u1 = cta_start(cta + 1, a.units, a.ctas);
-  const int n_mine = u1 - u0 > warp ? static_cast<int>((u1 - u0 - warp + kAttnWarps - 1) / kAttnWarps) : 0;
+  const int nk = static_cast<int>(u1 - u0);
   const uint64_t pol = l2_evict_first_policy();
-  // hfast: warp w keeps head (u0 + w) % kv; heads_of[h] = bit mask of those warps
-  const int h0 = a.hfast ? static_cast<int>(u0 % a.kv) : 0;
-  const int warp_h = a.hfast ? (h0 + warp) % a.kv : 0;
-
-  // cursors over this warp's tiles: `cons` computed, `iss` next code copy, `mc` next index copy
-  Cursor cons, iss, mc;
-  cons.init(u0 + warp, a);
-  iss = cons;
-  mc = cons;
-  // prologue: index copies of the first kStages + kMetaLead tiles (one group each), then
-  // the code copies of the first kStages tiles
-  int metas = 0;
-  for (; metas < kStages + kMetaLead; ++metas) {
-    if (metas < n_mine) {
-      copy_meta(a, meta + (metas % kMetaSlots) * G::kMeta, mc, lane);
-      mc.advance(a);
-    }
-    cp_async_commit();
-  }
-  cp_async_wait<0>();
-  __syncwarp();
-  int issued = 0;
-  for (; issued < kStages && issued < n_mine; ++issued) {
-    issue_tile<HD>(a, &tm_k, &tm_v, &tm_ks, &tm_vs, ring + issued * G::kStage, bars + issued, flags + issued,
-                   reinterpret_cast<const int32_t*>(meta + (issued % kMetaSlots) * G::kMeta), iss, lane, pol);
-    iss.advance(a);
-  }
-
   bool ok = true;
-  int drain_from = 0;
-  const int s_first = static_cast<int>(u0 / a.seg_units), s_last = static_cast<int>((u1 - 1) / a.seg_units);
-  int j = 0;
+
+  // prologue (warp 0): cache times of the first kMetaSlots units, codes of the first two
+  if (warp == 0) {
+    if (a.idx16 && lane == 0)
+      for (int m = 0; m < kMetaSlots && m < nk; ++m) issue_meta(a, meta + m * kMetaBytes, mbar + m, u0 + m);
+    __syncwarp();
+    for (int k = 0; k < kStages && k < nk && ok; ++k)
+      ok = issue_unit<HD>(a, &tm_k, &tm_v, &tm_ks, &tm_vs, smem + k * G::kStage, full + k, swz + k,
+                          meta + k * kMetaBytes, mbar + k, 0, abort, u0 + k, lane, pol);
+    if (!ok && lane == 0) {
+      atomicExch(&g_attn_status, QK_ERR_TIMEOUT);
+      *abort = 1;
+    }
+  }
+
+  const int s_first = static_cast<int>(u0 / a.nch), s_last = static_cast<int>((u1 - 1) / a.nch);
+  int k = 0;
   for (int sg = s_first; sg <= s_last; ++sg) {
-    const int b = a.hfast ? sg : sg / a.kv;
-    const int h_lo = a.hfast ? 0 : sg - b * a.kv, nh = a.hfast ? a.kv : 1;
+    const int b = sg / a.groups, hg = sg - b * a.groups;
     // q of the segment's heads: q_s[hl][r][d], zero rows for r >= a.r
-    for (int i = tid; i < nh * kHeads * HD; i += blockDim.x) {
+    for (int i = tid; i < kg * kHeads * HD; i += blockDim.x) {
       const int hl = i / (kHeads * HD), r = (i / HD) % kHeads, d = i % HD;
-      q_s[i] = r < a.r ? a.q[(static_cast<int64_t>(b) * a.hq + (h_lo + hl) * a.r + r) * HD + d] : 0;
+      q_s[i] = r < a.r ? a.q[(static_cast<int64_t>(b) * a.hq + (hg * kg + hl) * a.r + r) * HD + d] : 0;
     }
     const int len = a.valid ? 0 : a.lengths[b];
     __syncthreads();
-    const int hw = a.hfast ? warp_h : 0;  // this warp's head, relative to h_lo
-    const uint16_t* qh = q_s + hw * kHeads * HD;
+    const uint16_t* qh = q_s + hl_w * kHeads * HD;
     float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
     float o_acc[MT][4];
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt) o_acc[mt][0] = o_acc[mt][1] = o_acc[mt][2] = o_acc[mt][3] = 0.f;
 
-    for (; j < n_mine && cons.seg(a) == sg; ++j, cons.advance(a)) {
-      const int sidx = j % kStages;
-      uint8_t* stage = ring + sidx * G::kStage;
-      const bool got = ok && mbar_wait_bounded(bars + sidx, (j / kStages) & 1);
-      if (!__all_sync(0xffffffffu, got)) {  // a wait gave up: record it, stop issuing and computing
-        if (ok) {
-          if (lane == 0) atomicExch(&g_attn_status, QK_ERR_TIMEOUT);
-          drain_from = j;
+    for (; k < nk && (u0 + k) / a.nch == sg; ++k) {
+      const int sidx = k % kStages;
+      const uint8_t* stage = smem + sidx * G::kStage;
+      const bool got = ok && wait_or_abort(full + sidx, (k / kStages) & 1, abort);
+      if (!__all_sync(0xffffffffu, got) && ok) {
+        if (lane == 0) {
+          atomicExch(&g_attn_status, QK_ERR_TIMEOUT);
+          *abort = 1;
         }
         ok = false;
-        continue;
       }
-      // ---- fragments of this tile into registers; the stage is then refilled ----
+      const int s0 = static_cast<int>((u0 + k) % a.nch) * rows;
+      const int r0 = item_tile * 16;  // this warp's first row in the unit
+      // ---- fragments of this item into registers, then release the stage ----
       uint4 kw[2][KV4];
       float ks[2][KG];
       uint4 vw[4][VV4];
       float vsc[VV4][4];  // V scale of chunk jj (d in [128 jj + 16 g, +16): group g / 2 + 4 jj)
+      bool okv[2];
       {
-        const bool swz = flags[sidx] != 0;
+        const bool sw = swz[sidx] != 0;
         const uint8_t* kt = stage;
-        const uint8_t* vt = stage + G::kTile;
-        const uint16_t* kss = reinterpret_cast<const uint16_t*>(stage + 2 * G::kTile);
-        const uint16_t* vss = kss + G::kScale / 2;
+        const uint8_t* vt = stage + G::kCodes;
+        const uint16_t* kss = reinterpret_cast<const uint16_t*>(stage + 2 * G::kCodes) + hl_w * G::kGroups * rows;
+        const uint16_t* vss = kss + G::kScales / 2;
+        const int ch0 = hl_w * (HD / 16);  // this head's first 16-byte chunk in a kg-head row
 #pragma unroll
         for (int rh = 0; rh < 2; ++rh) {
-          const int row = g + 8 * rh;
+          const int row = r0 + g + 8 * rh;
 #pragma unroll
-          for (int i = 0; i < KV4; ++i) kw[rh][i] = lds_v4(kt + G::at(row, c * KV4 + i, swz));
+          for (int i = 0; i < KV4; ++i) kw[rh][i] = lds_v4(kt + G::at(rows, row, ch0 + c * KV4 + i, sw));
 #pragma unroll
-          for (int i = 0; i < KG; ++i) ks[rh][i] = bf16_to_f32(kss[(c * KG + i) * 16 + row]);
+          for (int i = 0; i < KG; ++i) ks[rh][i] = bf16_to_f32(kss[(c * KG + i) * rows + row]);
         }
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          const int row = 2 * c + (i & 1) + 8 * (i >> 1);
+          const int row = r0 + 2 * c + (i & 1) + 8 * (i >> 1);
 #pragma unroll
           for (int jj = 0; jj < VV4; ++jj) {
-            vw[i][jj] = lds_v4(vt + G::at(row, g + 8 * jj, swz));
-            vsc[jj][i] = bf16_to_f32(vss[(g / 2 + 4 * jj) * 16 + row]);
+            vw[i][jj] = lds_v4(vt + G::at(rows, row, ch0 + g + 8 * jj, sw));
+            vsc[jj][i] = bf16_to_f32(vss[(g / 2 + 4 * jj) * rows + row]);
           }
         }
-      }
-      // valid slots g and g + 8 of this tile
-      bool okv[2];
-      {
-        const uint8_t* mslot = meta + (j % kMetaSlots) * G::kMeta;
+        const uint8_t* mslot = meta + (k % kMetaSlots) * kMetaBytes;
 #pragma unroll
         for (int rh = 0; rh < 2; ++rh) {
-          const int s = cons.tile * 16 + g + 8 * rh;
+          const int s = s0 + r0 + g + 8 * rh;
           bool v = s < a.S;
           if (v) {
             if (!a.valid) v = s <= len;
-            else if (a.flag16 && cons.tile * 16 + 16 <= a.S) v = mslot[64 + g + 8 * rh] != 0;
+            else if (a.flag16) v = mslot[kUnitRows * 4 + r0 + g + 8 * rh] != 0;
             else v = a.valid[static_cast<int64_t>(b) * a.S + s] != 0;
           }
           okv[rh] = v;
         }
       }
-      __syncwarp();  // every lane has its fragments and flags: stage and index slot may be refilled
-      if (issued < n_mine) {
-        cp_async_wait<kMetaLead - 1>();  // the index copy of tile `issued`
-        __syncwarp();
-        issue_tile<HD>(a, &tm_k, &tm_v, &tm_ks, &tm_vs, stage, bars + sidx, flags + sidx,
-                       reinterpret_cast<const int32_t*>(meta + (issued % kMetaSlots) * G::kMeta), iss, lane, pol);
-        iss.advance(a);
-        ++issued;
+      __syncwarp();
+      if (lane == 0) mbar_arrive_release(empty + sidx);  // this warp is done with the stage
+      // warp k % 8 refills the stage with unit k + 2 (and the time slot with unit k + 4) once
+      // every warp has read unit k
+      if (warp == k % kAttnWarps && ok) {
+        if (!wait_or_abort(empty + sidx, (k / kStages) & 1, abort)) {
+          if (lane == 0) {
+            atomicExch(&g_attn_status, QK_ERR_TIMEOUT);
+            *abort = 1;
+          }
+          ok = false;
+        }
       }
-      if (metas < n_mine) {
-        copy_meta(a, meta + (metas % kMetaSlots) * G::kMeta, mc, lane);
-        mc.advance(a);
-        ++metas;
+      if (warp == k % kAttnWarps && ok) {
+        if (k + kStages < nk) {
+          const int kn = k + kStages;
+          const bool issued = issue_unit<HD>(a, &tm_k, &tm_v, &tm_ks, &tm_vs, smem + sidx * G::kStage, full + sidx,
+                                             swz + sidx, meta + (kn % kMetaSlots) * kMetaBytes, mbar + kn % kMetaSlots,
+                                             (kn / kMetaSlots) & 1, abort, u0 + kn, lane, pol);
+          if (!issued) {
+            if (lane == 0) {
+              atomicExch(&g_attn_status, QK_ERR_TIMEOUT);
+              *abort = 1;
+            }
+            ok = false;
+          }
+        }
+        if (ok && a.idx16 && lane == 0 && k + kMetaSlots < nk)
+          issue_meta(a, meta + (k % kMetaSlots) * kMetaBytes, mbar + k % kMetaSlots, u0 + k + kMetaSlots);
       }
-      cp_async_commit();
+      if (!ok) continue;
 
       // ---- QK^T: rows g, g+8 of the tile; lane quarter c holds d in [c*KB, (c+1)*KB) ----
       float sa[4] = {0.f, 0.f, 0.f, 0.f}, sb[4] = {0.f, 0.f, 0.f, 0.f};
@@ -538,8 +566,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
         float M = -INFINITY;
-        for (int w = 0; w < kAttnWarps; ++w)
-          if (!a.hfast || (h0 + w) % a.kv == warp_h) M = fmaxf(M, m_s[w * kHeads + 2 * c + hh]);
+        for (int w = hl_w; w < kAttnWarps; w += kg) M = fmaxf(M, m_s[w * kHeads + 2 * c + hh]);
         f[hh] = m_run[hh] == -INFINITY ? 0.f : expf(m_run[hh] - M);
         if (g == 0) f_s[warp * kHeads + 2 * c + hh] = f[hh];
       }
@@ -556,25 +583,21 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
       }
     }
     __syncthreads();
-    if (tid < nh * kHeads) {  // per (head, query head): the sum L
+    if (tid < kg * kHeads) {  // per (head, query head): the sum L
       const int hl = tid / kHeads, r = tid % kHeads;
       float L = 0.f;
-      for (int w = 0; w < kAttnWarps; ++w)
-        if (!a.hfast || (h0 + w) % a.kv == hl) L = __fadd_rn(L, __fmul_rn(l_s[w * kHeads + r], f_s[w * kHeads + r]));
+      for (int w = hl; w < kAttnWarps; w += kg) L = __fadd_rn(L, __fmul_rn(l_s[w * kHeads + r], f_s[w * kHeads + r]));
       hl_s[tid] = L;
     }
     __syncthreads();
-    const long long lo = static_cast<long long>(sg) * a.seg_units;
-    const bool whole = lo >= u0 && lo + a.seg_units <= u1;
+    const long long lo = static_cast<long long>(sg) * a.nch;
+    const bool whole = lo >= u0 && lo + a.nch <= u1;
     const int last = sg == s_first ? 0 : 1;
-    for (int i = tid; i < nh * a.r * HD; i += blockDim.x) {
+    for (int i = tid; i < kg * a.r * HD; i += blockDim.x) {
       const int hl = i / (a.r * HD), r = (i / HD) % a.r, d = i % HD;
-      // the warps of head hl: w = hl - h0 (mod kv), then every kv-th (all warps unless hfast)
-      const int step = a.hfast ? a.kv : 1;
-      const int w0 = a.hfast ? (hl - h0 + a.kv) % a.kv : 0;
       float O = 0.f;
-      for (int w = w0; w < kAttnWarps; w += step) O = __fadd_rn(O, o_buf[(w * kHeads + r) * G::kOP + G::oc(d)]);
-      const int h = h_lo + hl;
+      for (int w = hl; w < kAttnWarps; w += kg) O = __fadd_rn(O, o_buf[(w * kHeads + r) * G::kOP + G::oc(d)]);
+      const int h = hg * kg + hl;
       if (whole) {
         const int64_t oi = (static_cast<int64_t>(b) * a.hq + h * a.r + r) * HD + d;
         a.out[oi] = bf16_bits_rne(output_value(__fdiv_rn(O, hl_s[hl * kHeads + r]), a.gate, oi));
@@ -583,21 +606,23 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
         part[2 * kHeads + r * HD + d] = O;
       }
     }
-    if (!whole && tid < nh * kHeads) {
+    if (!whole && tid < kg * kHeads) {
       const int hl = tid / kHeads, r = tid % kHeads;
       float M = -INFINITY;
-      for (int w = 0; w < kAttnWarps; ++w)
-        if (!a.hfast || (h0 + w) % a.kv == hl) M = fmaxf(M, m_s[w * kHeads + r]);
-      float* part = a.part + (static_cast<int64_t>(2 * cta + last) * a.kv + h_lo + hl) * G::kSlotFloats;
+      for (int w = hl; w < kAttnWarps; w += kg) M = fmaxf(M, m_s[w * kHeads + r]);
+      float* part = a.part + (static_cast<int64_t>(2 * cta + last) * a.kv + hg * kg + hl) * G::kSlotFloats;
       part[r] = M;
       part[kHeads + r] = hl_s[tid];
     }
     __syncthreads();  // q_s, o_buf and the statistics are rewritten by the next segment
   }
-  // after a timeout, wait (bounded) for the copies still in flight before leaving
-  if (!ok)
-    for (int n = drain_from; n < issued; ++n) mbar_wait_bounded(bars + n % kStages, (n / kStages) & 1);
-  cp_async_wait<0>();
+  // after an abort, wait (bounded) for copies that may still be in flight before leaving
+  if (*abort && tid == 0) {
+    for (int i = 0; i < kStages; ++i) {
+      mbar_wait_bounded(full + i, 0);
+      mbar_wait_bounded(full + i, 1);
+    }
+  }
 }
 
 // Combine the partials of pairs cut by CTA boundaries: block (pair, query head, d slice);
@@ -611,9 +636,9 @@ __global__ void __launch_bounds__(kMergeThreads) attn_merge_kernel(AttnArgs a, i
   const int p = blockIdx.x, r = blockIdx.y;
   if (r >= a.r) return;
   const int b = p / a.kv, h = p - b * a.kv;
-  const int sg = a.hfast ? b : p;
-  const long long lo = static_cast<long long>(sg) * a.seg_units;
-  const int c0 = cta_of(lo, a.units, a.ctas), c1 = cta_of(lo + a.seg_units - 1, a.units, a.ctas);
+  const int sg = b * a.groups + h / a.kg;
+  const long long lo = static_cast<long long>(sg) * a.nch;
+  const int c0 = cta_of(lo, a.units, a.ctas), c1 = cta_of(lo + a.nch - 1, a.units, a.ctas);
   if (c0 == c1) return;  // finished by the split kernel
   const int n = c1 - c0 + 1;
   const int width = HD / dslices, dthreads = width / 8, groups = kMergeThreads / dthreads;
@@ -633,7 +658,7 @@ __global__ void __launch_bounds__(kMergeThreads) attn_merge_kernel(AttnArgs a, i
       x[u][0] = x[u][1] = make_float4(0.f, 0.f, 0.f, 0.f);
       if (k < n) {
         const int cc = c0 + k;
-        const int first = static_cast<int>(cta_start(cc, a.units, a.ctas) / a.seg_units);
+        const int first = static_cast<int>(cta_start(cc, a.units, a.ctas) / a.nch);
         const float* s = a.part + (static_cast<int64_t>(2 * cc + (first == sg ? 0 : 1)) * a.kv + h) * G::kSlotFloats;
         pm[u] = s[r];
         pl[u] = s[kHeads + r];
@@ -679,19 +704,29 @@ __global__ void __launch_bounds__(kMergeThreads) attn_merge_kernel(AttnArgs a, i
   for (int i = 0; i < 8; ++i) a.out[oi + i] = bf16_bits_rne(output_value(__fdiv_rn(O[i], L), a.gate, oi + i));
 }
 
-// CTAs of the split kernel for `units` tiles (one per SM, at least two tiles per warp).
+// KV heads per unit: the largest power of two dividing kv, at most 2 at head_dim 256 (the
+// query tile of more KV heads would not fit beside the ring) and 8 at head_dim 128.
+int heads_per_unit(int kv, int hd) {
+  int kg = 1;
+  while (kg * 2 <= (hd == 256 ? 2 : 8) && kv % (kg * 2) == 0) kg *= 2;
+  return kg;
+}
+
+// CTAs of the split kernel: one per SM, at most one per unit.
 int choose_ctas(long long units) {
-  long long c = units / kMinTilesPerCta;
   const long long cap = sm_count();
-  if (c > cap) c = cap;
-  return c < 1 ? 1 : static_cast<int>(c);
+  return static_cast<int>(units < cap ? (units < 1 ? 1 : units) : cap);
+}
+
+long long units_for(int B, int S, int kv, int hd) {
+  const int kg = heads_per_unit(kv, hd), rows = kUnitRows / kg;
+  return static_cast<long long>(B) * (kv / kg) * ((S + rows - 1) / rows);
 }
 
 size_t slot_bytes(int hd) { return static_cast<size_t>(2 * kHeads + kHeads * hd) * sizeof(float); }
 
 size_t workspace_for(int B, int S, int kv, int hd) {
-  const long long units = static_cast<long long>(B) * kv * ((S + 15) / 16);
-  const int ctas = choose_ctas(units);
+  const int ctas = choose_ctas(units_for(B, S, kv, hd));
   return ctas > 1 ? 2 * static_cast<size_t>(ctas) * kv * slot_bytes(hd) : 0;
 }
 
@@ -775,32 +810,31 @@ int qk_kv_q8_decode_attention(const uint16_t* q, const int8_t* k_codes, const in
   a.q = q; a.k_codes = k_codes; a.v_codes = v_codes; a.k_scale = k_scale; a.v_scale = v_scale;
   a.indices = indices; a.valid = valid; a.lengths = valid ? nullptr : lengths; a.gate = gate; a.out = out;
   a.B = B; a.S = S; a.T = T; a.hq = hq; a.kv = kv_heads; a.r = hq / kv_heads;
-  a.nt = (S + 15) / 16;
-  a.units = static_cast<long long>(B) * kv_heads * a.nt;
+  a.kg = heads_per_unit(kv_heads, head_dim);
+  a.rows = kUnitRows / a.kg;
+  a.groups = kv_heads / a.kg;
+  a.nch = (S + a.rows - 1) / a.rows;
+  a.units = units_for(B, S, kv_heads, head_dim);
   a.ctas = choose_ctas(a.units);
-  const size_t smem_limit = 227 * 1024;
-  const auto smem_of = [&](int nh) { return head_dim == 256 ? Geo<256>::smem(nh) : Geo<128>::smem(nh); };
-  a.hfast = kAttnWarps % kv_heads == 0 && smem_of(kv_heads) <= smem_limit;
-  QK_REQUIRE(smem_of(a.hfast ? kv_heads : 1) <= smem_limit, "attention geometry exceeds shared memory");
-  a.seg_units = a.hfast ? a.nt * kv_heads : a.nt;
   a.idx16 = (S % 4) == 0 && (reinterpret_cast<uintptr_t>(indices) & 15) == 0;
-  a.flag16 = valid && (S % 16) == 0 && (reinterpret_cast<uintptr_t>(valid) & 15) == 0;
+  a.flag16 = a.idx16 && valid && (S % 16) == 0 && (reinterpret_cast<uintptr_t>(valid) & 15) == 0;
   a.div = sqrtf(static_cast<float>(head_dim));
 
   CUtensorMap maps[4];
   memset(maps, 0, sizeof(maps));
-  const uint64_t rows = static_cast<uint64_t>(B) * T, width = static_cast<uint64_t>(kv_heads) * head_dim;
-  a.tma_codes = encode_2d(&maps[0], k_codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, width, rows, width, kBox, 16,
+  const uint64_t nrows = static_cast<uint64_t>(B) * T, width = static_cast<uint64_t>(kv_heads) * head_dim;
+  a.tma_codes = encode_2d(&maps[0], k_codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, width, nrows, width, kBox, a.rows,
                           CU_TENSOR_MAP_SWIZZLE_128B) &&
-                encode_2d(&maps[1], v_codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, width, rows, width, kBox, 16,
+                encode_2d(&maps[1], v_codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, width, nrows, width, kBox, a.rows,
                           CU_TENSOR_MAP_SWIZZLE_128B);
   const uint64_t planes = static_cast<uint64_t>(B) * kv_heads * (head_dim / 32);
+  const uint32_t scale_rows = static_cast<uint32_t>(a.kg * (head_dim / 32));
   a.tma_scales = a.tma_codes && (T % 8) == 0 && (reinterpret_cast<uintptr_t>(k_scale) & 15) == 0 &&
                  (reinterpret_cast<uintptr_t>(v_scale) & 15) == 0 &&
                  encode_2d(&maps[2], k_scale, CU_TENSOR_MAP_DATA_TYPE_UINT16, T, planes,
-                           static_cast<uint64_t>(T) * 2, 16, head_dim / 32, CU_TENSOR_MAP_SWIZZLE_NONE) &&
+                           static_cast<uint64_t>(T) * 2, a.rows, scale_rows, CU_TENSOR_MAP_SWIZZLE_NONE) &&
                  encode_2d(&maps[3], v_scale, CU_TENSOR_MAP_DATA_TYPE_UINT16, T, planes,
-                           static_cast<uint64_t>(T) * 2, 16, head_dim / 32, CU_TENSOR_MAP_SWIZZLE_NONE);
+                           static_cast<uint64_t>(T) * 2, a.rows, scale_rows, CU_TENSOR_MAP_SWIZZLE_NONE);
 
   if (a.ctas > 1) {
     const size_t need = workspace_for(B, S, kv_heads, head_dim);
@@ -810,7 +844,7 @@ int qk_kv_q8_decode_attention(const uint16_t* q, const int8_t* k_codes, const in
     a.part = static_cast<float*>(workspace);
   }
   cudaStream_t st = as_stream(stream);
-  const size_t smem = smem_of(a.hfast ? kv_heads : 1);
+  const size_t smem = head_dim == 256 ? Geo<256>::smem(a.kg) : Geo<128>::smem(a.kg);
   const void* kern = head_dim == 256 ? reinterpret_cast<const void*>(attn_stream_kernel<256>)
                                      : reinterpret_cast<const void*>(attn_stream_kernel<128>);
   if (int rc = allow_smem(kern, smem)) return rc;
@@ -820,9 +854,9 @@ int qk_kv_q8_decode_attention(const uint16_t* q, const int8_t* k_codes, const in
     attn_stream_kernel<128><<<a.ctas, kAttnWarps * 32, smem, st>>>(maps[0], maps[1], maps[2], maps[3], a);
   QK_LAUNCHED("attn_stream_kernel");
   if (a.ctas > 1) {
-    // partials per cut segment: about seg_units / (units / ctas) + 1; wider merges split d further
+    // partials per cut segment: about nch / (units / ctas) + 1; wider merges split d further
     const long long per = a.units / a.ctas;
-    const long long n = (a.seg_units + per - 1) / per + 1;
+    const long long n = (a.nch + per - 1) / per + 1;
     const int dslices = n > 32 ? 4 : (n > 8 ? 2 : 1);
     const dim3 grid(static_cast<unsigned>(static_cast<long long>(B) * kv_heads), kHeads, dslices);
     const cudaError_t e = head_dim == 256

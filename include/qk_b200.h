@@ -206,7 +206,8 @@ int qk_kv_q8_read(const int8_t* codes, const uint16_t* plane, const int32_t* ind
  * in which case slot s is valid iff s <= lengths[b]; out: BF16 [B, hq, hd].
  * Split-KV: one CTA per SM takes an equal, contiguous range of all pairs' 16-slot tiles; a
  * (b, kv head) pair cut by CTA boundaries leaves one partial (max, sum, out) per CTA in the
- * workspace for an LSE merge. The workspace is at most 2 * SMs * kv * (16 + 8 * hd) * 4 bytes. */
+ * workspace for an LSE merge. It is at most 2 * SMs * kv * (16 + 8 * hd) * 4 bytes, whatever
+ * B and S are. */
 size_t qk_kv_q8_attention_workspace_bytes(int B, int S, int hq, int kv_heads, int head_dim);
 int qk_kv_q8_decode_attention(const uint16_t* q, const int8_t* k_codes, const int8_t* v_codes,
                               const uint16_t* k_scale, const uint16_t* v_scale,
