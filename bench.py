@@ -429,13 +429,7 @@ def b200_arm(args):
     if sweep:
         line["sweep"] = sweep
     if rank == 0 and not args.no_attention:
-        peak_gbs, _ = hbm_peak()
-        attn = attention_sweep(device)
-        for r in attn:
-            r["frac"] = r["gbs"] / peak_gbs
-        line["attention"] = {"kernel": "attn_split_kernel + attn_merge_kernel (Q8 KV, 16q/2kv, hd 256)",
-                             "bytes_per_slot": ATTN_SLOT_BYTES, "l2": "flushed before every call",
-                             "configs": attn}
+        line["attention"] = attention_report(device, args)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         gbs, experts = cpu_port_gbs(raw, args.qtype, res["x"], res["ids"], res["weights"],
                                     budget_s=args.ref_budget)
@@ -454,7 +448,7 @@ ATTN_CONFIGS = ((1, 4096), (8, 4096), (32, 4096), (1, 32768), (8, 32768), (32, 3
 ATTN_SLOT_BYTES = 2 * 512 + 2 * 16 * 2  # K + V codes (2 kv heads x 256) + BF16 scales (16 groups)
 
 
-def attention_sweep(device, reps=20):
+def attention_sweep(device, reps=20, configs=ATTN_CONFIGS):
     """Q8 KV decode attention: 16 q / 2 kv heads, head dim 256,
     one query token per sequence, every slot of the context attended through a page table
     that is a random permutation (seed 0) of 256-token pages. K/V codes and BF16 scales
@@ -470,7 +464,7 @@ def attention_sweep(device, reps=20):
     stream = torch.cuda.current_stream(device)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
     results = []
-    for batch, ctx in ATTN_CONFIGS:
+    for batch, ctx in configs:
         g = torch.Generator(device=device).manual_seed(batch * 7 + ctx)
         k = torch.randint(-127, 128, (batch, ctx, 512), dtype=torch.int8, device=device, generator=g)
         v = torch.randint(-127, 128, (batch, ctx, 512), dtype=torch.int8, device=device, generator=g)
@@ -510,6 +504,31 @@ def attention_sweep(device, reps=20):
                         "tokens_per_s": batch / (ms * 1e-3)})
         del k, v, ks, vs
     return results
+
+
+def attention_report(device, args):
+    peak_gbs, _ = hbm_peak()
+    attn = attention_sweep(device, args.attn_reps, parse_attn_configs(args.attn_configs))
+    for r in attn:
+        r["frac"] = r["gbs"] / peak_gbs
+    return {"kernel": "attn_stream_kernel + attn_merge_kernel (Q8 KV, 16q/2kv, hd 256)",
+            "bytes_per_slot": ATTN_SLOT_BYTES, "l2": "flushed before every call", "configs": attn}
+
+
+def parse_attn_configs(text):
+    if not text:
+        return ATTN_CONFIGS
+    return tuple(tuple(int(v) for v in item.split("x")) for item in text.split(","))
+
+
+def attention_only(args):
+    """Only the Q8 KV decode attention sweep (one GPU), as one JSON line."""
+    import torch
+
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    print(json.dumps({"attention": attention_report(device, args)}), flush=True)
+    return 0
 
 
 def e2e_measure(fn, tensors, device, args, res, rank):
@@ -570,6 +589,11 @@ def main():
     parser.add_argument("--sweep", action="store_true", help="also time M in {1,4,16,64,256}")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--no-attention", action="store_true", help="skip the Q8 KV attention sweep")
+    parser.add_argument("--attention-only", action="store_true",
+                        help="only the Q8 KV attention sweep (no MoE step, no contract line)")
+    parser.add_argument("--attn-configs", default="",
+                        help="attention configs as BxCTX[,BxCTX...] (default: the six of the sweep)")
+    parser.add_argument("--attn-reps", type=int, default=20)
     parser.add_argument("--ref-budget", type=float, default=10.0,
                         help="seconds of CPU work per reference sample")
     args = parser.parse_args()
@@ -577,6 +601,8 @@ def main():
         parser.error("--warmup must be >= 3")
     if args.impl == "reference":
         return reference_arm(args)
+    if args.attention_only:
+        return attention_only(args)
     return b200_arm(args)
 
 

@@ -14,11 +14,13 @@
 // copy per 128-byte row piece and one load per scale. The units of all batch rows and head
 // groups are cut into one contiguous, equal range per CTA (stream-K, one CTA per SM).
 //
-// Pipeline (no producer warp): the CTA has a two-stage ring of units. Each warp waits for
-// the stage, loads its item's K and V fragments into registers and arrives on the stage's
-// "empty" barrier; warp k % 8 waits for that barrier, refills the stage with unit k + 2 and
-// starts the index copy of unit k + 4 (a four-slot ring of cache times and valid flags, so
-// address generation never waits on a load) - the refill work rotates over the warps.
+// Pipeline: the CTA has a two-stage ring of units and a four-slot ring of cache times and
+// valid flags, filled by one producer warp (its warpgroup gives registers to the eight
+// consumer warps through setmaxnreg). Each consumer warp waits for the stage, loads its
+// item's K and V fragments into registers and arrives on the stage's "empty" barrier; the
+// producer, once all eight have arrived, starts the time copy of unit k + 4 and the code
+// and scale copies of unit k + 2 (it checks that unit's cache times, landed two units
+// earlier, for a consecutive run). Units are stepped through with cursors (no divisions).
 // Then each warp
 //   - dequantises K in registers to bf16(code * scale) (read_quantized, :71-81; the
 //     product is exact so the only rounding is BF16 RNE) for QK^T as m16n8k16 MMAs (16
@@ -42,7 +44,13 @@
 namespace qk {
 namespace {
 
-constexpr int kAttnWarps = 8;   // warps per CTA (one CTA per SM); one (tile, head) item each
+constexpr int kAttnWarps = 8;   // consumer warps per CTA (one CTA per SM); one (tile, head) item each
+constexpr int kProducerWarps = 4;  // one warpgroup: its first warp issues the copies, the others leave
+constexpr int kThreads = (kAttnWarps + kProducerWarps) * 32;
+// setmaxnreg split of the launch's kThreads x 168 registers: consumers grow, producers shrink
+constexpr int kLaunchRegs = 168, kConsumerRegs = 232, kProducerRegs = 40;
+static_assert(kAttnWarps * 32 * kConsumerRegs + kProducerWarps * 32 * kProducerRegs <= kThreads * kLaunchRegs,
+              "register split exceeds the launch's registers");
 constexpr int kHeads = 8;       // query heads per KV head handled by the MMA column block
 constexpr int kStages = 2;      // unit ring depth
 constexpr int kMetaSlots = 4;   // cache-time ring: unit n's times are copied at unit n-4's release
@@ -55,19 +63,25 @@ template <int HD>
 struct Geo {
   static constexpr int kGroups = HD / 32;                 // scale groups per head row
   static constexpr int kCodes = kUnitRows * HD;           // one plane of a unit: [box][rows][128 B]
-  static constexpr int kScales = 8 * HD;                  // one scale plane: [kg * groups][rows] BF16
-  static constexpr int kStage = 2 * kCodes + 2 * kScales; // a multiple of 1024 (swizzle atoms)
+  static constexpr int kKgMax = HD == 256 ? 2 : 8;        // KV heads per unit at most
+  // one scale plane: [kg * groups][rows + 8] BF16 (the 8-time pad staggers the groups over
+  // the shared-memory banks), sized for the largest kg
+  static constexpr int kScales = 8 * HD + kKgMax * HD / 2;
+  static constexpr int kStage = (2 * kCodes + 2 * kScales + 1023) / 1024 * 1024;  // swizzle atoms
+  static constexpr int kQP = HD + 16;                     // q_s row (bf16): 4 blocks of HD / 4, each + 4
   static constexpr int kOP = HD == 256 ? 274 : 146;       // o_buf row (floats): conflict-free writes
   static constexpr int kOOff = kStages * kStage;          // float o_buf[warps][kHeads][kOP]
   static constexpr int kMOff = kOOff + kAttnWarps * kHeads * kOP * 4;  // float m_s, l_s, f_s [warps][kHeads]
   static constexpr int kIdxOff = kMOff + 3 * kAttnWarps * kHeads * 4;  // [kMetaSlots][kMetaBytes]
   static constexpr int kBarOff = kIdxOff + kMetaSlots * kMetaBytes;    // uint64 full[stages], meta[slots], empty[stages]
   static constexpr int kCtlOff = kBarOff + (2 * kStages + kMetaSlots) * 8; // uint32 swz[stages], abort
-  static constexpr int kQOff = kCtlOff + 64;                           // bf16 q_s[kg][kHeads][HD], then float L
+  static constexpr int kQOff = kCtlOff + 64;                           // bf16 q_s[kg][kHeads][kQP], then float L
   static constexpr int kSlotFloats = 2 * kHeads + kHeads * HD;         // partial: m, l, o
   static_assert(kStage % 1024 == 0, "stage size");
   // dynamic shared memory for kg KV heads per unit (plus slack to align to 1024)
-  static constexpr size_t smem(int kg) { return kQOff + static_cast<size_t>(kg) * kHeads * (HD * 2 + 4) + 1024; }
+  static constexpr size_t smem(int kg) { return kQOff + static_cast<size_t>(kg) * kHeads * (kQP * 2 + 4) + 1024; }
+  // q_s element of (head row, d): blocks of HD / 4 (one lane quarter's K bytes) 8 bytes apart
+  __device__ static int qi(int hrow, int d) { return hrow * kQP + (d / (HD / 4)) * (HD / 4 + 4) + d % (HD / 4); }
   // byte offset of (row, 16-byte chunk of the kg-head row) in a code plane of `rows` rows
   __device__ static int at(int rows, int row, int chunk, bool swz) {
     return (chunk >> 3) * (rows * kBox) + row * kBox + (((chunk & 7) ^ (swz ? (row & 7) : 0)) << 4);
@@ -95,6 +109,7 @@ struct AttnArgs {
   int groups;        // kv / kg head groups
   int nch;           // units per segment (batch row, head group) = ceil(S / rows)
   int tma_codes;     // code tiles of consecutive times use the tensor maps
+  int code3d;        // ... one 3D box per plane (else one 2D box per 128-byte column block)
   int tma_scales;    // ... and the scale tiles too (T % 8 == 0, aligned planes)
   int idx16;         // cache-time rows 16-byte aligned (S % 4 == 0): the time ring is used
   int flag16;        // valid rows 16-byte aligned (S % 16 == 0): flags ride in the time ring
@@ -146,6 +161,16 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
       : "memory");
 }
 
+// 3D tensor copy (no multicast): one box of a [col block][time row][128 bytes] view.
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar,
+                                            uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_addr(bar)), "l"(policy)
+      : "memory");
+}
+
 // Expected transaction bytes without an arrival, and a plain arrival (release): the
 // issuing warp registers the copies' bytes, issues them, makes its own stores, then arrives.
 __device__ __forceinline__ void mbar_expect_only(uint64_t* bar, uint32_t bytes) {
@@ -165,27 +190,38 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, vo
   return false;
 }
 
-// Unit n of the CTA order: segment (batch row, head group) and chunk of rows slots.
+// A unit of the CTA order: segment (batch row b, head group hg) and chunk ch of `rows`
+// slots. Decoded from the unit number once; cursors then step through consecutive units
+// without divisions.
 struct Unit {
-  int b, hg, s0, nvalid;
+  int b, hg, ch;
   __device__ Unit(long long n, const AttnArgs& a) {
     const int seg = static_cast<int>(n / a.nch);
-    const int chunk = static_cast<int>(n - static_cast<long long>(seg) * a.nch);
+    ch = static_cast<int>(n - static_cast<long long>(seg) * a.nch);
     b = seg / a.groups;
     hg = seg - b * a.groups;
-    s0 = chunk * a.rows;
-    nvalid = min(a.rows, a.S - s0);
   }
+  __device__ void next(const AttnArgs& a) {
+    if (++ch == a.nch) {
+      ch = 0;
+      if (++hg == a.groups) {
+        hg = 0;
+        ++b;
+      }
+    }
+  }
+  __device__ int s0(const AttnArgs& a) const { return ch * a.rows; }
+  __device__ int nvalid(const AttnArgs& a) const { return min(a.rows, a.S - ch * a.rows); }
 };
 
 // Start the copy of unit n's cache times (and valid flags) into a time-ring slot (one
 // thread; only when the rows are 16-byte aligned).
-__device__ __forceinline__ void issue_meta(const AttnArgs& a, uint8_t* slot, uint64_t* bar, long long n) {
-  const Unit u(n, a);
-  const int64_t row = static_cast<int64_t>(u.b) * a.S + u.s0;
-  const uint32_t flags = a.flag16 ? static_cast<uint32_t>(u.nvalid) : 0u;
-  mbar_expect_tx(bar, static_cast<uint32_t>(u.nvalid) * 4u + flags);
-  bulk_g2s(slot, a.indices + row, static_cast<uint32_t>(u.nvalid) * 4u, bar);
+__device__ __forceinline__ void issue_meta(const AttnArgs& a, uint8_t* slot, uint64_t* bar, const Unit& u) {
+  const int nvalid = u.nvalid(a);
+  const int64_t row = static_cast<int64_t>(u.b) * a.S + u.s0(a);
+  const uint32_t flags = a.flag16 ? static_cast<uint32_t>(nvalid) : 0u;
+  mbar_expect_tx(bar, static_cast<uint32_t>(nvalid) * 4u + flags);
+  bulk_g2s(slot, a.indices + row, static_cast<uint32_t>(nvalid) * 4u, bar);
   if (flags) bulk_g2s(slot + kUnitRows * 4, a.valid + row, flags, bar);
 }
 
@@ -196,48 +232,52 @@ template <int HD>
 __device__ __forceinline__ bool issue_unit(const AttnArgs& a, const CUtensorMap* tm_k, const CUtensorMap* tm_v,
                                            const CUtensorMap* tm_ks, const CUtensorMap* tm_vs, uint8_t* stage,
                                            uint64_t* full, uint32_t* swz, const uint8_t* mslot, uint64_t* mbar,
-                                           uint32_t mparity, volatile uint32_t* abort, long long n, int lane,
+                                           uint32_t mparity, volatile uint32_t* abort, const Unit& u, int lane,
                                            uint64_t pol) {
   using G = Geo<HD>;
-  const Unit u(n, a);
   const int rows = a.rows, kg = a.kg;
-  bool ok = true;
-  if (a.idx16) ok = wait_or_abort(mbar, mparity, abort);
-  if (!__all_sync(0xffffffffu, ok)) return false;
+  const int nvalid = u.nvalid(a);
   const int32_t* times = reinterpret_cast<const int32_t*>(mslot);
-  const int64_t trow = static_cast<int64_t>(u.b) * a.S + u.s0;
-  // lane l holds the times of slots l, l + 32, ... (rows <= 128)
-  int t[kUnitRows / 32];
-  bool run = true;
+  const int64_t trow = static_cast<int64_t>(u.b) * a.S + u.s0(a);
+  int t0;
+  bool run;
+  {
+    bool ok = true;
+    if (a.idx16) ok = wait_or_abort(mbar, mparity, abort);
+    if (!__all_sync(0xffffffffu, ok)) return false;
+    // lane l holds the times of slots l, l + 32, ... (rows <= 128)
+    int t[kUnitRows / 32];
+    run = true;
 #pragma unroll
-  for (int q = 0; q < kUnitRows / 32; ++q) t[q] = 0;
-  if (a.idx16) {
+    for (int q = 0; q < kUnitRows / 32; ++q) t[q] = 0;
+    if (a.idx16) {
+#pragma unroll
+      for (int q = 0; q < kUnitRows / 32; ++q) {
+        const int s = lane + 32 * q;
+        if (s < nvalid) t[q] = wrap_clamp(times[s], a.T);
+      }
+    } else {
+#pragma unroll
+      for (int q = 0; q < kUnitRows / 32; ++q) {
+        const int s = lane + 32 * q;
+        if (s < nvalid) t[q] = wrap_clamp(a.indices[trow + s], a.T);
+      }
+    }
+    t0 = __shfl_sync(0xffffffffu, t[0], 0);
 #pragma unroll
     for (int q = 0; q < kUnitRows / 32; ++q) {
       const int s = lane + 32 * q;
-      if (s < u.nvalid) t[q] = wrap_clamp(times[s], a.T);
+      if (s < nvalid && t[q] != t0 + s) run = false;
     }
-  } else {
-#pragma unroll
-    for (int q = 0; q < kUnitRows / 32; ++q) {
-      const int s = lane + 32 * q;
-      if (s < u.nvalid) t[q] = wrap_clamp(a.indices[trow + s], a.T);
-    }
+    run = __all_sync(0xffffffffu, run) && nvalid == rows;
   }
-  const int t0 = __shfl_sync(0xffffffffu, t[0], 0);
-#pragma unroll
-  for (int q = 0; q < kUnitRows / 32; ++q) {
-    const int s = lane + 32 * q;
-    if (s < u.nvalid && t[q] != t0 + s) run = false;
-  }
-  run = __all_sync(0xffffffffu, run) && u.nvalid == rows;
   const bool tma = a.tma_codes && run;  // times t0 .. t0 + rows - 1, all < T
   const bool tma_s = tma && a.tma_scales && (t0 & 7) == 0;
   const int nbox = kg * HD / kBox;
-  const uint32_t bytes = (tma ? 2u * G::kCodes : static_cast<uint32_t>(u.nvalid) * 2u * kg * HD) +
-                         (tma_s ? 2u * G::kScales : 0u);
+  const int sp = rows + 8;  // scale plane pitch (times)
+  const uint32_t bytes = (tma ? 2u * G::kCodes : static_cast<uint32_t>(nvalid) * 2u * kg * HD) +
+                         (tma_s ? 4u * kg * G::kGroups * sp : 0u);
   if (lane == 0) {
-    fence_proxy_async_smem();  // the warps' reads of the stage come before the new copies
     *swz = tma ? 1u : 0u;
     mbar_expect_only(full, bytes);
   }
@@ -245,7 +285,9 @@ __device__ __forceinline__ bool issue_unit(const AttnArgs& a, const CUtensorMap*
 
   bool generic = false;
   const int col0 = u.hg * kg * HD;  // first code byte of the head group in a cache row
-  if (tma) {
+  if (tma && a.code3d) {
+    if (lane < 2) tma_load_3d(stage + lane * G::kCodes, lane ? tm_v : tm_k, 0, u.b * a.T + t0, col0 / kBox, full, pol);
+  } else if (tma) {
     if (lane < 2 * nbox) {
       const int plane = lane / nbox, e = lane % nbox;
       tma_load_2d(stage + plane * G::kCodes + e * rows * kBox, plane ? tm_v : tm_k, col0 + e * kBox,
@@ -256,7 +298,7 @@ __device__ __forceinline__ bool issue_unit(const AttnArgs& a, const CUtensorMap*
     for (int item = lane; item < rows * 2 * nbox; item += 32) {
       const int s = item % rows, pe = item / rows, plane = pe / nbox, e = pe % nbox;
       uint8_t* dst = stage + plane * G::kCodes + e * rows * kBox + s * kBox;
-      if (s < u.nvalid) {
+      if (s < nvalid) {
         const int ts = wrap_clamp(a.idx16 ? times[s] : a.indices[trow + s], a.T);
         const int64_t off = (static_cast<int64_t>(u.b) * a.T + ts) * a.kv * HD + col0 + e * kBox;
         bulk_g2s_hint(dst, (plane ? a.v_codes : a.k_codes) + off, kBox, full, pol);
@@ -272,15 +314,15 @@ __device__ __forceinline__ bool issue_unit(const AttnArgs& a, const CUtensorMap*
   if (tma_s) {
     if (lane < 2) tma_load_2d(sc + lane * G::kScales, lane ? tm_vs : tm_ks, t0, grp0, full, pol);
   } else {
-    // [kg * groups][rows] per plane; rows past S are zero
+    // [kg * groups][rows + 8] per plane; rows past S are zero
     for (int item = lane; item < rows * kg * G::kGroups * 2; item += 32) {
       const int s = item % rows, rg = (item / rows) % (kg * G::kGroups), plane = item / (rows * kg * G::kGroups);
       uint16_t v = 0;
-      if (s < u.nvalid) {
+      if (s < nvalid) {
         const int ts = wrap_clamp(a.idx16 ? times[s] : a.indices[trow + s], a.T);
         v = (plane ? a.v_scale : a.k_scale)[static_cast<int64_t>(grp0 + rg) * a.T + ts];
       }
-      reinterpret_cast<uint16_t*>(sc + plane * G::kScales)[rg * rows + s] = v;
+      reinterpret_cast<uint16_t*>(sc + plane * G::kScales)[rg * sp + s] = v;
     }
     generic = true;
   }
@@ -293,8 +335,59 @@ __device__ __forceinline__ bool issue_unit(const AttnArgs& a, const CUtensorMap*
   return true;
 }
 
+// Barrier over the consumer warps only (the producer warpgroup never joins).
+__device__ __forceinline__ void consumer_sync() {
+  asm volatile("bar.sync 1, %0;" ::"n"(kAttnWarps * 32) : "memory");
+}
+
+template <int N>
+__device__ __forceinline__ void regs_grow() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+__device__ __forceinline__ void regs_shrink() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
+// The producer warp: for each unit of the CTA's range, wait until the consumers are done
+// with the unit two places back (its stage and time slot), start the time copy of the unit
+// two places ahead and the code / scale copies of this unit. Returns false on a timeout.
 template <int HD>
-__global__ void __launch_bounds__(kAttnWarps * 32, 1)
+__device__ __forceinline__ bool attn_produce(const AttnArgs& a, const CUtensorMap* tm_k, const CUtensorMap* tm_v,
+                                          const CUtensorMap* tm_ks, const CUtensorMap* tm_vs, uint8_t* smem,
+                                          long long u0, int nk, int lane) {
+  using G = Geo<HD>;
+  uint8_t* meta = smem + G::kIdxOff;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + G::kBarOff);
+  uint64_t* mbar = full + kStages;
+  uint64_t* empty = mbar + kMetaSlots;
+  uint32_t* swz = reinterpret_cast<uint32_t*>(smem + G::kCtlOff);
+  volatile uint32_t* abort = swz + kStages;
+  const uint64_t pol = l2_evict_first_policy();
+  Unit iss(u0, a), met(u0, a);
+  for (int m = 0; m < 2; ++m) {
+    if (a.idx16 && lane == 0 && m < nk) issue_meta(a, meta + m * kMetaBytes, mbar + m, met);
+    met.next(a);
+  }
+  for (int n = 0; n < nk; ++n) {
+    const int st = n % kStages;
+    if (n >= kStages && !__all_sync(0xffffffffu, wait_or_abort(empty + st, (n / kStages - 1) & 1, abort)))
+      return false;
+    const int nm = n + 2;  // its time slot held unit n - 2
+    if (a.idx16 && lane == 0 && nm < nk)
+      issue_meta(a, meta + (nm % kMetaSlots) * kMetaBytes, mbar + nm % kMetaSlots, met);
+    met.next(a);
+    if (!issue_unit<HD>(a, tm_k, tm_v, tm_ks, tm_vs, smem + st * G::kStage, full + st, swz + st,
+                        meta + (n % kMetaSlots) * kMetaBytes, mbar + n % kMetaSlots, (n / kMetaSlots) & 1, abort,
+                        iss, lane, pol))
+      return false;
+    iss.next(a);
+  }
+  return true;
+}
+
+template <int HD>
+__global__ void __launch_bounds__(kThreads, 1)
     attn_stream_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                        const __grid_constant__ CUtensorMap tm_ks, const __grid_constant__ CUtensorMap tm_vs,
                        AttnArgs a) {
@@ -323,7 +416,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
   uint32_t* swz = reinterpret_cast<uint32_t*>(smem + G::kCtlOff);
   volatile uint32_t* abort = swz + kStages;
   uint16_t* q_s = reinterpret_cast<uint16_t*>(smem + G::kQOff);
-  float* hl_s = reinterpret_cast<float*>(smem + G::kQOff + a.kg * kHeads * HD * 2);  // [kg][kHeads]
+  float* hl_s = reinterpret_cast<float*>(smem + G::kQOff + a.kg * kHeads * G::kQP * 2);  // [kg][kHeads]
 
   const int kg = a.kg, rows = a.rows;
   const int item_tile = warp / kg, hl_w = warp % kg;  // this warp's (tile, head) in every unit
@@ -340,41 +433,47 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
   const int cta = blockIdx.x;
   const long long u0 = cta_start(cta, a.units, a.ctas), u1 = cta_start(cta + 1, a.units, a.ctas);
   const int nk = static_cast<int>(u1 - u0);
-  const uint64_t pol = l2_evict_first_policy();
-  bool ok = true;
 
-  // prologue (warp 0): cache times of the first kMetaSlots units, codes of the first two
-  if (warp == 0) {
-    if (a.idx16 && lane == 0)
-      for (int m = 0; m < kMetaSlots && m < nk; ++m) issue_meta(a, meta + m * kMetaBytes, mbar + m, u0 + m);
-    __syncwarp();
-    for (int k = 0; k < kStages && k < nk && ok; ++k)
-      ok = issue_unit<HD>(a, &tm_k, &tm_v, &tm_ks, &tm_vs, smem + k * G::kStage, full + k, swz + k,
-                          meta + k * kMetaBytes, mbar + k, 0, abort, u0 + k, lane, pol);
-    if (!ok && lane == 0) {
-      atomicExch(&g_attn_status, QK_ERR_TIMEOUT);
-      *abort = 1;
+  if (warp >= kAttnWarps) {  // the producer warpgroup
+    regs_shrink<kProducerRegs>();
+    if (warp == kAttnWarps) {
+      if (!attn_produce<HD>(a, &tm_k, &tm_v, &tm_ks, &tm_vs, smem, u0, nk, lane) && lane == 0) {
+        atomicExch(&g_attn_status, QK_ERR_TIMEOUT);
+        *abort = 1;
+      }
+      // after an abort, wait (bounded) for copies that may still be in flight before leaving
+      if (*abort && lane == 0) {
+        for (int i = 0; i < kStages; ++i) {
+          mbar_wait_bounded(full + i, 0);
+          mbar_wait_bounded(full + i, 1);
+        }
+      }
     }
+    return;
   }
+  regs_grow<kConsumerRegs>();
+  bool ok = true;
+  Unit cur(u0, a);
 
   const int s_first = static_cast<int>(u0 / a.nch), s_last = static_cast<int>((u1 - 1) / a.nch);
   int k = 0;
   for (int sg = s_first; sg <= s_last; ++sg) {
     const int b = sg / a.groups, hg = sg - b * a.groups;
-    // q of the segment's heads: q_s[hl][r][d], zero rows for r >= a.r
-    for (int i = tid; i < kg * kHeads * HD; i += blockDim.x) {
+    // q of the segment's heads: q_s[hl][r][d] (padded blocks), zero rows for r >= a.r
+    for (int i = tid; i < kg * kHeads * HD; i += kAttnWarps * 32) {
       const int hl = i / (kHeads * HD), r = (i / HD) % kHeads, d = i % HD;
-      q_s[i] = r < a.r ? a.q[(static_cast<int64_t>(b) * a.hq + (hg * kg + hl) * a.r + r) * HD + d] : 0;
+      q_s[G::qi(hl * kHeads + r, d)] =
+          r < a.r ? a.q[(static_cast<int64_t>(b) * a.hq + (hg * kg + hl) * a.r + r) * HD + d] : 0;
     }
     const int len = a.valid ? 0 : a.lengths[b];
-    __syncthreads();
-    const uint16_t* qh = q_s + hl_w * kHeads * HD;
+    consumer_sync();
+    const uint16_t* qh = q_s + hl_w * kHeads * G::kQP;
     float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
     float o_acc[MT][4];
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt) o_acc[mt][0] = o_acc[mt][1] = o_acc[mt][2] = o_acc[mt][3] = 0.f;
 
-    for (; k < nk && (u0 + k) / a.nch == sg; ++k) {
+    for (; k < nk && cur.b == b && cur.hg == hg; ++k, cur.next(a)) {
       const int sidx = k % kStages;
       const uint8_t* stage = smem + sidx * G::kStage;
       const bool got = ok && wait_or_abort(full + sidx, (k / kStages) & 1, abort);
@@ -385,7 +484,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
         }
         ok = false;
       }
-      const int s0 = static_cast<int>((u0 + k) % a.nch) * rows;
+      const int s0 = cur.s0(a);
       const int r0 = item_tile * 16;  // this warp's first row in the unit
       // ---- fragments of this item into registers, then release the stage ----
       uint4 kw[2][KV4];
@@ -397,16 +496,20 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
         const bool sw = swz[sidx] != 0;
         const uint8_t* kt = stage;
         const uint8_t* vt = stage + G::kCodes;
-        const uint16_t* kss = reinterpret_cast<const uint16_t*>(stage + 2 * G::kCodes) + hl_w * G::kGroups * rows;
+        const int sp = rows + 8;  // scale plane pitch
+        const uint16_t* kss = reinterpret_cast<const uint16_t*>(stage + 2 * G::kCodes) + hl_w * G::kGroups * sp;
         const uint16_t* vss = kss + G::kScales / 2;
         const int ch0 = hl_w * (HD / 16);  // this head's first 16-byte chunk in a kg-head row
 #pragma unroll
         for (int rh = 0; rh < 2; ++rh) {
           const int row = r0 + g + 8 * rh;
 #pragma unroll
-          for (int i = 0; i < KV4; ++i) kw[rh][i] = lds_v4(kt + G::at(rows, row, ch0 + c * KV4 + i, sw));
+          // register i holds chunk (i + c) mod KV4 of the lane's K bytes: the lane quarters of
+          // a row pair then read distinct bank groups of the swizzled plane
+          for (int i = 0; i < KV4; ++i)
+            kw[rh][i] = lds_v4(kt + G::at(rows, row, ch0 + c * KV4 + ((i + c) & (KV4 - 1)), sw));
 #pragma unroll
-          for (int i = 0; i < KG; ++i) ks[rh][i] = bf16_to_f32(kss[(c * KG + i) * rows + row]);
+          for (int i = 0; i < KG; ++i) ks[rh][i] = bf16_to_f32(kss[(c * KG + i) * sp + row]);
         }
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
@@ -414,7 +517,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
 #pragma unroll
           for (int jj = 0; jj < VV4; ++jj) {
             vw[i][jj] = lds_v4(vt + G::at(rows, row, ch0 + g + 8 * jj, sw));
-            vsc[jj][i] = bf16_to_f32(vss[(g / 2 + 4 * jj) * rows + row]);
+            vsc[jj][i] = bf16_to_f32(vss[(g / 2 + 4 * jj) * sp + row]);
           }
         }
         const uint8_t* mslot = meta + (k % kMetaSlots) * kMetaBytes;
@@ -430,60 +533,35 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
           okv[rh] = v;
         }
       }
+      // this warp is done with the stage and the unit's time slot (release: every lane's
+      // reads come first); the producer refills them once all eight warps have arrived
       __syncwarp();
-      if (lane == 0) mbar_arrive_release(empty + sidx);  // this warp is done with the stage
-      // warp k % 8 refills the stage with unit k + 2 (and the time slot with unit k + 4) once
-      // every warp has read unit k
-      if (warp == k % kAttnWarps && ok) {
-        if (!wait_or_abort(empty + sidx, (k / kStages) & 1, abort)) {
-          if (lane == 0) {
-            atomicExch(&g_attn_status, QK_ERR_TIMEOUT);
-            *abort = 1;
-          }
-          ok = false;
-        }
-      }
-      if (warp == k % kAttnWarps && ok) {
-        if (k + kStages < nk) {
-          const int kn = k + kStages;
-          const bool issued = issue_unit<HD>(a, &tm_k, &tm_v, &tm_ks, &tm_vs, smem + sidx * G::kStage, full + sidx,
-                                             swz + sidx, meta + (kn % kMetaSlots) * kMetaBytes, mbar + kn % kMetaSlots,
-                                             (kn / kMetaSlots) & 1, abort, u0 + kn, lane, pol);
-          if (!issued) {
-            if (lane == 0) {
-              atomicExch(&g_attn_status, QK_ERR_TIMEOUT);
-              *abort = 1;
-            }
-            ok = false;
-          }
-        }
-        if (ok && a.idx16 && lane == 0 && k + kMetaSlots < nk)
-          issue_meta(a, meta + (k % kMetaSlots) * kMetaBytes, mbar + k % kMetaSlots, u0 + k + kMetaSlots);
-      }
+      if (lane == 0) mbar_arrive_release(empty + sidx);
       if (!ok) continue;
 
       // ---- QK^T: rows g, g+8 of the tile; lane quarter c holds d in [c*KB, (c+1)*KB) ----
-      float sa[4] = {0.f, 0.f, 0.f, 0.f}, sb[4] = {0.f, 0.f, 0.f, 0.f};
+      float sacc[4][4];  // four independent MMA chains over the k-steps
+#pragma unroll
+      for (int i = 0; i < 4; ++i) sacc[i][0] = sacc[i][1] = sacc[i][2] = sacc[i][3] = 0.f;
 #pragma unroll
       for (int st = 0; st < KSTEPS; ++st) {
-        const int gi = (st * 4) / 32;
+        const int j = (st / 4 + c) & (KV4 - 1);  // the chunk register st / 4 holds
         uint32_t af[4];
 #pragma unroll
         for (int rh = 0; rh < 2; ++rh) {
           const uint32_t wx = word(kw[rh][st / 4], st % 4) ^ 0x80808080u;
-          const float sc = ks[rh][gi];
+          const float sc = (KG == 1 || (j >> 1) == 0) ? ks[rh][0] : ks[rh][KG - 1];
           af[rh] = dq_pair(s8_at<0>(wx), s8_at<1>(wx), sc, sc);
           af[2 + rh] = dq_pair(s8_at<2>(wx), s8_at<3>(wx), sc, sc);
         }
-        const uint2 qb = *reinterpret_cast<const uint2*>(qh + g * HD + c * KB + 4 * st);
-        if (st & 1) mma_bf16(sb, af, qb.x, qb.y);
-        else mma_bf16(sa, af, qb.x, qb.y);
+        const uint2 qb = *reinterpret_cast<const uint2*>(qh + G::qi(g, c * KB + 16 * j + 4 * (st % 4)));
+        mma_bf16(sacc[st & 3], af, qb.x, qb.y);
       }
       // ---- scores, online softmax (heads 2c, 2c+1; slots g, g+8) ----
       float pr[4];
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        const float raw = bf16_round(sa[i] + sb[i]);
+        const float raw = bf16_round((sacc[0][i] + sacc[1][i]) + (sacc[2][i] + sacc[3][i]));
         const float sc = HD == 256 ? __fmul_rn(raw, 0.0625f) : __fdiv_rn(raw, a.div);
         pr[i] = okv[i >> 1] ? bf16_round(sc) : -INFINITY;
       }
@@ -560,7 +638,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
         l_s[warp * kHeads + 2 * c + hh] = l_run[hh];
       }
     }
-    __syncthreads();
+    consumer_sync();
     {
       float f[2];
 #pragma unroll
@@ -582,18 +660,18 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
         r1[G::oc(d0 + 1)] = __fmul_rn(o_acc[mt][3], f[1]);
       }
     }
-    __syncthreads();
+    consumer_sync();
     if (tid < kg * kHeads) {  // per (head, query head): the sum L
       const int hl = tid / kHeads, r = tid % kHeads;
       float L = 0.f;
       for (int w = hl; w < kAttnWarps; w += kg) L = __fadd_rn(L, __fmul_rn(l_s[w * kHeads + r], f_s[w * kHeads + r]));
       hl_s[tid] = L;
     }
-    __syncthreads();
+    consumer_sync();
     const long long lo = static_cast<long long>(sg) * a.nch;
     const bool whole = lo >= u0 && lo + a.nch <= u1;
     const int last = sg == s_first ? 0 : 1;
-    for (int i = tid; i < kg * a.r * HD; i += blockDim.x) {
+    for (int i = tid; i < kg * a.r * HD; i += kAttnWarps * 32) {
       const int hl = i / (a.r * HD), r = (i / HD) % a.r, d = i % HD;
       float O = 0.f;
       for (int w = hl; w < kAttnWarps; w += kg) O = __fadd_rn(O, o_buf[(w * kHeads + r) * G::kOP + G::oc(d)]);
@@ -614,14 +692,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1)
       part[r] = M;
       part[kHeads + r] = hl_s[tid];
     }
-    __syncthreads();  // q_s, o_buf and the statistics are rewritten by the next segment
-  }
-  // after an abort, wait (bounded) for copies that may still be in flight before leaving
-  if (*abort && tid == 0) {
-    for (int i = 0; i < kStages; ++i) {
-      mbar_wait_bounded(full + i, 0);
-      mbar_wait_bounded(full + i, 1);
-    }
+    consumer_sync();  // q_s, o_buf and the statistics are rewritten by the next segment
   }
 }
 
@@ -761,6 +832,22 @@ bool encode_2d(CUtensorMap* map, const void* base, CUtensorMapDataType type, uin
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// 3D map over a [rows][cols] byte plane viewed as [cols / 128][rows][128] (column blocks
+// outermost, so a box lands in shared memory as [block][row][128 bytes], the 2D boxes'
+// layout), box 128 x box_rows x box_blocks with the 128-byte swizzle.
+bool encode_blocks_3d(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows, uint32_t box_rows,
+                      uint32_t box_blocks) {
+  EncodeTiledFn fn = encoder();
+  if (!fn || cols % kBox) return false;
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(kBox), rows, cols / kBox};
+  const cuuint64_t strides[2] = {cols, static_cast<cuuint64_t>(kBox)};
+  const cuuint32_t box[3] = {static_cast<cuuint32_t>(kBox), box_rows, box_blocks};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 }  // namespace
 }  // namespace qk
 
@@ -823,18 +910,23 @@ int qk_kv_q8_decode_attention(const uint16_t* q, const int8_t* k_codes, const in
   CUtensorMap maps[4];
   memset(maps, 0, sizeof(maps));
   const uint64_t nrows = static_cast<uint64_t>(B) * T, width = static_cast<uint64_t>(kv_heads) * head_dim;
-  a.tma_codes = encode_2d(&maps[0], k_codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, width, nrows, width, kBox, a.rows,
-                          CU_TENSOR_MAP_SWIZZLE_128B) &&
-                encode_2d(&maps[1], v_codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, width, nrows, width, kBox, a.rows,
-                          CU_TENSOR_MAP_SWIZZLE_128B);
+  const uint32_t nblk = static_cast<uint32_t>(a.kg * head_dim / kBox);  // column blocks of a unit row
+  a.code3d = encode_blocks_3d(&maps[0], k_codes, width, nrows, a.rows, nblk) &&
+             encode_blocks_3d(&maps[1], v_codes, width, nrows, a.rows, nblk);
+  a.tma_codes = a.code3d ||
+                (encode_2d(&maps[0], k_codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, width, nrows, width, kBox, a.rows,
+                           CU_TENSOR_MAP_SWIZZLE_128B) &&
+                 encode_2d(&maps[1], v_codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, width, nrows, width, kBox, a.rows,
+                           CU_TENSOR_MAP_SWIZZLE_128B));
   const uint64_t planes = static_cast<uint64_t>(B) * kv_heads * (head_dim / 32);
+  // scale boxes: rows + 8 times (the padded plane pitch; times past T read as zero) x kg * groups
   const uint32_t scale_rows = static_cast<uint32_t>(a.kg * (head_dim / 32));
   a.tma_scales = a.tma_codes && (T % 8) == 0 && (reinterpret_cast<uintptr_t>(k_scale) & 15) == 0 &&
                  (reinterpret_cast<uintptr_t>(v_scale) & 15) == 0 &&
                  encode_2d(&maps[2], k_scale, CU_TENSOR_MAP_DATA_TYPE_UINT16, T, planes,
-                           static_cast<uint64_t>(T) * 2, a.rows, scale_rows, CU_TENSOR_MAP_SWIZZLE_NONE) &&
+                           static_cast<uint64_t>(T) * 2, a.rows + 8, scale_rows, CU_TENSOR_MAP_SWIZZLE_NONE) &&
                  encode_2d(&maps[3], v_scale, CU_TENSOR_MAP_DATA_TYPE_UINT16, T, planes,
-                           static_cast<uint64_t>(T) * 2, a.rows, scale_rows, CU_TENSOR_MAP_SWIZZLE_NONE);
+                           static_cast<uint64_t>(T) * 2, a.rows + 8, scale_rows, CU_TENSOR_MAP_SWIZZLE_NONE);
 
   if (a.ctas > 1) {
     const size_t need = workspace_for(B, S, kv_heads, head_dim);
@@ -848,10 +940,23 @@ int qk_kv_q8_decode_attention(const uint16_t* q, const int8_t* k_codes, const in
   const void* kern = head_dim == 256 ? reinterpret_cast<const void*>(attn_stream_kernel<256>)
                                      : reinterpret_cast<const void*>(attn_stream_kernel<128>);
   if (int rc = allow_smem(kern, smem)) return rc;
+  // the consumers' setmaxnreg.inc waits until the producers' registers are free: launch only
+  // with at least the registers the split adds up to (it would wait for ever otherwise)
+  static int regs[2] = {-1, -1};
+  int& nregs = regs[head_dim == 256 ? 1 : 0];
+  if (nregs < 0) {
+    cudaFuncAttributes attr{};
+    const cudaError_t e = cudaFuncGetAttributes(&attr, kern);
+    if (e != cudaSuccess) return cuda_error(e, "attn_stream_kernel attributes");
+    nregs = attr.numRegs;
+  }
+  if (nregs < kLaunchRegs)
+    return set_error(QK_ERR_CUDA, "attention kernel built with %d registers per thread, the split needs %d",
+                     nregs, kLaunchRegs);
   if (head_dim == 256)
-    attn_stream_kernel<256><<<a.ctas, kAttnWarps * 32, smem, st>>>(maps[0], maps[1], maps[2], maps[3], a);
+    attn_stream_kernel<256><<<a.ctas, kThreads, smem, st>>>(maps[0], maps[1], maps[2], maps[3], a);
   else
-    attn_stream_kernel<128><<<a.ctas, kAttnWarps * 32, smem, st>>>(maps[0], maps[1], maps[2], maps[3], a);
+    attn_stream_kernel<128><<<a.ctas, kThreads, smem, st>>>(maps[0], maps[1], maps[2], maps[3], a);
   QK_LAUNCHED("attn_stream_kernel");
   if (a.ctas > 1) {
     // partials per cut segment: about nch / (units / ctas) + 1; wider merges split d further
