@@ -133,15 +133,19 @@ __device__ __forceinline__ int wrap_clamp(int t, int T) {
   return t < 0 ? 0 : (t >= T ? T - 1 : t);
 }
 
-// Signed int8 byte i of `w` as FP32 (exact), via 2^23 + (byte ^ 0x80) - (2^23 + 128).
+// Byte I of `wx` (a code byte with its sign bit flipped, u = code + 128) as the FP32
+// number 2^15 + u: bit pattern 0x47 | 0x00 | u | 0x00, one byte permute.
 template <int I>
 __device__ __forceinline__ float s8_at(uint32_t wx) {
-  return __uint_as_float(__byte_perm(wx, 0x4bu, 0x4550u | I));
+  return __uint_as_float(__byte_perm(wx, 0x4700u, 0x5404u | (I << 4)));
 }
 
-__device__ __forceinline__ uint32_t dq_pair(float c0, float c1, float s0, float s1) {
-  const float2 code = __fadd2_rn(make_float2(c0, c1), make_float2(-8388736.f, -8388736.f));
-  const float2 v = __fmul2_rn(code, make_float2(s0, s1));
+// bf16(code * s) for two codes given as 2^15 + u: fma(2^15 + u, s, k) with k = -(2^15 + 128) s
+// is exactly code * s before the one rounding to FP32 (code * s has at most 16 significant
+// bits and k at most 17, so both are exact), then BF16 RNE as in read_quantized.
+__device__ __forceinline__ float dq_bias(float s) { return __fmul_rn(s, -32896.f); }
+__device__ __forceinline__ uint32_t dq_pair(float c0, float c1, float s0, float s1, float k0, float k1) {
+  const float2 v = __ffma2_rn(make_float2(c0, c1), make_float2(s0, s1), make_float2(k0, k1));
   return pack_bf16x2(v.x, v.y);
 }
 
@@ -488,8 +492,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int r0 = item_tile * 16;  // this warp's first row in the unit
       // ---- fragments of this item into registers, then release the stage ----
       uint4 kw[2][KV4];
-      float ks[2][KG];
-      uint4 vw[4][VV4];
+      float ks[2][KG];            // K scales
+      uint4 vw[4][VV4];           // V code words, sign bits flipped
       float vsc[VV4][4];  // V scale of chunk jj (d in [128 jj + 16 g, +16): group g / 2 + 4 jj)
       bool okv[2];
       {
@@ -517,6 +521,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int jj = 0; jj < VV4; ++jj) {
             vw[i][jj] = lds_v4(vt + G::at(rows, row, ch0 + g + 8 * jj, sw));
+            vw[i][jj].x ^= 0x80808080u;
+            vw[i][jj].y ^= 0x80808080u;
+            vw[i][jj].z ^= 0x80808080u;
+            vw[i][jj].w ^= 0x80808080u;
             vsc[jj][i] = bf16_to_f32(vss[(g / 2 + 4 * jj) * sp + row]);
           }
         }
@@ -550,9 +558,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int rh = 0; rh < 2; ++rh) {
           const uint32_t wx = word(kw[rh][st / 4], st % 4) ^ 0x80808080u;
-          const float sc = (KG == 1 || (j >> 1) == 0) ? ks[rh][0] : ks[rh][KG - 1];
-          af[rh] = dq_pair(s8_at<0>(wx), s8_at<1>(wx), sc, sc);
-          af[2 + rh] = dq_pair(s8_at<2>(wx), s8_at<3>(wx), sc, sc);
+          const bool g0 = KG == 1 || (j >> 1) == 0;
+          const float sc = g0 ? ks[rh][0] : ks[rh][KG - 1], kc = dq_bias(sc);
+          af[rh] = dq_pair(s8_at<0>(wx), s8_at<1>(wx), sc, sc, kc, kc);
+          af[2 + rh] = dq_pair(s8_at<2>(wx), s8_at<3>(wx), sc, sc, kc, kc);
         }
         const uint2 qb = *reinterpret_cast<const uint2*>(qh + G::qi(g, c * KB + 16 * j + 4 * (st % 4)));
         mma_bf16(sacc[st & 3], af, qb.x, qb.y);
@@ -577,21 +586,19 @@ __global__ void __launch_bounds__(kThreads, 1)
           alpha[hh] = 1.f;
           pr[hh] = pr[2 + hh] = 0.f;
         } else {
-          alpha[hh] = expf(m_run[hh] - m_new);
-          pr[hh] = expf(pr[hh] - m_new);
-          pr[2 + hh] = expf(pr[2 + hh] - m_new);
+          alpha[hh] = __expf(m_run[hh] - m_new);
+          pr[hh] = __expf(pr[hh] - m_new);
+          pr[2 + hh] = __expf(pr[2 + hh] - m_new);
         }
         m_run[hh] = m_new;
       }
-      // P in BF16 (the MMA operand); the running sum uses the same rounded values.
+      // P in BF16 (the MMA operand); the running sum uses the same rounded values. Each lane
+      // keeps the sum of its own slots (the lanes of a head are added at the segment's end).
       const uint32_t P0 = pack_bf16x2(pr[0], pr[1]), P1 = pack_bf16x2(pr[2], pr[3]);
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
-        float ps = __fadd_rn(bf16_to_f32(static_cast<uint16_t>(P0 >> (16 * hh))),
-                             bf16_to_f32(static_cast<uint16_t>(P1 >> (16 * hh))));
-        ps += __shfl_xor_sync(0xffffffffu, ps, 4);
-        ps += __shfl_xor_sync(0xffffffffu, ps, 8);
-        ps += __shfl_xor_sync(0xffffffffu, ps, 16);
+        const float ps = __fadd_rn(bf16_to_f32(static_cast<uint16_t>(P0 >> (16 * hh))),
+                                   bf16_to_f32(static_cast<uint16_t>(P1 >> (16 * hh))));
         l_run[hh] = __fadd_rn(__fmul_rn(l_run[hh], alpha[hh]), ps);
       }
       if (!__all_sync(0xffffffffu, alpha[0] == 1.f && alpha[1] == 1.f)) {
@@ -613,24 +620,31 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t af[4];
         uint32_t wx[4];
         const float(&vs)[4] = vsc[vi];
+        const float vb[4] = {dq_bias(vs[0]), dq_bias(vs[1]), dq_bias(vs[2]), dq_bias(vs[3])};
 #pragma unroll
-        for (int i = 0; i < 4; ++i) wx[i] = word(vw[i][vi], wi) ^ 0x80808080u;
+        for (int i = 0; i < 4; ++i) wx[i] = word(vw[i][vi], wi);
         if ((byte & 3) == 0) {
-          af[0] = dq_pair(s8_at<0>(wx[0]), s8_at<0>(wx[1]), vs[0], vs[1]);
-          af[1] = dq_pair(s8_at<1>(wx[0]), s8_at<1>(wx[1]), vs[0], vs[1]);
-          af[2] = dq_pair(s8_at<0>(wx[2]), s8_at<0>(wx[3]), vs[2], vs[3]);
-          af[3] = dq_pair(s8_at<1>(wx[2]), s8_at<1>(wx[3]), vs[2], vs[3]);
+          af[0] = dq_pair(s8_at<0>(wx[0]), s8_at<0>(wx[1]), vs[0], vs[1], vb[0], vb[1]);
+          af[1] = dq_pair(s8_at<1>(wx[0]), s8_at<1>(wx[1]), vs[0], vs[1], vb[0], vb[1]);
+          af[2] = dq_pair(s8_at<0>(wx[2]), s8_at<0>(wx[3]), vs[2], vs[3], vb[2], vb[3]);
+          af[3] = dq_pair(s8_at<1>(wx[2]), s8_at<1>(wx[3]), vs[2], vs[3], vb[2], vb[3]);
         } else {
-          af[0] = dq_pair(s8_at<2>(wx[0]), s8_at<2>(wx[1]), vs[0], vs[1]);
-          af[1] = dq_pair(s8_at<3>(wx[0]), s8_at<3>(wx[1]), vs[0], vs[1]);
-          af[2] = dq_pair(s8_at<2>(wx[2]), s8_at<2>(wx[3]), vs[2], vs[3]);
-          af[3] = dq_pair(s8_at<3>(wx[2]), s8_at<3>(wx[3]), vs[2], vs[3]);
+          af[0] = dq_pair(s8_at<2>(wx[0]), s8_at<2>(wx[1]), vs[0], vs[1], vb[0], vb[1]);
+          af[1] = dq_pair(s8_at<3>(wx[0]), s8_at<3>(wx[1]), vs[0], vs[1], vb[0], vb[1]);
+          af[2] = dq_pair(s8_at<2>(wx[2]), s8_at<2>(wx[3]), vs[2], vs[3], vb[2], vb[3]);
+          af[3] = dq_pair(s8_at<3>(wx[2]), s8_at<3>(wx[3]), vs[2], vs[3], vb[2], vb[3]);
         }
         mma_bf16(o_acc[mt], af, b0, b1);
       }
     }
 
     // ---- end of segment: per KV head, merge its warps (log-sum-exp, warp order) ----
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {  // the lanes' partial sums of a head
+      l_run[hh] += __shfl_xor_sync(0xffffffffu, l_run[hh], 4);
+      l_run[hh] += __shfl_xor_sync(0xffffffffu, l_run[hh], 8);
+      l_run[hh] += __shfl_xor_sync(0xffffffffu, l_run[hh], 16);
+    }
     if (g == 0) {
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
