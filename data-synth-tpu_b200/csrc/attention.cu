@@ -508,10 +508,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int rh = 0; rh < 2; ++rh) {
           const int row = r0 + g + 8 * rh;
 #pragma unroll
-          // register i holds chunk (i + c) mod KV4 of the lane's K bytes: the lane quarters of
-          // a row pair then read distinct bank groups of the swizzled plane
-          for (int i = 0; i < KV4; ++i)
-            kw[rh][i] = lds_v4(kt + G::at(rows, row, ch0 + c * KV4 + ((i + c) & (KV4 - 1)), sw));
+          for (int i = 0; i < KV4; ++i) kw[rh][i] = lds_v4(kt + G::at(rows, row, ch0 + c * KV4 + i, sw));
 #pragma unroll
           for (int i = 0; i < KG; ++i) ks[rh][i] = bf16_to_f32(kss[(c * KG + i) * sp + row]);
         }
@@ -553,13 +550,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int i = 0; i < 4; ++i) sacc[i][0] = sacc[i][1] = sacc[i][2] = sacc[i][3] = 0.f;
 #pragma unroll
       for (int st = 0; st < KSTEPS; ++st) {
-        const int j = (st / 4 + c) & (KV4 - 1);  // the chunk register st / 4 holds
+        const int j = st / 4;  // the lane's 16-byte chunk
         uint32_t af[4];
 #pragma unroll
         for (int rh = 0; rh < 2; ++rh) {
           const uint32_t wx = word(kw[rh][st / 4], st % 4) ^ 0x80808080u;
-          const bool g0 = KG == 1 || (j >> 1) == 0;
-          const float sc = g0 ? ks[rh][0] : ks[rh][KG - 1], kc = dq_bias(sc);
+          const float sc = ks[rh][j >> 1], kc = dq_bias(sc);
           af[rh] = dq_pair(s8_at<0>(wx), s8_at<1>(wx), sc, sc, kc, kc);
           af[2 + rh] = dq_pair(s8_at<2>(wx), s8_at<3>(wx), sc, sc, kc, kc);
         }
