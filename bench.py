@@ -314,7 +314,7 @@ def b200_arm(args):
                          hidden=HIDDEN, intermediate=INTER)
     stream = torch.cuda.current_stream(device)
 
-    def run_m(m, steps, warmup, profile):
+    def run_m(m, steps, warmup, profile, sync=True):
         x, ids, weights = workload(m, rank)
         xd = torch.from_numpy(x).to(device).to(torch.bfloat16)
         idd = torch.from_numpy(ids).to(device)
@@ -353,7 +353,7 @@ def b200_arm(args):
             step()
         graph.replay()
         torch.cuda.synchronize(device)
-        if dist:
+        if dist and sync:
             dist.barrier()
         torch.cuda.synchronize(device)
         t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -362,7 +362,7 @@ def b200_arm(args):
             graph.replay()
         t1.record(stream)
         torch.cuda.synchronize(device)
-        if dist:
+        if dist and sync:
             dist.barrier()
         ms = t0.elapsed_time(t1) / steps
         stage_ms = None
@@ -383,10 +383,11 @@ def b200_arm(args):
 
     peak, peak_kind = hbm_peak()
     with ClockSampler(local) as clocks:
-        # untimed soak so clocks settle before the measured region
+        # untimed soak so clocks settle before the measured region; no collectives inside,
+        # since each rank runs as many soak passes as fit in its own wall time
         soak_end = time.time() + args.soak
         while time.time() < soak_end:
-            run_m(args.m, 20, 1, False)
+            run_m(args.m, 20, 1, False, sync=False)
         res = run_m(args.m, args.steps, args.warmup, True)
     ms = res["ms"]
     if dist:
@@ -430,6 +431,8 @@ def b200_arm(args):
         line["sweep"] = sweep
     if rank == 0 and not args.no_attention:
         line["attention"] = attention_report(device, args)
+    if rank == 0 and world == 1 and not args.no_stack:
+        line["stack"] = stack_report(device, args)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         gbs, experts = cpu_port_gbs(raw, args.qtype, res["x"], res["ids"], res["weights"],
                                     budget_s=args.ref_budget)
@@ -515,6 +518,58 @@ def attention_report(device, args):
             "bytes_per_slot": ATTN_SLOT_BYTES, "l2": "flushed before every call", "configs": attn}
 
 
+def stack_report(device, args):
+    """Decode steps of the synthetic 48-layer MoE decoder stack (
+    hidden 2048, Q8-cache GQA 16 q / 2 kv heads of 256 at context 8192 through a random page
+    table of 256-slot pages, 512 routed experts top-10 + 1 shared expert, intermediate 512,
+    Q6_K) on one GPU, one CUDA-graph replay per step. tokens/s = B / step time; GB/s = the
+    step's algorithmic bytes (distinct routed experts per layer x packed bytes, the dense
+    weights, the K/V codes and scales of every attended slot) / step time."""
+    import torch
+
+    from qk_b200.decoder import StackConfig, SyntheticDecoder
+
+    cfg = StackConfig(layers=args.stack_layers, qtype=args.qtype)
+    peak, _ = hbm_peak()
+    t_build = time.time()
+    model = SyntheticDecoder(cfg, device, seed=1)
+    torch.cuda.synchronize(device)
+    build_s = time.time() - t_build
+    stream = torch.cuda.current_stream(device)
+    rows = []
+    for batch in args.stack_batches:
+        state = model.state(batch, seed=2)
+        for _ in range(2):
+            state.step()
+        torch.cuda.synchronize(device)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            state.step()
+        for _ in range(3):
+            graph.replay()
+        torch.cuda.synchronize(device)
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        steps = args.stack_steps
+        t0.record(stream)
+        for _ in range(steps):
+            graph.replay()
+        t1.record(stream)
+        torch.cuda.synchronize(device)
+        ms = t0.elapsed_time(t1) / steps
+        nbytes, distinct = state.step_bytes()
+        kernels, gemms = state.launches_per_step()
+        rows.append({"batch": batch, "ms_per_step": ms, "tokens_per_s": batch / (ms * 1e-3),
+                     "gbs": nbytes / (ms * 1e-3) / 1e9, "frac": nbytes / (ms * 1e-3) / 1e9 / peak,
+                     "bytes_per_step": nbytes, "distinct_experts_per_layer": statistics.mean(distinct),
+                     "launches_per_step": {"library": kernels, "cublas_gemm": gemms}})
+        del graph, state
+        torch.cuda.synchronize(device)
+    return {"workload": "synthetic 48-layer MoE decoder stack (configs[3]), 1 GPU",
+            "layers": cfg.layers, "context": cfg.context, "experts": cfg.experts, "top_k": cfg.top_k,
+            "shared_experts": 1, "qtype": cfg.qtype, "weights": "synthetic (random code bytes, fixed block scales)",
+            "l2": "inputs larger than L2 (packed experts of 48 layers)", "build_s": build_s, "batches": rows}
+
+
 def parse_attn_configs(text):
     if not text:
         return ATTN_CONFIGS
@@ -532,8 +587,12 @@ def attention_only(args):
 
 
 def e2e_measure(fn, tensors, device, args, res, rank):
-    """Public-call throughput with pinned host inputs/outputs copied every step."""
-    import numpy as np
+    """Public-call throughput with pinned host inputs/outputs copied every step.
+
+    Each step copies its x, ids and weights host -> device, runs the public ``fn`` and
+    copies its output device -> host. The three run on their own streams with two buffer
+    slots, so step i's compute overlaps step i+1's input copy and step i-1's output copy,
+    as a serving loop would pipeline them; events order each slot's reuse."""
     import torch
 
     x, ids, weights = res["x"], res["ids"], res["weights"]
@@ -541,35 +600,54 @@ def e2e_measure(fn, tensors, device, args, res, rank):
     x_h = torch.from_numpy(x).to(torch.bfloat16).pin_memory()
     ids_h = torch.from_numpy(ids).pin_memory()
     w_h = torch.from_numpy(weights).to(torch.bfloat16).pin_memory()
-    out_h = torch.empty((rows, HIDDEN), dtype=torch.bfloat16).pin_memory()
-    x_d = torch.empty_like(x_h, device=device)
-    ids_d = torch.empty_like(ids_h, device=device)
-    w_d = torch.empty_like(w_h, device=device)
-    stream = torch.cuda.current_stream(device)
+    slots = 2
+    out_h = [torch.empty((rows, HIDDEN), dtype=torch.bfloat16).pin_memory() for _ in range(slots)]
+    x_d = [torch.empty_like(x_h, device=device) for _ in range(slots)]
+    ids_d = [torch.empty_like(ids_h, device=device) for _ in range(slots)]
+    w_d = [torch.empty_like(w_h, device=device) for _ in range(slots)]
+    h2d, comp, d2h = (torch.cuda.Stream(device) for _ in range(3))
+    copied = [torch.cuda.Event() for _ in range(slots)]
+    computed = [torch.cuda.Event() for _ in range(slots)]
+    read = [torch.cuda.Event() for _ in range(slots)]
 
-    def step():
-        x_d.copy_(x_h, non_blocking=True)
-        ids_d.copy_(ids_h, non_blocking=True)
-        w_d.copy_(w_h, non_blocking=True)
-        out = fn(tensors["gate"], tensors["up"], tensors["down"], x_d, ids_d, w_d)
-        out_h.copy_(out, non_blocking=True)
+    def step(i):
+        s = i % slots
+        with torch.cuda.stream(h2d):
+            if i >= slots:
+                h2d.wait_event(computed[s])  # slot s inputs free once step i - 2 computed
+            x_d[s].copy_(x_h, non_blocking=True)
+            ids_d[s].copy_(ids_h, non_blocking=True)
+            w_d[s].copy_(w_h, non_blocking=True)
+            copied[s].record(h2d)
+        with torch.cuda.stream(comp):
+            comp.wait_event(copied[s])
+            out = fn(tensors["gate"], tensors["up"], tensors["down"], x_d[s], ids_d[s], w_d[s])
+            computed[s].record(comp)
+        with torch.cuda.stream(d2h):
+            d2h.wait_event(computed[s])
+            if i >= slots:
+                d2h.wait_event(read[s])
+            out_h[s].copy_(out, non_blocking=True)
+            out.record_stream(d2h)
+            read[s].record(d2h)
 
-    for _ in range(args.warmup):
-        step()
+    for i in range(max(args.warmup, slots)):
+        step(i)
     torch.cuda.synchronize(device)
     steps = max(3, args.steps // 2)
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    t0.record(stream)
-    for _ in range(steps):
-        step()
-    t1.record(stream)
+    t0.record(h2d)
+    for i in range(steps):
+        step(i)
+    t1.record(d2h)
     torch.cuda.synchronize(device)
     ms = t0.elapsed_time(t1) / steps
-    h2d = x_h.numel() * 2 + ids_h.numel() * 4 + w_h.numel() * 2
-    d2h = out_h.numel() * 2
+    h2d_bytes = x_h.numel() * 2 + ids_h.numel() * 4 + w_h.numel() * 2
+    d2h_bytes = out_h[0].numel() * 2
     world = int(os.environ.get("WORLD_SIZE", "1"))
     return {"value": res["bytes"] * world / (ms * 1e-3) / 1e9, "unit": "GB/s",
-            "ms_per_step": ms, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
+            "ms_per_step": ms, "h2d_bytes_per_step": h2d_bytes, "d2h_bytes_per_step": d2h_bytes,
+            "pipeline": "H2D, compute and D2H on separate streams, 2 buffer slots"}
 
 
 import ctypes  # noqa: E402
@@ -594,6 +672,11 @@ def main():
     parser.add_argument("--attn-configs", default="",
                         help="attention configs as BxCTX[,BxCTX...] (default: the six of the sweep)")
     parser.add_argument("--attn-reps", type=int, default=20)
+    parser.add_argument("--no-stack", action="store_true", help="skip the 48-layer decoder stack")
+    parser.add_argument("--stack-only", action="store_true", help="only the decoder stack (one GPU)")
+    parser.add_argument("--stack-batches", type=lambda t: [int(v) for v in t.split(",")], default=[1, 8, 64])
+    parser.add_argument("--stack-layers", type=int, default=48)
+    parser.add_argument("--stack-steps", type=int, default=10)
     parser.add_argument("--ref-budget", type=float, default=10.0,
                         help="seconds of CPU work per reference sample")
     args = parser.parse_args()
@@ -603,6 +686,13 @@ def main():
         return reference_arm(args)
     if args.attention_only:
         return attention_only(args)
+    if args.stack_only:
+        import torch
+
+        device = torch.device("cuda", 0)
+        torch.cuda.set_device(device)
+        print(json.dumps({"stack": stack_report(device, args)}), flush=True)
+        return 0
     return b200_arm(args)
 
 

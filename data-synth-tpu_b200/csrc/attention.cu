@@ -101,6 +101,8 @@ struct AttnArgs {
   const int32_t* lengths;
   const uint16_t* gate;
   uint16_t* out;
+  float* po;         // partial mode (time-sharded callers): FP32 [B, hq, HD] unnormalised output
+  float* pst;        // ... and FP32 [B, hq, 2] (max, sum) of it, in place of out
   float* part;       // [2 * ctas][kv][kSlotFloats]: CTA c's first (2c) and last (2c + 1) segment
   long long units;   // B * groups * nch
   int B, S, T, hq, kv, r, ctas;
@@ -688,19 +690,28 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int h = hg * kg + hl;
       if (whole) {
         const int64_t oi = (static_cast<int64_t>(b) * a.hq + h * a.r + r) * HD + d;
-        a.out[oi] = bf16_bits_rne(output_value(__fdiv_rn(O, hl_s[hl * kHeads + r]), a.gate, oi));
+        if (a.po)
+          a.po[oi] = O;
+        else
+          a.out[oi] = bf16_bits_rne(output_value(__fdiv_rn(O, hl_s[hl * kHeads + r]), a.gate, oi));
       } else {
         float* part = a.part + (static_cast<int64_t>(2 * cta + last) * a.kv + h) * G::kSlotFloats;
         part[2 * kHeads + r * HD + d] = O;
       }
     }
-    if (!whole && tid < kg * kHeads) {
+    if ((!whole || a.po) && tid < kg * kHeads) {
       const int hl = tid / kHeads, r = tid % kHeads;
       float M = -INFINITY;
       for (int w = hl; w < kAttnWarps; w += kg) M = fmaxf(M, m_s[w * kHeads + r]);
-      float* part = a.part + (static_cast<int64_t>(2 * cta + last) * a.kv + hg * kg + hl) * G::kSlotFloats;
-      part[r] = M;
-      part[kHeads + r] = hl_s[tid];
+      if (!whole) {
+        float* part = a.part + (static_cast<int64_t>(2 * cta + last) * a.kv + hg * kg + hl) * G::kSlotFloats;
+        part[r] = M;
+        part[kHeads + r] = hl_s[tid];
+      } else if (r < a.r) {
+        const int64_t si = (static_cast<int64_t>(b) * a.hq + (hg * kg + hl) * a.r + r) * 2;
+        a.pst[si] = M;
+        a.pst[si + 1] = hl_s[tid];
+      }
     }
     consumer_sync();  // q_s, o_buf and the statistics are rewritten by the next segment
   }
@@ -781,8 +792,41 @@ __global__ void __launch_bounds__(kMergeThreads) attn_merge_kernel(AttnArgs a, i
     for (int i = 0; i < 8; ++i) O[i] = __fadd_rn(O[i], __fmul_rn(sm_o[t * 8 + i], fk));
   }
   const int64_t oi = ((static_cast<int64_t>(b) * a.hq + h * a.r + r) * HD) + d0;
+  if (a.po) {  // partial mode: the unnormalised output and its (max, sum)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) a.po[oi + i] = O[i];
+    if (d0 == 0) {
+      const int64_t si = (static_cast<int64_t>(b) * a.hq + h * a.r + r) * 2;
+      a.pst[si] = M;
+      a.pst[si + 1] = L;
+    }
+    return;
+  }
 #pragma unroll
   for (int i = 0; i < 8; ++i) a.out[oi + i] = bf16_bits_rne(output_value(__fdiv_rn(O[i], L), a.gate, oi + i));
+}
+
+// Log-sum-exp combine of R partial (output, max, sum) sets in set order (the time shards of
+// one decode step, all-gathered across ranks): out = bf16(gate(sum_r o_r e^(m_r - M) /
+// sum_r l_r e^(m_r - M))). A set is rows * hd outputs followed by rows (max, sum) pairs.
+// Block = one (batch row, query head); thread = consecutive d.
+__global__ void __launch_bounds__(256) attn_combine_kernel(const float* __restrict__ parts, int R, long long rows,
+                                                           int hd, const uint16_t* gate, uint16_t* out) {
+  const long long row = blockIdx.x;
+  const long long set = rows * (hd + 2);
+  float M = -INFINITY;
+  for (int k = 0; k < R; ++k) M = fmaxf(M, parts[k * set + rows * hd + row * 2]);
+  for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+    float L = 0.f, O = 0.f;
+    for (int k = 0; k < R; ++k) {
+      const float* st = parts + k * set + rows * hd + row * 2;
+      const float f = st[0] == -INFINITY ? 0.f : expf(st[0] - M);
+      L = __fadd_rn(L, __fmul_rn(st[1], f));
+      O = __fadd_rn(O, __fmul_rn(parts[k * set + row * hd + d], f));
+    }
+    const int64_t oi = row * hd + d;
+    out[oi] = bf16_bits_rne(output_value(__fdiv_rn(O, L), gate, oi));
+  }
 }
 
 // KV heads per unit: the largest power of two dividing kv, at most 2 at head_dim 256 (the
@@ -886,19 +930,24 @@ int qk_kv_q8_attention_check(qk_stream_t stream) {
   return QK_OK;
 }
 
-int qk_kv_q8_decode_attention(const uint16_t* q, const int8_t* k_codes, const int8_t* v_codes,
-                              const uint16_t* k_scale, const uint16_t* v_scale,
-                              const int32_t* indices, const uint8_t* valid, const int32_t* lengths,
-                              const uint16_t* gate, int B, int S, int T, int hq, int kv_heads,
-                              int head_dim, uint16_t* out, void* workspace, size_t workspace_bytes,
-                              qk_stream_t stream) {
+}  // extern "C"
+
+namespace {
+
+// The split and merge launches of one decode attention call: the final BF16 output into
+// `out`, or (po != NULL) the unnormalised FP32 output and its (max, sum) statistics.
+int launch_attention(const uint16_t* q, const int8_t* k_codes, const int8_t* v_codes, const uint16_t* k_scale,
+                     const uint16_t* v_scale, const int32_t* indices, const uint8_t* valid, const int32_t* lengths,
+                     const uint16_t* gate, int B, int S, int T, int hq, int kv_heads, int head_dim, uint16_t* out,
+                     float* po, float* pst, void* workspace, size_t workspace_bytes, qk_stream_t stream) {
   QK_REQUIRE(B >= 0 && S > 0 && T > 0 && hq > 0 && kv_heads > 0, "invalid attention geometry");
   QK_REQUIRE(hq % kv_heads == 0, "Head counts must have integer repetition factors");
   QK_REQUIRE(hq / kv_heads <= kHeads, "at most %d query heads per KV head", kHeads);
   QK_REQUIRE(head_dim == 128 || head_dim == 256, "head_dim must be 128 or 256");
   QK_REQUIRE(valid || lengths, "either valid or lengths is required");
   if (B == 0) return QK_OK;
-  QK_REQUIRE(q && k_codes && v_codes && k_scale && v_scale && indices && out, "null pointer");
+  QK_REQUIRE(q && k_codes && v_codes && k_scale && v_scale && indices && (po ? pst != nullptr : out != nullptr),
+             "null pointer");
   QK_REQUIRE((reinterpret_cast<uintptr_t>(k_codes) & 15) == 0 && (reinterpret_cast<uintptr_t>(v_codes) & 15) == 0,
              "K/V code planes must be 16-byte aligned");
   QK_REQUIRE(static_cast<long long>(B) * T < (1ll << 31) && static_cast<long long>(B) * S < (1ll << 31),
@@ -906,6 +955,7 @@ int qk_kv_q8_decode_attention(const uint16_t* q, const int8_t* k_codes, const in
   AttnArgs a{};
   a.q = q; a.k_codes = k_codes; a.v_codes = v_codes; a.k_scale = k_scale; a.v_scale = v_scale;
   a.indices = indices; a.valid = valid; a.lengths = valid ? nullptr : lengths; a.gate = gate; a.out = out;
+  a.po = po; a.pst = pst;
   a.B = B; a.S = S; a.T = T; a.hq = hq; a.kv = kv_heads; a.r = hq / kv_heads;
   a.kg = heads_per_unit(kv_heads, head_dim);
   a.rows = kUnitRows / a.kg;
@@ -980,6 +1030,46 @@ int qk_kv_q8_decode_attention(const uint16_t* q, const int8_t* k_codes, const in
     if (e != cudaSuccess) return cuda_error(e, "attn_merge_kernel");
     QK_LAUNCHED("attn_merge_kernel");
   }
+  return QK_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int qk_kv_q8_decode_attention(const uint16_t* q, const int8_t* k_codes, const int8_t* v_codes,
+                              const uint16_t* k_scale, const uint16_t* v_scale,
+                              const int32_t* indices, const uint8_t* valid, const int32_t* lengths,
+                              const uint16_t* gate, int B, int S, int T, int hq, int kv_heads,
+                              int head_dim, uint16_t* out, void* workspace, size_t workspace_bytes,
+                              qk_stream_t stream) {
+  return launch_attention(q, k_codes, v_codes, k_scale, v_scale, indices, valid, lengths, gate, B, S, T, hq,
+                          kv_heads, head_dim, out, nullptr, nullptr, workspace, workspace_bytes, stream);
+}
+
+int qk_kv_q8_decode_attention_partial(const uint16_t* q, const int8_t* k_codes, const int8_t* v_codes,
+                                      const uint16_t* k_scale, const uint16_t* v_scale,
+                                      const int32_t* indices, const uint8_t* valid,
+                                      const int32_t* lengths, int B, int S, int T, int hq,
+                                      int kv_heads, int head_dim, float* partial, void* workspace,
+                                      size_t workspace_bytes, qk_stream_t stream) {
+  QK_REQUIRE(partial, "partial is required");
+  QK_REQUIRE((reinterpret_cast<uintptr_t>(partial) & 15) == 0, "partial must be 16-byte aligned");
+  float* stats = partial + static_cast<int64_t>(B) * hq * head_dim;
+  return launch_attention(q, k_codes, v_codes, k_scale, v_scale, indices, valid, lengths, nullptr, B, S, T, hq,
+                          kv_heads, head_dim, nullptr, partial, stats, workspace, workspace_bytes, stream);
+}
+
+int qk_kv_q8_attention_combine(const float* parts, int R, int B, int hq, int head_dim, const uint16_t* gate,
+                               uint16_t* out, qk_stream_t stream) {
+  QK_REQUIRE(R > 0 && B >= 0 && hq > 0 && head_dim > 0, "invalid combine geometry");
+  if (B == 0) return QK_OK;
+  QK_REQUIRE(parts && out, "null pointer");
+  const long long rows = static_cast<long long>(B) * hq;
+  QK_REQUIRE(rows < (1ll << 31), "B * hq must stay below 2^31");
+  cudaStream_t st = as_stream(stream);
+  attn_combine_kernel<<<static_cast<unsigned>(rows), 256, 0, st>>>(parts, R, rows, head_dim, gate, out);
+  QK_LAUNCHED("attn_combine_kernel");
   return QK_OK;
 }
 

@@ -1,0 +1,175 @@
+// The small per-token operations on either side of the routed-expert FFN and the Q8 decode
+// attention in a decoder layer (qwen38_tpu/math.py, attention_cache.py:128-150,
+// math.py:277-284): RMSNorm, the per-head q/k RMSNorm + rotary embedding of the attention
+// step, the shared expert's route, and the residual add. Each is one launch over all rows,
+// so a decode step of many layers is not bound by launches of tiny elementwise kernels.
+// These are latency-bound (a few KB per row); one block per row (or row x head).
+#include "common.cuh"
+
+namespace qk {
+namespace {
+
+constexpr int kRowThreads = 256;
+
+// Block-wide FP32 sum (all threads get the result). `red` holds kRowThreads / 32 floats.
+__device__ __forceinline__ float block_sum(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  __syncthreads();  // `red` may still be read by a previous call
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float s = 0.f;
+  for (int w = 0; w < nw; ++w) s += red[w];
+  return s;
+}
+
+// math.py:27-31 rms: bf16(xf * rsqrt(mean(xf^2) + eps) * gamma), one block per row.
+__global__ void __launch_bounds__(kRowThreads) rms_norm_kernel(const uint16_t* __restrict__ x,
+                                                               const uint16_t* __restrict__ gamma, int width,
+                                                               float eps, uint16_t* __restrict__ out) {
+  __shared__ float red[kRowThreads / 32];
+  const int64_t row = blockIdx.x;
+  const uint16_t* xr = x + row * width;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < width; i += blockDim.x) {
+    const float v = bf16_to_f32(xr[i]);
+    ss = fmaf(v, v, ss);
+  }
+  const float r = rsqrtf(__fadd_rn(__fdiv_rn(block_sum(ss, red), static_cast<float>(width)), eps));
+  for (int i = threadIdx.x; i < width; i += blockDim.x)
+    out[row * width + i] = bf16_bits_rne(__fmul_rn(__fmul_rn(bf16_to_f32(xr[i]), r), bf16_to_f32(gamma[i])));
+}
+
+// attention_cache.py:129-135: the fused projection output of one row is
+// [hq x (q hd | gate hd)] [kv x k hd] [kv x v hd] (BF16). Block (row, head slot):
+// slots < hq are query heads (rms with q_norm, rotary, and the gate copied out), the
+// next kv slots are key heads (rms with k_norm, rotary) with their value heads copied out.
+// Rotary (math.py:231-243 with one position for every section): dims i < half and
+// i + half of the first `rotary` dims rotate by angle position * inv_freq[i], with the
+// cosine and sine rounded to BF16; the rest pass through.
+__global__ void __launch_bounds__(kRowThreads) qk_norm_rope_kernel(
+    const uint16_t* __restrict__ qkv, const uint16_t* __restrict__ q_norm, const uint16_t* __restrict__ k_norm,
+    const float* __restrict__ inv_freq, const int32_t* __restrict__ positions, int hq, int kv, int hd, int rotary,
+    float eps, uint16_t* __restrict__ q_out, uint16_t* __restrict__ gate_out, uint16_t* __restrict__ k_out,
+    uint16_t* __restrict__ v_out) {
+  __shared__ float red[kRowThreads / 32];
+  __shared__ float normed[512];
+  const int64_t b = blockIdx.x;
+  const int slot = blockIdx.y, d = threadIdx.x;
+  const int64_t width = static_cast<int64_t>(2 * hq + 2 * kv) * hd;
+  const uint16_t* row = qkv + b * width;
+  const bool query = slot < hq;
+  const uint16_t* src = query ? row + static_cast<int64_t>(slot) * 2 * hd : row + static_cast<int64_t>(2 * hq + slot - hq) * hd;
+  const uint16_t* gamma = query ? q_norm : k_norm;
+  const float v = d < hd ? bf16_to_f32(src[d]) : 0.f;
+  const float r = rsqrtf(__fadd_rn(__fdiv_rn(block_sum(v * v, red), static_cast<float>(hd)), eps));
+  if (d < hd) normed[d] = bf16_round(__fmul_rn(__fmul_rn(v, r), bf16_to_f32(gamma[d])));
+  __syncthreads();
+  if (d >= hd) return;
+  float o = normed[d];
+  const int half = rotary / 2;
+  if (d < rotary) {
+    const int i = d < half ? d : d - half;
+    const float angle = __fmul_rn(static_cast<float>(positions[b]), inv_freq[i]);
+    const float cs = bf16_round(cosf(angle)), sn = bf16_round(sinf(angle));
+    const float a = normed[i], c = normed[i + half];
+    o = d < half ? __fsub_rn(__fmul_rn(a, cs), __fmul_rn(c, sn)) : __fadd_rn(__fmul_rn(c, cs), __fmul_rn(a, sn));
+  }
+  if (query) {
+    const int64_t oi = (b * hq + slot) * hd + d;
+    q_out[oi] = bf16_bits_rne(o);
+    gate_out[oi] = src[hd + d];
+  } else {
+    const int h = slot - hq;
+    const int64_t oi = (b * kv + h) * hd + d;
+    k_out[oi] = bf16_bits_rne(o);
+    v_out[oi] = row[static_cast<int64_t>(2 * hq + kv + h) * hd + d];
+  }
+}
+
+// out = bf16(f32(x) + f32(y)) over n values (out may alias x).
+__global__ void residual_add_kernel(const uint16_t* x, const uint16_t* __restrict__ y, int64_t n, uint16_t* out) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    out[i] = bf16_bits_rne(__fadd_rn(bf16_to_f32(x[i]), bf16_to_f32(y[i])));
+}
+
+// Routes of each row plus one route to the shared expert: ids_out[b] = ids[b] ++ shared_id,
+// w_out[b] = w[b] ++ bf16(sigmoid(bf16(h[b] . wsr))) (math.py:282-283, the shared expert's
+// sigmoid gate). One block per row.
+__global__ void __launch_bounds__(kRowThreads) append_shared_route_kernel(
+    const int32_t* __restrict__ ids, const uint16_t* __restrict__ w, int k, const uint16_t* __restrict__ h,
+    const uint16_t* __restrict__ wsr, int H, int shared_id, int32_t* __restrict__ ids_out,
+    uint16_t* __restrict__ w_out) {
+  __shared__ float red[kRowThreads / 32];
+  const int64_t b = blockIdx.x;
+  float s = 0.f;
+  for (int i = threadIdx.x; i < H; i += blockDim.x) s = fmaf(bf16_to_f32(h[b * H + i]), bf16_to_f32(wsr[i]), s);
+  const float dot = bf16_round(block_sum(s, red));
+  if (threadIdx.x < k) {
+    ids_out[b * (k + 1) + threadIdx.x] = ids[b * k + threadIdx.x];
+    w_out[b * (k + 1) + threadIdx.x] = w[b * k + threadIdx.x];
+  }
+  if (threadIdx.x == 0) {
+    ids_out[b * (k + 1) + k] = shared_id;
+    w_out[b * (k + 1) + k] = bf16_bits_rne(sigmoid_ref(dot));
+  }
+}
+
+}  // namespace
+}  // namespace qk
+
+using namespace qk;
+
+extern "C" {
+
+int qk_rms_norm(const uint16_t* x, const uint16_t* gamma, int rows, int width, float eps, uint16_t* out,
+                qk_stream_t stream) {
+  QK_REQUIRE(rows >= 0 && width > 0, "invalid rms geometry");
+  if (rows == 0) return QK_OK;
+  QK_REQUIRE(x && gamma && out, "null pointer");
+  rms_norm_kernel<<<rows, kRowThreads, 0, as_stream(stream)>>>(x, gamma, width, eps, out);
+  QK_LAUNCHED("rms_norm_kernel");
+  return QK_OK;
+}
+
+int qk_qk_norm_rope(const uint16_t* qkv, const uint16_t* q_norm, const uint16_t* k_norm, const float* inv_freq,
+                    const int32_t* positions, int B, int hq, int kv, int head_dim, int rotary_dim, float eps,
+                    uint16_t* q_out, uint16_t* gate_out, uint16_t* k_out, uint16_t* v_out, qk_stream_t stream) {
+  QK_REQUIRE(B >= 0 && hq > 0 && kv > 0, "invalid head geometry");
+  QK_REQUIRE(head_dim > 0 && head_dim <= kRowThreads, "head_dim must be in [1, %d]", kRowThreads);
+  QK_REQUIRE(rotary_dim >= 0 && rotary_dim <= head_dim && rotary_dim % 2 == 0, "rotary_dim must be even and <= head_dim");
+  if (B == 0) return QK_OK;
+  QK_REQUIRE(qkv && q_norm && k_norm && positions && q_out && gate_out && k_out && v_out, "null pointer");
+  QK_REQUIRE(inv_freq || rotary_dim == 0, "inv_freq is required when rotary_dim > 0");
+  qk_norm_rope_kernel<<<dim3(B, hq + kv), kRowThreads, 0, as_stream(stream)>>>(
+      qkv, q_norm, k_norm, inv_freq, positions, hq, kv, head_dim, rotary_dim, eps, q_out, gate_out, k_out, v_out);
+  QK_LAUNCHED("qk_norm_rope_kernel");
+  return QK_OK;
+}
+
+int qk_residual_add(const uint16_t* x, const uint16_t* y, int64_t n, uint16_t* out, qk_stream_t stream) {
+  QK_REQUIRE(n >= 0, "invalid size");
+  if (n == 0) return QK_OK;
+  QK_REQUIRE(x && y && out, "null pointer");
+  const int64_t blocks = (n + 255) / 256;
+  residual_add_kernel<<<static_cast<unsigned>(blocks < 4 * 148 ? blocks : 4 * 148), 256, 0, as_stream(stream)>>>(
+      x, y, n, out);
+  QK_LAUNCHED("residual_add_kernel");
+  return QK_OK;
+}
+
+int qk_append_shared_route(const int32_t* ids, const uint16_t* weights, int B, int k, const uint16_t* h,
+                           const uint16_t* shared_router, int H, int shared_id, int32_t* ids_out,
+                           uint16_t* weights_out, qk_stream_t stream) {
+  QK_REQUIRE(B >= 0 && k > 0 && k < kRowThreads && H > 0, "invalid route geometry");
+  if (B == 0) return QK_OK;
+  QK_REQUIRE(ids && weights && h && shared_router && ids_out && weights_out, "null pointer");
+  append_shared_route_kernel<<<B, kRowThreads, 0, as_stream(stream)>>>(ids, weights, k, h, shared_router, H,
+                                                                       shared_id, ids_out, weights_out);
+  QK_LAUNCHED("append_shared_route_kernel");
+  return QK_OK;
+}
+
+}  // extern "C"

@@ -44,6 +44,7 @@ struct Workspace {
   int32_t* entry_token;   // [B k] token of each entry (expert-sorted)
   float* entry_weight;    // [B k] bf16-valued route weight of each entry
   int32_t* route_entry;   // [B k] entry of route (b, j), -1 if none
+  int32_t* entry_route;   // [B k] route b * k + j that owns each entry
   uint8_t* xt;            // gate/up activation tiles [rows_max x H bf16]
   uint8_t* ht;            // down activation tiles [rows_max x I bf16]
   uint16_t* y;            // [B k, H]
@@ -84,6 +85,7 @@ size_t layout(const qk_moe_desc& d, int max_tokens, uint8_t* base, Workspace* ws
   uint8_t* et = take(R * 4);
   uint8_t* ew = take(R * 4);
   uint8_t* re = take(R * 4);
+  uint8_t* er = take(R * 4);
   uint8_t* xt = take(rows * d.hidden * 2);
   uint8_t* ht = take(rows * d.intermediate * 2);
   uint8_t* y = take(R * d.hidden * 2);
@@ -98,6 +100,7 @@ size_t layout(const qk_moe_desc& d, int max_tokens, uint8_t* base, Workspace* ws
     ws->entry_token = reinterpret_cast<int32_t*>(et);
     ws->entry_weight = reinterpret_cast<float*>(ew);
     ws->route_entry = reinterpret_cast<int32_t*>(re);
+    ws->entry_route = reinterpret_cast<int32_t*>(er);
     ws->xt = xt;
     ws->ht = ht;
     ws->y = reinterpret_cast<uint16_t*>(y);
@@ -245,6 +248,7 @@ __global__ void __launch_bounds__(1024) moe_route_kernel(const int32_t* __restri
         slot = offsets[e] + atomicAdd(&cursor[e], 1);
         ws.entry_token[slot] = b;
         ws.entry_weight[slot] = w;
+        ws.entry_route[slot] = b * k + j;
       }
       ws.route_entry[b * k + j] = slot;
     }
@@ -296,18 +300,23 @@ __global__ void __launch_bounds__(256) moe_dispatch_kernel(const uint16_t* __res
 // ------------------------------------------------------------------------------------
 constexpr int kMaxTopK = 32;
 
-// One warp per token: lane j holds route j's entry; ranks by expert id give the reference's
-// ascending-expert accumulation order. Each lane owns 8 columns of each 256-column block
-// and, per entry, loads all its blocks of a 2048-column group before accumulating them in
-// FP32, so a token's loads are in flight together.
+// One warp per (token, 256-column block): lane j holds route j's entry; ranks by expert id
+// give the reference's ascending-expert accumulation order. Each lane owns 8 columns of the
+// block and loads the rows of up to 8 routes before accumulating them in FP32, so a warp's
+// loads are in flight together; small batches still spread over many SMs.
+// With `yr` (tensor parallel: the FP32 down projection of each route, summed over the
+// tensor ranks) the expert output of route (b, j) is bf16(yr[b * k + j]) (grouped_experts.py:
+// 113-119: psum before the BF16 rounding); otherwise the entry's BF16 y.
 __global__ void __launch_bounds__(256) moe_combine_kernel(const int32_t* __restrict__ ids, int B,
                                                           int k, int H, int out_bf16, void* out,
-                                                          Workspace ws) {
-  constexpr int kBlocks = 8;  // 256-column blocks per group
+                                                          const float* __restrict__ yr, Workspace ws) {
+  constexpr int kBatch = 8;  // route rows in flight per lane
   pdl_wait();
   const int lane = threadIdx.x & 31;
-  const int b = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  if (b >= B) return;
+  const int blocks = H / 256;
+  const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (gw >= B * blocks) return;
+  const int b = gw / blocks, c0 = (gw - b * blocks) * 256 + lane * 8;
   const int entry = lane < k ? ws.route_entry[b * k + lane] : -1;
   const int eid = entry >= 0 ? ids[b * k + lane] : 0x7fffffff;
   const float w = entry >= 0 ? ws.entry_weight[entry] : 0.f;
@@ -318,50 +327,55 @@ __global__ void __launch_bounds__(256) moe_combine_kernel(const int32_t* __restr
     n += vj;
     rank += vj && (ej < eid);  // entries of a token name distinct experts
   }
-  for (int g0 = 0; g0 < H; g0 += kBlocks * 256) {
-    float acc[kBlocks][8];
+  float acc[8];
 #pragma unroll
-    for (int cb = 0; cb < kBlocks; ++cb)
+  for (int t = 0; t < 8; ++t) acc[t] = 0.f;
+  for (int i0 = 0; i0 < n; i0 += kBatch) {
+    uint4 v[kBatch];
+    float wi[kBatch];
 #pragma unroll
-      for (int t = 0; t < 8; ++t) acc[cb][t] = 0.f;
-    for (int i = 0; i < n; ++i) {
+    for (int u = 0; u < kBatch; ++u) {
+      const int i = i0 + u;
+      v[u] = make_uint4(0, 0, 0, 0);
+      wi[u] = 0.f;
+      if (i >= n) continue;
       const unsigned who = __ballot_sync(0xffffffffu, entry >= 0 && rank == i);
       const int src = __ffs(who) - 1;
       const int ent = __shfl_sync(0xffffffffu, entry, src);
-      const float wi = __shfl_sync(0xffffffffu, w, src);
-      const uint16_t* yrow = ws.y + static_cast<int64_t>(ent) * H + g0 + lane * 8;
-      uint4 v[kBlocks];
-#pragma unroll
-      for (int cb = 0; cb < kBlocks; ++cb)
-        v[cb] = g0 + cb * 256 < H ? ld_nc_v4(yrow + cb * 256) : make_uint4(0, 0, 0, 0);
-#pragma unroll
-      for (int cb = 0; cb < kBlocks; ++cb) {
-        const uint32_t p[4] = {v[cb].x, v[cb].y, v[cb].z, v[cb].w};
-#pragma unroll
-        for (int t = 0; t < 8; ++t) {
-          const float y = bf16_to_f32(static_cast<uint16_t>(p[t >> 1] >> (16 * (t & 1))));
-          acc[cb][t] = __fadd_rn(acc[cb][t], __fmul_rn(y, wi));
-        }
-      }
-    }
-#pragma unroll
-    for (int cb = 0; cb < kBlocks; ++cb) {
-      const int c0 = g0 + cb * 256 + lane * 8;
-      if (c0 >= H) break;
-      const int64_t o = static_cast<int64_t>(b) * H + c0;
-      if (out_bf16) {
-        uint32_t q[4];
-#pragma unroll
-        for (int t = 0; t < 4; ++t)
-          q[t] = static_cast<uint32_t>(bf16_bits_rne(acc[cb][2 * t])) |
-                 (static_cast<uint32_t>(bf16_bits_rne(acc[cb][2 * t + 1])) << 16);
-        *reinterpret_cast<uint4*>(static_cast<uint16_t*>(out) + o) = make_uint4(q[0], q[1], q[2], q[3]);
+      wi[u] = __shfl_sync(0xffffffffu, w, src);
+      if (yr) {
+        const float* f = yr + (static_cast<int64_t>(b) * k + src) * H + c0;
+        const float4 f0 = *reinterpret_cast<const float4*>(f), f1 = *reinterpret_cast<const float4*>(f + 4);
+        v[u] = make_uint4(bf16_bits_rne(f0.x) | (static_cast<uint32_t>(bf16_bits_rne(f0.y)) << 16),
+                          bf16_bits_rne(f0.z) | (static_cast<uint32_t>(bf16_bits_rne(f0.w)) << 16),
+                          bf16_bits_rne(f1.x) | (static_cast<uint32_t>(bf16_bits_rne(f1.y)) << 16),
+                          bf16_bits_rne(f1.z) | (static_cast<uint32_t>(bf16_bits_rne(f1.w)) << 16));
       } else {
-        float4* f = reinterpret_cast<float4*>(static_cast<float*>(out) + o);
-        f[0] = make_float4(acc[cb][0], acc[cb][1], acc[cb][2], acc[cb][3]);
-        f[1] = make_float4(acc[cb][4], acc[cb][5], acc[cb][6], acc[cb][7]);
+        v[u] = ld_nc_v4(ws.y + static_cast<int64_t>(ent) * H + c0);
       }
     }
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) {
+      if (i0 + u >= n) break;
+      const uint32_t p[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+#pragma unroll
+      for (int t = 0; t < 8; ++t) {
+        const float y = bf16_to_f32(static_cast<uint16_t>(p[t >> 1] >> (16 * (t & 1))));
+        acc[t] = __fadd_rn(acc[t], __fmul_rn(y, wi[u]));
+      }
+    }
+  }
+  const int64_t o = static_cast<int64_t>(b) * H + c0;
+  if (out_bf16) {
+    uint32_t q[4];
+#pragma unroll
+    for (int t = 0; t < 4; ++t)
+      q[t] = static_cast<uint32_t>(bf16_bits_rne(acc[2 * t])) | (static_cast<uint32_t>(bf16_bits_rne(acc[2 * t + 1])) << 16);
+    *reinterpret_cast<uint4*>(static_cast<uint16_t*>(out) + o) = make_uint4(q[0], q[1], q[2], q[3]);
+  } else {
+    float4* f = reinterpret_cast<float4*>(static_cast<float*>(out) + o);
+    f[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    f[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
   }
 }
 
@@ -385,11 +399,16 @@ size_t qk_moe_workspace_bytes(const qk_moe_desc* desc, int max_tokens) {
   return layout(*desc, max_tokens, nullptr, nullptr);
 }
 
+// phase kFull: all five launches; kPartial: route .. down with the FP32 down projection of
+// every route written to `yr` [B * top_k, hidden] (no combine); kCombine: only the combine,
+// from `yr` and the routing metadata a kPartial call left in the same workspace.
+enum { kFull = 0, kPartial = 1, kCombine = 2 };
+
 static int moe_forward_impl(const qk_moe_desc* desc, const uint8_t* gate, const uint8_t* up,
                             const uint8_t* down, const uint16_t* x, const int32_t* ids,
                             const uint16_t* weights, int B, int out_dtype, void* out,
                             void* workspace, size_t workspace_bytes, qk_stream_t stream,
-                            void* const* events) {
+                            void* const* events, float* yr = nullptr, int phase = kFull) {
   QK_REQUIRE(desc, "null descriptor");
   const qk_moe_desc& d = *desc;
   if (!supported(d.gate_type) || d.gate_type != d.up_type || d.gate_type != d.down_type)
@@ -401,7 +420,12 @@ static int moe_forward_impl(const qk_moe_desc* desc, const uint8_t* gate, const 
   QK_REQUIRE(B >= 0, "batch must be non-negative");
   QK_REQUIRE(out_dtype == QK_OUT_F32 || out_dtype == QK_OUT_BF16, "out_dtype must be F32 or BF16");
   if (B == 0) return QK_OK;
-  QK_REQUIRE(gate && up && down && x && ids && weights && out, "null pointer");
+  if (phase == kCombine)
+    QK_REQUIRE(ids && yr && out, "null pointer");
+  else
+    QK_REQUIRE(gate && up && down && x && ids && weights && (phase == kPartial ? yr != nullptr : out != nullptr),
+               "null pointer");
+  if (yr) QK_REQUIRE((reinterpret_cast<uintptr_t>(yr) & 15) == 0, "y_routes must be 16-byte aligned");
   const size_t need = layout(d, B, nullptr, nullptr);
   if (!workspace || workspace_bytes < need)
     return set_error(QK_ERR_WORKSPACE, "workspace needs %zu bytes, got %zu", need, workspace_bytes);
@@ -412,6 +436,14 @@ static int moe_forward_impl(const qk_moe_desc* desc, const uint8_t* gate, const 
     if (events && events[i]) cudaEventRecord(static_cast<cudaEvent_t>(events[i]), st);
   };
 
+  if (phase == kCombine) {
+    const cudaError_t e = launch_dependent(moe_combine_kernel, dim3((B * (d.hidden / 256) + 7) / 8), dim3(256), 0, st, ids, B, d.top_k,
+                                           d.hidden, static_cast<int>(out_dtype == QK_OUT_BF16), out,
+                                           static_cast<const float*>(yr), ws);
+    if (e != cudaSuccess) return cuda_error(e, "moe_combine_kernel");
+    count_launch(1);
+    return QK_OK;
+  }
   mark(0);
   const size_t route_smem = (3 * static_cast<size_t>(d.num_experts) + 1) * 4;
   int rc = allow_smem(reinterpret_cast<const void*>(moe_route_kernel), route_smem);
@@ -461,6 +493,8 @@ static int moe_forward_impl(const qk_moe_desc* desc, const uint8_t* gate, const 
   dn.xt = ws.ht;
   dn.ht = nullptr;
   dn.y = ws.y;
+  dn.yr = phase == kPartial ? yr : nullptr;
+  dn.entry_route = ws.entry_route;
   dn.nrows = d.hidden;
   mark(1);
   rc = q6 ? launch_umma<QType::Q6_K, kModeGateUp>(gu, sms, st) : launch_umma<QType::Q4_K, kModeGateUp>(gu, sms, st);
@@ -469,9 +503,11 @@ static int moe_forward_impl(const qk_moe_desc* desc, const uint8_t* gate, const 
   rc = q6 ? launch_umma<QType::Q6_K, kModeDown>(dn, sms, st) : launch_umma<QType::Q4_K, kModeDown>(dn, sms, st);
   if (rc) return rc;
   mark(3);
+  if (phase == kPartial) return QK_OK;
   {
-    const cudaError_t e = launch_dependent(moe_combine_kernel, dim3((B + 7) / 8), dim3(256), 0, st, ids, B, d.top_k,
-                                           d.hidden, static_cast<int>(out_dtype == QK_OUT_BF16), out, ws);
+    const cudaError_t e = launch_dependent(moe_combine_kernel, dim3((B * (d.hidden / 256) + 7) / 8), dim3(256), 0, st, ids, B, d.top_k,
+                                           d.hidden, static_cast<int>(out_dtype == QK_OUT_BF16), out,
+                                           static_cast<const float*>(nullptr), ws);
     if (e != cudaSuccess) return cuda_error(e, "moe_combine_kernel");
     count_launch(1);
   }
@@ -494,6 +530,21 @@ int qk_moe_forward_profiled(const qk_moe_desc* desc, const uint8_t* gate, const 
                             void* const* events) {
   return moe_forward_impl(desc, gate, up, down, x, ids, weights, B, out_dtype, out, workspace,
                           workspace_bytes, stream, events);
+}
+
+int qk_moe_forward_tp_partial(const qk_moe_desc* desc, const uint8_t* gate, const uint8_t* up,
+                              const uint8_t* down, const uint16_t* x, const int32_t* ids,
+                              const uint16_t* weights, int B, float* y_routes, void* workspace,
+                              size_t workspace_bytes, qk_stream_t stream) {
+  return moe_forward_impl(desc, gate, up, down, x, ids, weights, B, QK_OUT_F32, nullptr, workspace,
+                          workspace_bytes, stream, nullptr, y_routes, kPartial);
+}
+
+int qk_moe_forward_tp_combine(const qk_moe_desc* desc, const float* y_routes, const int32_t* ids, int B,
+                              int out_dtype, void* out, void* workspace, size_t workspace_bytes,
+                              qk_stream_t stream) {
+  return moe_forward_impl(desc, nullptr, nullptr, nullptr, nullptr, ids, nullptr, B, out_dtype, out, workspace,
+                          workspace_bytes, stream, nullptr, const_cast<float*>(y_routes), kCombine);
 }
 
 int qk_cast_f32_bf16(const float* in, uint16_t* out, int64_t n, qk_stream_t stream) {

@@ -4,57 +4,103 @@
 //   probs = numerics.softmax(linear(f32(x), f32(Wr)))      (HIGHEST: FP32 dot)
 //   w, ids = lax.top_k(probs, k); w = numerics.divide(w, sum(w))
 //   w = compute_cast(where(active, w, 0), bf16)
-// One CTA handles up to 8 tokens: its 8 warps compute the logits of all experts for the
-// CTA's tokens (each router row is read once per CTA; fixed-order reductions), then warp t
-// runs softmax and the k selection rounds for token t. Divisions are IEEE; exp is expf.
+// A thread-block cluster of kCluster CTAs handles up to 8 tokens. Each CTA stages the
+// tokens' x rows in shared memory and computes the logits of its slice of the experts (one
+// warp per expert row, fixed-order reductions; each router row is read once per cluster),
+// storing them into the first CTA's shared memory (distributed shared memory). After the
+// cluster barrier the first CTA's warp t runs softmax and the k selection rounds for token
+// t. Divisions are IEEE; exp is expf.
+#include <cooperative_groups.h>
+
 #include "common.cuh"
+
+namespace cg = cooperative_groups;
 
 namespace qk {
 namespace {
 
 constexpr int kTok = 8;
+constexpr int kCluster = 8;
 
-__global__ void __launch_bounds__(256) router_kernel(const uint16_t* __restrict__ x,
-                                                     const float* __restrict__ w,
-                                                     const float* __restrict__ logits_in,
-                                                     const uint8_t* __restrict__ active, int T,
-                                                     int H, int E, int k, int32_t* __restrict__ ids,
-                                                     uint16_t* __restrict__ weights,
-                                                     float* __restrict__ probs_out) {
-  extern __shared__ float lg[];  // [kTok][E]
+__global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(256)
+    router_kernel(const uint16_t* __restrict__ x, const float* __restrict__ w, const float* __restrict__ logits_in,
+                  const uint8_t* __restrict__ active, int T, int H, int E, int k, int32_t* __restrict__ ids,
+                  uint16_t* __restrict__ weights, float* __restrict__ probs_out) {
+  extern __shared__ __align__(16) float lg[];  // [kTok][E], then x rows [kTok][H] (BF16)
+  uint16_t* xs = reinterpret_cast<uint16_t*>(lg + kTok * E);
+  cg::cluster_group cluster = cg::this_cluster();
+  const unsigned crank = cluster.block_rank();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int t0 = blockIdx.x * kTok;
+  const int t0 = (blockIdx.x / kCluster) * kTok;
   const int nt = min(kTok, T - t0);
 
   if (logits_in) {
-    for (int i = threadIdx.x; i < nt * E; i += blockDim.x)
-      lg[i] = logits_in[static_cast<int64_t>(t0) * E + i];
+    if (crank == 0)
+      for (int i = threadIdx.x; i < nt * E; i += blockDim.x) lg[i] = logits_in[static_cast<int64_t>(t0) * E + i];
   } else {
-    for (int e = warp; e < E; e += 8) {
-      float acc[kTok];
+    const int pieces = nt * H / 8;  // 16-byte pieces of the token rows
+    for (int i = threadIdx.x; i < pieces; i += blockDim.x)
+      reinterpret_cast<uint4*>(xs)[i] = reinterpret_cast<const uint4*>(x + static_cast<int64_t>(t0) * H)[i];
+    __syncthreads();
+    float* lg0 = cluster.map_shared_rank(lg, 0);
+    const int per = (E + kCluster - 1) / kCluster, e0 = static_cast<int>(crank) * per;
+    const int e1 = min(E, e0 + per);
+    // Each warp takes two router rows at a time and keeps kU 16-byte loads per row in flight
+    // (the loads are issued before the FMAs that use them); every lane still adds its
+    // columns h = 4 lane + 128 i in increasing i, so the logits do not depend on kU.
+    constexpr int kU = 4;
+    for (int ea = e0 + warp; ea < e1; ea += 16) {
+      const int eb = ea + 8;
+      const bool has_b = eb < e1;
+      float acc[2][kTok];
 #pragma unroll
-      for (int t = 0; t < kTok; ++t) acc[t] = 0.f;
-      const float* wr = w + static_cast<int64_t>(e) * H;
-      for (int h = lane * 4; h < H; h += 128) {
-        const float4 wv = *reinterpret_cast<const float4*>(wr + h);
+      for (int t = 0; t < kTok; ++t) acc[0][t] = acc[1][t] = 0.f;
+      const float* wa = w + static_cast<int64_t>(ea) * H;
+      const float* wb = w + static_cast<int64_t>(has_b ? eb : ea) * H;
+      for (int h0 = lane * 4; h0 < H; h0 += 128 * kU) {
+        float4 va[kU], vb[kU];
 #pragma unroll
-        for (int t = 0; t < kTok; ++t) {
-          if (t >= nt) break;
-          const uint2 xv = *reinterpret_cast<const uint2*>(x + static_cast<int64_t>(t0 + t) * H + h);
-          acc[t] = fmaf(wv.x, bf16_to_f32(static_cast<uint16_t>(xv.x & 0xffffu)), acc[t]);
-          acc[t] = fmaf(wv.y, bf16_to_f32(static_cast<uint16_t>(xv.x >> 16)), acc[t]);
-          acc[t] = fmaf(wv.z, bf16_to_f32(static_cast<uint16_t>(xv.y & 0xffffu)), acc[t]);
-          acc[t] = fmaf(wv.w, bf16_to_f32(static_cast<uint16_t>(xv.y >> 16)), acc[t]);
+        for (int u = 0; u < kU; ++u) {
+          const int h = h0 + 128 * u;
+          va[u] = h < H ? *reinterpret_cast<const float4*>(wa + h) : make_float4(0.f, 0.f, 0.f, 0.f);
+          vb[u] = h < H && has_b ? *reinterpret_cast<const float4*>(wb + h) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+          const int h = h0 + 128 * u;
+          if (h >= H) break;
+#pragma unroll
+          for (int t = 0; t < kTok; ++t) {
+            if (t >= nt) break;
+            const uint2 xv = *reinterpret_cast<const uint2*>(xs + t * H + h);
+            const float x0 = bf16_to_f32(static_cast<uint16_t>(xv.x & 0xffffu));
+            const float x1 = bf16_to_f32(static_cast<uint16_t>(xv.x >> 16));
+            const float x2 = bf16_to_f32(static_cast<uint16_t>(xv.y & 0xffffu));
+            const float x3 = bf16_to_f32(static_cast<uint16_t>(xv.y >> 16));
+            acc[0][t] = fmaf(va[u].x, x0, acc[0][t]);
+            acc[0][t] = fmaf(va[u].y, x1, acc[0][t]);
+            acc[0][t] = fmaf(va[u].z, x2, acc[0][t]);
+            acc[0][t] = fmaf(va[u].w, x3, acc[0][t]);
+            acc[1][t] = fmaf(vb[u].x, x0, acc[1][t]);
+            acc[1][t] = fmaf(vb[u].y, x1, acc[1][t]);
+            acc[1][t] = fmaf(vb[u].z, x2, acc[1][t]);
+            acc[1][t] = fmaf(vb[u].w, x3, acc[1][t]);
+          }
         }
       }
 #pragma unroll
-      for (int t = 0; t < kTok; ++t) {
-        float v = acc[t];
-        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-        if (lane == 0 && t < nt) lg[t * E + e] = v;
+      for (int r = 0; r < 2; ++r) {
+#pragma unroll
+        for (int t = 0; t < kTok; ++t) {
+          float v = acc[r][t];
+          for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+          if (lane == 0 && t < nt && (r == 0 || has_b)) lg0[t * E + (r == 0 ? ea : eb)] = v;
+        }
       }
     }
   }
+  cluster.sync();  // every CTA's logits are in the first CTA's shared memory
+  if (crank != 0) return;
   __syncthreads();
   if (warp >= nt) return;
   const int t = t0 + warp;
@@ -127,11 +173,14 @@ static int router_launch(const uint16_t* x, const float* w, const float* logits,
   QK_REQUIRE(T >= 0 && E > 0 && k > 0 && k <= E && k <= 32, "Invalid expert top-k");
   if (T == 0) return QK_OK;
   QK_REQUIRE(ids && weights, "null pointer");
-  const size_t smem = static_cast<size_t>(kTok) * E * 4;
-  QK_REQUIRE(smem <= 200 * 1024, "too many experts for the router kernel (E <= 6400)");
+  const size_t smem = static_cast<size_t>(kTok) * E * 4 + (x ? static_cast<size_t>(kTok) * H * 2 : 0);
+  QK_REQUIRE(smem <= 200 * 1024, "too many experts or too wide a hidden size for the router kernel "
+             "(8 * (4 E + 2 H) bytes must stay within 200 KB)");
   int rc = allow_smem(reinterpret_cast<const void*>(router_kernel), smem);
   if (rc) return rc;
-  router_kernel<<<(T + kTok - 1) / kTok, 256, smem, as_stream(stream)>>>(x, w, logits, active, T, H, E, k, ids, weights, probs);
+  const int blocks = (T + kTok - 1) / kTok;
+  router_kernel<<<blocks * kCluster, 256, smem, as_stream(stream)>>>(x, w, logits, active, T, H, E, k, ids, weights,
+                                                                     probs);
   QK_LAUNCHED("router_kernel");
   return QK_OK;
 }
@@ -140,10 +189,10 @@ extern "C" {
 
 int qk_router_topk(const uint16_t* x, const float* router_w, const uint8_t* active, int T, int H,
                    int E, int k, int32_t* ids, uint16_t* weights, float* probs, qk_stream_t stream) {
-  QK_REQUIRE(H > 0 && H % 4 == 0, "hidden must be a positive multiple of 4");
+  QK_REQUIRE(H > 0 && H % 8 == 0, "hidden must be a positive multiple of 8");
   QK_REQUIRE(T == 0 || (x && router_w), "null pointer");
-  QK_REQUIRE((reinterpret_cast<uintptr_t>(x) & 7) == 0 && (reinterpret_cast<uintptr_t>(router_w) & 15) == 0,
-             "x must be 8-byte and router_w 16-byte aligned");
+  QK_REQUIRE((reinterpret_cast<uintptr_t>(x) & 15) == 0 && (reinterpret_cast<uintptr_t>(router_w) & 15) == 0,
+             "x and router_w must be 16-byte aligned");
   return router_launch(x, router_w, nullptr, active, T, H, E, k, ids, weights, probs, stream);
 }
 

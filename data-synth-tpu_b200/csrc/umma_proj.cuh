@@ -101,6 +101,8 @@ struct UArgs {
   uint8_t* ht;       // gate/up: activation tiles of the down pass
   int nkb_out;       // gate/up: K blocks of the down pass
   uint16_t* y;       // down: y [entries, nrows]
+  float* yr;         // down, tensor parallel: FP32 y of each entry's route [B * top_k, nrows]
+  const int32_t* entry_route;  // down: route b * top_k + j of each entry
   float* out;        // dense: out [M, nrows], or with ksplit the block partials [nkb, M, nrows]
   int nrows;         // output rows of the matrix (I, H or N)
   int ksplit;        // dense: one work item per K block (partial sums, reduced in K order)
@@ -385,8 +387,12 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) umma_proj_kernel(const UArgs 
           for (int col = 0; col < kMaxTok; ++col) {
             if (col >= c.ntok) break;
             const int64_t orow = c.entry0 + col;
-            if (MODE == kModeDown) A.y[orow * A.nrows + R] = bf16_bits_rne(acc[col]);
-            else obase[orow * A.nrows + R] = acc[col];
+            if (MODE == kModeDown) {
+              if (A.yr) A.yr[static_cast<int64_t>(A.entry_route[orow]) * A.nrows + R] = acc[col];
+              else A.y[orow * A.nrows + R] = bf16_bits_rne(acc[col]);
+            } else {
+              obase[orow * A.nrows + R] = acc[col];
+            }
           }
         }
       }

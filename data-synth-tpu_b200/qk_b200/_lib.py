@@ -69,6 +69,11 @@ SIGNATURES = {
         _i,
         [ctypes.POINTER(MoeDesc), _p, _p, _p, _p, _p, _p, _i, _i, _p, _p, _sz, _p, _p],
     ),
+    "qk_moe_forward_tp_partial": (
+        _i,
+        [ctypes.POINTER(MoeDesc), _p, _p, _p, _p, _p, _p, _i, _p, _p, _sz, _p],
+    ),
+    "qk_moe_forward_tp_combine": (_i, [ctypes.POINTER(MoeDesc), _p, _p, _i, _i, _p, _p, _sz, _p]),
     "qk_cast_f32_bf16": (_i, [_p, _p, _i64, _p]),
     "qk_moe_check": (_i, [_p, _p]),
     "qk_kv_q8_quantize": (_i, [_p, _i, _i64, _i, _i, _p, _p, _p]),
@@ -80,6 +85,18 @@ SIGNATURES = {
         _i,
         [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _i, _p, _p, _sz, _p],
     ),
+    "qk_kv_q8_decode_attention_partial": (
+        _i,
+        [_p, _p, _p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _i, _p, _p, _sz, _p],
+    ),
+    "qk_kv_q8_attention_combine": (_i, [_p, _i, _i, _i, _i, _p, _p, _p]),
+    "qk_rms_norm": (_i, [_p, _p, _i, _i, ctypes.c_float, _p, _p]),
+    "qk_qk_norm_rope": (
+        _i,
+        [_p, _p, _p, _p, _p, _i, _i, _i, _i, _i, ctypes.c_float, _p, _p, _p, _p, _p],
+    ),
+    "qk_residual_add": (_i, [_p, _p, _i64, _p, _p]),
+    "qk_append_shared_route": (_i, [_p, _p, _i, _i, _p, _p, _i, _i, _p, _p, _p]),
     "qk_ep_plan": (_i, [_p, _p, _i, _i, _i, _i, _p, _p, _p, _p, _p, _p]),
     "qk_gather_rows": (_i, [_p, _p, _i64, _i64, _p, _p]),
     "qk_ep_combine": (_i, [_p, _p, _p, _p, _i, _i, _i, _i, _p, _p]),

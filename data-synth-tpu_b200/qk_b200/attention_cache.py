@@ -159,3 +159,151 @@ class DecodeAttention:
 
 
 decode_attention = DecodeAttention()
+
+
+# ---- time-sharded cache (the reference's layout over ranks) ---------------------------
+#
+# The reference shards the cache's time axis over the "expert" mesh axis
+# (engine.py:350-369: codes P(None, "expert", None), scale planes P(None, "expert")), so
+# rank r holds cache times [r * T / world, (r + 1) * T / world). The dense decode step
+# (attention_cache.py:146-149: indices = arange(T), mask = indices <= lengths) then
+# reduces its softmax over the shards. Here each rank runs the split-KV kernel over its own
+# times and writes an unnormalised partial (output, max, sum); the ranks all-gather the
+# partials (rank order is time order) and a log-sum-exp combine finishes the output.
+
+
+def time_shard(max_context, rank, world):
+    """``(first time, times)`` of ``rank``'s slice of a ``max_context`` cache."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError("rank must lie in [0, world)")
+    if max_context % world:
+        raise ValueError("Cache time axis must divide evenly over the ranks")
+    size = max_context // world
+    return rank * size, size
+
+
+def local_lengths(lengths, first):
+    """Per-row last valid local slot: global slot ``t`` is valid iff ``t <= lengths[b]``
+    (``attention_cache.py:148``), so local slot ``s`` is valid iff ``s <= lengths[b] - first``
+    (negative: no valid slot in this shard)."""
+    return lengths.to(torch.int32) - int(first)
+
+
+def local_write_target(lengths, active, first, size, max_context):
+    """Local time and active flag of the cache write of ``attention_cache.py:138-140``
+    (``lengths`` clipped to ``[0, max_context - 1]``): only the rank whose slice holds the
+    time writes it."""
+    t = lengths.to(torch.int64).clamp(0, max_context - 1) - int(first)
+    mine = (t >= 0) & (t < size)
+    if active is not None:
+        mine = mine & active.to(device=mine.device, dtype=torch.bool)
+    return torch.where(mine, t, torch.zeros_like(t)).to(torch.int32), mine
+
+
+def partial_set_floats(batch, hq, hd):
+    """FP32 values of one partial set: ``batch * hq * hd`` outputs, then ``batch * hq``
+    (max, sum) pairs."""
+    return batch * hq * (hd + 2)
+
+
+def split_partial(partial, batch, hq, hd):
+    """Views ``(o [B, hq, hd], stats [B, hq, 2])`` of one flat partial set."""
+    n = batch * hq * hd
+    return partial[:n].view(batch, hq, hd), partial[n:].view(batch, hq, 2)
+
+
+def decode_attention_partial(q, cache, indices, c, *, lengths=None, valid=None, workspace=None):
+    """Split-KV decode attention over ``cache`` that stops before normalising: one flat FP32
+    partial set (``split_partial`` gives its unnormalised output and (max, sum) views)."""
+    if q.dtype != torch.bfloat16 or q.dim() != 3:
+        raise TypeError("q must be BF16 [B, query_heads, head_dim]")
+    batch, hq, hd = q.shape
+    if hq != c.query_heads or hd != c.head_dim:
+        raise ValueError("q must be [B, query_heads, head_dim] of the cache config")
+    if (lengths is None) == (valid is None):
+        raise ValueError("pass exactly one of lengths or valid")
+    device = q.device
+    selected = indices.shape[1]
+    idx = indices.to(device=device, dtype=torch.int32).contiguous()
+    lens = None if lengths is None else lengths.to(device=device, dtype=torch.int32).contiguous()
+    val = None if valid is None else valid.to(device=device, dtype=torch.uint8).contiguous()
+    need = int(_lib.load().qk_kv_q8_attention_workspace_bytes(batch, selected, hq, c.kv_heads, hd))
+    ws = workspace
+    if need and (ws is None or ws.numel() < need):
+        ws = torch.empty(need, dtype=torch.uint8, device=device)
+    partial = torch.empty(partial_set_floats(batch, hq, hd), dtype=torch.float32, device=device)
+    with torch.cuda.device(device):
+        _lib.call("qk_kv_q8_decode_attention_partial", _lib.ptr(q.contiguous()), _lib.ptr(cache["k"]),
+                  _lib.ptr(cache["v"]), _lib.ptr(cache["k_scale"]), _lib.ptr(cache["v_scale"]),
+                  _lib.ptr(idx), _lib.ptr(val), _lib.ptr(lens), batch, selected, cache["k"].shape[1],
+                  hq, c.kv_heads, hd, _lib.ptr(partial), _lib.ptr(ws) if need else None, need,
+                  _lib.stream_handle(device))
+    return partial
+
+
+def combine_partials(parts, batch, hq, hd, gate=None):
+    """Log-sum-exp merge of the ``R`` consecutive partial sets in ``parts`` (flat FP32, set
+    order = time order), then the output gate (``attention_cache.py:169-170``):
+    BF16 ``[B, hq, hd]``."""
+    per = partial_set_floats(batch, hq, hd)
+    if parts.dim() != 1 or parts.dtype != torch.float32 or parts.numel() % per:
+        raise ValueError("parts must be a flat FP32 tensor of whole partial sets")
+    device = parts.device
+    g = None if gate is None else gate.to(torch.bfloat16).contiguous()
+    out = torch.empty((batch, hq, hd), dtype=torch.bfloat16, device=device)
+    with torch.cuda.device(device):
+        _lib.call("qk_kv_q8_attention_combine", _lib.ptr(parts.contiguous()), parts.numel() // per,
+                  batch, hq, hd, _lib.ptr(g), _lib.ptr(out), _lib.stream_handle(device))
+    return out
+
+
+def gather_partials(partial, group, world):
+    """All ranks' partial sets, concatenated in rank order (one all-gather)."""
+    if world == 1:
+        return partial
+    import torch.distributed as dist
+
+    parts = torch.empty(world * partial.numel(), dtype=partial.dtype, device=partial.device)
+    dist.all_gather_into_tensor(parts, partial, group=group)
+    return parts
+
+
+class TimeShardedAttention:
+    """Decode step over a cache whose time axis is split over the ranks of ``group``.
+
+    ``cache`` is this rank's slice (``empty_cache`` with ``max_context / world`` times);
+    ``c.max_context`` is the whole context. ``write`` stores this step's key/value on the
+    rank that owns time ``lengths[b]``; ``__call__`` attends over every rank's slots
+    ``<= lengths[b]`` and returns the same BF16 ``[B, hq, hd]`` on every rank.
+    """
+
+    def __init__(self, group=None):
+        import torch.distributed as dist
+
+        self.group = group
+        self.world = dist.get_world_size(group) if group is not None else 1
+        self.rank = dist.get_rank(group) if group is not None else 0
+        self._ws = None
+
+    def shard(self, c):
+        return time_shard(c.max_context, self.rank, self.world)
+
+    def write(self, cache, key, value, lengths, active, c):
+        first, size = self.shard(c)
+        t, mine = local_write_target(lengths.to(key.device), active, first, size, c.max_context)
+        return write_quantized(cache, key, value, t, mine, c)
+
+    def __call__(self, q, cache, lengths, c, *, gate=None):
+        first, size = self.shard(c)
+        if cache["k"].shape[1] != size:
+            raise ValueError("cache must hold this rank's max_context / world times")
+        batch, hq, hd = q.shape
+        indices = torch.arange(size, dtype=torch.int32, device=q.device).expand(batch, size)
+        lens = lengths.to(q.device).clamp(0, c.max_context - 1)
+        need = int(_lib.load().qk_kv_q8_attention_workspace_bytes(batch, size, hq, c.kv_heads, hd))
+        if need and (self._ws is None or self._ws.numel() < need):
+            self._ws = torch.empty(need, dtype=torch.uint8, device=q.device)
+        partial = decode_attention_partial(q, cache, indices, c, lengths=local_lengths(lens, first),
+                                           workspace=self._ws)
+        parts = gather_partials(partial, self.group, self.world)
+        return combine_partials(parts, batch, hq, hd, gate)

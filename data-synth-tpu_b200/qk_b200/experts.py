@@ -23,11 +23,12 @@ EXPERT_ROW_TILE = 128
 
 
 class ExpertFFN:
-    def __init__(self, group, gate_type, up_type, down_type, hidden, intermediate):
+    def __init__(self, group, gate_type, up_type, down_type, hidden, intermediate, tensor_parallel=1):
         self.group = group
         self.types = tuple(normalize_qtype(t) for t in (gate_type, up_type, down_type))
         self.hidden = hidden
         self.intermediate = intermediate
+        self.tensor_parallel = tensor_parallel
         self._workspace = {}
 
     def _rank_world(self):
@@ -40,7 +41,7 @@ class ExpertFFN:
     def desc(self, num_experts, first_expert, top_k):
         return _lib.MoeDesc(
             GGML_TYPE[self.types[0]], GGML_TYPE[self.types[1]], GGML_TYPE[self.types[2]],
-            self.hidden, self.intermediate, num_experts, first_expert, top_k,
+            self.hidden, self.intermediate // self.tensor_parallel, num_experts, first_expert, top_k,
         )
 
     def workspace(self, desc, batch, device):
@@ -88,8 +89,45 @@ class ExpertFFN:
         self.last_workspace = ws
         return out
 
+    def tensor_partial(self, gate, up, down, x, ids, weights):
+        """Tensor parallel, first half: this rank's slice of every expert; returns the FP32
+        down projection of every route ``[B * k, hidden]`` (before the tensor all-reduce)
+        and the workspace the combine reads."""
+        self._check(gate, up, down, x, ids, weights)
+        batch, top_k = ids.shape
+        desc = self.desc(gate.shape[0], 0, top_k)
+        device = x.device
+        ws = self.workspace(desc, batch, device)
+        x = x.contiguous()
+        ids = ids.to(torch.int32).contiguous()
+        weights = weights.to(torch.bfloat16).contiguous()
+        y_routes = torch.empty((batch * top_k, self.hidden), dtype=torch.float32, device=device)
+        with torch.cuda.device(device):
+            _lib.call("qk_moe_forward_tp_partial", desc, _lib.ptr(gate), _lib.ptr(up), _lib.ptr(down),
+                      _lib.ptr(x), _lib.ptr(ids), _lib.ptr(weights), batch, _lib.ptr(y_routes), _lib.ptr(ws),
+                      ws.numel(), _lib.stream_handle(device))
+        self.last_workspace = ws
+        return y_routes, ids, ws
+
+    def tensor_combine(self, y_routes, ids, ws, num_experts):
+        """Tensor parallel, second half: BF16 of each route's summed down projection,
+        route-weighted and added in ascending expert order."""
+        batch, top_k = ids.shape
+        desc = self.desc(num_experts, 0, top_k)
+        out = torch.empty((batch, self.hidden), dtype=torch.bfloat16, device=ids.device)
+        with torch.cuda.device(ids.device):
+            _lib.call("qk_moe_forward_tp_combine", desc, _lib.ptr(y_routes), _lib.ptr(ids), batch,
+                      _lib.QK_OUT_BF16, _lib.ptr(out), _lib.ptr(ws), ws.numel(), _lib.stream_handle(ids.device))
+        return out
+
     def __call__(self, gate, up, down, x, ids, weights):
         rank, world = self._rank_world()
+        if self.tensor_parallel > 1:
+            import torch.distributed as dist
+
+            y_routes, ids32, ws = self.tensor_partial(gate, up, down, x, ids, weights)
+            dist.all_reduce(y_routes, group=self.group)  # grouped_experts.py:113-118
+            return self.tensor_combine(y_routes, ids32, ws, gate.shape[0])
         if world == 1:
             return self._run(gate, up, down, x, ids, weights, None, torch.bfloat16)
         import torch.distributed as dist
@@ -138,14 +176,25 @@ def expert_parallel(
         raise ValueError("Expert group size must be a positive integer")
     if type(tensor_parallel) is not int or tensor_parallel < 1:
         raise ValueError("Tensor parallel size must divide the device count")
-    if tensor_parallel != 1:
-        raise NotImplementedError("tensor-parallel experts are not built in this library")
+    if tensor_parallel > 1:
+        # every rank of `group` holds every expert's 1/tp slice of the intermediate channels
+        # (put_expert_bytes(..., tensor_rank=r, tensor_parallel=tp)); a mesh that also splits
+        # the experts over ranks is not built here
+        if group is None:
+            raise ValueError("tensor parallel experts need a process group")
+        import torch.distributed as dist
+
+        if dist.get_world_size(group) != tensor_parallel:
+            raise NotImplementedError("tensor_parallel must equal the process group's size "
+                                      "(expert x tensor meshes are not built)")
+        if (intermediate // tensor_parallel) % 256 or intermediate % tensor_parallel:
+            raise ValueError("Tensor slices must contain whole down quantization blocks")
     types = tuple(normalize_qtype(t) for t in (gate_type, up_type, down_type))
     if len(set(types)) != 1 or types[0] not in ("Q6_K", "Q4_K"):
         raise ValueError("expert kernels take gate/up/down all Q6_K or all Q4_K")
     if hidden % 256 or intermediate % 256:
         raise ValueError("hidden and intermediate must be multiples of 256")
-    return ExpertFFN(group, *types, hidden, intermediate)
+    return ExpertFFN(group, *types, hidden, intermediate, tensor_parallel)
 
 
 __all__ = ["ExpertFFN", "expert_parallel", "expert_shape", "EXPERT_ROW_TILE"]

@@ -46,17 +46,57 @@ def local_range(num_experts, rank, world):
     return rank * per, per
 
 
-def put_expert_bytes(raw, kind, qtype, hidden, intermediate, *, rank=0, world=1, device=None):
-    """This rank's experts as a device tensor ``uint8[E_local, tiled_bytes_per_expert]``."""
+def tensor_slice(raw, kind, qtype, hidden, intermediate, tensor_parallel, tensor_rank):
+    """Tensor rank ``tensor_rank``'s bytes of every expert in ``raw`` ``[E, bytes]`` (NumPy or
+    torch): the slice ``split_expert_bytes(...)[tensor_rank]`` - gate/up rows
+    ``[r * I/tp, (r + 1) * I/tp)``, down columns of the same range in whole blocks."""
+    if kind not in {"gate", "up", "down"}:
+        raise ValueError("Unknown expert projection")
+    block, size = BLOCK_LAYOUTS[normalize_qtype(qtype)]
+    if intermediate % tensor_parallel:
+        raise ValueError("Intermediate channels must divide tensor parallel size")
+    if not 0 <= tensor_rank < tensor_parallel:
+        raise ValueError("tensor rank must lie in [0, tensor_parallel)")
+    local = intermediate // tensor_parallel
+    count = len(raw)
+    if kind == "down":
+        if local % block:
+            raise ValueError("Tensor slices must contain whole down quantization blocks")
+        part = raw.reshape(count, hidden, tensor_parallel, local // block, size)[:, :, tensor_rank]
+    else:
+        if hidden % block:
+            raise ValueError("Hidden channels must contain whole quantization blocks")
+        part = raw.reshape(count, tensor_parallel, local, hidden // block, size)[:, tensor_rank]
+    return part.reshape(count, -1)
+
+
+def put_expert_bytes(raw, kind, qtype, hidden, intermediate, *, rank=0, world=1, device=None,
+                     tensor_rank=0, tensor_parallel=1):
+    """This rank's experts as a device tensor ``uint8[E_local, tiled_bytes_per_expert]``.
+
+    With ``tensor_parallel > 1`` every expert of the range is cut to tensor rank
+    ``tensor_rank``'s slice of the intermediate channels (``tensor_slice``), tiled as a
+    matrix of ``intermediate / tensor_parallel`` channels."""
     name = normalize_qtype(qtype)
     if name not in TILED_TYPES:
         raise ValueError(f"expert kernels take {TILED_TYPES}; got {name}")
-    rows, width = expert_shape(kind, hidden, intermediate)
     values, size = BLOCK_LAYOUTS[name]
     first, count = local_range(len(raw), rank, world)
     device = torch.device(device or "cuda")
-    per_raw = rows * ((width + values - 1) // values) * size
     part = raw[first : first + count]
+    if tensor_parallel > 1:
+        full = expert_shape(kind, hidden, intermediate)
+        per_full = full[0] * ((full[1] + values - 1) // values) * size
+        if part.reshape(count, -1).shape[1] != per_full:
+            raise ValueError(f"{kind} expert must hold {per_full} bytes; got {part.reshape(count, -1).shape[1]}")
+        part = tensor_slice(part.reshape(count, -1), kind, name, hidden, intermediate, tensor_parallel, tensor_rank)
+        if isinstance(part, np.ndarray):
+            part = np.ascontiguousarray(part)
+        else:
+            part = part.contiguous()
+        intermediate //= tensor_parallel
+    rows, width = expert_shape(kind, hidden, intermediate)
+    per_raw = rows * ((width + values - 1) // values) * size
     if isinstance(part, np.ndarray):
         if part.dtype != np.uint8:
             raise TypeError("GGUF expert bytes must have dtype uint8")

@@ -142,6 +142,22 @@ int qk_moe_forward_profiled(const qk_moe_desc* desc, const uint8_t* gate, const 
                             const uint16_t* weights, int B, int out_dtype, void* out,
                             void* workspace, size_t workspace_bytes, qk_stream_t stream,
                             void* const* events);
+/* Tensor parallel inside the experts (grouped_experts.py:113-119, tensor_parallel > 1):
+ * each tensor rank holds every expert's slice of I (desc->intermediate = I / tp, a
+ * multiple of 256: whole down blocks, parallel.py:40-61). qk_moe_forward_tp_partial runs
+ * route, dispatch, gate/up + SwiGLU and down for this slice and writes the FP32 down
+ * projection of every route to y_routes [B * top_k, hidden] (16-byte aligned; rows of
+ * merged or dropped routes are left as they were). The caller all-reduces y_routes over
+ * the tensor ranks (the reference's psum before the BF16 rounding) and then calls
+ * qk_moe_forward_tp_combine with the same workspace, which rounds each route's sum to
+ * BF16 and adds f32(y) * f32(route weight) in ascending expert order. */
+int qk_moe_forward_tp_partial(const qk_moe_desc* desc, const uint8_t* gate, const uint8_t* up,
+                              const uint8_t* down, const uint16_t* x, const int32_t* ids,
+                              const uint16_t* weights, int B, float* y_routes, void* workspace,
+                              size_t workspace_bytes, qk_stream_t stream);
+int qk_moe_forward_tp_combine(const qk_moe_desc* desc, const float* y_routes, const int32_t* ids,
+                              int B, int out_dtype, void* out, void* workspace,
+                              size_t workspace_bytes, qk_stream_t stream);
 /* BF16 (RNE) of an FP32 array: the cast after the expert-parallel all-reduce
  * (experts.py:131, psum(out).astype(x.dtype)). */
 int qk_cast_f32_bf16(const float* in, uint16_t* out, int64_t n, qk_stream_t stream);
@@ -215,6 +231,54 @@ int qk_kv_q8_decode_attention(const uint16_t* q, const int8_t* k_codes, const in
                               const int32_t* lengths, const uint16_t* gate, int B, int S, int T,
                               int hq, int kv_heads, int head_dim, uint16_t* out, void* workspace,
                               size_t workspace_bytes, qk_stream_t stream);
+
+/* Time-sharded decode attention: the cache's time axis split over ranks, as the reference
+ * shards it (engine.py:350-369, P(None, "expert", ...) on the time axis of the codes and
+ * the scale planes, with attention_cache.py:152-170 reduced over the shards by SPMD).
+ * qk_kv_q8_decode_attention_partial runs the same split-KV kernel over this rank's slots
+ * and writes, in place of the BF16 output, one partial set (16-byte aligned, FP32):
+ * B * hq * head_dim unnormalised outputs, then B * hq pairs (max score, sum of
+ * exp(score - max)); a row with no valid slot has max -inf and sum 0. Same workspace as
+ * qk_kv_q8_decode_attention. */
+int qk_kv_q8_decode_attention_partial(const uint16_t* q, const int8_t* k_codes,
+                                      const int8_t* v_codes, const uint16_t* k_scale,
+                                      const uint16_t* v_scale, const int32_t* indices,
+                                      const uint8_t* valid, const int32_t* lengths, int B, int S,
+                                      int T, int hq, int kv_heads, int head_dim, float* partial,
+                                      void* workspace, size_t workspace_bytes, qk_stream_t stream);
+/* Log-sum-exp combine of R consecutive partial sets (e.g. all-gathered from R ranks, rank
+ * order = time order), merged in set order, then the output rule of
+ * attention_cache.py:169-170: out = bf16(bf16(o) * bf16(sigmoid(gate))) when gate != NULL.
+ * out: BF16 [B, hq, head_dim]. */
+int qk_kv_q8_attention_combine(const float* parts, int R, int B, int hq, int head_dim,
+                               const uint16_t* gate, uint16_t* out, qk_stream_t stream);
+
+/* ---- decoder-layer glue around the path -----------------------------------------
+ * The per-token steps on either side of the routed FFN and the decode attention in a
+ * decoder layer, one launch each over all rows (BF16 storage bits throughout). */
+
+/* qwen38_tpu/math.py:27-31 rms(x, gamma, eps): out = bf16(x * rsqrt(mean(x^2) + eps) *
+ * gamma) per row of `width` values. */
+int qk_rms_norm(const uint16_t* x, const uint16_t* gamma, int rows, int width, float eps,
+                uint16_t* out, qk_stream_t stream);
+/* qwen38_tpu/attention_cache.py:129-135 (q/gate split, q_norm / k_norm rms, rope of
+ * math.py:231-243 with one position per row for every rotary section). qkv: the fused
+ * projection rows [B, hq * (q hd | gate hd) + kv * hd (k) + kv * hd (v)]; inv_freq: FP32
+ * [rotary_dim / 2]; positions: int32 [B]. Outputs q, gate [B, hq, hd], k, v [B, kv, hd]. */
+int qk_qk_norm_rope(const uint16_t* qkv, const uint16_t* q_norm, const uint16_t* k_norm,
+                    const float* inv_freq, const int32_t* positions, int B, int hq, int kv,
+                    int head_dim, int rotary_dim, float eps, uint16_t* q_out,
+                    uint16_t* gate_out, uint16_t* k_out, uint16_t* v_out, qk_stream_t stream);
+/* out = bf16(x + y) over n BF16 values (out may alias x): the residual add. */
+int qk_residual_add(const uint16_t* x, const uint16_t* y, int64_t n, uint16_t* out,
+                    qk_stream_t stream);
+/* The shared expert as one more route (math.py:282-283): ids_out / weights_out [B, k + 1]
+ * are the k routes of each row followed by (shared_id, bf16(sigmoid(bf16(h . shared_router)))),
+ * so one qk_moe_forward over routed + shared experts applies the shared expert's gate. */
+int qk_append_shared_route(const int32_t* ids, const uint16_t* weights, int B, int k,
+                           const uint16_t* h, const uint16_t* shared_router, int H,
+                           int shared_id, int32_t* ids_out, uint16_t* weights_out,
+                           qk_stream_t stream);
 
 /* No counterpart in the reference. QK_ERR_TIMEOUT if a bounded device wait of an earlier
  * qk_kv_q8_decode_attention on this device gave up (its output is then not valid), else

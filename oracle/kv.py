@@ -109,3 +109,42 @@ def attention(q, keys, values, mask, gate=None):
     if gate is not None:
         out = bf16_round((out * bf16_round(sigmoid(gate))).astype(np.float32))
     return out
+
+
+def attention_partial(q, keys, values, mask):
+    """One time shard of the decode attention (test infrastructure for the time-sharded
+    path; the reference reduces ``attention_cache.py:159-168`` over the shards of
+    ``engine.py:350-369`` inside SPMD). Scores as in ``attention``; then per (row, head)
+    ``m = max`` valid score, ``l = sum exp(score - m)``, ``o = sum exp(score - m) * v``.
+    Returns the flat FP32 partial set: ``o`` ``[B, hq, hd]`` then ``(m, l)`` ``[B, hq, 2]``."""
+    batch, hq, hd = q.shape
+    kv = keys.shape[2]
+    r = hq // kv
+    qg = q.reshape(batch, kv, r, hd).astype(np.float64)
+    raw = bf16_round(np.einsum("bkrd,btkd->bkrt", qg, keys.astype(np.float64)).astype(np.float32))
+    score = bf16_round((raw / np.float32(np.sqrt(hd))).astype(np.float32)).astype(np.float64)
+    score = np.where(mask[:, None, None, :], score, -np.inf)
+    m = np.max(score, axis=-1) if score.shape[-1] else np.full(score.shape[:-1], -np.inf)
+    with np.errstate(invalid="ignore"):
+        p = np.where(np.isfinite(m)[..., None], np.exp(score - m[..., None]), 0.0)
+    l_sum = p.sum(-1)
+    o = np.einsum("bkrt,btkd->bkrd", p, values.astype(np.float64))
+    stats = np.stack([m, l_sum], -1).reshape(batch, hq, 2)
+    return np.concatenate([o.reshape(-1), stats.reshape(-1)]).astype(np.float32)
+
+
+def combine_partials(parts, batch, hq, hd, gate=None):
+    """Log-sum-exp merge of consecutive flat partial sets (``attention_partial``) in set
+    order, then BF16 and the output gate of ``attention_cache.py:169-170``."""
+    per = batch * hq * (hd + 2)
+    parts = np.asarray(parts, np.float64).reshape(-1, per)
+    o = parts[:, : batch * hq * hd].reshape(-1, batch, hq, hd)
+    st = parts[:, batch * hq * hd :].reshape(-1, batch, hq, 2)
+    m_all = st[..., 0].max(0)
+    with np.errstate(invalid="ignore"):
+        f = np.where(np.isfinite(st[..., 0]), np.exp(st[..., 0] - m_all[None]), 0.0)
+        out = (o * f[..., None]).sum(0) / (st[..., 1] * f).sum(0)[..., None]
+    out = bf16_round(out.astype(np.float32))
+    if gate is not None:
+        out = bf16_round((out * bf16_round(sigmoid(gate))).astype(np.float32))
+    return out

@@ -1,0 +1,179 @@
+"""Decoder-layer glue kernels and one layer of the synthetic decoder stack against the oracle.
+
+The stack's step is checked stage by stage: each stage's GPU output is compared with the
+oracle applied to the GPU's own input of that stage, so a near-tie somewhere upstream
+cannot move a later comparison.
+"""
+
+import numpy as np
+import pytest
+
+from oracle import kv, layer, layout, moe
+from oracle.precision import bf16_round
+from util import bf16_tensor, rel_err, to_f32
+
+pytestmark = pytest.mark.gpu
+
+
+def test_rms_norm_matches_oracle(cuda_device):
+    from qk_b200 import _lib
+
+    rng = np.random.default_rng(3)
+    x = bf16_round(rng.normal(size=(7, 2048)).astype(np.float32) * 3)
+    gamma = bf16_round(rng.uniform(0.5, 1.5, 2048).astype(np.float32))
+    xd, gd = bf16_tensor(x, cuda_device), bf16_tensor(gamma, cuda_device)
+    out = xd.clone()
+    _lib.call("qk_rms_norm", _lib.ptr(xd), _lib.ptr(gd), 7, 2048, 1e-6, _lib.ptr(out), _lib.stream_handle(cuda_device))
+    got, expected = to_f32(out), layer.rms(x, gamma, 1e-6)
+    assert np.mean(got == expected) > 0.99
+    assert rel_err(got, expected)[0] < 1e-2
+
+
+def test_qk_norm_rope_matches_oracle(cuda_device):
+    import torch
+
+    from qk_b200 import _lib
+
+    rng = np.random.default_rng(4)
+    B, hq, kvh, hd, rot = 3, 16, 2, 256, 64
+    qkv = bf16_round(rng.normal(size=(B, (2 * hq + 2 * kvh) * hd)).astype(np.float32))
+    qn = bf16_round(rng.uniform(0.5, 1.5, hd).astype(np.float32))
+    kn = bf16_round(rng.uniform(0.5, 1.5, hd).astype(np.float32))
+    pos = np.array([0, 17, 8191], np.int32)
+    inv = layer.inv_freq(rot, 1e7)
+    outs = [torch.empty((B, h, hd), dtype=torch.bfloat16, device=cuda_device) for h in (hq, hq, kvh, kvh)]
+    # device inputs stay referenced until the kernel has run (the caching allocator would
+    # otherwise hand a freed input's memory to the next one)
+    ins = [bf16_tensor(qkv, cuda_device), bf16_tensor(qn, cuda_device), bf16_tensor(kn, cuda_device),
+           torch.from_numpy(inv).to(cuda_device), torch.from_numpy(pos).to(cuda_device)]
+    _lib.call("qk_qk_norm_rope", *[_lib.ptr(t) for t in ins], B, hq, kvh, hd, rot, 1e-6,
+              *[_lib.ptr(o) for o in outs], _lib.stream_handle(cuda_device))
+    torch.cuda.synchronize(cuda_device)
+    expected = layer.qk_norm_rope(qkv, qn, kn, pos, hq, kvh, hd, rot, 1e7, 1e-6)
+    for name, got, exp in zip(("q", "gate", "k", "v"), outs, expected):
+        got = to_f32(got)
+        if name in ("gate", "v"):
+            np.testing.assert_array_equal(got, exp)
+        else:
+            assert np.mean(got == exp) > 0.98, name
+            assert rel_err(got, exp)[0] < 1e-2, name
+
+
+def test_residual_add_and_shared_route(cuda_device):
+    import torch
+
+    from qk_b200 import _lib
+
+    rng = np.random.default_rng(5)
+    x = bf16_round(rng.normal(size=(5, 512)).astype(np.float32))
+    y = bf16_round(rng.normal(size=(5, 512)).astype(np.float32))
+    xd, yd = bf16_tensor(x, cuda_device), bf16_tensor(y, cuda_device)
+    _lib.call("qk_residual_add", _lib.ptr(xd), _lib.ptr(yd), x.size, _lib.ptr(xd), _lib.stream_handle(cuda_device))
+    np.testing.assert_array_equal(to_f32(xd), bf16_round(x + y))
+    ids = rng.integers(0, 64, (5, 4)).astype(np.int32)
+    w = bf16_round(rng.uniform(0, 1, (5, 4)).astype(np.float32))
+    wsr = bf16_round(rng.normal(0, 0.05, 512).astype(np.float32))
+    ids_out = torch.empty((5, 5), dtype=torch.int32, device=cuda_device)
+    w_out = torch.empty((5, 5), dtype=torch.bfloat16, device=cuda_device)
+    ins = [torch.from_numpy(ids).to(cuda_device), bf16_tensor(w, cuda_device), bf16_tensor(x, cuda_device),
+           bf16_tensor(wsr, cuda_device)]
+    _lib.call("qk_append_shared_route", _lib.ptr(ins[0]), _lib.ptr(ins[1]), 5, 4, _lib.ptr(ins[2]),
+              _lib.ptr(ins[3]), 512, 64, _lib.ptr(ids_out), _lib.ptr(w_out), _lib.stream_handle(cuda_device))
+    got_ids, got_w = ids_out.cpu().numpy(), to_f32(w_out)
+    np.testing.assert_array_equal(got_ids[:, :4], ids)
+    assert (got_ids[:, 4] == 64).all()
+    np.testing.assert_array_equal(got_w[:, :4], w)
+    gate = layer.shared_gate(x, wsr)
+    assert np.max(np.abs(got_w[:, 4] - gate)) <= 2 ** -8  # one BF16 step of a value in (0, 1)
+
+
+def _np(t):
+    return to_f32(t) if t.dtype == __import__("torch").bfloat16 else t.float().cpu().numpy()
+
+
+@pytest.mark.parametrize("qtype", ["Q6_K", "Q4_K"])
+def test_one_decoder_layer_stage_by_stage(cuda_device, qtype):
+    import torch
+
+    from qk_b200.decoder import StackConfig, SyntheticDecoder
+
+    cfg = StackConfig(layers=1, hidden=512, intermediate=256, experts=8, top_k=2, query_heads=8, kv_heads=2,
+                      head_dim=128, rotary_dim=32, context=256, page=16, qtype=qtype)
+    model = SyntheticDecoder(cfg, cuda_device, seed=11)
+    state = model.state(3, seed=12)
+    L = model.layers[0]
+    cache0 = {n: (state.caches[0][n].cpu().numpy() if n in ("k", "v") else to_f32(state.caches[0][n]))
+              for n in ("k", "v", "k_scale", "v_scale")}
+    x0 = to_f32(state.x)
+    state.step()
+    torch.cuda.synchronize(cuda_device)
+    hq, kvh, hd, H = cfg.query_heads, cfg.kv_heads, cfg.head_dim, cfg.hidden
+    pos = state.positions.cpu().numpy()
+    idx = state.indices.cpu().numpy()
+
+    # attention half
+    qkv = to_f32(state.qkv)
+    mx, _ = rel_err(qkv, layer.linear(layer.rms(x0, _np(L.attn_norm), cfg.eps), _np(L.w_qkv)))
+    assert mx < 1e-2, ("qkv", mx)
+    q, gate, k, v = layer.qk_norm_rope(qkv, _np(L.q_norm), _np(L.k_norm), pos, hq, kvh, hd, cfg.rotary_dim,
+                                       cfg.rope_theta, cfg.eps)
+    assert rel_err(to_f32(state.q), q)[0] < 1e-2 and rel_err(to_f32(state.k), k)[0] < 1e-2
+    np.testing.assert_array_equal(to_f32(state.gate), gate)
+    kv.write_quantized(cache0, to_f32(state.k), to_f32(state.v), pos, np.ones(3, bool), kvh, hd)
+    for n in ("k", "v"):
+        np.testing.assert_array_equal(state.caches[0][n].cpu().numpy(), cache0[n])
+    keys = kv.read_quantized(cache0["k"], cache0["k_scale"], idx, kvh, hd)
+    values = kv.read_quantized(cache0["v"], cache0["v_scale"], idx, kvh, hd)
+    o = kv.attention(to_f32(state.q), keys, values, np.arange(cfg.context)[None, :] <= pos[:, None],
+                     to_f32(state.gate))
+    mx, l2 = rel_err(to_f32(state.o), o)
+    assert mx < 1e-2 and l2 < 5e-3, ("attention", mx, l2)
+    a = to_f32(state.a)
+    assert rel_err(a, layer.linear(to_f32(state.o).reshape(3, -1), _np(L.w_o)))[0] < 1e-2
+    x1 = bf16_round((x0 + a).astype(np.float32))
+
+    # MoE half
+    h2 = to_f32(state.h)
+    assert rel_err(h2, layer.rms(x1, _np(L.ffn_norm), cfg.eps))[0] < 1e-2
+    ids_all = state.ids_all[0].cpu().numpy()
+    w_all = to_f32(state.w_all)
+    ids, w, _ = moe.routes(h2, _np(L.router), cfg.top_k)
+    np.testing.assert_array_equal(ids_all[:, :cfg.top_k], ids)
+    np.testing.assert_array_equal(w_all[:, :cfg.top_k], w)
+    assert (ids_all[:, cfg.top_k] == cfg.experts).all()
+    assert np.max(np.abs(w_all[:, cfg.top_k] - layer.shared_gate(h2, _np(L.shared_router)))) <= 2 ** -8
+    raw = {}
+    for kind in ("gate", "up", "down"):
+        rows, width = (H, cfg.intermediate) if kind == "down" else (cfg.intermediate, H)
+        t = L.experts[kind].cpu().numpy()
+        raw[kind] = np.stack([layout.untile(t[e], qtype, rows, width).reshape(-1) for e in range(t.shape[0])])
+    y = moe.expert_ffn(raw["gate"], raw["up"], raw["down"], h2, ids_all, w_all, gate_type=qtype, up_type=qtype,
+                       down_type=qtype, hidden=H, intermediate=cfg.intermediate)
+    mx, l2 = rel_err(to_f32(state.y), y)
+    assert mx < 1e-2 and l2 < 5e-3, ("experts", mx, l2)
+    np.testing.assert_array_equal(to_f32(state.x), bf16_round((x1 + to_f32(state.y)).astype(np.float32)))
+
+
+def test_stack_step_in_a_cuda_graph_is_finite_and_repeatable(cuda_device):
+    import torch
+
+    from qk_b200.decoder import StackConfig, SyntheticDecoder
+
+    cfg = StackConfig(layers=3, experts=64, top_k=4, context=1024)
+    model = SyntheticDecoder(cfg, cuda_device, seed=21)
+    state = model.state(8, seed=22)
+    x0 = state.x.clone()
+    state.step()
+    eager = state.x.clone()
+    graph = torch.cuda.CUDAGraph()
+    state.x.copy_(x0)
+    torch.cuda.synchronize(cuda_device)
+    with torch.cuda.graph(graph):
+        state.step()
+    state.x.copy_(x0)
+    graph.replay()
+    torch.cuda.synchronize(cuda_device)
+    assert torch.isfinite(state.x.float()).all()
+    assert torch.equal(state.x.view(torch.int16), eager.view(torch.int16))
+    nbytes, distinct = state.step_bytes()
+    assert len(distinct) == 3 and all(1 <= d <= 65 for d in distinct) and nbytes > 0

@@ -222,3 +222,34 @@ def test_expert_all_to_all_dispatch_matches_single_device_layer_gloo(tmp_path):
     for rank in range(2):
         got, expected = np.load(f"{result}.{rank}.npy")
         np.testing.assert_array_equal(got, expected)
+
+
+@pytest.mark.parametrize("qtype", ["Q6_K", "Q4_K"])
+def test_tensor_slices_are_the_split_expert_bytes(qtype):
+    """put_expert_bytes' tensor slice (NumPy or torch input) equals the reference's split."""
+    import torch
+
+    from qk_b200.parallel import split_expert_bytes, tensor_slice
+    from qk_b200.quant import block_layout
+
+    hidden, inter = 512, 1024
+    rng = np.random.default_rng(9)
+    size = block_layout(qtype)[1]
+    for kind, rows, width in (("gate", inter, hidden), ("up", inter, hidden), ("down", hidden, inter)):
+        raw = rng.integers(0, 256, (3, rows * (width // 256) * size), dtype=np.uint8)
+        for tp in (1, 2, 4):
+            split = split_expert_bytes(raw, kind, qtype, hidden, inter, tp)
+            for r in range(tp):
+                np.testing.assert_array_equal(tensor_slice(raw, kind, qtype, hidden, inter, tp, r), split[r])
+                got = tensor_slice(torch.from_numpy(raw), kind, qtype, hidden, inter, tp, r)
+                np.testing.assert_array_equal(got.contiguous().numpy(), split[r])
+    with pytest.raises(ValueError, match="whole down"):
+        tensor_slice(np.zeros((1, 512 * 2 * size), np.uint8), "down", qtype, 512, 512, 4, 0)
+
+
+def test_tensor_parallel_factory_contract():
+    from qk_b200.experts import expert_parallel
+
+    with pytest.raises(ValueError, match="process group"):
+        expert_parallel(None, gate_type="Q6_K", up_type="Q6_K", down_type="Q6_K", hidden=2048,
+                        intermediate=512, tensor_parallel=2)
