@@ -431,6 +431,8 @@ def b200_arm(args):
         line["sweep"] = sweep
     if rank == 0 and not args.no_attention:
         line["attention"] = attention_report(device, args)
+    if rank == 0 and world == 1:
+        line["layer"] = layer_report(raw, device, args)
     if rank == 0 and world == 1 and not args.no_stack:
         line["stack"] = stack_report(device, args)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -516,6 +518,52 @@ def attention_report(device, args):
         r["frac"] = r["gbs"] / peak_gbs
     return {"kernel": "attn_stream_kernel + attn_merge_kernel (Q8 KV, 16q/2kv, hd 256)",
             "bytes_per_slot": ATTN_SLOT_BYTES, "l2": "flushed before every call", "configs": attn}
+
+
+def layer_report(raw, device, args):
+    """BASELINE.json configs[0] on one GPU: one routed-MoE layer call (router top-4 of 64 +
+    expert SwiGLU + combine) on T = 8 tokens (N(0, 1), seed 0), router N(0, 0.02) FP32
+    (seed 2), the first 64 of the bench's Q6_K experts (N(0, 0.02), seed 1). The layer touches
+    at most 32 experts (82 MB, less than L2), so L2 is flushed before every timed call."""
+    import numpy as np
+    import torch
+
+    from qk_b200.experts import expert_parallel
+    from qk_b200.parallel import put_expert_bytes
+    from qk_b200.routing import routes
+
+    count, T, k = 64, 8, 4
+    tensors = {n: put_expert_bytes(raw[n][:count], n, args.qtype, HIDDEN, INTER, device=device) for n in raw}
+    x = torch.from_numpy(np.random.default_rng(0).normal(size=(T, HIDDEN)).astype(np.float32)).to(device).bfloat16()
+    router = torch.from_numpy(np.random.default_rng(2).normal(0, 0.02, (count, HIDDEN)).astype(np.float32)).to(device)
+    fn = expert_parallel(gate_type=args.qtype, up_type=args.qtype, down_type=args.qtype, hidden=HIDDEN,
+                         intermediate=INTER)
+    stream = torch.cuda.current_stream(device)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+
+    def call():
+        ids, w = routes(x, router, k)
+        return fn(tensors["gate"], tensors["up"], tensors["down"], x, ids, w), ids
+
+    for _ in range(3):
+        call()
+    times = []
+    for _ in range(args.attn_reps):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        _, ids = call()
+        e1.record(stream)
+        torch.cuda.synchronize(device)
+        times.append(e0.elapsed_time(e1))
+    ms = statistics.median(times)
+    active = int(torch.unique(ids).numel())
+    nbytes = active * packed_bytes_per_expert(args.qtype) + count * HIDDEN * 4 + T * HIDDEN * 4
+    peak, _ = hbm_peak()
+    return {"workload": "configs[0]: one routed-MoE layer, T=8, top-4 of 64 experts, 1 GPU", "qtype": args.qtype,
+            "us": ms * 1e3, "tokens_per_s": T / (ms * 1e-3), "active_experts": active,
+            "gbs": nbytes / (ms * 1e-3) / 1e9, "frac": nbytes / (ms * 1e-3) / 1e9 / peak,
+            "l2": "flushed before every call", "launches_per_call": 6}
 
 
 def stack_report(device, args):

@@ -111,8 +111,9 @@ size_t layout(const qk_moe_desc& d, int max_tokens, uint8_t* base, Workspace* ws
 // ------------------------------------------------------------------------------------
 // 1. routing metadata (one CTA)
 // ------------------------------------------------------------------------------------
-__global__ void __launch_bounds__(1024) moe_route_kernel(const int32_t* __restrict__ ids,
-                                                         const uint16_t* __restrict__ weights,
+constexpr int kStagedRoutes = 4096;
+
+__global__ void __launch_bounds__(1024) moe_route_kernel(const int32_t* ids, const uint16_t* weights,
                                                          int B, int k, int E, int first,
                                                          Workspace ws) {
   extern __shared__ int32_t sh[];
@@ -122,7 +123,20 @@ __global__ void __launch_bounds__(1024) moe_route_kernel(const int32_t* __restri
   int32_t* offsets = sh + 2 * E;   // [E + 1]
   __shared__ int32_t chunk_base[33], active_base[33];
   const int tid = threadIdx.x, nt = blockDim.x;
+  // The routes staged in shared memory when they fit (kStagedRoutes): both passes read
+  // every route of a token k times.
+  const bool staged = B * k <= kStagedRoutes;
+  int32_t* s_ids = sh + 3 * E + 1;                                                   // [B k]
+  uint16_t* s_w = reinterpret_cast<uint16_t*>(s_ids + (staged ? B * k : 0));          // [B k]
   for (int e = tid; e < E; e += nt) counts[e] = cursor[e] = 0;
+  if (staged) {
+    for (int i = tid; i < B * k; i += nt) {
+      s_ids[i] = ids[i];
+      s_w[i] = weights[i];
+    }
+    ids = s_ids;
+    weights = s_w;
+  }
   __syncthreads();
 
   // Pass 1: entries per expert. The first slot j of a token that names expert e owns
@@ -445,7 +459,8 @@ static int moe_forward_impl(const qk_moe_desc* desc, const uint8_t* gate, const 
     return QK_OK;
   }
   mark(0);
-  const size_t route_smem = (3 * static_cast<size_t>(d.num_experts) + 1) * 4;
+  const size_t routes = static_cast<size_t>(B) * d.top_k;
+  const size_t route_smem = (3 * static_cast<size_t>(d.num_experts) + 1) * 4 + (routes <= kStagedRoutes ? routes * 6 : 0);
   int rc = allow_smem(reinterpret_cast<const void*>(moe_route_kernel), route_smem);
   if (rc) return rc;
   moe_route_kernel<<<1, 1024, route_smem, st>>>(ids, weights, B, d.top_k, d.num_experts, d.first_expert, ws);

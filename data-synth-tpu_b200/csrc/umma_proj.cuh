@@ -43,12 +43,23 @@
 
 namespace qk {
 
+// TMEM split (overridable when building: -DQK_UMMA_ISSUERS=.. -DQK_UMMA_ABUF=.. -DQK_UMMA_DBUF=..)
+#ifndef QK_UMMA_ISSUERS
+#define QK_UMMA_ISSUERS 4
+#endif
+#ifndef QK_UMMA_ABUF
+#define QK_UMMA_ABUF 3
+#endif
+#ifndef QK_UMMA_DBUF
+#define QK_UMMA_DBUF 1
+#endif
 constexpr int kDecodeWarps = 16;
 constexpr int kProducerWarp = 16;
 constexpr int kMmaWarp0 = 17;
-constexpr int kMmaIssuers = 4;  // each takes 16 / kMmaIssuers of a block's 16 K steps
-constexpr int kABuffers = 3;
-constexpr int kDBuffers = 1;
+constexpr int kMmaIssuers = QK_UMMA_ISSUERS;  // each takes 16 / kMmaIssuers of a block's 16 K steps
+constexpr int kABuffers = QK_UMMA_ABUF;
+constexpr int kDBuffers = QK_UMMA_DBUF;
+static_assert(16 % kMmaIssuers == 0 && 16 / kMmaIssuers >= 4, "issuers take whole 64-value K atoms");
 static_assert(kABuffers * 128 + kDBuffers * kMmaIssuers * 32 <= 512, "TMEM columns");
 constexpr int kEpilogueWarp0 = kMmaWarp0 + kMmaIssuers;
 constexpr int kUmmaThreads = (kEpilogueWarp0 + 4) * 32;

@@ -107,6 +107,39 @@ def test_zero_weights_give_zero_and_ids_outside_rank_are_ignored(cuda_device):
     np.testing.assert_array_equal(got, 0)
 
 
+@pytest.mark.parametrize("qtype", ["Q6_K", "Q4_K"])
+def test_garbage_experts_do_not_leak_nan(cuda_device, qtype):
+    """The NaN-isolation contract of test_qwen38_small_groups.py:227-264: an expert whose
+    bytes decode to NaN (every byte 0xFF, so its FP16 block scales are NaN) must not reach
+    the output when it is routed with weight 0 (a finished row) or not routed at all."""
+    import torch
+
+    from qk_b200.experts import expert_parallel
+    from qk_b200.parallel import put_expert_bytes
+
+    hidden, intermediate, count = 256, 256, 4
+    rng = np.random.default_rng(31)
+    raw = make_experts(rng, count, hidden, intermediate, qtype)
+    x = rng.normal(size=(6, hidden)).astype(np.float32)
+    ids = np.array([[0, 3], [1, 3], [2, 3], [0, 1], [1, 2], [3, 0]], np.int32)
+    w = bf16_round(rng.uniform(0.1, 1.0, (6, 2)).astype(np.float32))
+    w[:3, 1] = 0.0   # rows 0-2 route to the garbage expert 3 with weight 0
+    w[5, 0] = 0.0    # row 5 too
+    clean, _, dev = run_layer(cuda_device, raw, qtype, hidden, intermediate, x, ids, w)
+    for name in ("gate", "up", "down"):  # expert 3's tiles become 0xFF bytes on the device
+        dev[name][3].fill_(0xFF)
+    fn = expert_parallel(gate_type=qtype, up_type=qtype, down_type=qtype, hidden=hidden,
+                         intermediate=intermediate)
+    got = to_f32(fn(dev["gate"], dev["up"], dev["down"], bf16_tensor(x, cuda_device),
+                    torch.from_numpy(ids).to(cuda_device), bf16_tensor(w, cuda_device)))
+    fn.check_status()
+    assert np.isfinite(got).all()
+    np.testing.assert_array_equal(got, clean)
+    expected = moe.expert_ffn(raw["gate"], raw["up"], raw["down"], x, ids, w, gate_type=qtype, up_type=qtype,
+                              down_type=qtype, hidden=hidden, intermediate=intermediate)
+    assert rel_err(got, expected)[0] < LAYER_TOL
+
+
 def test_partial_sums_over_two_expert_ranges_add_up_to_the_layer(cuda_device):
     """The expert-parallel decomposition (per-rank FP32 partial + all-reduce) on one GPU."""
     import torch
