@@ -28,6 +28,8 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 __global__ void __launch_bounds__(kRowThreads) rms_norm_kernel(const uint16_t* __restrict__ x,
                                                                const uint16_t* __restrict__ gamma, int width,
                                                                float eps, uint16_t* __restrict__ out) {
+  pdl_wait();  // launched as a programmatic dependent: the previous kernel's outputs first
+  pdl_trigger();
   __shared__ float red[kRowThreads / 32];
   const int64_t row = blockIdx.x;
   const uint16_t* xr = x + row * width;
@@ -53,6 +55,8 @@ __global__ void __launch_bounds__(kRowThreads) qk_norm_rope_kernel(
     const float* __restrict__ inv_freq, const int32_t* __restrict__ positions, int hq, int kv, int hd, int rotary,
     float eps, uint16_t* __restrict__ q_out, uint16_t* __restrict__ gate_out, uint16_t* __restrict__ k_out,
     uint16_t* __restrict__ v_out) {
+  pdl_wait();  // launched as a programmatic dependent: the previous kernel's outputs first
+  pdl_trigger();
   __shared__ float red[kRowThreads / 32];
   __shared__ float normed[512];
   const int64_t b = blockIdx.x;
@@ -90,6 +94,8 @@ __global__ void __launch_bounds__(kRowThreads) qk_norm_rope_kernel(
 
 // out = bf16(f32(x) + f32(y)) over n values (out may alias x).
 __global__ void residual_add_kernel(const uint16_t* x, const uint16_t* __restrict__ y, int64_t n, uint16_t* out) {
+  pdl_wait();
+  pdl_trigger();
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x)
     out[i] = bf16_bits_rne(__fadd_rn(bf16_to_f32(x[i]), bf16_to_f32(y[i])));
@@ -102,6 +108,8 @@ __global__ void __launch_bounds__(kRowThreads) append_shared_route_kernel(
     const int32_t* __restrict__ ids, const uint16_t* __restrict__ w, int k, const uint16_t* __restrict__ h,
     const uint16_t* __restrict__ wsr, int H, int shared_id, int32_t* __restrict__ ids_out,
     uint16_t* __restrict__ w_out) {
+  pdl_wait();  // launched as a programmatic dependent: the previous kernel's outputs first
+  pdl_trigger();
   __shared__ float red[kRowThreads / 32];
   const int64_t b = blockIdx.x;
   float s = 0.f;
@@ -129,8 +137,10 @@ int qk_rms_norm(const uint16_t* x, const uint16_t* gamma, int rows, int width, f
   QK_REQUIRE(rows >= 0 && width > 0, "invalid rms geometry");
   if (rows == 0) return QK_OK;
   QK_REQUIRE(x && gamma && out, "null pointer");
-  rms_norm_kernel<<<rows, kRowThreads, 0, as_stream(stream)>>>(x, gamma, width, eps, out);
-  QK_LAUNCHED("rms_norm_kernel");
+  const cudaError_t e = launch_dependent(rms_norm_kernel, dim3(rows), dim3(kRowThreads), 0, as_stream(stream), x, gamma,
+                                         width, eps, out);
+  if (e != cudaSuccess) return cuda_error(e, "rms_norm_kernel");
+  count_launch();
   return QK_OK;
 }
 
@@ -143,9 +153,11 @@ int qk_qk_norm_rope(const uint16_t* qkv, const uint16_t* q_norm, const uint16_t*
   if (B == 0) return QK_OK;
   QK_REQUIRE(qkv && q_norm && k_norm && positions && q_out && gate_out && k_out && v_out, "null pointer");
   QK_REQUIRE(inv_freq || rotary_dim == 0, "inv_freq is required when rotary_dim > 0");
-  qk_norm_rope_kernel<<<dim3(B, hq + kv), kRowThreads, 0, as_stream(stream)>>>(
-      qkv, q_norm, k_norm, inv_freq, positions, hq, kv, head_dim, rotary_dim, eps, q_out, gate_out, k_out, v_out);
-  QK_LAUNCHED("qk_norm_rope_kernel");
+  const cudaError_t e = launch_dependent(qk_norm_rope_kernel, dim3(B, hq + kv), dim3(kRowThreads), 0, as_stream(stream),
+                                         qkv, q_norm, k_norm, inv_freq, positions, hq, kv, head_dim, rotary_dim, eps,
+                                         q_out, gate_out, k_out, v_out);
+  if (e != cudaSuccess) return cuda_error(e, "qk_norm_rope_kernel");
+  count_launch();
   return QK_OK;
 }
 
@@ -154,9 +166,10 @@ int qk_residual_add(const uint16_t* x, const uint16_t* y, int64_t n, uint16_t* o
   if (n == 0) return QK_OK;
   QK_REQUIRE(x && y && out, "null pointer");
   const int64_t blocks = (n + 255) / 256;
-  residual_add_kernel<<<static_cast<unsigned>(blocks < 4 * 148 ? blocks : 4 * 148), 256, 0, as_stream(stream)>>>(
-      x, y, n, out);
-  QK_LAUNCHED("residual_add_kernel");
+  const cudaError_t e = launch_dependent(residual_add_kernel, dim3(static_cast<unsigned>(blocks < 4 * 148 ? blocks : 4 * 148)),
+                                         dim3(256), 0, as_stream(stream), x, y, n, out);
+  if (e != cudaSuccess) return cuda_error(e, "residual_add_kernel");
+  count_launch();
   return QK_OK;
 }
 
@@ -166,9 +179,10 @@ int qk_append_shared_route(const int32_t* ids, const uint16_t* weights, int B, i
   QK_REQUIRE(B >= 0 && k > 0 && k < kRowThreads && H > 0, "invalid route geometry");
   if (B == 0) return QK_OK;
   QK_REQUIRE(ids && weights && h && shared_router && ids_out && weights_out, "null pointer");
-  append_shared_route_kernel<<<B, kRowThreads, 0, as_stream(stream)>>>(ids, weights, k, h, shared_router, H,
-                                                                       shared_id, ids_out, weights_out);
-  QK_LAUNCHED("append_shared_route_kernel");
+  const cudaError_t e = launch_dependent(append_shared_route_kernel, dim3(B), dim3(kRowThreads), 0, as_stream(stream),
+                                         ids, weights, k, h, shared_router, H, shared_id, ids_out, weights_out);
+  if (e != cudaSuccess) return cuda_error(e, "append_shared_route_kernel");
+  count_launch();
   return QK_OK;
 }
 

@@ -117,6 +117,7 @@ __global__ void __launch_bounds__(1024) moe_route_kernel(const int32_t* ids, con
                                                          int B, int k, int E, int first,
                                                          Workspace ws) {
   extern __shared__ int32_t sh[];
+  pdl_wait();     // launched as a programmatic dependent: the routes' producer first
   pdl_trigger();  // the dispatch may launch now (it waits for this kernel before reading)
   int32_t* counts = sh;            // [E]
   int32_t* cursor = sh + E;        // [E]
@@ -463,8 +464,12 @@ static int moe_forward_impl(const qk_moe_desc* desc, const uint8_t* gate, const 
   const size_t route_smem = (3 * static_cast<size_t>(d.num_experts) + 1) * 4 + (routes <= kStagedRoutes ? routes * 6 : 0);
   int rc = allow_smem(reinterpret_cast<const void*>(moe_route_kernel), route_smem);
   if (rc) return rc;
-  moe_route_kernel<<<1, 1024, route_smem, st>>>(ids, weights, B, d.top_k, d.num_experts, d.first_expert, ws);
-  QK_LAUNCHED("moe_route_kernel");
+  {
+    const cudaError_t e = launch_dependent(moe_route_kernel, dim3(1), dim3(1024), route_smem, st, ids, weights, B,
+                                           d.top_k, d.num_experts, d.first_expert, ws);
+    if (e != cudaSuccess) return cuda_error(e, "moe_route_kernel");
+    count_launch(1);
+  }
 
   const int sms = sm_count();
   const int64_t rows_max = static_cast<int64_t>(chunks_bound(d, B)) * kMaxTok;

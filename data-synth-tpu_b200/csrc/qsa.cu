@@ -1,0 +1,266 @@
+// Sparse-attention token selection (QSA indexer) feeding the Q8 KV decode attention.
+//
+// Replaces the selection half of qwen38_tpu/attention_cache.py:84-125 (select_tokens), after
+// the block keys are up to date:
+//   scores[b, t] = sum_h relu(q[b, h] . keys[b, t]) / sqrt(dim)   (FP32, :100-112)
+//   scores[b, t] = -inf for t >= count, count = (lengths[b] + 1) // ratio   (:113-114)
+//   selected = lax.top_k(scores, K), K = min(budget // ratio, blocks)      (:115-116)
+//   indices = [selected * ratio + r for r < ratio] ++ [count * ratio + j for j < ratio - 1]
+//   valid   = [selected < count] * ratio ++ [j < (lengths + 1) % ratio]   (:117-122)
+//   indices = where(valid, indices, 0)                                      (:123-124)
+//
+// qsa_scores_kernel: HBM-bound pass over the block keys (dim BF16 values per block); a warp
+// takes four blocks at a time, its lanes split the dimension, and the query heads live in
+// shared memory. qsa_select_kernel: one CTA per row; radix select (4 passes of 8 bits over
+// an order-preserving key of the FP32 score) finds the K-th largest score, a block-wide scan
+// keeps every larger score and the lowest-index equal ones (lax.top_k's tie rule), and a
+// bitonic sort orders the K blocks by (score descending, index ascending), top_k's order.
+#include <cmath>
+
+#include "common.cuh"
+
+namespace qk {
+namespace {
+
+constexpr int kScoreWarps = 8;
+constexpr int kBlocksPerWarp = 4;  // blocks a warp scores at once (loads in flight)
+constexpr int kSelThreads = 1024;
+constexpr int kMaxHeads = 8, kMaxDim = 256, kMaxK = 1024, kMaxBlocks = 16384;
+
+__global__ void __launch_bounds__(kScoreWarps * 32) qsa_scores_kernel(const uint16_t* __restrict__ query,
+                                                                      const uint16_t* __restrict__ keys,
+                                                                      const int32_t* __restrict__ lengths, int heads,
+                                                                      int dim, int blocks, int ratio, float root,
+                                                                      float* __restrict__ scores) {
+  __shared__ float qs[kMaxHeads * kMaxDim];
+  const int b = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int i = threadIdx.x; i < heads * dim; i += blockDim.x)
+    qs[i] = bf16_to_f32(query[static_cast<int64_t>(b) * heads * dim + i]);
+  __syncthreads();
+  const int count = (lengths[b] + 1) / ratio;
+  const int per_lane = dim / 32;  // 2, 4 or 8 values (dim 64, 128 or 256)
+  const int t0 = (blockIdx.x * kScoreWarps + warp) * kBlocksPerWarp;
+  const uint16_t* kb = keys + static_cast<int64_t>(b) * blocks * dim;
+  float kv[kBlocksPerWarp][8];
+#pragma unroll
+  for (int u = 0; u < kBlocksPerWarp; ++u) {
+    const int t = t0 + u;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) kv[u][j] = 0.f;
+    if (t >= blocks) continue;
+    const uint16_t* row = kb + static_cast<int64_t>(t) * dim + lane * per_lane;
+    for (int j = 0; j < per_lane; ++j) kv[u][j] = bf16_to_f32(row[j]);
+  }
+#pragma unroll
+  for (int u = 0; u < kBlocksPerWarp; ++u) {
+    const int t = t0 + u;
+    float score = 0.f;
+    for (int h = 0; h < heads; ++h) {
+      float dot = 0.f;
+      for (int j = 0; j < per_lane; ++j) dot = fmaf(qs[h * dim + lane * per_lane + j], kv[u][j], dot);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+      score = __fadd_rn(score, fmaxf(dot, 0.f));
+    }
+    if (lane == 0 && t < blocks)
+      scores[static_cast<int64_t>(b) * blocks + t] = t < count ? __fdiv_rn(score, root) : -INFINITY;
+  }
+}
+
+// Order-preserving map of an FP32 score to an unsigned key (larger score, larger key).
+__device__ __forceinline__ uint32_t score_key(float f) {
+  const uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// Exclusive block-wide scan of one int per thread (kSelThreads threads); returns the total.
+__device__ __forceinline__ int block_scan(int v, int* warp_sums, int* excl) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int incl = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int n = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += n;
+  }
+  __syncthreads();  // warp_sums may still be read by a previous scan
+  if (lane == 31) warp_sums[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    const int s = warp_sums[lane];
+    int si = s;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int n = __shfl_up_sync(0xffffffffu, si, o);
+      if (lane >= o) si += n;
+    }
+    warp_sums[lane] = si - s;  // exclusive prefix of the warp totals
+    if (lane == 31) warp_sums[32] = si;
+  }
+  __syncthreads();
+  *excl = warp_sums[warp] + incl - v;
+  return warp_sums[32];
+}
+
+__global__ void __launch_bounds__(kSelThreads) qsa_select_kernel(const float* __restrict__ scores,
+                                                                 const int32_t* __restrict__ lengths, int blocks,
+                                                                 int ratio, int K, int width,
+                                                                 int32_t* __restrict__ indices,
+                                                                 uint8_t* __restrict__ valid) {
+  extern __shared__ uint32_t keys[];                        // [blocks]
+  __shared__ uint32_t sel_key[kMaxK];
+  __shared__ int32_t sel_idx[kMaxK];
+  __shared__ int hist[256];
+  __shared__ int warp_sums[33];
+  __shared__ uint32_t s_prefix;
+  __shared__ int s_remaining;
+  const int b = blockIdx.x, tid = threadIdx.x;
+  const float* row = scores + static_cast<int64_t>(b) * blocks;
+  for (int i = tid; i < blocks; i += kSelThreads) keys[i] = score_key(row[i]);
+  if (tid == 0) {
+    s_prefix = 0;
+    s_remaining = K;
+  }
+  __syncthreads();
+
+  // radix select of the K-th largest key, 8 bits at a time from the top
+  uint32_t mask = 0;
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    for (int i = tid; i < 256; i += kSelThreads) hist[i] = 0;
+    __syncthreads();
+    const uint32_t prefix = s_prefix;
+    for (int i = tid; i < blocks; i += kSelThreads)
+      if ((keys[i] & mask) == prefix) atomicAdd(&hist[(keys[i] >> shift) & 255u], 1);
+    __syncthreads();
+    if (tid == 0) {
+      int acc = 0, need = s_remaining, bin = 255;
+      for (; bin > 0; --bin) {
+        if (acc + hist[bin] >= need) break;
+        acc += hist[bin];
+      }
+      s_remaining = need - acc;  // how many keys of this bin (and prefix) still to take
+      s_prefix = prefix | (static_cast<uint32_t>(bin) << shift);
+    }
+    mask |= 255u << shift;
+    __syncthreads();
+  }
+  const uint32_t T = s_prefix;
+  const int take_equal = s_remaining;  // keys equal to T to keep, lowest block index first
+
+  // keep every key > T and the first take_equal keys == T (in block order): each thread
+  // scans a contiguous chunk of blocks
+  const int per = (blocks + kSelThreads - 1) / kSelThreads;
+  const int lo = min(blocks, tid * per), hi = min(blocks, lo + per);
+  int n_eq = 0;
+  for (int i = lo; i < hi; ++i) n_eq += keys[i] == T;
+  int eq_before = 0;
+  block_scan(n_eq, warp_sums, &eq_before);
+  int n_take = 0;
+  {
+    int e = eq_before;
+    for (int i = lo; i < hi; ++i) {
+      const uint32_t k = keys[i];
+      if (k > T) ++n_take;
+      else if (k == T) n_take += e++ < take_equal;
+    }
+  }
+  int pos = 0;
+  block_scan(n_take, warp_sums, &pos);
+  {
+    int e = eq_before;
+    for (int i = lo; i < hi; ++i) {
+      const uint32_t k = keys[i];
+      const bool take = k > T || (k == T && e++ < take_equal);
+      if (take && pos < K) {
+        sel_key[pos] = k;
+        sel_idx[pos] = i;
+        ++pos;
+      }
+    }
+  }
+  // pad to a power of two and sort by (key descending, index ascending)
+  int P = 1;
+  while (P < K) P <<= 1;
+  for (int i = K + tid; i < P; i += kSelThreads) {
+    sel_key[i] = 0;
+    sel_idx[i] = 0x7fffffff;
+  }
+  __syncthreads();
+  for (int size = 2; size <= P; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int i = tid; i < P; i += kSelThreads) {
+        const int j = i ^ stride;
+        if (j > i) {
+          // "before": higher key, or equal key and lower index
+          const bool i_first = sel_key[i] > sel_key[j] || (sel_key[i] == sel_key[j] && sel_idx[i] < sel_idx[j]);
+          const bool ascending_block = (i & size) == 0;  // this half sorts "before"-first
+          if (i_first != ascending_block) {
+            const uint32_t tk = sel_key[i];
+            sel_key[i] = sel_key[j];
+            sel_key[j] = tk;
+            const int ti = sel_idx[i];
+            sel_idx[i] = sel_idx[j];
+            sel_idx[j] = ti;
+          }
+        }
+      }
+      __syncthreads();
+    }
+  }
+  // expand to token indices and flags
+  const int len1 = lengths[b] + 1, count = len1 / ratio;
+  int32_t* out_i = indices + static_cast<int64_t>(b) * width;
+  uint8_t* out_v = valid + static_cast<int64_t>(b) * width;
+  for (int i = tid; i < K * ratio; i += kSelThreads) {
+    const int blk = sel_idx[i / ratio];
+    const bool ok = blk < count;
+    out_i[i] = ok ? blk * ratio + i % ratio : 0;
+    out_v[i] = ok;
+  }
+  for (int j = tid; j < ratio - 1; j += kSelThreads) {
+    const bool ok = j < len1 % ratio;
+    out_i[K * ratio + j] = ok ? count * ratio + j : 0;
+    out_v[K * ratio + j] = ok;
+  }
+}
+
+}  // namespace
+}  // namespace qk
+
+using namespace qk;
+
+extern "C" {
+
+int qk_qsa_block_scores(const uint16_t* query, const uint16_t* keys, const int32_t* lengths, int B, int heads,
+                        int dim, int blocks, int ratio, float* scores, qk_stream_t stream) {
+  QK_REQUIRE(B >= 0 && blocks > 0 && ratio >= 2, "invalid indexer geometry");
+  QK_REQUIRE(heads >= 1 && heads <= kMaxHeads, "indexer heads must be in [1, %d]", kMaxHeads);
+  QK_REQUIRE(dim == 64 || dim == 128 || dim == 256, "indexer dim must be 64, 128 or 256");
+  if (B == 0) return QK_OK;
+  QK_REQUIRE(query && keys && lengths && scores, "null pointer");
+  const int per_cta = kScoreWarps * kBlocksPerWarp;
+  const dim3 grid((blocks + per_cta - 1) / per_cta, B);
+  qsa_scores_kernel<<<grid, kScoreWarps * 32, 0, as_stream(stream)>>>(
+      query, keys, lengths, heads, dim, blocks, ratio, static_cast<float>(std::sqrt(static_cast<double>(dim))), scores);
+  QK_LAUNCHED("qsa_scores_kernel");
+  return QK_OK;
+}
+
+int qk_qsa_select(const float* scores, const int32_t* lengths, int B, int blocks, int ratio, int budget,
+                  int32_t* indices, uint8_t* valid, qk_stream_t stream) {
+  QK_REQUIRE(B >= 0 && blocks > 0 && ratio >= 2, "invalid indexer geometry");
+  QK_REQUIRE(blocks <= kMaxBlocks, "at most %d index blocks per row", kMaxBlocks);
+  QK_REQUIRE(budget >= ratio && budget % ratio == 0, "Invalid sparse attention indexer dimensions or budget");
+  const int K = min(budget / ratio, blocks);
+  QK_REQUIRE(K <= kMaxK, "at most %d selected blocks", kMaxK);
+  if (B == 0) return QK_OK;
+  QK_REQUIRE(scores && lengths && indices && valid, "null pointer");
+  const int width = K * ratio + ratio - 1;
+  const size_t smem = static_cast<size_t>(blocks) * 4;
+  if (int rc = allow_smem(reinterpret_cast<const void*>(qsa_select_kernel), smem)) return rc;
+  qsa_select_kernel<<<B, kSelThreads, smem, as_stream(stream)>>>(scores, lengths, blocks, ratio, K, width, indices,
+                                                                 valid);
+  QK_LAUNCHED("qsa_select_kernel");
+  return QK_OK;
+}
+
+}  // extern "C"

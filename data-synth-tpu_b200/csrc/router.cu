@@ -28,6 +28,8 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(256)
                   uint16_t* __restrict__ weights, float* __restrict__ probs_out) {
   extern __shared__ __align__(16) float lg[];  // [kTok][E], then x rows [kTok][H] (BF16)
   uint16_t* xs = reinterpret_cast<uint16_t*>(lg + kTok * E);
+  pdl_wait();  // launched as a programmatic dependent: the previous kernel's outputs first
+  pdl_trigger();
   cg::cluster_group cluster = cg::this_cluster();
   const unsigned crank = cluster.block_rank();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -179,9 +181,10 @@ static int router_launch(const uint16_t* x, const float* w, const float* logits,
   int rc = allow_smem(reinterpret_cast<const void*>(router_kernel), smem);
   if (rc) return rc;
   const int blocks = (T + kTok - 1) / kTok;
-  router_kernel<<<blocks * kCluster, 256, smem, as_stream(stream)>>>(x, w, logits, active, T, H, E, k, ids, weights,
-                                                                     probs);
-  QK_LAUNCHED("router_kernel");
+  const cudaError_t e = launch_dependent(router_kernel, dim3(blocks * kCluster), dim3(256), smem, as_stream(stream), x, w,
+                                         logits, active, T, H, E, k, ids, weights, probs);
+  if (e != cudaSuccess) return cuda_error(e, "router_kernel");
+  count_launch();
   return QK_OK;
 }
 
