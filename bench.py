@@ -431,6 +431,7 @@ def b200_arm(args):
         line["sweep"] = sweep
     if rank == 0 and not args.no_attention:
         line["attention"] = attention_report(device, args)
+        line["qsa_select"] = qsa_report(device, args)
     if rank == 0 and world == 1:
         line["layer"] = layer_report(raw, device, args)
     if rank == 0 and world == 1 and not args.no_stack:
@@ -618,6 +619,57 @@ def stack_report(device, args):
             "l2": "inputs larger than L2 (packed experts of 48 layers)", "build_s": build_s, "batches": rows}
 
 
+def qsa_report(device, args):
+    """Sparse token selection (attention_cache.py:84-125) at the attention sweep's long
+    context: B in {1, 8, 32} rows, context 32768 -> 8192 index blocks of 128 BF16 values
+    (ratio 4), 4 indexer heads, budget 2048 tokens (K = 512 blocks). Bytes per call = the
+    index keys read (B x 8192 x 256 B) + the scores written and read back; L2 is flushed
+    before every call."""
+    import torch
+
+    from qk_b200 import _lib
+
+    stream = torch.cuda.current_stream(device)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+    peak, _ = hbm_peak()
+    rows = []
+    for batch in (1, 8, 32):
+        blocks, heads, dim, ratio, budget = 8192, 4, 128, 4, 2048
+        g = torch.Generator(device=device).manual_seed(batch)
+        q = torch.randn((batch, heads, dim), device=device, generator=g).to(torch.bfloat16)
+        k = torch.randn((batch, blocks, dim), device=device, generator=g).to(torch.bfloat16)
+        lengths = torch.full((batch,), blocks * ratio - 1, dtype=torch.int32, device=device)
+        scores = torch.empty((batch, blocks), dtype=torch.float32, device=device)
+        K = budget // ratio
+        idx = torch.empty((batch, K * ratio + ratio - 1), dtype=torch.int32, device=device)
+        val = torch.empty(idx.shape, dtype=torch.uint8, device=device)
+        st = _lib.stream_handle(device)
+
+        def call():
+            _lib.call("qk_qsa_block_scores", _lib.ptr(q), _lib.ptr(k), _lib.ptr(lengths), batch, heads, dim, blocks,
+                      ratio, _lib.ptr(scores), st)
+            _lib.call("qk_qsa_select", _lib.ptr(scores), _lib.ptr(lengths), batch, blocks, ratio, budget,
+                      _lib.ptr(idx), _lib.ptr(val), st)
+
+        for _ in range(3):
+            call()
+        times = []
+        for _ in range(args.attn_reps):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            call()
+            e1.record(stream)
+            torch.cuda.synchronize(device)
+            times.append(e0.elapsed_time(e1))
+        ms = statistics.median(times)
+        nbytes = batch * blocks * (dim * 2 + 8)
+        rows.append({"batch": batch, "us": ms * 1e3, "gbs": nbytes / (ms * 1e-3) / 1e9,
+                     "frac": nbytes / (ms * 1e-3) / 1e9 / peak})
+    return {"kernel": "qsa_scores_kernel + qsa_select_kernel (8192 blocks x 128, 4 heads, K = 512)",
+            "l2": "flushed before every call", "configs": rows}
+
+
 def parse_attn_configs(text):
     if not text:
         return ATTN_CONFIGS
@@ -721,6 +773,7 @@ def main():
                         help="attention configs as BxCTX[,BxCTX...] (default: the six of the sweep)")
     parser.add_argument("--attn-reps", type=int, default=20)
     parser.add_argument("--no-stack", action="store_true", help="skip the 48-layer decoder stack")
+    parser.add_argument("--qsa-only", action="store_true", help="only the sparse token selection (one GPU)")
     parser.add_argument("--stack-only", action="store_true", help="only the decoder stack (one GPU)")
     parser.add_argument("--stack-batches", type=lambda t: [int(v) for v in t.split(",")], default=[1, 8, 64])
     parser.add_argument("--stack-layers", type=int, default=48)
@@ -734,6 +787,13 @@ def main():
         return reference_arm(args)
     if args.attention_only:
         return attention_only(args)
+    if args.qsa_only:
+        import torch
+
+        device = torch.device("cuda", 0)
+        torch.cuda.set_device(device)
+        print(json.dumps({"qsa_select": qsa_report(device, args)}), flush=True)
+        return 0
     if args.stack_only:
         import torch
 

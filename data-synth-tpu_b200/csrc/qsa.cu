@@ -15,6 +15,7 @@
 // an order-preserving key of the FP32 score) finds the K-th largest score, a block-wide scan
 // keeps every larger score and the lowest-index equal ones (lax.top_k's tie rule), and a
 // bitonic sort orders the K blocks by (score descending, index ascending), top_k's order.
+#include <algorithm>
 #include <cmath>
 
 #include "common.cuh"
@@ -27,37 +28,51 @@ constexpr int kBlocksPerWarp = 4;  // blocks a warp scores at once (loads in fli
 constexpr int kSelThreads = 1024;
 constexpr int kMaxHeads = 8, kMaxDim = 256, kMaxK = 1024, kMaxBlocks = 16384;
 
+// PER = dim / 32 values of each block's key per lane (2, 4 or 8: dim 64, 128 or 256).
+template <int PER>
 __global__ void __launch_bounds__(kScoreWarps * 32) qsa_scores_kernel(const uint16_t* __restrict__ query,
                                                                       const uint16_t* __restrict__ keys,
                                                                       const int32_t* __restrict__ lengths, int heads,
-                                                                      int dim, int blocks, int ratio, float root,
+                                                                      int blocks, int ratio, float root,
                                                                       float* __restrict__ scores) {
+  constexpr int dim = PER * 32;
   __shared__ float qs[kMaxHeads * kMaxDim];
   const int b = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int i = threadIdx.x; i < heads * dim; i += blockDim.x)
     qs[i] = bf16_to_f32(query[static_cast<int64_t>(b) * heads * dim + i]);
   __syncthreads();
   const int count = (lengths[b] + 1) / ratio;
-  const int per_lane = dim / 32;  // 2, 4 or 8 values (dim 64, 128 or 256)
   const int t0 = (blockIdx.x * kScoreWarps + warp) * kBlocksPerWarp;
   const uint16_t* kb = keys + static_cast<int64_t>(b) * blocks * dim;
-  float kv[kBlocksPerWarp][8];
+  uint32_t raw[kBlocksPerWarp][PER / 2];  // the lane's PER BF16 values of each block
 #pragma unroll
   for (int u = 0; u < kBlocksPerWarp; ++u) {
     const int t = t0 + u;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) kv[u][j] = 0.f;
-    if (t >= blocks) continue;
-    const uint16_t* row = kb + static_cast<int64_t>(t) * dim + lane * per_lane;
-    for (int j = 0; j < per_lane; ++j) kv[u][j] = bf16_to_f32(row[j]);
+    const uint16_t* row = kb + static_cast<int64_t>(t < blocks ? t : 0) * dim + lane * PER;
+    if constexpr (PER == 8) {
+      const uint4 v = t < blocks ? *reinterpret_cast<const uint4*>(row) : make_uint4(0, 0, 0, 0);
+      raw[u][0] = v.x;
+      raw[u][1] = v.y;
+      raw[u][2] = v.z;
+      raw[u][3] = v.w;
+    } else if constexpr (PER == 4) {
+      const uint2 v = t < blocks ? *reinterpret_cast<const uint2*>(row) : make_uint2(0, 0);
+      raw[u][0] = v.x;
+      raw[u][1] = v.y;
+    } else {
+      raw[u][0] = t < blocks ? *reinterpret_cast<const uint32_t*>(row) : 0u;
+    }
   }
 #pragma unroll
   for (int u = 0; u < kBlocksPerWarp; ++u) {
     const int t = t0 + u;
     float score = 0.f;
     for (int h = 0; h < heads; ++h) {
+      const float* q = qs + h * dim + lane * PER;
       float dot = 0.f;
-      for (int j = 0; j < per_lane; ++j) dot = fmaf(qs[h * dim + lane * per_lane + j], kv[u][j], dot);
+#pragma unroll
+      for (int j = 0; j < PER; ++j)
+        dot = fmaf(q[j], bf16_to_f32(static_cast<uint16_t>(raw[u][j / 2] >> (16 * (j & 1)))), dot);
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
       score = __fadd_rn(score, fmaxf(dot, 0.f));
@@ -128,17 +143,40 @@ __global__ void __launch_bounds__(kSelThreads) qsa_select_kernel(const float* __
     for (int i = tid; i < 256; i += kSelThreads) hist[i] = 0;
     __syncthreads();
     const uint32_t prefix = s_prefix;
-    for (int i = tid; i < blocks; i += kSelThreads)
-      if ((keys[i] & mask) == prefix) atomicAdd(&hist[(keys[i] >> shift) & 255u], 1);
+    // one shared-memory atomic per distinct bin of a warp (scores that share their top bits
+    // would otherwise serialise on one counter)
+    for (int i = tid; i < blocks; i += kSelThreads) {
+      const uint32_t k = keys[i];
+      const uint32_t bin = (k & mask) == prefix ? (k >> shift) & 255u : 256u;
+      const unsigned peers = __match_any_sync(__activemask(), bin);
+      if (bin < 256u && (tid & 31) == __ffs(peers) - 1) atomicAdd(&hist[bin], __popc(peers));
+    }
     __syncthreads();
-    if (tid == 0) {
-      int acc = 0, need = s_remaining, bin = 255;
-      for (; bin > 0; --bin) {
-        if (acc + hist[bin] >= need) break;
-        acc += hist[bin];
+    if (tid < 32) {
+      // warp 0 finds the bin holding the need-th largest key: lane l sums bins 8l .. 8l + 7,
+      // a suffix scan gives the count above each lane's bins, and the lane whose bins
+      // reach `need` walks them from the top
+      const int lane = tid, need = s_remaining;
+      int mine = 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) mine += hist[8 * lane + j];
+      int suffix = mine;  // keys in the bins of this lane and every higher lane
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int n = __shfl_down_sync(0xffffffffu, suffix, o);
+        if (lane + o < 32) suffix += n;
       }
-      s_remaining = need - acc;  // how many keys of this bin (and prefix) still to take
-      s_prefix = prefix | (static_cast<uint32_t>(bin) << shift);
+      const int above = suffix - mine;  // keys in the bins of higher lanes
+      const bool here = above < need && suffix >= need;  // exactly one lane
+      if (here) {
+        int acc = above, bin = 8 * lane + 7;
+        for (; bin > 8 * lane; --bin) {
+          if (acc + hist[bin] >= need) break;
+          acc += hist[bin];
+        }
+        s_remaining = need - acc;  // how many keys of this bin (and prefix) still to take
+        s_prefix = prefix | (static_cast<uint32_t>(bin) << shift);
+      }
     }
     mask |= 255u << shift;
     __syncthreads();
@@ -177,35 +215,32 @@ __global__ void __launch_bounds__(kSelThreads) qsa_select_kernel(const float* __
       }
     }
   }
-  // pad to a power of two and sort by (key descending, index ascending)
-  int P = 1;
-  while (P < K) P <<= 1;
-  for (int i = K + tid; i < P; i += kSelThreads) {
-    sel_key[i] = 0;
-    sel_idx[i] = 0x7fffffff;
-  }
   __syncthreads();
-  for (int size = 2; size <= P; size <<= 1) {
+  // sort the K kept blocks by (key descending, index ascending): thread t holds element t of
+  // a 1024-entry bitonic network as one 64-bit value key << 32 | ~index (padding sorts last);
+  // strides below 32 exchange by warp shuffle, larger ones through shared memory
+  uint64_t v = tid < K ? (static_cast<uint64_t>(sel_key[tid]) << 32) | (0xffffffffu - static_cast<uint32_t>(sel_idx[tid]))
+                       : 0ull;
+  uint64_t* xch = reinterpret_cast<uint64_t*>(keys);  // the keys are no longer needed
+  for (int size = 2; size <= kSelThreads; size <<= 1) {
+    const bool desc = (tid & size) == 0;
     for (int stride = size >> 1; stride > 0; stride >>= 1) {
-      for (int i = tid; i < P; i += kSelThreads) {
-        const int j = i ^ stride;
-        if (j > i) {
-          // "before": higher key, or equal key and lower index
-          const bool i_first = sel_key[i] > sel_key[j] || (sel_key[i] == sel_key[j] && sel_idx[i] < sel_idx[j]);
-          const bool ascending_block = (i & size) == 0;  // this half sorts "before"-first
-          if (i_first != ascending_block) {
-            const uint32_t tk = sel_key[i];
-            sel_key[i] = sel_key[j];
-            sel_key[j] = tk;
-            const int ti = sel_idx[i];
-            sel_idx[i] = sel_idx[j];
-            sel_idx[j] = ti;
-          }
-        }
+      uint64_t other;
+      if (stride >= 32) {
+        __syncthreads();
+        xch[tid] = v;
+        __syncthreads();
+        other = xch[tid ^ stride];
+      } else {
+        other = __shfl_xor_sync(0xffffffffu, v, stride);
       }
-      __syncthreads();
+      const bool lower = (tid & stride) == 0;
+      v = (lower == desc) ? (v > other ? v : other) : (v < other ? v : other);
     }
   }
+  __syncthreads();
+  if (tid < K) sel_idx[tid] = static_cast<int32_t>(0xffffffffu - static_cast<uint32_t>(v));
+  __syncthreads();
   // expand to token indices and flags
   const int len1 = lengths[b] + 1, count = len1 / ratio;
   int32_t* out_i = indices + static_cast<int64_t>(b) * width;
@@ -239,8 +274,15 @@ int qk_qsa_block_scores(const uint16_t* query, const uint16_t* keys, const int32
   QK_REQUIRE(query && keys && lengths && scores, "null pointer");
   const int per_cta = kScoreWarps * kBlocksPerWarp;
   const dim3 grid((blocks + per_cta - 1) / per_cta, B);
-  qsa_scores_kernel<<<grid, kScoreWarps * 32, 0, as_stream(stream)>>>(
-      query, keys, lengths, heads, dim, blocks, ratio, static_cast<float>(std::sqrt(static_cast<double>(dim))), scores);
+  QK_REQUIRE((reinterpret_cast<uintptr_t>(keys) & 15) == 0, "keys must be 16-byte aligned");
+  const float root = static_cast<float>(std::sqrt(static_cast<double>(dim)));
+  const cudaStream_t st = as_stream(stream);
+  if (dim == 64)
+    qsa_scores_kernel<2><<<grid, kScoreWarps * 32, 0, st>>>(query, keys, lengths, heads, blocks, ratio, root, scores);
+  else if (dim == 128)
+    qsa_scores_kernel<4><<<grid, kScoreWarps * 32, 0, st>>>(query, keys, lengths, heads, blocks, ratio, root, scores);
+  else
+    qsa_scores_kernel<8><<<grid, kScoreWarps * 32, 0, st>>>(query, keys, lengths, heads, blocks, ratio, root, scores);
   QK_LAUNCHED("qsa_scores_kernel");
   return QK_OK;
 }
@@ -255,7 +297,8 @@ int qk_qsa_select(const float* scores, const int32_t* lengths, int B, int blocks
   if (B == 0) return QK_OK;
   QK_REQUIRE(scores && lengths && indices && valid, "null pointer");
   const int width = K * ratio + ratio - 1;
-  const size_t smem = static_cast<size_t>(blocks) * 4;
+  // keys [blocks] (4 B each), reused as the sort's 1024 x 8 B exchange buffer
+  const size_t smem = std::max(static_cast<size_t>(blocks) * 4, static_cast<size_t>(kSelThreads) * 8);
   if (int rc = allow_smem(reinterpret_cast<const void*>(qsa_select_kernel), smem)) return rc;
   qsa_select_kernel<<<B, kSelThreads, smem, as_stream(stream)>>>(scores, lengths, blocks, ratio, K, width, indices,
                                                                  valid);

@@ -21,8 +21,9 @@ namespace {
 
 constexpr int kTok = 8;
 constexpr int kCluster = 8;
+constexpr int kWarps = 16;  // warps per CTA (each takes two router rows at a time)
 
-__global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(256)
+__global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kWarps * 32)
     router_kernel(const uint16_t* __restrict__ x, const float* __restrict__ w, const float* __restrict__ logits_in,
                   const uint8_t* __restrict__ active, int T, int H, int E, int k, int32_t* __restrict__ ids,
                   uint16_t* __restrict__ weights, float* __restrict__ probs_out) {
@@ -50,9 +51,9 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(256)
     // Each warp takes two router rows at a time and keeps kU 16-byte loads per row in flight
     // (the loads are issued before the FMAs that use them); every lane still adds its
     // columns h = 4 lane + 128 i in increasing i, so the logits do not depend on kU.
-    constexpr int kU = 4;
-    for (int ea = e0 + warp; ea < e1; ea += 16) {
-      const int eb = ea + 8;
+    constexpr int kU = 8;
+    for (int ea = e0 + warp; ea < e1; ea += 2 * kWarps) {
+      const int eb = ea + kWarps;
       const bool has_b = eb < e1;
       float acc[2][kTok];
 #pragma unroll
@@ -181,7 +182,7 @@ static int router_launch(const uint16_t* x, const float* w, const float* logits,
   int rc = allow_smem(reinterpret_cast<const void*>(router_kernel), smem);
   if (rc) return rc;
   const int blocks = (T + kTok - 1) / kTok;
-  const cudaError_t e = launch_dependent(router_kernel, dim3(blocks * kCluster), dim3(256), smem, as_stream(stream), x, w,
+  const cudaError_t e = launch_dependent(router_kernel, dim3(blocks * kCluster), dim3(kWarps * 32), smem, as_stream(stream), x, w,
                                          logits, active, T, H, E, k, ids, weights, probs);
   if (e != cudaSuccess) return cuda_error(e, "router_kernel");
   count_launch();

@@ -122,6 +122,36 @@ def read_quantized(cache, name, indices, c, dtype, *, scale_gather=None):
     return out
 
 
+def select_tokens_from_keys(query, keys, lengths, *, ratio=4, budget=2048):
+    """The selection half of ``attention_cache.py:84-125`` (``select_tokens``) once the block
+    keys are current: ``query`` BF16 ``[B, indexer_heads, indexer_dim]`` (normed and rotated),
+    ``keys`` BF16 ``[B, blocks, indexer_dim]``, ``lengths`` ``[B]`` -> ``(indices int32, valid
+    bool)`` ``[B, K * ratio + ratio - 1]`` with ``K = min(budget // ratio, blocks)``, ready for
+    :func:`decode_attention` (``valid=``)."""
+    if budget < ratio or budget % ratio or ratio < 2:
+        raise ValueError("Invalid sparse attention indexer dimensions or budget")
+    if query.dtype != torch.bfloat16 or keys.dtype != torch.bfloat16:
+        raise TypeError("query and keys must be BF16")
+    batch, heads, dim = query.shape
+    if keys.dim() != 3 or keys.shape[0] != batch or keys.shape[2] != dim:
+        raise ValueError("keys must be [B, blocks, indexer_dim]")
+    blocks = keys.shape[1]
+    device = query.device
+    K = min(budget // ratio, blocks)
+    lens = lengths.to(device=device, dtype=torch.int32).contiguous()
+    scores = torch.empty((batch, blocks), dtype=torch.float32, device=device)
+    indices = torch.empty((batch, K * ratio + ratio - 1), dtype=torch.int32, device=device)
+    valid = torch.empty(indices.shape, dtype=torch.uint8, device=device)
+    q, k = query.contiguous(), keys.contiguous()
+    with torch.cuda.device(device):
+        st = _lib.stream_handle(device)
+        _lib.call("qk_qsa_block_scores", _lib.ptr(q), _lib.ptr(k), _lib.ptr(lens), batch, heads, dim, blocks,
+                  ratio, _lib.ptr(scores), st)
+        _lib.call("qk_qsa_select", _lib.ptr(scores), _lib.ptr(lens), batch, blocks, ratio, budget,
+                  _lib.ptr(indices), _lib.ptr(valid), st)
+    return indices, valid.bool()
+
+
 class DecodeAttention:
     """Split-KV decode attention over the Q8 cache with a cached workspace."""
 

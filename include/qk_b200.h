@@ -253,6 +253,21 @@ int qk_kv_q8_decode_attention_partial(const uint16_t* q, const int8_t* k_codes,
 int qk_kv_q8_attention_combine(const float* parts, int R, int B, int hq, int head_dim,
                                const uint16_t* gate, uint16_t* out, qk_stream_t stream);
 
+/* ---- sparse token selection (QSA indexer) -------------------------------------
+ * Replaces the selection half of attention_cache.py:84-125 select_tokens, once the block
+ * keys are current. qk_qsa_block_scores: query BF16 [B, heads, dim] (normed, rotated),
+ * keys BF16 [B, blocks, dim] (16-byte aligned), lengths int32 [B] -> scores FP32
+ * [B, blocks] = sum_h relu(q_h . k_t) / sqrt(dim) for t < (lengths + 1) / ratio, else -inf
+ * (:100-114). heads <= 8, dim in {64, 128, 256}. qk_qsa_select: top K = min(budget / ratio,
+ * blocks) blocks per row (lax.top_k order: score descending, ties to the lower block) ->
+ * indices int32 / valid uint8 [B, K * ratio + ratio - 1]: the selected blocks' tokens, then
+ * the ratio - 1 tail tokens, invalid entries index 0 (:115-124). blocks <= 16384, K <= 1024. */
+int qk_qsa_block_scores(const uint16_t* query, const uint16_t* keys, const int32_t* lengths, int B,
+                        int heads, int dim, int blocks, int ratio, float* scores,
+                        qk_stream_t stream);
+int qk_qsa_select(const float* scores, const int32_t* lengths, int B, int blocks, int ratio,
+                  int budget, int32_t* indices, uint8_t* valid, qk_stream_t stream);
+
 /* ---- decoder-layer glue around the path -----------------------------------------
  * The per-token steps on either side of the routed FFN and the decode attention in a
  * decoder layer, one launch each over all rows (BF16 storage bits throughout). */

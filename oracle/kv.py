@@ -148,3 +148,36 @@ def combine_partials(parts, batch, hq, hd, gate=None):
     if gate is not None:
         out = bf16_round((out * bf16_round(sigmoid(gate))).astype(np.float32))
     return out
+
+
+def qsa_scores(query, keys, lengths, ratio):
+    """``attention_cache.py:100-114``: ``sum_h relu(q_h . k_t) / sqrt(dim)`` (FP32 values from an
+    exact dot), ``-inf`` for blocks ``t >= (lengths + 1) // ratio``."""
+    q = np.asarray(query, np.float64)
+    k = np.asarray(keys, np.float64)
+    dots = np.einsum("bhd,btd->bth", q, k).astype(np.float32)
+    scores = (np.maximum(dots, 0).astype(np.float64).sum(-1) / np.sqrt(q.shape[-1])).astype(np.float32)
+    count = (np.asarray(lengths) + 1) // ratio
+    return np.where(np.arange(k.shape[1])[None, :] < count[:, None], scores, np.float32(-np.inf)).astype(np.float32)
+
+
+def qsa_select(scores, lengths, ratio, budget):
+    """``attention_cache.py:115-124``: ``lax.top_k`` (score descending, ties to the lower
+    block), then the selected blocks' tokens and the tail tokens, invalid entries index 0."""
+    scores = np.asarray(scores, np.float32)
+    batch, blocks = scores.shape
+    K = min(budget // ratio, blocks)
+    lengths = np.asarray(lengths)
+    count = (lengths + 1) // ratio
+    out_i, out_v = [], []
+    for b in range(batch):
+        order = np.lexsort((np.arange(blocks), -scores[b].astype(np.float64)))[:K]
+        tokens = (order[:, None] * ratio + np.arange(ratio)).reshape(-1)
+        ok = np.repeat(order < count[b], ratio)
+        tail = count[b] * ratio + np.arange(ratio - 1)
+        tail_ok = np.arange(ratio - 1) < (lengths[b] + 1) % ratio
+        idx = np.concatenate([tokens, tail])
+        val = np.concatenate([ok, tail_ok])
+        out_i.append(np.where(val, idx, 0).astype(np.int32))
+        out_v.append(val)
+    return np.stack(out_i), np.stack(out_v)
