@@ -187,3 +187,105 @@ int qk_append_shared_route(const int32_t* ids, const uint16_t* weights, int B, i
 }
 
 }  // extern "C"
+
+// ---- greedy sampling with a non-finite check (qwen38_tpu/run.py:46-55 checked_argmax) ----
+namespace qk {
+namespace {
+
+constexpr int kArgThreads = 1024;
+
+// (value, index) pair order of jnp.argmax: NaN above everything, then larger value, then the
+// lower index.
+__device__ __forceinline__ bool arg_better(float a, int ia, float b, int ib) {
+  const bool na = a != a, nb = b != b;
+  if (na || nb) return na && (!nb || ia < ib);
+  return a > b || (a == b && ia < ib);
+}
+
+template <typename T>
+__device__ __forceinline__ float logit_at(const T* row, int64_t i);
+template <>
+__device__ __forceinline__ float logit_at<uint16_t>(const uint16_t* row, int64_t i) {
+  return bf16_to_f32(row[i]);
+}
+template <>
+__device__ __forceinline__ float logit_at<float>(const float* row, int64_t i) {
+  return row[i];
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kArgThreads) checked_argmax_kernel(const T* __restrict__ logits, int64_t V,
+                                                                     int32_t* __restrict__ out) {
+  __shared__ float sv[32];
+  __shared__ int si[32], sc[32];
+  pdl_wait();
+  const int64_t b = blockIdx.x;
+  const T* row = logits + b * V;
+  float best = -INFINITY;
+  int bi = 0x7fffffff, bad = 0;
+  for (int64_t i = threadIdx.x; i < V; i += kArgThreads) {
+    const float v = logit_at<T>(row, i);
+    bad += !isfinite(v);
+    if (arg_better(v, static_cast<int>(i), best, bi)) {
+      best = v;
+      bi = static_cast<int>(i);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    bad += __shfl_xor_sync(0xffffffffu, bad, o);
+    if (arg_better(ov, oi, best, bi)) {
+      best = ov;
+      bi = oi;
+    }
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) {
+    sv[warp] = best;
+    si[warp] = bi;
+    sc[warp] = bad;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    best = sv[lane];
+    bi = si[lane];
+    bad = sc[lane];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      bad += __shfl_xor_sync(0xffffffffu, bad, o);
+      if (arg_better(ov, oi, best, bi)) {
+        best = ov;
+        bi = oi;
+      }
+    }
+    if (lane == 0) {
+      out[2 * b] = bi;
+      out[2 * b + 1] = bad;
+    }
+  }
+}
+
+}  // namespace
+}  // namespace qk
+
+extern "C" int qk_checked_argmax(const void* logits, int in_dtype, int B, int64_t V, int32_t* out,
+                                 qk_stream_t stream) {
+  using namespace qk;
+  QK_REQUIRE(B >= 0 && V > 0 && V < (int64_t{1} << 31), "invalid logits geometry");
+  QK_REQUIRE(in_dtype == QK_OUT_F32 || in_dtype == QK_OUT_BF16, "logits must be FP32 or BF16");
+  if (B == 0) return QK_OK;
+  QK_REQUIRE(logits && out, "null pointer");
+  const cudaError_t e =
+      in_dtype == QK_OUT_BF16
+          ? launch_dependent(checked_argmax_kernel<uint16_t>, dim3(B), dim3(kArgThreads), 0, as_stream(stream),
+                             static_cast<const uint16_t*>(logits), V, out)
+          : launch_dependent(checked_argmax_kernel<float>, dim3(B), dim3(kArgThreads), 0, as_stream(stream),
+                             static_cast<const float*>(logits), V, out);
+  if (e != cudaSuccess) return cuda_error(e, "checked_argmax_kernel");
+  count_launch();
+  return QK_OK;
+}

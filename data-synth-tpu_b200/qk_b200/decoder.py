@@ -38,6 +38,20 @@ from .parallel import expert_shape, put_expert_bytes
 from .quant import BLOCK_LAYOUTS, GGML_TYPE, normalize_qtype
 
 
+def checked_argmax(logits):
+    """``run.py:46-55``: per row ``(argmax, count of non-finite logits)`` as int32 ``[B, 2]``;
+    the first maximum wins and a NaN counts as the maximum (``jnp.argmax``)."""
+    if logits.dim() != 2 or logits.dtype not in (torch.bfloat16, torch.float32):
+        raise TypeError("logits must be a BF16 or FP32 [B, V] tensor")
+    logits = logits.contiguous()
+    out = torch.empty((logits.shape[0], 2), dtype=torch.int32, device=logits.device)
+    code = _lib.QK_OUT_BF16 if logits.dtype == torch.bfloat16 else _lib.QK_OUT_F32
+    with torch.cuda.device(logits.device):
+        _lib.call("qk_checked_argmax", _lib.ptr(logits), code, logits.shape[0], logits.shape[1], _lib.ptr(out),
+                  _lib.stream_handle(logits.device))
+    return out
+
+
 @dataclass(frozen=True)
 class StackConfig:
     layers: int = 48

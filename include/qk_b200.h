@@ -295,6 +295,13 @@ int qk_append_shared_route(const int32_t* ids, const uint16_t* weights, int B, i
                            int shared_id, int32_t* ids_out, uint16_t* weights_out,
                            qk_stream_t stream);
 
+/* qwen38_tpu/run.py:46-55 checked_argmax(logits): out int32 [B, 2] = (argmax over the V
+ * logits of the row - the first maximum, a NaN counting as the maximum, as jnp.argmax -
+ * and the number of non-finite logits in the row). logits: [B, V] FP32 or BF16 (in_dtype
+ * QK_OUT_F32 / QK_OUT_BF16). */
+int qk_checked_argmax(const void* logits, int in_dtype, int B, int64_t V, int32_t* out,
+                      qk_stream_t stream);
+
 /* No counterpart in the reference. QK_ERR_TIMEOUT if a bounded device wait of an earlier
  * qk_kv_q8_decode_attention on this device gave up (its output is then not valid), else
  * QK_OK; clears the flag. Synchronises `stream`. */

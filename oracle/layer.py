@@ -94,3 +94,10 @@ def decode_step(x, layers, caches, indices, positions, cfg):
                            down_type=cfg.qtype, hidden=cfg.hidden, intermediate=cfg.intermediate)
         x = bf16_round((x + y).astype(np.float32))
     return x
+
+
+def checked_argmax(logits):
+    """``run.py:46-55``: ``(argmax, count of non-finite)`` per row; NumPy's argmax takes the
+    first maximum and treats NaN as the maximum, as ``jnp.argmax`` does."""
+    logits = np.asarray(logits, np.float32)
+    return np.stack([np.argmax(logits, -1), np.sum(~np.isfinite(logits), -1)], -1).astype(np.int32)

@@ -87,6 +87,27 @@ def test_residual_add_and_shared_route(cuda_device):
     assert np.max(np.abs(got_w[:, 4] - gate)) <= 2 ** -8  # one BF16 step of a value in (0, 1)
 
 
+@pytest.mark.parametrize("dtype", ["bf16", "f32"])
+def test_checked_argmax(cuda_device, dtype):
+    import torch
+
+    from qk_b200.decoder import checked_argmax
+
+    rng = np.random.default_rng(6)
+    V = 151936
+    logits = bf16_round(rng.normal(size=(6, V)).astype(np.float32))
+    logits[1, [5, 70000, 151935]] = 9.0            # tied maximum: the first one
+    logits[2, 1234] = np.nan                        # a NaN is the maximum
+    logits[2, 99] = np.inf
+    logits[3, :] = np.nan                           # all NaN: index 0, V non-finite
+    logits[4, :] = -np.inf                          # all -inf: index 0
+    logits[5, [7, 8]] = [np.inf, np.inf]            # +inf ties
+    t = torch.from_numpy(logits).to(cuda_device)
+    got = checked_argmax(t.bfloat16() if dtype == "bf16" else t).cpu().numpy()
+    np.testing.assert_array_equal(got, layer.checked_argmax(logits))
+    assert got[3].tolist() == [0, V] and got[1, 0] == 5 and got[2].tolist() == [1234, 2]
+
+
 def _np(t):
     return to_f32(t) if t.dtype == __import__("torch").bfloat16 else t.float().cpu().numpy()
 
