@@ -53,7 +53,8 @@ struct Workspace {
 inline size_t align256(size_t n) { return (n + 255) & ~size_t(255); }
 
 // Activation-tile rows: each active expert's entries rounded up to 16 per chunk.
-// Token chunks: each active expert's entries in runs of kMaxTok.
+// Token chunks: each active expert's entries in runs of kMaxTok (or of kWideTok; the
+// narrow chunks bound both).
 inline size_t chunks_bound(const qk_moe_desc& d, int max_tokens) {
   const size_t R = static_cast<size_t>(max_tokens) * d.top_k;
   const size_t E = static_cast<size_t>(d.num_experts);
@@ -114,7 +115,7 @@ size_t layout(const qk_moe_desc& d, int max_tokens, uint8_t* base, Workspace* ws
 constexpr int kStagedRoutes = 4096;
 
 __global__ void __launch_bounds__(1024) moe_route_kernel(const int32_t* ids, const uint16_t* weights,
-                                                         int B, int k, int E, int first,
+                                                         int B, int k, int E, int first, int ctok,
                                                          Workspace ws) {
   extern __shared__ int32_t sh[];
   pdl_wait();     // launched as a programmatic dependent: the routes' producer first
@@ -198,15 +199,15 @@ __global__ void __launch_bounds__(1024) moe_route_kernel(const int32_t* ids, con
       ws.meta->status = 0;
     }
     __syncwarp();
-    // Token chunks (<= kMaxTok entries of one expert) and their activation-tile rows
+    // Token chunks (<= ctok entries of one expert) and their activation-tile rows
     // (each chunk padded to a multiple of 16 rows), in active-expert order.
     const int n_act = active_base[32];
     const int per2 = (n_act + 31) / 32, lo2 = min(n_act, tid * per2), hi2 = min(n_act, lo2 + per2);
     int ch_sum = 0, row_sum = 0;
     for (int a = lo2; a < hi2; ++a) {
-      const int m = counts[ws.active[a]], nch = (m + kMaxTok - 1) / kMaxTok;
+      const int m = counts[ws.active[a]], nch = (m + ctok - 1) / ctok;
       ch_sum += nch;
-      row_sum += kMaxTok * (nch - 1) + (((m - kMaxTok * (nch - 1)) + 15) & ~15);
+      row_sum += ctok * (nch - 1) + (((m - ctok * (nch - 1)) + 15) & ~15);
     }
     int ch_incl = ch_sum, row_incl = row_sum;
     for (int o = 1; o < 32; o <<= 1) {
@@ -218,11 +219,11 @@ __global__ void __launch_bounds__(1024) moe_route_kernel(const int32_t* ids, con
     }
     int cb = ch_incl - ch_sum, rb = row_incl - row_sum;
     for (int a = lo2; a < hi2; ++a) {
-      const int m = counts[ws.active[a]], nch = (m + kMaxTok - 1) / kMaxTok;
+      const int m = counts[ws.active[a]], nch = (m + ctok - 1) / ctok;
       ws.chunk_off[a] = cb;
       ws.row_off[a] = rb;
       cb += nch;
-      rb += kMaxTok * (nch - 1) + (((m - kMaxTok * (nch - 1)) + 15) & ~15);
+      rb += ctok * (nch - 1) + (((m - ctok * (nch - 1)) + 15) & ~15);
     }
     if (tid == 31) {
       ws.chunk_off[n_act] = ch_incl;
@@ -238,10 +239,10 @@ __global__ void __launch_bounds__(1024) moe_route_kernel(const int32_t* ids, con
   {
     const int n_act = ws.meta->n_active;
     for (int a = tid; a < n_act; a += nt) {
-      const int e = ws.active[a], m = counts[e], nch = (m + kMaxTok - 1) / kMaxTok;
+      const int e = ws.active[a], m = counts[e], nch = (m + ctok - 1) / ctok;
       const int c0 = ws.chunk_off[a], r0 = ws.row_off[a], e0 = offsets[e];
       for (int ch = 0; ch < nch; ++ch)
-        ws.chunk_rec[c0 + ch] = make_int4(e, min(kMaxTok, m - kMaxTok * ch), e0 + kMaxTok * ch, r0 + kMaxTok * ch);
+        ws.chunk_rec[c0 + ch] = make_int4(e, min(ctok, m - ctok * ch), e0 + ctok * ch, r0 + ctok * ch);
     }
   }
 
@@ -273,18 +274,18 @@ __global__ void __launch_bounds__(1024) moe_route_kernel(const int32_t* ids, con
 // ------------------------------------------------------------------------------------
 // 2. dispatch: x rows of every chunk into the swizzled activation tiles (zero padding rows)
 // ------------------------------------------------------------------------------------
-__global__ void __launch_bounds__(256) moe_dispatch_kernel(const uint16_t* __restrict__ x, int H,
+__global__ void __launch_bounds__(256) moe_dispatch_kernel(const uint16_t* __restrict__ x, int H, int ctok,
                                                            Workspace ws) {
   // One warp per (token chunk, tile row): the chunk's record gives the row's place; the
   // lanes load the row's 16-byte pieces (H / 8 of them) eight at a time before storing them
   // into the swizzled tile. Rows past the chunk's tokens (up to the 16-row padding) are zero.
   constexpr int kU = 8;
   pdl_wait();
-  const int n_rows = ws.meta->n_chunks * kMaxTok;
+  const int n_rows = ws.meta->n_chunks * ctok;
   const int lane = threadIdx.x & 31, cpr = H / 8, nkb = H / 256;
   const int warps = gridDim.x * (blockDim.x >> 5);
   for (int g = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); g < n_rows; g += warps) {
-    const int ci = g / kMaxTok, rr = g % kMaxTok;
+    const int ci = g / ctok, rr = g % ctok;
     const int4 rec = ws.chunk_rec[ci];  // {expert, tokens, first entry, first tile row}
     const int ntok = rec.y, r16 = (ntok + 15) & ~15;
     if (rr >= r16) continue;
@@ -461,12 +462,16 @@ static int moe_forward_impl(const qk_moe_desc* desc, const uint8_t* gate, const 
   }
   mark(0);
   const size_t routes = static_cast<size_t>(B) * d.top_k;
+  // The wide form (128-token chunks) when the routes average at least 64 tokens per expert
+  // the rank holds (prefill-sized batches); the narrow form (32-token chunks) otherwise.
+  const bool wide = routes >= 64 * static_cast<size_t>(d.num_experts);
+  const int ctok = wide ? kWideTok : kMaxTok;
   const size_t route_smem = (3 * static_cast<size_t>(d.num_experts) + 1) * 4 + (routes <= kStagedRoutes ? routes * 6 : 0);
   int rc = allow_smem(reinterpret_cast<const void*>(moe_route_kernel), route_smem);
   if (rc) return rc;
   {
     const cudaError_t e = launch_dependent(moe_route_kernel, dim3(1), dim3(1024), route_smem, st, ids, weights, B,
-                                           d.top_k, d.num_experts, d.first_expert, ws);
+                                           d.top_k, d.num_experts, d.first_expert, ctok, ws);
     if (e != cudaSuccess) return cuda_error(e, "moe_route_kernel");
     count_launch(1);
   }
@@ -477,7 +482,7 @@ static int moe_forward_impl(const qk_moe_desc* desc, const uint8_t* gate, const 
   if (dgrid > sms * 8) dgrid = sms * 8;
   {
     const cudaError_t e = launch_dependent(moe_dispatch_kernel, dim3(static_cast<unsigned>(dgrid)), dim3(256), 0, st,
-                                           x, d.hidden, ws);
+                                           x, d.hidden, ctok, ws);
     if (e != cudaSuccess) return cuda_error(e, "moe_dispatch_kernel");
     count_launch(1);
   }
@@ -517,10 +522,17 @@ static int moe_forward_impl(const qk_moe_desc* desc, const uint8_t* gate, const 
   dn.entry_route = ws.entry_route;
   dn.nrows = d.hidden;
   mark(1);
-  rc = q6 ? launch_umma<QType::Q6_K, kModeGateUp>(gu, sms, st) : launch_umma<QType::Q4_K, kModeGateUp>(gu, sms, st);
+  if (wide)
+    rc = q6 ? launch_umma<QType::Q6_K, kModeGateUp, true>(gu, sms, st)
+            : launch_umma<QType::Q4_K, kModeGateUp, true>(gu, sms, st);
+  else
+    rc = q6 ? launch_umma<QType::Q6_K, kModeGateUp>(gu, sms, st) : launch_umma<QType::Q4_K, kModeGateUp>(gu, sms, st);
   if (rc) return rc;
   mark(2);
-  rc = q6 ? launch_umma<QType::Q6_K, kModeDown>(dn, sms, st) : launch_umma<QType::Q4_K, kModeDown>(dn, sms, st);
+  if (wide)
+    rc = q6 ? launch_umma<QType::Q6_K, kModeDown, true>(dn, sms, st) : launch_umma<QType::Q4_K, kModeDown, true>(dn, sms, st);
+  else
+    rc = q6 ? launch_umma<QType::Q6_K, kModeDown>(dn, sms, st) : launch_umma<QType::Q4_K, kModeDown>(dn, sms, st);
   if (rc) return rc;
   mark(3);
   if (phase == kPartial) return QK_OK;

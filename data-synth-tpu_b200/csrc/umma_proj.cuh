@@ -1,7 +1,8 @@
 // Packed-weight projection on the 5th-generation tensor core (tcgen05), decode regime.
 //
-// Work item: one token chunk (<= kMaxTok routed rows of one expert, or of x) times one
-// 128-row MMA tile of the weight matrix, over the item's K blocks. The 128-row A operand
+// Work item: one token chunk (<= 32 routed rows of one expert, <= 128 in the wide form, or
+// up to 32 rows of x) times one 128-row MMA tile of the weight matrix, over the item's K
+// blocks. The 128-row A operand
 // is two 64-row weight tiles with interleaved rows: TMEM lane L holds row L >> 1 of tile
 // L & 1. For gate/up the two tiles are the gate and up rows of the same 64 rows of I, so
 // the SwiGLU partners sit in neighbouring lanes; for down / dense they are rows
@@ -34,8 +35,9 @@
 //               and write h = SwiGLU (gate/up), y (down) or the FP32 output (dense).
 // TMEM: A buffers [0, 384) (3 x 128 columns = 256 BF16 of K per lane; three, so a decode
 // group never waits for the MMA of the stage it decoded last), accumulators [384, 512)
-// (4 issuers x kMaxTok columns). Every wait is bounded; on give-up the CTA records
-// QK_ERR_TIMEOUT in `status` and leaves its loops.
+// (4 issuers x 32 columns; the wide form: 1 issuer x 128 columns, the epilogue reading them
+// 32 columns at a time). Every wait is bounded; on give-up the CTA records QK_ERR_TIMEOUT in
+// `status` and leaves its loops.
 #pragma once
 
 #include "rowtile.cuh"
@@ -59,20 +61,37 @@ constexpr int kMmaWarp0 = 17;
 constexpr int kMmaIssuers = QK_UMMA_ISSUERS;  // each takes 16 / kMmaIssuers of a block's 16 K steps
 constexpr int kABuffers = QK_UMMA_ABUF;
 constexpr int kDBuffers = QK_UMMA_DBUF;
-static_assert(16 % kMmaIssuers == 0 && 16 / kMmaIssuers >= 4, "issuers take whole 64-value K atoms");
-static_assert(kABuffers * 128 + kDBuffers * kMmaIssuers * 32 <= 512, "TMEM columns");
-constexpr int kEpilogueWarp0 = kMmaWarp0 + kMmaIssuers;
-constexpr int kUmmaThreads = (kEpilogueWarp0 + 4) * 32;
-constexpr int kMaxTok = 32;           // tokens per chunk (MMA N <= 32)
+constexpr int kMaxTok = 32;           // tokens per chunk of the narrow (decode) form (MMA N <= 32)
+constexpr int kWideTok = 128;         // tokens per chunk of the wide (many tokens per expert) form
 constexpr int kXGranule = 16 * 512;   // activation tile of 16 tokens x one K block
-constexpr int kXGranules = 8;         // activation ring: 64 KB
 constexpr int kXSlots = 8;            // stages that can hold activation granules at once
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kAccCol = kABuffers * 128;
 
 enum { kModeGateUp = 0, kModeDown = 1, kModeDense = 2 };
 
-template <QType QT>
+// The two forms of the pass. Narrow: chunks of <= 32 tokens, kMmaIssuers MMA-issuing warps
+// (one per scheduler; small-N MMAs are issue-bound), a 64 KB activation ring. Wide: chunks
+// of <= 128 tokens, so an expert's weights are decoded once per 128 tokens instead of once
+// per 32, one issuer (an M=128, N=128 MMA keeps the tensor pipe busy for its issue time),
+// and a 128 KB activation ring (two stages of 128 tokens).
+template <bool W>
+struct Form {
+  static constexpr int kTok = W ? kWideTok : kMaxTok;
+  static constexpr int kIssuers = W ? 1 : kMmaIssuers;
+  static constexpr int kXGranules = W ? 16 : 8;
+  // TMEM: A buffers of 128 columns, then the accumulators. (Two A and two accumulator
+  // buffers for the wide form measured the same as three and one.)
+  static constexpr int kABuf = W ? 3 : kABuffers;
+  static constexpr int kDBuf = W ? 1 : kDBuffers;
+  static constexpr uint32_t kAccCol = kABuf * 128;
+  static constexpr int kEpilogueWarp0 = kMmaWarp0 + kIssuers;
+  static constexpr int kThreads = (kEpilogueWarp0 + 4) * 32;
+  static_assert(16 % kIssuers == 0 && 16 / kIssuers >= 4, "issuers take whole 64-value K atoms");
+  static_assert(kABuf * 128 + kDBuf * kIssuers * kTok <= 512, "TMEM columns");
+};
+constexpr int kUmmaThreads = Form<false>::kThreads;
+
+template <QType QT, bool W = false>
 struct UCfg {
   static constexpr int kTile = HalfTile<QT>::kBytes;
   // The second tile starts 64 bytes past a 128-byte boundary, so the two 16-row halves a
@@ -82,8 +101,8 @@ struct UCfg {
   // Activation ring (1024-aligned granules at the start) and weight ring. The weight ring
   // gets the rest: at ~2.7 us loaded HBM latency an SM needs ~130 KB of weights in flight
   // to take its share of the HBM bandwidth, besides the two stages being decoded.
-  static constexpr int kXBytes = kXGranules * kXGranule;
-  static constexpr int kWStages = (225 * 1024 - kXBytes) / kWStageBytes;  // 6 (Q6_K), 8 (Q4_K)
+  static constexpr int kXBytes = Form<W>::kXGranules * kXGranule;
+  static constexpr int kWStages = (225 * 1024 - kXBytes) / kWStageBytes;  // narrow 6 (Q6_K), 8 (Q4_K)
   static constexpr size_t kWOff = kXBytes;
   static constexpr size_t kBarOff = kWOff + static_cast<size_t>(kWStages) * kWStageBytes;
   static constexpr size_t kSmem = 1024 + kBarOff + 512;
@@ -193,11 +212,18 @@ __device__ __forceinline__ int item_tiles(const UArgs& A, int e, int p, const ui
   return rt1 < A.tiles64 ? 2 : 1;
 }
 
-template <QType QT, int MODE>
-__global__ void __launch_bounds__(kUmmaThreads, 1) umma_proj_kernel(const UArgs A) {
-  using Cfg = UCfg<QT>;
+template <QType QT, int MODE, bool W = false>
+__global__ void __launch_bounds__(Form<W>::kThreads, 1) umma_proj_kernel(const UArgs A) {
+  using Cfg = UCfg<QT, W>;
   using HT = HalfTile<QT>;
   constexpr int SW = Cfg::kWStages;
+  constexpr int NI = Form<W>::kIssuers;       // MMA-issuing warps
+  constexpr int TOK = Form<W>::kTok;          // tokens per chunk (accumulator columns per issuer)
+  constexpr int XG = Form<W>::kXGranules;     // activation ring granules
+  constexpr int EW0 = Form<W>::kEpilogueWarp0;
+  constexpr int AB = Form<W>::kABuf;          // A buffers
+  constexpr int DB = Form<W>::kDBuf;          // accumulator buffers
+  constexpr uint32_t kAccCol = Form<W>::kAccCol;
   constexpr int TB = Cfg::kTile;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -208,10 +234,10 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) umma_proj_kernel(const UArgs 
   uint64_t* xfull = wempty + SW;
   uint64_t* xempty = xfull + kXSlots;
   uint64_t* afull = xempty + kXSlots;
-  uint64_t* aempty = afull + kABuffers;
-  uint64_t* dfull = aempty + kABuffers;
-  uint64_t* dempty = dfull + kDBuffers;
-  volatile uint32_t* xoff = reinterpret_cast<volatile uint32_t*>(dempty + kDBuffers);  // [kXSlots] granule of each stage
+  uint64_t* aempty = afull + AB;
+  uint64_t* dfull = aempty + AB;
+  uint64_t* dempty = dfull + DB;
+  volatile uint32_t* xoff = reinterpret_cast<volatile uint32_t*>(dempty + DB);  // [kXSlots] granule of each stage
   uint32_t* tmem_sh = const_cast<uint32_t*>(xoff + kXSlots);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -224,14 +250,14 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) umma_proj_kernel(const UArgs 
     }
     for (int s = 0; s < kXSlots; ++s) {
       mbar_init(&xfull[s], 1);
-      mbar_init(&xempty[s], kMmaIssuers);  // the MMA commits
+      mbar_init(&xempty[s], NI);  // the MMA commits
     }
-    for (int i = 0; i < kABuffers; ++i) {
+    for (int i = 0; i < AB; ++i) {
       mbar_init(&afull[i], kDecodeWarps / 2);
-      mbar_init(&aempty[i], kMmaIssuers);
+      mbar_init(&aempty[i], NI);
     }
-    for (int i = 0; i < kDBuffers; ++i) {
-      mbar_init(&dfull[i], kMmaIssuers);
+    for (int i = 0; i < DB; ++i) {
+      mbar_init(&dfull[i], NI);
       mbar_init(&dempty[i], 4);
     }
     fence_mbar_init();
@@ -253,8 +279,8 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) umma_proj_kernel(const UArgs 
     if (lane == 0) {
       const uint64_t wpol = l2_evict_first_policy(), xpol = l2_evict_last_policy();
       uint32_t sc = 0;
-      uint32_t xlo = 0, xused = 0, xhead = 0, xcnt = 0;  // granule ring: oldest live stage, granules
-                                                          // held, next free granule, 2-bit counts
+      uint32_t xlo = 0, xused = 0, xhead = 0;  // granule ring: oldest live stage, granules held,
+      uint64_t xcnt = 0;                         // next free granule, 8-bit counts per stage slot
       for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
         const ItemInfo it = item_info(A, item);
         const ChunkInfo c = chunk_info<MODE>(A, it.ci);
@@ -267,14 +293,14 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) umma_proj_kernel(const UArgs 
         for (int i = 0; i < it.kb1 - it.kb0 && ok; ++i, ++sc) {
           const int kb = it.kblock(i);
           // activation granules: contiguous, skipping a tail granule too short for the tile
-          const uint32_t off = xhead + g > kXGranules ? 0u : xhead;
-          const uint32_t need = g + (off == 0u && xhead != 0u ? kXGranules - xhead : 0u);
-          while (xused + need > kXGranules || sc - xlo >= kXSlots) {
+          const uint32_t off = xhead + g > XG ? 0u : xhead;
+          const uint32_t need = g + (off == 0u && xhead != 0u ? XG - xhead : 0u);
+          while (xused + need > XG || sc - xlo >= kXSlots) {
             if (!mbar_wait_bounded(&xempty[xlo % kXSlots], (xlo / kXSlots) & 1)) {
               ok = false;
               break;
             }
-            xused -= (xcnt >> (2 * (xlo % kXSlots))) & 3u;
+            xused -= static_cast<uint32_t>(xcnt >> (8 * (xlo % kXSlots))) & 255u;
             ++xlo;
           }
           const int s = sc % SW;
@@ -283,9 +309,9 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) umma_proj_kernel(const UArgs 
             break;
           }
           const uint32_t j = sc % kXSlots;
-          xcnt = (xcnt & ~(3u << (2 * j))) | (need << (2 * j));
+          xcnt = (xcnt & ~(uint64_t{255} << (8 * j))) | (static_cast<uint64_t>(need) << (8 * j));
           xused += need;
-          xhead = (off + g) % kXGranules;
+          xhead = (off + g) % XG;
           xoff[j] = off;
           mbar_expect_tx(&xfull[j], xbytes);
           bulk_g2s_hint(xring + off * kXGranule, xsrc + static_cast<int64_t>(kb) * xbytes, xbytes, &xfull[j], xpol);
@@ -297,7 +323,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) umma_proj_kernel(const UArgs 
         }
       }
     }
-  } else if (warp >= kMmaWarp0 && warp < kEpilogueWarp0) {
+  } else if (warp >= kMmaWarp0 && warp < EW0) {
     if (lane == 0) {
       const uint32_t mi = static_cast<uint32_t>(warp - kMmaWarp0);
       uint32_t sc = 0, ic = 0;
@@ -306,21 +332,21 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) umma_proj_kernel(const UArgs 
         const ChunkInfo c = chunk_info<MODE>(A, it.ci);
         const uint32_t idesc = idesc_bf16_m128(static_cast<uint32_t>(c.r16));
         const uint32_t atom = static_cast<uint32_t>(c.r16 >> 3) * 1024u;  // bytes per 64-value K atom
-        const uint32_t d = ic % kDBuffers;
-        const uint32_t dcol = tbase + kAccCol + (d * kMmaIssuers + mi) * kMaxTok;
-        if (ic >= kDBuffers && !mbar_wait_bounded(&dempty[d], ((ic / kDBuffers) - 1) & 1)) {
+        const uint32_t d = ic % DB;
+        const uint32_t dcol = tbase + kAccCol + (d * NI + mi) * TOK;
+        if (ic >= DB && !mbar_wait_bounded(&dempty[d], ((ic / DB) - 1) & 1)) {
           ok = false;
           break;
         }
         tc_fence_after();
         for (int i = 0; i < it.kb1 - it.kb0; ++i, ++sc) {
-          const uint32_t j = sc % kXSlots, b = sc % kABuffers;
-          if (!mbar_wait_bounded(&xfull[j], (sc / kXSlots) & 1) || !mbar_wait_bounded(&afull[b], (sc / kABuffers) & 1)) {
+          const uint32_t j = sc % kXSlots, b = sc % AB;
+          if (!mbar_wait_bounded(&xfull[j], (sc / kXSlots) & 1) || !mbar_wait_bounded(&afull[b], (sc / AB) & 1)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          constexpr int kSteps = 16 / kMmaIssuers;  // K steps of 16 values per issuer
+          constexpr int kSteps = 16 / NI;  // K steps of 16 values per issuer
           const uint32_t xs = smem_addr(xring + xoff[j] * kXGranule);
           const uint64_t bd = sdesc_sw128(xs + (mi * kSteps / 4) * atom, 1024u);
           const uint32_t acol = tbase + b * 128 + mi * kSteps * 8;
@@ -335,74 +361,83 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) umma_proj_kernel(const UArgs 
         ++ic;
       }
     }
-  } else if (warp >= kEpilogueWarp0) {
+  } else if (warp >= EW0) {
     // ---------------- epilogue ----------------
     const int q = warp & 3, L = 32 * q + lane;
     uint32_t ic = 0;
     for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++ic) {
       const ItemInfo it = item_info(A, item);
       const ChunkInfo c = chunk_info<MODE>(A, it.ci);
-      const uint32_t d = ic % kDBuffers;
-      if (!mbar_wait_bounded(&dfull[d], (ic / kDBuffers) & 1)) {
+      const uint32_t d = ic % DB;
+      if (!mbar_wait_bounded(&dfull[d], (ic / DB) & 1)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      // acc = ((D0 + D1) + D2) + D3 over the issuers' accumulators, eight columns at a time;
-      // the accumulators are released before the outputs are computed.
-      const uint32_t dcol = tbase + (static_cast<uint32_t>(32 * q) << 16) + kAccCol + d * kMmaIssuers * kMaxTok;
-      float acc[kMaxTok];
-#pragma unroll
-      for (int cg = 0; cg < kMaxTok / 8; ++cg) {
-        if (8 * cg >= c.r16) break;
-        uint32_t v[kMmaIssuers][8];
-#pragma unroll
-        for (int i = 0; i < kMmaIssuers; ++i) tmem_ld8(dcol + i * kMaxTok + 8 * cg, v[i]);
-        tmem_wait_ld();
-#pragma unroll
-        for (int jj = 0; jj < 8; ++jj) {
-          float a = __uint_as_float(v[0][jj]);
-#pragma unroll
-          for (int i = 1; i < kMmaIssuers; ++i) a = __fadd_rn(a, __uint_as_float(v[i][jj]));
-          acc[8 * cg + jj] = a;
-        }
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&dempty[d]);
+      // acc = ((D0 + D1) + D2) + D3 over the issuers' accumulators, in groups of 32 token
+      // columns (one group in the narrow form), eight columns at a time; the accumulators are
+      // released once the last group is in registers, before its outputs are computed.
+      const uint32_t dcol = tbase + (static_cast<uint32_t>(32 * q) << 16) + kAccCol + d * NI * TOK;
       const int t = L & 1, r = L >> 1;
-      if (MODE == kModeGateUp) {
-        // lane pair (gate row r, up row r): the even lane takes the first half of the token
-        // columns, the odd lane the second; each gets its partner's value by shuffle.
-        const int R = 64 * it.p + r;  // row of I = K index of the down pass
-        uint8_t* hbase = A.ht + c.xrow * 512 * A.nkb_out + static_cast<int64_t>(R >> 8) * c.r16 * 512;
-        const int half = c.r16 >> 1;
+      const int c_end = W ? c.r16 : 1;  // the narrow form has one group (r16 <= 32)
+      for (int c0 = 0; c0 < c_end; c0 += 32) {
+        const int gcols = W ? min(32, c.r16 - c0) : c.r16;  // a multiple of 16
+        float acc[32];
 #pragma unroll
-        for (int col = 0; col < kMaxTok; ++col) {
-          if (col >= c.r16) break;
-          const float other = __shfl_xor_sync(0xffffffffu, acc[col], 1);
-          if ((col < half) == (t == 0)) {
-            const float gb = bf16_round(t == 0 ? acc[col] : other);
-            const float ub = bf16_round(t == 0 ? other : acc[col]);
-            const float act = bf16_round(__fmul_rn(gb, sigmoid_ref(gb)));  // silu, math.py:19-20
-            *reinterpret_cast<uint16_t*>(hbase + xt_offset(c.r16, col, R & 255)) = bf16_bits_rne(__fmul_rn(act, ub));
+        for (int cg = 0; cg < 4; ++cg) {
+          if (8 * cg >= gcols) break;
+          uint32_t v[NI][8];
+#pragma unroll
+          for (int i = 0; i < NI; ++i) tmem_ld8(dcol + i * TOK + c0 + 8 * cg, v[i]);
+          tmem_wait_ld();
+#pragma unroll
+          for (int jj = 0; jj < 8; ++jj) {
+            float a = __uint_as_float(v[0][jj]);
+#pragma unroll
+            for (int i = 1; i < NI; ++i) a = __fadd_rn(a, __uint_as_float(v[i][jj]));
+            acc[8 * cg + jj] = a;
           }
         }
-      } else {
-        const int R = 128 * it.p + 64 * t + r;
-        if (R < A.nrows) {
-          float* obase = MODE == kModeDense
-                             ? (A.ksplit ? A.out + static_cast<int64_t>(it.kb0) * A.m_dense * A.nrows : A.out)
-                             : nullptr;
+        if (!W || c0 + 32 >= c.r16) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&dempty[d]);
+        }
+        if (MODE == kModeGateUp) {
+          // lane pair (gate row r, up row r): the even lane takes the first half of the
+          // group's token columns, the odd lane the second; each gets its partner's value by
+          // shuffle.
+          const int R = 64 * it.p + r;  // row of I = K index of the down pass
+          uint8_t* hbase = A.ht + c.xrow * 512 * A.nkb_out + static_cast<int64_t>(R >> 8) * c.r16 * 512;
+          const int half = gcols >> 1;
 #pragma unroll
-          for (int col = 0; col < kMaxTok; ++col) {
-            if (col >= c.ntok) break;
-            const int64_t orow = c.entry0 + col;
-            if (MODE == kModeDown) {
-              if (A.yr) A.yr[static_cast<int64_t>(A.entry_route[orow]) * A.nrows + R] = acc[col];
-              else A.y[orow * A.nrows + R] = bf16_bits_rne(acc[col]);
-            } else {
-              obase[orow * A.nrows + R] = acc[col];
+          for (int col = 0; col < 32; ++col) {
+            if (col >= gcols) break;
+            const float other = __shfl_xor_sync(0xffffffffu, acc[col], 1);
+            if ((col < half) == (t == 0)) {
+              const float gb = bf16_round(t == 0 ? acc[col] : other);
+              const float ub = bf16_round(t == 0 ? other : acc[col]);
+              const float act = bf16_round(__fmul_rn(gb, sigmoid_ref(gb)));  // silu, math.py:19-20
+              *reinterpret_cast<uint16_t*>(hbase + xt_offset(c.r16, c0 + col, R & 255)) =
+                  bf16_bits_rne(__fmul_rn(act, ub));
+            }
+          }
+        } else {
+          const int R = 128 * it.p + 64 * t + r;
+          if (R < A.nrows) {
+            float* obase = MODE == kModeDense
+                               ? (A.ksplit ? A.out + static_cast<int64_t>(it.kb0) * A.m_dense * A.nrows : A.out)
+                               : nullptr;
+#pragma unroll
+            for (int col = 0; col < 32; ++col) {
+              if (c0 + col >= c.ntok) break;
+              const int64_t orow = c.entry0 + c0 + col;
+              if (MODE == kModeDown) {
+                if (A.yr) A.yr[static_cast<int64_t>(A.entry_route[orow]) * A.nrows + R] = acc[col];
+                else A.y[orow * A.nrows + R] = bf16_bits_rne(acc[col]);
+              } else {
+                obase[orow * A.nrows + R] = acc[col];
+              }
             }
           }
         }
@@ -434,8 +469,8 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) umma_proj_kernel(const UArgs 
           else HT::clear(regs);
           __syncwarp();
           if (lane == 0) mbar_arrive(&wempty[s]);
-          const uint32_t b = sc % kABuffers;
-          if (sc >= kABuffers && !mbar_wait_bounded(&aempty[b], ((sc / kABuffers) - 1) & 1)) {
+          const uint32_t b = sc % AB;
+          if (sc >= AB && !mbar_wait_bounded(&aempty[b], ((sc / AB) - 1) & 1)) {
             ok = false;
             break;
           }
@@ -462,12 +497,13 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) umma_proj_kernel(const UArgs 
   }
 }
 
-template <QType QT, int MODE>
+template <QType QT, int MODE, bool W = false>
 int launch_umma(const UArgs& A, int grid, cudaStream_t st) {
-  using Cfg = UCfg<QT>;
-  int rc = allow_smem(reinterpret_cast<const void*>(umma_proj_kernel<QT, MODE>), Cfg::kSmem);
+  using Cfg = UCfg<QT, W>;
+  int rc = allow_smem(reinterpret_cast<const void*>(umma_proj_kernel<QT, MODE, W>), Cfg::kSmem);
   if (rc) return rc;
-  const cudaError_t e = launch_dependent(umma_proj_kernel<QT, MODE>, dim3(grid), dim3(kUmmaThreads), Cfg::kSmem, st, A);
+  const cudaError_t e = launch_dependent(umma_proj_kernel<QT, MODE, W>, dim3(grid), dim3(Form<W>::kThreads), Cfg::kSmem,
+                                         st, A);
   if (e != cudaSuccess) return cuda_error(e, "umma_proj_kernel");
   count_launch(1);
   return QK_OK;

@@ -92,6 +92,30 @@ def test_many_tokens_per_expert_duplicates_and_finished_rows(cuda_device, tokens
     np.testing.assert_array_equal(got[::7], 0)
 
 
+@pytest.mark.parametrize("qtype", ["Q6_K", "Q4_K"])
+def test_wide_form_chunks_of_128_tokens(cuda_device, qtype):
+    """Routes averaging >= 64 tokens per expert take the wide form (128-token chunks, one
+    MMA issuer, N up to 128): 300 tokens per expert give chunks of 128, 128 and a ragged
+    last one; an expert with a single token shares the call."""
+    hidden, intermediate, count, k = 512, 512, 5, 2
+    rng = np.random.default_rng(300)
+    raw = make_experts(rng, count, hidden, intermediate, qtype)
+    batch = 300 * (count - 1) // k + 1
+    ids = rng.integers(0, count - 1, (batch, k)).astype(np.int32)
+    ids[0, 1] = count - 1            # the last expert: one token
+    ids[1:4, 1] = ids[1:4, 0]        # duplicate routes merge
+    weights = bf16_round(rng.uniform(0.05, 1.0, (batch, k)).astype(np.float32))
+    weights[5::11] = 0
+    x = rng.normal(size=(batch, hidden)).astype(np.float32)
+    assert batch * k >= 64 * count   # the wide form
+    got, _, _ = run_layer(cuda_device, raw, qtype, hidden, intermediate, x, ids, weights)
+    expected = moe.expert_ffn(raw["gate"], raw["up"], raw["down"], x, ids, weights, gate_type=qtype,
+                              up_type=qtype, down_type=qtype, hidden=hidden, intermediate=intermediate)
+    mx, l2 = rel_err(got, expected)
+    assert mx < LAYER_TOL and l2 < 2e-3, (mx, l2)
+    np.testing.assert_array_equal(got[5::11], 0)
+
+
 def test_zero_weights_give_zero_and_ids_outside_rank_are_ignored(cuda_device):
     hidden, intermediate, count = 256, 256, 4
     rng = np.random.default_rng(3)
