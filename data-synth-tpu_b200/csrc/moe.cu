@@ -142,21 +142,21 @@ __global__ void __launch_bounds__(1024) moe_route_kernel(const int32_t* ids, con
   __syncthreads();
 
   // Pass 1: entries per expert. The first slot j of a token that names expert e owns
-  // the merged entry; its weight is bf16 of the FP32 sum over all slots naming e.
-  for (int b = tid; b < B; b += nt) {
-    for (int j = 0; j < k; ++j) {
-      const int e = ids[b * k + j] - first;
-      int own = e >= 0 && e < E;
-      for (int jj = 0; own && jj < j; ++jj) own = ids[b * k + jj] - first != e;
-      float w = 0.f;
-      if (own) {
-        for (int jj = j; jj < k; ++jj)
-          if (ids[b * k + jj] - first == e) w = __fadd_rn(w, bf16_to_f32(weights[b * k + jj]));
-        w = bf16_round(w);
-        own = w != 0.f;
-      }
-      if (own) atomicAdd(&counts[e], 1);
+  // the merged entry; its weight is bf16 of the FP32 sum over all slots naming e. One
+  // thread per route (b, j).
+  for (int route = tid; route < B * k; route += nt) {
+    const int b = route / k, j = route - b * k;
+    const int e = ids[b * k + j] - first;
+    int own = e >= 0 && e < E;
+    for (int jj = 0; own && jj < j; ++jj) own = ids[b * k + jj] - first != e;
+    float w = 0.f;
+    if (own) {
+      for (int jj = j; jj < k; ++jj)
+        if (ids[b * k + jj] - first == e) w = __fadd_rn(w, bf16_to_f32(weights[b * k + jj]));
+      w = bf16_round(w);
+      own = w != 0.f;
     }
+    if (own) atomicAdd(&counts[e], 1);
   }
   __syncthreads();
 
@@ -246,28 +246,27 @@ __global__ void __launch_bounds__(1024) moe_route_kernel(const int32_t* ids, con
     }
   }
 
-  // Pass 2: place entries.
-  for (int b = tid; b < B; b += nt) {
-    for (int j = 0; j < k; ++j) {
-      const int e = ids[b * k + j] - first;
-      int own = e >= 0 && e < E;
-      for (int jj = 0; own && jj < j; ++jj) own = ids[b * k + jj] - first != e;
-      float w = 0.f;
-      if (own) {
-        for (int jj = j; jj < k; ++jj)
-          if (ids[b * k + jj] - first == e) w = __fadd_rn(w, bf16_to_f32(weights[b * k + jj]));
-        w = bf16_round(w);
-        own = w != 0.f;
-      }
-      int slot = -1;
-      if (own) {
-        slot = offsets[e] + atomicAdd(&cursor[e], 1);
-        ws.entry_token[slot] = b;
-        ws.entry_weight[slot] = w;
-        ws.entry_route[slot] = b * k + j;
-      }
-      ws.route_entry[b * k + j] = slot;
+  // Pass 2: place entries (one thread per route).
+  for (int route = tid; route < B * k; route += nt) {
+    const int b = route / k, j = route - b * k;
+    const int e = ids[b * k + j] - first;
+    int own = e >= 0 && e < E;
+    for (int jj = 0; own && jj < j; ++jj) own = ids[b * k + jj] - first != e;
+    float w = 0.f;
+    if (own) {
+      for (int jj = j; jj < k; ++jj)
+        if (ids[b * k + jj] - first == e) w = __fadd_rn(w, bf16_to_f32(weights[b * k + jj]));
+      w = bf16_round(w);
+      own = w != 0.f;
     }
+    int slot = -1;
+    if (own) {
+      slot = offsets[e] + atomicAdd(&cursor[e], 1);
+      ws.entry_token[slot] = b;
+      ws.entry_weight[slot] = w;
+      ws.entry_route[slot] = b * k + j;
+    }
+    ws.route_entry[b * k + j] = slot;
   }
 }
 
