@@ -30,6 +30,34 @@ class ExpertFFN:
         self.intermediate = intermediate
         self.tensor_parallel = tensor_parallel
         self._workspace = {}
+        self.tensor_group = self.expert_group = None
+        self.expert_rank = 0
+        if tensor_parallel > 1 and group is not None:
+            self._mesh_groups()
+
+    def _mesh_groups(self):
+        """The ("expert", "tensor") mesh of parallel.py:28-33 over `group`: rank = e * tp + t.
+        The tensor group of a rank is the tp ranks holding slices of its experts; the expert
+        group is the ranks holding the same slice of the other experts. Every rank builds
+        every group (torch.distributed.new_group is collective)."""
+        import torch.distributed as dist
+
+        tp = self.tensor_parallel
+        ranks = dist.get_process_group_ranks(self.group)
+        me = dist.get_rank(self.group)
+        ep = len(ranks) // tp
+        self.expert_rank = me // tp
+        if ep == 1:
+            self.tensor_group = self.group
+            return
+        for e in range(ep):
+            g = dist.new_group([ranks[e * tp + t] for t in range(tp)])
+            if e == me // tp:
+                self.tensor_group = g
+        for t in range(tp):
+            g = dist.new_group([ranks[e * tp + t] for e in range(ep)])
+            if t == me % tp:
+                self.expert_group = g
 
     def _rank_world(self):
         if self.group is None:
@@ -89,13 +117,13 @@ class ExpertFFN:
         self.last_workspace = ws
         return out
 
-    def tensor_partial(self, gate, up, down, x, ids, weights):
-        """Tensor parallel, first half: this rank's slice of every expert; returns the FP32
-        down projection of every route ``[B * k, hidden]`` (before the tensor all-reduce)
-        and the workspace the combine reads."""
+    def tensor_partial(self, gate, up, down, x, ids, weights, first_expert=0):
+        """Tensor parallel, first half: this rank's slice of its experts [first_expert,
+        first_expert + E_local); returns the FP32 down projection of every route ``[B * k,
+        hidden]`` (before the tensor all-reduce) and the workspace the combine reads."""
         self._check(gate, up, down, x, ids, weights)
         batch, top_k = ids.shape
-        desc = self.desc(gate.shape[0], 0, top_k)
+        desc = self.desc(gate.shape[0], first_expert, top_k)
         device = x.device
         ws = self.workspace(desc, batch, device)
         x = x.contiguous()
@@ -109,15 +137,24 @@ class ExpertFFN:
         self.last_workspace = ws
         return y_routes, ids, ws
 
-    def tensor_combine(self, y_routes, ids, ws, num_experts):
+    def tensor_combine(self, y_routes, ids, ws, num_experts, out_dtype=torch.bfloat16):
         """Tensor parallel, second half: BF16 of each route's summed down projection,
-        route-weighted and added in ascending expert order."""
+        route-weighted and added in ascending expert order; BF16, or the FP32 sum that an
+        expert-parallel all-reduce adds (``out_dtype=torch.float32``)."""
         batch, top_k = ids.shape
         desc = self.desc(num_experts, 0, top_k)
-        out = torch.empty((batch, self.hidden), dtype=torch.bfloat16, device=ids.device)
+        out = torch.empty((batch, self.hidden), dtype=out_dtype, device=ids.device)
+        code = _lib.QK_OUT_BF16 if out_dtype == torch.bfloat16 else _lib.QK_OUT_F32
         with torch.cuda.device(ids.device):
             _lib.call("qk_moe_forward_tp_combine", desc, _lib.ptr(y_routes), _lib.ptr(ids), batch,
-                      _lib.QK_OUT_BF16, _lib.ptr(out), _lib.ptr(ws), ws.numel(), _lib.stream_handle(ids.device))
+                      code, _lib.ptr(out), _lib.ptr(ws), ws.numel(), _lib.stream_handle(ids.device))
+        return out
+
+    def _cast_bf16(self, partial):
+        out = torch.empty(partial.shape, dtype=torch.bfloat16, device=partial.device)
+        with torch.cuda.device(partial.device):
+            _lib.call("qk_cast_f32_bf16", _lib.ptr(partial), _lib.ptr(out), partial.numel(),
+                      _lib.stream_handle(partial.device))
         return out
 
     def __call__(self, gate, up, down, x, ids, weights):
@@ -125,20 +162,22 @@ class ExpertFFN:
         if self.tensor_parallel > 1:
             import torch.distributed as dist
 
-            y_routes, ids32, ws = self.tensor_partial(gate, up, down, x, ids, weights)
-            dist.all_reduce(y_routes, group=self.group)  # grouped_experts.py:113-118
-            return self.tensor_combine(y_routes, ids32, ws, gate.shape[0])
+            count = gate.shape[0]
+            y_routes, ids32, ws = self.tensor_partial(gate, up, down, x, ids, weights,
+                                                      self.expert_rank * count)
+            dist.all_reduce(y_routes, group=self.tensor_group)  # grouped_experts.py:113-118
+            if self.expert_group is None:
+                return self.tensor_combine(y_routes, ids32, ws, count)
+            partial = self.tensor_combine(y_routes, ids32, ws, count, torch.float32)
+            dist.all_reduce(partial, group=self.expert_group)  # experts.py:130-131
+            return self._cast_bf16(partial)
         if world == 1:
             return self._run(gate, up, down, x, ids, weights, None, torch.bfloat16)
         import torch.distributed as dist
 
         partial = self._run(gate, up, down, x, ids, weights, None, torch.float32)
         dist.all_reduce(partial, group=self.group)
-        out = torch.empty(partial.shape, dtype=torch.bfloat16, device=partial.device)
-        with torch.cuda.device(partial.device):
-            _lib.call("qk_cast_f32_bf16", _lib.ptr(partial), _lib.ptr(out), partial.numel(),
-                      _lib.stream_handle(partial.device))
-        return out
+        return self._cast_bf16(partial)
 
     def check_status(self):
         """Raise if a bounded device wait of the last call gave up (synchronises)."""
@@ -177,16 +216,15 @@ def expert_parallel(
     if type(tensor_parallel) is not int or tensor_parallel < 1:
         raise ValueError("Tensor parallel size must divide the device count")
     if tensor_parallel > 1:
-        # every rank of `group` holds every expert's 1/tp slice of the intermediate channels
-        # (put_expert_bytes(..., tensor_rank=r, tensor_parallel=tp)); a mesh that also splits
-        # the experts over ranks is not built here
+        # the ("expert", "tensor") mesh of parallel.py:28-33 over `group`: rank e * tp + t holds
+        # tensor slice t of expert range e (put_expert_bytes(..., rank=e, world=ep,
+        # tensor_rank=t, tensor_parallel=tp))
         if group is None:
             raise ValueError("tensor parallel experts need a process group")
         import torch.distributed as dist
 
-        if dist.get_world_size(group) != tensor_parallel:
-            raise NotImplementedError("tensor_parallel must equal the process group's size "
-                                      "(expert x tensor meshes are not built)")
+        if dist.get_world_size(group) % tensor_parallel:
+            raise ValueError("Tensor parallel size must divide the device count")
         if (intermediate // tensor_parallel) % 256 or intermediate % tensor_parallel:
             raise ValueError("Tensor slices must contain whole down quantization blocks")
     types = tuple(normalize_qtype(t) for t in (gate_type, up_type, down_type))

@@ -83,6 +83,46 @@ def test_two_tensor_slices_match_the_whole_experts(cuda_device, qtype):
     assert np.isfinite(to_f32(got)).all()
 
 
+@pytest.mark.parametrize("qtype", ["Q6_K", "Q4_K"])
+def test_expert_by_tensor_mesh_emulated(cuda_device, qtype):
+    """The ("expert", "tensor") mesh (parallel.py:28-33) with 2 expert ranks x 2 tensor
+    ranks emulated on one GPU: each expert rank's tensor slices are summed in FP32 before
+    the BF16 rounding (grouped_experts.py:113-119), the expert ranks' FP32 partials are then
+    added (experts.py:130-131) and rounded."""
+    import torch
+
+    from qk_b200.experts import ExpertFFN, expert_parallel
+    from qk_b200.parallel import put_expert_bytes
+
+    ep, tp, per, B, k = 2, 2, 4, 29, 3
+    count = ep * per
+    raw = _experts(qtype, count, 71)
+    x, ids, w = _tokens(B, k, count, 72)
+    xd, idd, wd = bf16_tensor(x, cuda_device), torch.from_numpy(ids).to(cuda_device), bf16_tensor(w, cuda_device)
+    fn = ExpertFFN(None, qtype, qtype, qtype, HIDDEN, INTER, tensor_parallel=tp)
+    total = None
+    for e in range(ep):
+        y_sum, last = None, None
+        for t in range(tp):
+            mine = {n: put_expert_bytes(raw[n], n, qtype, HIDDEN, INTER, rank=e, world=ep, device=cuda_device,
+                                        tensor_rank=t, tensor_parallel=tp) for n in raw}
+            y_routes, ids32, ws = fn.tensor_partial(mine["gate"], mine["up"], mine["down"], xd, idd, wd, e * per)
+            y_sum = y_routes.clone() if y_sum is None else y_sum + y_routes
+            last = (ids32, ws)
+        part = fn.tensor_combine(y_sum, last[0], last[1], per, torch.float32)
+        total = part if total is None else total + part
+    got = to_f32(total.to(torch.bfloat16))
+    whole = {n: put_expert_bytes(raw[n], n, qtype, HIDDEN, INTER, device=cuda_device) for n in raw}
+    single = expert_parallel(gate_type=qtype, up_type=qtype, down_type=qtype, hidden=HIDDEN, intermediate=INTER)(
+        whole["gate"], whole["up"], whole["down"], xd, idd, wd)
+    mx, l2 = rel_err(got, to_f32(single))
+    assert mx < 1e-2 and l2 < 5e-3, (mx, l2)
+    expected = moe.expert_ffn(raw["gate"], raw["up"], raw["down"], x, ids, w, gate_type=qtype, up_type=qtype,
+                              down_type=qtype, hidden=HIDDEN, intermediate=INTER)
+    mx, l2 = rel_err(got, expected)
+    assert mx < 1e-2 and l2 < 5e-3, (mx, l2)
+
+
 def _port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))

@@ -253,3 +253,40 @@ def test_tensor_parallel_factory_contract():
     with pytest.raises(ValueError, match="process group"):
         expert_parallel(None, gate_type="Q6_K", up_type="Q6_K", down_type="Q6_K", hidden=2048,
                         intermediate=512, tensor_parallel=2)
+
+
+def _mesh_rank(rank, world, port, path):
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from qk_b200.experts import expert_parallel
+
+        fn = expert_parallel(dist.group.WORLD, gate_type="Q6_K", up_type="Q6_K", down_type="Q6_K", hidden=2048,
+                             intermediate=512, tensor_parallel=2)
+        tg = dist.get_process_group_ranks(fn.tensor_group)
+        eg = dist.get_process_group_ranks(fn.expert_group)
+        np.save(f"{path}.{rank}.npy", np.array([fn.expert_rank] + tg + eg))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_expert_tensor_mesh_groups_on_gloo(tmp_path):
+    """The ("expert", "tensor") mesh of parallel.py:28-33 over 4 ranks with tp = 2: rank
+    e * 2 + t sums its tensor slices with rank e * 2 + (1 - t) and its expert partials with
+    rank (1 - e) * 2 + t."""
+    import socket
+
+    import torch.multiprocessing as mp
+
+    with socket.socket() as sock:
+        sock.bind(("127.0.0.1", 0))
+        port = sock.getsockname()[1]
+    path = tmp_path / "mesh"
+    mp.start_processes(_mesh_rank, args=(4, port, str(path)), nprocs=4, start_method="spawn")
+    for rank in range(4):
+        e, t = divmod(rank, 2)
+        got = np.load(f"{path}.{rank}.npy").tolist()
+        assert got == [e, 2 * e, 2 * e + 1, t, 2 + t]
