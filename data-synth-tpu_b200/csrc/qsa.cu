@@ -258,12 +258,128 @@ __global__ void __launch_bounds__(kSelThreads) qsa_select_kernel(const float* __
   }
 }
 
+// ---- the key-maintenance half of select_tokens (attention_cache.py:86-99) ----
+
+struct QsaRope {
+  const float* inv_freq;  // [rotary / 2]: theta^(-2i / rotary)
+  const int32_t* axis;    // [rotary / 2]: which of the 3 position components rotates pair i
+  int rotary;
+};
+
+// In place on v[0 .. dim) of one thread block (thread d owns v[d]; dim <= blockDim.x):
+// math.py:27-31 rms with gamma, then math.py:231-243 rope at positions pos[3] (the
+// rotary cosine and sine rounded to BF16). Returns this thread's BF16 result.
+__device__ float rms_rope(float v, int d, int dim, const uint16_t* gamma, float eps, const int32_t* pos,
+                          const QsaRope& rp, float* red, float* row) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  float ss = d < dim ? v * v : 0.f;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  __syncthreads();
+  if (lane == 0) red[warp] = ss;
+  __syncthreads();
+  float tot = 0.f;
+  for (int w = 0; w < nw; ++w) tot += red[w];
+  const float r = rsqrtf(__fadd_rn(__fdiv_rn(tot, static_cast<float>(dim)), eps));
+  if (d < dim) row[d] = bf16_round(__fmul_rn(__fmul_rn(v, r), bf16_to_f32(gamma[d])));
+  __syncthreads();
+  if (d >= dim) return 0.f;
+  float o = row[d];
+  const int half = rp.rotary / 2;
+  if (d < rp.rotary) {
+    const int i = d < half ? d : d - half;
+    const float angle = __fmul_rn(static_cast<float>(pos[rp.axis[i]]), rp.inv_freq[i]);
+    const float cs = bf16_round(cosf(angle)), sn = bf16_round(sinf(angle));
+    const float a = row[i], c = row[i + half];
+    o = bf16_round(d < half ? __fsub_rn(__fmul_rn(a, cs), __fmul_rn(c, sn)) : __fadd_rn(__fmul_rn(c, cs), __fmul_rn(a, sn)));
+  }
+  return o;
+}
+
+// One block per row b (thread d = channel d): write this step's raw key into the tail at
+// slot lengths % ratio (active rows), note the block start on slot 0, pool the tail (FP32
+// mean, BF16), rms + rope it at the block start and, on the block's last slot, store it as
+// key lengths / ratio.
+__global__ void qsa_update_keys_kernel(const uint16_t* __restrict__ raw_k, const int32_t* __restrict__ lengths,
+                                       const int32_t* __restrict__ positions, const uint8_t* __restrict__ active,
+                                       const uint16_t* __restrict__ k_norm, float eps, QsaRope rp, int ratio, int dim,
+                                       int blocks, uint16_t* tail, int32_t* starts, uint16_t* keys) {
+  __shared__ float red[32];
+  __shared__ float row[kMaxDim];
+  const int b = blockIdx.x, d = threadIdx.x;
+  const bool on = active ? active[b] != 0 : true;
+  const int len = lengths[b], slot = len % ratio;
+  uint16_t* tb = tail + static_cast<int64_t>(b) * ratio * dim;
+  if (on && d < dim) tb[slot * dim + d] = raw_k[static_cast<int64_t>(b) * dim + d];
+  __syncthreads();
+  if (on && slot == 0 && d < 3) starts[b * 3 + d] = positions[b * 3 + d];
+  float sum = 0.f;
+  if (d < dim)
+    for (int j = 0; j < ratio; ++j) sum = __fadd_rn(sum, bf16_to_f32(tb[j * dim + d]));
+  const float pooled = bf16_round(__fdiv_rn(sum, static_cast<float>(ratio)));
+  __syncthreads();  // every thread has read starts[] written above before rms_rope reads it
+  int32_t st[3];
+  for (int c = 0; c < 3; ++c) st[c] = starts[b * 3 + c];
+  const float key = rms_rope(pooled, d, dim, k_norm, eps, st, rp, red, row);
+  const int blk = len / ratio;
+  if (on && slot == ratio - 1 && d < dim && blk < blocks)
+    keys[(static_cast<int64_t>(b) * blocks + blk) * dim + d] = bf16_bits_rne(key);
+}
+
+// Block (row b, head h): rms + rope of the query head at positions[b] (attention_cache.py:98-99).
+__global__ void qsa_query_kernel(const uint16_t* __restrict__ raw_q, const int32_t* __restrict__ positions,
+                                 const uint16_t* __restrict__ q_norm, float eps, QsaRope rp, int heads, int dim,
+                                 uint16_t* __restrict__ query) {
+  __shared__ float red[32];
+  __shared__ float row[kMaxDim];
+  const int b = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
+  const int64_t base = (static_cast<int64_t>(b) * heads + h) * dim;
+  const float v = d < dim ? bf16_to_f32(raw_q[base + d]) : 0.f;
+  int32_t pos[3];
+  for (int c = 0; c < 3; ++c) pos[c] = positions[b * 3 + c];
+  const float o = rms_rope(v, d, dim, q_norm, eps, pos, rp, red, row);
+  if (d < dim) query[base + d] = bf16_bits_rne(o);
+}
+
 }  // namespace
 }  // namespace qk
 
 using namespace qk;
 
 extern "C" {
+
+int qk_qsa_update_keys(const uint16_t* raw_k, const int32_t* lengths, const int32_t* positions,
+                       const uint8_t* active, const uint16_t* k_norm, float eps, const float* inv_freq,
+                       const int32_t* axis, int rotary, int B, int ratio, int dim, int blocks, uint16_t* tail,
+                       int32_t* starts, uint16_t* keys, qk_stream_t stream) {
+  QK_REQUIRE(B >= 0 && ratio >= 2 && blocks > 0, "invalid indexer geometry");
+  QK_REQUIRE(dim > 0 && dim <= kMaxDim && rotary >= 0 && rotary <= dim && rotary % 2 == 0, "invalid indexer dim");
+  if (B == 0) return QK_OK;
+  QK_REQUIRE(raw_k && lengths && positions && k_norm && tail && starts && keys, "null pointer");
+  QK_REQUIRE(rotary == 0 || (inv_freq && axis), "inv_freq and axis are required");
+  const int threads = (dim + 31) / 32 * 32;
+  qsa_update_keys_kernel<<<B, threads, 0, as_stream(stream)>>>(raw_k, lengths, positions, active, k_norm, eps,
+                                                               QsaRope{inv_freq, axis, rotary}, ratio, dim, blocks,
+                                                               tail, starts, keys);
+  QK_LAUNCHED("qsa_update_keys_kernel");
+  return QK_OK;
+}
+
+int qk_qsa_query(const uint16_t* raw_q, const int32_t* positions, const uint16_t* q_norm, float eps,
+                 const float* inv_freq, const int32_t* axis, int rotary, int B, int heads, int dim, uint16_t* query,
+                 qk_stream_t stream) {
+  QK_REQUIRE(B >= 0 && heads > 0, "invalid indexer geometry");
+  QK_REQUIRE(dim > 0 && dim <= kMaxDim && rotary >= 0 && rotary <= dim && rotary % 2 == 0, "invalid indexer dim");
+  if (B == 0) return QK_OK;
+  QK_REQUIRE(raw_q && positions && q_norm && query, "null pointer");
+  QK_REQUIRE(rotary == 0 || (inv_freq && axis), "inv_freq and axis are required");
+  const int threads = (dim + 31) / 32 * 32;
+  qsa_query_kernel<<<dim3(B, heads), threads, 0, as_stream(stream)>>>(raw_q, positions, q_norm, eps,
+                                                                      QsaRope{inv_freq, axis, rotary}, heads, dim,
+                                                                      query);
+  QK_LAUNCHED("qsa_query_kernel");
+  return QK_OK;
+}
 
 int qk_qsa_block_scores(const uint16_t* query, const uint16_t* keys, const int32_t* lengths, int B, int heads,
                         int dim, int blocks, int ratio, float* scores, qk_stream_t stream) {

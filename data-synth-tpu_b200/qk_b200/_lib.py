@@ -92,6 +92,11 @@ SIGNATURES = {
     "qk_kv_q8_attention_combine": (_i, [_p, _i, _i, _i, _i, _p, _p, _p]),
     "qk_qsa_block_scores": (_i, [_p, _p, _p, _i, _i, _i, _i, _i, _p, _p]),
     "qk_qsa_select": (_i, [_p, _p, _i, _i, _i, _i, _p, _p, _p]),
+    "qk_qsa_update_keys": (
+        _i,
+        [_p, _p, _p, _p, _p, ctypes.c_float, _p, _p, _i, _i, _i, _i, _i, _p, _p, _p, _p],
+    ),
+    "qk_qsa_query": (_i, [_p, _p, _p, ctypes.c_float, _p, _p, _i, _i, _i, _i, _p, _p]),
     "qk_checked_argmax": (_i, [_p, _i, _i, _i64, _p, _p]),
     "qk_rms_norm": (_i, [_p, _p, _i, _i, ctypes.c_float, _p, _p]),
     "qk_qk_norm_rope": (

@@ -122,6 +122,81 @@ def read_quantized(cache, name, indices, c, dtype, *, scale_gather=None):
     return out
 
 
+@dataclass(frozen=True)
+class IndexerConfig:
+    """The ``ModelConfig`` fields ``select_tokens`` reads (``config.py:28-38``)."""
+
+    qsa_budget: int = 2048
+    indexer_heads: int = 4
+    indexer_dim: int = 128
+    indexer_compress: int = 4
+    rotary_dim: int = 64
+    rope_theta: float = 10_000_000.0
+    mrope_sections: tuple = (11, 11, 10)
+    eps: float = 1e-6
+
+    def __post_init__(self):
+        if (self.indexer_heads < 1 or self.indexer_dim < self.rotary_dim or self.indexer_compress < 2
+                or self.qsa_budget < self.indexer_compress or self.qsa_budget % self.indexer_compress):
+            raise ValueError("Invalid sparse attention indexer dimensions or budget")  # config.py:59-65
+
+    def rope_tables(self, device):
+        """``(inv_freq FP32 [rotary/2], axis int32 [rotary/2])`` of ``math.py:231-238``: pair i turns
+        by ``positions[axis[i]] * theta^(-2i/rotary)``."""
+        import numpy as np
+
+        half = self.rotary_dim // 2
+        inv = np.power(np.float32(self.rope_theta),
+                       -np.arange(half, dtype=np.float32) * 2 / np.float32(self.rotary_dim)).astype(np.float32)
+        axis = np.zeros(half, np.int32)
+        for dim, offset in ((1, 1), (2, 2)):
+            idx = np.arange(offset, self.mrope_sections[dim] * 3, 3)
+            axis[idx[idx < half]] = dim
+        return torch.from_numpy(inv).to(device), torch.from_numpy(axis).to(device)
+
+
+def empty_index_cache(batch, max_context, ic, device=None):
+    """The indexer state of ``engine.py:372-380``: block keys, the open block's raw keys and
+    its start position."""
+    device = torch.device(device or "cuda")
+    blocks = (max_context + ic.indexer_compress - 1) // ic.indexer_compress
+    return {
+        "index_keys": torch.zeros((batch, blocks, ic.indexer_dim), dtype=torch.bfloat16, device=device),
+        "index_tail": torch.zeros((batch, ic.indexer_compress, ic.indexer_dim), dtype=torch.bfloat16, device=device),
+        "index_start": torch.zeros((batch, 3), dtype=torch.int32, device=device),
+    }
+
+
+def select_tokens(x, w, cache, lengths, positions, active, c):
+    """``attention_cache.py:84-125``: update the indexer state with this step's token and
+    select the sparse attention's tokens. ``x`` BF16 ``[B, H]``; ``w`` holds ``index_k``
+    ``[dim, H]``, ``index_q`` ``[heads * dim, H]``, ``index_k_norm`` / ``index_q_norm`` ``[dim]``
+    (BF16); ``positions`` int32 ``[B, 3]``; ``c`` an :class:`IndexerConfig`. The cache's
+    ``index_*`` entries are updated in place. Returns ``(indices, valid, cache)``."""
+    batch = x.shape[0]
+    device = x.device
+    ratio, dim, heads = c.indexer_compress, c.indexer_dim, c.indexer_heads
+    keys = cache["index_keys"]
+    inv, axis = c.rope_tables(device)
+    lens = lengths.to(device=device, dtype=torch.int32).contiguous()
+    pos = positions.to(device=device, dtype=torch.int32).contiguous()
+    act = None if active is None else active.to(device=device, dtype=torch.uint8).contiguous()
+    x = x.contiguous()
+    raw_k = torch.matmul(x, w["index_k"].t()).contiguous()     # linear(x, index_k), :90
+    raw_q = torch.matmul(x, w["index_q"].t()).contiguous()     # linear(x, index_q), :98
+    query = torch.empty((batch, heads, dim), dtype=torch.bfloat16, device=device)
+    with torch.cuda.device(device):
+        st = _lib.stream_handle(device)
+        _lib.call("qk_qsa_update_keys", _lib.ptr(raw_k), _lib.ptr(lens), _lib.ptr(pos), _lib.ptr(act),
+                  _lib.ptr(w["index_k_norm"].contiguous()), c.eps, _lib.ptr(inv), _lib.ptr(axis), c.rotary_dim,
+                  batch, ratio, dim, keys.shape[1], _lib.ptr(cache["index_tail"]), _lib.ptr(cache["index_start"]),
+                  _lib.ptr(keys), st)
+        _lib.call("qk_qsa_query", _lib.ptr(raw_q), _lib.ptr(pos), _lib.ptr(w["index_q_norm"].contiguous()), c.eps,
+                  _lib.ptr(inv), _lib.ptr(axis), c.rotary_dim, batch, heads, dim, _lib.ptr(query), st)
+    indices, valid = select_tokens_from_keys(query, keys, lens, ratio=ratio, budget=c.qsa_budget)
+    return indices, valid, cache
+
+
 def select_tokens_from_keys(query, keys, lengths, *, ratio=4, budget=2048):
     """The selection half of ``attention_cache.py:84-125`` (``select_tokens``) once the block
     keys are current: ``query`` BF16 ``[B, indexer_heads, indexer_dim]`` (normed and rotated),

@@ -267,6 +267,22 @@ int qk_qsa_block_scores(const uint16_t* query, const uint16_t* keys, const int32
                         qk_stream_t stream);
 int qk_qsa_select(const float* scores, const int32_t* lengths, int B, int blocks, int ratio,
                   int budget, int32_t* indices, uint8_t* valid, qk_stream_t stream);
+/* The key-maintenance half of select_tokens (attention_cache.py:86-99). Rotary (math.py:
+ * 231-243) with three position components: pair i (i < rotary / 2) turns by
+ * positions[b, axis[i]] * inv_freq[i], cosine and sine rounded to BF16.
+ * qk_qsa_update_keys: raw_k BF16 [B, dim] (linear(x, index_k)); for active rows (active
+ * uint8 [B] or NULL) writes it to tail BF16 [B, ratio, dim] at slot lengths % ratio, copies
+ * positions int32 [B, 3] to starts [B, 3] on slot 0, pools the tail (FP32 mean, BF16),
+ * normalises (k_norm) and rotates it at the block start, and on slot ratio - 1 stores it to
+ * keys BF16 [B, blocks, dim] at block lengths / ratio. qk_qsa_query: raw_q BF16
+ * [B, heads, dim] (linear(x, index_q)) -> query = rope(rms(raw_q, q_norm), positions). */
+int qk_qsa_update_keys(const uint16_t* raw_k, const int32_t* lengths, const int32_t* positions,
+                       const uint8_t* active, const uint16_t* k_norm, float eps, const float* inv_freq,
+                       const int32_t* axis, int rotary, int B, int ratio, int dim, int blocks,
+                       uint16_t* tail, int32_t* starts, uint16_t* keys, qk_stream_t stream);
+int qk_qsa_query(const uint16_t* raw_q, const int32_t* positions, const uint16_t* q_norm, float eps,
+                 const float* inv_freq, const int32_t* axis, int rotary, int B, int heads, int dim,
+                 uint16_t* query, qk_stream_t stream);
 
 /* ---- decoder-layer glue around the path -----------------------------------------
  * The per-token steps on either side of the routed FFN and the decode attention in a

@@ -181,3 +181,45 @@ def qsa_select(scores, lengths, ratio, budget):
         out_i.append(np.where(val, idx, 0).astype(np.int32))
         out_v.append(val)
     return np.stack(out_i), np.stack(out_v)
+
+
+def qsa_rope(x, positions, inv, axis, rotary):
+    """``math.py:231-243`` with three position components: ``x`` ``[B, heads, dim]``,
+    ``positions`` ``[B, 3]``; pair i turns by ``positions[:, axis[i]] * inv[i]``."""
+    half = rotary // 2
+    angles = (np.asarray(positions, np.float32)[:, axis] * inv[None, :]).astype(np.float32)
+    cs = bf16_round(np.cos(angles.astype(np.float64)).astype(np.float32))[:, None, :]
+    sn = bf16_round(np.sin(angles.astype(np.float64)).astype(np.float32))[:, None, :]
+    a, b = x[..., :half], x[..., half:rotary]
+    rot = np.concatenate([(a * cs - b * sn).astype(np.float32), (b * cs + a * sn).astype(np.float32)], -1)
+    return np.concatenate([bf16_round(rot), x[..., rotary:]], -1)
+
+
+def _rms(x, gamma, eps):
+    x = np.asarray(x, np.float32)
+    mean = np.mean(x.astype(np.float64) ** 2, axis=-1, keepdims=True)
+    r = (1.0 / np.sqrt(mean + eps)).astype(np.float32)
+    return bf16_round(((x * r).astype(np.float32) * np.asarray(gamma, np.float32)).astype(np.float32))
+
+
+def qsa_update(state, raw_k, lengths, positions, active, k_norm, eps, inv, axis, rotary, ratio):
+    """``attention_cache.py:86-97`` on NumPy state ``{index_keys [B, blocks, dim],
+    index_tail [B, ratio, dim], index_start [B, 3]}`` (in place)."""
+    lengths = np.asarray(lengths)
+    for b in range(len(lengths)):
+        slot = lengths[b] % ratio
+        if active[b]:
+            state["index_tail"][b, slot] = raw_k[b]
+            if slot == 0:
+                state["index_start"][b] = positions[b]
+    pooled = bf16_round(np.mean(state["index_tail"].astype(np.float64), axis=1).astype(np.float32))
+    block = qsa_rope(_rms(pooled, k_norm, eps)[:, None, :], state["index_start"], inv, axis, rotary)[:, 0]
+    for b in range(len(lengths)):
+        if active[b] and lengths[b] % ratio == ratio - 1:
+            state["index_keys"][b, lengths[b] // ratio] = block[b]
+    return state
+
+
+def qsa_query(raw_q, positions, q_norm, eps, inv, axis, rotary):
+    """``attention_cache.py:98-99``: rope(rms(raw_q, q_norm), positions), ``raw_q`` ``[B, heads, dim]``."""
+    return qsa_rope(_rms(raw_q, q_norm, eps), positions, inv, axis, rotary)

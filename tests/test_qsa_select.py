@@ -3,8 +3,9 @@
 CPU: the oracle's selection keeps the properties the reference's own test checks
 (test_qwen38_compute.py:120-190): the selected count, no duplicates, every tail token, only
 top-scoring blocks, no future token. GPU: the block scores against the oracle, the selection
-from the GPU's own scores bit-exact against the oracle's (ties included), and the selected
-tokens through the Q8 decode attention.
+from the GPU's own scores bit-exact against the oracle's (ties included), the selected
+tokens through the Q8 decode attention, and whole select_tokens decode steps (key update,
+query, selection) against the oracle.
 """
 
 import numpy as np
@@ -133,3 +134,57 @@ def test_selected_tokens_through_decode_attention(cuda_device):
     expected = kv.attention(q, keys, values, val)
     mx, l2 = rel_err(got, expected)
     assert mx < 1e-2 and l2 < 5e-3, (mx, l2)
+
+
+@pytest.mark.gpu
+def test_select_tokens_step_by_step_matches_oracle(cuda_device):
+    """Decode steps through the whole select_tokens (attention_cache.py:84-125), as the
+    reference's own test drives it (test_qwen38_compute.py:120-190): two rows, 67 steps,
+    positions (t, t // 2, t % 7). Each step the tail and block start match the oracle's update
+    on the same raw keys bit for bit, the block keys within the BF16 tolerance, and the
+    selection keeps the reference test's properties under the oracle's query scores."""
+    import torch
+
+    from qk_b200.attention_cache import IndexerConfig, empty_index_cache, select_tokens
+
+    ic = IndexerConfig(qsa_budget=32, indexer_heads=4, indexer_dim=64, indexer_compress=4, rotary_dim=32)
+    B, H, steps, T = 2, 256, 67, 68
+    rng = np.random.default_rng(33)
+    inputs = bf16_round(rng.normal(size=(B, steps, H)).astype(np.float32))
+    w = {"index_k": bf16_tensor(rng.normal(0, 0.1, (64, H)).astype(np.float32), cuda_device),
+         "index_q": bf16_tensor(rng.normal(0, 0.1, (4 * 64, H)).astype(np.float32), cuda_device),
+         "index_k_norm": bf16_tensor(rng.uniform(0.5, 1.5, 64).astype(np.float32), cuda_device),
+         "index_q_norm": bf16_tensor(rng.uniform(0.5, 1.5, 64).astype(np.float32), cuda_device)}
+    cache = empty_index_cache(B, T, ic, cuda_device)
+    state = {"index_keys": np.zeros((B, T // 4, 64), np.float32), "index_tail": np.zeros((B, 4, 64), np.float32),
+             "index_start": np.zeros((B, 3), np.int32)}
+    inv, axis = (t.cpu().numpy() for t in ic.rope_tables("cpu"))
+    kn, qn = to_f32(w["index_k_norm"]), to_f32(w["index_q_norm"])
+    active = np.ones(B, bool)
+    for step in range(steps):
+        x = bf16_tensor(inputs[:, step], cuda_device)
+        pos = np.broadcast_to(np.array([step, step // 2, step % 7], np.int32), (B, 3)).copy()
+        lengths = np.full(B, step, np.int32)
+        indices, valid, _ = select_tokens(x, w, cache, torch.from_numpy(lengths), torch.from_numpy(pos),
+                                          torch.ones(B, dtype=torch.bool), ic)
+        raw_k = to_f32(torch.matmul(x, w["index_k"].t()))
+        kv.qsa_update(state, raw_k, lengths, pos, active, kn, ic.eps, inv, axis, 32, 4)
+        np.testing.assert_array_equal(to_f32(cache["index_tail"]), state["index_tail"])
+        np.testing.assert_array_equal(cache["index_start"].cpu().numpy(), state["index_start"])
+        got_keys = to_f32(cache["index_keys"])
+        assert rel_err(got_keys, state["index_keys"])[0] < 1e-2 if state["index_keys"].any() else True
+        state["index_keys"] = got_keys.copy()  # the selection below scores the kernel's keys
+        raw_q = to_f32(torch.matmul(x, w["index_q"].t())).reshape(B, 4, 64)
+        query = kv.qsa_query(raw_q, pos, qn, ic.eps, inv, axis, 32)
+        scores = kv.qsa_scores(query, got_keys, lengths, 4)
+        n = (step + 1) // 4
+        idx, val = indices.cpu().numpy(), valid.cpu().numpy()
+        for row in range(B):
+            sel = idx[row, val[row]]
+            assert len(sel) == min(n, 8) * 4 + (step + 1) % 4
+            assert len(np.unique(sel)) == len(sel)
+            assert set(range(n * 4, step + 1)).issubset(set(sel))
+            assert sel.max(initial=0) <= step
+            chosen = sel[sel < n * 4] // 4
+            if n > 8:
+                assert np.min(scores[row, chosen]) >= np.partition(scores[row, :n], n - 8)[n - 8] - 1e-2
