@@ -8,14 +8,14 @@ NumPy restatements of ``kaggle/qwen38_tpu/math.py``:
   cosine and sine rounded to BF16;
 * the q/gate split and q_norm / k_norm of ``attention_cache.py:129-135``;
 * the shared expert's gate ``sigmoid(linear(x, shared_router))`` of ``math.py:282-283``;
+* ``checked_argmax`` of ``run.py:46-55``.
 
-and a whole decode step of the synthetic stack (``decode_step``) built from these, the KV
-oracle and the routed-FFN oracle.
+The decoder stack's GPU test checks each stage of a layer with these, the KV oracle and the
+routed-FFN oracle.
 """
 
 import numpy as np
 
-from . import kv, moe
 from .precision import bf16_round, sigmoid
 
 
@@ -64,36 +64,6 @@ def shared_gate(h, shared_router):
 def linear(x, w):
     """``compute_cast(x @ w^T)`` with exact accumulation, math.py:10-16."""
     return bf16_round((np.asarray(x, np.float64) @ np.asarray(w, np.float64).T).astype(np.float32))
-
-
-def decode_step(x, layers, caches, indices, positions, cfg):
-    """One decode step of the synthetic stack (the layer order of ``qk_b200.decoder``).
-
-    ``layers``: per layer a dict of FP32-valued weights (``w_qkv``, ``w_o``, norms,
-    ``router``, ``shared_router``) and raw GGUF expert bytes ``gate``/``up``/``down``
-    ``[experts + 1, bytes]`` (the last one the shared expert); ``caches``: per layer the
-    KV oracle's cache dict, updated in place. Returns the new BF16-valued ``x``."""
-    hq, kvh, hd = cfg.query_heads, cfg.kv_heads, cfg.head_dim
-    x = bf16_round(np.asarray(x, np.float32))
-    for L, cache in zip(layers, caches):
-        h = rms(x, L["attn_norm"], cfg.eps)
-        qkv = linear(h, L["w_qkv"])
-        q, gate, k, v = qk_norm_rope(qkv, L["q_norm"], L["k_norm"], positions, hq, kvh, hd, cfg.rotary_dim,
-                                     cfg.rope_theta, cfg.eps)
-        kv.write_quantized(cache, k, v, positions, np.ones(len(positions), bool), kvh, hd)
-        keys = kv.read_quantized(cache["k"], cache["k_scale"], indices, kvh, hd)
-        values = kv.read_quantized(cache["v"], cache["v_scale"], indices, kvh, hd)
-        mask = np.arange(indices.shape[1])[None, :] <= np.asarray(positions)[:, None]
-        o = kv.attention(q, keys, values, mask, gate)
-        x = bf16_round((x + linear(o.reshape(len(x), -1), L["w_o"])).astype(np.float32))
-        h2 = rms(x, L["ffn_norm"], cfg.eps)
-        ids, w, _ = moe.routes(h2, L["router"], cfg.top_k)
-        ids = np.concatenate([ids, np.full((len(x), 1), cfg.experts, np.int32)], 1)
-        w = np.concatenate([w, shared_gate(h2, L["shared_router"])[:, None]], 1)
-        y = moe.expert_ffn(L["gate"], L["up"], L["down"], h2, ids, w, gate_type=cfg.qtype, up_type=cfg.qtype,
-                           down_type=cfg.qtype, hidden=cfg.hidden, intermediate=cfg.intermediate)
-        x = bf16_round((x + y).astype(np.float32))
-    return x
 
 
 def checked_argmax(logits):
