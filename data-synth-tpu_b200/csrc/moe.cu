@@ -463,7 +463,10 @@ static int moe_forward_impl(const qk_moe_desc* desc, const uint8_t* gate, const 
   const size_t routes = static_cast<size_t>(B) * d.top_k;
   // The wide form (128-token chunks) when the routes average at least 64 tokens per expert
   // the rank holds (prefill-sized batches); the narrow form (32-token chunks) otherwise.
-  const bool wide = routes >= 64 * static_cast<size_t>(d.num_experts);
+#ifndef QK_WIDE_MIN_TOKENS
+#define QK_WIDE_MIN_TOKENS 64
+#endif
+  const bool wide = routes >= QK_WIDE_MIN_TOKENS * static_cast<size_t>(d.num_experts);
   const int ctok = wide ? kWideTok : kMaxTok;
   const size_t route_smem = (3 * static_cast<size_t>(d.num_experts) + 1) * 4 + (routes <= kStagedRoutes ? routes * 6 : 0);
   int rc = allow_smem(reinterpret_cast<const void*>(moe_route_kernel), route_smem);
