@@ -129,8 +129,9 @@ __global__ void dequant_rows_kernel(const uint8_t* __restrict__ raw, int qtype, 
 // ---- tiled layout (the format is stated in oracle/layout.py and rowtile.cuh) ----
 
 inline int tile_bytes(int qtype) {
-  return qtype == QK_TYPE_Q6_K ? HalfTile<QType::Q6_K>::kBytes
+  return qtype == QK_TYPE_Q6_K   ? HalfTile<QType::Q6_K>::kBytes
          : qtype == QK_TYPE_Q4_K ? HalfTile<QType::Q4_K>::kBytes
+         : qtype == QK_TYPE_Q8_0 ? HalfTile<QType::Q8_0>::kBytes
                                  : 0;
 }
 
@@ -243,6 +244,44 @@ __global__ void repack_q4_kernel(const uint8_t* __restrict__ in, uint8_t* __rest
   }
 }
 
+// Q8_0: super-blocks of 8 GGUF blocks (rowtile.cuh). One CTA per tile; byte `off` of the
+// tile is chunk off / 1024, row (off % 1024) / 16, byte off % 16 of the chunk. Raw rows have
+// nblk32 blocks of 34 bytes; super-block blocks past them are zero.
+template <bool kPack>
+__global__ void repack_q8_kernel(const uint8_t* __restrict__ in, uint8_t* __restrict__ out, int64_t rows,
+                                 int64_t nblk, int64_t nblk32, int32_t* bad_scales) {
+  constexpr int TB = HalfTile<QType::Q8_0>::kBytes;
+  const int64_t tile = blockIdx.x;
+  const int64_t strip = tile / nblk, kb = tile % nblk;
+  for (int off = threadIdx.x; off < TB; off += blockDim.x) {
+    const int c = off >> 10, r = (off & 1023) >> 4, byte = off & 15;
+    const int64_t row = strip * kTileRows + r;
+    int j, src;  // GGUF block of the super-block and byte of it
+    if (c == 0) {
+      j = byte >> 1;
+      src = byte & 1;
+    } else {
+      const int code = (c - 1) * 16 + byte;
+      j = code >> 5;
+      src = 2 + (code & 31);
+    }
+    const int64_t blk = kb * 8 + j;
+    const bool exists = row < rows && blk < nblk32;
+    const int64_t raw_off = (row * nblk32 + blk) * 34 + src;
+    const int64_t tiled_off = tile * TB + off;
+    if (kPack) {
+      uint8_t v = 0;
+      if (exists) {
+        v = in[raw_off];
+        if (bad_scales && c == 0 && src == 1 && (v & 0x7c) == 0x7c) atomicAdd(bad_scales, 1);
+      }
+      out[tiled_off] = v;
+    } else if (exists) {
+      out[raw_off] = in[tiled_off];
+    }
+  }
+}
+
 // Decode of the tiled layout through the half-block decoders of the tensor-core kernels:
 // kExact selects the reference-exact form (signed zeros included), otherwise the fused
 // form the kernels run (equal values; a zero may carry the other sign). One thread per
@@ -314,8 +353,8 @@ int64_t qk_tiled_bytes(int qtype, int64_t rows, int64_t row_width) {
 static int repack_common(const uint8_t* in, int qtype, int64_t rows, int64_t row_width,
                          uint8_t* out, int32_t* bad, qk_stream_t stream, bool pack) {
   const int tb = tile_bytes(qtype);
-  if (tb == 0) return set_error(QK_ERR_UNSUPPORTED_TYPE, "tiled layout supports Q6_K and Q4_K; got %d", qtype);
-  QK_REQUIRE(rows > 0 && row_width > 0, "Expected [output_features, ceil(input_features / 256), bytes]");
+  if (tb == 0) return set_error(QK_ERR_UNSUPPORTED_TYPE, "tiled layout supports Q6_K, Q4_K and Q8_0; got %d", qtype);
+  QK_REQUIRE(rows > 0 && row_width > 0, "Expected [output_features, ceil(input_features / block), bytes]");
   QK_REQUIRE(in && out, "null pointer");
   const int64_t nblk = (row_width + 255) / 256;
   const int64_t tiles = (rows + kTileRows - 1) / kTileRows * nblk;
@@ -325,6 +364,10 @@ static int repack_common(const uint8_t* in, int qtype, int64_t rows, int64_t row
   if (qtype == QK_TYPE_Q6_K) {
     if (pack) repack_q6_kernel<true><<<g, kTileRows, 0, st>>>(in, out, rows, nblk, bad);
     else repack_q6_kernel<false><<<g, kTileRows, 0, st>>>(in, out, rows, nblk, nullptr);
+  } else if (qtype == QK_TYPE_Q8_0) {
+    const int64_t nblk32 = (row_width + 31) / 32;
+    if (pack) repack_q8_kernel<true><<<g, 256, 0, st>>>(in, out, rows, nblk, nblk32, bad);
+    else repack_q8_kernel<false><<<g, 256, 0, st>>>(in, out, rows, nblk, nblk32, nullptr);
   } else {
     if (pack) repack_q4_kernel<true><<<g, 256, 0, st>>>(in, out, rows, nblk, bad);
     else repack_q4_kernel<false><<<g, 256, 0, st>>>(in, out, rows, nblk, nullptr);
@@ -345,7 +388,7 @@ int qk_unpack_rows(const uint8_t* tiled, int qtype, int64_t rows, int64_t row_wi
 
 int qk_dequantize_tiled(const uint8_t* tiled, int qtype, int64_t rows, int64_t row_width,
                         int out_dtype, void* out, qk_stream_t stream) {
-  if (tile_bytes(qtype) == 0) return set_error(QK_ERR_UNSUPPORTED_TYPE, "tiled layout supports Q6_K and Q4_K; got %d", qtype);
+  if (tile_bytes(qtype) == 0) return set_error(QK_ERR_UNSUPPORTED_TYPE, "tiled layout supports Q6_K, Q4_K and Q8_0; got %d", qtype);
   QK_REQUIRE(rows > 0 && row_width > 0, "rows and row_width must be positive");
   const bool fused = (out_dtype & QK_DECODE_FUSED) != 0;
   out_dtype &= ~QK_DECODE_FUSED;
@@ -360,6 +403,9 @@ int qk_dequantize_tiled(const uint8_t* tiled, int qtype, int64_t rows, int64_t r
   if (qtype == QK_TYPE_Q6_K) {
     if (fused) dequant_tiled_kernel<QType::Q6_K, false><<<grid, 2 * kTileRows, 0, st>>>(tiled, rows, row_width, nblk, bf, out);
     else dequant_tiled_kernel<QType::Q6_K, true><<<grid, 2 * kTileRows, 0, st>>>(tiled, rows, row_width, nblk, bf, out);
+  } else if (qtype == QK_TYPE_Q8_0) {
+    if (fused) dequant_tiled_kernel<QType::Q8_0, false><<<grid, 2 * kTileRows, 0, st>>>(tiled, rows, row_width, nblk, bf, out);
+    else dequant_tiled_kernel<QType::Q8_0, true><<<grid, 2 * kTileRows, 0, st>>>(tiled, rows, row_width, nblk, bf, out);
   } else {
     if (fused) dequant_tiled_kernel<QType::Q4_K, false><<<grid, 2 * kTileRows, 0, st>>>(tiled, rows, row_width, nblk, bf, out);
     else dequant_tiled_kernel<QType::Q4_K, true><<<grid, 2 * kTileRows, 0, st>>>(tiled, rows, row_width, nblk, bf, out);

@@ -79,8 +79,8 @@ size_t qk_quant_gemm_workspace_bytes(int64_t M, int64_t K, int64_t N) {
 
 int qk_quant_gemm(const uint16_t* x, int64_t M, int64_t K, const uint8_t* w_tiled, int qtype,
                   int64_t N, float* out, void* workspace, size_t workspace_bytes, qk_stream_t stream) {
-  if (qtype != QK_TYPE_Q6_K && qtype != QK_TYPE_Q4_K)
-    return set_error(QK_ERR_UNSUPPORTED_TYPE, "packed projection supports Q6_K and Q4_K; got %d", qtype);
+  if (qtype != QK_TYPE_Q6_K && qtype != QK_TYPE_Q4_K && qtype != QK_TYPE_Q8_0)
+    return set_error(QK_ERR_UNSUPPORTED_TYPE, "packed projection supports Q6_K, Q4_K and Q8_0; got %d", qtype);
   QK_REQUIRE(M >= 0 && K > 0 && N > 0, "x must be a nonempty [M,K] BF16 array");
   QK_REQUIRE(M < (1 << 30) && K < (1 << 30) && N < (1 << 30), "dimension too large");
   if (M == 0) return QK_OK;
@@ -113,8 +113,9 @@ int qk_quant_gemm(const uint16_t* x, int64_t M, int64_t K, const uint8_t* w_tile
   a.out = a.ksplit ? reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + xt_bytes(M, K)) : out;
   const int64_t items = static_cast<int64_t>(a.n_chunks_dense) * a.items_per_chunk * (a.ksplit ? nkb : 1);
   const int grid = static_cast<int>(items < sms ? items : sms);
-  int rc = qtype == QK_TYPE_Q6_K ? launch_umma<QType::Q6_K, kModeDense>(a, grid, st)
-                                 : launch_umma<QType::Q4_K, kModeDense>(a, grid, st);
+  int rc = qtype == QK_TYPE_Q6_K   ? launch_umma<QType::Q6_K, kModeDense>(a, grid, st)
+           : qtype == QK_TYPE_Q4_K ? launch_umma<QType::Q4_K, kModeDense>(a, grid, st)
+                                   : launch_umma<QType::Q8_0, kModeDense>(a, grid, st);
   if (rc || !a.ksplit) return rc;
   const int64_t mn = M * N;
   int64_t rgrid = (mn + 255) / 256;

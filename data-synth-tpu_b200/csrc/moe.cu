@@ -88,7 +88,7 @@ size_t layout(const qk_moe_desc& d, int max_tokens, uint8_t* base, Workspace* ws
   uint8_t* re = take(R * 4);
   uint8_t* er = take(R * 4);
   uint8_t* xt = take(rows * d.hidden * 2);
-  uint8_t* ht = take(rows * d.intermediate * 2);
+  uint8_t* ht = take(rows * ((d.intermediate + 255) / 256 * 256) * 2);  // whole 256-value K blocks
   uint8_t* y = take(R * d.hidden * 2);
   if (ws) {
     ws->meta = reinterpret_cast<MoeMeta*>(meta);
@@ -401,6 +401,8 @@ __global__ void cast_kernel(const float* __restrict__ in, uint16_t* __restrict__
 }
 
 bool supported(int t) { return t == QK_TYPE_Q6_K || t == QK_TYPE_Q4_K; }
+// The down projection also takes Q8_0 (the real checkpoints' down type, checkpoints/q6.json).
+bool supported_down(int t) { return supported(t) || t == QK_TYPE_Q8_0; }
 
 }  // namespace
 }  // namespace qk
@@ -426,10 +428,15 @@ static int moe_forward_impl(const qk_moe_desc* desc, const uint8_t* gate, const 
                             void* const* events, float* yr = nullptr, int phase = kFull) {
   QK_REQUIRE(desc, "null descriptor");
   const qk_moe_desc& d = *desc;
-  if (!supported(d.gate_type) || d.gate_type != d.up_type || d.gate_type != d.down_type)
-    return set_error(QK_ERR_UNSUPPORTED_TYPE, "expert types must all be Q6_K or all Q4_K (got %d/%d/%d)", d.gate_type, d.up_type, d.down_type);
+  if (!supported(d.gate_type) || d.gate_type != d.up_type || !supported_down(d.down_type))
+    return set_error(QK_ERR_UNSUPPORTED_TYPE,
+                     "expert types: gate and up both Q6_K or both Q4_K, down Q6_K, Q4_K or Q8_0 (got %d/%d/%d)",
+                     d.gate_type, d.up_type, d.down_type);
   QK_REQUIRE(d.hidden > 0 && d.hidden % 256 == 0, "hidden must be a positive multiple of 256");
-  QK_REQUIRE(d.intermediate > 0 && d.intermediate % 256 == 0, "intermediate must be a positive multiple of 256");
+  // The gate/up tiles zero-pad their rows to 64; the down projection reads whole GGUF blocks
+  // of intermediate (256 values for the k-quants, 32 for Q8_0).
+  QK_REQUIRE(d.intermediate > 0 && d.intermediate % (d.down_type == QK_TYPE_Q8_0 ? 32 : 256) == 0,
+             "intermediate must be a positive multiple of the down type's block (256, or 32 for Q8_0)");
   QK_REQUIRE(d.num_experts > 0 && d.num_experts <= 4096, "num_experts must be in [1, 4096]");
   QK_REQUIRE(d.top_k > 0 && d.top_k <= kMaxTopK, "top_k must be in [1, %d]", kMaxTopK);
   QK_REQUIRE(B >= 0, "batch must be non-negative");
@@ -460,6 +467,13 @@ static int moe_forward_impl(const qk_moe_desc* desc, const uint8_t* gate, const 
     return QK_OK;
   }
   mark(0);
+  if (d.intermediate % 256) {
+    // The down pass reads whole 256-value K blocks of h; the padded channels must be zero
+    // (their decoded weights are zero, and 0 * NaN would not be).
+    const size_t bytes = rows_bound(d, B) * ((d.intermediate + 255) / 256 * 256) * 2;
+    const cudaError_t e = cudaMemsetAsync(ws.ht, 0, bytes, st);
+    if (e != cudaSuccess) return cuda_error(e, "clearing the padded activation tiles");
+  }
   const size_t routes = static_cast<size_t>(B) * d.top_k;
   // The wide form (128-token chunks) when the routes average at least 64 tokens per expert
   // the rank holds (prefill-sized batches); the narrow form (32-token chunks) otherwise.
@@ -495,8 +509,8 @@ static int moe_forward_impl(const qk_moe_desc* desc, const uint8_t* gate, const 
   gu.wb = up;
   gu.expert_bytes = qk_tiled_bytes(d.gate_type, d.intermediate, d.hidden);
   gu.nkb = d.hidden / 256;
-  gu.tiles64 = d.intermediate / kTileRows;
-  gu.items_per_chunk = d.intermediate / kTileRows;  // 64 rows of I (gate + up) per MMA tile
+  gu.tiles64 = (d.intermediate + kTileRows - 1) / kTileRows;
+  gu.items_per_chunk = gu.tiles64;  // 64 rows of I (gate + up) per MMA tile
   gu.xt = ws.xt;
   gu.n_chunks_p = &ws.meta->n_chunks;
   gu.chunk_off = ws.chunk_off;
@@ -507,14 +521,14 @@ static int moe_forward_impl(const qk_moe_desc* desc, const uint8_t* gate, const 
   gu.offsets = ws.offsets;
   gu.n_active_p = &ws.meta->n_active;
   gu.ht = ws.ht;
-  gu.nkb_out = d.intermediate / 256;
+  gu.nkb_out = (d.intermediate + 255) / 256;
   gu.nrows = d.intermediate;
   gu.status = &ws.meta->status;
   UArgs dn = gu;
   dn.wa = down;
   dn.wb = nullptr;
   dn.expert_bytes = qk_tiled_bytes(d.down_type, d.hidden, d.intermediate);
-  dn.nkb = d.intermediate / 256;
+  dn.nkb = (d.intermediate + 255) / 256;
   dn.tiles64 = d.hidden / kTileRows;
   dn.items_per_chunk = d.hidden / (2 * kTileRows);
   dn.xt = ws.ht;
@@ -531,10 +545,12 @@ static int moe_forward_impl(const qk_moe_desc* desc, const uint8_t* gate, const 
     rc = q6 ? launch_umma<QType::Q6_K, kModeGateUp>(gu, sms, st) : launch_umma<QType::Q4_K, kModeGateUp>(gu, sms, st);
   if (rc) return rc;
   mark(2);
-  if (wide)
-    rc = q6 ? launch_umma<QType::Q6_K, kModeDown, true>(dn, sms, st) : launch_umma<QType::Q4_K, kModeDown, true>(dn, sms, st);
+  if (d.down_type == QK_TYPE_Q8_0)
+    rc = wide ? launch_umma<QType::Q8_0, kModeDown, true>(dn, sms, st) : launch_umma<QType::Q8_0, kModeDown>(dn, sms, st);
+  else if (d.down_type == QK_TYPE_Q6_K)
+    rc = wide ? launch_umma<QType::Q6_K, kModeDown, true>(dn, sms, st) : launch_umma<QType::Q6_K, kModeDown>(dn, sms, st);
   else
-    rc = q6 ? launch_umma<QType::Q6_K, kModeDown>(dn, sms, st) : launch_umma<QType::Q4_K, kModeDown>(dn, sms, st);
+    rc = wide ? launch_umma<QType::Q4_K, kModeDown, true>(dn, sms, st) : launch_umma<QType::Q4_K, kModeDown>(dn, sms, st);
   if (rc) return rc;
   mark(3);
   if (phase == kPartial) return QK_OK;

@@ -36,7 +36,7 @@
 
 namespace qk {
 
-enum class QType { Q6_K = 14, Q4_K = 12 };
+enum class QType { Q6_K = 14, Q4_K = 12, Q8_0 = 8 };
 
 constexpr int kTileRows = 64;
 
@@ -220,6 +220,62 @@ struct HalfTile<QType::Q4_K> {
           const uint32_t code = (word >> (4 * (j & 1))) & 0x0f0f0f0fu;
           code4<kExact, true>(code, ds, 0.f, dm, out[2 * i], out[2 * i + 1]);
         }
+        emit(jj * 16 + half16 * 8, out);
+      }
+    }
+  }
+};
+
+// Q8_0 (gguf_quant.py:111-114: v = f32(d) * q, 32 values per 34-byte block) in super-blocks
+// of 256 values = 8 GGUF blocks, 272 bytes per row: chunk 0 holds the 8 FP16 scales, chunks
+// 1 .. 16 the 256 int8 codes (16 per chunk). A row whose width is not a multiple of 256 is
+// padded with zero blocks (d = 0, codes 0), which decode to zeros.
+// Half h: scale bytes 8h .. 8h + 7 of chunk 0 and code chunks 1 + 8h .. 8 + 8h.
+template <>
+struct HalfTile<QType::Q8_0> {
+  static constexpr int kBlockBytes = 272;
+  static constexpr int kChunks = 17;
+  static constexpr int kBytes = kTileRows * kBlockBytes;  // 17408
+
+  struct Regs {
+    uint32_t d[2];   // the 4 FP16 scales of the half
+    uint32_t w[32];  // its 128 codes
+  };
+
+  __device__ __forceinline__ static void clear(Regs& r) {
+    r.d[0] = r.d[1] = 0;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) r.w[i] = 0;
+  }
+
+  template <int h>
+  __device__ __forceinline__ static void load(Regs& r, const uint8_t* tile, int row) {
+    const uint2 s = *reinterpret_cast<const uint2*>(tile + row * 16 + 8 * h);
+    r.d[0] = s.x;
+    r.d[1] = s.y;
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      const uint4 v = lds128(tile + ((1 + 8 * h + c) * kTileRows + row) * 16);
+      r.w[4 * c] = v.x;
+      r.w[4 * c + 1] = v.y;
+      r.w[4 * c + 2] = v.z;
+      r.w[4 * c + 3] = v.w;
+    }
+  }
+
+  // Codes are signed; flipping their sign bits gives code + 128 in [1, 255], decoded with
+  // offset 128: (1024 + code + 128) d - 1152 d = code d, exact in FP32 (19 significant bits).
+  template <bool kExact, int h, typename Emit>
+  __device__ __forceinline__ static void decode(const Regs& r, Emit&& emit) {
+#pragma unroll
+    for (int jj = 0; jj < 4; ++jj) {  // GGUF block 4h + jj of the super-block
+      const float d = f16_to_f32(static_cast<uint16_t>(r.d[jj >> 1] >> (16 * (jj & 1))));
+#pragma unroll
+      for (int half16 = 0; half16 < 2; ++half16) {
+        uint32_t out[8];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          code4<kExact, false>(r.w[8 * jj + 4 * half16 + i] ^ 0x80808080u, d, 128.f, 0.f, out[2 * i], out[2 * i + 1]);
         emit(jj * 16 + half16 * 8, out);
       }
     }

@@ -414,7 +414,7 @@ __global__ void __launch_bounds__(Form<W>::kThreads, 1) umma_proj_kernel(const U
           for (int col = 0; col < 32; ++col) {
             if (col >= gcols) break;
             const float other = __shfl_xor_sync(0xffffffffu, acc[col], 1);
-            if ((col < half) == (t == 0)) {
+            if ((col < half) == (t == 0) && R < A.nrows) {  // rows past I: zero-padded tile rows
               const float gb = bf16_round(t == 0 ? acc[col] : other);
               const float ub = bf16_round(t == 0 ? other : acc[col]);
               const float act = bf16_round(__fmul_rn(gb, sigmoid_ref(gb)));  // silu, math.py:19-20

@@ -202,8 +202,10 @@ def expert_parallel(
 ):
     """Return the routed FFN for this process's experts; see the module docstring.
 
-    ``compute`` "int8_q8" only changes Q8_0 projections in the reference; with the
-    Q6_K/Q4_K types this library takes it computes exactly like "bf16". ``row_tile`` and
+    ``compute`` "int8_q8" only changes Q8_0 projections in the reference (its W8A8 dot,
+    qwen38_tpu/compute.py:20-34); with Q6_K/Q4_K projections it computes exactly like
+    "bf16". A Q8_0 down projection runs the "bf16" form (dequantise, BF16 dot); "int8_q8"
+    with a Q8_0 down is refused rather than computed differently. ``row_tile`` and
     ``group_size`` shape the reference's XLA loops and do not change results; they are
     validated and otherwise unused (the kernels tile rows by 32 and stream experts).
     """
@@ -225,13 +227,17 @@ def expert_parallel(
 
         if dist.get_world_size(group) % tensor_parallel:
             raise ValueError("Tensor parallel size must divide the device count")
-        if (intermediate // tensor_parallel) % 256 or intermediate % tensor_parallel:
-            raise ValueError("Tensor slices must contain whole down quantization blocks")
     types = tuple(normalize_qtype(t) for t in (gate_type, up_type, down_type))
-    if len(set(types)) != 1 or types[0] not in ("Q6_K", "Q4_K"):
-        raise ValueError("expert kernels take gate/up/down all Q6_K or all Q4_K")
-    if hidden % 256 or intermediate % 256:
-        raise ValueError("hidden and intermediate must be multiples of 256")
+    if types[0] != types[1] or types[0] not in ("Q6_K", "Q4_K") or types[2] not in ("Q6_K", "Q4_K", "Q8_0"):
+        raise ValueError("expert kernels take gate and up both Q6_K or both Q4_K, down Q6_K, Q4_K or Q8_0")
+    if compute == "int8_q8" and types[2] == "Q8_0":
+        raise ValueError("the int8_q8 expert policy (W8A8 Q8_0 dot) is not built; use compute='bf16'")
+    # the down projection reads whole GGUF blocks of intermediate (gate/up tiles pad rows to 64)
+    step = 32 if types[2] == "Q8_0" else 256
+    if tensor_parallel > 1 and ((intermediate // tensor_parallel) % step or intermediate % tensor_parallel):
+        raise ValueError("Tensor slices must contain whole down quantization blocks")
+    if hidden % 256 or intermediate % step:
+        raise ValueError(f"hidden must be a multiple of 256 and intermediate a multiple of {step}")
     return ExpertFFN(group, *types, hidden, intermediate, tensor_parallel)
 
 

@@ -3,7 +3,7 @@
 Mirrors ``kaggle/packed_q6``: ``pack_q6``/``unpack_q6`` (``layout.py:49-108``) and
 ``q6_matmul`` (``kernel.py:98-148``), with this build's tile layout (64 rows x 256
 values per tile, see ``csrc/rowtile.cuh``) instead of the TPU SoA tiles. ``pack_rows``
-and ``quant_matmul`` are the type-generic forms (Q6_K, Q4_K).
+and ``quant_matmul`` are the type-generic forms (Q6_K, Q4_K, Q8_0).
 """
 
 from dataclasses import dataclass
@@ -14,7 +14,7 @@ import torch
 from . import _lib
 from .quant import BLOCK_LAYOUTS, GGML_TYPE, normalize_qtype
 
-TILED_TYPES = ("Q6_K", "Q4_K")
+TILED_TYPES = ("Q6_K", "Q4_K", "Q8_0")
 
 
 @dataclass(frozen=True)
@@ -26,7 +26,9 @@ class PackedWeights:
 
     @property
     def input_blocks(self):
-        return (self.input_features + 255) // 256
+        """GGUF blocks per row (256 values for the k-quants, 32 for Q8_0)."""
+        values = BLOCK_LAYOUTS[self.qtype][0]
+        return (self.input_features + values - 1) // values
 
     def storage(self):
         original = self.output_features * self.input_blocks * BLOCK_LAYOUTS[self.qtype][1]
@@ -58,7 +60,7 @@ def _device_raw(raw, device):
 
 
 def pack_rows(raw, input_features, qtype="Q6_K", device=None):
-    """Repack ``uint8[N, ceil(K/256), bpb]`` GGUF rows into device tiles (no arithmetic)."""
+    """Repack ``uint8[N, ceil(K/block_values), bpb]`` GGUF rows into device tiles (no arithmetic)."""
     name = normalize_qtype(qtype)
     if name not in TILED_TYPES:
         raise ValueError(f"tiled layout supports {TILED_TYPES}; got {name}")
@@ -69,10 +71,10 @@ def pack_rows(raw, input_features, qtype="Q6_K", device=None):
         raise TypeError(f"GGUF {name} input must have dtype uint8")
     if isinstance(raw, torch.Tensor) and raw.dtype != torch.uint8:
         raise TypeError(f"GGUF {name} input must have dtype uint8")
-    blocks = (input_features + 255) // 256
-    size = BLOCK_LAYOUTS[name][1]
+    values, size = BLOCK_LAYOUTS[name]
+    blocks = (input_features + values - 1) // values
     if raw.ndim != 3 or raw.shape[0] < 1 or tuple(raw.shape[1:]) != (blocks, size):
-        raise ValueError("Expected [output_features, ceil(input_features / 256), bytes_per_block]")
+        raise ValueError(f"Expected [output_features, ceil(input_features / {values}), bytes_per_block]")
     src = _device_raw(raw, device)
     rows = int(src.shape[0])
     out = torch.empty(tiled_bytes(name, rows, input_features), dtype=torch.uint8, device=device)
@@ -91,7 +93,7 @@ def pack_q6(raw, input_features, device=None):
 
 
 def unpack_rows(packed):
-    """Inverse byte transform -> ``uint8[N, ceil(K/256), bpb]`` on the device."""
+    """Inverse byte transform -> ``uint8[N, ceil(K/block_values), bpb]`` on the device."""
     size = BLOCK_LAYOUTS[packed.qtype][1]
     out = torch.empty((packed.output_features, packed.input_blocks, size), dtype=torch.uint8,
                       device=packed.data.device)

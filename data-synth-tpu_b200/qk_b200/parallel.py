@@ -110,7 +110,7 @@ def put_expert_bytes(raw, kind, qtype, hidden, intermediate, *, rank=0, world=1,
     bad = torch.zeros(1, dtype=torch.int32, device=device)
     stream = _lib.stream_handle(device)
     with torch.cuda.device(device):
-        if rows % 16 == 0:  # experts never share a 16-row strip: one launch for all
+        if rows % 64 == 0:  # experts never share a 64-row tile: one launch for all
             _lib.call("qk_repack_rows", _lib.ptr(src), GGML_TYPE[name], count * rows, width,
                       _lib.ptr(out), _lib.ptr(bad), stream)
         else:

@@ -9,7 +9,10 @@ tile the first ``16 * C`` bytes of every row's (re-packed) block are stored as
 rows' FP16 scales as ``[row][2 B]`` (block bytes 208..209). A decode thread of the
 tensor-core kernels reads chunk ``c`` of its row ``r`` at ``(c*64 + r)*16``.
 
-Q4_K blocks keep their GGUF bytes. Q6_K blocks re-pack the 6-bit codes losslessly: sub-block
+Q4_K blocks keep their GGUF bytes. Q8_0 (32-value blocks of an FP16 scale and 32 int8
+codes) groups the 8 blocks of a 256-value column into one 272-byte super-block: chunk 0 is
+the 8 scales (``[block][2 B]``), chunks 1..16 the 256 codes in position order; blocks past
+the row's end are zero. Q6_K blocks re-pack the 6-bit codes losslessly: sub-block
 ``j`` (values ``16j .. 16j+15``) becomes three little-endian words ``W0, W1, W2`` at bytes
 ``12j .. 12j+11``; byte ``i`` of ``Wn`` holds code ``4n + i`` in bits 0..5 and bits
 ``2n .. 2n+1`` of code ``12 + i`` in bits 6..7. Bytes 192..207 are the sub-scales.
@@ -18,8 +21,8 @@ Q4_K blocks keep their GGUF bytes. Q6_K blocks re-pack the 6-bit codes losslessl
 import numpy as np
 
 TILE_ROWS = 64
-BLOCK_BYTES = {"Q6_K": 210, "Q4_K": 144}
-CHUNKS = {"Q6_K": 13, "Q4_K": 9}
+BLOCK_BYTES = {"Q6_K": 210, "Q4_K": 144, "Q8_0": 272}  # Q8_0: the 8-block super-block
+CHUNKS = {"Q6_K": 13, "Q4_K": 9, "Q8_0": 17}
 TILE_BYTES = {q: TILE_ROWS * b for q, b in BLOCK_BYTES.items()}
 
 
@@ -79,9 +82,32 @@ def unrepack_q6_codes(packed):
     return out
 
 
+def _q8_super(raw):
+    """Q8_0 ``uint8[rows, nblk32, 34]`` -> super-blocks ``uint8[rows, ceil(nblk32 / 8), 272]``."""
+    rows, nblk32, _ = raw.shape
+    nsup = (nblk32 + 7) // 8
+    full = np.zeros((rows, nsup * 8, 34), np.uint8)
+    full[:, :nblk32] = raw
+    full = full.reshape(rows, nsup, 8, 34)
+    return np.concatenate([full[..., :2].reshape(rows, nsup, 16), full[..., 2:].reshape(rows, nsup, 256)], -1)
+
+
+def _q8_blocks(sup, nblk32):
+    """Inverse of :func:`_q8_super`."""
+    rows, nsup, _ = sup.shape
+    out = np.zeros((rows, nsup, 8, 34), np.uint8)
+    out[..., :2] = sup[..., :16].reshape(rows, nsup, 8, 2)
+    out[..., 2:] = sup[..., 16:].reshape(rows, nsup, 8, 32)
+    return out.reshape(rows, nsup * 8, 34)[:, :nblk32]
+
+
 def tile(raw, qtype):
-    """``uint8[rows, nblk, bpb]`` -> flat tiled bytes."""
+    """``uint8[rows, nblk, bpb]`` (Q8_0: ``[rows, nblk32, 34]``) -> flat tiled bytes."""
     raw = np.asarray(raw, np.uint8)
+    if qtype == "Q8_0":
+        if raw.shape[-1] != 34:
+            raise ValueError("Q8_0 blocks contain 34 bytes")
+        raw = _q8_super(raw)
     rows, nblk, size = raw.shape
     if size != BLOCK_BYTES[qtype]:
         raise ValueError(f"{qtype} blocks contain {BLOCK_BYTES[qtype]} bytes")
@@ -111,4 +137,6 @@ def untile(tiled, qtype, rows, row_width):
     if qtype == "Q6_K":
         out[..., 208:210] = t[..., 16 * c * TILE_ROWS :].reshape(g, nblk, TILE_ROWS, 2)
     raw = out.transpose(0, 2, 1, 3).reshape(-1, nblk, size)[:rows]
+    if qtype == "Q8_0":
+        return _q8_blocks(raw, (row_width + 31) // 32)
     return unrepack_q6_codes(raw) if qtype == "Q6_K" else raw

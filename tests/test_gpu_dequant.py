@@ -72,6 +72,28 @@ def test_repack_is_lossless_and_fragment_decode_is_bit_exact(cuda_device, qtype,
     np.testing.assert_array_equal(fused, expected)
 
 
+@pytest.mark.parametrize("rows,width", [(1, 32), (17, 96), (65, 263), (130, 2048), (64, 2080)])
+def test_q8_0_repack_is_lossless_and_fragment_decode_is_bit_exact(cuda_device, rows, width):
+    """Q8_0 rows (32-value blocks) in 256-value tile columns: ragged last columns are zero."""
+    import torch
+
+    from qk_b200.packed import dequantize_packed, pack_rows, unpack_rows
+
+    rng = np.random.default_rng(rows * 5 + width)
+    raw = rng.integers(0, 256, (rows, (width + 31) // 32, 34), dtype=np.uint8)
+    raw[..., 0:2] = rng.uniform(-0.05, 0.05, raw.shape[:2]).astype("<f2").view(np.uint8).reshape(*raw.shape[:2], 2)
+    raw[..., 2] = 0x80  # the code -128 in every block
+    packed = pack_rows(raw, width, "Q8_0", cuda_device)
+    assert packed.data.numel() == layout.tiled_bytes("Q8_0", rows, width)
+    np.testing.assert_array_equal(packed.data.cpu().numpy(), layout.tile(raw, "Q8_0"))
+    np.testing.assert_array_equal(unpack_rows(packed).cpu().numpy(), raw)
+    expected = bf16_round(gguf.dequantize_rows(raw, "Q8_0", width))
+    for dtype in (torch.bfloat16, torch.float32):  # FP32 out: the BF16 MMA operands, widened
+        got = to_f32(dequantize_packed(packed, dtype))
+        np.testing.assert_array_equal(got.view(np.uint32), expected.view(np.uint32))
+        np.testing.assert_array_equal(to_f32(dequantize_packed(packed, dtype, fused=True)), expected)
+
+
 @pytest.mark.parametrize("scale", [np.inf, -np.inf, np.nan])
 def test_nonfinite_block_scale_rejected(cuda_device, scale):
     from qk_b200.packed import pack_q6
@@ -120,7 +142,7 @@ def test_packed_projection_matches_reference_fp64_dot(golden, cuda_device):
         np.testing.assert_allclose(got, data[f"expected_{key}"], rtol=2e-5, atol=2e-4)
 
 
-@pytest.mark.parametrize("qtype", ["Q6_K", "Q4_K"])
+@pytest.mark.parametrize("qtype", ["Q6_K", "Q4_K", "Q8_0"])
 @pytest.mark.parametrize("m", [1, 5, 33, 70])
 def test_quant_matmul_against_oracle(cuda_device, qtype, m):
     from qk_b200.packed import pack_rows, quant_matmul

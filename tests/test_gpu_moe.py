@@ -13,23 +13,25 @@ pytestmark = pytest.mark.gpu
 LAYER_TOL = 1e-2
 
 
-def make_experts(rng, count, hidden, intermediate, qtype):
+def make_experts(rng, count, hidden, intermediate, qtype, down_type=None):
     raw = {}
     for kind, (rows, width) in (("gate", (intermediate, hidden)), ("up", (intermediate, hidden)),
                                 ("down", (hidden, intermediate))):
         w = rng.normal(0, 0.02, (count, rows, width)).astype(np.float32)
-        raw[kind] = gguf.encode(w, qtype).reshape(count, -1)
+        raw[kind] = gguf.encode(w, (down_type or qtype) if kind == "down" else qtype).reshape(count, -1)
     return raw
 
 
-def run_layer(device, raw, qtype, hidden, intermediate, x, ids, weights):
+def run_layer(device, raw, qtype, hidden, intermediate, x, ids, weights, down_type=None):
     import torch
 
     from qk_b200.experts import expert_parallel
     from qk_b200.parallel import put_expert_bytes
 
-    dev = {k: put_expert_bytes(v, k, qtype, hidden, intermediate, device=device) for k, v in raw.items()}
-    fn = expert_parallel(gate_type=qtype, up_type=qtype, down_type=qtype, hidden=hidden,
+    down_type = down_type or qtype
+    dev = {k: put_expert_bytes(v, k, down_type if k == "down" else qtype, hidden, intermediate, device=device)
+           for k, v in raw.items()}
+    fn = expert_parallel(gate_type=qtype, up_type=qtype, down_type=down_type, hidden=hidden,
                          intermediate=intermediate)
     out = fn(dev["gate"], dev["up"], dev["down"], bf16_tensor(x, device),
              torch.from_numpy(np.asarray(ids, np.int32)).to(device), bf16_tensor(weights, device))
@@ -37,16 +39,21 @@ def run_layer(device, raw, qtype, hidden, intermediate, x, ids, weights):
     return to_f32(out), fn, dev
 
 
-def test_routed_ffn_matches_reference_numpy_oracle_golden(golden, cuda_device):
+@pytest.mark.parametrize("label", ["mixed", "q6"])
+def test_routed_ffn_matches_reference_numpy_oracle_golden(golden, cuda_device, label):
+    """The reference's own routed-FFN case ("mixed": Q6_K gate/up, Q8_0 down, I = 32,
+    routing_validation.py:193-243) and its Q6_K-down twin, against the reference oracle's
+    BF16 outputs."""
     from make_golden import ROUTING_BATCHES, routing_inputs
 
     data = golden("routing_ffn.npz")
-    packed, batches, down_type, hidden, intermediate, count = routing_inputs("q6", gguf.encode_q8_0)
+    packed, batches, down_type, hidden, intermediate, count = routing_inputs(label, gguf.encode_q8_0)
     flat = {k: v.reshape(count, -1) for k, v in packed.items()}
     for batch in ROUTING_BATCHES:
         ids, weights, source = batches[batch]
-        got, _, _ = run_layer(cuda_device, flat, "Q6_K", hidden, intermediate, source, ids, weights)
-        expected = (data[f"q6_b{batch}_bf16_bits"].astype(np.uint32) << 16).view(np.float32)
+        got, _, _ = run_layer(cuda_device, flat, "Q6_K", hidden, intermediate, source, ids, weights,
+                              down_type=down_type)
+        expected = (data[f"{label}_b{batch}_bf16_bits"].astype(np.uint32) << 16).view(np.float32)
         # routing_validation.py:262 BF16 tolerance
         np.testing.assert_allclose(got, expected, atol=3e-3, rtol=3e-3)
         np.testing.assert_array_equal(got[np.all(weights == 0, axis=-1)], 0)
@@ -114,6 +121,25 @@ def test_wide_form_chunks_of_128_tokens(cuda_device, qtype):
     mx, l2 = rel_err(got, expected)
     assert mx < LAYER_TOL and l2 < 2e-3, (mx, l2)
     np.testing.assert_array_equal(got[5::11], 0)
+
+
+@pytest.mark.parametrize("qtype,intermediate,batch", [
+    ("Q6_K", 512, 8), ("Q6_K", 640, 8), ("Q4_K", 96, 5), ("Q6_K", 640, 700)])
+def test_q8_0_down_projection(cuda_device, qtype, intermediate, batch):
+    """Q6_K/Q4_K gate and up with a Q8_0 down (the type mix of the reference's checkpoints):
+    I a multiple of 256, ragged against the 256-value K blocks (640: two and a half, 96: a
+    padded gate/up tile), and 700 tokens on 8 experts (the wide form)."""
+    hidden, count, k = 512, 8, 2
+    rng = np.random.default_rng(intermediate + batch)
+    raw = make_experts(rng, count, hidden, intermediate, qtype, "Q8_0")
+    ids = rng.integers(0, count, (batch, k)).astype(np.int32)
+    weights = bf16_round(rng.uniform(0.05, 1.0, (batch, k)).astype(np.float32))
+    x = rng.normal(size=(batch, hidden)).astype(np.float32)
+    got, _, _ = run_layer(cuda_device, raw, qtype, hidden, intermediate, x, ids, weights, down_type="Q8_0")
+    expected = moe.expert_ffn(raw["gate"], raw["up"], raw["down"], x, ids, weights, gate_type=qtype,
+                              up_type=qtype, down_type="Q8_0", hidden=hidden, intermediate=intermediate)
+    mx, l2 = rel_err(got, expected)
+    assert mx < LAYER_TOL and l2 < 2e-3, (mx, l2)
 
 
 def test_zero_weights_give_zero_and_ids_outside_rank_are_ignored(cuda_device):
@@ -207,6 +233,12 @@ def test_contract_errors(cuda_device):
     with pytest.raises(ValueError, match="row tile"):
         expert_parallel(gate_type="Q6_K", up_type="Q6_K", down_type="Q6_K", hidden=256,
                         intermediate=256, row_tile=0)
-    with pytest.raises(ValueError):
+    with pytest.raises(ValueError, match="int8_q8"):
         expert_parallel(gate_type="Q6_K", up_type="Q6_K", down_type="Q8_0", hidden=256,
+                        intermediate=256, compute="int8_q8")
+    with pytest.raises(ValueError, match="gate and up"):
+        expert_parallel(gate_type="Q6_K", up_type="Q4_K", down_type="Q6_K", hidden=256,
                         intermediate=256)
+    with pytest.raises(ValueError, match="multiple of 256"):
+        expert_parallel(gate_type="Q6_K", up_type="Q6_K", down_type="Q6_K", hidden=256,
+                        intermediate=96)

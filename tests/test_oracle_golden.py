@@ -150,3 +150,18 @@ def test_encoders_round_trip_through_reference_decoder_layout(qtype):
     assert rel < (0.02 if qtype == "Q6_K" else 0.08)
     tiled = layout.tile(raw, qtype)
     np.testing.assert_array_equal(layout.untile(tiled, qtype, 48, 512), raw)
+
+
+@pytest.mark.parametrize("rows,width", [(1, 32), (48, 512), (70, 288)])
+def test_q8_0_tiles_round_trip_and_place_codes_in_position_order(rows, width):
+    rng = np.random.default_rng(rows + width)
+    raw = gguf.encode(rng.normal(0, 0.02, (rows, width)).astype(np.float32), "Q8_0")
+    tiled = layout.tile(raw, "Q8_0")
+    assert tiled.size == layout.tiled_bytes("Q8_0", rows, width)
+    np.testing.assert_array_equal(layout.untile(tiled, "Q8_0", rows, width), raw)
+    nsup = (width + 255) // 256
+    body = tiled.reshape(-1, nsup, 17, 64, 16)  # [row tile][column][chunk][row][16 B]
+    r, j = rows - 1, raw.shape[1] - 1
+    np.testing.assert_array_equal(body[r // 64, j // 8, 0, r % 64, 2 * (j % 8) : 2 * (j % 8) + 2], raw[r, j, :2])
+    codes = body[r // 64, j // 8, 1:, r % 64].reshape(256)[32 * (j % 8) : 32 * (j % 8) + 32]
+    np.testing.assert_array_equal(codes, raw[r, j, 2:])
