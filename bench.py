@@ -578,7 +578,7 @@ def stack_report(device, args):
 
     from qk_b200.decoder import StackConfig, SyntheticDecoder
 
-    cfg = StackConfig(layers=args.stack_layers, qtype=args.qtype)
+    cfg = StackConfig(layers=args.stack_layers, qtype=args.qtype, down_qtype=args.stack_down_qtype)
     peak, _ = hbm_peak()
     t_build = time.time()
     model = SyntheticDecoder(cfg, device, seed=1)
@@ -615,7 +615,8 @@ def stack_report(device, args):
         torch.cuda.synchronize(device)
     return {"workload": "synthetic 48-layer MoE decoder stack (configs[3]), 1 GPU",
             "layers": cfg.layers, "context": cfg.context, "experts": cfg.experts, "top_k": cfg.top_k,
-            "shared_experts": 1, "qtype": cfg.qtype, "weights": "synthetic (random code bytes, fixed block scales)",
+            "shared_experts": 1, "qtype": cfg.qtype, "down_qtype": cfg.down_qtype or cfg.qtype,
+            "weights": "synthetic (random code bytes, fixed block scales)",
             "l2": "inputs larger than L2 (packed experts of 48 layers)", "build_s": build_s, "batches": rows}
 
 
@@ -777,6 +778,8 @@ def main():
     parser.add_argument("--stack-only", action="store_true", help="only the decoder stack (one GPU)")
     parser.add_argument("--stack-batches", type=lambda t: [int(v) for v in t.split(",")], default=[1, 8, 64])
     parser.add_argument("--stack-layers", type=int, default=48)
+    parser.add_argument("--stack-down-qtype", choices=("Q6_K", "Q4_K", "Q8_0"), default=None,
+                        help="down projection type of the stack's experts (default: --qtype)")
     parser.add_argument("--stack-steps", type=int, default=10)
     parser.add_argument("--ref-budget", type=float, default=10.0,
                         help="seconds of CPU work per reference sample")

@@ -66,13 +66,16 @@ class StackConfig:
     rope_theta: float = 10_000_000.0
     eps: float = 1e-6
     qtype: str = "Q6_K"
+    down_qtype: str | None = None  # None: the same as qtype; "Q8_0": the checkpoints' type mix
     context: int = 8192
     page: int = 256
 
 
 # FP16 block-scale bytes inside one raw block and the scale giving a ~0.02 value spread:
 # Q6_K d (offset 208) * int8 sub-scale * (q - 32); Q4_K d (offset 0) * 6-bit scale * q - dmin.
-_SCALE_BYTES = {"Q6_K": ((208, 2.0 ** -16),), "Q4_K": ((0, 2.0 ** -11), (2, 2.0 ** -12))}
+# Q8_0 d (offset 0) * int8 code.
+_SCALE_BYTES = {"Q6_K": ((208, 2.0 ** -16),), "Q4_K": ((0, 2.0 ** -11), (2, 2.0 ** -12)),
+                "Q8_0": ((0, 2.0 ** -12),)}
 
 
 def synthetic_expert_bytes(qtype, count, rows, width, generator, device):
@@ -103,9 +106,9 @@ class LayerWeights:
         self.k_norm = torch.ones(hd, dtype=torch.bfloat16, device=device)
         self.router = normal((cfg.experts, H), torch.float32)
         self.shared_router = normal((H,))
-        qtype = normalize_qtype(cfg.qtype)
         self.experts = {}
         for kind in ("gate", "up", "down"):
+            qtype = normalize_qtype((cfg.down_qtype or cfg.qtype) if kind == "down" else cfg.qtype)
             rows, width = expert_shape(kind, H, cfg.intermediate)
             raw = synthetic_expert_bytes(qtype, cfg.experts + 1, rows, width, generator, device)
             self.experts[kind] = put_expert_bytes(raw, kind, qtype, H, cfg.intermediate, device=device)
@@ -129,8 +132,8 @@ class SyntheticDecoder:
         half = cfg.rotary_dim // 2
         inv = np.power(np.float32(cfg.rope_theta), -np.arange(half, dtype=np.float32) * 2 / np.float32(cfg.rotary_dim))
         self.inv_freq = torch.from_numpy(inv.astype(np.float32)).to(self.device)
-        q = normalize_qtype(cfg.qtype)
-        self.desc = _lib.MoeDesc(GGML_TYPE[q], GGML_TYPE[q], GGML_TYPE[q], cfg.hidden, cfg.intermediate,
+        q, qd = normalize_qtype(cfg.qtype), normalize_qtype(cfg.down_qtype or cfg.qtype)
+        self.desc = _lib.MoeDesc(GGML_TYPE[q], GGML_TYPE[q], GGML_TYPE[qd], cfg.hidden, cfg.intermediate,
                                  cfg.experts + 1, 0, cfg.top_k + 1)
 
     def state(self, batch, seed=2):

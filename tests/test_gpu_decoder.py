@@ -112,14 +112,14 @@ def _np(t):
     return to_f32(t) if t.dtype == __import__("torch").bfloat16 else t.float().cpu().numpy()
 
 
-@pytest.mark.parametrize("qtype", ["Q6_K", "Q4_K"])
-def test_one_decoder_layer_stage_by_stage(cuda_device, qtype):
+@pytest.mark.parametrize("qtype,down_qtype", [("Q6_K", None), ("Q4_K", None), ("Q6_K", "Q8_0")])
+def test_one_decoder_layer_stage_by_stage(cuda_device, qtype, down_qtype):
     import torch
 
     from qk_b200.decoder import StackConfig, SyntheticDecoder
 
     cfg = StackConfig(layers=1, hidden=512, intermediate=256, experts=8, top_k=2, query_heads=8, kv_heads=2,
-                      head_dim=128, rotary_dim=32, context=256, page=16, qtype=qtype)
+                      head_dim=128, rotary_dim=32, context=256, page=16, qtype=qtype, down_qtype=down_qtype)
     model = SyntheticDecoder(cfg, cuda_device, seed=11)
     state = model.state(3, seed=12)
     L = model.layers[0]
@@ -164,12 +164,14 @@ def test_one_decoder_layer_stage_by_stage(cuda_device, qtype):
     assert (ids_all[:, cfg.top_k] == cfg.experts).all()
     assert np.max(np.abs(w_all[:, cfg.top_k] - layer.shared_gate(h2, _np(L.shared_router)))) <= 2 ** -8
     raw = {}
+    down_qtype = down_qtype or qtype
     for kind in ("gate", "up", "down"):
         rows, width = (H, cfg.intermediate) if kind == "down" else (cfg.intermediate, H)
         t = L.experts[kind].cpu().numpy()
-        raw[kind] = np.stack([layout.untile(t[e], qtype, rows, width).reshape(-1) for e in range(t.shape[0])])
+        kt = down_qtype if kind == "down" else qtype
+        raw[kind] = np.stack([layout.untile(t[e], kt, rows, width).reshape(-1) for e in range(t.shape[0])])
     y = moe.expert_ffn(raw["gate"], raw["up"], raw["down"], h2, ids_all, w_all, gate_type=qtype, up_type=qtype,
-                       down_type=qtype, hidden=H, intermediate=cfg.intermediate)
+                       down_type=down_qtype, hidden=H, intermediate=cfg.intermediate)
     mx, l2 = rel_err(to_f32(state.y), y)
     assert mx < 1e-2 and l2 < 5e-3, ("experts", mx, l2)
     np.testing.assert_array_equal(to_f32(state.x), bf16_round((x1 + to_f32(state.y)).astype(np.float32)))
