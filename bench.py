@@ -116,6 +116,43 @@ def step_bytes(qtype, ids):
     return active * packed_bytes_per_expert(qtype) + rows * HIDDEN * 2 * 2, active
 
 
+PARITY_TOL = 1e-2  # north-star layer tolerance: max relative error (BF16, FP32 accumulation)
+PARITY_ROWS = 64
+
+
+def moe_parity(raw, qtype, res):
+    """Max relative error of a seeded sample of the timed step's output rows against the
+    oracle's routed FFN (experts.py:61-131 restated); only the sampled rows' experts are
+    decoded, so this costs seconds. Runs after the timed region."""
+    import numpy as np
+    import torch
+
+    from oracle import moe
+
+    x, ids, weights = res["x"], res["ids"], res["weights"]
+    rows = np.sort(np.random.default_rng(1000 + res["m"]).choice(x.shape[0], PARITY_ROWS, replace=False))
+    expected = moe.expert_ffn(raw["gate"], raw["up"], raw["down"], x[rows], ids[rows], weights[rows],
+                              gate_type=qtype, up_type=qtype, down_type=qtype, hidden=HIDDEN,
+                              intermediate=INTER)
+    got = res["out"].to(torch.float32).cpu().numpy()[rows]
+    err = float(np.max(np.abs(got - expected)) / max(np.max(np.abs(expected)), 1e-30))
+    return {"moe_rows": PARITY_ROWS, "moe_max_rel_err": err, "tolerance": PARITY_TOL,
+            "ok": bool(np.all(np.isfinite(got)) and err < PARITY_TOL)}
+
+
+def sweep_row(qtype, r, peak):
+    gbs = r["bytes"] / (r["ms"] * 1e-3) / 1e9
+    gu = r["gate_up_bytes"] / (r["stage_ms"][1] * 1e-3) / 1e9
+    return {"qtype": qtype, "m": r["m"], "ms_per_step": r["ms"], "gbs": gbs, "frac": gbs / peak,
+            "gate_up_gbs": gu, "gate_up_frac": gu / peak,
+            "tflops": r["rows"] * FLOPS_PER_ROW / (r["ms"] * 1e-3) / 1e12,
+            "rows_per_s": r["rows"] / (r["ms"] * 1e-3), "active_experts": r["active"],
+            "stage_ms": dict(zip(("route_dispatch", "gate_up", "down", "combine"), r["stage_ms"]))}
+
+
+FLOPS_PER_ROW = 2 * (2 * INTER * HIDDEN + HIDDEN * INTER)
+
+
 def kernel_bytes(qtype, ids):
     """Algorithmic bytes of the gate/up (dominant) launch: gate+up packed bytes of the routed
     experts + x rows read + h rows written."""
@@ -314,7 +351,8 @@ def b200_arm(args):
                          hidden=HIDDEN, intermediate=INTER)
     stream = torch.cuda.current_stream(device)
 
-    def run_m(m, steps, warmup, profile, sync=True):
+    def run_m(m, steps, warmup, profile, sync=True, qtype=None):
+        qtype = qtype or args.qtype
         x, ids, weights = workload(m, rank)
         xd = torch.from_numpy(x).to(device).to(torch.bfloat16)
         idd = torch.from_numpy(ids).to(device)
@@ -376,9 +414,9 @@ def b200_arm(args):
                     acc[i] += events[i].elapsed_time(events[i + 1])
             stage_ms = [a / reps for a in acc]
         fn.check_status()
-        nbytes, active = step_bytes(args.qtype, ids)
+        nbytes, active = step_bytes(qtype, ids)
         return dict(m=m, ms=ms, bytes=nbytes, active=active, rows=rows, stage_ms=stage_ms,
-                    gate_up_bytes=kernel_bytes(args.qtype, ids), x=x, ids=ids, weights=weights,
+                    gate_up_bytes=kernel_bytes(qtype, ids), x=x, ids=ids, weights=weights,
                     out=out)
 
     peak, peak_kind = hbm_peak()
@@ -403,11 +441,24 @@ def b200_arm(args):
     e2e = e2e_measure(fn, tensors, device, args, res, rank)
 
     sweep = []
-    if args.sweep and rank == 0 and world == 1:
+    if not args.no_sweep and rank == 0 and world == 1:
         for m in SWEEP_M:
-            r = run_m(m, max(5, args.steps // 4), 2, False)
-            sweep.append({"m": m, "ms_per_step": r["ms"], "gbs": r["bytes"] / (r["ms"] * 1e-3) / 1e9,
-                          "rows_per_s": r["rows"] / (r["ms"] * 1e-3), "active_experts": r["active"]})
+            r = run_m(m, max(5, args.steps // 4), 3, True)
+            sweep.append(sweep_row(args.qtype, r, peak))
+        other = "Q4_K" if args.qtype == "Q6_K" else "Q6_K"
+        raw_o = synth_experts(other, EXPERTS)
+        tensors_o = {k: put_expert_bytes(v, k, other, HIDDEN, INTER, device=device) for k, v in raw_o.items()}
+        fn_o = expert_parallel(gate_type=other, up_type=other, down_type=other, hidden=HIDDEN, intermediate=INTER)
+        saved = (tensors, fn)
+        tensors, fn = tensors_o, fn_o
+        for m in SWEEP_M:
+            r = run_m(m, max(5, args.steps // 4), 3, True, qtype=other)
+            sweep.append(sweep_row(other, r, peak))
+        tensors, fn = saved
+        del tensors_o, raw_o
+
+    # parity of the timed step: a seeded sample of output rows against the oracle
+    parity = moe_parity(raw, args.qtype, res) if rank == 0 else None
 
     gate_up_ms = res["stage_ms"][1]
     achieved = res["gate_up_bytes"] / (gate_up_ms * 1e-3) / 1e9
@@ -429,9 +480,17 @@ def b200_arm(args):
     }
     if sweep:
         line["sweep"] = sweep
+    if parity is not None:
+        line["parity"] = parity
     if rank == 0 and not args.no_attention:
         line["attention"] = attention_report(device, args)
         line["qsa_select"] = qsa_report(device, args)
+        errs = [r["parity_max_rel_err"] for r in line["attention"]["configs"]]
+        line["parity"]["attention_rows"] = len(errs)
+        line["parity"]["attention_max_rel_err"] = max(errs)
+        line["parity"]["ok"] = line["parity"]["ok"] and max(errs) < PARITY_TOL
+    if parity is not None:
+        line["parity_checked"] = bool(line["parity"]["ok"])
     if rank == 0 and world == 1:
         line["layer"] = layer_report(raw, device, args)
     if rank == 0 and world == 1 and not args.no_stack:
@@ -454,67 +513,110 @@ ATTN_CONFIGS = ((1, 4096), (8, 4096), (32, 4096), (1, 32768), (8, 32768), (32, 3
 ATTN_SLOT_BYTES = 2 * 512 + 2 * 16 * 2  # K + V codes (2 kv heads x 256) + BF16 scales (16 groups)
 
 
-def attention_sweep(device, reps=20, configs=ATTN_CONFIGS):
-    """Q8 KV decode attention: 16 q / 2 kv heads, head dim 256,
-    one query token per sequence, every slot of the context attended through a page table
-    that is a random permutation (seed 0) of 256-token pages. K/V codes and BF16 scales
-    are synthetic (uniform codes, scales in [0.001, 0.021)); the kernel's cost does not
-    depend on their values. Bytes per step = B * ctx * 1088 (codes + scales); each timed
-    call follows an L2 flush."""
+def attention_inputs(device, batch, ctx):
+    """Inputs of one configs[2] call: 16 q / 2 kv heads, head dim 256, one query token per
+    sequence, every slot of the context attended through a page table that is a random
+    permutation (seed 0) of 256-token pages. K/V codes and BF16 scales are synthetic
+    (uniform codes, scales in [0.001, 0.021)); the kernel's cost does not depend on their
+    values. The same tensors feed the timed sweep and the parity tests."""
     import numpy as np
     import torch
 
     from qk_b200 import _lib
 
     lib = _lib.load()
+    g = torch.Generator(device=device).manual_seed(batch * 7 + ctx)
+    k = torch.randint(-127, 128, (batch, ctx, 512), dtype=torch.int8, device=device, generator=g)
+    v = torch.randint(-127, 128, (batch, ctx, 512), dtype=torch.int8, device=device, generator=g)
+    ks = (torch.rand((batch * 16, ctx), device=device, generator=g) * 0.02 + 0.001).to(torch.bfloat16)
+    vs = (torch.rand((batch * 16, ctx), device=device, generator=g) * 0.02 + 0.001).to(torch.bfloat16)
+    rng = np.random.default_rng(0)
+    pages = ctx // 256
+    table = np.stack([rng.permutation(pages) for _ in range(batch)])
+    slots = np.arange(ctx)
+    idx = torch.from_numpy(np.ascontiguousarray((table[:, slots // 256] * 256 + slots % 256).astype(np.int32))).to(device)
+    lengths = torch.full((batch,), ctx - 1, dtype=torch.int32, device=device)
+    q = torch.randn((batch, 16, 256), device=device, generator=g).to(torch.bfloat16)
+    out = torch.empty((batch, 16, 256), dtype=torch.bfloat16, device=device)
+    need = int(lib.qk_kv_q8_attention_workspace_bytes(batch, ctx, 16, 2, 256))
+    ws = torch.empty(max(need, 1), dtype=torch.uint8, device=device)
+    return dict(batch=batch, ctx=ctx, device=device, k=k, v=v, ks=ks, vs=vs, idx=idx, lengths=lengths, q=q,
+                out=out, ws=ws, need=need)
+
+
+def attention_call(inp):
+    """One decode attention call through the C ABI on `inp` (attention_inputs); returns out."""
+    from qk_b200 import _lib
+
+    lib = _lib.load()
+    batch, ctx, need = inp["batch"], inp["ctx"], inp["need"]
+    _lib.check(lib.qk_kv_q8_decode_attention(
+        _lib.ptr(inp["q"]), _lib.ptr(inp["k"]), _lib.ptr(inp["v"]), _lib.ptr(inp["ks"]), _lib.ptr(inp["vs"]),
+        _lib.ptr(inp["idx"]), None, _lib.ptr(inp["lengths"]), None, batch, ctx, ctx, 16, 2, 256,
+        _lib.ptr(inp["out"]), _lib.ptr(inp["ws"]) if need else None, need, _lib.stream_handle(inp["device"])))
+    return inp["out"]
+
+
+def attention_parity(inp, row):
+    """Max relative error of row `row` of the last call's output against the oracle
+    (attention_cache.py:152-170 restated)."""
+    import numpy as np
+    import torch
+
+    from oracle import kv
+
+    def f32(t):
+        return t.detach().to(torch.float32).cpu().numpy()
+
+    ctx = inp["ctx"]
+    sel = inp["idx"][row : row + 1].cpu().numpy()
+    codes = {n: inp[n][row : row + 1].cpu().numpy() for n in ("k", "v")}
+    planes = {n: f32(inp[n + "s"][row * 16 : (row + 1) * 16]) for n in ("k", "v")}
+    keys = kv.read_quantized(codes["k"], planes["k"], sel, 2, 256)
+    values = kv.read_quantized(codes["v"], planes["v"], sel, 2, 256)
+    mask = np.arange(ctx)[None, :] <= int(inp["lengths"][row])
+    expected = kv.attention(f32(inp["q"][row : row + 1]), keys, values, mask)
+    got = f32(inp["out"][row : row + 1])
+    return float(np.max(np.abs(got - expected)) / max(np.max(np.abs(expected)), 1e-30))
+
+
+def attention_sweep(device, reps=20, configs=ATTN_CONFIGS, parity=False):
+    """Q8 KV decode attention over `configs`, inputs from
+    attention_inputs. Bytes per step = B * ctx * 1088 (codes + scales); each timed call
+    follows an L2 flush. With `parity`, one row of each configuration's output is checked
+    against the oracle after the timing."""
+    import torch
+
     stream = torch.cuda.current_stream(device)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
     results = []
     for batch, ctx in configs:
-        g = torch.Generator(device=device).manual_seed(batch * 7 + ctx)
-        k = torch.randint(-127, 128, (batch, ctx, 512), dtype=torch.int8, device=device, generator=g)
-        v = torch.randint(-127, 128, (batch, ctx, 512), dtype=torch.int8, device=device, generator=g)
-        ks = (torch.rand((batch * 16, ctx), device=device, generator=g) * 0.02 + 0.001).to(torch.bfloat16)
-        vs = (torch.rand((batch * 16, ctx), device=device, generator=g) * 0.02 + 0.001).to(torch.bfloat16)
-        rng = np.random.default_rng(0)
-        pages = ctx // 256
-        table = np.stack([rng.permutation(pages) for _ in range(batch)])
-        slots = np.arange(ctx)
-        idx = torch.from_numpy(np.ascontiguousarray((table[:, slots // 256] * 256 + slots % 256).astype(np.int32))).to(device)
-        lengths = torch.full((batch,), ctx - 1, dtype=torch.int32, device=device)
-        q = torch.randn((batch, 16, 256), device=device, generator=g).to(torch.bfloat16)
-        out = torch.empty((batch, 16, 256), dtype=torch.bfloat16, device=device)
-        need = int(lib.qk_kv_q8_attention_workspace_bytes(batch, ctx, 16, 2, 256))
-        ws = torch.empty(max(need, 1), dtype=torch.uint8, device=device)
-
-        def call():
-            _lib.check(lib.qk_kv_q8_decode_attention(
-                _lib.ptr(q), _lib.ptr(k), _lib.ptr(v), _lib.ptr(ks), _lib.ptr(vs), _lib.ptr(idx), None,
-                _lib.ptr(lengths), None, batch, ctx, ctx, 16, 2, 256, _lib.ptr(out),
-                _lib.ptr(ws) if need else None, need, _lib.stream_handle(device)))
-
+        inp = attention_inputs(device, batch, ctx)
         for _ in range(3):
-            call()
+            attention_call(inp)
         times = []
         for _ in range(reps):
             flush.zero_()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(stream)
-            call()
+            attention_call(inp)
             e1.record(stream)
             torch.cuda.synchronize(device)
             times.append(e0.elapsed_time(e1))
         ms = statistics.median(times)
         nbytes = batch * ctx * ATTN_SLOT_BYTES
-        results.append({"batch": batch, "ctx": ctx, "us": ms * 1e3, "gbs": nbytes / (ms * 1e-3) / 1e9,
-                        "tokens_per_s": batch / (ms * 1e-3)})
-        del k, v, ks, vs
+        r = {"batch": batch, "ctx": ctx, "us": ms * 1e3, "gbs": nbytes / (ms * 1e-3) / 1e9,
+             "tokens_per_s": batch / (ms * 1e-3)}
+        if parity:
+            r["parity_max_rel_err"] = attention_parity(inp, batch - 1)
+        results.append(r)
+        del inp
     return results
 
 
 def attention_report(device, args):
     peak_gbs, _ = hbm_peak()
-    attn = attention_sweep(device, args.attn_reps, parse_attn_configs(args.attn_configs))
+    attn = attention_sweep(device, args.attn_reps, parse_attn_configs(args.attn_configs), parity=True)
     for r in attn:
         r["frac"] = r["gbs"] / peak_gbs
     return {"kernel": "attn_stream_kernel + attn_merge_kernel (Q8 KV, 16q/2kv, hd 256)",
@@ -765,7 +867,8 @@ def main():
     parser.add_argument("--m", type=int, default=16, help="tokens per expert")
     parser.add_argument("--qtype", choices=("Q6_K", "Q4_K"), default="Q6_K")
     parser.add_argument("--soak", type=float, default=1.0, help="untimed seconds before timing")
-    parser.add_argument("--sweep", action="store_true", help="also time M in {1,4,16,64,256}")
+    parser.add_argument("--no-sweep", action="store_true",
+                        help="skip the M in {1,4,16,64,256} sweep over Q6_K and Q4_K")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--no-attention", action="store_true", help="skip the Q8 KV attention sweep")
     parser.add_argument("--attention-only", action="store_true",

@@ -584,9 +584,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           alpha[hh] = 1.f;
           pr[hh] = pr[2 + hh] = 0.f;
         } else {
-          alpha[hh] = __expf(m_run[hh] - m_new);
-          pr[hh] = __expf(pr[hh] - m_new);
-          pr[2 + hh] = __expf(pr[2 + hh] - m_new);
+          alpha[hh] = exp_ref(m_run[hh] - m_new);
+          pr[hh] = exp_ref(pr[hh] - m_new);
+          pr[2 + hh] = exp_ref(pr[2 + hh] - m_new);
         }
         m_run[hh] = m_new;
       }
@@ -657,7 +657,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int hh = 0; hh < 2; ++hh) {
         float M = -INFINITY;
         for (int w = hl_w; w < kAttnWarps; w += kg) M = fmaxf(M, m_s[w * kHeads + 2 * c + hh]);
-        f[hh] = m_run[hh] == -INFINITY ? 0.f : expf(m_run[hh] - M);
+        f[hh] = m_run[hh] == -INFINITY ? 0.f : exp_ref(m_run[hh] - M);
         if (g == 0) f_s[warp * kHeads + 2 * c + hh] = f[hh];
       }
       float* ob = o_buf + warp * kHeads * G::kOP;
@@ -763,8 +763,8 @@ __global__ void __launch_bounds__(kMergeThreads) attn_merge_kernel(AttnArgs a, i
     for (int u = 0; u < 4; ++u) {
       const float M = fmaxf(m, pm[u]);
       if (M == -INFINITY) continue;
-      const float fo = m == -INFINITY ? 0.f : expf(m - M);
-      const float fn = pm[u] == -INFINITY ? 0.f : expf(pm[u] - M);
+      const float fo = m == -INFINITY ? 0.f : exp_ref(m - M);
+      const float fn = pm[u] == -INFINITY ? 0.f : exp_ref(pm[u] - M);
       l = __fadd_rn(__fmul_rn(l, fo), __fmul_rn(pl[u], fn));
       const float xs[8] = {x[u][0].x, x[u][0].y, x[u][0].z, x[u][0].w,
                            x[u][1].x, x[u][1].y, x[u][1].z, x[u][1].w};
@@ -786,7 +786,7 @@ __global__ void __launch_bounds__(kMergeThreads) attn_merge_kernel(AttnArgs a, i
   for (int i = 0; i < 8; ++i) O[i] = 0.f;
   for (int k = 0; k < groups; ++k) {
     const int t = k * dthreads + dt;
-    const float fk = sm_m[t] == -INFINITY ? 0.f : expf(sm_m[t] - M);
+    const float fk = sm_m[t] == -INFINITY ? 0.f : exp_ref(sm_m[t] - M);
     L = __fadd_rn(L, __fmul_rn(sm_l[t], fk));
 #pragma unroll
     for (int i = 0; i < 8; ++i) O[i] = __fadd_rn(O[i], __fmul_rn(sm_o[t * 8 + i], fk));
@@ -820,7 +820,7 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(const float* __restri
     float L = 0.f, O = 0.f;
     for (int k = 0; k < R; ++k) {
       const float* st = parts + k * set + rows * hd + row * 2;
-      const float f = st[0] == -INFINITY ? 0.f : expf(st[0] - M);
+      const float f = st[0] == -INFINITY ? 0.f : exp_ref(st[0] - M);
       L = __fadd_rn(L, __fmul_rn(st[1], f));
       O = __fadd_rn(O, __fmul_rn(parts[k * set + row * hd + d], f));
     }

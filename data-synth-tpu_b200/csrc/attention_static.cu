@@ -12,14 +12,18 @@
 // Limit: kStaticScratchBytes (16 MiB). The split kernel runs one CTA per SM and each CTA
 // leaves at most two partial rows per KV head, so the workspace query never exceeds
 // 2 * SMs * kv_heads * (16 + 8 * head_dim) * 4 bytes whatever B and S are: 4.9 MB for 2 KV
-// heads at head_dim 256 and 9.9 MB for 8 KV heads at head_dim 128 on a 148-SM B200. A
-// geometry whose query exceeds the array is refused with QK_ERR_WORKSPACE before anything
-// runs.
+// heads at head_dim 256 and 9.9 MB for 8 KV heads at head_dim 128 on a 148-SM B200. On a
+// 148-SM B200 the bound exceeds the array once kv_heads * head_dim reaches 2048 (8 KV heads
+// of 256, 16 of 128: about 19.5-19.7 MB); such a geometry, or any whose query exceeds the
+// array, is refused with QK_ERR_WORKSPACE before anything runs.
 //
 // Set-up: the first call on each device (the device current on the calling thread) looks
 // up the array's device address with cudaGetSymbolAddress and caches it. That first call
-// should therefore come before any stream capture. Nothing in the scratch has to start at
-// zero: the split kernel writes every partial row before the merge kernel reads it.
+// should therefore come before any stream capture. The cached address belongs to the
+// device's primary context: after cudaDeviceReset (or any teardown of that context) the
+// library must be reloaded before this entry point is called again. Nothing in the scratch
+// has to start at zero: the split kernel writes every partial row before the merge kernel
+// reads it.
 //
 // The scratch is one array per device. Two calls that can overlap on the same device (on
 // different streams, or from different host threads) race on it. Calls issued in order on

@@ -98,10 +98,34 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
   return r;
 }
 
+// numerics.py:13-14 accurate FP32 exp (AccuracyMode.HIGHEST): CUDA's expf, whose documented
+// maximum error is 2 ulp, inside the reference's 5e-7 relative budget
+// (numerics_validation.py:40). Every exponential of the kernels goes through it; qk_numerics
+// evaluates it for the FP64 check.
+__device__ __forceinline__ float exp_ref(float x) { return expf(x); }
+
 // numerics.py:42-45 sigmoid: divide(x >= 0 ? 1 : e, 1 + e), e = exp(-|x|), IEEE divide.
 __device__ __forceinline__ float sigmoid_ref(float x) {
-  float e = expf(-fabsf(x));
+  float e = exp_ref(-fabsf(x));
   return __fdiv_rn(x >= 0.f ? 1.f : e, __fadd_rn(1.f, e));
+}
+
+// numerics.py:48-51 softmax of one row of n values, in place, by one warp: the maximum,
+// exp(x - max), a lane-strided FP32 sum folded by an XOR butterfly, then an IEEE divide.
+// The router uses it for its probabilities; qk_numerics exposes it for the FP64 check.
+__device__ __forceinline__ void softmax_row_warp(float* row, int n, int lane) {
+  float mx = -INFINITY;
+  for (int e = lane; e < n; e += 32) mx = fmaxf(mx, row[e]);
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  float sum = 0.f;
+  for (int e = lane; e < n; e += 32) {
+    const float ex = exp_ref(row[e] - mx);
+    row[e] = ex;
+    sum = __fadd_rn(sum, ex);
+  }
+  for (int o = 16; o > 0; o >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, o));
+  for (int e = lane; e < n; e += 32) row[e] = __fdiv_rn(row[e], sum);
+  __syncwarp();
 }
 
 // ---------------------------------------------------------------------------------

@@ -9,7 +9,7 @@
 // warp per expert row, fixed-order reductions; each router row is read once per cluster),
 // storing them into the first CTA's shared memory (distributed shared memory). After the
 // cluster barrier the first CTA's warp t runs softmax and the k selection rounds for token
-// t. Divisions are IEEE; exp is expf.
+// t. Divisions are IEEE; exp is exp_ref (expf).
 #include <cooperative_groups.h>
 
 #include "common.cuh"
@@ -110,21 +110,9 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kWarps * 32)
   float* row = lg + warp * E;
 
   // softmax (numerics.py:48-51)
-  float mx = -INFINITY;
-  for (int e = lane; e < E; e += 32) mx = fmaxf(mx, row[e]);
-  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  float sum = 0.f;
-  for (int e = lane; e < E; e += 32) {
-    const float ex = expf(row[e] - mx);
-    row[e] = ex;
-    sum = __fadd_rn(sum, ex);
-  }
-  for (int o = 16; o > 0; o >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, o));
-  for (int e = lane; e < E; e += 32) {
-    row[e] = __fdiv_rn(row[e], sum);
-    if (probs_out) probs_out[static_cast<int64_t>(t) * E + e] = row[e];
-  }
-  __syncwarp();
+  softmax_row_warp(row, E, lane);
+  if (probs_out)
+    for (int e = lane; e < E; e += 32) probs_out[static_cast<int64_t>(t) * E + e] = row[e];
 
   // top-k: k rounds of warp argmax; ties go to the lower expert index (lax.top_k).
   float mine = 0.f;  // lane j keeps the j-th selected probability

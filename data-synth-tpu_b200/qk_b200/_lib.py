@@ -25,6 +25,8 @@ QK_OUT_F32 = 0
 QK_OUT_BF16 = 1
 QK_DECODE_FUSED = 0x100
 
+QK_NUM_EXP, QK_NUM_SIGMOID, QK_NUM_DIVIDE, QK_NUM_SOFTMAX, QK_NUM_SILU_BF16 = range(5)
+
 _p = ctypes.c_void_p
 _i = ctypes.c_int
 _i64 = ctypes.c_int64
@@ -109,6 +111,7 @@ SIGNATURES = {
     "qk_gather_rows": (_i, [_p, _p, _i64, _i64, _p, _p]),
     "qk_ep_combine": (_i, [_p, _p, _p, _p, _i, _i, _i, _i, _p, _p]),
     "qk_kv_q8_attention_check": (_i, [_p]),
+    "qk_numerics": (_i, [_i, _p, _p, _p, _i64, _i, _p]),
     "qk_kv_q8_decode_attention_noalloc": (
         _i,
         [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _i, _p, _p],

@@ -16,22 +16,16 @@ from .quant import BLOCK_LAYOUTS, GGML_TYPE, normalize_qtype
 
 
 def split_expert_bytes(raw, kind, qtype, hidden, intermediate, tensor_parallel):
-    if kind not in {"gate", "up", "down"}:
-        raise ValueError("Unknown expert projection")
-    block, size = BLOCK_LAYOUTS[normalize_qtype(qtype)]
-    if intermediate % tensor_parallel:
-        raise ValueError("Intermediate channels must divide tensor parallel size")
-    local = intermediate // tensor_parallel
-    count = len(raw)
-    if kind == "down":
-        if local % block:
-            raise ValueError("Tensor slices must contain whole down quantization blocks")
-        rows = np.asarray(raw).reshape(count, hidden, tensor_parallel, local // block, size)
-        return rows.transpose(2, 0, 1, 3, 4).reshape(tensor_parallel, count, -1).copy()
-    if hidden % block:
-        raise ValueError("Hidden channels must contain whole quantization blocks")
-    rows = np.asarray(raw).reshape(count, tensor_parallel, local, hidden // block, size)
-    return rows.transpose(1, 0, 2, 3, 4).reshape(tensor_parallel, count, -1).copy()
+    """Every tensor rank's slice of every expert, ``uint8[tensor_parallel, E, bytes / tp]``.
+
+    The byte contract of ``qwen38_tpu/parallel.py:40-61`` (pinned by a golden of that
+    function): entry ``[t]`` is ``tensor_slice(raw, ..., t)``, so gate/up keep whole rows
+    and down keeps whole quantisation blocks. The argument checks (and their messages)
+    are ``tensor_slice``'s."""
+    raw = np.asarray(raw)
+    slices = [tensor_slice(raw, kind, qtype, hidden, intermediate, tensor_parallel, t)
+              for t in range(tensor_parallel)]
+    return np.stack(slices).astype(np.uint8, copy=False)
 
 
 def expert_shape(kind, hidden, intermediate):

@@ -326,11 +326,22 @@ int qk_checked_argmax(const void* logits, int in_dtype, int B, int64_t V, int32_
  * QK_OK; clears the flag. Synchronises `stream`. */
 int qk_kv_q8_attention_check(qk_stream_t stream);
 
+/* Replaces the FP32 elementary functions of qwen38_tpu/numerics.py:13-51 (exp, divide,
+ * sigmoid, softmax) as the kernels compute them, for the reference's FP64 validation
+ * (numerics_validation.py:12-74, 5e-7 relative budget). Elementwise over n FP32 values:
+ * out = exp(a), sigmoid(a), a / b (b read only by QK_NUM_DIVIDE), or the SwiGLU
+ * activation bf16(bf16(a) * sigmoid(bf16(a))); QK_NUM_SOFTMAX normalises rows of row_len
+ * values (n a multiple of row_len) exactly as the router kernel does. */
+enum { QK_NUM_EXP = 0, QK_NUM_SIGMOID = 1, QK_NUM_DIVIDE = 2, QK_NUM_SOFTMAX = 3, QK_NUM_SILU_BF16 = 4 };
+int qk_numerics(int op, const float* a, const float* b, float* out, int64_t n, int row_len,
+                qk_stream_t stream);
+
 /* No counterpart in the reference. qk_kv_q8_decode_attention without a workspace, for
  * callers that cannot provide device memory at the call. The split scratch is a fixed
  * 16 MiB array in the library's device image (QK_ATTN_STATIC_SCRATCH_BYTES). A geometry
  * whose qk_kv_q8_attention_workspace_bytes() exceeds it returns QK_ERR_WORKSPACE and
- * runs nothing. The first call on a device looks up the array's address, so make it
+ * runs nothing: the need is 2 * SMs * kv_heads * (16 + 8 * head_dim) * 4 bytes, so on a
+ * 148-SM B200 kv_heads * head_dim >= 2048 is refused. The first call on a device looks up the array's address, so make it
  * before any stream capture. The scratch is shared per device, so overlapping calls
  * (other streams or threads) race on it; calls in order on one stream are safe. */
 #define QK_ATTN_STATIC_SCRATCH_BYTES (16u << 20)

@@ -24,6 +24,7 @@ The fixtures are committed; tests never read the reference at run time. Sources:
 
 import ast
 import hashlib
+import os
 import sys
 from pathlib import Path
 
@@ -298,7 +299,9 @@ def split_golden(quant, funcs):
 
 
 def main():
-    root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("QK_REFERENCE_ROOT")
+    if not root:
+        sys.exit("usage: make_golden.py REFERENCE_CHECKOUT (or set QK_REFERENCE_ROOT)")
     gguf_quant, quant, q6ref, funcs = load_reference(root)
     decode_golden(gguf_quant, quant)
     q6_golden(q6ref)

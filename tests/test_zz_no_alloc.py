@@ -93,19 +93,24 @@ def test_workspace_is_bounded_by_the_sm_count_whatever_the_batch(cuda_device):
 
 
 def test_noalloc_refuses_a_workspace_above_the_fixed_scratch_unrun(cuda_device):
-    """The refusal path, driven through a geometry the kernel accepts but whose scratch
-    would not fit: checked against the query, so it only runs where the query exceeds it."""
+    """The refusal path, driven through a geometry the kernel accepts but whose scratch does
+    not fit: 16 KV heads of 128 need 2 * SMs * 16 * (16 + 8 * 128) * 4 bytes, 19.7 MB on a
+    148-SM B200, above the 16 MiB array. The call must fail before any launch, so the
+    operand pointers are never dereferenced."""
+    import torch
+
     from qk_b200 import _lib
 
     lib = _lib.load()
-    batch, S, T = 150, 512, 512
-    need = int(lib.qk_kv_q8_attention_workspace_bytes(batch, S, HQ, KV, HD))
-    if need <= STATIC_SCRATCH_BYTES:
-        pytest.skip(f"this device needs {need} bytes for {batch}x{S}, within the fixed scratch")
+    hq, kv, hd = 16, 16, 128
+    batch, S, T = 150, 4096, 4096
+    sms = torch.cuda.get_device_properties(cuda_device).multi_processor_count
+    need = int(lib.qk_kv_q8_attention_workspace_bytes(batch, S, hq, kv, hd))
+    assert need > STATIC_SCRATCH_BYTES, (sms, need)
     launches = _lib.launch_count()
     dummy = ctypes.c_void_p(256)
-    rc = lib.qk_kv_q8_decode_attention_noalloc(*([dummy] * 6), None, dummy, None, batch, S, T, HQ,
-                                               KV, HD, dummy, _lib.stream_handle(cuda_device))
+    rc = lib.qk_kv_q8_decode_attention_noalloc(*([dummy] * 6), None, dummy, None, batch, S, T, hq,
+                                               kv, hd, dummy, _lib.stream_handle(cuda_device))
     assert rc == _lib.QK_ERR_WORKSPACE
     assert "fixed" in _lib.last_error() and str(need) in _lib.last_error()
     assert _lib.launch_count() == launches
