@@ -91,15 +91,34 @@ def synth_experts(qtype, count, seed=1):
         return {k: f[k] for k in ("gate", "up", "down")}
 
 
-def workload(m, rank=0):
-    """Activation rows, expert assignment and route weights for M rows per expert."""
+def workload_ids(m, rank=0, world=1):
+    """Expert of each of rank `rank`'s 128 * M rows: uniform over the 128 * world experts of
+    all ranks (seed [10, rank]); with one rank, uniform over its 128."""
+    import numpy as np
+
+    return np.random.default_rng([10, rank]).integers(0, EXPERTS * world, (EXPERTS * m, 1)).astype(np.int32)
+
+
+def workload(m, rank=0, world=1):
+    """Activation rows (N(0, 1), seed [0, rank]), expert assignment and route weights (1) of
+    rank `rank`'s 128 * M rows."""
     import numpy as np
 
     rows = EXPERTS * m
     x = np.random.default_rng([0, rank]).normal(size=(rows, HIDDEN)).astype(np.float32)
-    ids = np.random.default_rng([10, rank]).integers(0, EXPERTS, (rows, 1)).astype(np.int32)
     weights = np.ones((rows, 1), np.float32)
-    return x, ids, weights
+    return x, workload_ids(m, rank, world), weights
+
+
+def ep_step_bytes(qtype, m, world):
+    """Algorithmic bytes of one expert-parallel step summed over ranks: every rank's routed
+    experts (those any rank's rows name) x packed bytes, plus every rank's x rows read and
+    output rows written."""
+    import numpy as np
+
+    every = np.concatenate([workload_ids(m, r, world)[:, 0] for r in range(world)])
+    active = len(np.unique(every))
+    return active * packed_bytes_per_expert(qtype) + world * EXPERTS * m * HIDDEN * 2 * 2, active
 
 
 def packed_bytes_per_expert(qtype):
@@ -319,7 +338,9 @@ def config_dict(args, world):
         "workload": f"expert_gemm_{args.qtype.lower()}_m{args.m}",
         "experts_per_gpu": EXPERTS, "hidden": HIDDEN, "intermediate": INTER, "qtype": args.qtype,
         "tokens_per_expert": args.m, "rows_per_gpu": EXPERTS * args.m, "top_k": 1,
-        "parallelism": f"ep{world} (independent expert shards)",
+        "parallelism": (f"ep{world}: each rank's rows routed uniformly over all {EXPERTS * world} experts of "
+                        "the ranks, dispatched and combined through peer memory (ExpertAllToAll)")
+        if world > 1 else "ep1",
         "l2": "inputs larger than L2 (331 MB packed weights per GPU)",
     }
 
@@ -419,6 +440,46 @@ def b200_arm(args):
                     gate_up_bytes=kernel_bytes(qtype, ids), x=x, ids=ids, weights=weights,
                     out=out)
 
+    def run_ep(m, steps, warmup):
+        """The expert-parallel step over all ranks (ExpertAllToAll, peer memory): this rank's
+        rows routed uniformly over every rank's experts, dispatched, computed by their
+        owners and combined back."""
+        from qk_b200.ep import ExpertAllToAll
+
+        x, ids, weights = workload(m, rank, world)
+        xd = torch.from_numpy(x).to(device).to(torch.bfloat16)
+        idd = torch.from_numpy(ids).to(device)
+        wd = torch.from_numpy(weights).to(device).to(torch.bfloat16)
+        rows = x.shape[0]
+        layer = ExpertAllToAll(dist.group.WORLD, gate_type=args.qtype, up_type=args.qtype,
+                               down_type=args.qtype, hidden=HIDDEN, intermediate=INTER,
+                               experts_per_rank=EXPERTS, top_k=1, max_tokens=rows, device=device)
+
+        def step():
+            return layer(tensors["gate"], tensors["up"], tensors["down"], xd, idd, wd)
+
+        for _ in range(warmup):
+            step()
+        torch.cuda.synchronize(device)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            step()
+        graph.replay()
+        torch.cuda.synchronize(device)
+        dist.barrier()
+        torch.cuda.synchronize(device)
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for _ in range(steps):
+            graph.replay()
+        t1.record(stream)
+        torch.cuda.synchronize(device)
+        dist.barrier()
+        ms = t0.elapsed_time(t1) / steps
+        layer.check_status()
+        return dict(m=m, ms=ms, rows=rows, x=x, ids=ids, weights=weights, out=layer.out[:rows], layer=layer,
+                    graph=graph)
+
     peak, peak_kind = hbm_peak()
     with ClockSampler(local) as clocks:
         # untimed soak so clocks settle before the measured region; no collectives inside,
@@ -427,18 +488,31 @@ def b200_arm(args):
         while time.time() < soak_end:
             run_m(args.m, 20, 1, False, sync=False)
         res = run_m(args.m, args.steps, args.warmup, True)
-    ms = res["ms"]
+        ep = run_ep(args.m, args.steps, args.warmup) if world > 1 else None
+    ms = res["ms"] if ep is None else ep["ms"]
     if dist:
         t = torch.tensor([ms], device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
-    value = res["bytes"] * world / (ms * 1e-3) / 1e9
+    if ep is None:
+        step_total = res["bytes"]
+    else:
+        step_total, _ = ep_step_bytes(args.qtype, args.m, world)
+    value = step_total / (ms * 1e-3) / 1e9
 
-    # launches: a graph replay runs the 5 kernels of one qk_moe_forward
-    launches_per_step = 5
+    # launches per step: the 5 kernels of one qk_moe_forward; the expert-parallel step adds
+    # the dispatch, the wait for the sources and the final combine (the expert pass's
+    # combine stores to the sources)
+    launches_per_step = 5 if ep is None else 7
 
     # e2e through the public call with host buffers
-    e2e = e2e_measure(fn, tensors, device, args, res, rank)
+    if ep is None:
+        def call(xs, ids_s, ws_s, out_s):
+            return fn(tensors["gate"], tensors["up"], tensors["down"], xs, ids_s, ws_s)
+    else:
+        def call(xs, ids_s, ws_s, out_s):
+            return ep["layer"](tensors["gate"], tensors["up"], tensors["down"], xs, ids_s, ws_s, out=out_s)
+    e2e = e2e_measure(call, device, args, res if ep is None else ep, step_total // world if ep else res["bytes"])
 
     sweep = []
     if not args.no_sweep and rank == 0 and world == 1:
@@ -457,8 +531,16 @@ def b200_arm(args):
         tensors, fn = saved
         del tensors_o, raw_o
 
-    # parity of the timed step: a seeded sample of output rows against the oracle
-    parity = moe_parity(raw, args.qtype, res) if rank == 0 else None
+    # parity of the timed step: a seeded sample of output rows against the oracle (with
+    # several ranks, of the expert-parallel step: every rank holds the same 128 experts'
+    # bytes, so global expert g computes with the bytes of expert g % 128)
+    parity = None
+    if rank == 0:
+        if ep is None:
+            parity = moe_parity(raw, args.qtype, res)
+        else:
+            parity = moe_parity(raw, args.qtype, dict(ep, ids=ep["ids"] % EXPERTS))
+    layer_ep = ep_layer_report(device, dist, world, rank, args) if not args.no_ep_layer else None
 
     gate_up_ms = res["stage_ms"][1]
     achieved = res["gate_up_bytes"] / (gate_up_ms * 1e-3) / 1e9
@@ -478,6 +560,18 @@ def b200_arm(args):
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clocks.summary(),
     }
+    if ep is not None:
+        t = torch.tensor([res["ms"]], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        local_ms = float(t.item())
+        line["expert_parallel"] = {
+            "step_ms": ms, "local_only_ms": local_ms, "exchange_overhead_ms": ms - local_ms,
+            "exchange_share": (ms - local_ms) / ms,
+            "exchange": "peer-memory stores over NVLink (dispatch of x rows, return of FP32 partials)",
+            "bytes_over_nvlink_per_rank": int(ep["rows"] * (world - 1) / world * HIDDEN * (2 + 4)),
+            "local_only": "the same rows and kernels on this rank's own 128 experts, no exchange"}
+    if layer_ep is not None:
+        line["ep_layer"] = layer_ep
     if sweep:
         line["sweep"] = sweep
     if parity is not None:
@@ -511,6 +605,97 @@ def b200_arm(args):
 
 ATTN_CONFIGS = ((1, 4096), (8, 4096), (32, 4096), (1, 32768), (8, 32768), (32, 32768))
 ATTN_SLOT_BYTES = 2 * 512 + 2 * 16 * 2  # K + V codes (2 kv heads x 256) + BF16 scales (16 groups)
+
+
+EP_LAYER_EXPERTS, EP_LAYER_TOPK, EP_LAYER_TOKENS = 512, 10, 512
+
+
+def ep_layer_report(device, dist, world, rank, args):
+    """The routed-expert layer of BASELINE.json configs[3] across the ranks: 512 Q6_K experts
+    (hidden 2048, intermediate 512), top-10 routes, a global batch of 512 decode tokens
+    (strong scaling: 512 / world tokens and 512 / world experts per rank). Tokens go to the
+    experts' owners and back through peer memory (ExpertAllToAll; with one rank the same
+    layer exchanges with itself). Experts are random code bytes with fixed block scales (the
+    kernels' cost does not depend on the values); routes are 10 distinct experts per token
+    (seed [4, rank]) with softmax-like BF16 weights. One step is one CUDA-graph replay.
+    Bytes = the distinct experts all ranks' routes name x packed bytes + every rank's x rows
+    read and output rows written."""
+    import numpy as np
+    import torch
+
+    from qk_b200.decoder import synthetic_expert_bytes
+    from qk_b200.ep import ExpertAllToAll
+    from qk_b200.parallel import expert_shape, put_expert_bytes
+
+    E, k, T = EP_LAYER_EXPERTS, EP_LAYER_TOPK, EP_LAYER_TOKENS
+    if E % world or T % world:
+        return None
+    per, tokens = E // world, T // world
+    g = torch.Generator(device=device).manual_seed(100 + rank)
+    tensors = {}
+    for kind in ("gate", "up", "down"):
+        rows, width = expert_shape(kind, HIDDEN, INTER)
+        raw = synthetic_expert_bytes(args.qtype, per, rows, width, g, device)
+        tensors[kind] = put_expert_bytes(raw, kind, args.qtype, HIDDEN, INTER, device=device)
+        del raw
+
+    def routes(r):
+        rng = np.random.default_rng([4, r])
+        ids = np.argsort(rng.random((tokens, E)), axis=1)[:, :k].astype(np.int32)
+        w = rng.random((tokens, k)).astype(np.float32)
+        return ids, w / w.sum(axis=1, keepdims=True)
+
+    ids, w = routes(rank)
+    x = torch.randn((tokens, HIDDEN), device=device, generator=g).to(torch.bfloat16)
+    idd = torch.from_numpy(ids).to(device)
+    wd = torch.from_numpy(w).to(device).to(torch.bfloat16)
+    layer = ExpertAllToAll(dist.group.WORLD if dist else None, gate_type=args.qtype, up_type=args.qtype,
+                           down_type=args.qtype, hidden=HIDDEN, intermediate=INTER, experts_per_rank=per, top_k=k,
+                           max_tokens=tokens, device=device)
+    stream = torch.cuda.current_stream(device)
+
+    def step():
+        layer(tensors["gate"], tensors["up"], tensors["down"], x, idd, wd)
+
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize(device)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    graph.replay()
+    torch.cuda.synchronize(device)
+    if dist:
+        dist.barrier()
+    steps = max(10, args.steps // 2)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(steps):
+        graph.replay()
+    t1.record(stream)
+    torch.cuda.synchronize(device)
+    ms = t0.elapsed_time(t1) / steps
+    if dist:
+        dist.barrier()
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    layer.check_status()
+    del graph
+    torch.cuda.synchronize(device)
+    if dist:
+        dist.barrier()
+    layer.close()
+    every = np.concatenate([routes(r)[0].reshape(-1) for r in range(world)])
+    active = len(np.unique(every))
+    nbytes = active * packed_bytes_per_expert(args.qtype) + T * HIDDEN * 2 * 2
+    peak, _ = hbm_peak()
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    return {"workload": "configs[3] routed-expert layer: 512 Q6_K experts, top-10, global batch 512, "
+                        "strong scaling over the ranks", "experts_per_rank": per, "tokens_per_rank": tokens,
+            "qtype": args.qtype, "ms_per_step": ms, "tokens_per_s": T / (ms * 1e-3), "gbs": gbs,
+            "frac_of_aggregate_hbm": gbs / (peak * world), "active_experts": active,
+            "exchange": "peer memory (ExpertAllToAll)" if world > 1 else "one rank (the exchange writes to itself)"}
 
 
 def attention_inputs(device, batch, ctx):
@@ -789,7 +974,7 @@ def attention_only(args):
     return 0
 
 
-def e2e_measure(fn, tensors, device, args, res, rank):
+def e2e_measure(call, device, args, res, step_bytes_rank):
     """Public-call throughput with pinned host inputs/outputs copied every step.
 
     Each step copies its x, ids and weights host -> device, runs the public ``fn`` and
@@ -805,6 +990,7 @@ def e2e_measure(fn, tensors, device, args, res, rank):
     w_h = torch.from_numpy(weights).to(torch.bfloat16).pin_memory()
     slots = 2
     out_h = [torch.empty((rows, HIDDEN), dtype=torch.bfloat16).pin_memory() for _ in range(slots)]
+    out_d = [torch.empty((rows, HIDDEN), dtype=torch.bfloat16, device=device) for _ in range(slots)]
     x_d = [torch.empty_like(x_h, device=device) for _ in range(slots)]
     ids_d = [torch.empty_like(ids_h, device=device) for _ in range(slots)]
     w_d = [torch.empty_like(w_h, device=device) for _ in range(slots)]
@@ -824,7 +1010,7 @@ def e2e_measure(fn, tensors, device, args, res, rank):
             copied[s].record(h2d)
         with torch.cuda.stream(comp):
             comp.wait_event(copied[s])
-            out = fn(tensors["gate"], tensors["up"], tensors["down"], x_d[s], ids_d[s], w_d[s])
+            out = call(x_d[s], ids_d[s], w_d[s], out_d[s])
             computed[s].record(comp)
         with torch.cuda.stream(d2h):
             d2h.wait_event(computed[s])
@@ -848,7 +1034,13 @@ def e2e_measure(fn, tensors, device, args, res, rank):
     h2d_bytes = x_h.numel() * 2 + ids_h.numel() * 4 + w_h.numel() * 2
     d2h_bytes = out_h[0].numel() * 2
     world = int(os.environ.get("WORLD_SIZE", "1"))
-    return {"value": res["bytes"] * world / (ms * 1e-3) / 1e9, "unit": "GB/s",
+    if world > 1:
+        import torch.distributed as dist
+
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return {"value": step_bytes_rank * world / (ms * 1e-3) / 1e9, "unit": "GB/s",
             "ms_per_step": ms, "h2d_bytes_per_step": h2d_bytes, "d2h_bytes_per_step": d2h_bytes,
             "pipeline": "H2D, compute and D2H on separate streams, 2 buffer slots"}
 
@@ -877,6 +1069,7 @@ def main():
                         help="attention configs as BxCTX[,BxCTX...] (default: the six of the sweep)")
     parser.add_argument("--attn-reps", type=int, default=20)
     parser.add_argument("--no-stack", action="store_true", help="skip the 48-layer decoder stack")
+    parser.add_argument("--no-ep-layer", action="store_true", help="skip the configs[3] expert-parallel layer")
     parser.add_argument("--qsa-only", action="store_true", help="only the sparse token selection (one GPU)")
     parser.add_argument("--stack-only", action="store_true", help="only the decoder stack (one GPU)")
     parser.add_argument("--stack-batches", type=lambda t: [int(v) for v in t.split(",")], default=[1, 8, 64])

@@ -19,6 +19,8 @@
 //                expert order (the reference's accumulation order, experts.py:129), then
 //                BF16 (experts.py:131), or the FP32 partial sum for an EP all-reduce.
 #include "common.cuh"
+#include "ep_p2p.cuh"
+#include "umma_prefill.cuh"
 #include "umma_proj.cuh"
 
 namespace qk {
@@ -400,7 +402,82 @@ __global__ void cast_kernel(const float* __restrict__ in, uint16_t* __restrict__
     out[i] = bf16_bits_rne(in[i]);
 }
 
+// Expert-parallel form of the combine (qk_ep_p2p_expert): the rows are the received slots
+// [source s][token b] of this rank's exchange region. Each slot that its source sent (some
+// route names one of this rank's experts) gets the FP32 sum of f32(y) * f32(route) over its
+// entries in ascending expert order, stored straight into the source's region at
+// ret[this rank][b] (over NVLink for another rank). Unsent slots are not written. The last
+// CTA raises ret_flag[this rank] in every source's region.
+__global__ void __launch_bounds__(256) moe_combine_push_kernel(const int32_t* __restrict__ ids, int Bp, int k, int H,
+                                                               Workspace ws, uint8_t* const* __restrict__ peers,
+                                                               uint8_t* own, EpLayout L, int rank) {
+  pdl_wait();
+  EpCtrl* ctrl = reinterpret_cast<EpCtrl*>(own);
+  const uint32_t epoch = ctrl->epoch;
+  const int lane = threadIdx.x & 31;
+  const int blocks = H / 256;
+  const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (gw < Bp * blocks) {
+    const int b = gw / blocks, c0 = (gw - b * blocks) * 256 + lane * 8;
+    const int id = lane < k ? ids[b * k + lane] : -1;
+    if (__any_sync(0xffffffffu, id >= 0)) {
+      const int entry = lane < k ? ws.route_entry[b * k + lane] : -1;
+      const int eid = entry >= 0 ? id : 0x7fffffff;
+      const float w = entry >= 0 ? ws.entry_weight[entry] : 0.f;
+      int rank_in = 0, n = 0;
+      for (int j = 0; j < k; ++j) {
+        const int ej = __shfl_sync(0xffffffffu, eid, j);
+        const int vj = __shfl_sync(0xffffffffu, entry, j) >= 0;
+        n += vj;
+        rank_in += vj && (ej < eid);
+      }
+      float acc[8];
+#pragma unroll
+      for (int t = 0; t < 8; ++t) acc[t] = 0.f;
+      for (int i = 0; i < n; ++i) {
+        const unsigned who = __ballot_sync(0xffffffffu, entry >= 0 && rank_in == i);
+        const int src = __ffs(who) - 1;
+        const int ent = __shfl_sync(0xffffffffu, entry, src);
+        const float wi = __shfl_sync(0xffffffffu, w, src);
+        const uint4 v = ld_nc_v4(ws.y + static_cast<int64_t>(ent) * H + c0);
+        const uint32_t p[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+          const float y = bf16_to_f32(static_cast<uint16_t>(p[t >> 1] >> (16 * (t & 1))));
+          acc[t] = __fadd_rn(acc[t], __fmul_rn(y, wi));
+        }
+      }
+      const int src_rank = b / L.max_tokens, tok = b - src_rank * L.max_tokens;
+      float* dst = reinterpret_cast<float*>(peers[src_rank] + L.ret) +
+                   (static_cast<size_t>(rank) * L.max_tokens + tok) * H + c0;
+      reinterpret_cast<float4*>(dst)[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+      reinterpret_cast<float4*>(dst)[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+    }
+  }
+  if (ep_last_cta(&ctrl->combine_arrivals)) {
+    for (int t = threadIdx.x; t < L.world; t += blockDim.x)
+      ep_store_release(&reinterpret_cast<EpCtrl*>(peers[t])->ret_flag[rank], epoch);
+  }
+}
+
+// Waits until every source has raised its recv_flag for this rank's current epoch.
+__global__ void ep_wait_sources_kernel(uint8_t* own, int world) {
+  EpCtrl* ctrl = reinterpret_cast<EpCtrl*>(own);
+  const uint32_t epoch = ctrl->epoch;
+  for (int t = threadIdx.x; t < world; t += blockDim.x)
+    if (!ep_wait_flag(&ctrl->recv_flag[t], epoch)) atomicExch(&ctrl->status, QK_ERR_TIMEOUT);
+  __syncthreads();
+  pdl_trigger();
+}
+
 bool supported(int t) { return t == QK_TYPE_Q6_K || t == QK_TYPE_Q4_K; }
+
+// The narrow MoE passes copy two K blocks per bulk copy (umma_pair_kernel); building with
+// -DQK_PAIR_COPIES=0 restores one copy per K block (umma_proj_kernel).
+#ifndef QK_PAIR_COPIES
+#define QK_PAIR_COPIES 1
+#endif
+constexpr bool kPairCopies = QK_PAIR_COPIES != 0;
 // The down projection also takes Q8_0 (the real checkpoints' down type, checkpoints/q6.json).
 bool supported_down(int t) { return supported(t) || t == QK_TYPE_Q8_0; }
 
@@ -419,13 +496,22 @@ size_t qk_moe_workspace_bytes(const qk_moe_desc* desc, int max_tokens) {
 // phase kFull: all five launches; kPartial: route .. down with the FP32 down projection of
 // every route written to `yr` [B * top_k, hidden] (no combine); kCombine: only the combine,
 // from `yr` and the routing metadata a kPartial call left in the same workspace.
-enum { kFull = 0, kPartial = 1, kCombine = 2 };
+enum { kFull = 0, kPartial = 1, kCombine = 2, kPush = 3 };
+
+// The exchange region of the expert-parallel form (phase kPush).
+struct PushArgs {
+  uint8_t* const* peers;
+  uint8_t* own;
+  EpLayout L;
+  int rank;
+};
 
 static int moe_forward_impl(const qk_moe_desc* desc, const uint8_t* gate, const uint8_t* up,
                             const uint8_t* down, const uint16_t* x, const int32_t* ids,
                             const uint16_t* weights, int B, int out_dtype, void* out,
                             void* workspace, size_t workspace_bytes, qk_stream_t stream,
-                            void* const* events, float* yr = nullptr, int phase = kFull) {
+                            void* const* events, float* yr = nullptr, int phase = kFull,
+                            const PushArgs* push = nullptr) {
   QK_REQUIRE(desc, "null descriptor");
   const qk_moe_desc& d = *desc;
   if (!supported(d.gate_type) || d.gate_type != d.up_type || !supported_down(d.down_type))
@@ -445,7 +531,8 @@ static int moe_forward_impl(const qk_moe_desc* desc, const uint8_t* gate, const 
   if (phase == kCombine)
     QK_REQUIRE(ids && yr && out, "null pointer");
   else
-    QK_REQUIRE(gate && up && down && x && ids && weights && (phase == kPartial ? yr != nullptr : out != nullptr),
+    QK_REQUIRE(gate && up && down && x && ids && weights &&
+                   (phase == kPartial ? yr != nullptr : phase == kPush ? push != nullptr : out != nullptr),
                "null pointer");
   if (yr) QK_REQUIRE((reinterpret_cast<uintptr_t>(yr) & 15) == 0, "y_routes must be 16-byte aligned");
   const size_t need = layout(d, B, nullptr, nullptr);
@@ -474,15 +561,26 @@ static int moe_forward_impl(const qk_moe_desc* desc, const uint8_t* gate, const 
     const cudaError_t e = cudaMemsetAsync(ws.ht, 0, bytes, st);
     if (e != cudaSuccess) return cuda_error(e, "clearing the padded activation tiles");
   }
-  const size_t routes = static_cast<size_t>(B) * d.top_k;
+  // The expert-parallel form receives [world x max_tokens] slots of which about max_tokens
+  // carry routes for this rank when the experts are evenly loaded: the form follows that.
+  const size_t routes = static_cast<size_t>(phase == kPush ? push->L.max_tokens : B) * d.top_k;
   // The wide form (128-token chunks) when the routes average at least 64 tokens per expert
   // the rank holds (prefill-sized batches); the narrow form (32-token chunks) otherwise.
 #ifndef QK_WIDE_MIN_TOKENS
 #define QK_WIDE_MIN_TOKENS 64
 #endif
-  const bool wide = routes >= QK_WIDE_MIN_TOKENS * static_cast<size_t>(d.num_experts);
-  const int ctok = wide ? kWideTok : kMaxTok;
-  const size_t route_smem = (3 * static_cast<size_t>(d.num_experts) + 1) * 4 + (routes <= kStagedRoutes ? routes * 6 : 0);
+  // The prefill form (256-token chunks, each weight decoded once per 256 tokens into shared
+  // memory, all of TMEM as accumulators) from QK_PREFILL_MIN_TOKENS routes per expert.
+#ifndef QK_PREFILL_MIN_TOKENS
+#define QK_PREFILL_MIN_TOKENS 192
+#endif
+  const bool prefill = routes >= QK_PREFILL_MIN_TOKENS * static_cast<size_t>(d.num_experts);
+  const bool wide = !prefill && routes >= QK_WIDE_MIN_TOKENS * static_cast<size_t>(d.num_experts);
+  const int ctok = prefill ? kPTok : wide ? kWideTok : kMaxTok;
+  // the route kernel stages all B * top_k routes in shared memory when they fit
+  const size_t all_routes = static_cast<size_t>(B) * d.top_k;
+  const size_t route_smem =
+      (3 * static_cast<size_t>(d.num_experts) + 1) * 4 + (all_routes <= kStagedRoutes ? all_routes * 6 : 0);
   int rc = allow_smem(reinterpret_cast<const void*>(moe_route_kernel), route_smem);
   if (rc) return rc;
   {
@@ -538,22 +636,47 @@ static int moe_forward_impl(const qk_moe_desc* desc, const uint8_t* gate, const 
   dn.entry_route = ws.entry_route;
   dn.nrows = d.hidden;
   mark(1);
-  if (wide)
+  if (prefill) {
+    gu.items_per_chunk = (gu.tiles64 + 1) / 2;  // 128 rows of I (gate and up) per item
+    dn.items_per_chunk = (dn.tiles64 + 3) / 4;  // 256 rows of H per item
+    rc = q6 ? launch_prefill<QType::Q6_K, kModeGateUp>(gu, sms, st) : launch_prefill<QType::Q4_K, kModeGateUp>(gu, sms, st);
+  } else if (wide) {
     rc = q6 ? launch_umma<QType::Q6_K, kModeGateUp, true>(gu, sms, st)
             : launch_umma<QType::Q4_K, kModeGateUp, true>(gu, sms, st);
-  else
+  } else if (kPairCopies) {
+    rc = q6 ? launch_pair<QType::Q6_K, kModeGateUp>(gu, sms, st) : launch_pair<QType::Q4_K, kModeGateUp>(gu, sms, st);
+  } else {
     rc = q6 ? launch_umma<QType::Q6_K, kModeGateUp>(gu, sms, st) : launch_umma<QType::Q4_K, kModeGateUp>(gu, sms, st);
+  }
   if (rc) return rc;
   mark(2);
-  if (d.down_type == QK_TYPE_Q8_0)
-    rc = wide ? launch_umma<QType::Q8_0, kModeDown, true>(dn, sms, st) : launch_umma<QType::Q8_0, kModeDown>(dn, sms, st);
-  else if (d.down_type == QK_TYPE_Q6_K)
-    rc = wide ? launch_umma<QType::Q6_K, kModeDown, true>(dn, sms, st) : launch_umma<QType::Q6_K, kModeDown>(dn, sms, st);
-  else
-    rc = wide ? launch_umma<QType::Q4_K, kModeDown, true>(dn, sms, st) : launch_umma<QType::Q4_K, kModeDown>(dn, sms, st);
+  if (prefill) {
+    if (d.down_type == QK_TYPE_Q8_0) rc = launch_prefill<QType::Q8_0, kModeDown>(dn, sms, st);
+    else if (d.down_type == QK_TYPE_Q6_K) rc = launch_prefill<QType::Q6_K, kModeDown>(dn, sms, st);
+    else rc = launch_prefill<QType::Q4_K, kModeDown>(dn, sms, st);
+  } else if (wide) {
+    if (d.down_type == QK_TYPE_Q8_0) rc = launch_umma<QType::Q8_0, kModeDown, true>(dn, sms, st);
+    else if (d.down_type == QK_TYPE_Q6_K) rc = launch_umma<QType::Q6_K, kModeDown, true>(dn, sms, st);
+    else rc = launch_umma<QType::Q4_K, kModeDown, true>(dn, sms, st);
+  } else if (kPairCopies) {
+    if (d.down_type == QK_TYPE_Q8_0) rc = launch_pair<QType::Q8_0, kModeDown>(dn, sms, st);
+    else if (d.down_type == QK_TYPE_Q6_K) rc = launch_pair<QType::Q6_K, kModeDown>(dn, sms, st);
+    else rc = launch_pair<QType::Q4_K, kModeDown>(dn, sms, st);
+  } else {
+    if (d.down_type == QK_TYPE_Q8_0) rc = launch_umma<QType::Q8_0, kModeDown>(dn, sms, st);
+    else if (d.down_type == QK_TYPE_Q6_K) rc = launch_umma<QType::Q6_K, kModeDown>(dn, sms, st);
+    else rc = launch_umma<QType::Q4_K, kModeDown>(dn, sms, st);
+  }
   if (rc) return rc;
   mark(3);
   if (phase == kPartial) return QK_OK;
+  if (phase == kPush) {
+    const cudaError_t e = launch_dependent(moe_combine_push_kernel, dim3((B * (d.hidden / 256) + 7) / 8), dim3(256), 0, st,
+                                           ids, B, d.top_k, d.hidden, ws, push->peers, push->own, push->L, push->rank);
+    if (e != cudaSuccess) return cuda_error(e, "moe_combine_push_kernel");
+    count_launch(1);
+    return QK_OK;
+  }
   {
     const cudaError_t e = launch_dependent(moe_combine_kernel, dim3((B * (d.hidden / 256) + 7) / 8), dim3(256), 0, st, ids, B, d.top_k,
                                            d.hidden, static_cast<int>(out_dtype == QK_OUT_BF16), out,
@@ -595,6 +718,25 @@ int qk_moe_forward_tp_combine(const qk_moe_desc* desc, const float* y_routes, co
                               qk_stream_t stream) {
   return moe_forward_impl(desc, nullptr, nullptr, nullptr, nullptr, ids, nullptr, B, out_dtype, out, workspace,
                           workspace_bytes, stream, nullptr, const_cast<float*>(y_routes), kCombine);
+}
+
+int qk_ep_p2p_expert(const qk_moe_desc* desc, const uint8_t* gate, const uint8_t* up, const uint8_t* down,
+                     void* const* peers, void* region, int world, int rank, int max_tokens, void* workspace,
+                     size_t workspace_bytes, qk_stream_t stream) {
+  QK_REQUIRE(desc && peers && region, "null pointer");
+  QK_REQUIRE(world >= 1 && world <= kEpMaxRanks && rank >= 0 && rank < world, "bad rank or world");
+  QK_REQUIRE(max_tokens >= 1, "max_tokens must be positive");
+  QK_REQUIRE(desc->first_expert == rank * desc->num_experts,
+             "first_expert must be rank * num_experts (contiguous expert ranges, parallel.py:64-87)");
+  const EpLayout L = ep_layout(world, max_tokens, desc->hidden, desc->top_k);
+  uint8_t* own = static_cast<uint8_t*>(region);
+  ep_wait_sources_kernel<<<1, 64, 0, as_stream(stream)>>>(own, world);
+  QK_LAUNCHED("ep_wait_sources_kernel");
+  PushArgs push{reinterpret_cast<uint8_t* const*>(peers), own, L, rank};
+  return moe_forward_impl(desc, gate, up, down, reinterpret_cast<const uint16_t*>(own + L.recv_x),
+                          reinterpret_cast<const int32_t*>(own + L.recv_ids),
+                          reinterpret_cast<const uint16_t*>(own + L.recv_w), world * max_tokens, QK_OUT_F32,
+                          nullptr, workspace, workspace_bytes, stream, nullptr, nullptr, kPush, &push);
 }
 
 int qk_cast_f32_bf16(const float* in, uint16_t* out, int64_t n, qk_stream_t stream) {

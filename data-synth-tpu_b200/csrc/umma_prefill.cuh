@@ -1,0 +1,481 @@
+// Packed-weight expert projection for many tokens per expert (prefill): tcgen05 MMAs with
+// both operands in shared memory and all 512 TMEM columns as accumulators.
+//
+// The decode-regime kernel (umma_proj.cuh) decodes each weight tile into TMEM once per token
+// chunk of <= 32 (or 128) tokens, so with hundreds of tokens per expert the decode, not the
+// tensor core, bounds it. Here a work item is (token chunk of <= 256 tokens of one expert,
+// weight pair p), and each weight value is decoded once per 256 tokens:
+//   gate/up: pair p = I rows [128p, 128p + 128): MMA tile 0 is gate tile 2p and up tile 2p
+//            with interleaved rows (A row r = row r >> 1 of gate (r even) or up (r odd)), MMA
+//            tile 1 the same for tiles 2p + 1, so SwiGLU partners sit in neighbouring TMEM
+//            lanes; the epilogue writes h = bf16(silu(bf16 g) * bf16 u) as the down pass's
+//            activation tiles.
+//   down:    pair p = H rows [256p, 256p + 256): MMA tile t is rows 256p + 128t .. + 127
+//            (weight tiles 4p + 2t, 4p + 2t + 1); the epilogue writes y = bf16(h Wd^T).
+// TMEM: MMA tile t accumulates into columns [256t, 256t + 256) (one column per token).
+//
+// The K loop runs over 64-value K atoms. Per atom, 8 decode warps (a group; the two groups
+// take alternate atoms) turn one quarter block of each of the item's 256 weight rows into the
+// BF16 A operand (2 x [128 rows x 128 B], 128-byte-swizzled K-major) in shared memory; the
+// producer streams the packed weights (one half K block of the 4 weight tiles per stage:
+// the half's code chunks, the scale chunk and, for Q6_K, the d plane) and the activation
+// atom ([tokens x 128 B], the layout the dispatch / gate-up epilogue wrote) with 1-D bulk
+// copies (no multicast); one thread issues 2 x 4 MMAs (M = 128, N = chunk tokens rounded to
+// 16, K = 16) per atom. Warps: 0-15 decode, 16 producer, 17 MMA, 18-25 epilogue (two per TMEM
+// lane quadrant, each taking half of the token columns). Every wait is bounded; on give-up
+// the CTA records QK_ERR_TIMEOUT in `status` and leaves its loops.
+#pragma once
+
+#include "rowtile.cuh"
+#include "umma.cuh"
+#include "umma_proj.cuh"
+
+namespace qk {
+
+constexpr int kPTok = 256;  // tokens per chunk of the prefill form (MMA N <= 256)
+constexpr int kPDecodeWarps = 16;
+constexpr int kPProducerWarp = 16;
+constexpr int kPMmaWarp = 17;
+constexpr int kPEpilogueWarp0 = 18;
+constexpr int kPEpilogueWarps = 8;
+constexpr int kPThreads = (kPEpilogueWarp0 + kPEpilogueWarps) * 32;  // 832
+constexpr int kPAtomA = 2 * 128 * 128;                                // A operand of one atom: 32 KB
+constexpr int kPAtomB = kPTok * 128;                                  // B operand of one atom: 32 KB
+
+// One quarter block (64 values = one K atom) of one weight row, decoded from a half-block
+// stage of its 64-row tile. The stage holds, per tile, the half's code chunks as
+// [chunk][64 rows][16 B], then (Q6_K) the scale chunk and the d plane, or (Q4_K) the header
+// chunk first, or (Q8_0) the scale chunk first.
+template <QType QT>
+struct QuarterTile;
+
+template <>
+struct QuarterTile<QType::Q6_K> {
+  // per tile: 6 code chunks (6 KB), the scale chunk (1 KB), d (128 B)
+  static constexpr int kStageTileBytes = 6 * 1024 + 1024 + 128;
+  // the half's bytes of one 64-row tile: three copies (codes, scale chunk, d plane)
+  __device__ __forceinline__ static uint32_t issue(uint8_t* dst, const uint8_t* tile, int h, uint64_t* bar,
+                                                   uint64_t pol) {
+    bulk_g2s_hint(dst, tile + 6 * h * 1024, 6 * 1024, bar, pol);
+    bulk_g2s_hint(dst + 6 * 1024, tile + 12 * 1024, 1024, bar, pol);
+    bulk_g2s_hint(dst + 7 * 1024, tile + HalfTile<QType::Q6_K>::kScaleOff, 128, bar, pol);
+    return kStageTileBytes;
+  }
+  // emit(k0, out[8]): 16 values at K positions k0 .. k0 + 15 of the atom
+  template <typename Emit>
+  __device__ __forceinline__ static void decode(const uint8_t* st, int row, int h, int qq, Emit&& emit) {
+    uint32_t w[12];
+#pragma unroll
+    for (int c = 0; c < 3; ++c) {
+      const uint4 v = lds128(st + ((3 * qq + c) * kTileRows + row) * 16);
+      w[4 * c] = v.x;
+      w[4 * c + 1] = v.y;
+      w[4 * c + 2] = v.z;
+      w[4 * c + 3] = v.w;
+    }
+    const uint32_t sc = *reinterpret_cast<const uint32_t*>(st + 6 * 1024 + row * 16 + 8 * h + 4 * qq);
+    const float d = f16_to_f32(*reinterpret_cast<const uint16_t*>(st + 7 * 1024 + row * 2));
+#pragma unroll
+    for (int jj = 0; jj < 4; ++jj) {
+      const float ds = __fmul_rn(d, static_cast<float>(static_cast<int8_t>((sc >> (8 * jj)) & 0xffu)));
+      const uint32_t w0 = w[3 * jj], w1 = w[3 * jj + 1], w2 = w[3 * jj + 2];
+      const uint32_t c3 = ((w0 >> 6) & 0x03030303u) | ((w1 >> 4) & 0x0c0c0c0cu) | ((w2 >> 2) & 0x30303030u);
+      uint32_t out[8];
+      code4<false, false>(w0 & 0x3f3f3f3fu, ds, 32.f, 0.f, out[0], out[1]);
+      code4<false, false>(w1 & 0x3f3f3f3fu, ds, 32.f, 0.f, out[2], out[3]);
+      code4<false, false>(w2 & 0x3f3f3f3fu, ds, 32.f, 0.f, out[4], out[5]);
+      code4<false, false>(c3, ds, 32.f, 0.f, out[6], out[7]);
+      emit(16 * jj, out);
+    }
+  }
+};
+
+template <>
+struct QuarterTile<QType::Q4_K> {
+  // per tile: the header chunk (d, dmin, packed scales; 1 KB), then the half's 4 code chunks
+  static constexpr int kStageTileBytes = 5 * 1024;
+  __device__ __forceinline__ static uint32_t issue(uint8_t* dst, const uint8_t* tile, int h, uint64_t* bar,
+                                                   uint64_t pol) {
+    bulk_g2s_hint(dst, tile, 1024, bar, pol);
+    bulk_g2s_hint(dst + 1024, tile + (1 + 4 * h) * 1024, 4 * 1024, bar, pol);
+    return kStageTileBytes;
+  }
+  template <typename Emit>
+  __device__ __forceinline__ static void decode(const uint8_t* st, int row, int h, int qq, Emit&& emit) {
+    const uint4 hd = lds128(st + row * 16);
+    const uint32_t hdw[4] = {hd.x, hd.y, hd.z, hd.w};
+    auto scale_byte = [&](int i) { return static_cast<int>((hdw[1 + (i >> 2)] >> (8 * (i & 3))) & 0xffu); };
+    uint32_t w[8];
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      const uint4 v = lds128(st + 1024 + ((2 * qq + c) * kTileRows + row) * 16);
+      w[4 * c] = v.x;
+      w[4 * c + 1] = v.y;
+      w[4 * c + 2] = v.z;
+      w[4 * c + 3] = v.w;
+    }
+    const float d = f16_to_f32(static_cast<uint16_t>(hdw[0] & 0xffffu));
+    const float dmin = f16_to_f32(static_cast<uint16_t>(hdw[0] >> 16));
+#pragma unroll
+    for (int s = 0; s < 2; ++s) {
+      const int j = 4 * h + 2 * qq + s;  // sub-block of 32 values (gguf_quant.py:118-135)
+      int sc, m;
+      if (j < 4) {
+        sc = scale_byte(j) & 63;
+        m = scale_byte(j + 4) & 63;
+      } else {
+        sc = (scale_byte(j + 4) & 15) | ((scale_byte(j - 4) >> 6) << 4);
+        m = (scale_byte(j + 4) >> 4) | ((scale_byte(j) >> 6) << 4);
+      }
+      const float ds = __fmul_rn(d, static_cast<float>(sc));
+      const float dm = __fmul_rn(dmin, static_cast<float>(m));
+#pragma unroll
+      for (int half16 = 0; half16 < 2; ++half16) {
+        uint32_t out[8];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const uint32_t code = (w[4 * half16 + i] >> (4 * s)) & 0x0f0f0f0fu;
+          code4<false, true>(code, ds, 0.f, dm, out[2 * i], out[2 * i + 1]);
+        }
+        emit(32 * s + 16 * half16, out);
+      }
+    }
+  }
+};
+
+template <>
+struct QuarterTile<QType::Q8_0> {
+  // per tile: the scale chunk (1 KB: 8 FP16 scales per row), then the half's 8 code chunks
+  static constexpr int kStageTileBytes = 9 * 1024;
+  __device__ __forceinline__ static uint32_t issue(uint8_t* dst, const uint8_t* tile, int h, uint64_t* bar,
+                                                   uint64_t pol) {
+    bulk_g2s_hint(dst, tile, 1024, bar, pol);
+    bulk_g2s_hint(dst + 1024, tile + (1 + 8 * h) * 1024, 8 * 1024, bar, pol);
+    return kStageTileBytes;
+  }
+  template <typename Emit>
+  __device__ __forceinline__ static void decode(const uint8_t* st, int row, int h, int qq, Emit&& emit) {
+    const uint32_t dw = *reinterpret_cast<const uint32_t*>(st + row * 16 + 8 * h + 4 * qq);
+#pragma unroll
+    for (int s = 0; s < 2; ++s) {  // GGUF block 4h + 2qq + s: 32 values
+      const float d = f16_to_f32(static_cast<uint16_t>(dw >> (16 * s)));
+#pragma unroll
+      for (int half16 = 0; half16 < 2; ++half16) {
+        const uint4 v = lds128(st + 1024 + ((4 * qq + 2 * s + half16) * kTileRows + row) * 16);
+        const uint32_t words[4] = {v.x, v.y, v.z, v.w};
+        uint32_t out[8];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) code4<false, false>(words[i] ^ 0x80808080u, d, 128.f, 0.f, out[2 * i], out[2 * i + 1]);
+        emit(32 * s + 16 * half16, out);
+      }
+    }
+  }
+};
+
+template <QType QT>
+struct PCfg {
+  static constexpr int kStageBytes = 4 * QuarterTile<QT>::kStageTileBytes;  // one half K block, 4 tiles
+  static constexpr int kRawStages = 2;
+  static constexpr int kBBufs = QT == QType::Q8_0 ? 2 : 3;
+  static constexpr size_t kAOff = 0;
+  static constexpr size_t kBOff = kAOff + 2 * kPAtomA;
+  static constexpr size_t kRawOff = kBOff + static_cast<size_t>(kBBufs) * kPAtomB;
+  static constexpr size_t kBarOff = kRawOff + static_cast<size_t>(kRawStages) * kStageBytes;
+  static constexpr size_t kSmem = 1024 + kBarOff + 256;
+  static_assert(kSmem <= 232448, "shared memory of the prefill form");
+};
+
+// A operand byte offset of (row, K position) inside one MMA tile's [128 rows x 64] atom.
+__device__ __forceinline__ uint32_t a_offset(uint32_t row, uint32_t k) {
+  const uint32_t chunk = k >> 3;
+  return (row >> 3) * 1024u + (row & 7) * 128u + ((chunk ^ (row & 7)) << 4) + (k & 7) * 2u;
+}
+
+// D[tmem] (+)= A[smem] * B[smem], M = 128, N from the descriptor, K = 16. One thread issues.
+__device__ __forceinline__ void umma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                        uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+template <QType QT, int MODE>
+__global__ void __launch_bounds__(kPThreads, 1) umma_prefill_kernel(const UArgs A) {
+  using Cfg = PCfg<QT>;
+  using QTile = QuarterTile<QT>;
+  constexpr int NB = Cfg::kBBufs;
+  constexpr int RS = Cfg::kRawStages;
+  constexpr int TB = HalfTile<QT>::kBytes;  // bytes of one 64-row tile of one K block
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* abuf = smem + Cfg::kAOff;
+  uint8_t* bbuf = smem + Cfg::kBOff;
+  uint8_t* raw = smem + Cfg::kRawOff;
+  uint64_t* raw_full = reinterpret_cast<uint64_t*>(smem + Cfg::kBarOff);
+  uint64_t* raw_empty = raw_full + RS;
+  uint64_t* b_full = raw_empty + RS;
+  uint64_t* b_empty = b_full + NB;
+  uint64_t* a_full = b_empty + NB;
+  uint64_t* a_empty = a_full + 2;
+  uint64_t* acc_full = a_empty + 2;
+  uint64_t* acc_empty = acc_full + 1;
+  uint32_t* tmem_sh = reinterpret_cast<uint32_t*>(acc_empty + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  pdl_trigger();
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < RS; ++s) {
+      mbar_init(&raw_full[s], 1);
+      mbar_init(&raw_empty[s], kPDecodeWarps);  // both decode groups read every raw stage
+    }
+    for (int s = 0; s < NB; ++s) {
+      mbar_init(&b_full[s], 1);
+      mbar_init(&b_empty[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&a_full[s], kPDecodeWarps / 2);
+      mbar_init(&a_empty[s], 1);
+    }
+    mbar_init(acc_full, 1);
+    mbar_init(acc_empty, kPEpilogueWarps);
+    fence_mbar_init();
+  }
+  if (warp == 0) tmem_alloc(tmem_sh, kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tmem_sh;
+  pdl_wait();
+  const int n_chunks = *A.n_chunks_p;
+  const int n_items = n_chunks * A.items_per_chunk;
+  const int n_atoms = 4 * A.nkb;  // K atoms of 64 values per item
+  bool ok = true;
+  const bool idle = static_cast<int>(blockIdx.x) >= n_items;
+
+  // weight tile w (0..3) of pair p: gate/up -> gate 2p, up 2p, gate 2p+1, up 2p+1;
+  // down -> 4p .. 4p + 3. Returns nullptr when the tile lies past the matrix.
+  auto tile_ptr = [&](int e, int p, int w, int kb) -> const uint8_t* {
+    int rt;
+    const uint8_t* base;
+    if (MODE == kModeGateUp) {
+      rt = 2 * p + (w >> 1);
+      base = ((w & 1) ? A.wb : A.wa) + static_cast<int64_t>(e) * A.expert_bytes;
+    } else {
+      rt = 4 * p + w;
+      base = A.wa + static_cast<int64_t>(e) * A.expert_bytes;
+    }
+    if (rt >= A.tiles64) return nullptr;
+    return base + (static_cast<int64_t>(rt) * A.nkb + kb) * TB;
+  };
+
+  if (idle) {
+  } else if (warp == kPProducerWarp) {
+    if (lane == 0) {
+      const uint64_t wpol = l2_evict_first_policy(), xpol = l2_evict_last_policy();
+      uint32_t hc = 0, ac = 0;  // half-block stages and atoms issued so far
+      for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
+        const int ci = item / A.items_per_chunk, p = item % A.items_per_chunk;
+        const ChunkInfo c = chunk_info<MODE>(A, ci);
+        const uint8_t* xsrc = A.xt + c.xrow * 512 * A.nkb;
+        const uint32_t xatom = static_cast<uint32_t>(c.r16) * 128u;
+        for (int hs = 0; hs < 2 * A.nkb && ok; ++hs, ++hc) {
+          const int s = hc % RS;
+          if (hc >= RS && !mbar_wait_bounded(&raw_empty[s], ((hc / RS) - 1) & 1)) {
+            ok = false;
+            break;
+          }
+          uint8_t* st = raw + static_cast<size_t>(s) * Cfg::kStageBytes;
+          uint32_t bytes = 0;
+          const uint8_t* tp[4];
+#pragma unroll
+          for (int w = 0; w < 4; ++w) {
+            tp[w] = tile_ptr(c.e, p, w, hs >> 1);
+            if (tp[w]) bytes += QTile::kStageTileBytes;
+          }
+          mbar_expect_tx(&raw_full[s], bytes);
+#pragma unroll
+          for (int w = 0; w < 4; ++w)
+            if (tp[w]) QTile::issue(st + w * QTile::kStageTileBytes, tp[w], hs & 1, &raw_full[s], wpol);
+          for (int a2 = 0; a2 < 2; ++a2, ++ac) {
+            const int bsl = ac % NB;
+            if (ac >= NB && !mbar_wait_bounded(&b_empty[bsl], ((ac / NB) - 1) & 1)) {
+              ok = false;
+              break;
+            }
+            const int atom = 2 * hs + a2;  // K atom: block atom >> 2, atom & 3 inside it
+            mbar_expect_tx(&b_full[bsl], xatom);
+            bulk_g2s_hint(bbuf + static_cast<size_t>(bsl) * kPAtomB,
+                          xsrc + static_cast<int64_t>(atom >> 2) * c.r16 * 512 + (atom & 3) * xatom, xatom,
+                          &b_full[bsl], xpol);
+          }
+        }
+      }
+    }
+  } else if (warp == kPMmaWarp) {
+    if (lane == 0) {
+      uint32_t ac = 0, ic = 0;
+      for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++ic) {
+        const int ci = item / A.items_per_chunk;
+        const ChunkInfo c = chunk_info<MODE>(A, ci);
+        const uint32_t idesc = idesc_bf16_m128(static_cast<uint32_t>(c.r16));
+        if (ic >= 1 && !mbar_wait_bounded(acc_empty, (ic - 1) & 1)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        for (int at = 0; at < n_atoms; ++at, ++ac) {
+          const int ab = ac & 1, bsl = ac % NB;
+          if (!mbar_wait_bounded(&a_full[ab], (ac >> 1) & 1) || !mbar_wait_bounded(&b_full[bsl], (ac / NB) & 1)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t as = smem_addr(abuf + ab * kPAtomA), bs = smem_addr(bbuf + static_cast<size_t>(bsl) * kPAtomB);
+#pragma unroll
+          for (int t = 0; t < 2; ++t) {
+            const uint64_t ad = sdesc_sw128(as + t * (kPAtomA / 2), 1024u);
+            const uint64_t bd = sdesc_sw128(bs, 1024u);
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks)
+              umma_ss(tbase + 256u * t, ad + ks * 2, bd + ks * 2, idesc, (at != 0) || (ks != 0));
+          }
+          umma_commit(&a_empty[ab]);
+          umma_commit(&b_empty[bsl]);
+        }
+        if (!ok) break;
+        umma_commit(acc_full);
+      }
+    }
+  } else if (warp >= kPEpilogueWarp0) {
+    const int ew = warp - kPEpilogueWarp0;
+    const int q = warp & 3, L = 32 * q + lane;  // TMEM lane quadrant of this warp
+    const int half = ew >> 2;                    // token columns [128 half, 128 half + 128)
+    uint32_t ic = 0;
+    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++ic) {
+      const int ci = item / A.items_per_chunk, p = item % A.items_per_chunk;
+      const ChunkInfo c = chunk_info<MODE>(A, ci);
+      if (!mbar_wait_bounded(acc_full, ic & 1)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const int c_lo = 128 * half, c_hi = min(c.r16, c_lo + 128);
+#pragma unroll 1
+      for (int t = 0; t < 2; ++t) {
+        const uint32_t tcol = tbase + (static_cast<uint32_t>(32 * q) << 16) + 256u * t;
+#pragma unroll 1
+        for (int c0 = c_lo; c0 < c_hi; c0 += 32) {
+          float acc[32];
+#pragma unroll
+          for (int cg = 0; cg < 4; ++cg) {
+            uint32_t v[8];
+            tmem_ld8(tcol + c0 + 8 * cg, v);
+            tmem_wait_ld();
+#pragma unroll
+            for (int jj = 0; jj < 8; ++jj) acc[8 * cg + jj] = __uint_as_float(v[jj]);
+          }
+          if (MODE == kModeGateUp) {
+            // lane pair (gate row r, up row r) of weight tile pair (2p + t): the even lane writes
+            // the first 16 tokens of the group, the odd lane the last 16
+            const int tt = L & 1, r = L >> 1;
+            const int R = 64 * (2 * p + t) + r;  // row of I
+            uint8_t* hbase = A.ht + c.xrow * 512 * A.nkb_out + static_cast<int64_t>(R >> 8) * c.r16 * 512;
+#pragma unroll
+            for (int col = 0; col < 32; ++col) {
+              const float other = __shfl_xor_sync(0xffffffffu, acc[col], 1);
+              if ((col < 16) == (tt == 0) && R < A.nrows && c0 + col < c.r16) {
+                const float gb = bf16_round(tt == 0 ? acc[col] : other);
+                const float ub = bf16_round(tt == 0 ? other : acc[col]);
+                const float act = bf16_round(__fmul_rn(gb, sigmoid_ref(gb)));  // silu, math.py:19-20
+                *reinterpret_cast<uint16_t*>(hbase + xt_offset(c.r16, c0 + col, R & 255)) =
+                    bf16_bits_rne(__fmul_rn(act, ub));
+              }
+            }
+          } else {
+            const int R = 256 * p + 128 * t + L;  // row of H
+            if (R < A.nrows) {
+#pragma unroll
+              for (int col = 0; col < 32; ++col) {
+                if (c0 + col >= c.ntok) break;
+                const int64_t orow = c.entry0 + c0 + col;
+                if (A.yr) A.yr[static_cast<int64_t>(A.entry_route[orow]) * A.nrows + R] = acc[col];
+                else A.y[orow * A.nrows + R] = bf16_bits_rne(acc[col]);
+              }
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(acc_empty);
+    }
+  } else {
+    // ---------------- decode warps: group g takes the atoms with ac % 2 == g ----------------
+    const int g = warp >> 3, ar = 32 * (warp & 7) + lane;  // A row 0..255 of the atom
+    const int t = ar >> 7, r = ar & 127;                   // MMA tile, row inside it
+    // weight tile (0..3 of the item) and its row: gate/up interleave gate and up rows
+    const int wt = MODE == kModeGateUp ? 2 * t + (r & 1) : 2 * t + (r >> 6);
+    const int wrow = MODE == kModeGateUp ? (r >> 1) : (r & 63);
+    uint32_t ac = 0;
+    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
+      const int p = item % A.items_per_chunk;
+      const int rt = MODE == kModeGateUp ? 2 * p + (wt >> 1) : 4 * p + wt;
+      const bool mine = rt < A.tiles64;
+      for (int at = 0; at < n_atoms; ++at, ++ac) {
+        if ((ac & 1) != static_cast<uint32_t>(g)) continue;
+        const uint32_t hc = ac >> 1;  // the raw stage of atom ac (two atoms per half block)
+        const int s = hc % RS;
+        if (!mbar_wait_bounded(&raw_full[s], (hc / RS) & 1)) {
+          ok = false;
+          break;
+        }
+        if (ac >= 2 && !mbar_wait_bounded(&a_empty[g], ((ac >> 1) - 1) & 1)) {
+          ok = false;
+          break;
+        }
+        uint8_t* dst = abuf + g * kPAtomA + t * (kPAtomA / 2);
+        const int hh = (at >> 1) & 1, qq = at & 1;  // half of the K block, quarter of the half
+        if (mine) {
+          const uint8_t* st = raw + static_cast<size_t>(s) * Cfg::kStageBytes + wt * QTile::kStageTileBytes;
+          QTile::decode(st, wrow, hh, qq, [&](int k0, const uint32_t(&o)[8]) {
+            *reinterpret_cast<uint4*>(dst + a_offset(r, k0)) = make_uint4(o[0], o[1], o[2], o[3]);
+            *reinterpret_cast<uint4*>(dst + a_offset(r, k0 + 8)) = make_uint4(o[4], o[5], o[6], o[7]);
+          });
+        } else {
+#pragma unroll
+          for (int k0 = 0; k0 < 64; k0 += 8) *reinterpret_cast<uint4*>(dst + a_offset(r, k0)) = make_uint4(0, 0, 0, 0);
+        }
+        fence_proxy_async_smem();  // the generic-proxy stores must be visible to the MMA
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&raw_empty[s]);
+          mbar_arrive(&a_full[g]);
+        }
+      }
+    }
+  }
+
+  if (!ok && lane == 0 && A.status) atomicExch(A.status, QK_ERR_TIMEOUT);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tbase, kTmemCols);
+  }
+}
+
+template <QType QT, int MODE>
+int launch_prefill(const UArgs& A, int grid, cudaStream_t st) {
+  using Cfg = PCfg<QT>;
+  int rc = allow_smem(reinterpret_cast<const void*>(umma_prefill_kernel<QT, MODE>), Cfg::kSmem);
+  if (rc) return rc;
+  const cudaError_t e = launch_dependent(umma_prefill_kernel<QT, MODE>, dim3(grid), dim3(kPThreads), Cfg::kSmem, st, A);
+  if (e != cudaSuccess) return cuda_error(e, "umma_prefill_kernel");
+  count_launch(1);
+  return QK_OK;
+}
+
+}  // namespace qk

@@ -112,6 +112,20 @@ SIGNATURES = {
     "qk_ep_combine": (_i, [_p, _p, _p, _p, _i, _i, _i, _i, _p, _p]),
     "qk_kv_q8_attention_check": (_i, [_p]),
     "qk_numerics": (_i, [_i, _p, _p, _p, _i64, _i, _p]),
+    "qk_ep_p2p_bytes": (_sz, [_i, _i, _i, _i]),
+    "qk_ep_p2p_reset": (_i, [_p, _p]),
+    "qk_ep_p2p_status": (_i, [_p, _p]),
+    "qk_ep_p2p_dispatch": (_i, [_p, _p, _i, _i, _i, _i, _i, _i, _p, _p, _p, _i, _p]),
+    "qk_ep_p2p_expert": (
+        _i,
+        [ctypes.POINTER(MoeDesc), _p, _p, _p, _p, _p, _i, _i, _i, _p, _sz, _p],
+    ),
+    "qk_ep_p2p_combine": (_i, [_p, _i, _i, _i, _i, _i, _i, _p, _p, _i, _p, _p]),
+    "qk_device_alloc": (_i, [_sz, ctypes.POINTER(_p)]),
+    "qk_device_free": (_i, [_p]),
+    "qk_ipc_get_handle": (_i, [_p, _p]),
+    "qk_ipc_open_handle": (_i, [_p, ctypes.POINTER(_p)]),
+    "qk_ipc_close_handle": (_i, [_p]),
     "qk_kv_q8_decode_attention_noalloc": (
         _i,
         [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _i, _p, _p],

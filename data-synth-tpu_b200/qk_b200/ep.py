@@ -1,4 +1,9 @@
-"""Expert parallelism with token dispatch over ``torch.distributed`` all-to-all (NCCL).
+"""Expert parallelism with token dispatch.
+
+Two forms of the same layer. ``ExpertAllToAll`` (the product path) moves tokens and
+partial outputs through peer memory over NVLink with no host synchronisation
+(``qk_ep_p2p_*``, ``csrc/ep_p2p.cu``). ``ExpertAllToAllNccl`` (below) is the variable-size
+NCCL all-to-all form, whose split sizes are read back to the host every call.
 
 The reference's expert-parallel layer replicates every token on every rank and adds the
 ranks' partial outputs with a ``psum`` (``qwen38_tpu/experts.py:130-131``, placement
@@ -11,8 +16,8 @@ back, and combines them per token in ascending expert order in FP32
 tokens. Per layer it moves ``routes * hidden * 2`` bytes each way over NVLink instead of
 all-reducing ``tokens * hidden * 4`` bytes.
 
-    fn = ExpertAllToAll(group, gate_type="Q6_K", up_type="Q6_K", down_type="Q6_K",
-                        hidden=2048, intermediate=512, experts_per_rank=E // world)
+    fn = ExpertAllToAllNccl(group, gate_type="Q6_K", up_type="Q6_K", down_type="Q6_K",
+                            hidden=2048, intermediate=512, experts_per_rank=E // world)
     out = fn(gate, up, down, x, ids, weights)   # this rank's tokens -> bf16 [B, hidden]
 
 ``ops`` carries the four local steps; the default uses this library's kernels
@@ -95,8 +100,10 @@ class DeviceOps:
         return out
 
 
-class ExpertAllToAll:
-    """Routed expert FFN with token dispatch; see the module docstring."""
+class ExpertAllToAllNccl:
+    """Routed expert FFN with token dispatch over NCCL all-to-all; see the module docstring.
+    Each call reads the per-rank send counts back to the host (two synchronisations), so it
+    cannot be captured in a CUDA graph; ``ExpertAllToAll`` has neither limitation."""
 
     def __init__(self, group, *, gate_type, up_type, down_type, hidden, intermediate,
                  experts_per_rank, ops=None):
@@ -153,4 +160,153 @@ class ExpertAllToAll:
         return self.ops.combine(y_send, plan, ids, self.hidden)
 
 
-__all__ = ["ExpertAllToAll", "DeviceOps", "Plan"]
+class ExchangeRegion:
+    """This rank's exchange region of the peer-to-peer layer and the table of every rank's
+    region as mapped in this process (CUDA IPC handles exchanged over ``group``).
+
+    ``regions``/``rank`` instead of ``group``: ranks emulated in one process on one device
+    (test infrastructure), every region already allocated here."""
+
+    def __init__(self, group, *, max_tokens, hidden, top_k, device, world=None, rank=None,
+                 shared=None):
+        import ctypes
+
+        self.device = torch.device(device)
+        lib = _lib.load()
+        if shared is not None:
+            world, rank = shared["world"], rank
+        elif group is None:
+            world, rank = 1, 0
+        else:
+            import torch.distributed as dist
+
+            world, rank = dist.get_world_size(group), dist.get_rank(group)
+        self.world, self.rank = world, rank
+        self.max_tokens, self.hidden, self.top_k = max_tokens, hidden, top_k
+        self.bytes = int(lib.qk_ep_p2p_bytes(world, max_tokens, hidden, top_k))
+        if self.bytes == 0:
+            raise ValueError("bad exchange geometry")
+        self._opened = []
+        self._owned = None
+        with torch.cuda.device(self.device):
+            if shared is not None:
+                self.base = shared["regions"][rank]
+                bases = shared["regions"]
+            else:
+                ptr = ctypes.c_void_p()
+                _lib.check(lib.qk_device_alloc(self.bytes, ctypes.byref(ptr)))
+                self._owned = ptr.value
+                self.base = ptr.value
+                _lib.check(lib.qk_ep_p2p_reset(ctypes.c_void_p(self.base), _lib.stream_handle(self.device)))
+                torch.cuda.synchronize(self.device)
+                bases = [None] * world
+                bases[rank] = self.base
+                if world > 1:
+                    import torch.distributed as dist
+
+                    handle = (ctypes.c_uint8 * 64)()
+                    _lib.check(lib.qk_ipc_get_handle(ctypes.c_void_p(self.base), handle))
+                    handles = [None] * world
+                    dist.all_gather_object(handles, bytes(handle), group=group)
+                    for r in range(world):
+                        if r == rank:
+                            continue
+                        p = ctypes.c_void_p()
+                        buf = (ctypes.c_uint8 * 64).from_buffer_copy(handles[r])
+                        _lib.check(lib.qk_ipc_open_handle(buf, ctypes.byref(p)))
+                        self._opened.append(p.value)
+                        bases[r] = p.value
+                    # every region is cleared before any peer may write into it
+                    dist.barrier(group=group)
+            self.peers = torch.tensor(bases, dtype=torch.int64, device=self.device)
+
+    @property
+    def region(self):
+        import ctypes
+
+        return ctypes.c_void_p(self.base)
+
+    def status(self):
+        with torch.cuda.device(self.device):
+            _lib.check(_lib.load().qk_ep_p2p_status(self.region, _lib.stream_handle(self.device)))
+
+    def close(self):
+        import ctypes
+
+        lib = _lib.load()
+        for p in self._opened:
+            lib.qk_ipc_close_handle(ctypes.c_void_p(p))
+        self._opened = []
+        if self._owned is not None:
+            lib.qk_device_free(ctypes.c_void_p(self._owned))
+            self._owned = None
+
+
+class ExpertAllToAll:
+    """Routed expert FFN with token dispatch over peer memory (``csrc/ep_p2p.cu``).
+
+    Rank r of ``group`` holds experts ``[r * experts_per_rank, (r + 1) * experts_per_rank)``
+    (``parallel.py:64-87``) and its own tokens (at most ``max_tokens`` per call). A call is
+    three launches' worth of stream-ordered work on every rank, none of which waits for
+    the host: each token row goes once to every rank that owns one of its experts; the
+    owner runs its experts and returns the token's FP32 partial sum (ascending expert
+    order); the source adds the partials in ascending rank order and rounds to BF16. That
+    is the reference's expert-parallel arithmetic (local sum, ``psum``, cast;
+    ``experts.py:128-131``); with one rank it is bit-identical to ``expert_parallel``.
+
+    Every rank must make the same sequence of calls. The output is a view of a buffer the
+    layer owns (valid until its next call) unless ``out`` is given."""
+
+    def __init__(self, group, *, gate_type, up_type, down_type, hidden, intermediate,
+                 experts_per_rank, top_k, max_tokens, device=None, region=None):
+        self.types = tuple(normalize_qtype(t) for t in (gate_type, up_type, down_type))
+        self.hidden, self.intermediate = hidden, intermediate
+        self.experts_per_rank, self.top_k, self.max_tokens = experts_per_rank, top_k, max_tokens
+        self.device = torch.device("cuda", torch.cuda.current_device()) if device is None \
+            else torch.device(device)
+        self.region = region or ExchangeRegion(group, max_tokens=max_tokens, hidden=hidden,
+                                               top_k=top_k, device=self.device)
+        self.world, self.rank = self.region.world, self.region.rank
+        self.desc = _lib.MoeDesc(*(GGML_TYPE[t] for t in self.types), hidden, intermediate,
+                                 experts_per_rank, self.rank * experts_per_rank, top_k)
+        need = int(_lib.load().qk_moe_workspace_bytes(self.desc, self.world * max_tokens))
+        self.workspace = torch.empty(max(need, 1), dtype=torch.uint8, device=self.device)
+        self.out = torch.empty((max_tokens, hidden), dtype=torch.bfloat16, device=self.device)
+
+    def __call__(self, gate, up, down, x, ids, weights, out=None):
+        if x.dim() != 2 or x.shape[1] != self.hidden:
+            raise TypeError("x must be a [B, hidden] tensor")
+        B = x.shape[0]
+        if ids.shape != (B, self.top_k) or weights.shape != ids.shape:
+            raise ValueError("ids and weights must be [B, top_k]")
+        if B > self.max_tokens:
+            raise ValueError(f"batch {B} exceeds max_tokens {self.max_tokens}")
+        if gate.shape[0] != self.experts_per_rank:
+            raise ValueError("gate, up and down must hold this rank's experts_per_rank experts")
+        if ids.dtype != torch.int32 or weights.dtype != torch.bfloat16 or x.dtype != torch.bfloat16:
+            raise TypeError("x and weights must be bfloat16, ids int32")
+        out = self.out[:B] if out is None else out
+        lib = _lib.load()
+        st = _lib.stream_handle(self.device)
+        peers, region = _lib.ptr(self.region.peers), self.region.region
+        _lib.check(lib.qk_ep_p2p_dispatch(peers, region, self.world, self.rank, self.max_tokens,
+                                          self.hidden, self.top_k, self.experts_per_rank,
+                                          _lib.ptr(x), _lib.ptr(ids), _lib.ptr(weights), B, st))
+        _lib.check(lib.qk_ep_p2p_expert(self.desc, _lib.ptr(gate), _lib.ptr(up), _lib.ptr(down),
+                                        peers, region, self.world, self.rank, self.max_tokens,
+                                        _lib.ptr(self.workspace), self.workspace.numel(), st))
+        _lib.check(lib.qk_ep_p2p_combine(region, self.world, self.rank, self.max_tokens,
+                                         self.hidden, self.top_k, self.experts_per_rank,
+                                         _lib.ptr(ids), _lib.ptr(weights), B, _lib.ptr(out), st))
+        return out
+
+    def check_status(self):
+        """Raise if a bounded wait on a peer gave up (synchronises the stream)."""
+        self.region.status()
+        _lib.call("qk_moe_check", _lib.ptr(self.workspace), _lib.stream_handle(self.device))
+
+    def close(self):
+        self.region.close()
+
+
+__all__ = ["ExpertAllToAll", "ExpertAllToAllNccl", "ExchangeRegion", "DeviceOps", "Plan"]

@@ -191,6 +191,43 @@ int qk_ep_combine(const uint16_t* y, const int32_t* route_slot, const int32_t* i
                   const float* route_weight, int B, int k, int H, int out_dtype, void* out,
                   qk_stream_t stream);
 
+/* ---- expert parallel over peer memory (no host synchronisation) ---------------------
+ * The same layer as experts.py:61-131 with experts sharded over ranks (parallel.py:64-87)
+ * and each rank keeping its own tokens. Every rank allocates one exchange region of
+ * qk_ep_p2p_bytes() bytes (qk_device_alloc), clears its control words (qk_ep_p2p_reset),
+ * exports it (qk_ipc_get_handle) and maps every peer's (qk_ipc_open_handle); `peers` is a
+ * DEVICE array of `world` region pointers as mapped in this process (its own at [rank]).
+ * A step is three stream-ordered calls on every rank, with the same max_tokens everywhere:
+ * qk_ep_p2p_dispatch stores each token row once into every owner of one of its routed
+ * experts (slot = token index, so no counts cross ranks); qk_ep_p2p_expert runs this rank's
+ * experts over the received slots and stores each slot's FP32 partial (ascending expert
+ * order) back into its source; qk_ep_p2p_combine adds a token's partials in ascending rank
+ * order and rounds once to BF16 (experts.py:128-131: local sum, psum, cast). Waits on peers
+ * are bounded; qk_ep_p2p_status reports one that gave up (QK_ERR_TIMEOUT). No call
+ * allocates, and all sizes are fixed by (world, max_tokens), so a step can be captured in
+ * a CUDA graph. */
+size_t qk_ep_p2p_bytes(int world, int max_tokens, int hidden, int top_k);
+int qk_ep_p2p_reset(void* region, qk_stream_t stream);
+int qk_ep_p2p_status(const void* region, qk_stream_t stream);
+int qk_ep_p2p_dispatch(void* const* peers, void* region, int world, int rank, int max_tokens,
+                       int hidden, int top_k, int experts_per_rank, const uint16_t* x,
+                       const int32_t* ids, const uint16_t* weights, int B, qk_stream_t stream);
+/* desc: this rank's experts (num_experts = experts_per_rank, first_expert = rank *
+ * experts_per_rank); workspace of qk_moe_workspace_bytes(desc, world * max_tokens). */
+int qk_ep_p2p_expert(const qk_moe_desc* desc, const uint8_t* gate, const uint8_t* up,
+                     const uint8_t* down, void* const* peers, void* region, int world, int rank,
+                     int max_tokens, void* workspace, size_t workspace_bytes, qk_stream_t stream);
+int qk_ep_p2p_combine(void* region, int world, int rank, int max_tokens, int hidden, int top_k,
+                      int experts_per_rank, const int32_t* ids, const uint16_t* weights, int B,
+                      uint16_t* out, qk_stream_t stream);
+/* Device memory another process of the node can map: cudaMalloc / cudaFree and the CUDA
+ * IPC handle (64 bytes) of an allocation, opened with peer access enabled. */
+int qk_device_alloc(size_t bytes, void** ptr);
+int qk_device_free(void* ptr);
+int qk_ipc_get_handle(void* ptr, uint8_t* handle64);
+int qk_ipc_open_handle(const uint8_t* handle64, void** ptr);
+int qk_ipc_close_handle(void* ptr);
+
 /* ---- Q8 KV cache -------------------------------------------------------------
  * Cache layout is the reference's (attention_cache.py:26-43, engine.py:350-369):
  * codes int8 [B, T, kv_heads * head_dim]; scale planes BF16 [B * G, T] with

@@ -1,5 +1,5 @@
 """Expert parallelism with token dispatch (qk_ep_plan / qk_gather_rows / qk_ep_combine and
-ExpertAllToAll) on the GPU: bit-identical to the single-device routed FFN."""
+ExpertAllToAllNccl) on the GPU: bit-identical to the single-device routed FFN."""
 
 import os
 
@@ -68,7 +68,7 @@ def test_plan_counts_slots_and_merged_weights(cuda_device):
 def test_all_to_all_layer_on_one_device_equals_routed_ffn(cuda_device):
     import torch
 
-    from qk_b200.ep import ExpertAllToAll
+    from qk_b200.ep import ExpertAllToAllNccl
     from qk_b200.experts import expert_parallel
     from qk_b200.parallel import put_expert_bytes
 
@@ -79,7 +79,7 @@ def test_all_to_all_layer_on_one_device_equals_routed_ffn(cuda_device):
     args = (t["gate"], t["up"], t["down"], bf16_tensor(x, cuda_device), torch.from_numpy(ids).to(cuda_device),
             bf16_tensor(w, cuda_device))
     ref = expert_parallel(gate_type="Q6_K", up_type="Q6_K", down_type="Q6_K", hidden=HIDDEN, intermediate=INTER)(*args)
-    fn = ExpertAllToAll(None, gate_type="Q6_K", up_type="Q6_K", down_type="Q6_K", hidden=HIDDEN,
+    fn = ExpertAllToAllNccl(None, gate_type="Q6_K", up_type="Q6_K", down_type="Q6_K", hidden=HIDDEN,
                         intermediate=INTER, experts_per_rank=count)
     got = fn(*args)
     torch.cuda.synchronize(cuda_device)
@@ -98,7 +98,7 @@ def _two_gpu_rank(rank, world, port, path):
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
                             device_id=dev)
     try:
-        from qk_b200.ep import ExpertAllToAll
+        from qk_b200.ep import ExpertAllToAllNccl
         from qk_b200.experts import expert_parallel
         from qk_b200.parallel import put_expert_bytes
 
@@ -107,7 +107,7 @@ def _two_gpu_rank(rank, world, port, path):
         raw = _experts(count, 21)
         x, ids, w = _tokens(17 + 5 * rank, k, count, 30 + rank)
         mine = {n: put_expert_bytes(raw[n], n, "Q6_K", HIDDEN, INTER, rank=rank, world=world, device=dev) for n in raw}
-        fn = ExpertAllToAll(dist.group.WORLD, gate_type="Q6_K", up_type="Q6_K", down_type="Q6_K",
+        fn = ExpertAllToAllNccl(dist.group.WORLD, gate_type="Q6_K", up_type="Q6_K", down_type="Q6_K",
                             hidden=HIDDEN, intermediate=INTER, experts_per_rank=per)
         xd, idd, wd = bf16_tensor(x, dev), torch.from_numpy(ids).to(dev), bf16_tensor(w, dev)
         got = fn(mine["gate"], mine["up"], mine["down"], xd, idd, wd)

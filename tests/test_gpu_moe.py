@@ -101,23 +101,51 @@ def test_many_tokens_per_expert_duplicates_and_finished_rows(cuda_device, tokens
 
 @pytest.mark.parametrize("qtype", ["Q6_K", "Q4_K"])
 def test_wide_form_chunks_of_128_tokens(cuda_device, qtype):
-    """Routes averaging >= 64 tokens per expert take the wide form (128-token chunks, one
-    MMA issuer, N up to 128): 300 tokens per expert give chunks of 128, 128 and a ragged
-    last one; an expert with a single token shares the call."""
+    """Routes averaging 64 to 191 tokens per expert take the wide form (128-token chunks, one
+    MMA issuer, N up to 128): 150 tokens per expert give chunks of 128 and a ragged last one;
+    an expert with a single token shares the call."""
     hidden, intermediate, count, k = 512, 512, 5, 2
     rng = np.random.default_rng(300)
     raw = make_experts(rng, count, hidden, intermediate, qtype)
-    batch = 300 * (count - 1) // k + 1
+    batch = 150 * (count - 1) // k + 1
     ids = rng.integers(0, count - 1, (batch, k)).astype(np.int32)
     ids[0, 1] = count - 1            # the last expert: one token
     ids[1:4, 1] = ids[1:4, 0]        # duplicate routes merge
     weights = bf16_round(rng.uniform(0.05, 1.0, (batch, k)).astype(np.float32))
     weights[5::11] = 0
     x = rng.normal(size=(batch, hidden)).astype(np.float32)
-    assert batch * k >= 64 * count   # the wide form
+    assert 64 * count <= batch * k < 192 * count   # the wide form
     got, _, _ = run_layer(cuda_device, raw, qtype, hidden, intermediate, x, ids, weights)
     expected = moe.expert_ffn(raw["gate"], raw["up"], raw["down"], x, ids, weights, gate_type=qtype,
                               up_type=qtype, down_type=qtype, hidden=hidden, intermediate=intermediate)
+    mx, l2 = rel_err(got, expected)
+    assert mx < LAYER_TOL and l2 < 2e-3, (mx, l2)
+    np.testing.assert_array_equal(got[5::11], 0)
+
+
+@pytest.mark.parametrize("qtype,down_type,hidden,intermediate", [
+    ("Q6_K", "Q6_K", 512, 512), ("Q4_K", "Q4_K", 768, 256), ("Q6_K", "Q8_0", 512, 640),
+    ("Q4_K", "Q8_0", 256, 96)])
+def test_prefill_form_chunks_of_256_tokens(cuda_device, qtype, down_type, hidden, intermediate):
+    """Routes averaging >= 192 tokens per expert take the prefill form (256-token chunks,
+    weights decoded into shared memory, both MMA operands in shared memory, 512 TMEM
+    accumulator columns): 600 tokens per expert give chunks of 256, 256 and a ragged 88 (not a
+    multiple of 16); an expert with one token, merged duplicate routes and finished rows share
+    the call; I = 640 and 96 leave tile pairs and K blocks partly empty."""
+    count, k = 5, 2
+    rng = np.random.default_rng(600 + intermediate)
+    raw = make_experts(rng, count, hidden, intermediate, qtype, down_type)
+    batch = 600 * (count - 1) // k + 1
+    ids = np.stack([rng.choice(count - 1, k, replace=False) for _ in range(batch)]).astype(np.int32)
+    ids[0, 1] = count - 1            # the last expert: one token
+    ids[1:4, 1] = ids[1:4, 0]        # duplicate routes merge
+    weights = bf16_round(rng.uniform(0.05, 1.0, (batch, k)).astype(np.float32))
+    weights[5::11] = 0
+    x = rng.normal(size=(batch, hidden)).astype(np.float32)
+    assert batch * k >= 192 * count  # the prefill form
+    got, _, _ = run_layer(cuda_device, raw, qtype, hidden, intermediate, x, ids, weights, down_type=down_type)
+    expected = moe.expert_ffn(raw["gate"], raw["up"], raw["down"], x, ids, weights, gate_type=qtype,
+                              up_type=qtype, down_type=down_type, hidden=hidden, intermediate=intermediate)
     mx, l2 = rel_err(got, expected)
     assert mx < LAYER_TOL and l2 < 2e-3, (mx, l2)
     np.testing.assert_array_equal(got[5::11], 0)

@@ -114,7 +114,7 @@ def test_expert_parallel_partials_all_reduce_to_the_layer_gloo(tmp_path):
 
 
 class _NumpyOps:
-    """The four local steps of ExpertAllToAll restated with the oracle (CPU, test only)."""
+    """The four local steps of ExpertAllToAllNccl restated with the oracle (CPU, test only)."""
 
     def __init__(self, qtype, hidden, intermediate):
         self.qtype, self.hidden, self.intermediate = qtype, hidden, intermediate
@@ -182,7 +182,7 @@ def _a2a_rank(rank, world, port, result_path):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
-        from qk_b200.ep import ExpertAllToAll
+        from qk_b200.ep import ExpertAllToAllNccl
 
         hidden, inter, per, k = 256, 256, 3, 3
         count = per * world
@@ -197,7 +197,7 @@ def _a2a_rank(rank, world, port, result_path):
         weights = bf16_round(trng.uniform(0.1, 1, (B, k)).astype(np.float32))
         weights[1, 2] = 0.0    # a dropped route
         mine = slice(rank * per, (rank + 1) * per)
-        fn = ExpertAllToAll(dist.group.WORLD, gate_type="Q6_K", up_type="Q6_K", down_type="Q6_K",
+        fn = ExpertAllToAllNccl(dist.group.WORLD, gate_type="Q6_K", up_type="Q6_K", down_type="Q6_K",
                             hidden=hidden, intermediate=inter, experts_per_rank=per,
                             ops=_NumpyOps("Q6_K", hidden, inter))
         got = fn(raw["gate"][mine], raw["up"][mine], raw["down"][mine], torch.from_numpy(x),
