@@ -81,6 +81,17 @@ __device__ __forceinline__ float bf16_round(float x) {
   return __uint_as_float(static_cast<uint32_t>(bf16_bits_rne(x)) << 16);
 }
 
+// bf16_round by the hardware conversion (cvt.rn.bf16.f32): the same result for finite and
+// infinite values; a NaN comes out as the canonical quiet NaN instead of the quieted payload.
+__device__ __forceinline__ uint16_t bf16_bits_hw(float x) {
+  uint16_t r;
+  asm("cvt.rn.bf16.f32 %0, %1;" : "=h"(r) : "f"(x));
+  return r;
+}
+__device__ __forceinline__ float bf16_round_hw(float x) {
+  return __uint_as_float(static_cast<uint32_t>(bf16_bits_hw(x)) << 16);
+}
+
 __device__ __forceinline__ float bf16_to_f32(uint16_t bits) {
   return __uint_as_float(static_cast<uint32_t>(bits) << 16);
 }

@@ -471,13 +471,6 @@ __global__ void ep_wait_sources_kernel(uint8_t* own, int world) {
 }
 
 bool supported(int t) { return t == QK_TYPE_Q6_K || t == QK_TYPE_Q4_K; }
-
-// The narrow MoE passes copy two K blocks per bulk copy (umma_pair_kernel); building with
-// -DQK_PAIR_COPIES=0 restores one copy per K block (umma_proj_kernel).
-#ifndef QK_PAIR_COPIES
-#define QK_PAIR_COPIES 1
-#endif
-constexpr bool kPairCopies = QK_PAIR_COPIES != 0;
 // The down projection also takes Q8_0 (the real checkpoints' down type, checkpoints/q6.json).
 bool supported_down(int t) { return supported(t) || t == QK_TYPE_Q8_0; }
 
@@ -643,8 +636,6 @@ static int moe_forward_impl(const qk_moe_desc* desc, const uint8_t* gate, const 
   } else if (wide) {
     rc = q6 ? launch_umma<QType::Q6_K, kModeGateUp, true>(gu, sms, st)
             : launch_umma<QType::Q4_K, kModeGateUp, true>(gu, sms, st);
-  } else if (kPairCopies) {
-    rc = q6 ? launch_pair<QType::Q6_K, kModeGateUp>(gu, sms, st) : launch_pair<QType::Q4_K, kModeGateUp>(gu, sms, st);
   } else {
     rc = q6 ? launch_umma<QType::Q6_K, kModeGateUp>(gu, sms, st) : launch_umma<QType::Q4_K, kModeGateUp>(gu, sms, st);
   }
@@ -658,10 +649,6 @@ static int moe_forward_impl(const qk_moe_desc* desc, const uint8_t* gate, const 
     if (d.down_type == QK_TYPE_Q8_0) rc = launch_umma<QType::Q8_0, kModeDown, true>(dn, sms, st);
     else if (d.down_type == QK_TYPE_Q6_K) rc = launch_umma<QType::Q6_K, kModeDown, true>(dn, sms, st);
     else rc = launch_umma<QType::Q4_K, kModeDown, true>(dn, sms, st);
-  } else if (kPairCopies) {
-    if (d.down_type == QK_TYPE_Q8_0) rc = launch_pair<QType::Q8_0, kModeDown>(dn, sms, st);
-    else if (d.down_type == QK_TYPE_Q6_K) rc = launch_pair<QType::Q6_K, kModeDown>(dn, sms, st);
-    else rc = launch_pair<QType::Q4_K, kModeDown>(dn, sms, st);
   } else {
     if (d.down_type == QK_TYPE_Q8_0) rc = launch_umma<QType::Q8_0, kModeDown>(dn, sms, st);
     else if (d.down_type == QK_TYPE_Q6_K) rc = launch_umma<QType::Q6_K, kModeDown>(dn, sms, st);

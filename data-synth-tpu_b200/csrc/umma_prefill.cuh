@@ -16,12 +16,14 @@
 //
 // The K loop runs over 64-value K atoms. Per atom, 8 decode warps (a group; the two groups
 // take alternate atoms) turn one quarter block of each of the item's 256 weight rows into the
-// BF16 A operand (2 x [128 rows x 128 B], 128-byte-swizzled K-major) in shared memory; the
-// producer streams the packed weights (one half K block of the 4 weight tiles per stage:
-// the half's code chunks, the scale chunk and, for Q6_K, the d plane) and the activation
-// atom ([tokens x 128 B], the layout the dispatch / gate-up epilogue wrote) with 1-D bulk
-// copies (no multicast); one thread issues 2 x 4 MMAs (M = 128, N = chunk tokens rounded to
-// 16, K = 16) per atom. Warps: 0-15 decode, 16 producer, 17 MMA, 18-25 epilogue (two per TMEM
+// BF16 A operand (2 x [128 rows x 128 B], 128-byte-swizzled K-major) in shared memory. The
+// producer streams each K block of the item's 4 weight tiles (one 1-D bulk copy per tile:
+// a copy costs its SM ~0.3 us up to ~16 KB, so copies must be large) and each activation atom
+// ([tokens x 128 B], the layout the dispatch / gate-up epilogue wrote; 32 KB at 256 tokens),
+// no multicast. The weight stage is single: every decode warp takes its two quarters of the
+// block into registers first and releases the stage, so the next block's copies overlap the
+// block's four atoms. One thread issues 2 x 4 MMAs (M = 128, N = chunk tokens rounded to 16,
+// K = 16) per atom. Warps: 0-15 decode, 16 producer, 17 MMA, 18-25 epilogue (two per TMEM
 // lane quadrant, each taking half of the token columns). Every wait is bounded; on give-up
 // the CTA records QK_ERR_TIMEOUT in `status` and leaves its loops.
 #pragma once
@@ -42,43 +44,50 @@ constexpr int kPThreads = (kPEpilogueWarp0 + kPEpilogueWarps) * 32;  // 832
 constexpr int kPAtomA = 2 * 128 * 128;                                // A operand of one atom: 32 KB
 constexpr int kPAtomB = kPTok * 128;                                  // B operand of one atom: 32 KB
 
-// One quarter block (64 values = one K atom) of one weight row, decoded from a half-block
-// stage of its 64-row tile. The stage holds, per tile, the half's code chunks as
-// [chunk][64 rows][16 B], then (Q6_K) the scale chunk and the d plane, or (Q4_K) the header
-// chunk first, or (Q8_0) the scale chunk first.
+// Decode of one weight row's quarter blocks (64 values = one K atom) from a K-block stage of
+// its 64-row tile (the tile's whole block, as one bulk copy). Decode group g handles the
+// atoms g and g + 2 of every K block, i.e. quarter g of both halves: `load` reads their
+// bytes into registers once per K block (so the stage can be refilled while the group
+// decodes), `decode<h>` then produces quarter g of half h.
 template <QType QT>
-struct QuarterTile;
+struct QuarterRegs;
 
 template <>
-struct QuarterTile<QType::Q6_K> {
-  // per tile: 6 code chunks (6 KB), the scale chunk (1 KB), d (128 B)
-  static constexpr int kStageTileBytes = 6 * 1024 + 1024 + 128;
-  // the half's bytes of one 64-row tile: three copies (codes, scale chunk, d plane)
-  __device__ __forceinline__ static uint32_t issue(uint8_t* dst, const uint8_t* tile, int h, uint64_t* bar,
-                                                   uint64_t pol) {
-    bulk_g2s_hint(dst, tile + 6 * h * 1024, 6 * 1024, bar, pol);
-    bulk_g2s_hint(dst + 6 * 1024, tile + 12 * 1024, 1024, bar, pol);
-    bulk_g2s_hint(dst + 7 * 1024, tile + HalfTile<QType::Q6_K>::kScaleOff, 128, bar, pol);
-    return kStageTileBytes;
+struct QuarterRegs<QType::Q6_K> {
+  uint32_t w[2][12];  // re-packed codes of sub-blocks 8h + 4g .. + 3 (three words each)
+  uint32_t sc[2];     // their int8 sub-scales
+  float d;
+  __device__ __forceinline__ void load(const uint8_t* tile, int row, int g) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+#pragma unroll
+      for (int c = 0; c < 3; ++c) {
+        const uint4 v = lds128(tile + ((6 * h + 3 * g + c) * kTileRows + row) * 16);
+        w[h][4 * c] = v.x;
+        w[h][4 * c + 1] = v.y;
+        w[h][4 * c + 2] = v.z;
+        w[h][4 * c + 3] = v.w;
+      }
+      sc[h] = *reinterpret_cast<const uint32_t*>(tile + (12 * kTileRows + row) * 16 + 8 * h + 4 * g);
+    }
+    d = f16_to_f32(*reinterpret_cast<const uint16_t*>(tile + HalfTile<QType::Q6_K>::kScaleOff + row * 2));
+  }
+  __device__ __forceinline__ void clear() {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+#pragma unroll
+      for (int i = 0; i < 12; ++i) w[h][i] = 0;
+      sc[h] = 0;
+    }
+    d = 0.f;
   }
   // emit(k0, out[8]): 16 values at K positions k0 .. k0 + 15 of the atom
-  template <typename Emit>
-  __device__ __forceinline__ static void decode(const uint8_t* st, int row, int h, int qq, Emit&& emit) {
-    uint32_t w[12];
-#pragma unroll
-    for (int c = 0; c < 3; ++c) {
-      const uint4 v = lds128(st + ((3 * qq + c) * kTileRows + row) * 16);
-      w[4 * c] = v.x;
-      w[4 * c + 1] = v.y;
-      w[4 * c + 2] = v.z;
-      w[4 * c + 3] = v.w;
-    }
-    const uint32_t sc = *reinterpret_cast<const uint32_t*>(st + 6 * 1024 + row * 16 + 8 * h + 4 * qq);
-    const float d = f16_to_f32(*reinterpret_cast<const uint16_t*>(st + 7 * 1024 + row * 2));
+  template <int h, typename Emit>
+  __device__ __forceinline__ void decode(int g, Emit&& emit) const {
 #pragma unroll
     for (int jj = 0; jj < 4; ++jj) {
-      const float ds = __fmul_rn(d, static_cast<float>(static_cast<int8_t>((sc >> (8 * jj)) & 0xffu)));
-      const uint32_t w0 = w[3 * jj], w1 = w[3 * jj + 1], w2 = w[3 * jj + 2];
+      const float ds = __fmul_rn(d, static_cast<float>(static_cast<int8_t>((sc[h] >> (8 * jj)) & 0xffu)));
+      const uint32_t w0 = w[h][3 * jj], w1 = w[h][3 * jj + 1], w2 = w[h][3 * jj + 2];
       const uint32_t c3 = ((w0 >> 6) & 0x03030303u) | ((w1 >> 4) & 0x0c0c0c0cu) | ((w2 >> 2) & 0x30303030u);
       uint32_t out[8];
       code4<false, false>(w0 & 0x3f3f3f3fu, ds, 32.f, 0.f, out[0], out[1]);
@@ -91,34 +100,44 @@ struct QuarterTile<QType::Q6_K> {
 };
 
 template <>
-struct QuarterTile<QType::Q4_K> {
-  // per tile: the header chunk (d, dmin, packed scales; 1 KB), then the half's 4 code chunks
-  static constexpr int kStageTileBytes = 5 * 1024;
-  __device__ __forceinline__ static uint32_t issue(uint8_t* dst, const uint8_t* tile, int h, uint64_t* bar,
-                                                   uint64_t pol) {
-    bulk_g2s_hint(dst, tile, 1024, bar, pol);
-    bulk_g2s_hint(dst + 1024, tile + (1 + 4 * h) * 1024, 4 * 1024, bar, pol);
-    return kStageTileBytes;
-  }
-  template <typename Emit>
-  __device__ __forceinline__ static void decode(const uint8_t* st, int row, int h, int qq, Emit&& emit) {
-    const uint4 hd = lds128(st + row * 16);
-    const uint32_t hdw[4] = {hd.x, hd.y, hd.z, hd.w};
-    auto scale_byte = [&](int i) { return static_cast<int>((hdw[1 + (i >> 2)] >> (8 * (i & 3))) & 0xffu); };
-    uint32_t w[8];
+struct QuarterRegs<QType::Q4_K> {
+  uint32_t hd[4];     // d | dmin << 16, then the 12 packed scale bytes
+  uint32_t w[2][8];   // quant bytes of sub-blocks 4h + 2g and 4h + 2g + 1 (32 bytes)
+  __device__ __forceinline__ void load(const uint8_t* tile, int row, int g) {
+    const uint4 v = lds128(tile + row * 16);
+    hd[0] = v.x;
+    hd[1] = v.y;
+    hd[2] = v.z;
+    hd[3] = v.w;
 #pragma unroll
-    for (int c = 0; c < 2; ++c) {
-      const uint4 v = lds128(st + 1024 + ((2 * qq + c) * kTileRows + row) * 16);
-      w[4 * c] = v.x;
-      w[4 * c + 1] = v.y;
-      w[4 * c + 2] = v.z;
-      w[4 * c + 3] = v.w;
-    }
-    const float d = f16_to_f32(static_cast<uint16_t>(hdw[0] & 0xffffu));
-    const float dmin = f16_to_f32(static_cast<uint16_t>(hdw[0] >> 16));
+    for (int h = 0; h < 2; ++h)
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const uint4 u = lds128(tile + ((1 + 4 * h + 2 * g + c) * kTileRows + row) * 16);
+        w[h][4 * c] = u.x;
+        w[h][4 * c + 1] = u.y;
+        w[h][4 * c + 2] = u.z;
+        w[h][4 * c + 3] = u.w;
+      }
+  }
+  __device__ __forceinline__ void clear() {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) hd[i] = 0;
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) w[h][i] = 0;
+  }
+  __device__ __forceinline__ int scale_byte(int i) const {
+    return static_cast<int>((hd[1 + (i >> 2)] >> (8 * (i & 3))) & 0xffu);
+  }
+  template <int h, typename Emit>
+  __device__ __forceinline__ void decode(int g, Emit&& emit) const {
+    const float d = f16_to_f32(static_cast<uint16_t>(hd[0] & 0xffffu));
+    const float dmin = f16_to_f32(static_cast<uint16_t>(hd[0] >> 16));
 #pragma unroll
     for (int s = 0; s < 2; ++s) {
-      const int j = 4 * h + 2 * qq + s;  // sub-block of 32 values (gguf_quant.py:118-135)
+      const int j = 4 * h + 2 * g + s;  // sub-block of 32 values (gguf_quant.py:118-135)
       int sc, m;
       if (j < 4) {
         sc = scale_byte(j) & 63;
@@ -134,7 +153,7 @@ struct QuarterTile<QType::Q4_K> {
         uint32_t out[8];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          const uint32_t code = (w[4 * half16 + i] >> (4 * s)) & 0x0f0f0f0fu;
+          const uint32_t code = (w[h][4 * half16 + i] >> (4 * s)) & 0x0f0f0f0fu;
           code4<false, true>(code, ds, 0.f, dm, out[2 * i], out[2 * i + 1]);
         }
         emit(32 * s + 16 * half16, out);
@@ -144,28 +163,42 @@ struct QuarterTile<QType::Q4_K> {
 };
 
 template <>
-struct QuarterTile<QType::Q8_0> {
-  // per tile: the scale chunk (1 KB: 8 FP16 scales per row), then the half's 8 code chunks
-  static constexpr int kStageTileBytes = 9 * 1024;
-  __device__ __forceinline__ static uint32_t issue(uint8_t* dst, const uint8_t* tile, int h, uint64_t* bar,
-                                                   uint64_t pol) {
-    bulk_g2s_hint(dst, tile, 1024, bar, pol);
-    bulk_g2s_hint(dst + 1024, tile + (1 + 8 * h) * 1024, 8 * 1024, bar, pol);
-    return kStageTileBytes;
-  }
-  template <typename Emit>
-  __device__ __forceinline__ static void decode(const uint8_t* st, int row, int h, int qq, Emit&& emit) {
-    const uint32_t dw = *reinterpret_cast<const uint32_t*>(st + row * 16 + 8 * h + 4 * qq);
+struct QuarterRegs<QType::Q8_0> {
+  uint32_t dw[2];      // FP16 scales of GGUF blocks 4h + 2g, 4h + 2g + 1
+  uint32_t w[2][16];   // their 64 codes
+  __device__ __forceinline__ void load(const uint8_t* tile, int row, int g) {
 #pragma unroll
-    for (int s = 0; s < 2; ++s) {  // GGUF block 4h + 2qq + s: 32 values
-      const float d = f16_to_f32(static_cast<uint16_t>(dw >> (16 * s)));
+    for (int h = 0; h < 2; ++h) {
+      dw[h] = *reinterpret_cast<const uint32_t*>(tile + row * 16 + 8 * h + 4 * g);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const uint4 v = lds128(tile + ((1 + 8 * h + 4 * g + c) * kTileRows + row) * 16);
+        w[h][4 * c] = v.x;
+        w[h][4 * c + 1] = v.y;
+        w[h][4 * c + 2] = v.z;
+        w[h][4 * c + 3] = v.w;
+      }
+    }
+  }
+  __device__ __forceinline__ void clear() {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      dw[h] = 0;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) w[h][i] = 0;
+    }
+  }
+  template <int h, typename Emit>
+  __device__ __forceinline__ void decode(int g, Emit&& emit) const {
+#pragma unroll
+    for (int s = 0; s < 2; ++s) {
+      const float d = f16_to_f32(static_cast<uint16_t>(dw[h] >> (16 * s)));
 #pragma unroll
       for (int half16 = 0; half16 < 2; ++half16) {
-        const uint4 v = lds128(st + 1024 + ((4 * qq + 2 * s + half16) * kTileRows + row) * 16);
-        const uint32_t words[4] = {v.x, v.y, v.z, v.w};
         uint32_t out[8];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) code4<false, false>(words[i] ^ 0x80808080u, d, 128.f, 0.f, out[2 * i], out[2 * i + 1]);
+        for (int i = 0; i < 4; ++i)
+          code4<false, false>(w[h][8 * s + 4 * half16 + i] ^ 0x80808080u, d, 128.f, 0.f, out[2 * i], out[2 * i + 1]);
         emit(32 * s + 16 * half16, out);
       }
     }
@@ -174,14 +207,16 @@ struct QuarterTile<QType::Q8_0> {
 
 template <QType QT>
 struct PCfg {
-  static constexpr int kStageBytes = 4 * QuarterTile<QT>::kStageTileBytes;  // one half K block, 4 tiles
-  static constexpr int kRawStages = 2;
+  static constexpr int kTile = HalfTile<QT>::kBytes;   // one 64-row tile of one K block
+  static constexpr int kTileStride = kTile + 64;       // neighbouring tiles on other banks
+  static constexpr int kStageBytes = 4 * kTileStride;  // one K block of the item's 4 tiles
   static constexpr int kBBufs = QT == QType::Q8_0 ? 2 : 3;
   static constexpr size_t kAOff = 0;
   static constexpr size_t kBOff = kAOff + 2 * kPAtomA;
   static constexpr size_t kRawOff = kBOff + static_cast<size_t>(kBBufs) * kPAtomB;
-  static constexpr size_t kBarOff = kRawOff + static_cast<size_t>(kRawStages) * kStageBytes;
-  static constexpr size_t kSmem = 1024 + kBarOff + 256;
+  static constexpr size_t kBarOff = kRawOff + kStageBytes;
+  static constexpr size_t kEpiOff = kBarOff + 256;  // output staging of the 8 epilogue warps
+  static constexpr size_t kSmem = 1024 + kEpiOff + kPEpilogueWarps * 512;
   static_assert(kSmem <= 232448, "shared memory of the prefill form");
 };
 
@@ -204,33 +239,32 @@ __device__ __forceinline__ void umma_ss(uint32_t d_tmem, uint64_t a_desc, uint64
 template <QType QT, int MODE>
 __global__ void __launch_bounds__(kPThreads, 1) umma_prefill_kernel(const UArgs A) {
   using Cfg = PCfg<QT>;
-  using QTile = QuarterTile<QT>;
+  using QR = QuarterRegs<QT>;
   constexpr int NB = Cfg::kBBufs;
-  constexpr int RS = Cfg::kRawStages;
-  constexpr int TB = HalfTile<QT>::kBytes;  // bytes of one 64-row tile of one K block
+  constexpr int TB = Cfg::kTile;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* abuf = smem + Cfg::kAOff;
   uint8_t* bbuf = smem + Cfg::kBOff;
   uint8_t* raw = smem + Cfg::kRawOff;
   uint64_t* raw_full = reinterpret_cast<uint64_t*>(smem + Cfg::kBarOff);
-  uint64_t* raw_empty = raw_full + RS;
-  uint64_t* b_full = raw_empty + RS;
+  uint64_t* raw_empty = raw_full + 1;
+  uint64_t* b_full = raw_empty + 1;
   uint64_t* b_empty = b_full + NB;
   uint64_t* a_full = b_empty + NB;
   uint64_t* a_empty = a_full + 2;
   uint64_t* acc_full = a_empty + 2;
   uint64_t* acc_empty = acc_full + 1;
   uint32_t* tmem_sh = reinterpret_cast<uint32_t*>(acc_empty + 1);
+  // 512 B of output staging per epilogue warp
+  uint16_t* estage = reinterpret_cast<uint16_t*>(smem + Cfg::kEpiOff) + (threadIdx.x / 32 - kPEpilogueWarp0) * 256;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   pdl_trigger();
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < RS; ++s) {
-      mbar_init(&raw_full[s], 1);
-      mbar_init(&raw_empty[s], kPDecodeWarps);  // both decode groups read every raw stage
-    }
+    mbar_init(raw_full, 1);
+    mbar_init(raw_empty, kPDecodeWarps);  // every decode warp loads its registers from each stage
     for (int s = 0; s < NB; ++s) {
       mbar_init(&b_full[s], 1);
       mbar_init(&b_empty[s], 1);
@@ -256,7 +290,7 @@ __global__ void __launch_bounds__(kPThreads, 1) umma_prefill_kernel(const UArgs 
   const bool idle = static_cast<int>(blockIdx.x) >= n_items;
 
   // weight tile w (0..3) of pair p: gate/up -> gate 2p, up 2p, gate 2p+1, up 2p+1;
-  // down -> 4p .. 4p + 3. Returns nullptr when the tile lies past the matrix.
+  // down -> 4p .. 4p + 3. nullptr when the tile lies past the matrix.
   auto tile_ptr = [&](int e, int p, int w, int kb) -> const uint8_t* {
     int rt;
     const uint8_t* base;
@@ -275,41 +309,39 @@ __global__ void __launch_bounds__(kPThreads, 1) umma_prefill_kernel(const UArgs 
   } else if (warp == kPProducerWarp) {
     if (lane == 0) {
       const uint64_t wpol = l2_evict_first_policy(), xpol = l2_evict_last_policy();
-      uint32_t hc = 0, ac = 0;  // half-block stages and atoms issued so far
+      uint32_t kc = 0, ac = 0;  // K-block stages and atoms issued so far
       for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
         const int ci = item / A.items_per_chunk, p = item % A.items_per_chunk;
         const ChunkInfo c = chunk_info<MODE>(A, ci);
         const uint8_t* xsrc = A.xt + c.xrow * 512 * A.nkb;
         const uint32_t xatom = static_cast<uint32_t>(c.r16) * 128u;
-        for (int hs = 0; hs < 2 * A.nkb && ok; ++hs, ++hc) {
-          const int s = hc % RS;
-          if (hc >= RS && !mbar_wait_bounded(&raw_empty[s], ((hc / RS) - 1) & 1)) {
+        for (int kb = 0; kb < A.nkb && ok; ++kb, ++kc) {
+          // the item's 4 weight tiles of this K block: one copy each, once every decode warp
+          // has taken the previous block into its registers
+          if (kc >= 1 && !mbar_wait_bounded(raw_empty, (kc - 1) & 1)) {
             ok = false;
             break;
           }
-          uint8_t* st = raw + static_cast<size_t>(s) * Cfg::kStageBytes;
-          uint32_t bytes = 0;
           const uint8_t* tp[4];
+          uint32_t bytes = 0;
 #pragma unroll
           for (int w = 0; w < 4; ++w) {
-            tp[w] = tile_ptr(c.e, p, w, hs >> 1);
-            if (tp[w]) bytes += QTile::kStageTileBytes;
+            tp[w] = tile_ptr(c.e, p, w, kb);
+            if (tp[w]) bytes += TB;
           }
-          mbar_expect_tx(&raw_full[s], bytes);
+          mbar_expect_tx(raw_full, bytes);
 #pragma unroll
           for (int w = 0; w < 4; ++w)
-            if (tp[w]) QTile::issue(st + w * QTile::kStageTileBytes, tp[w], hs & 1, &raw_full[s], wpol);
-          for (int a2 = 0; a2 < 2; ++a2, ++ac) {
+            if (tp[w]) bulk_g2s_hint(raw + w * Cfg::kTileStride, tp[w], TB, raw_full, wpol);
+          for (int a4 = 0; a4 < 4; ++a4, ++ac) {
             const int bsl = ac % NB;
             if (ac >= NB && !mbar_wait_bounded(&b_empty[bsl], ((ac / NB) - 1) & 1)) {
               ok = false;
               break;
             }
-            const int atom = 2 * hs + a2;  // K atom: block atom >> 2, atom & 3 inside it
             mbar_expect_tx(&b_full[bsl], xatom);
             bulk_g2s_hint(bbuf + static_cast<size_t>(bsl) * kPAtomB,
-                          xsrc + static_cast<int64_t>(atom >> 2) * c.r16 * 512 + (atom & 3) * xatom, xatom,
-                          &b_full[bsl], xpol);
+                          xsrc + static_cast<int64_t>(kb) * c.r16 * 512 + a4 * xatom, xatom, &b_full[bsl], xpol);
           }
         }
       }
@@ -367,10 +399,10 @@ __global__ void __launch_bounds__(kPThreads, 1) umma_prefill_kernel(const UArgs 
       for (int t = 0; t < 2; ++t) {
         const uint32_t tcol = tbase + (static_cast<uint32_t>(32 * q) << 16) + 256u * t;
 #pragma unroll 1
-        for (int c0 = c_lo; c0 < c_hi; c0 += 32) {
-          float acc[32];
+        for (int c0 = c_lo; c0 < c_hi; c0 += 16) {
+          float acc[16];
 #pragma unroll
-          for (int cg = 0; cg < 4; ++cg) {
+          for (int cg = 0; cg < 2; ++cg) {
             uint32_t v[8];
             tmem_ld8(tcol + c0 + 8 * cg, v);
             tmem_wait_ld();
@@ -379,26 +411,25 @@ __global__ void __launch_bounds__(kPThreads, 1) umma_prefill_kernel(const UArgs 
           }
           if (MODE == kModeGateUp) {
             // lane pair (gate row r, up row r) of weight tile pair (2p + t): the even lane writes
-            // the first 16 tokens of the group, the odd lane the last 16
-            const int tt = L & 1, r = L >> 1;
-            const int R = 64 * (2 * p + t) + r;  // row of I
-            uint8_t* hbase = A.ht + c.xrow * 512 * A.nkb_out + static_cast<int64_t>(R >> 8) * c.r16 * 512;
+            // tokens c0 .. c0 + 7 of the group, the odd lane c0 + 8 .. c0 + 15. Every lane works
+            // on its own token at each step (no divergence, eight independent chains).
+            const int R0 = 64 * (2 * p + t) + 16 * q;  // the warp's first row of I
+            uint8_t* hbase = A.ht + c.xrow * 512 * A.nkb_out + static_cast<int64_t>(R0 >> 8) * c.r16 * 512;
+            swiglu_group16(acc, lane, estage, hbase, c.r16, c0, R0 & 255, R0, A.nrows);
+          } else if (!A.yr) {
+            const int R0 = 256 * p + 128 * t + 32 * q;  // the warp's 32 consecutive rows of H
 #pragma unroll
-            for (int col = 0; col < 32; ++col) {
-              const float other = __shfl_xor_sync(0xffffffffu, acc[col], 1);
-              if ((col < 16) == (tt == 0) && R < A.nrows && c0 + col < c.r16) {
-                const float gb = bf16_round(tt == 0 ? acc[col] : other);
-                const float ub = bf16_round(tt == 0 ? other : acc[col]);
-                const float act = bf16_round(__fmul_rn(gb, sigmoid_ref(gb)));  // silu, math.py:19-20
-                *reinterpret_cast<uint16_t*>(hbase + xt_offset(c.r16, c0 + col, R & 255)) =
-                    bf16_bits_rne(__fmul_rn(act, ub));
-              }
+            for (int g8 = 0; g8 < 2; ++g8) {
+              float a8[8];
+#pragma unroll
+              for (int i = 0; i < 8; ++i) a8[i] = acc[8 * g8 + i];
+              store_y8(a8, lane, estage, A.y, c.entry0, c0 + 8 * g8, c.ntok, A.nrows, R0, R0 + 16, false);
             }
           } else {
             const int R = 256 * p + 128 * t + L;  // row of H
             if (R < A.nrows) {
 #pragma unroll
-              for (int col = 0; col < 32; ++col) {
+              for (int col = 0; col < 16; ++col) {
                 if (c0 + col >= c.ntok) break;
                 const int64_t orow = c.entry0 + c0 + col;
                 if (A.yr) A.yr[static_cast<int64_t>(A.entry_route[orow]) * A.nrows + R] = acc[col];
@@ -413,46 +444,43 @@ __global__ void __launch_bounds__(kPThreads, 1) umma_prefill_kernel(const UArgs 
       if (lane == 0) mbar_arrive(acc_empty);
     }
   } else {
-    // ---------------- decode warps: group g takes the atoms with ac % 2 == g ----------------
+    // ---- decode warps: group g takes atoms g and g + 2 of every K block (ac % 2 == g) ----
     const int g = warp >> 3, ar = 32 * (warp & 7) + lane;  // A row 0..255 of the atom
     const int t = ar >> 7, r = ar & 127;                   // MMA tile, row inside it
     // weight tile (0..3 of the item) and its row: gate/up interleave gate and up rows
     const int wt = MODE == kModeGateUp ? 2 * t + (r & 1) : 2 * t + (r >> 6);
     const int wrow = MODE == kModeGateUp ? (r >> 1) : (r & 63);
-    uint32_t ac = 0;
+    uint8_t* dst0 = abuf + g * kPAtomA + t * (kPAtomA / 2);
+    uint32_t kc = 0, ac = static_cast<uint32_t>(g);  // this group's atoms: g, g + 2, g + 4, ...
+    auto store = [&](int k0, const uint32_t(&o)[8]) {
+      *reinterpret_cast<uint4*>(dst0 + a_offset(r, k0)) = make_uint4(o[0], o[1], o[2], o[3]);
+      *reinterpret_cast<uint4*>(dst0 + a_offset(r, k0 + 8)) = make_uint4(o[4], o[5], o[6], o[7]);
+    };
     for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
       const int p = item % A.items_per_chunk;
       const int rt = MODE == kModeGateUp ? 2 * p + (wt >> 1) : 4 * p + wt;
       const bool mine = rt < A.tiles64;
-      for (int at = 0; at < n_atoms; ++at, ++ac) {
-        if ((ac & 1) != static_cast<uint32_t>(g)) continue;
-        const uint32_t hc = ac >> 1;  // the raw stage of atom ac (two atoms per half block)
-        const int s = hc % RS;
-        if (!mbar_wait_bounded(&raw_full[s], (hc / RS) & 1)) {
+      for (int kb = 0; kb < A.nkb && ok; ++kb, ++kc) {
+        if (!mbar_wait_bounded(raw_full, kc & 1)) {
           ok = false;
           break;
         }
-        if (ac >= 2 && !mbar_wait_bounded(&a_empty[g], ((ac >> 1) - 1) & 1)) {
-          ok = false;
-          break;
-        }
-        uint8_t* dst = abuf + g * kPAtomA + t * (kPAtomA / 2);
-        const int hh = (at >> 1) & 1, qq = at & 1;  // half of the K block, quarter of the half
-        if (mine) {
-          const uint8_t* st = raw + static_cast<size_t>(s) * Cfg::kStageBytes + wt * QTile::kStageTileBytes;
-          QTile::decode(st, wrow, hh, qq, [&](int k0, const uint32_t(&o)[8]) {
-            *reinterpret_cast<uint4*>(dst + a_offset(r, k0)) = make_uint4(o[0], o[1], o[2], o[3]);
-            *reinterpret_cast<uint4*>(dst + a_offset(r, k0 + 8)) = make_uint4(o[4], o[5], o[6], o[7]);
-          });
-        } else {
-#pragma unroll
-          for (int k0 = 0; k0 < 64; k0 += 8) *reinterpret_cast<uint4*>(dst + a_offset(r, k0)) = make_uint4(0, 0, 0, 0);
-        }
-        fence_proxy_async_smem();  // the generic-proxy stores must be visible to the MMA
+        QR regs;
+        if (mine) regs.load(raw + wt * Cfg::kTileStride, wrow, g);
+        else regs.clear();
         __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(&raw_empty[s]);
-          mbar_arrive(&a_full[g]);
+        if (lane == 0) mbar_arrive(raw_empty);
+#pragma unroll
+        for (int h = 0; h < 2; ++h, ac += 2) {  // atoms 2h + g of this K block
+          if (ac >= 2 && !mbar_wait_bounded(&a_empty[g], ((ac >> 1) - 1) & 1)) {
+            ok = false;
+            break;
+          }
+          if (h == 0) regs.template decode<0>(g, store);
+          else regs.template decode<1>(g, store);
+          fence_proxy_async_smem();  // the generic-proxy stores must be visible to the MMA
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&a_full[g]);
         }
       }
     }

@@ -102,10 +102,12 @@ struct UCfg {
   // gets the rest: at ~2.7 us loaded HBM latency an SM needs ~130 KB of weights in flight
   // to take its share of the HBM bandwidth, besides the two stages being decoded.
   static constexpr int kXBytes = Form<W>::kXGranules * kXGranule;
-  static constexpr int kWStages = (225 * 1024 - kXBytes) / kWStageBytes;  // narrow 6 (Q6_K), 8 (Q4_K)
+  static constexpr int kWStages = (223 * 1024 - kXBytes) / kWStageBytes;  // narrow 6 (Q6_K), 8 (Q4_K)
   static constexpr size_t kWOff = kXBytes;
   static constexpr size_t kBarOff = kWOff + static_cast<size_t>(kWStages) * kWStageBytes;
-  static constexpr size_t kSmem = 1024 + kBarOff + 512;
+  static constexpr size_t kEpiOff = kBarOff + 512;  // output staging of the 4 epilogue warps
+  static constexpr size_t kSmem = 1024 + kEpiOff + 4 * 512;
+  static_assert(kSmem <= 232448, "shared memory");
 };
 
 struct UArgs {
@@ -212,6 +214,59 @@ __device__ __forceinline__ int item_tiles(const UArgs& A, int e, int p, const ui
   return rt1 < A.tiles64 ? 2 : 1;
 }
 
+// SwiGLU of one 16-token group held by a gate/up lane pair, written as 16-byte chunks of the
+// down pass's activation tiles. Lane `lane` of the warp holds, in acc[i], the accumulator of
+// token first + i for row r = lane >> 1 of the warp's 16 consecutive I rows (K positions
+// k0 .. k0 + 15 of the down pass, k0 a multiple of 16 inside one 256-value block): the gate
+// row on even lanes, the up row on odd ones. The pair exchanges values by shuffle; lane t of
+// the pair computes h = bf16(bf16(silu(bf16 g)) * bf16 u) (experts.py:103-107,
+// math.py:10-20) for tokens 8t .. 8t + 7, all lanes on the same path. The 16 x 16 BF16
+// results pass through `stage` (512 B of this warp's shared memory) so that each lane then
+// stores one 16-byte chunk (8 K positions of one token): wide stores instead of 2-byte ones,
+// which the L2 takes at a fraction of the rate. Rows at or past `rows` (zero-padded tile rows)
+// are not written.
+__device__ __forceinline__ void swiglu_group16(const float (&acc)[16], int lane, uint16_t* stage, uint8_t* hbase,
+                                               int r16, int first, int k0, int row0, int rows) {
+  const int t = lane & 1, r = lane >> 1;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float mine = t == 0 ? acc[j] : acc[8 + j];
+    const float send = t == 0 ? acc[8 + j] : acc[j];
+    const float other = __shfl_xor_sync(0xffffffffu, send, 1);
+    const float gb = bf16_round_hw(t == 0 ? mine : other);
+    const float ub = bf16_round_hw(t == 0 ? other : mine);
+    const float act = bf16_round_hw(__fmul_rn(gb, sigmoid_ref(gb)));
+    stage[(8 * t + j) * 16 + r] = bf16_bits_hw(__fmul_rn(act, ub));
+  }
+  __syncwarp();
+  const int T = lane >> 1, c = lane & 1;
+  const uint4 v = *reinterpret_cast<const uint4*>(stage + T * 16 + 8 * c);
+  if (row0 + 8 * c < rows)
+    *reinterpret_cast<uint4*>(hbase + xt_offset(r16, first + T, k0 + 8 * c)) = v;
+  __syncwarp();
+}
+
+// BF16 y of 8 tokens for the warp's 32 rows, stored as 16-byte chunks of the [entries, rows]
+// output. Lane `lane` holds acc[i] = the FP32 result of token first + i for its row
+// rowbase[lane] (two runs of 16 consecutive rows: lanes 2i -> run 0 row i, 2i + 1 -> run 1
+// row i when `interleaved`; otherwise one run of 32 rows, lane i -> row i). `stage` is 512 B
+// of this warp's shared memory. Tokens at or past ntok are not written.
+__device__ __forceinline__ void store_y8(const float (&acc)[8], int lane, uint16_t* stage, uint16_t* y, int64_t entry0,
+                                         int first, int ntok, int nrows, int row_a, int row_b, bool interleaved) {
+  // position of this lane's row inside the 32-row staging line: run 0 then run 1
+  const int pos = interleaved ? ((lane & 1) * 16 + (lane >> 1)) : lane;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) stage[j * 32 + pos] = bf16_bits_hw(acc[j]);
+  __syncwarp();
+  const int T = lane >> 2, part = lane & 3;  // token, 8-row piece of its 32 rows
+  const int row = part < 2 ? row_a + 8 * part : row_b + 8 * (part - 2);
+  if (first + T < ntok && row < nrows) {
+    const uint4 v = *reinterpret_cast<const uint4*>(stage + T * 32 + 8 * part);
+    *reinterpret_cast<uint4*>(y + (entry0 + first + T) * nrows + row) = v;
+  }
+  __syncwarp();
+}
+
 template <QType QT, int MODE, bool W = false>
 __global__ void __launch_bounds__(Form<W>::kThreads, 1) umma_proj_kernel(const UArgs A) {
   using Cfg = UCfg<QT, W>;
@@ -239,6 +294,8 @@ __global__ void __launch_bounds__(Form<W>::kThreads, 1) umma_proj_kernel(const U
   uint64_t* dempty = dfull + DB;
   volatile uint32_t* xoff = reinterpret_cast<volatile uint32_t*>(dempty + DB);  // [kXSlots] granule of each stage
   uint32_t* tmem_sh = const_cast<uint32_t*>(xoff + kXSlots);
+  // 512 B of output staging per epilogue warp
+  uint16_t* estage = reinterpret_cast<uint16_t*>(smem + Cfg::kEpiOff) + (threadIdx.x / 32 - EW0) * 256;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   pdl_trigger();  // the next pass may be launched now; its CTAs start as these ones leave
@@ -404,23 +461,32 @@ __global__ void __launch_bounds__(Form<W>::kThreads, 1) umma_proj_kernel(const U
           if (lane == 0) mbar_arrive(&dempty[d]);
         }
         if (MODE == kModeGateUp) {
-          // lane pair (gate row r, up row r): the even lane takes the first half of the
-          // group's token columns, the odd lane the second; each gets its partner's value by
-          // shuffle.
-          const int R = 64 * it.p + r;  // row of I = K index of the down pass
-          uint8_t* hbase = A.ht + c.xrow * 512 * A.nkb_out + static_cast<int64_t>(R >> 8) * c.r16 * 512;
-          const int half = gcols >> 1;
+          // lane pair (gate row r, up row r): in each group of 16 token columns the even lane
+          // writes the first 8, the odd lane the last 8, every lane on its own token at each
+          // step (no divergence); each gets its partner's value by shuffle. Rows past I are
+          // zero-padded tile rows and are not written.
+          const int R0 = 64 * it.p + 16 * q;  // the warp's first row of I = K index of the down pass
+          uint8_t* hbase = A.ht + c.xrow * 512 * A.nkb_out + static_cast<int64_t>(R0 >> 8) * c.r16 * 512;
+          float lo[16];
 #pragma unroll
-          for (int col = 0; col < 32; ++col) {
-            if (col >= gcols) break;
-            const float other = __shfl_xor_sync(0xffffffffu, acc[col], 1);
-            if ((col < half) == (t == 0) && R < A.nrows) {  // rows past I: zero-padded tile rows
-              const float gb = bf16_round(t == 0 ? acc[col] : other);
-              const float ub = bf16_round(t == 0 ? other : acc[col]);
-              const float act = bf16_round(__fmul_rn(gb, sigmoid_ref(gb)));  // silu, math.py:19-20
-              *reinterpret_cast<uint16_t*>(hbase + xt_offset(c.r16, c0 + col, R & 255)) =
-                  bf16_bits_rne(__fmul_rn(act, ub));
-            }
+          for (int i = 0; i < 16; ++i) lo[i] = acc[i];
+          swiglu_group16(lo, lane, estage, hbase, c.r16, c0, R0 & 255, R0, A.nrows);
+          if (gcols > 16) {
+            float hi[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) hi[i] = acc[16 + i];
+            swiglu_group16(hi, lane, estage, hbase, c.r16, c0 + 16, R0 & 255, R0, A.nrows);
+          }
+        } else if (MODE == kModeDown && !A.yr) {
+          // rows 128p + 16q + i (even lanes) and 128p + 64 + 16q + i (odd lanes), 8 tokens at a time
+          const int ra = 128 * it.p + 16 * q, rb = ra + 64;
+#pragma unroll
+          for (int g8 = 0; g8 < 4; ++g8) {
+            if (8 * g8 >= gcols) break;
+            float a8[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) a8[i] = acc[8 * g8 + i];
+            store_y8(a8, lane, estage, A.y, c.entry0, c0 + 8 * g8, c.ntok, A.nrows, ra, rb, true);
           }
         } else {
           const int R = 128 * it.p + 64 * t + r;
@@ -495,337 +561,6 @@ __global__ void __launch_bounds__(Form<W>::kThreads, 1) umma_proj_kernel(const U
     tc_fence_after();
     tmem_dealloc(tbase, kTmemCols);
   }
-}
-
-// ---------------------------------------------------------------------------------------
-// The narrow MoE passes with two K blocks per copy (umma_pair_kernel).
-//
-// A 1-D bulk copy costs its SM about 0.3 us whatever its size up to ~16 KB (measured on
-// B200: 8 KB copies stream at 26 GB/s per SM, 13 KB ones at 43 GB/s, 27 KB ones at the
-// ~48 GB/s per-SM ceiling), so one copy per 64-row tile per K block (plus one per activation
-// tile) leaves the SM's copy queue, not HBM, as the bound. Here a weight stage holds two
-// consecutive K blocks of both tiles (each tile's two blocks are contiguous in the tiled
-// layout: one copy per tile) and the activation tiles of the same two blocks arrive in one
-// copy too: three copies per two K blocks instead of six. Decode and MMA still work per K
-// block: the first block of a stage goes to decode group 0, the second to group 1; a stage
-// with one block (an odd count of K blocks) is released by group 1 without decoding. Items
-// start at a pair of K blocks that depends on their MMA tile (even block counts), so the
-// items of one chunk do not all read the same activation tiles at once.
-template <QType QT>
-struct UPCfg {
-  static constexpr int kTile = HalfTile<QT>::kBytes;
-  static constexpr int kPairTile = 2 * kTile;                        // one tile, two K blocks
-  static constexpr int kTile1 = (kPairTile + 127) / 128 * 128 + 64;  // second tile: other banks
-  static constexpr int kWStageBytes = (kTile1 + kPairTile + 127) / 128 * 128;
-  static constexpr int kXBytes = Form<false>::kXGranules * kXGranule;
-  static constexpr int kWStages = (225 * 1024 - kXBytes) / kWStageBytes;  // 3 (Q6_K), 4 (Q4_K), 2 (Q8_0)
-  static constexpr size_t kWOff = kXBytes;
-  static constexpr size_t kBarOff = kWOff + static_cast<size_t>(kWStages) * kWStageBytes;
-  static constexpr size_t kSmem = 1024 + kBarOff + 512;
-  static_assert(kWStages >= 2, "weight ring");
-};
-
-// K block pair jp of an item with n K blocks: first block (relative to kb0) and block count.
-__device__ __forceinline__ int2 pair_blocks(int n, int p, int jp) {
-  const int npairs = (n + 1) >> 1;
-  const int j = (n & 1) ? jp : (jp + p) % npairs;
-  return make_int2(2 * j, min(2, n - 2 * j));
-}
-
-template <QType QT, int MODE>
-__global__ void __launch_bounds__(kUmmaThreads, 1) umma_pair_kernel(const UArgs A) {
-  static_assert(MODE == kModeGateUp || MODE == kModeDown, "MoE passes only");
-  using Cfg = UPCfg<QT>;
-  using HT = HalfTile<QT>;
-  constexpr int SW = Cfg::kWStages;
-  constexpr int NI = kMmaIssuers;
-  constexpr int TOK = kMaxTok;
-  constexpr int XG = Form<false>::kXGranules;
-  constexpr int EW0 = Form<false>::kEpilogueWarp0;
-  constexpr int AB = kABuffers;
-  constexpr int DB = kDBuffers;
-  constexpr uint32_t kAccCol = Form<false>::kAccCol;
-  constexpr int TB = Cfg::kTile;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* xring = smem;
-  uint8_t* wring = smem + Cfg::kWOff;
-  uint64_t* wfull = reinterpret_cast<uint64_t*>(smem + Cfg::kBarOff);
-  uint64_t* wempty = wfull + SW;
-  uint64_t* xfull = wempty + SW;
-  uint64_t* xempty = xfull + kXSlots;
-  uint64_t* afull = xempty + kXSlots;
-  uint64_t* aempty = afull + AB;
-  uint64_t* dfull = aempty + AB;
-  uint64_t* dempty = dfull + DB;
-  volatile uint32_t* xoff = reinterpret_cast<volatile uint32_t*>(dempty + DB);  // [kXSlots] granule of each pair
-  uint32_t* tmem_sh = const_cast<uint32_t*>(xoff + kXSlots);
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  pdl_trigger();
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < SW; ++s) {
-      mbar_init(&wfull[s], 1);
-      mbar_init(&wempty[s], kDecodeWarps);  // both decode groups read every weight stage
-    }
-    for (int s = 0; s < kXSlots; ++s) {
-      mbar_init(&xfull[s], 1);
-      mbar_init(&xempty[s], NI);
-    }
-    for (int i = 0; i < AB; ++i) {
-      mbar_init(&afull[i], kDecodeWarps / 2);
-      mbar_init(&aempty[i], NI);
-    }
-    for (int i = 0; i < DB; ++i) {
-      mbar_init(&dfull[i], NI);
-      mbar_init(&dempty[i], 4);
-    }
-    fence_mbar_init();
-  }
-  if (warp == 0) tmem_alloc(tmem_sh, kTmemCols);
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tbase = *tmem_sh;
-  pdl_wait();
-  const int n_chunks = *A.n_chunks_p;
-  const int n_items = n_chunks * A.items_per_chunk;
-  const int n = A.nkb;                  // K blocks per item
-  const int npairs = (n + 1) >> 1;
-  bool ok = true;
-  const bool idle = static_cast<int>(blockIdx.x) >= n_items;
-
-  if (idle) {
-  } else if (warp == kProducerWarp) {
-    if (lane == 0) {
-      const uint64_t wpol = l2_evict_first_policy(), xpol = l2_evict_last_policy();
-      uint32_t ps = 0;                          // weight / activation pair stages issued
-      uint32_t xlo = 0, xused = 0, xhead = 0;  // granule ring: oldest live pair, granules held,
-      uint64_t xcnt = 0;                       // next free granule, 8-bit counts per pair slot
-      for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
-        const ItemInfo it = item_info(A, item);
-        const ChunkInfo c = chunk_info<MODE>(A, it.ci);
-        const uint8_t *w0, *w1;
-        int rt0, rt1;
-        const int nt = item_tiles<MODE>(A, c.e, it.p, w0, w1, rt0, rt1);
-        const uint32_t g = static_cast<uint32_t>(c.r16) / 16;  // granules per activation tile
-        const uint32_t xbytes = g * kXGranule;
-        const uint8_t* xsrc = A.xt + c.xrow * 512 * A.nkb;
-        for (int jp = 0; jp < npairs && ok; ++jp, ++ps) {
-          const int2 pb = pair_blocks(n, it.p, jp);
-          const int kb = pb.x;
-          const uint32_t gg = g * static_cast<uint32_t>(pb.y);
-          const uint32_t off = xhead + gg > XG ? 0u : xhead;
-          const uint32_t need = gg + (off == 0u && xhead != 0u ? XG - xhead : 0u);
-          while (xused + need > XG || ps - xlo >= kXSlots) {
-            if (!mbar_wait_bounded(&xempty[xlo % kXSlots], (xlo / kXSlots) & 1)) {
-              ok = false;
-              break;
-            }
-            xused -= static_cast<uint32_t>(xcnt >> (8 * (xlo % kXSlots))) & 255u;
-            ++xlo;
-          }
-          const int s = ps % SW;
-          if (!ok || (ps >= SW && !mbar_wait_bounded(&wempty[s], ((ps / SW) - 1) & 1))) {
-            ok = false;
-            break;
-          }
-          const uint32_t j = ps % kXSlots;
-          xcnt = (xcnt & ~(uint64_t{255} << (8 * j))) | (static_cast<uint64_t>(need) << (8 * j));
-          xused += need;
-          xhead = (off + gg) % XG;
-          xoff[j] = off;
-          mbar_expect_tx(&xfull[j], xbytes * pb.y);
-          bulk_g2s_hint(xring + off * kXGranule, xsrc + static_cast<int64_t>(kb) * xbytes, xbytes * pb.y, &xfull[j],
-                        xpol);
-          uint8_t* st = wring + static_cast<size_t>(s) * Cfg::kWStageBytes;
-          mbar_expect_tx(&wfull[s], static_cast<uint32_t>(TB * pb.y * nt));
-          bulk_g2s_hint(st, w0 + (static_cast<int64_t>(rt0) * A.nkb + kb) * TB, TB * pb.y, &wfull[s], wpol);
-          if (nt == 2)
-            bulk_g2s_hint(st + Cfg::kTile1, w1 + (static_cast<int64_t>(rt1) * A.nkb + kb) * TB, TB * pb.y, &wfull[s],
-                          wpol);
-        }
-      }
-    }
-  } else if (warp >= kMmaWarp0 && warp < EW0) {
-    if (lane == 0) {
-      const uint32_t mi = static_cast<uint32_t>(warp - kMmaWarp0);
-      uint32_t sc = 0, ps = 0, ic = 0;
-      for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
-        const ItemInfo it = item_info(A, item);
-        const ChunkInfo c = chunk_info<MODE>(A, it.ci);
-        const uint32_t idesc = idesc_bf16_m128(static_cast<uint32_t>(c.r16));
-        const uint32_t atom = static_cast<uint32_t>(c.r16 >> 3) * 1024u;  // bytes per 64-value K atom
-        const uint32_t g = static_cast<uint32_t>(c.r16) / 16;
-        const uint32_t d = ic % DB;
-        const uint32_t dcol = tbase + kAccCol + (d * NI + mi) * TOK;
-        if (ic >= DB && !mbar_wait_bounded(&dempty[d], ((ic / DB) - 1) & 1)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        int i = 0;  // K blocks of the item so far
-        for (int jp = 0; jp < npairs && ok; ++jp, ++ps) {
-          const int nb = pair_blocks(n, it.p, jp).y;
-          const uint32_t j = ps % kXSlots;
-          if (!mbar_wait_bounded(&xfull[j], (ps / kXSlots) & 1)) {
-            ok = false;
-            break;
-          }
-          for (int bi = 0; bi < nb; ++bi, ++sc, ++i) {
-            const uint32_t b = sc % AB;
-            if (!mbar_wait_bounded(&afull[b], (sc / AB) & 1)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-            constexpr int kSteps = 16 / NI;
-            const uint32_t xs = smem_addr(xring + (xoff[j] + bi * g) * kXGranule);
-            const uint64_t bd = sdesc_sw128(xs + (mi * kSteps / 4) * atom, 1024u);
-            const uint32_t acol = tbase + b * 128 + mi * kSteps * 8;
-#pragma unroll
-            for (int ks = 0; ks < kSteps; ++ks)
-              umma_ts(dcol, acol + ks * 8, bd + (((ks >> 2) * atom) >> 4) + (ks & 3) * 2, idesc, (i != 0) || (ks != 0));
-            umma_commit(&aempty[b]);
-          }
-          if (ok) umma_commit(&xempty[j]);
-        }
-        if (!ok) break;
-        umma_commit(&dfull[d]);
-        ++ic;
-      }
-    }
-  } else if (warp >= EW0) {
-    const int q = warp & 3, L = 32 * q + lane;
-    uint32_t ic = 0;
-    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++ic) {
-      const ItemInfo it = item_info(A, item);
-      const ChunkInfo c = chunk_info<MODE>(A, it.ci);
-      const uint32_t d = ic % DB;
-      if (!mbar_wait_bounded(&dfull[d], (ic / DB) & 1)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      const uint32_t dcol = tbase + (static_cast<uint32_t>(32 * q) << 16) + kAccCol + d * NI * TOK;
-      const int t = L & 1, r = L >> 1;
-      const int gcols = c.r16;  // <= 32, a multiple of 16
-      float acc[32];
-#pragma unroll
-      for (int cg = 0; cg < 4; ++cg) {
-        if (8 * cg >= gcols) break;
-        uint32_t v[NI][8];
-#pragma unroll
-        for (int ii = 0; ii < NI; ++ii) tmem_ld8(dcol + ii * TOK + 8 * cg, v[ii]);
-        tmem_wait_ld();
-#pragma unroll
-        for (int jj = 0; jj < 8; ++jj) {
-          float a = __uint_as_float(v[0][jj]);
-#pragma unroll
-          for (int ii = 1; ii < NI; ++ii) a = __fadd_rn(a, __uint_as_float(v[ii][jj]));
-          acc[8 * cg + jj] = a;
-        }
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&dempty[d]);
-      if (MODE == kModeGateUp) {
-        const int R = 64 * it.p + r;
-        uint8_t* hbase = A.ht + c.xrow * 512 * A.nkb_out + static_cast<int64_t>(R >> 8) * c.r16 * 512;
-        const int half = gcols >> 1;
-#pragma unroll
-        for (int col = 0; col < 32; ++col) {
-          if (col >= gcols) break;
-          const float other = __shfl_xor_sync(0xffffffffu, acc[col], 1);
-          if ((col < half) == (t == 0) && R < A.nrows) {
-            const float gb = bf16_round(t == 0 ? acc[col] : other);
-            const float ub = bf16_round(t == 0 ? other : acc[col]);
-            const float act = bf16_round(__fmul_rn(gb, sigmoid_ref(gb)));  // silu, math.py:19-20
-            *reinterpret_cast<uint16_t*>(hbase + xt_offset(c.r16, col, R & 255)) = bf16_bits_rne(__fmul_rn(act, ub));
-          }
-        }
-      } else {
-        const int R = 128 * it.p + 64 * t + r;
-        if (R < A.nrows) {
-#pragma unroll
-          for (int col = 0; col < 32; ++col) {
-            if (col >= c.ntok) break;
-            const int64_t orow = c.entry0 + col;
-            if (A.yr) A.yr[static_cast<int64_t>(A.entry_route[orow]) * A.nrows + R] = acc[col];
-            else A.y[orow * A.nrows + R] = bf16_bits_rne(acc[col]);
-          }
-        }
-      }
-    }
-  } else {
-    // ---------------- decode warps: group g takes block g of every pair stage ----------------
-    const int g = warp >> 3, q = warp & 3, L = 32 * q + lane;
-    const int t = L & 1, r = L >> 1;
-    auto run = [&](auto hc) {
-      constexpr int h = decltype(hc)::value;
-      uint32_t sc = 0, ps = 0;
-      for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
-        const ItemInfo it = item_info(A, item);
-        const bool mine = MODE == kModeGateUp || t == 0 || 2 * it.p + 1 < A.tiles64;
-        for (int jp = 0; jp < npairs && ok; ++jp, ++ps) {
-          const int nb = pair_blocks(n, it.p, jp).y;
-          const int s = ps % SW;
-          const uint32_t bsc = sc + g;  // the K block this group decodes in this stage
-          sc += nb;
-          if (!mbar_wait_bounded(&wfull[s], (ps / SW) & 1)) {
-            ok = false;
-            break;
-          }
-          if (g >= nb) {  // a one-block stage: group 1 only releases it
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&wempty[s]);
-            continue;
-          }
-          typename HT::Regs regs;
-          if (mine)
-            HT::template load<h>(regs, wring + static_cast<size_t>(s) * Cfg::kWStageBytes + t * Cfg::kTile1 + g * TB, r);
-          else
-            HT::clear(regs);
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&wempty[s]);
-          const uint32_t b = bsc % AB;
-          if (bsc >= AB && !mbar_wait_bounded(&aempty[b], ((bsc / AB) - 1) & 1)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t col0 = tbase + (static_cast<uint32_t>(32 * q) << 16) + b * 128 + h * 64;
-          HT::template decode<false, h>(regs, [&](int col, const uint32_t(&o)[8]) { tmem_st8(col0 + col, o); });
-          tmem_wait_st();
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&afull[b]);
-        }
-      }
-    };
-    if (((warp >> 2) & 1) == 0) run(std::integral_constant<int, 0>{});
-    else run(std::integral_constant<int, 1>{});
-  }
-
-  if (!ok && lane == 0 && A.status) atomicExch(A.status, QK_ERR_TIMEOUT);
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 0) {
-    tc_fence_after();
-    tmem_dealloc(tbase, kTmemCols);
-  }
-}
-
-template <QType QT, int MODE>
-int launch_pair(const UArgs& A, int grid, cudaStream_t st) {
-  using Cfg = UPCfg<QT>;
-  int rc = allow_smem(reinterpret_cast<const void*>(umma_pair_kernel<QT, MODE>), Cfg::kSmem);
-  if (rc) return rc;
-  const cudaError_t e = launch_dependent(umma_pair_kernel<QT, MODE>, dim3(grid), dim3(kUmmaThreads), Cfg::kSmem, st, A);
-  if (e != cudaSuccess) return cuda_error(e, "umma_pair_kernel");
-  count_launch(1);
-  return QK_OK;
 }
 
 template <QType QT, int MODE, bool W = false>
