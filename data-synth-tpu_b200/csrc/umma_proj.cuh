@@ -55,6 +55,15 @@ namespace qk {
 #ifndef QK_UMMA_DBUF
 #define QK_UMMA_DBUF 1
 #endif
+// Decode order: 0 = load a stage's codes into registers, release the weight slot, then wait
+// for the A buffer and decode; 1 = wait for the A buffer, then load and decode in one
+// stretch and release the slot after the decode.
+#ifndef QK_LATE_RELEASE
+#define QK_LATE_RELEASE 0
+#endif
+#ifndef QK_TMEM_ST32
+#define QK_TMEM_ST32 1
+#endif
 constexpr int kDecodeWarps = 16;
 constexpr int kProducerWarp = 16;
 constexpr int kMmaWarp0 = 17;
@@ -516,6 +525,9 @@ __global__ void __launch_bounds__(Form<W>::kThreads, 1) umma_proj_kernel(const U
     auto run = [&](auto hc) {
       constexpr int h = decltype(hc)::value;
       uint32_t sc = 0;
+#ifdef QK_STAGGER_NS
+      if (g == 1) __nanosleep(QK_STAGGER_NS);  // start the second decode group half a stage later
+#endif
       for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
         // The decode needs no chunk metadata: only whether its tile exists.
         const ItemInfo it = item_info(A, item);
@@ -530,23 +542,54 @@ __global__ void __launch_bounds__(Form<W>::kThreads, 1) umma_proj_kernel(const U
           // Lanes of a missing second tile (odd lanes when the matrix ends inside the MMA
           // tile) decode zeros: tcgen05.st / wait::st are warp-collective, so every lane
           // of the warp must run them.
-          typename HT::Regs regs;
-          if (mine) HT::template load<h>(regs, wring + static_cast<size_t>(s) * Cfg::kWStageBytes + t * Cfg::kTile1, r);
-          else HT::clear(regs);
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&wempty[s]);
           const uint32_t b = sc % AB;
+#if QK_LATE_RELEASE
+          // wait for the A buffer first, then load and decode in one stretch (the shared-memory
+          // loads of later sub-blocks overlap the decode of earlier ones); the weight slot is
+          // released after the decode
           if (sc >= AB && !mbar_wait_bounded(&aempty[b], ((sc / AB) - 1) & 1)) {
             ok = false;
             break;
           }
           tc_fence_after();
+          typename HT::Regs regs;
+          if (mine) HT::template load<h>(regs, wring + static_cast<size_t>(s) * Cfg::kWStageBytes + t * Cfg::kTile1, r);
+          else HT::clear(regs);
+#else
+          typename HT::Regs regs;
+          if (mine) HT::template load<h>(regs, wring + static_cast<size_t>(s) * Cfg::kWStageBytes + t * Cfg::kTile1, r);
+          else HT::clear(regs);
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&wempty[s]);
+          if (sc >= AB && !mbar_wait_bounded(&aempty[b], ((sc / AB) - 1) & 1)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+#endif
           const uint32_t col0 = tbase + (static_cast<uint32_t>(32 * q) << 16) + b * 128 + h * 64;
+#if QK_TMEM_ST32
+          // 32 columns per TMEM store: four decode steps land in distinct registers, and one
+          // tcgen05.st takes them (the registers of an 8-column store are not free for the next
+          // step's results until the store has read them)
+          uint32_t sbuf[32];
+          HT::template decode<false, h>(regs, [&](int col, const uint32_t(&o)[8]) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) sbuf[(col & 31) + i] = o[i];
+            if ((col & 31) == 24) tmem_st32(col0 + (col & ~31), sbuf);
+          });
+#else
           HT::template decode<false, h>(regs, [&](int col, const uint32_t(&o)[8]) { tmem_st8(col0 + col, o); });
+#endif
           tmem_wait_st();
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&afull[b]);
+          if (lane == 0) {
+#if QK_LATE_RELEASE
+            mbar_arrive(&wempty[s]);
+#endif
+            mbar_arrive(&afull[b]);
+          }
         }
       }
     };
