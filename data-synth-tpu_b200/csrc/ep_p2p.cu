@@ -35,7 +35,7 @@
 namespace qk {
 namespace {
 
-__global__ void __launch_bounds__(256) ep_dispatch_kernel(uint8_t* const* __restrict__ peers, uint8_t* own, EpLayout L,
+__global__ void __launch_bounds__(512) ep_dispatch_kernel(uint8_t* const* __restrict__ peers, uint8_t* own, EpLayout L,
                                                           int rank, int experts_per_rank,
                                                           const uint16_t* __restrict__ x,
                                                           const int32_t* __restrict__ ids,
@@ -65,9 +65,19 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(uint8_t* const* __rest
       reinterpret_cast<uint16_t*>(pb + L.recv_w)[slot * k + lane] = wt;
     }
     if (routed) {
+      // the row's 16-byte pieces, eight per lane in flight before they are stored
+      constexpr int kU = 8;
       const uint4* src = reinterpret_cast<const uint4*>(x + static_cast<int64_t>(b) * H);
       uint4* dstp = reinterpret_cast<uint4*>(pb + L.recv_x + slot * H * 2);
-      for (int c = lane; c < H / 8; c += 32) dstp[c] = ld_nc_v4(src + c);
+      for (int c0 = lane; c0 < H / 8; c0 += 32 * kU) {
+        uint4 v[kU];
+#pragma unroll
+        for (int u = 0; u < kU; ++u)
+          if (c0 + 32 * u < H / 8) v[u] = ld_nc_v4(src + c0 + 32 * u);
+#pragma unroll
+        for (int u = 0; u < kU; ++u)
+          if (c0 + 32 * u < H / 8) dstp[c0 + 32 * u] = v[u];
+      }
     }
   }
   if (ep_last_cta(&ctrl->dispatch_arrivals)) {
@@ -179,10 +189,10 @@ int qk_ep_p2p_dispatch(void* const* peers, void* region, int world, int rank, in
   QK_REQUIRE(B == 0 || (x && ids && weights), "null pointer");
   const EpLayout L = ep_layout(world, max_tokens, hidden, top_k);
   const int64_t warps = static_cast<int64_t>(world) * max_tokens;
-  int64_t grid = (warps + 7) / 8;
-  const int64_t cap = static_cast<int64_t>(sm_count()) * 8;
+  int64_t grid = (warps + 15) / 16;
+  const int64_t cap = static_cast<int64_t>(sm_count());  // few CTAs: one system-scope fence each
   if (grid > cap) grid = cap;
-  const cudaError_t e = launch_dependent(ep_dispatch_kernel, dim3(static_cast<unsigned>(grid)), dim3(256), 0,
+  const cudaError_t e = launch_dependent(ep_dispatch_kernel, dim3(static_cast<unsigned>(grid)), dim3(512), 0,
                                          as_stream(stream), reinterpret_cast<uint8_t* const*>(peers),
                                          static_cast<uint8_t*>(region), L, rank, experts_per_rank, x, ids, weights, B);
   if (e != cudaSuccess) return cuda_error(e, "ep_dispatch_kernel");

@@ -408,7 +408,7 @@ __global__ void cast_kernel(const float* __restrict__ in, uint16_t* __restrict__
 // entries in ascending expert order, stored straight into the source's region at
 // ret[this rank][b] (over NVLink for another rank). Unsent slots are not written. The last
 // CTA raises ret_flag[this rank] in every source's region.
-__global__ void __launch_bounds__(256) moe_combine_push_kernel(const int32_t* __restrict__ ids, int Bp, int k, int H,
+__global__ void __launch_bounds__(512) moe_combine_push_kernel(const int32_t* __restrict__ ids, int Bp, int k, int H,
                                                                Workspace ws, uint8_t* const* __restrict__ peers,
                                                                uint8_t* own, EpLayout L, int rank) {
   pdl_wait();
@@ -416,42 +416,63 @@ __global__ void __launch_bounds__(256) moe_combine_push_kernel(const int32_t* __
   const uint32_t epoch = ctrl->epoch;
   const int lane = threadIdx.x & 31;
   const int blocks = H / 256;
-  const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  if (gw < Bp * blocks) {
-    const int b = gw / blocks, c0 = (gw - b * blocks) * 256 + lane * 8;
+  const int nwarps = gridDim.x * (blockDim.x >> 5);
+  // One CTA per SM walks all received slots, a warp per slot: the system-scope fence and the
+  // arrival at the end of the kernel cost about as much per CTA as a slot's work, so the grid
+  // is kept small. A warp reads the slot's route metadata once; then, per entry, its lanes
+  // load all their 256-column pieces of the y row at once, so the loads are in flight
+  // together before the FP32 partial is stored into the source's region.
+  constexpr int kSplit = 1;  // warps per slot
+  for (int gwi = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); gwi < Bp * kSplit; gwi += nwarps) {
+    const int b = gwi / kSplit, part = gwi - b * kSplit;
+    const int cb_lo = blocks * part / kSplit, cb_hi = blocks * (part + 1) / kSplit;
     const int id = lane < k ? ids[b * k + lane] : -1;
-    if (__any_sync(0xffffffffu, id >= 0)) {
-      const int entry = lane < k ? ws.route_entry[b * k + lane] : -1;
-      const int eid = entry >= 0 ? id : 0x7fffffff;
-      const float w = entry >= 0 ? ws.entry_weight[entry] : 0.f;
-      int rank_in = 0, n = 0;
-      for (int j = 0; j < k; ++j) {
-        const int ej = __shfl_sync(0xffffffffu, eid, j);
-        const int vj = __shfl_sync(0xffffffffu, entry, j) >= 0;
-        n += vj;
-        rank_in += vj && (ej < eid);
-      }
-      float acc[8];
+    if (!__any_sync(0xffffffffu, id >= 0)) continue;
+    const int entry = lane < k ? ws.route_entry[b * k + lane] : -1;
+    const int eid = entry >= 0 ? id : 0x7fffffff;
+    const float w = entry >= 0 ? ws.entry_weight[entry] : 0.f;
+    int rank_in = 0, n = 0;
+    for (int j = 0; j < k; ++j) {
+      const int ej = __shfl_sync(0xffffffffu, eid, j);
+      const int vj = __shfl_sync(0xffffffffu, entry, j) >= 0;
+      n += vj;
+      rank_in += vj && (ej < eid);
+    }
+    const int src_rank = b / L.max_tokens, tok = b - src_rank * L.max_tokens;
+    float* dst = reinterpret_cast<float*>(peers[src_rank] + L.ret) + (static_cast<size_t>(rank) * L.max_tokens + tok) * H;
+    for (int cb0 = cb_lo; cb0 < cb_hi; cb0 += 8) {  // up to 8 pieces of 256 columns at a time
+      float acc[8][8];
 #pragma unroll
-      for (int t = 0; t < 8; ++t) acc[t] = 0.f;
+      for (int cc = 0; cc < 8; ++cc)
+#pragma unroll
+        for (int t = 0; t < 8; ++t) acc[cc][t] = 0.f;
       for (int i = 0; i < n; ++i) {
         const unsigned who = __ballot_sync(0xffffffffu, entry >= 0 && rank_in == i);
         const int src = __ffs(who) - 1;
         const int ent = __shfl_sync(0xffffffffu, entry, src);
         const float wi = __shfl_sync(0xffffffffu, w, src);
-        const uint4 v = ld_nc_v4(ws.y + static_cast<int64_t>(ent) * H + c0);
-        const uint32_t p[4] = {v.x, v.y, v.z, v.w};
+        uint4 v[8];
 #pragma unroll
-        for (int t = 0; t < 8; ++t) {
-          const float y = bf16_to_f32(static_cast<uint16_t>(p[t >> 1] >> (16 * (t & 1))));
-          acc[t] = __fadd_rn(acc[t], __fmul_rn(y, wi));
+        for (int cc = 0; cc < 8; ++cc)
+          if (cb0 + cc < cb_hi) v[cc] = ld_nc_v4(ws.y + static_cast<int64_t>(ent) * H + (cb0 + cc) * 256 + lane * 8);
+#pragma unroll
+        for (int cc = 0; cc < 8; ++cc) {
+          if (cb0 + cc >= cb_hi) break;
+          const uint32_t p[4] = {v[cc].x, v[cc].y, v[cc].z, v[cc].w};
+#pragma unroll
+          for (int t = 0; t < 8; ++t) {
+            const float y = bf16_to_f32(static_cast<uint16_t>(p[t >> 1] >> (16 * (t & 1))));
+            acc[cc][t] = __fadd_rn(acc[cc][t], __fmul_rn(y, wi));
+          }
         }
       }
-      const int src_rank = b / L.max_tokens, tok = b - src_rank * L.max_tokens;
-      float* dst = reinterpret_cast<float*>(peers[src_rank] + L.ret) +
-                   (static_cast<size_t>(rank) * L.max_tokens + tok) * H + c0;
-      reinterpret_cast<float4*>(dst)[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
-      reinterpret_cast<float4*>(dst)[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+#pragma unroll
+      for (int cc = 0; cc < 8; ++cc) {
+        if (cb0 + cc >= cb_hi) break;
+        float4* o = reinterpret_cast<float4*>(dst + (cb0 + cc) * 256 + lane * 8);
+        o[0] = make_float4(acc[cc][0], acc[cc][1], acc[cc][2], acc[cc][3]);
+        o[1] = make_float4(acc[cc][4], acc[cc][5], acc[cc][6], acc[cc][7]);
+      }
     }
   }
   if (ep_last_cta(&ctrl->combine_arrivals)) {
@@ -658,10 +679,14 @@ static int moe_forward_impl(const qk_moe_desc* desc, const uint8_t* gate, const 
   mark(3);
   if (phase == kPartial) return QK_OK;
   if (phase == kPush) {
-    const cudaError_t e = launch_dependent(moe_combine_push_kernel, dim3((B * (d.hidden / 256) + 7) / 8), dim3(256), 0, st,
-                                           ids, B, d.top_k, d.hidden, ws, push->peers, push->own, push->L, push->rank);
+    int64_t pgrid = (static_cast<int64_t>(B) + 15) / 16;
+    if (pgrid > sms) pgrid = sms;
+    const cudaError_t e = launch_dependent(moe_combine_push_kernel, dim3(static_cast<unsigned>(pgrid)), dim3(512), 0,
+                                           st, ids, B, d.top_k, d.hidden, ws, push->peers, push->own, push->L,
+                                           push->rank);
     if (e != cudaSuccess) return cuda_error(e, "moe_combine_push_kernel");
     count_launch(1);
+    mark(4);
     return QK_OK;
   }
   {
@@ -707,9 +732,28 @@ int qk_moe_forward_tp_combine(const qk_moe_desc* desc, const float* y_routes, co
                           workspace_bytes, stream, nullptr, const_cast<float*>(y_routes), kCombine);
 }
 
+static int ep_p2p_expert_impl(const qk_moe_desc* desc, const uint8_t* gate, const uint8_t* up, const uint8_t* down,
+                              void* const* peers, void* region, int world, int rank, int max_tokens, void* workspace,
+                              size_t workspace_bytes, qk_stream_t stream, void* const* events);
+
 int qk_ep_p2p_expert(const qk_moe_desc* desc, const uint8_t* gate, const uint8_t* up, const uint8_t* down,
                      void* const* peers, void* region, int world, int rank, int max_tokens, void* workspace,
                      size_t workspace_bytes, qk_stream_t stream) {
+  return ep_p2p_expert_impl(desc, gate, up, down, peers, region, world, rank, max_tokens, workspace,
+                            workspace_bytes, stream, nullptr);
+}
+
+int qk_ep_p2p_expert_profiled(const qk_moe_desc* desc, const uint8_t* gate, const uint8_t* up,
+                              const uint8_t* down, void* const* peers, void* region, int world, int rank,
+                              int max_tokens, void* workspace, size_t workspace_bytes, qk_stream_t stream,
+                              void* const* events) {
+  return ep_p2p_expert_impl(desc, gate, up, down, peers, region, world, rank, max_tokens, workspace,
+                            workspace_bytes, stream, events);
+}
+
+static int ep_p2p_expert_impl(const qk_moe_desc* desc, const uint8_t* gate, const uint8_t* up, const uint8_t* down,
+                              void* const* peers, void* region, int world, int rank, int max_tokens, void* workspace,
+                              size_t workspace_bytes, qk_stream_t stream, void* const* events) {
   QK_REQUIRE(desc && peers && region, "null pointer");
   QK_REQUIRE(world >= 1 && world <= kEpMaxRanks && rank >= 0 && rank < world, "bad rank or world");
   QK_REQUIRE(max_tokens >= 1, "max_tokens must be positive");
@@ -723,7 +767,7 @@ int qk_ep_p2p_expert(const qk_moe_desc* desc, const uint8_t* gate, const uint8_t
   return moe_forward_impl(desc, gate, up, down, reinterpret_cast<const uint16_t*>(own + L.recv_x),
                           reinterpret_cast<const int32_t*>(own + L.recv_ids),
                           reinterpret_cast<const uint16_t*>(own + L.recv_w), world * max_tokens, QK_OUT_F32,
-                          nullptr, workspace, workspace_bytes, stream, nullptr, nullptr, kPush, &push);
+                          nullptr, workspace, workspace_bytes, stream, events, nullptr, kPush, &push);
 }
 
 int qk_cast_f32_bf16(const float* in, uint16_t* out, int64_t n, qk_stream_t stream) {

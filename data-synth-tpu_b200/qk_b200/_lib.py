@@ -120,6 +120,10 @@ SIGNATURES = {
         _i,
         [ctypes.POINTER(MoeDesc), _p, _p, _p, _p, _p, _i, _i, _i, _p, _sz, _p],
     ),
+    "qk_ep_p2p_expert_profiled": (
+        _i,
+        [ctypes.POINTER(MoeDesc), _p, _p, _p, _p, _p, _i, _i, _i, _p, _sz, _p, _p],
+    ),
     "qk_ep_p2p_combine": (_i, [_p, _i, _i, _i, _i, _i, _i, _p, _p, _i, _p, _p]),
     "qk_device_alloc": (_i, [_sz, ctypes.POINTER(_p)]),
     "qk_device_free": (_i, [_p]),

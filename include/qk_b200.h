@@ -217,6 +217,13 @@ int qk_ep_p2p_dispatch(void* const* peers, void* region, int world, int rank, in
 int qk_ep_p2p_expert(const qk_moe_desc* desc, const uint8_t* gate, const uint8_t* up,
                      const uint8_t* down, void* const* peers, void* region, int world, int rank,
                      int max_tokens, void* workspace, size_t workspace_bytes, qk_stream_t stream);
+/* qk_ep_p2p_expert with CUDA events (5, cudaEvent_t) recorded before the route kernel and
+ * after the dispatch, gate/up, down and combine-and-return passes, as qk_moe_forward_profiled
+ * does; for stage timing. */
+int qk_ep_p2p_expert_profiled(const qk_moe_desc* desc, const uint8_t* gate, const uint8_t* up,
+                              const uint8_t* down, void* const* peers, void* region, int world, int rank,
+                              int max_tokens, void* workspace, size_t workspace_bytes, qk_stream_t stream,
+                              void* const* events);
 int qk_ep_p2p_combine(void* region, int world, int rank, int max_tokens, int hidden, int top_k,
                       int experts_per_rank, const int32_t* ids, const uint16_t* weights, int B,
                       uint16_t* out, qk_stream_t stream);
