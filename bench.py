@@ -587,8 +587,10 @@ def b200_arm(args):
         line["parity_checked"] = bool(line["parity"]["ok"])
     if rank == 0 and world == 1:
         line["layer"] = layer_report(raw, device, args)
-    if rank == 0 and world == 1 and not args.no_stack:
-        line["stack"] = stack_report(device, args)
+    if not args.no_stack:
+        stack = stack_report(device, args, dist)
+        if rank == 0:
+            line["stack"] = stack
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         gbs, experts = cpu_port_gbs(raw, args.qtype, res["x"], res["ids"], res["weights"],
                                     budget_s=args.ref_budget)
@@ -854,7 +856,7 @@ def layer_report(raw, device, args):
             "l2": "flushed before every call", "launches_per_call": 6}
 
 
-def stack_report(device, args):
+def stack_report(device, args, dist=None):
     """Decode steps of the synthetic 48-layer MoE decoder stack (
     hidden 2048, Q8-cache GQA 16 q / 2 kv heads of 256 at context 8192 through a random page
     table of 256-slot pages, 512 routed experts top-10 + 1 shared expert, intermediate 512,
@@ -867,8 +869,9 @@ def stack_report(device, args):
 
     cfg = StackConfig(layers=args.stack_layers, qtype=args.qtype, down_qtype=args.stack_down_qtype)
     peak, _ = hbm_peak()
+    world = dist.get_world_size() if dist else 1
     t_build = time.time()
-    model = SyntheticDecoder(cfg, device, seed=1)
+    model = SyntheticDecoder(cfg, device, seed=1, group=dist.group.WORLD if dist else None)
     torch.cuda.synchronize(device)
     build_s = time.time() - t_build
     stream = torch.cuda.current_stream(device)
@@ -884,6 +887,8 @@ def stack_report(device, args):
         for _ in range(3):
             graph.replay()
         torch.cuda.synchronize(device)
+        if dist:
+            dist.barrier()
         t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         steps = args.stack_steps
         t0.record(stream)
@@ -893,14 +898,29 @@ def stack_report(device, args):
         torch.cuda.synchronize(device)
         ms = t0.elapsed_time(t1) / steps
         nbytes, distinct = state.step_bytes()
+        if dist:
+            t = torch.tensor([ms, float(nbytes)], device=device, dtype=torch.float64)
+            dist.all_reduce(t[:1], op=dist.ReduceOp.MAX)
+            dist.all_reduce(t[1:], op=dist.ReduceOp.SUM)
+            ms, nbytes = float(t[0]), int(t[1])
         kernels, gemms = state.launches_per_step()
-        rows.append({"batch": batch, "ms_per_step": ms, "tokens_per_s": batch / (ms * 1e-3),
-                     "gbs": nbytes / (ms * 1e-3) / 1e9, "frac": nbytes / (ms * 1e-3) / 1e9 / peak,
+        tokens = batch * world
+        rows.append({"batch": tokens, "batch_per_gpu": batch, "ms_per_step": ms, "tokens_per_s": tokens / (ms * 1e-3),
+                     "gbs": nbytes / (ms * 1e-3) / 1e9, "frac": nbytes / (ms * 1e-3) / 1e9 / (peak * world),
                      "bytes_per_step": nbytes, "distinct_experts_per_layer": statistics.mean(distinct),
                      "launches_per_step": {"library": kernels, "cublas_gemm": gemms}})
-        del graph, state
+        del graph
         torch.cuda.synchronize(device)
-    return {"workload": "synthetic 48-layer MoE decoder stack (configs[3]), 1 GPU",
+        if dist:
+            dist.barrier()
+        state.close()
+        del state
+        torch.cuda.synchronize(device)
+    return {"workload": ("synthetic 48-layer MoE decoder stack (configs[3]), 1 GPU" if world == 1 else
+                         f"synthetic 48-layer MoE decoder stack (configs[3]), expert parallel over {world} GPUs: "
+                         "each rank decodes batch_per_gpu sequences (attention data parallel) and holds "
+                         f"{cfg.experts // world} routed experts + the shared expert per layer; tokens cross "
+                         "ranks through peer memory (ExpertAllToAll)"),
             "layers": cfg.layers, "context": cfg.context, "experts": cfg.experts, "top_k": cfg.top_k,
             "shared_experts": 1, "qtype": cfg.qtype, "down_qtype": cfg.down_qtype or cfg.qtype,
             "weights": "synthetic (random code bytes, fixed block scales)",

@@ -104,9 +104,12 @@ __global__ void residual_add_kernel(const uint16_t* x, const uint16_t* __restric
 // Routes of each row plus one route to the shared expert: ids_out[b] = ids[b] ++ shared_id,
 // w_out[b] = w[b] ++ bf16(sigmoid(bf16(h[b] . wsr))) (math.py:282-283, the shared expert's
 // sigmoid gate). One block per row.
+// per > 0 (expert parallel): routed expert e is renumbered (e / per) * (per + 1) + e % per, so
+// each rank's slice of `per` routed experts is followed by one more local slot (its copy of
+// the shared expert); shared_id is then the caller's own slot.
 __global__ void __launch_bounds__(kRowThreads) append_shared_route_kernel(
     const int32_t* __restrict__ ids, const uint16_t* __restrict__ w, int k, const uint16_t* __restrict__ h,
-    const uint16_t* __restrict__ wsr, int H, int shared_id, int32_t* __restrict__ ids_out,
+    const uint16_t* __restrict__ wsr, int H, int shared_id, int per, int32_t* __restrict__ ids_out,
     uint16_t* __restrict__ w_out) {
   pdl_wait();  // launched as a programmatic dependent: the previous kernel's outputs first
   pdl_trigger();
@@ -116,7 +119,8 @@ __global__ void __launch_bounds__(kRowThreads) append_shared_route_kernel(
   for (int i = threadIdx.x; i < H; i += blockDim.x) s = fmaf(bf16_to_f32(h[b * H + i]), bf16_to_f32(wsr[i]), s);
   const float dot = bf16_round(block_sum(s, red));
   if (threadIdx.x < k) {
-    ids_out[b * (k + 1) + threadIdx.x] = ids[b * k + threadIdx.x];
+    const int e = ids[b * k + threadIdx.x];
+    ids_out[b * (k + 1) + threadIdx.x] = per > 0 && e >= 0 ? (e / per) * (per + 1) + e % per : e;
     w_out[b * (k + 1) + threadIdx.x] = w[b * k + threadIdx.x];
   }
   if (threadIdx.x == 0) {
@@ -180,7 +184,23 @@ int qk_append_shared_route(const int32_t* ids, const uint16_t* weights, int B, i
   if (B == 0) return QK_OK;
   QK_REQUIRE(ids && weights && h && shared_router && ids_out && weights_out, "null pointer");
   const cudaError_t e = launch_dependent(append_shared_route_kernel, dim3(B), dim3(kRowThreads), 0, as_stream(stream),
-                                         ids, weights, k, h, shared_router, H, shared_id, ids_out, weights_out);
+                                         ids, weights, k, h, shared_router, H, shared_id, 0, ids_out, weights_out);
+  if (e != cudaSuccess) return cuda_error(e, "append_shared_route_kernel");
+  count_launch();
+  return QK_OK;
+}
+
+int qk_append_shared_route_ep(const int32_t* ids, const uint16_t* weights, int B, int k, const uint16_t* h,
+                              const uint16_t* shared_router, int H, int experts_per_rank, int rank,
+                              int32_t* ids_out, uint16_t* weights_out, qk_stream_t stream) {
+  QK_REQUIRE(B >= 0 && k > 0 && k < kRowThreads && H > 0, "invalid route geometry");
+  QK_REQUIRE(experts_per_rank > 0 && rank >= 0, "invalid expert partition");
+  if (B == 0) return QK_OK;
+  QK_REQUIRE(ids && weights && h && shared_router && ids_out && weights_out, "null pointer");
+  const int shared_id = rank * (experts_per_rank + 1) + experts_per_rank;
+  const cudaError_t e = launch_dependent(append_shared_route_kernel, dim3(B), dim3(kRowThreads), 0, as_stream(stream),
+                                         ids, weights, k, h, shared_router, H, shared_id, experts_per_rank, ids_out,
+                                         weights_out);
   if (e != cudaSuccess) return cuda_error(e, "append_shared_route_kernel");
   count_launch();
   return QK_OK;

@@ -107,6 +107,7 @@ SIGNATURES = {
     ),
     "qk_residual_add": (_i, [_p, _p, _i64, _p, _p]),
     "qk_append_shared_route": (_i, [_p, _p, _i, _i, _p, _p, _i, _i, _p, _p, _p]),
+    "qk_append_shared_route_ep": (_i, [_p, _p, _i, _i, _p, _p, _i, _i, _i, _p, _p, _p]),
     "qk_ep_plan": (_i, [_p, _p, _i, _i, _i, _i, _p, _p, _p, _p, _p, _p]),
     "qk_gather_rows": (_i, [_p, _p, _i64, _i64, _p, _p]),
     "qk_ep_combine": (_i, [_p, _p, _p, _p, _i, _i, _i, _i, _p, _p]),

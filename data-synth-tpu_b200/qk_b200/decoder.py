@@ -92,7 +92,11 @@ def synthetic_expert_bytes(qtype, count, rows, width, generator, device):
 
 
 class LayerWeights:
-    def __init__(self, cfg, generator, device):
+    """One layer's weights. ``experts_here`` packed experts: all routed experts plus the
+    shared one (one device), or one rank's slice of routed experts plus its own copy of the
+    shared expert (expert parallel)."""
+
+    def __init__(self, cfg, generator, device, experts_here=None, expert_generator=None):
         H, hq, kv, hd = cfg.hidden, cfg.query_heads, cfg.kv_heads, cfg.head_dim
 
         def normal(shape, dtype=torch.bfloat16):
@@ -110,7 +114,8 @@ class LayerWeights:
         for kind in ("gate", "up", "down"):
             qtype = normalize_qtype((cfg.down_qtype or cfg.qtype) if kind == "down" else cfg.qtype)
             rows, width = expert_shape(kind, H, cfg.intermediate)
-            raw = synthetic_expert_bytes(qtype, cfg.experts + 1, rows, width, generator, device)
+            count = cfg.experts + 1 if experts_here is None else experts_here
+            raw = synthetic_expert_bytes(qtype, count, rows, width, expert_generator or generator, device)
             self.experts[kind] = put_expert_bytes(raw, kind, qtype, H, cfg.intermediate, device=device)
             del raw
 
@@ -122,21 +127,46 @@ class LayerWeights:
 
 
 class SyntheticDecoder:
-    """All layers' weights of a :class:`StackConfig` on one device."""
+    """All layers' weights of a :class:`StackConfig` on one device, or, with a process
+    ``group`` of several ranks, one rank's part of the expert-parallel model: the dense
+    weights replicated, each layer's routed experts sharded (``experts / world`` per rank,
+    ``parallel.py:64-87``) plus a copy of the shared expert on every rank. Each rank then
+    decodes its own sequences (attention is data parallel) and the routed FFN exchanges
+    tokens through :class:`qk_b200.ep.ExpertAllToAll` (peer memory, no host synchronisation,
+    graph-capturable)."""
 
-    def __init__(self, cfg, device, seed=1):
+    def __init__(self, cfg, device, seed=1, group=None):
         self.cfg = cfg
         self.device = torch.device(device)
+        self.group = group
+        if group is None:
+            self.world, self.rank = 1, 0
+        else:
+            import torch.distributed as dist
+
+            self.world, self.rank = dist.get_world_size(group), dist.get_rank(group)
+        if cfg.experts % self.world:
+            raise ValueError("Expert count must divide expert parallel size")
+        self.per = cfg.experts // self.world
+        ep = self.world > 1
+        # the dense weights are the same on every rank; the expert bytes differ per rank
         g = torch.Generator(device=self.device).manual_seed(seed)
-        self.layers = [LayerWeights(cfg, g, self.device) for _ in range(cfg.layers)]
+        ge = torch.Generator(device=self.device).manual_seed(seed * 1000 + 7 + self.rank)
+        self.layers = [LayerWeights(cfg, g, self.device, experts_here=self.per + 1 if ep else None,
+                                    expert_generator=ge if ep else None) for _ in range(cfg.layers)]
         half = cfg.rotary_dim // 2
         inv = np.power(np.float32(cfg.rope_theta), -np.arange(half, dtype=np.float32) * 2 / np.float32(cfg.rotary_dim))
         self.inv_freq = torch.from_numpy(inv.astype(np.float32)).to(self.device)
         q, qd = normalize_qtype(cfg.qtype), normalize_qtype(cfg.down_qtype or cfg.qtype)
         self.desc = _lib.MoeDesc(GGML_TYPE[q], GGML_TYPE[q], GGML_TYPE[qd], cfg.hidden, cfg.intermediate,
                                  cfg.experts + 1, 0, cfg.top_k + 1)
+        self.types = (q, q, qd)
 
     def state(self, batch, seed=2):
+        """Decode state of ``batch`` sequences on this rank (with several ranks the global
+        batch is ``batch * world``; every rank must create its states in the same order)."""
+        if self.world > 1:
+            return DecodeState(self, batch, seed + 101 * self.rank, global_batch=batch * self.world)
         return DecodeState(self, batch, seed)
 
 
@@ -145,9 +175,10 @@ class DecodeState:
     every slot of the context in use), a page table of ``page``-slot pages in random order,
     and every intermediate buffer of one decode step."""
 
-    def __init__(self, model, batch, seed):
+    def __init__(self, model, batch, seed, global_batch=None):
         cfg, dev = model.cfg, model.device
         self.model, self.batch = model, batch
+        self.global_batch = batch if global_batch is None else global_batch
         H, hq, kv, hd, T = cfg.hidden, cfg.query_heads, cfg.kv_heads, cfg.head_dim, cfg.context
         g = torch.Generator(device=dev).manual_seed(seed)
         groups = kv * hd // 32
@@ -187,6 +218,14 @@ class DecodeState:
         self.attn_ws = torch.empty(max(self.attn_ws_bytes, 16), dtype=torch.uint8, device=dev)
         self.moe_ws_bytes = int(lib.qk_moe_workspace_bytes(model.desc, batch))
         self.moe_ws = torch.empty(max(self.moe_ws_bytes, 16), dtype=torch.uint8, device=dev)
+        self.ep = None
+        if model.world > 1:
+            from .ep import ExpertAllToAll
+
+            # every rank creates its exchange in the same order (a collective set-up)
+            self.ep = ExpertAllToAll(model.group, gate_type=model.types[0], up_type=model.types[1],
+                                     down_type=model.types[2], hidden=H, intermediate=cfg.intermediate,
+                                     experts_per_rank=model.per + 1, top_k=k + 1, max_tokens=batch, device=dev)
 
     def step(self):
         """One decode step of every layer on the current stream (no allocation, capturable)."""
@@ -216,24 +255,41 @@ class DecodeState:
             _lib.check(lib.qk_router_topk(P(self.h), P(L.router), None, B, H, cfg.experts, cfg.top_k, P(self.ids),
                                           P(self.w), None, st))
             ids_all = self.ids_all[li]
-            _lib.check(lib.qk_append_shared_route(P(self.ids), P(self.w), B, cfg.top_k, P(self.h),
-                                                  P(L.shared_router), H, cfg.experts, P(ids_all), P(self.w_all), st))
-            _lib.check(lib.qk_moe_forward(m.desc, P(L.experts["gate"]), P(L.experts["up"]), P(L.experts["down"]),
-                                          P(self.h), P(ids_all), P(self.w_all), B, _lib.QK_OUT_BF16, P(self.y),
-                                          P(self.moe_ws), self.moe_ws_bytes, st))
+            if self.ep is None:
+                _lib.check(lib.qk_append_shared_route(P(self.ids), P(self.w), B, cfg.top_k, P(self.h),
+                                                      P(L.shared_router), H, cfg.experts, P(ids_all), P(self.w_all),
+                                                      st))
+                _lib.check(lib.qk_moe_forward(m.desc, P(L.experts["gate"]), P(L.experts["up"]),
+                                              P(L.experts["down"]), P(self.h), P(ids_all), P(self.w_all), B,
+                                              _lib.QK_OUT_BF16, P(self.y), P(self.moe_ws), self.moe_ws_bytes, st))
+            else:
+                _lib.check(lib.qk_append_shared_route_ep(P(self.ids), P(self.w), B, cfg.top_k, P(self.h),
+                                                         P(L.shared_router), H, m.per, m.rank, P(ids_all),
+                                                         P(self.w_all), st))
+                self.ep(L.experts["gate"], L.experts["up"], L.experts["down"], self.h, ids_all, self.w_all,
+                        out=self.y)
             _lib.check(lib.qk_residual_add(P(self.x), P(self.y), B * H, P(self.x), st))
         return self.x
 
     def launches_per_step(self):
         # rms, norm/rope, append, attention (split + merge when split), residual, rms, router,
-        # shared route, MoE (route, dispatch, gate/up, down, combine), residual; plus 2 GEMMs
+        # shared route, MoE (route, dispatch, gate/up, down, combine; expert parallel: dispatch,
+        # wait, route, dispatch, gate/up, down, combine-and-return, final combine), residual;
+        # plus 2 GEMMs
         attn = 2 if self.attn_ws_bytes else 1
-        return self.model.cfg.layers * (9 + attn + 5), self.model.cfg.layers * 2
+        moe = 5 if self.ep is None else 8
+        return self.model.cfg.layers * (9 + attn + moe), self.model.cfg.layers * 2
+
+    def close(self):
+        if self.ep is not None:
+            self.ep.close()
+            self.ep = None
 
     def step_bytes(self):
-        """Algorithmic HBM bytes of the last step: the distinct experts each layer routed to
-        (shared included) times their packed bytes, the dense weights, and the KV cache
-        (codes and BF16 scales of every attended slot)."""
+        """Algorithmic HBM bytes of the last step on this rank: the distinct experts each layer
+        routed to (shared included; with several ranks, of this rank's tokens) times their
+        packed bytes, the dense weights, and the KV cache (codes and BF16 scales of every
+        attended slot)."""
         cfg = self.model.cfg
         total, distinct = 0, []
         for li, L in enumerate(self.model.layers):

@@ -357,6 +357,15 @@ int qk_append_shared_route(const int32_t* ids, const uint16_t* weights, int B, i
                            const uint16_t* h, const uint16_t* shared_router, int H,
                            int shared_id, int32_t* ids_out, uint16_t* weights_out,
                            qk_stream_t stream);
+/* The expert-parallel form of qk_append_shared_route: every rank holds its slice of
+ * experts_per_rank routed experts followed by its own copy of the shared expert, so routed id
+ * e becomes (e / experts_per_rank) * (experts_per_rank + 1) + e % experts_per_rank and the
+ * shared route names this rank's copy, rank * (experts_per_rank + 1) + experts_per_rank
+ * (math.py:282-283 with the experts placed as parallel.py:64-87 places them). */
+int qk_append_shared_route_ep(const int32_t* ids, const uint16_t* weights, int B, int k,
+                              const uint16_t* h, const uint16_t* shared_router, int H,
+                              int experts_per_rank, int rank, int32_t* ids_out,
+                              uint16_t* weights_out, qk_stream_t stream);
 
 /* qwen38_tpu/run.py:46-55 checked_argmax(logits): out int32 [B, 2] = (argmax over the V
  * logits of the row - the first maximum, a NaN counting as the maximum, as jnp.argmax -

@@ -200,3 +200,90 @@ def test_stack_step_in_a_cuda_graph_is_finite_and_repeatable(cuda_device):
     assert torch.equal(state.x.view(torch.int16), eager.view(torch.int16))
     nbytes, distinct = state.step_bytes()
     assert len(distinct) == 3 and all(1 <= d <= 65 for d in distinct) and nbytes > 0
+
+
+def test_expert_parallel_shared_route_renumbers_the_routed_experts(cuda_device):
+    """qk_append_shared_route_ep: routed expert e -> (e / per) * (per + 1) + e % per (each rank's
+    slice followed by its copy of the shared expert), the shared route names this rank's copy,
+    and the gate weight is the one qk_append_shared_route computes."""
+    import torch
+
+    from qk_b200 import _lib
+
+    rng = np.random.default_rng(12)
+    B, k, H, per, rank = 9, 10, 2048, 64, 3
+    ids = np.stack([rng.choice(8 * per, k, replace=False) for _ in range(B)]).astype(np.int32)
+    w = bf16_round(rng.uniform(0.01, 0.2, (B, k)).astype(np.float32))
+    h = bf16_round(rng.normal(size=(B, H)).astype(np.float32))
+    wsr = bf16_round(rng.normal(0, 0.02, H).astype(np.float32))
+    idd, wd = torch.from_numpy(ids).to(cuda_device), bf16_tensor(w, cuda_device)
+    hd, wsd = bf16_tensor(h, cuda_device), bf16_tensor(wsr, cuda_device)
+    st = _lib.stream_handle(cuda_device)
+    outs = {}
+    for name, extra in (("plain", (8 * per,)), ("ep", (per, rank))):
+        ids_all = torch.empty((B, k + 1), dtype=torch.int32, device=cuda_device)
+        w_all = torch.empty((B, k + 1), dtype=torch.bfloat16, device=cuda_device)
+        fn = "qk_append_shared_route" if name == "plain" else "qk_append_shared_route_ep"
+        _lib.call(fn, _lib.ptr(idd), _lib.ptr(wd), B, k, _lib.ptr(hd), _lib.ptr(wsd), H, *extra,
+                  _lib.ptr(ids_all), _lib.ptr(w_all), st)
+        outs[name] = (ids_all.cpu().numpy(), to_f32(w_all))
+    ids_ep, w_ep = outs["ep"]
+    np.testing.assert_array_equal(ids_ep[:, :k], (ids // per) * (per + 1) + ids % per)
+    np.testing.assert_array_equal(ids_ep[:, k], rank * (per + 1) + per)
+    np.testing.assert_array_equal(w_ep, outs["plain"][1])
+
+
+def _two_gpu_stack_rank(rank, world, port, path):
+    import datetime
+    import os
+
+    import torch
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=dev)
+    try:
+        from qk_b200.decoder import StackConfig, SyntheticDecoder
+
+        cfg = StackConfig(layers=2, experts=64, top_k=4, context=512)
+        model = SyntheticDecoder(cfg, dev, seed=1, group=dist.group.WORLD)
+        state = model.state(3, seed=2)
+        state.step()
+        torch.cuda.synchronize(dev)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            state.step()
+        x0 = state.x.clone()
+        graph.replay()
+        graph.replay()
+        torch.cuda.synchronize(dev)
+        state.ep.check_status()
+        x = state.x.float()
+        np.save(f"{path}.{rank}.npy", np.array([bool(torch.isfinite(x).all()), not torch.equal(x0, state.x)]))
+        del graph
+        dist.barrier()
+        state.close()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_expert_parallel_stack_on_two_gpus(tmp_path):
+    """The decoder stack with its routed experts split over two ranks (each rank decodes its
+    own sequences, tokens cross through peer memory) steps in a CUDA graph and stays finite."""
+    import socket
+
+    import torch
+    import torch.multiprocessing as mp
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    path = tmp_path / "stack2"
+    mp.start_processes(_two_gpu_stack_rank, args=(2, port, str(path)), nprocs=2, start_method="spawn")
+    for rank in range(2):
+        assert np.load(f"{path}.{rank}.npy").all(), rank
