@@ -591,6 +591,10 @@ def b200_arm(args):
         stack = stack_report(device, args, dist)
         if rank == 0:
             line["stack"] = stack
+    if not args.no_generation:
+        gen = generation_report(device, dist, args)
+        if rank == 0 and gen is not None:
+            line["generation"] = gen
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         gbs, experts = cpu_port_gbs(raw, args.qtype, res["x"], res["ids"], res["weights"],
                                     budget_s=args.ref_budget)
@@ -698,6 +702,92 @@ def ep_layer_report(device, dist, world, rank, args):
             "qtype": args.qtype, "ms_per_step": ms, "tokens_per_s": T / (ms * 1e-3), "gbs": gbs,
             "frac_of_aggregate_hbm": gbs / (peak * world), "active_experts": active,
             "exchange": "peer memory (ExpertAllToAll)" if world > 1 else "one rank (the exchange writes to itself)"}
+
+
+def generation_report(device, dist, args):
+    """the 48-layer synthetic MoE model with every expert Q4_K (512
+    routed, top-10, + 1 shared), batched static generation of 64 sequences: a prefill of 2048
+    random prompt ids (uniform over a vocabulary of 151936, embedding N(0, 0.02), tied output
+    head) and 512 greedy decode steps (checked_argmax), end to end on the device. With N
+    ranks the 64 sequences are split 64 / N per rank (strong scaling): attention data
+    parallel, experts sharded with the exchange through peer memory. Also the prefill-regime
+    grouped GEMM of the last layer (1 GPU: 131072 tokens x 11 routes, ~2560 tokens per routed
+    expert): its gate/up and down passes' TFLOP/s against the measured sustained BF16 peak."""
+    import ctypes
+
+    import torch
+
+    from qk_b200.decoder import StackConfig, SyntheticDecoder
+    from qk_b200.generate import StaticGeneration
+
+    world = dist.get_world_size() if dist else 1
+    seqs, prompt, new = args.gen_batch, args.gen_prompt, args.gen_new
+    if seqs % world:
+        return None
+    cfg = StackConfig(layers=args.stack_layers, qtype="Q4_K", context=prompt + new)
+    t_build = time.time()
+    model = SyntheticDecoder(cfg, device, seed=11, group=dist.group.WORLD if dist else None)
+    gen = StaticGeneration(model, seqs // world, prompt, new, seed=0)
+    torch.cuda.synchronize(device)
+    build_s = time.time() - t_build
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+    if world == 1:
+        for e in ev:
+            e.record()
+        torch.cuda.synchronize(device)
+        gen.moe_events = (ctypes.c_void_p * 5)(*[e.cuda_event for e in ev])
+    gen.capture()  # the decode step's graph (its warm-up step is undone)
+    torch.cuda.synchronize(device)
+    if dist:
+        dist.barrier()
+    stream = torch.cuda.current_stream(device)
+    t = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    t[0].record(stream)
+    gen.prefill()
+    t[1].record(stream)
+    gen.decode()
+    t[2].record(stream)
+    torch.cuda.synchronize(device)
+    prefill_ms, decode_ms = t[0].elapsed_time(t[1]), t[1].elapsed_time(t[2])
+    nonfinite = int(gen.nonfinite.item())
+    if dist:
+        tt = torch.tensor([prefill_ms, decode_ms], device=device)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        prefill_ms, decode_ms = float(tt[0]), float(tt[1])
+        dist.barrier()
+    total_ms = prefill_ms + decode_ms
+    out = {"workload": "configs[4]: 48-layer MoE model, Q4_K experts (512 top-10 + shared), static generation",
+           "sequences": seqs, "prompt_tokens": prompt, "new_tokens": new, "vocab": 151936,
+           "sequences_per_gpu": seqs // world, "build_s": build_s,
+           "prefill_ms": prefill_ms, "decode_ms": decode_ms, "end_to_end_ms": total_ms,
+           "generated_tokens_per_s": seqs * new / (total_ms * 1e-3),
+           "prefill_tokens_per_s": seqs * prompt / (prefill_ms * 1e-3),
+           "decode_tokens_per_s": seqs * (new - 1) / (decode_ms * 1e-3),
+           "nonfinite_logits": nonfinite,
+           "parallelism": "1 GPU" if world == 1 else f"ep{world}: attention data parallel, experts sharded"}
+    if world == 1:
+        st = [ev[i].elapsed_time(ev[i + 1]) for i in range(4)]
+        routes = seqs * prompt * (cfg.top_k + 1)
+        sustained = peak_tflops("bf16_tflops_sustained")
+        gu = routes * 2 * (2 * cfg.intermediate * cfg.hidden) / (st[1] * 1e-3) / 1e12
+        dn = routes * 2 * (cfg.intermediate * cfg.hidden) / (st[2] * 1e-3) / 1e12
+        out["prefill_grouped_gemm"] = {
+            "layer": "last", "tokens": seqs * prompt, "routes": routes,
+            "stage_ms": dict(zip(("route_dispatch", "gate_up", "down", "combine"), st)),
+            "gate_up_tflops": gu, "down_tflops": dn, "peak_tflops": sustained,
+            "gate_up_frac": gu / sustained, "down_frac": dn / sustained,
+            "kernel": "umma_prefill_kernel (256-token chunks, tcgen05 kind::f16, A and B in shared memory)"}
+    gen.close()
+    del gen, model
+    torch.cuda.synchronize(device)
+    return out
+
+
+def peak_tflops(key="bf16_tflops"):
+    try:
+        return float(json.loads((ROOT / "MEASURED_PEAKS.json").read_text())[key])
+    except (OSError, KeyError, ValueError):
+        return 1400.0 if "sustained" in key else 1590.0
 
 
 def attention_inputs(device, batch, ctx):
@@ -1090,6 +1180,11 @@ def main():
     parser.add_argument("--attn-reps", type=int, default=20)
     parser.add_argument("--no-stack", action="store_true", help="skip the 48-layer decoder stack")
     parser.add_argument("--no-ep-layer", action="store_true", help="skip the configs[3] expert-parallel layer")
+    parser.add_argument("--no-generation", action="store_true", help="skip the configs[4] static generation")
+    parser.add_argument("--generation-only", action="store_true", help="only the configs[4] static generation (one GPU)")
+    parser.add_argument("--gen-batch", type=int, default=64)
+    parser.add_argument("--gen-prompt", type=int, default=2048)
+    parser.add_argument("--gen-new", type=int, default=512)
     parser.add_argument("--qsa-only", action="store_true", help="only the sparse token selection (one GPU)")
     parser.add_argument("--stack-only", action="store_true", help="only the decoder stack (one GPU)")
     parser.add_argument("--stack-batches", type=lambda t: [int(v) for v in t.split(",")], default=[1, 8, 64])
@@ -1112,6 +1207,13 @@ def main():
         device = torch.device("cuda", 0)
         torch.cuda.set_device(device)
         print(json.dumps({"qsa_select": qsa_report(device, args)}), flush=True)
+        return 0
+    if args.generation_only:
+        import torch
+
+        device = torch.device("cuda", 0)
+        torch.cuda.set_device(device)
+        print(json.dumps({"generation": generation_report(device, None, args)}), flush=True)
         return 0
     if args.stack_only:
         import torch

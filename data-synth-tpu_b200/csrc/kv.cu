@@ -49,12 +49,13 @@ __global__ void quantize_kernel(const void* __restrict__ x, int in_bf16, int64_t
   }
 }
 
-// write_quantized: one thread per (row b, tensor k/v, channel).
+// write_quantized: one thread per (input row, tensor k/v, channel). With W > 1 (a prompt
+// chunk) input row r is token r % W of cache row r / W, written at time time[r / W] + r % W.
 __global__ void append_kernel(const void* __restrict__ key, const void* __restrict__ value, int in_bf16,
                               const int32_t* __restrict__ time, const uint8_t* __restrict__ active,
                               int8_t* k_codes, int8_t* v_codes, uint16_t* k_scale, uint16_t* v_scale,
-                              int B, int T, int D, int group) {
-  const int64_t total = static_cast<int64_t>(B) * 2 * D;
+                              int B, int T, int D, int group, int W = 1) {
+  const int64_t total = static_cast<int64_t>(B) * W * 2 * D;
   const int G = D / group;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t base = static_cast<int64_t>(blockIdx.x) * blockDim.x; base < total; base += stride) {
@@ -67,14 +68,16 @@ __global__ void append_kernel(const void* __restrict__ key, const void* __restri
     int8_t code;
     uint16_t sb;
     quantize_lane(in ? load_in(src, static_cast<int64_t>(b) * D + col, in_bf16) : 0.f, group, code, sb);
-    if (!in || (active && !active[b])) continue;
-    int t = time[b];
+    const int row = b / W, tok = b - row * W;  // cache row and token of the chunk
+    if (!in || (active && !active[row])) continue;
+    int t = time[row];
     if (t < 0) t += T;
+    t += tok;
     if (t < 0 || t >= T) continue;  // out-of-range scatter updates are dropped
     int8_t* codes = which ? v_codes : k_codes;
     uint16_t* plane = which ? v_scale : k_scale;
-    codes[(static_cast<int64_t>(b) * T + t) * D + col] = code;
-    if (col % group == 0) plane[(static_cast<int64_t>(b) * G + col / group) * T + t] = sb;
+    codes[(static_cast<int64_t>(row) * T + t) * D + col] = code;
+    if (col % group == 0) plane[(static_cast<int64_t>(row) * G + col / group) * T + t] = sb;
   }
 }
 
@@ -150,6 +153,23 @@ int qk_kv_q8_append(const void* key, const void* value, int in_dtype, const int3
   const int D = kv_heads * head_dim;
   append_kernel<<<grid_for(static_cast<int64_t>(B) * 2 * D, 256), 256, 0, as_stream(stream)>>>(
       key, value, in_dtype == QK_OUT_BF16, time, active, k_codes, v_codes, k_scale, v_scale, B, T, D, group);
+  QK_LAUNCHED("append_kernel");
+  return QK_OK;
+}
+
+int qk_kv_q8_append_chunk(const void* key, const void* value, int in_dtype, const int32_t* start,
+                          const uint8_t* active, int8_t* k_codes, int8_t* v_codes, uint16_t* k_scale,
+                          uint16_t* v_scale, int B, int W, int T, int kv_heads, int head_dim,
+                          qk_stream_t stream) {
+  QK_REQUIRE(in_dtype == QK_OUT_F32 || in_dtype == QK_OUT_BF16, "in_dtype must be F32 or BF16");
+  QK_REQUIRE(B >= 0 && W >= 1 && T > 0 && kv_heads > 0 && head_dim > 0, "invalid cache geometry");
+  const int group = head_dim < 32 ? head_dim : 32;  // config.py:91-93
+  QK_REQUIRE(pow2_le32(group) && head_dim % group == 0, "KV head dimension must divide into cache quantization groups");
+  if (B == 0) return QK_OK;
+  QK_REQUIRE(key && value && start && k_codes && v_codes && k_scale && v_scale, "null pointer");
+  const int D = kv_heads * head_dim;
+  append_kernel<<<grid_for(static_cast<int64_t>(B) * W * 2 * D, 256), 256, 0, as_stream(stream)>>>(
+      key, value, in_dtype == QK_OUT_BF16, start, active, k_codes, v_codes, k_scale, v_scale, B, T, D, group, W);
   QK_LAUNCHED("append_kernel");
   return QK_OK;
 }

@@ -80,6 +80,7 @@ SIGNATURES = {
     "qk_moe_check": (_i, [_p, _p]),
     "qk_kv_q8_quantize": (_i, [_p, _i, _i64, _i, _i, _p, _p, _p]),
     "qk_kv_q8_append": (_i, [_p, _p, _i, _p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _p]),
+    "qk_kv_q8_append_chunk": (_i, [_p, _p, _i, _p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _p]),
     "qk_kv_q8_gather_scales": (_i, [_p, _p, _i, _i, _i, _i, _p, _p]),
     "qk_kv_q8_read": (_i, [_p, _p, _p, _i, _i, _i, _i, _i, _i, _p, _p]),
     "qk_kv_q8_attention_workspace_bytes": (_sz, [_i, _i, _i, _i, _i]),

@@ -191,11 +191,11 @@ class DecodeState:
             self.caches.append(cache)
         self.cache_config = CacheConfig(kv_heads=kv, head_dim=hd, query_heads=hq, max_context=T)
         rng = np.random.default_rng(0)
-        pages = T // cfg.page
-        table = np.stack([rng.permutation(pages) for _ in range(batch)])
+        page = cfg.page if T % cfg.page == 0 else 1  # a context that is not whole pages: no paging
+        table = np.stack([rng.permutation(T // page) for _ in range(batch)]) if page > 1 else None
         slots = np.arange(T)
-        self.indices = torch.from_numpy(
-            np.ascontiguousarray((table[:, slots // cfg.page] * cfg.page + slots % cfg.page).astype(np.int32))).to(dev)
+        order = table[:, slots // page] * page + slots % page if page > 1 else np.tile(slots, (batch, 1))
+        self.indices = torch.from_numpy(np.ascontiguousarray(order.astype(np.int32))).to(dev)
         self.positions = torch.full((batch,), T - 1, dtype=torch.int32, device=dev)
         bf = dict(dtype=torch.bfloat16, device=dev)
         self.x = (torch.randn((batch, H), device=dev, generator=g)).to(torch.bfloat16)

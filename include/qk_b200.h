@@ -251,6 +251,13 @@ int qk_kv_q8_append(const void* key, const void* value, int in_dtype, const int3
                     const uint8_t* active, int8_t* k_codes, int8_t* v_codes, uint16_t* k_scale,
                     uint16_t* v_scale, int B, int T, int kv_heads, int head_dim,
                     qk_stream_t stream);
+/* A prompt chunk of W tokens per cache row (the write of the chunked prefill,
+ * engine.py:449-500 forward_chunk through attention_cache.py:26-43): key/value
+ * [B * W, kv_heads, head_dim]; token j of row b is written at time start[b] + j. */
+int qk_kv_q8_append_chunk(const void* key, const void* value, int in_dtype, const int32_t* start,
+                          const uint8_t* active, int8_t* k_codes, int8_t* v_codes, uint16_t* k_scale,
+                          uint16_t* v_scale, int B, int W, int T, int kv_heads, int head_dim,
+                          qk_stream_t stream);
 /* attention_cache.py:46-68 gather_scale_plane(plane, indices, groups): out BF16
  * [B, S, groups]; negative indices wrap once, then clamp (test_qwen38_kv_gather.py:22-32). */
 int qk_kv_q8_gather_scales(const uint16_t* plane, const int32_t* indices, int B, int S,
