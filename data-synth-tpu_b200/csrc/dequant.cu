@@ -316,6 +316,33 @@ __global__ void __launch_bounds__(2 * kTileRows) dequant_tiled_kernel(const uint
   }
 }
 
+// The reference's TPU input form of a Q6_K projection (packed_q6/layout.py:49-91, PackedQ6):
+// per (64-row output tile, K block) one 13,312-byte data tile holding the rows' GGUF bytes
+// [0, 128) as [row][128], then [128, 192) as [row][64], then [192, 208) as [row][16], and a
+// separate scale plane holding the rows' FP16 `d` bytes [208, 210) as [tile][block][row][2].
+// This kernel restores the GGUF rows [rows, blocks, 210] from the two planes (the inverse,
+// unpack_q6, is layout.py:93-108); rows past `rows` in the last tile are padding and skipped.
+// One CTA per (tile, block); each thread writes bytes of the tile's rows in order.
+__global__ void q6_soa_to_rows_kernel(const uint8_t* __restrict__ data, const uint8_t* __restrict__ scales,
+                                      int64_t rows, int64_t blocks, uint8_t* __restrict__ raw) {
+  constexpr int kRows = 64, kBlock = 210, kDataTile = kRows * 208;
+  const int64_t tb = blockIdx.x;  // tile * blocks + block
+  const int64_t tile = tb / blocks, blk = tb % blocks;
+  const uint8_t* src = data + tb * kDataTile;
+  const uint8_t* sc = scales + tb * (kRows * 2);
+  for (int i = threadIdx.x; i < kRows * kBlock; i += blockDim.x) {
+    const int r = i / kBlock, b = i % kBlock;
+    const int64_t row = tile * kRows + r;
+    if (row >= rows) break;
+    uint8_t v;
+    if (b < 128) v = src[r * 128 + b];
+    else if (b < 192) v = src[kRows * 128 + r * 64 + (b - 128)];
+    else if (b < 208) v = src[kRows * 192 + r * 16 + (b - 192)];
+    else v = sc[r * 2 + (b - 208)];
+    raw[(row * blocks + blk) * kBlock + b] = v;
+  }
+}
+
 int grid_for(int64_t total, int block) {
   int64_t g = (total + block - 1) / block;
   const int64_t cap = static_cast<int64_t>(sm_count()) * 32;
@@ -411,6 +438,19 @@ int qk_dequantize_tiled(const uint8_t* tiled, int qtype, int64_t rows, int64_t r
     else dequant_tiled_kernel<QType::Q4_K, true><<<grid, 2 * kTileRows, 0, st>>>(tiled, rows, row_width, nblk, bf, out);
   }
   QK_LAUNCHED("dequant_tiled_kernel");
+  return QK_OK;
+}
+
+int qk_q6_soa_to_rows(const uint8_t* data, const uint8_t* scales, int64_t rows, int64_t input_features,
+                      uint8_t* raw, qk_stream_t stream) {
+  QK_REQUIRE(rows > 0 && input_features > 0, "rows and input_features must be positive");
+  QK_REQUIRE(data && scales && raw, "null pointer");
+  const int64_t blocks = (input_features + 255) / 256;
+  const int64_t tiles = (rows + 63) / 64;
+  QK_REQUIRE(tiles * blocks < (1ll << 31), "too many tiles");
+  q6_soa_to_rows_kernel<<<static_cast<unsigned>(tiles * blocks), 256, 0, as_stream(stream)>>>(
+      data, scales, rows, blocks, raw);
+  QK_LAUNCHED("q6_soa_to_rows_kernel");
   return QK_OK;
 }
 

@@ -58,6 +58,7 @@ SIGNATURES = {
     "qk_repack_rows": (_i, [_p, _i, _i64, _i64, _p, _p, _p]),
     "qk_unpack_rows": (_i, [_p, _i, _i64, _i64, _p, _p]),
     "qk_dequantize_tiled": (_i, [_p, _i, _i64, _i64, _i, _p, _p]),
+    "qk_q6_soa_to_rows": (_i, [_p, _p, _i64, _i64, _p, _p]),
     "qk_quant_gemm_workspace_bytes": (_sz, [_i64, _i64, _i64]),
     "qk_quant_gemm": (_i, [_p, _i64, _i64, _p, _i, _i64, _p, _p, _sz, _p]),
     "qk_router_topk": (_i, [_p, _p, _p, _i, _i, _i, _i, _p, _p, _p, _p]),

@@ -106,6 +106,64 @@ def unpack_rows(packed):
 
 unpack_q6 = unpack_rows
 
+# The reference's TPU input form of a Q6_K projection (packed_q6/layout.py:13-18, 49-91):
+# per (64-row tile, K block) a 13,312-byte data tile and a 128-byte scale tile; the scale
+# plane is padded to whole 512-byte fetch windows.
+SOA_TILE_BYTES = 64 * 208
+SOA_SCALE_TILE_BYTES = 64 * 2
+SOA_SCALE_FETCH_BYTES = 512
+
+
+def soa_plane_bytes(output_features, input_features):
+    """``(data bytes, scale bytes)`` of the reference's ``PackedQ6`` planes."""
+    tiles = (output_features + 63) // 64
+    blocks = (input_features + 255) // 256
+    scale = tiles * blocks * SOA_SCALE_TILE_BYTES
+    scale = (scale + SOA_SCALE_FETCH_BYTES - 1) // SOA_SCALE_FETCH_BYTES * SOA_SCALE_FETCH_BYTES
+    return tiles * blocks * SOA_TILE_BYTES, scale
+
+
+def _flat_u8(plane, device):
+    if isinstance(plane, np.ndarray):
+        if plane.dtype != np.uint8:
+            return None
+        return torch.from_numpy(np.ascontiguousarray(plane).reshape(-1)).to(device)
+    if not isinstance(plane, torch.Tensor) or plane.dtype != torch.uint8:
+        return None
+    return plane.reshape(-1).to(device).contiguous()
+
+
+def from_soa(data, scales=None, input_features=None, output_features=None, device=None):
+    """The reference's ``PackedQ6`` planes -> this build's tiles on the device.
+
+    ``data``/``scales`` are the flat uint8 planes of ``packed_q6.layout.pack_q6``
+    (``layout.py:49-91``), NumPy or torch; or pass a ``PackedQ6``-like object (``.data``,
+    ``.scales``, ``.input_features``, ``.output_features``) as ``data``. The planes go back
+    to GGUF rows on the device (``qk_q6_soa_to_rows``, the inverse of ``pack_q6``) and are
+    repacked into the tile layout, all on the device and without arithmetic, so the result
+    equals ``pack_q6`` of the original rows byte for byte."""
+    if scales is None and hasattr(data, "scales"):
+        data, scales, input_features, output_features = (
+            data.data, data.scales, data.input_features, data.output_features)
+    if type(input_features) is not int or input_features < 1:
+        raise ValueError("input_features must be a positive integer")
+    if type(output_features) is not int or output_features < 1:
+        raise ValueError("output_features must be positive")
+    device = torch.device(device or "cuda")
+    want_data, want_scales = soa_plane_bytes(output_features, input_features)
+    d = _flat_u8(data, device)
+    if d is None or d.numel() != want_data or (getattr(data, "ndim", 1) != 1):
+        raise ValueError("Packed Q6 dtype/shape does not match projection dimensions")
+    sc = _flat_u8(scales, device)
+    if sc is None or sc.numel() != want_scales or (getattr(scales, "ndim", 1) != 1):
+        raise ValueError("Packed Q6 scale dtype/shape does not match projection dimensions")
+    blocks = (input_features + 255) // 256
+    raw = torch.empty((output_features, blocks, 210), dtype=torch.uint8, device=device)
+    with torch.cuda.device(device):
+        _lib.call("qk_q6_soa_to_rows", _lib.ptr(d), _lib.ptr(sc), output_features, input_features,
+                  _lib.ptr(raw), _lib.stream_handle(device))
+    return pack_rows(raw, input_features, "Q6_K", device)
+
 
 def dequantize_packed(packed, dtype=torch.bfloat16, *, fused=False):
     """Decode tiles through the GEMM kernels' fragment decoder -> ``[N, K]``.
@@ -155,14 +213,21 @@ def quant_matmul(x, packed):
     return out
 
 
-def q6_matmul(x, packed, *, output_features, batch_tile=8):
-    """``packed_q6.kernel.q6_matmul`` contract: FP32 ``[M, N]``; validates like the reference."""
+def q6_matmul(x, packed, scales=None, *, output_features, batch_tile=8):
+    """``packed_q6.kernel.q6_matmul`` contract: FP32 ``[M, N]``; validates like the reference.
+
+    ``packed`` is a :class:`PackedWeights` of this build's tiles, or, with ``scales``, the
+    reference's flat ``PackedQ6`` data plane (``kernel.py:99``: ``q6_matmul(x, packed,
+    scales, *, output_features)``), which is converted on the device first
+    (:func:`from_soa`; convert once with it to keep the conversion out of a loop)."""
     if not isinstance(x, torch.Tensor) or x.dim() != 2 or min(x.shape) < 1 or x.dtype != torch.bfloat16:
         raise ValueError("x must be a nonempty [M,K] BF16 array")
     if type(output_features) is not int or output_features < 1:
         raise ValueError("output_features must be positive")
     if type(batch_tile) is not int or batch_tile < 8 or batch_tile % 8:
         raise ValueError("batch_tile must be a positive multiple of 8")
+    if scales is not None:
+        packed = from_soa(packed, scales, x.shape[1], output_features, x.device)
     if packed.qtype != "Q6_K" or packed.output_features != output_features or (
         packed.input_features != x.shape[1]
     ):

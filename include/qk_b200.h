@@ -83,6 +83,12 @@ int qk_repack_rows(const uint8_t* raw, int qtype, int64_t rows, int64_t row_widt
                    uint8_t* tiled, int32_t* bad_scales, qk_stream_t stream);
 int qk_unpack_rows(const uint8_t* tiled, int qtype, int64_t rows, int64_t row_width,
                    uint8_t* raw, qk_stream_t stream);
+/* The reference's own TPU input form of a Q6_K projection (packed_q6/layout.py:49-91,
+ * PackedQ6.data / PackedQ6.scales, layout "q6_k_soa_n64_k256_v1") back to GGUF rows
+ * raw [rows, ceil(input_features / 256), 210]: the inverse byte transform of pack_q6
+ * (unpack_q6, layout.py:93-108), on the device. Feed the rows to qk_repack_rows. */
+int qk_q6_soa_to_rows(const uint8_t* data, const uint8_t* scales, int64_t rows,
+                      int64_t input_features, uint8_t* raw, qk_stream_t stream);
 /* Decode of the tiled layout through the GEMM kernels' in-register fragment decoder:
  * bit-identical to qk_dequantize_rows on the raw rows (signed zeros included), or with
  * out_dtype | QK_DECODE_FUSED the exact arithmetic the GEMM kernels run. */

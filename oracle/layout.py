@@ -140,3 +140,24 @@ def untile(tiled, qtype, rows, row_width):
     if qtype == "Q8_0":
         return _q8_blocks(raw, (row_width + 31) // 32)
     return unrepack_q6_codes(raw) if qtype == "Q6_K" else raw
+
+
+def soa_to_rows(data, scales, outputs, inputs):
+    """The reference's SoA planes of a Q6_K projection back to GGUF rows
+    ``uint8[outputs, ceil(inputs / 256), 210]``: ``packed_q6/layout.py:93-108`` (``unpack_q6``).
+
+    Per (64-row tile, K block) the data tile holds the rows' bytes ``[0, 128)`` as
+    ``[row][128]``, ``[128, 192)`` as ``[row][64]``, ``[192, 208)`` as ``[row][16]``; the
+    scale plane holds bytes ``[208, 210)`` as ``[tile][block][row][2]``."""
+    blocks = (inputs + 255) // 256
+    tiles = (outputs + TILE_ROWS - 1) // TILE_ROWS
+    d = np.asarray(data, np.uint8).reshape(tiles, blocks, TILE_ROWS * 208)
+    raw = np.empty((tiles, blocks, TILE_ROWS, 210), np.uint8)
+    offset = 0
+    for first, last in ((0, 128), (128, 192), (192, 208)):
+        width = last - first
+        raw[..., first:last] = d[..., offset:offset + TILE_ROWS * width].reshape(tiles, blocks, TILE_ROWS, width)
+        offset += TILE_ROWS * width
+    raw[..., 208:210] = np.asarray(scales, np.uint8)[:tiles * blocks * TILE_ROWS * 2].reshape(
+        tiles, blocks, TILE_ROWS, 2)
+    return raw.transpose(0, 2, 1, 3).reshape(tiles * TILE_ROWS, blocks, 210)[:outputs]

@@ -11,6 +11,8 @@ The fixtures are committed; tests never read the reference at run time. Sources:
 * gguf-py 0.19.0 ``gguf.quants.dequantize`` - the third-party pin of the same decoders;
 * ``packed_q6/reference.py`` ``fixture``, ``decode_reference``, ``projection_reference``
   - the packed-Q6 projection golden (``tests/test_packed_q6.py:51-81`` cases);
+* ``packed_q6/layout.py`` ``pack_q6`` - the reference's SoA planes of fixture rows
+  (``soa_q6.npz``), the input form ``qk_q6_soa_to_rows`` restores;
 * pure-NumPy functions that live in modules importing JAX are executed from their own
   source text (extracted with ``ast``, no JAX needed): ``compute.pack_q8``,
   ``compute.numpy_q8_matmul`` and the test oracle ``scale_oracle``
@@ -39,6 +41,7 @@ def load_reference(root):
     kaggle = Path(root) / "kaggle"
     sys.path.insert(0, str(kaggle))
     from glm53_offload import gguf_quant
+    from packed_q6 import layout as q6layout
     from packed_q6 import reference as q6ref
     from qwen38_tpu import quant
 
@@ -58,6 +61,7 @@ def load_reference(root):
         "pack_q8": extract(compute, "pack_q8"),
         "numpy_q8_matmul": extract(compute, "numpy_q8_matmul"),
         "scale_oracle": extract(kaggle / "tests" / "test_qwen38_kv_gather.py", "scale_oracle"),
+        "pack_q6": q6layout.pack_q6,
     }
     return gguf_quant, quant, q6ref, funcs
 
@@ -298,16 +302,40 @@ def split_golden(quant, funcs):
     np.savez_compressed(HERE / "split_experts.npz", **out)
 
 
+SOA_CASES = ((64, 256), (70, 300), (130, 512))
+
+
+def soa_golden(q6ref, funcs):
+    """The reference's SoA planes (``packed_q6/layout.py:49-91``) of fixture rows."""
+    out = {"cases": np.array(SOA_CASES, np.int64)}
+    for outputs, inputs in SOA_CASES:
+        raw = q6ref.fixture(outputs, inputs)
+        packed = funcs["pack_q6"](raw, inputs)
+        key = f"{outputs}_{inputs}"
+        out[f"raw_{key}"] = raw
+        out[f"data_{key}"] = np.asarray(packed.data)
+        out[f"scales_{key}"] = np.asarray(packed.scales)
+    np.savez_compressed(HERE / "soa_q6.npz", **out)
+
+
 def main():
-    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("QK_REFERENCE_ROOT")
+    args = [a for a in sys.argv[1:] if not a.startswith("--only=")]
+    only = [a.split("=", 1)[1] for a in sys.argv[1:] if a.startswith("--only=")]
+    root = args[0] if args else os.environ.get("QK_REFERENCE_ROOT")
     if not root:
-        sys.exit("usage: make_golden.py REFERENCE_CHECKOUT (or set QK_REFERENCE_ROOT)")
+        sys.exit("usage: make_golden.py REFERENCE_CHECKOUT [--only=NAME] (or set QK_REFERENCE_ROOT)")
     gguf_quant, quant, q6ref, funcs = load_reference(root)
-    decode_golden(gguf_quant, quant)
-    q6_golden(q6ref)
-    routing_golden(quant, funcs)
-    q8_golden(funcs)
-    split_golden(quant, funcs)
+    steps = {
+        "decode": lambda: decode_golden(gguf_quant, quant),
+        "q6": lambda: q6_golden(q6ref),
+        "routing": lambda: routing_golden(quant, funcs),
+        "q8": lambda: q8_golden(funcs),
+        "split": lambda: split_golden(quant, funcs),
+        "soa": lambda: soa_golden(q6ref, funcs),
+    }
+    for name, step in steps.items():
+        if not only or name in only:
+            step()
     for path in sorted(HERE.glob("*.npz")):
         print(f"{path.name}: {path.stat().st_size} bytes")
 

@@ -171,3 +171,37 @@ def test_accumulator_is_reset_between_row_and_token_tiles(cuda_device):
     result = q6_matmul(x, packed, output_features=128).cpu().numpy()
     np.testing.assert_array_equal(result[:, :64], result[:, 64:])
     np.testing.assert_array_equal(result[:20], -result[20:])
+
+
+def test_reference_soa_planes_restore_gguf_rows_and_project(golden, cuda_device):
+    """The reference's ``PackedQ6`` planes (its own ``pack_q6`` output) through
+    ``qk_q6_soa_to_rows`` give back the GGUF rows byte for byte, ``from_soa`` equals
+    ``pack_q6`` of those rows, and ``q6_matmul(x, data, scales, ...)`` (the reference's call
+    form, ``packed_q6/kernel.py:99``) equals the projection over this build's tiles."""
+    import torch
+
+    from qk_b200 import _lib
+    from qk_b200.packed import from_soa, pack_q6, q6_matmul
+
+    data = golden("soa_q6.npz")
+    for outputs, inputs in data["cases"]:
+        outputs, inputs = int(outputs), int(inputs)
+        key = f"{outputs}_{inputs}"
+        d = torch.from_numpy(data[f"data_{key}"]).to(cuda_device)
+        sc = torch.from_numpy(data[f"scales_{key}"]).to(cuda_device)
+        raw = torch.empty((outputs, (inputs + 255) // 256, 210), dtype=torch.uint8, device=cuda_device)
+        _lib.call("qk_q6_soa_to_rows", _lib.ptr(d), _lib.ptr(sc), outputs, inputs, _lib.ptr(raw),
+                  _lib.stream_handle(cuda_device))
+        assert np.array_equal(raw.cpu().numpy(), data[f"raw_{key}"])
+        mine = pack_q6(data[f"raw_{key}"], inputs, device=cuda_device)
+        assert torch.equal(from_soa(data[f"data_{key}"], data[f"scales_{key}"], inputs, outputs,
+                                    device=cuda_device).data, mine.data)
+        x = torch.randn(9, inputs, generator=torch.Generator().manual_seed(outputs)).to(
+            cuda_device, torch.bfloat16)
+        want = q6_matmul(x, mine, output_features=outputs)
+        got = q6_matmul(x, d, sc, output_features=outputs)
+        assert torch.equal(got, want)
+    with pytest.raises(ValueError, match="Packed Q6 dtype/shape"):
+        q6_matmul(x, d[:-1], sc, output_features=outputs)
+    with pytest.raises(ValueError, match="Packed Q6 scale dtype/shape"):
+        q6_matmul(x, d, sc[:-512], output_features=outputs)

@@ -165,3 +165,14 @@ def test_q8_0_tiles_round_trip_and_place_codes_in_position_order(rows, width):
     np.testing.assert_array_equal(body[r // 64, j // 8, 0, r % 64, 2 * (j % 8) : 2 * (j % 8) + 2], raw[r, j, :2])
     codes = body[r // 64, j // 8, 1:, r % 64].reshape(256)[32 * (j % 8) : 32 * (j % 8) + 32]
     np.testing.assert_array_equal(codes, raw[r, j, 2:])
+
+
+def test_soa_restatement_inverts_the_reference_pack_q6(golden):
+    """``oracle.layout.soa_to_rows`` against the reference's own ``pack_q6`` planes."""
+    from oracle.layout import soa_to_rows
+
+    data = golden("soa_q6.npz")
+    for outputs, inputs in data["cases"]:
+        key = f"{outputs}_{inputs}"
+        raw = soa_to_rows(data[f"data_{key}"], data[f"scales_{key}"], int(outputs), int(inputs))
+        assert np.array_equal(raw, data[f"raw_{key}"])
