@@ -12,7 +12,9 @@ import pytest
 
 gguf = pytest.importorskip("gguf")
 
-H, I, E = 512, 256, 4
+# I = 512: a tensor-parallel slice of 256 intermediate channels is one whole Q6_K / Q4_K
+# down block, which the reference's split requires (qwen38_tpu/parallel.py:53-55)
+H, I, E = 512, 512, 4
 
 
 def finite_blocks(rng, shape, qtype):
