@@ -406,6 +406,10 @@ def b200_arm(args):
         for _ in range(warmup):
             step()
         torch.cuda.synchronize(device)
+        launched = qk_b200.launch_count()
+        step()  # one more eager step, counting this library's kernel launches
+        launches = qk_b200.launch_count() - launched
+        torch.cuda.synchronize(device)
         # capture one step in a CUDA graph so the timed loop is free of host launch gaps
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph):
@@ -436,7 +440,7 @@ def b200_arm(args):
             stage_ms = [a / reps for a in acc]
         fn.check_status()
         nbytes, active = step_bytes(qtype, ids)
-        return dict(m=m, ms=ms, bytes=nbytes, active=active, rows=rows, stage_ms=stage_ms,
+        return dict(m=m, ms=ms, bytes=nbytes, active=active, rows=rows, stage_ms=stage_ms, launches=launches,
                     gate_up_bytes=kernel_bytes(qtype, ids), x=x, ids=ids, weights=weights,
                     out=out)
 
@@ -461,6 +465,10 @@ def b200_arm(args):
         for _ in range(warmup):
             step()
         torch.cuda.synchronize(device)
+        launched = qk_b200.launch_count()
+        step()
+        launches = qk_b200.launch_count() - launched
+        torch.cuda.synchronize(device)
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph):
             step()
@@ -478,6 +486,7 @@ def b200_arm(args):
         ms = t0.elapsed_time(t1) / steps
         layer.check_status()
         return dict(m=m, ms=ms, rows=rows, x=x, ids=ids, weights=weights, out=layer.out[:rows], layer=layer,
+                    launches=launches,
                     graph=graph)
 
     peak, peak_kind = hbm_peak()
@@ -500,10 +509,10 @@ def b200_arm(args):
         step_total, _ = ep_step_bytes(args.qtype, args.m, world)
     value = step_total / (ms * 1e-3) / 1e9
 
-    # launches per step: the 5 kernels of one qk_moe_forward; the expert-parallel step adds
-    # the dispatch, the wait for the sources and the final combine (the expert pass's
-    # combine stores to the sources)
-    launches_per_step = 5 if ep is None else 7
+    # launches per step, counted by the library around one eager step: route, dispatch,
+    # gate/up, down (and the combine unless the routes are top-1); the expert-parallel step
+    # adds the dispatch, the wait for the sources and the final combine
+    launches_per_step = res["launches"] if ep is None else ep["launches"]
 
     # e2e through the public call with host buffers
     if ep is None:
@@ -790,6 +799,36 @@ def peak_tflops(key="bf16_tflops"):
         return 1400.0 if "sustained" in key else 1590.0
 
 
+def flushed_graph_times(call, device, reps, flush):
+    """Device times (ms) of `reps` replays of `call` captured in a CUDA graph, each after an
+    L2 flush (`flush`, a buffer larger than L2, zeroed). The graph keeps the host's per-call
+    work (argument checks, tensor map encoding, launches) out of the timed region: issued
+    eagerly, it can reach the GPU after the flush has drained and leave an idle gap between
+    the events."""
+    import torch
+
+    stream = torch.cuda.current_stream(device)
+    for _ in range(3):
+        call()
+    torch.cuda.synchronize(device)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        call()
+    graph.replay()
+    torch.cuda.synchronize(device)
+    times = []
+    for _ in range(reps):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        graph.replay()
+        e1.record(stream)
+        torch.cuda.synchronize(device)
+        times.append(e0.elapsed_time(e1))
+    del graph
+    return times
+
+
 def attention_inputs(device, batch, ctx):
     """Inputs of one configs[2] call: 16 q / 2 kv heads, head dim 256, one query token per
     sequence, every slot of the context attended through a page table that is a random
@@ -864,22 +903,11 @@ def attention_sweep(device, reps=20, configs=ATTN_CONFIGS, parity=False):
     against the oracle after the timing."""
     import torch
 
-    stream = torch.cuda.current_stream(device)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
     results = []
     for batch, ctx in configs:
         inp = attention_inputs(device, batch, ctx)
-        for _ in range(3):
-            attention_call(inp)
-        times = []
-        for _ in range(reps):
-            flush.zero_()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(stream)
-            attention_call(inp)
-            e1.record(stream)
-            torch.cuda.synchronize(device)
-            times.append(e0.elapsed_time(e1))
+        times = flushed_graph_times(lambda: attention_call(inp), device, reps, flush)
         ms = statistics.median(times)
         nbytes = batch * ctx * ATTN_SLOT_BYTES
         r = {"batch": batch, "ctx": ctx, "us": ms * 1e3, "gbs": nbytes / (ms * 1e-3) / 1e9,
@@ -925,17 +953,8 @@ def layer_report(raw, device, args):
         ids, w = routes(x, router, k)
         return fn(tensors["gate"], tensors["up"], tensors["down"], x, ids, w), ids
 
-    for _ in range(3):
-        call()
-    times = []
-    for _ in range(args.attn_reps):
-        flush.zero_()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        _, ids = call()
-        e1.record(stream)
-        torch.cuda.synchronize(device)
-        times.append(e0.elapsed_time(e1))
+    times = flushed_graph_times(call, device, args.attn_reps, flush)
+    _, ids = call()
     ms = statistics.median(times)
     active = int(torch.unique(ids).numel())
     nbytes = active * packed_bytes_per_expert(args.qtype) + count * HIDDEN * 4 + T * HIDDEN * 4
@@ -1041,25 +1060,14 @@ def qsa_report(device, args):
         K = budget // ratio
         idx = torch.empty((batch, K * ratio + ratio - 1), dtype=torch.int32, device=device)
         val = torch.empty(idx.shape, dtype=torch.uint8, device=device)
-        st = _lib.stream_handle(device)
-
         def call():
+            st = _lib.stream_handle(device)  # the current stream: the capture stream under a graph
             _lib.call("qk_qsa_block_scores", _lib.ptr(q), _lib.ptr(k), _lib.ptr(lengths), batch, heads, dim, blocks,
                       ratio, _lib.ptr(scores), st)
             _lib.call("qk_qsa_select", _lib.ptr(scores), _lib.ptr(lengths), batch, blocks, ratio, budget,
                       _lib.ptr(idx), _lib.ptr(val), st)
 
-        for _ in range(3):
-            call()
-        times = []
-        for _ in range(args.attn_reps):
-            flush.zero_()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(stream)
-            call()
-            e1.record(stream)
-            torch.cuda.synchronize(device)
-            times.append(e0.elapsed_time(e1))
+        times = flushed_graph_times(call, device, args.attn_reps, flush)
         ms = statistics.median(times)
         nbytes = batch * blocks * (dim * 2 + 8)
         rows.append({"batch": batch, "us": ms * 1e3, "gbs": nbytes / (ms * 1e-3) / 1e9,

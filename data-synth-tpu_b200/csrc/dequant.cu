@@ -132,6 +132,8 @@ inline int tile_bytes(int qtype) {
   return qtype == QK_TYPE_Q6_K   ? HalfTile<QType::Q6_K>::kBytes
          : qtype == QK_TYPE_Q4_K ? HalfTile<QType::Q4_K>::kBytes
          : qtype == QK_TYPE_Q8_0 ? HalfTile<QType::Q8_0>::kBytes
+         : qtype == QK_TYPE_Q5_K ? HalfTile<QType::Q5_K>::kBytes
+         : qtype == QK_TYPE_Q5_1 ? HalfTile<QType::Q5_1>::kBytes
                                  : 0;
 }
 
@@ -219,17 +221,19 @@ __global__ void __launch_bounds__(kTileRows) repack_q6_kernel(const uint8_t* __r
   }
 }
 
-// Q4_K: a byte transpose. One CTA per tile; tiled[...] <- raw[...] (or the reverse).
-template <bool kPack>
-__global__ void repack_q4_kernel(const uint8_t* __restrict__ in, uint8_t* __restrict__ out, int64_t rows,
-                                 int64_t nblk, int32_t* bad_scales) {
-  constexpr int TB = HalfTile<QType::Q4_K>::kBytes;
+// Q4_K and Q5_K: a byte transpose of the GGUF block bytes. One CTA per tile; byte `off` of
+// the tile is chunk off / 1024, row (off % 1024) / 16, byte off % 16 of the chunk, i.e. block
+// byte 16 * chunk + off % 16. tiled[...] <- raw[...] (or the reverse).
+template <bool kPack, int kBlockBytes>
+__global__ void repack_k_kernel(const uint8_t* __restrict__ in, uint8_t* __restrict__ out, int64_t rows,
+                                int64_t nblk, int32_t* bad_scales) {
+  constexpr int TB = kTileRows * kBlockBytes;
   const int64_t tile = blockIdx.x;
   const int64_t strip = tile / nblk, kb = tile % nblk;
   for (int off = threadIdx.x; off < TB; off += blockDim.x) {
     const int r = (off & 1023) >> 4, src = (off >> 10) * 16 + (off & 15);
     const int64_t row = strip * kTileRows + r;
-    const int64_t raw_off = (row * nblk + kb) * 144 + src;
+    const int64_t raw_off = (row * nblk + kb) * kBlockBytes + src;
     const int64_t tiled_off = tile * TB + off;
     if (kPack) {
       uint8_t v = 0;
@@ -239,6 +243,48 @@ __global__ void repack_q4_kernel(const uint8_t* __restrict__ in, uint8_t* __rest
       }
       out[tiled_off] = v;
     } else if (row < rows) {
+      out[raw_off] = in[tiled_off];
+    }
+  }
+}
+
+// Q5_1: super-blocks of 8 GGUF blocks of 24 bytes (rowtile.cuh). One CTA per tile; chunk c,
+// row r, byte b of the tile hold, for c < 2, byte b % 4 of block 4c + b / 4 (d, m); for
+// c in {2, 3}, byte 4 + b % 4 of block 4 (c - 2) + b / 4 (the high-bit word); for c >= 4,
+// byte 8 + b of block c - 4 (the nibbles). Raw rows have nblk32 blocks; super-block blocks
+// past them are zero.
+template <bool kPack>
+__global__ void repack_q51_kernel(const uint8_t* __restrict__ in, uint8_t* __restrict__ out, int64_t rows,
+                                  int64_t nblk, int64_t nblk32, int32_t* bad_scales) {
+  constexpr int TB = HalfTile<QType::Q5_1>::kBytes;
+  const int64_t tile = blockIdx.x;
+  const int64_t strip = tile / nblk, kb = tile % nblk;
+  for (int off = threadIdx.x; off < TB; off += blockDim.x) {
+    const int c = off >> 10, r = (off & 1023) >> 4, byte = off & 15;
+    const int64_t row = strip * kTileRows + r;
+    int j, src;
+    if (c < 2) {
+      j = 4 * c + (byte >> 2);
+      src = byte & 3;
+    } else if (c < 4) {
+      j = 4 * (c - 2) + (byte >> 2);
+      src = 4 + (byte & 3);
+    } else {
+      j = c - 4;
+      src = 8 + byte;
+    }
+    const int64_t blk = kb * 8 + j;
+    const bool exists = row < rows && blk < nblk32;
+    const int64_t raw_off = (row * nblk32 + blk) * 24 + src;
+    const int64_t tiled_off = tile * TB + off;
+    if (kPack) {
+      uint8_t v = 0;
+      if (exists) {
+        v = in[raw_off];
+        if (bad_scales && src == 1 && (v & 0x7c) == 0x7c) atomicAdd(bad_scales, 1);
+      }
+      out[tiled_off] = v;
+    } else if (exists) {
       out[raw_off] = in[tiled_off];
     }
   }
@@ -380,7 +426,8 @@ int64_t qk_tiled_bytes(int qtype, int64_t rows, int64_t row_width) {
 static int repack_common(const uint8_t* in, int qtype, int64_t rows, int64_t row_width,
                          uint8_t* out, int32_t* bad, qk_stream_t stream, bool pack) {
   const int tb = tile_bytes(qtype);
-  if (tb == 0) return set_error(QK_ERR_UNSUPPORTED_TYPE, "tiled layout supports Q6_K, Q4_K and Q8_0; got %d", qtype);
+  if (tb == 0)
+    return set_error(QK_ERR_UNSUPPORTED_TYPE, "tiled layout supports Q6_K, Q4_K, Q5_K, Q8_0 and Q5_1; got %d", qtype);
   QK_REQUIRE(rows > 0 && row_width > 0, "Expected [output_features, ceil(input_features / block), bytes]");
   QK_REQUIRE(in && out, "null pointer");
   const int64_t nblk = (row_width + 255) / 256;
@@ -395,9 +442,16 @@ static int repack_common(const uint8_t* in, int qtype, int64_t rows, int64_t row
     const int64_t nblk32 = (row_width + 31) / 32;
     if (pack) repack_q8_kernel<true><<<g, 256, 0, st>>>(in, out, rows, nblk, nblk32, bad);
     else repack_q8_kernel<false><<<g, 256, 0, st>>>(in, out, rows, nblk, nblk32, nullptr);
+  } else if (qtype == QK_TYPE_Q5_1) {
+    const int64_t nblk32 = (row_width + 31) / 32;
+    if (pack) repack_q51_kernel<true><<<g, 256, 0, st>>>(in, out, rows, nblk, nblk32, bad);
+    else repack_q51_kernel<false><<<g, 256, 0, st>>>(in, out, rows, nblk, nblk32, nullptr);
+  } else if (qtype == QK_TYPE_Q5_K) {
+    if (pack) repack_k_kernel<true, 176><<<g, 256, 0, st>>>(in, out, rows, nblk, bad);
+    else repack_k_kernel<false, 176><<<g, 256, 0, st>>>(in, out, rows, nblk, nullptr);
   } else {
-    if (pack) repack_q4_kernel<true><<<g, 256, 0, st>>>(in, out, rows, nblk, bad);
-    else repack_q4_kernel<false><<<g, 256, 0, st>>>(in, out, rows, nblk, nullptr);
+    if (pack) repack_k_kernel<true, 144><<<g, 256, 0, st>>>(in, out, rows, nblk, bad);
+    else repack_k_kernel<false, 144><<<g, 256, 0, st>>>(in, out, rows, nblk, nullptr);
   }
   QK_LAUNCHED("repack_kernel");
   return QK_OK;
@@ -415,7 +469,8 @@ int qk_unpack_rows(const uint8_t* tiled, int qtype, int64_t rows, int64_t row_wi
 
 int qk_dequantize_tiled(const uint8_t* tiled, int qtype, int64_t rows, int64_t row_width,
                         int out_dtype, void* out, qk_stream_t stream) {
-  if (tile_bytes(qtype) == 0) return set_error(QK_ERR_UNSUPPORTED_TYPE, "tiled layout supports Q6_K, Q4_K and Q8_0; got %d", qtype);
+  if (tile_bytes(qtype) == 0)
+    return set_error(QK_ERR_UNSUPPORTED_TYPE, "tiled layout supports Q6_K, Q4_K, Q5_K, Q8_0 and Q5_1; got %d", qtype);
   QK_REQUIRE(rows > 0 && row_width > 0, "rows and row_width must be positive");
   const bool fused = (out_dtype & QK_DECODE_FUSED) != 0;
   out_dtype &= ~QK_DECODE_FUSED;
@@ -433,6 +488,12 @@ int qk_dequantize_tiled(const uint8_t* tiled, int qtype, int64_t rows, int64_t r
   } else if (qtype == QK_TYPE_Q8_0) {
     if (fused) dequant_tiled_kernel<QType::Q8_0, false><<<grid, 2 * kTileRows, 0, st>>>(tiled, rows, row_width, nblk, bf, out);
     else dequant_tiled_kernel<QType::Q8_0, true><<<grid, 2 * kTileRows, 0, st>>>(tiled, rows, row_width, nblk, bf, out);
+  } else if (qtype == QK_TYPE_Q5_K) {
+    if (fused) dequant_tiled_kernel<QType::Q5_K, false><<<grid, 2 * kTileRows, 0, st>>>(tiled, rows, row_width, nblk, bf, out);
+    else dequant_tiled_kernel<QType::Q5_K, true><<<grid, 2 * kTileRows, 0, st>>>(tiled, rows, row_width, nblk, bf, out);
+  } else if (qtype == QK_TYPE_Q5_1) {
+    if (fused) dequant_tiled_kernel<QType::Q5_1, false><<<grid, 2 * kTileRows, 0, st>>>(tiled, rows, row_width, nblk, bf, out);
+    else dequant_tiled_kernel<QType::Q5_1, true><<<grid, 2 * kTileRows, 0, st>>>(tiled, rows, row_width, nblk, bf, out);
   } else {
     if (fused) dequant_tiled_kernel<QType::Q4_K, false><<<grid, 2 * kTileRows, 0, st>>>(tiled, rows, row_width, nblk, bf, out);
     else dequant_tiled_kernel<QType::Q4_K, true><<<grid, 2 * kTileRows, 0, st>>>(tiled, rows, row_width, nblk, bf, out);

@@ -79,8 +79,10 @@ size_t qk_quant_gemm_workspace_bytes(int64_t M, int64_t K, int64_t N) {
 
 int qk_quant_gemm(const uint16_t* x, int64_t M, int64_t K, const uint8_t* w_tiled, int qtype,
                   int64_t N, float* out, void* workspace, size_t workspace_bytes, qk_stream_t stream) {
-  if (qtype != QK_TYPE_Q6_K && qtype != QK_TYPE_Q4_K && qtype != QK_TYPE_Q8_0)
-    return set_error(QK_ERR_UNSUPPORTED_TYPE, "packed projection supports Q6_K, Q4_K and Q8_0; got %d", qtype);
+  if (qtype != QK_TYPE_Q6_K && qtype != QK_TYPE_Q4_K && qtype != QK_TYPE_Q8_0 && qtype != QK_TYPE_Q5_K &&
+      qtype != QK_TYPE_Q5_1)
+    return set_error(QK_ERR_UNSUPPORTED_TYPE, "packed projection supports Q6_K, Q4_K, Q5_K, Q8_0 and Q5_1; got %d",
+                     qtype);
   QK_REQUIRE(M >= 0 && K > 0 && N > 0, "x must be a nonempty [M,K] BF16 array");
   QK_REQUIRE(M < (1 << 30) && K < (1 << 30) && N < (1 << 30), "dimension too large");
   if (M == 0) return QK_OK;
@@ -115,6 +117,8 @@ int qk_quant_gemm(const uint16_t* x, int64_t M, int64_t K, const uint8_t* w_tile
   const int grid = static_cast<int>(items < sms ? items : sms);
   int rc = qtype == QK_TYPE_Q6_K   ? launch_umma<QType::Q6_K, kModeDense>(a, grid, st)
            : qtype == QK_TYPE_Q4_K ? launch_umma<QType::Q4_K, kModeDense>(a, grid, st)
+           : qtype == QK_TYPE_Q5_K ? launch_umma<QType::Q5_K, kModeDense>(a, grid, st)
+           : qtype == QK_TYPE_Q5_1 ? launch_umma<QType::Q5_1, kModeDense>(a, grid, st)
                                    : launch_umma<QType::Q8_0, kModeDense>(a, grid, st);
   if (rc || !a.ksplit) return rc;
   const int64_t mn = M * N;

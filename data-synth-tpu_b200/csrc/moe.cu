@@ -18,6 +18,8 @@
 //  5. combine  - per token, FP32 sum of f32(y) * f32(route) over its experts in ascending
 //                expert order (the reference's accumulation order, experts.py:129), then
 //                BF16 (experts.py:131), or the FP32 partial sum for an EP all-reduce.
+#include <type_traits>
+
 #include "common.cuh"
 #include "ep_p2p.cuh"
 #include "umma_prefill.cuh"
@@ -50,9 +52,17 @@ struct Workspace {
   uint8_t* xt;            // gate/up activation tiles [rows_max x H bf16]
   uint8_t* ht;            // down activation tiles [rows_max x I bf16]
   uint16_t* y;            // [B k, H]
+  int32_t* hist;          // [kRouteCtas][E] entries per (route CTA, expert), many-route calls only
 };
 
 inline size_t align256(size_t n) { return (n + 255) & ~size_t(255); }
+
+constexpr int kStagedRoutes = 4096;
+// Above this many routes the metadata is built by three kernels over many CTAs (count,
+// tables, place) instead of one CTA.
+constexpr int kManyRoutes = 16384;
+constexpr int kRouteCtas = 256;         // CTAs of the count / place kernels at most
+constexpr int kRouteThreads = 512;
 
 // Activation-tile rows: each active expert's entries rounded up to 16 per chunk.
 // Token chunks: each active expert's entries in runs of kMaxTok (or of kWideTok; the
@@ -92,6 +102,7 @@ size_t layout(const qk_moe_desc& d, int max_tokens, uint8_t* base, Workspace* ws
   uint8_t* xt = take(rows * d.hidden * 2);
   uint8_t* ht = take(rows * ((d.intermediate + 255) / 256 * 256) * 2);  // whole 256-value K blocks
   uint8_t* y = take(R * d.hidden * 2);
+  uint8_t* hist = take(R > kManyRoutes ? kRouteCtas * E * 4 : 0);
   if (ws) {
     ws->meta = reinterpret_cast<MoeMeta*>(meta);
     ws->counts = reinterpret_cast<int32_t*>(counts);
@@ -107,62 +118,48 @@ size_t layout(const qk_moe_desc& d, int max_tokens, uint8_t* base, Workspace* ws
     ws->xt = xt;
     ws->ht = ht;
     ws->y = reinterpret_cast<uint16_t*>(y);
+    ws->hist = reinterpret_cast<int32_t*>(hist);
   }
   return off;
 }
 
 // ------------------------------------------------------------------------------------
-// 1. routing metadata (one CTA)
+// 1. routing metadata
 // ------------------------------------------------------------------------------------
-constexpr int kStagedRoutes = 4096;
 
-__global__ void __launch_bounds__(1024) moe_route_kernel(const int32_t* ids, const uint16_t* weights,
-                                                         int B, int k, int E, int first, int ctok,
-                                                         Workspace ws) {
-  extern __shared__ int32_t sh[];
-  pdl_wait();     // launched as a programmatic dependent: the routes' producer first
-  pdl_trigger();  // the dispatch may launch now (it waits for this kernel before reading)
-  int32_t* counts = sh;            // [E]
-  int32_t* cursor = sh + E;        // [E]
-  int32_t* offsets = sh + 2 * E;   // [E + 1]
-  __shared__ int32_t chunk_base[33], active_base[33];
+// Route (b, j)'s entry: the first slot j of a token that names local expert e owns the
+// merged entry; its weight is bf16 of the FP32 sum over all slots naming e, in slot order
+// (experts.py:66-73). Zero-weight entries are dropped (experts.py:74-76). Returns the local
+// expert, or -1 when the route owns no entry.
+__device__ __forceinline__ int route_owner(const int32_t* ids, const uint16_t* weights, int b, int j, int k, int E,
+                                           int first, float& w) {
+  const int e = ids[b * k + j] - first;
+  int own = e >= 0 && e < E;
+  for (int jj = 0; own && jj < j; ++jj) own = ids[b * k + jj] - first != e;
+  w = 0.f;
+  if (own) {
+    for (int jj = j; jj < k; ++jj)
+      if (ids[b * k + jj] - first == e) w = __fadd_rn(w, bf16_to_f32(weights[b * k + jj]));
+    w = bf16_round(w);
+    own = w != 0.f;
+  }
+  return own ? e : -1;
+}
+
+// The tables every later pass reads, from the entry counts per expert (`counts`, shared
+// memory, [E]): exclusive offsets (`offsets`, shared memory, [E + 1], and ws.offsets),
+// ws.counts, the ascending active-expert list, and the token chunks (<= ctok entries of
+// one expert) with their activation-tile rows (each chunk padded to a multiple of 16 rows)
+// and one record per chunk. Run by a whole CTA: warp 0 scans into shared memory (`tab`,
+// [3 E + 2] ints: active list, chunk offsets, row offsets), then every thread copies the
+// tables out and writes the chunk records, so no thread waits on a global read.
+__device__ void route_tables(const int32_t* counts, int32_t* offsets, int32_t* tab, int E, int ctok,
+                             const Workspace& ws) {
+  __shared__ int32_t base[2][33], n_act_sh;
+  int32_t* active = tab;                // [E]
+  int32_t* chunk_off = tab + E;         // [E + 1]
+  int32_t* row_off = tab + 2 * E + 1;   // [E + 1]
   const int tid = threadIdx.x, nt = blockDim.x;
-  // The routes staged in shared memory when they fit (kStagedRoutes): both passes read
-  // every route of a token k times.
-  const bool staged = B * k <= kStagedRoutes;
-  int32_t* s_ids = sh + 3 * E + 1;                                                   // [B k]
-  uint16_t* s_w = reinterpret_cast<uint16_t*>(s_ids + (staged ? B * k : 0));          // [B k]
-  for (int e = tid; e < E; e += nt) counts[e] = cursor[e] = 0;
-  if (staged) {
-    for (int i = tid; i < B * k; i += nt) {
-      s_ids[i] = ids[i];
-      s_w[i] = weights[i];
-    }
-    ids = s_ids;
-    weights = s_w;
-  }
-  __syncthreads();
-
-  // Pass 1: entries per expert. The first slot j of a token that names expert e owns
-  // the merged entry; its weight is bf16 of the FP32 sum over all slots naming e. One
-  // thread per route (b, j).
-  for (int route = tid; route < B * k; route += nt) {
-    const int b = route / k, j = route - b * k;
-    const int e = ids[b * k + j] - first;
-    int own = e >= 0 && e < E;
-    for (int jj = 0; own && jj < j; ++jj) own = ids[b * k + jj] - first != e;
-    float w = 0.f;
-    if (own) {
-      for (int jj = j; jj < k; ++jj)
-        if (ids[b * k + jj] - first == e) w = __fadd_rn(w, bf16_to_f32(weights[b * k + jj]));
-      w = bf16_round(w);
-      own = w != 0.f;
-    }
-    if (own) atomicAdd(&counts[e], 1);
-  }
-  __syncthreads();
-
-  // Exclusive scan over experts (warp 0, contiguous chunks per lane) + active list.
   if (tid < 32) {
     const int per = (E + 31) / 32, lo = min(E, tid * per), hi = min(E, lo + per);
     int sum = 0, act = 0;
@@ -178,36 +175,25 @@ __global__ void __launch_bounds__(1024) moe_route_kernel(const int32_t* ids, con
         iact += a;
       }
     }
-    chunk_base[tid] = incl - sum;
-    active_base[tid] = iact - act;
-    if (tid == 31) {
-      chunk_base[32] = incl;
-      active_base[32] = iact;
-    }
-    __syncwarp();
-    int run = chunk_base[tid], arun = active_base[tid];
+    int run = incl - sum, arun = iact - act;
     for (int e = lo; e < hi; ++e) {
       offsets[e] = run;
-      ws.offsets[e] = run;
-      ws.counts[e] = counts[e];
       run += counts[e];
-      if (counts[e] > 0) ws.active[arun++] = e;
+      if (counts[e] > 0) active[arun++] = e;
     }
+    const int total = __shfl_sync(0xffffffffu, incl, 31), n_act = __shfl_sync(0xffffffffu, iact, 31);
     if (tid == 31) {
-      offsets[E] = chunk_base[32];
-      ws.offsets[E] = chunk_base[32];
-      ws.meta->n_entries = chunk_base[32];
-      ws.meta->n_active = active_base[32];
+      offsets[E] = total;
+      n_act_sh = n_act;
+      ws.meta->n_entries = total;
+      ws.meta->n_active = n_act;
       ws.meta->status = 0;
     }
     __syncwarp();
-    // Token chunks (<= ctok entries of one expert) and their activation-tile rows
-    // (each chunk padded to a multiple of 16 rows), in active-expert order.
-    const int n_act = active_base[32];
     const int per2 = (n_act + 31) / 32, lo2 = min(n_act, tid * per2), hi2 = min(n_act, lo2 + per2);
     int ch_sum = 0, row_sum = 0;
     for (int a = lo2; a < hi2; ++a) {
-      const int m = counts[ws.active[a]], nch = (m + ctok - 1) / ctok;
+      const int m = counts[active[a]], nch = (m + ctok - 1) / ctok;
       ch_sum += nch;
       row_sum += ctok * (nch - 1) + (((m - ctok * (nch - 1)) + 15) & ~15);
     }
@@ -221,49 +207,156 @@ __global__ void __launch_bounds__(1024) moe_route_kernel(const int32_t* ids, con
     }
     int cb = ch_incl - ch_sum, rb = row_incl - row_sum;
     for (int a = lo2; a < hi2; ++a) {
-      const int m = counts[ws.active[a]], nch = (m + ctok - 1) / ctok;
-      ws.chunk_off[a] = cb;
-      ws.row_off[a] = rb;
+      const int m = counts[active[a]], nch = (m + ctok - 1) / ctok;
+      chunk_off[a] = cb;
+      row_off[a] = rb;
       cb += nch;
       rb += ctok * (nch - 1) + (((m - ctok * (nch - 1)) + 15) & ~15);
     }
     if (tid == 31) {
-      ws.chunk_off[n_act] = ch_incl;
-      ws.row_off[n_act] = row_incl;
+      chunk_off[n_act] = ch_incl;
+      row_off[n_act] = row_incl;
       ws.meta->n_chunks = ch_incl;
       ws.meta->row_total = row_incl;
     }
   }
   __syncthreads();
 
-  // Chunk records: the tensor-core passes read one record per token chunk instead of
-  // searching the chunk tables.
-  {
-    const int n_act = ws.meta->n_active;
-    for (int a = tid; a < n_act; a += nt) {
-      const int e = ws.active[a], m = counts[e], nch = (m + ctok - 1) / ctok;
-      const int c0 = ws.chunk_off[a], r0 = ws.row_off[a], e0 = offsets[e];
-      for (int ch = 0; ch < nch; ++ch)
-        ws.chunk_rec[c0 + ch] = make_int4(e, min(ctok, m - ctok * ch), e0 + ctok * ch, r0 + ctok * ch);
-    }
+  // Copies of the tables for the later passes, and one record per token chunk (the
+  // tensor-core passes read one record per chunk instead of searching the chunk tables).
+  const int n_act = n_act_sh;
+  for (int e = tid; e <= E; e += nt) {
+    ws.offsets[e] = offsets[e];
+    if (e < E) ws.counts[e] = counts[e];
   }
+  for (int a = tid; a <= n_act; a += nt) {
+    ws.chunk_off[a] = chunk_off[a];
+    ws.row_off[a] = row_off[a];
+    if (a == n_act) break;
+    const int e = active[a], m = counts[e], nch = (m + ctok - 1) / ctok;
+    ws.active[a] = e;
+    const int c0 = chunk_off[a], r0 = row_off[a], e0 = offsets[e];
+    for (int ch = 0; ch < nch; ++ch)
+      ws.chunk_rec[c0 + ch] = make_int4(e, min(ctok, m - ctok * ch), e0 + ctok * ch, r0 + ctok * ch);
+  }
+}
+
+// One CTA builds everything (B * k <= kManyRoutes).
+__global__ void __launch_bounds__(1024) moe_route_kernel(const int32_t* ids, const uint16_t* weights,
+                                                         int B, int k, int E, int first, int ctok,
+                                                         Workspace ws) {
+  extern __shared__ int32_t sh[];
+  pdl_wait();     // launched as a programmatic dependent: the routes' producer first
+  pdl_trigger();  // the dispatch may launch now (it waits for this kernel before reading)
+  int32_t* counts = sh;            // [E]
+  int32_t* cursor = sh + E;        // [E]
+  int32_t* offsets = sh + 2 * E;   // [E + 1]
+  int32_t* tab = sh + 3 * E + 1;   // [3 E + 2] route_tables' scratch
+  const int tid = threadIdx.x, nt = blockDim.x;
+  // The routes staged in shared memory when they fit (kStagedRoutes): both passes read
+  // every route of a token k times.
+  const bool staged = B * k <= kStagedRoutes;
+  int32_t* s_ids = sh + 6 * E + 3;                                                   // [B k]
+  uint16_t* s_w = reinterpret_cast<uint16_t*>(s_ids + (staged ? B * k : 0));          // [B k]
+  for (int e = tid; e < E; e += nt) counts[e] = cursor[e] = 0;
+  if (staged) {
+    for (int i = tid; i < B * k; i += nt) {
+      s_ids[i] = ids[i];
+      s_w[i] = weights[i];
+    }
+    ids = s_ids;
+    weights = s_w;
+  }
+  __syncthreads();
+
+  // Pass 1: entries per expert, one thread per route (b, j).
+  for (int route = tid; route < B * k; route += nt) {
+    const int b = route / k, j = route - b * k;
+    float w;
+    const int e = route_owner(ids, weights, b, j, k, E, first, w);
+    if (e >= 0) atomicAdd(&counts[e], 1);
+  }
+  __syncthreads();
+  route_tables(counts, offsets, tab, E, ctok, ws);
 
   // Pass 2: place entries (one thread per route).
   for (int route = tid; route < B * k; route += nt) {
     const int b = route / k, j = route - b * k;
-    const int e = ids[b * k + j] - first;
-    int own = e >= 0 && e < E;
-    for (int jj = 0; own && jj < j; ++jj) own = ids[b * k + jj] - first != e;
-    float w = 0.f;
-    if (own) {
-      for (int jj = j; jj < k; ++jj)
-        if (ids[b * k + jj] - first == e) w = __fadd_rn(w, bf16_to_f32(weights[b * k + jj]));
-      w = bf16_round(w);
-      own = w != 0.f;
-    }
+    float w;
+    const int e = route_owner(ids, weights, b, j, k, E, first, w);
     int slot = -1;
-    if (own) {
+    if (e >= 0) {
       slot = offsets[e] + atomicAdd(&cursor[e], 1);
+      ws.entry_token[slot] = b;
+      ws.entry_weight[slot] = w;
+      ws.entry_route[slot] = b * k + j;
+    }
+    ws.route_entry[b * k + j] = slot;
+  }
+}
+
+// Many routes (B * k > kManyRoutes): CTA g of the count and place kernels takes the tokens
+// [g B / G, (g + 1) B / G). The count kernel writes the CTA's entries per expert to
+// ws.hist[g][E]; the tables kernel turns each expert's column into exclusive prefixes over
+// the CTAs and builds the tables from the column sums; the place kernel puts CTA g's
+// entries of expert e at offsets[e] + hist[g][e] onwards. Inside one CTA the order of an
+// expert's entries is free (each entry is one independent token column of the projections).
+__global__ void __launch_bounds__(kRouteThreads) moe_route_count_kernel(const int32_t* ids, const uint16_t* weights,
+                                                                        int B, int k, int E, int first, Workspace ws) {
+  extern __shared__ int32_t sh[];  // [E]
+  pdl_wait();
+  pdl_trigger();
+  const int G = gridDim.x, g = blockIdx.x;
+  for (int e = threadIdx.x; e < E; e += blockDim.x) sh[e] = 0;
+  __syncthreads();
+  const int b0 = static_cast<int>(static_cast<int64_t>(g) * B / G), b1 = static_cast<int>(static_cast<int64_t>(g + 1) * B / G);
+  for (int route = b0 * k + threadIdx.x; route < b1 * k; route += blockDim.x) {
+    const int b = route / k, j = route - b * k;
+    float w;
+    const int e = route_owner(ids, weights, b, j, k, E, first, w);
+    if (e >= 0) atomicAdd(&sh[e], 1);
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) ws.hist[static_cast<int64_t>(g) * E + e] = sh[e];
+}
+
+__global__ void __launch_bounds__(1024) moe_route_tables_kernel(int G, int E, int ctok, Workspace ws) {
+  extern __shared__ int32_t sh[];
+  int32_t* counts = sh;       // [E]
+  int32_t* offsets = sh + E;  // [E + 1]
+  int32_t* tab = sh + 2 * E + 1;  // [3 E + 2]
+  pdl_wait();
+  pdl_trigger();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    int run = 0;
+    for (int g = 0; g < G; ++g) {
+      const int64_t i = static_cast<int64_t>(g) * E + e;
+      const int v = ws.hist[i];
+      ws.hist[i] = run;
+      run += v;
+    }
+    counts[e] = run;
+  }
+  __syncthreads();
+  route_tables(counts, offsets, tab, E, ctok, ws);
+}
+
+__global__ void __launch_bounds__(kRouteThreads) moe_route_place_kernel(const int32_t* ids, const uint16_t* weights,
+                                                                        int B, int k, int E, int first, Workspace ws) {
+  extern __shared__ int32_t sh[];  // [E] next slot of each expert
+  pdl_wait();
+  pdl_trigger();
+  const int G = gridDim.x, g = blockIdx.x;
+  for (int e = threadIdx.x; e < E; e += blockDim.x) sh[e] = ws.offsets[e] + ws.hist[static_cast<int64_t>(g) * E + e];
+  __syncthreads();
+  const int b0 = static_cast<int>(static_cast<int64_t>(g) * B / G), b1 = static_cast<int>(static_cast<int64_t>(g + 1) * B / G);
+  for (int route = b0 * k + threadIdx.x; route < b1 * k; route += blockDim.x) {
+    const int b = route / k, j = route - b * k;
+    float w;
+    const int e = route_owner(ids, weights, b, j, k, E, first, w);
+    int slot = -1;
+    if (e >= 0) {
+      slot = atomicAdd(&sh[e], 1);
       ws.entry_token[slot] = b;
       ws.entry_weight[slot] = w;
       ws.entry_route[slot] = b * k + j;
@@ -317,82 +410,102 @@ __global__ void __launch_bounds__(256) moe_dispatch_kernel(const uint16_t* __res
 // ------------------------------------------------------------------------------------
 constexpr int kMaxTopK = 32;
 
-// One warp per (token, 256-column block): lane j holds route j's entry; ranks by expert id
-// give the reference's ascending-expert accumulation order. Each lane owns 8 columns of the
-// block and loads the rows of up to 8 routes before accumulating them in FP32, so a warp's
-// loads are in flight together; small batches still spread over many SMs.
-// With `yr` (tensor parallel: the FP32 down projection of each route, summed over the
-// tensor ranks) the expert output of route (b, j) is bf16(yr[b * k + j]) (grouped_experts.py:
+// One warp per token: lane j < k holds route j's entry, and its rank among the token's
+// entries by expert id gives the reference's ascending-expert accumulation order
+// (experts.py:129); lane i then learns which lane holds rank i. Each lane owns 8 columns of
+// every 256-column block and walks the row in groups of 4 blocks: for two routes at a time it
+// loads all 8 of its 16-byte pieces before adding them, in rank order, into FP32 sums, so the
+// loads of a warp are in flight together and the route metadata is read once per token.
+// With `yr` (tensor parallel: the FP32 down projection of each route, summed over the tensor
+// ranks) the expert output of route (b, j) is bf16(yr[b * k + j]) (grouped_experts.py:
 // 113-119: psum before the BF16 rounding); otherwise the entry's BF16 y.
 __global__ void __launch_bounds__(256) moe_combine_kernel(const int32_t* __restrict__ ids, int B,
                                                           int k, int H, int out_bf16, void* out,
                                                           const float* __restrict__ yr, Workspace ws) {
-  constexpr int kBatch = 8;  // route rows in flight per lane
+  constexpr int kG = 4;  // 256-column blocks per group
   pdl_wait();
   const int lane = threadIdx.x & 31;
-  const int blocks = H / 256;
-  const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  if (gw >= B * blocks) return;
-  const int b = gw / blocks, c0 = (gw - b * blocks) * 256 + lane * 8;
+  const int b = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (b >= B) return;
   const int entry = lane < k ? ws.route_entry[b * k + lane] : -1;
   const int eid = entry >= 0 ? ids[b * k + lane] : 0x7fffffff;
   const float w = entry >= 0 ? ws.entry_weight[entry] : 0.f;
-  int rank = 0, n = 0;
+  int rank = 0, n = 0, src_of_rank = 0;
   for (int j = 0; j < k; ++j) {
     const int ej = __shfl_sync(0xffffffffu, eid, j);
     const int vj = __shfl_sync(0xffffffffu, entry, j) >= 0;
     n += vj;
     rank += vj && (ej < eid);  // entries of a token name distinct experts
   }
-  float acc[8];
-#pragma unroll
-  for (int t = 0; t < 8; ++t) acc[t] = 0.f;
-  for (int i0 = 0; i0 < n; i0 += kBatch) {
-    uint4 v[kBatch];
-    float wi[kBatch];
-#pragma unroll
-    for (int u = 0; u < kBatch; ++u) {
-      const int i = i0 + u;
-      v[u] = make_uint4(0, 0, 0, 0);
-      wi[u] = 0.f;
-      if (i >= n) continue;
-      const unsigned who = __ballot_sync(0xffffffffu, entry >= 0 && rank == i);
-      const int src = __ffs(who) - 1;
-      const int ent = __shfl_sync(0xffffffffu, entry, src);
-      wi[u] = __shfl_sync(0xffffffffu, w, src);
-      if (yr) {
-        const float* f = yr + (static_cast<int64_t>(b) * k + src) * H + c0;
-        const float4 f0 = *reinterpret_cast<const float4*>(f), f1 = *reinterpret_cast<const float4*>(f + 4);
-        v[u] = make_uint4(bf16_bits_rne(f0.x) | (static_cast<uint32_t>(bf16_bits_rne(f0.y)) << 16),
-                          bf16_bits_rne(f0.z) | (static_cast<uint32_t>(bf16_bits_rne(f0.w)) << 16),
-                          bf16_bits_rne(f1.x) | (static_cast<uint32_t>(bf16_bits_rne(f1.y)) << 16),
-                          bf16_bits_rne(f1.z) | (static_cast<uint32_t>(bf16_bits_rne(f1.w)) << 16));
-      } else {
-        v[u] = ld_nc_v4(ws.y + static_cast<int64_t>(ent) * H + c0);
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < kBatch; ++u) {
-      if (i0 + u >= n) break;
-      const uint32_t p[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
-#pragma unroll
-      for (int t = 0; t < 8; ++t) {
-        const float y = bf16_to_f32(static_cast<uint16_t>(p[t >> 1] >> (16 * (t & 1))));
-        acc[t] = __fadd_rn(acc[t], __fmul_rn(y, wi[u]));
-      }
-    }
+  for (int j = 0; j < k; ++j) {
+    const int rj = __shfl_sync(0xffffffffu, rank, j);
+    const int vj = __shfl_sync(0xffffffffu, entry, j) >= 0;
+    if (vj && rj == lane) src_of_rank = j;
   }
-  const int64_t o = static_cast<int64_t>(b) * H + c0;
-  if (out_bf16) {
-    uint32_t q[4];
+  const int blocks = H / 256;
+  for (int g0 = 0; g0 < blocks; g0 += kG) {
+    float acc[kG][8];
 #pragma unroll
-    for (int t = 0; t < 4; ++t)
-      q[t] = static_cast<uint32_t>(bf16_bits_rne(acc[2 * t])) | (static_cast<uint32_t>(bf16_bits_rne(acc[2 * t + 1])) << 16);
-    *reinterpret_cast<uint4*>(static_cast<uint16_t*>(out) + o) = make_uint4(q[0], q[1], q[2], q[3]);
-  } else {
-    float4* f = reinterpret_cast<float4*>(static_cast<float*>(out) + o);
-    f[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
-    f[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+    for (int q = 0; q < kG; ++q)
+#pragma unroll
+      for (int t = 0; t < 8; ++t) acc[q][t] = 0.f;
+    for (int i0 = 0; i0 < n; i0 += 2) {
+      uint4 v[2][kG];
+      float wi[2];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int i = i0 + u;
+        const int src = __shfl_sync(0xffffffffu, src_of_rank, i < n ? i : 0);
+        const int ent = __shfl_sync(0xffffffffu, entry, src);
+        wi[u] = __shfl_sync(0xffffffffu, w, src);
+#pragma unroll
+        for (int q = 0; q < kG; ++q) {
+          v[u][q] = make_uint4(0, 0, 0, 0);
+          const int c0 = (g0 + q) * 256 + lane * 8;
+          if (i >= n || g0 + q >= blocks) continue;
+          if (yr) {
+            const float* f = yr + (static_cast<int64_t>(b) * k + src) * H + c0;
+            const float4 f0 = *reinterpret_cast<const float4*>(f), f1 = *reinterpret_cast<const float4*>(f + 4);
+            v[u][q] = make_uint4(bf16_bits_rne(f0.x) | (static_cast<uint32_t>(bf16_bits_rne(f0.y)) << 16),
+                                 bf16_bits_rne(f0.z) | (static_cast<uint32_t>(bf16_bits_rne(f0.w)) << 16),
+                                 bf16_bits_rne(f1.x) | (static_cast<uint32_t>(bf16_bits_rne(f1.y)) << 16),
+                                 bf16_bits_rne(f1.z) | (static_cast<uint32_t>(bf16_bits_rne(f1.w)) << 16));
+          } else {
+            v[u][q] = ld_nc_v4(ws.y + static_cast<int64_t>(ent) * H + c0);
+          }
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        if (i0 + u >= n) break;
+#pragma unroll
+        for (int q = 0; q < kG; ++q) {
+          const uint32_t p[4] = {v[u][q].x, v[u][q].y, v[u][q].z, v[u][q].w};
+#pragma unroll
+          for (int t = 0; t < 8; ++t) {
+            const float y = bf16_to_f32(static_cast<uint16_t>(p[t >> 1] >> (16 * (t & 1))));
+            acc[q][t] = __fadd_rn(acc[q][t], __fmul_rn(y, wi[u]));
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < kG; ++q) {
+      if (g0 + q >= blocks) break;
+      const int64_t o = static_cast<int64_t>(b) * H + (g0 + q) * 256 + lane * 8;
+      if (out_bf16) {
+        uint32_t r[4];
+#pragma unroll
+        for (int t = 0; t < 4; ++t)
+          r[t] = static_cast<uint32_t>(bf16_bits_rne(acc[q][2 * t])) |
+                 (static_cast<uint32_t>(bf16_bits_rne(acc[q][2 * t + 1])) << 16);
+        *reinterpret_cast<uint4*>(static_cast<uint16_t*>(out) + o) = make_uint4(r[0], r[1], r[2], r[3]);
+      } else {
+        float4* f = reinterpret_cast<float4*>(static_cast<float*>(out) + o);
+        f[0] = make_float4(acc[q][0], acc[q][1], acc[q][2], acc[q][3]);
+        f[1] = make_float4(acc[q][4], acc[q][5], acc[q][6], acc[q][7]);
+      }
+    }
   }
 }
 
@@ -491,9 +604,38 @@ __global__ void ep_wait_sources_kernel(uint8_t* own, int world) {
   pdl_trigger();
 }
 
-bool supported(int t) { return t == QK_TYPE_Q6_K || t == QK_TYPE_Q4_K; }
-// The down projection also takes Q8_0 (the real checkpoints' down type, checkpoints/q6.json).
-bool supported_down(int t) { return supported(t) || t == QK_TYPE_Q8_0; }
+// Gate and up: Q6_K, Q4_K or Q5_K (the Q4 checkpoint's gate/up types, checkpoints/q4.json).
+bool supported(int t) { return t == QK_TYPE_Q6_K || t == QK_TYPE_Q4_K || t == QK_TYPE_Q5_K; }
+// Down: those k-quants but Q5_K, Q8_0 (the Q6 checkpoint's down type, checkpoints/q6.json) or
+// Q5_1 (the Q4 checkpoint's, checkpoints/q4.json).
+bool supported_down(int t) {
+  return t == QK_TYPE_Q6_K || t == QK_TYPE_Q4_K || t == QK_TYPE_Q8_0 || t == QK_TYPE_Q5_1;
+}
+
+// One projection pass of `form` (0 narrow, 1 wide, 2 prefill) for weight type qtype.
+template <int MODE>
+int launch_pass(int qtype, int form, const UArgs& a, int sms, cudaStream_t st) {
+  auto go = [&](auto q) -> int {
+    constexpr QType Q = decltype(q)::value;
+    if (form == 2) return launch_prefill<Q, MODE>(a, sms, st);
+    if (form == 1) return launch_umma<Q, MODE, true>(a, sms, st);
+    return launch_umma<Q, MODE>(a, sms, st);
+  };
+  switch (qtype) {
+    case QK_TYPE_Q6_K: return go(std::integral_constant<QType, QType::Q6_K>{});
+    case QK_TYPE_Q4_K: return go(std::integral_constant<QType, QType::Q4_K>{});
+    case QK_TYPE_Q5_K:
+      if constexpr (MODE == kModeGateUp) return go(std::integral_constant<QType, QType::Q5_K>{});
+      break;
+    case QK_TYPE_Q8_0:
+      if constexpr (MODE == kModeDown) return go(std::integral_constant<QType, QType::Q8_0>{});
+      break;
+    case QK_TYPE_Q5_1:
+      if constexpr (MODE == kModeDown) return go(std::integral_constant<QType, QType::Q5_1>{});
+      break;
+  }
+  return set_error(QK_ERR_UNSUPPORTED_TYPE, "no projection pass for type %d", qtype);
+}
 
 }  // namespace
 }  // namespace qk
@@ -530,13 +672,14 @@ static int moe_forward_impl(const qk_moe_desc* desc, const uint8_t* gate, const 
   const qk_moe_desc& d = *desc;
   if (!supported(d.gate_type) || d.gate_type != d.up_type || !supported_down(d.down_type))
     return set_error(QK_ERR_UNSUPPORTED_TYPE,
-                     "expert types: gate and up both Q6_K or both Q4_K, down Q6_K, Q4_K or Q8_0 (got %d/%d/%d)",
+                     "expert types: gate and up both Q6_K, Q4_K or Q5_K, down Q6_K, Q4_K, Q8_0 or Q5_1 (got %d/%d/%d)",
                      d.gate_type, d.up_type, d.down_type);
   QK_REQUIRE(d.hidden > 0 && d.hidden % 256 == 0, "hidden must be a positive multiple of 256");
   // The gate/up tiles zero-pad their rows to 64; the down projection reads whole GGUF blocks
   // of intermediate (256 values for the k-quants, 32 for Q8_0).
-  QK_REQUIRE(d.intermediate > 0 && d.intermediate % (d.down_type == QK_TYPE_Q8_0 ? 32 : 256) == 0,
-             "intermediate must be a positive multiple of the down type's block (256, or 32 for Q8_0)");
+  const bool down32 = d.down_type == QK_TYPE_Q8_0 || d.down_type == QK_TYPE_Q5_1;  // 32-value blocks
+  QK_REQUIRE(d.intermediate > 0 && d.intermediate % (down32 ? 32 : 256) == 0,
+             "intermediate must be a positive multiple of the down type's block (256, or 32 for Q8_0 and Q5_1)");
   QK_REQUIRE(d.num_experts > 0 && d.num_experts <= 4096, "num_experts must be in [1, 4096]");
   QK_REQUIRE(d.top_k > 0 && d.top_k <= kMaxTopK, "top_k must be in [1, %d]", kMaxTopK);
   QK_REQUIRE(B >= 0, "batch must be non-negative");
@@ -560,7 +703,7 @@ static int moe_forward_impl(const qk_moe_desc* desc, const uint8_t* gate, const 
   };
 
   if (phase == kCombine) {
-    const cudaError_t e = launch_dependent(moe_combine_kernel, dim3((B * (d.hidden / 256) + 7) / 8), dim3(256), 0, st, ids, B, d.top_k,
+    const cudaError_t e = launch_dependent(moe_combine_kernel, dim3((B + 7) / 8), dim3(256), 0, st, ids, B, d.top_k,
                                            d.hidden, static_cast<int>(out_dtype == QK_OUT_BF16), out,
                                            static_cast<const float*>(yr), ws);
     if (e != cudaSuccess) return cuda_error(e, "moe_combine_kernel");
@@ -591,17 +734,37 @@ static int moe_forward_impl(const qk_moe_desc* desc, const uint8_t* gate, const 
   const bool prefill = routes >= QK_PREFILL_MIN_TOKENS * static_cast<size_t>(d.num_experts);
   const bool wide = !prefill && routes >= QK_WIDE_MIN_TOKENS * static_cast<size_t>(d.num_experts);
   const int ctok = prefill ? kPTok : wide ? kWideTok : kMaxTok;
-  // the route kernel stages all B * top_k routes in shared memory when they fit
   const size_t all_routes = static_cast<size_t>(B) * d.top_k;
-  const size_t route_smem =
-      (3 * static_cast<size_t>(d.num_experts) + 1) * 4 + (all_routes <= kStagedRoutes ? all_routes * 6 : 0);
-  int rc = allow_smem(reinterpret_cast<const void*>(moe_route_kernel), route_smem);
-  if (rc) return rc;
-  {
+  const int E = d.num_experts;
+  int rc;
+  if (all_routes <= static_cast<size_t>(kManyRoutes)) {
+    // one CTA; it stages all B * top_k routes in shared memory when they fit
+    const size_t route_smem = (6 * static_cast<size_t>(E) + 3) * 4 + (all_routes <= kStagedRoutes ? all_routes * 6 : 0);
+    rc = allow_smem(reinterpret_cast<const void*>(moe_route_kernel), route_smem);
+    if (rc) return rc;
     const cudaError_t e = launch_dependent(moe_route_kernel, dim3(1), dim3(1024), route_smem, st, ids, weights, B,
-                                           d.top_k, d.num_experts, d.first_expert, ctok, ws);
+                                           d.top_k, E, d.first_expert, ctok, ws);
     if (e != cudaSuccess) return cuda_error(e, "moe_route_kernel");
     count_launch(1);
+  } else {
+    // count, tables, place: about 4096 routes per CTA of the count and place kernels
+    int G = static_cast<int>((all_routes + 4095) / 4096);
+    if (G > kRouteCtas) G = kRouteCtas;
+    if (G > B) G = B;
+    const size_t hsmem = static_cast<size_t>(E) * 4, tsmem = (5 * static_cast<size_t>(E) + 3) * 4;
+    rc = allow_smem(reinterpret_cast<const void*>(moe_route_count_kernel), hsmem);
+    if (!rc) rc = allow_smem(reinterpret_cast<const void*>(moe_route_tables_kernel), tsmem);
+    if (!rc) rc = allow_smem(reinterpret_cast<const void*>(moe_route_place_kernel), hsmem);
+    if (rc) return rc;
+    cudaError_t e = launch_dependent(moe_route_count_kernel, dim3(G), dim3(kRouteThreads), hsmem, st, ids, weights, B,
+                                     d.top_k, E, d.first_expert, ws);
+    if (e != cudaSuccess) return cuda_error(e, "moe_route_count_kernel");
+    e = launch_dependent(moe_route_tables_kernel, dim3(1), dim3(1024), tsmem, st, G, E, ctok, ws);
+    if (e != cudaSuccess) return cuda_error(e, "moe_route_tables_kernel");
+    e = launch_dependent(moe_route_place_kernel, dim3(G), dim3(kRouteThreads), hsmem, st, ids, weights, B, d.top_k, E,
+                         d.first_expert, ws);
+    if (e != cudaSuccess) return cuda_error(e, "moe_route_place_kernel");
+    count_launch(3);
   }
 
   const int sms = sm_count();
@@ -615,7 +778,6 @@ static int moe_forward_impl(const qk_moe_desc* desc, const uint8_t* gate, const 
     count_launch(1);
   }
 
-  const bool q6 = d.gate_type == QK_TYPE_Q6_K;
   UArgs gu{};
   gu.wa = gate;
   gu.wb = up;
@@ -650,31 +812,15 @@ static int moe_forward_impl(const qk_moe_desc* desc, const uint8_t* gate, const 
   dn.entry_route = ws.entry_route;
   dn.nrows = d.hidden;
   mark(1);
+  const int form = prefill ? 2 : wide ? 1 : 0;
   if (prefill) {
     gu.items_per_chunk = (gu.tiles64 + 1) / 2;  // 128 rows of I (gate and up) per item
     dn.items_per_chunk = (dn.tiles64 + 3) / 4;  // 256 rows of H per item
-    rc = q6 ? launch_prefill<QType::Q6_K, kModeGateUp>(gu, sms, st) : launch_prefill<QType::Q4_K, kModeGateUp>(gu, sms, st);
-  } else if (wide) {
-    rc = q6 ? launch_umma<QType::Q6_K, kModeGateUp, true>(gu, sms, st)
-            : launch_umma<QType::Q4_K, kModeGateUp, true>(gu, sms, st);
-  } else {
-    rc = q6 ? launch_umma<QType::Q6_K, kModeGateUp>(gu, sms, st) : launch_umma<QType::Q4_K, kModeGateUp>(gu, sms, st);
   }
+  rc = launch_pass<kModeGateUp>(d.gate_type, form, gu, sms, st);
   if (rc) return rc;
   mark(2);
-  if (prefill) {
-    if (d.down_type == QK_TYPE_Q8_0) rc = launch_prefill<QType::Q8_0, kModeDown>(dn, sms, st);
-    else if (d.down_type == QK_TYPE_Q6_K) rc = launch_prefill<QType::Q6_K, kModeDown>(dn, sms, st);
-    else rc = launch_prefill<QType::Q4_K, kModeDown>(dn, sms, st);
-  } else if (wide) {
-    if (d.down_type == QK_TYPE_Q8_0) rc = launch_umma<QType::Q8_0, kModeDown, true>(dn, sms, st);
-    else if (d.down_type == QK_TYPE_Q6_K) rc = launch_umma<QType::Q6_K, kModeDown, true>(dn, sms, st);
-    else rc = launch_umma<QType::Q4_K, kModeDown, true>(dn, sms, st);
-  } else {
-    if (d.down_type == QK_TYPE_Q8_0) rc = launch_umma<QType::Q8_0, kModeDown>(dn, sms, st);
-    else if (d.down_type == QK_TYPE_Q6_K) rc = launch_umma<QType::Q6_K, kModeDown>(dn, sms, st);
-    else rc = launch_umma<QType::Q4_K, kModeDown>(dn, sms, st);
-  }
+  rc = launch_pass<kModeDown>(d.down_type, form, dn, sms, st);
   if (rc) return rc;
   mark(3);
   if (phase == kPartial) return QK_OK;
@@ -690,7 +836,7 @@ static int moe_forward_impl(const qk_moe_desc* desc, const uint8_t* gate, const 
     return QK_OK;
   }
   {
-    const cudaError_t e = launch_dependent(moe_combine_kernel, dim3((B * (d.hidden / 256) + 7) / 8), dim3(256), 0, st, ids, B, d.top_k,
+    const cudaError_t e = launch_dependent(moe_combine_kernel, dim3((B + 7) / 8), dim3(256), 0, st, ids, B, d.top_k,
                                            d.hidden, static_cast<int>(out_dtype == QK_OUT_BF16), out,
                                            static_cast<const float*>(nullptr), ws);
     if (e != cudaSuccess) return cuda_error(e, "moe_combine_kernel");

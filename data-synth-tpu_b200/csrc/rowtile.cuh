@@ -36,7 +36,7 @@
 
 namespace qk {
 
-enum class QType { Q6_K = 14, Q4_K = 12, Q8_0 = 8 };
+enum class QType { Q6_K = 14, Q4_K = 12, Q8_0 = 8, Q5_K = 13, Q5_1 = 7 };
 
 constexpr int kTileRows = 64;
 
@@ -276,6 +276,169 @@ struct HalfTile<QType::Q8_0> {
 #pragma unroll
         for (int i = 0; i < 4; ++i)
           code4<kExact, false>(r.w[8 * jj + 4 * half16 + i] ^ 0x80808080u, d, 128.f, 0.f, out[2 * i], out[2 * i + 1]);
+        emit(jj * 16 + half16 * 8, out);
+      }
+    }
+  }
+};
+
+// Q5_K (gguf_quant.py:115-157: v = (d * sc) * q - dmin * m, q = low nibble | high bit << 4):
+// the GGUF block bytes unchanged, as [chunk][row][16 B] - chunk 0 holds d, dmin and the 12
+// packed scale bytes (as Q4_K), chunks 1-2 the 32 high-bit bytes (bit j of byte l is the fifth
+// bit of value 32 j + l), chunks 3-10 the 128 nibble bytes (value 32 j + l in byte
+// 32 (j / 2) + l, nibble j % 2). Half h: chunk 0, chunks 1-2 and nibble chunks 3 + 4h .. 6 + 4h.
+template <>
+struct HalfTile<QType::Q5_K> {
+  static constexpr int kBlockBytes = 176;
+  static constexpr int kChunks = 11;
+  static constexpr int kBytes = kTileRows * kBlockBytes;  // 11264
+
+  struct Regs {
+    uint32_t hd[4];  // d | dmin << 16, then the 12 packed scale bytes
+    uint32_t qh[8];  // the 32 high-bit bytes
+    uint32_t w[16];  // nibble bytes of sub-blocks 4h .. 4h + 3
+  };
+
+  __device__ __forceinline__ static void clear(Regs& r) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) r.hd[i] = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) r.qh[i] = 0;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) r.w[i] = 0;
+  }
+
+  template <int h>
+  __device__ __forceinline__ static void load(Regs& r, const uint8_t* tile, int row) {
+    const uint4 v = lds128(tile + row * 16);
+    r.hd[0] = v.x;
+    r.hd[1] = v.y;
+    r.hd[2] = v.z;
+    r.hd[3] = v.w;
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      const uint4 u = lds128(tile + ((1 + c) * kTileRows + row) * 16);
+      r.qh[4 * c] = u.x;
+      r.qh[4 * c + 1] = u.y;
+      r.qh[4 * c + 2] = u.z;
+      r.qh[4 * c + 3] = u.w;
+    }
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const uint4 u = lds128(tile + ((3 + 4 * h + c) * kTileRows + row) * 16);
+      r.w[4 * c] = u.x;
+      r.w[4 * c + 1] = u.y;
+      r.w[4 * c + 2] = u.z;
+      r.w[4 * c + 3] = u.w;
+    }
+  }
+
+  __device__ __forceinline__ static int scale_byte(const Regs& r, int i) {
+    return static_cast<int>((r.hd[1 + (i >> 2)] >> (8 * (i & 3))) & 0xffu);
+  }
+
+  template <bool kExact, int h, typename Emit>
+  __device__ __forceinline__ static void decode(const Regs& r, Emit&& emit) {
+    const float d = f16_to_f32(static_cast<uint16_t>(r.hd[0] & 0xffffu));
+    const float dmin = f16_to_f32(static_cast<uint16_t>(r.hd[0] >> 16));
+#pragma unroll
+    for (int jj = 0; jj < 4; ++jj) {
+      const int j = 4 * h + jj;  // sub-block of 32 values
+      int sc, m;
+      if (j < 4) {
+        sc = scale_byte(r, j) & 63;
+        m = scale_byte(r, j + 4) & 63;
+      } else {
+        sc = (scale_byte(r, j + 4) & 15) | ((scale_byte(r, j - 4) >> 6) << 4);
+        m = (scale_byte(r, j + 4) >> 4) | ((scale_byte(r, j) >> 6) << 4);
+      }
+      const float ds = __fmul_rn(d, static_cast<float>(sc));
+      const float dm = __fmul_rn(dmin, static_cast<float>(m));
+#pragma unroll
+      for (int half16 = 0; half16 < 2; ++half16) {
+        uint32_t out[8];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int wi = 4 * half16 + i;  // bytes 4 wi .. 4 wi + 3 of the sub-block's 32
+          const uint32_t lo = (r.w[8 * (jj >> 1) + wi] >> (4 * (j & 1))) & 0x0f0f0f0fu;
+          const uint32_t hi = ((r.qh[wi] >> j) & 0x01010101u) << 4;
+          code4<kExact, true>(lo | hi, ds, 0.f, dm, out[2 * i], out[2 * i + 1]);
+        }
+        emit(jj * 16 + half16 * 8, out);
+      }
+    }
+  }
+};
+
+// Q5_1 (quant.py:31-55: v = d * q + m, q = low nibble | high bit << 4, 32 values per 24-byte
+// block) in super-blocks of 256 values = 8 GGUF blocks, 192 bytes per row: chunk h holds the
+// (d, m) FP16 pairs of blocks 4h .. 4h + 3, chunk 2 + h their 32-bit high-bit words, chunks
+// 4 .. 11 the 16 nibble bytes of blocks 0 .. 7 (value p < 16 in the low nibble of byte p,
+// value 16 + p in its high nibble). Blocks past the row's end are zero and decode to zeros.
+// Half h: chunks h, 2 + h and 4 + 4h .. 7 + 4h.
+template <>
+struct HalfTile<QType::Q5_1> {
+  static constexpr int kBlockBytes = 192;
+  static constexpr int kChunks = 12;
+  static constexpr int kBytes = kTileRows * kBlockBytes;  // 12288
+
+  struct Regs {
+    uint32_t dm[4];  // d | m << 16 of the half's 4 blocks
+    uint32_t qh[4];  // their high-bit words
+    uint32_t w[16];  // their nibble bytes
+  };
+
+  __device__ __forceinline__ static void clear(Regs& r) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) r.dm[i] = r.qh[i] = 0;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) r.w[i] = 0;
+  }
+
+  template <int h>
+  __device__ __forceinline__ static void load(Regs& r, const uint8_t* tile, int row) {
+    const uint4 a = lds128(tile + (h * kTileRows + row) * 16);
+    const uint4 b = lds128(tile + ((2 + h) * kTileRows + row) * 16);
+    r.dm[0] = a.x;
+    r.dm[1] = a.y;
+    r.dm[2] = a.z;
+    r.dm[3] = a.w;
+    r.qh[0] = b.x;
+    r.qh[1] = b.y;
+    r.qh[2] = b.z;
+    r.qh[3] = b.w;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const uint4 u = lds128(tile + ((4 + 4 * h + c) * kTileRows + row) * 16);
+      r.w[4 * c] = u.x;
+      r.w[4 * c + 1] = u.y;
+      r.w[4 * c + 2] = u.z;
+      r.w[4 * c + 3] = u.w;
+    }
+  }
+
+  // The 4 high bits (bits n .. n + 3 of `qh`) of four codes, one per byte, at bit 4: the
+  // multiply spreads bit i of the nibble to bit 8 i + 4 (the partial products do not overlap).
+  __device__ __forceinline__ static uint32_t high4(uint32_t qh, int n) {
+    return (((qh >> n) & 15u) * 0x02040810u) & 0x10101010u;
+  }
+
+  // v = d * q + m: fma(1024 + q, d, -1024 d) is d * q exactly (both factors have at most 11
+  // significant bits), then one FP32 addition of m, as the reference rounds it.
+  template <bool kExact, int h, typename Emit>
+  __device__ __forceinline__ static void decode(const Regs& r, Emit&& emit) {
+#pragma unroll
+    for (int jj = 0; jj < 4; ++jj) {  // GGUF block 4h + jj of the super-block
+      const float d = f16_to_f32(static_cast<uint16_t>(r.dm[jj] & 0xffffu));
+      const float m = f16_to_f32(static_cast<uint16_t>(r.dm[jj] >> 16));
+#pragma unroll
+      for (int half16 = 0; half16 < 2; ++half16) {  // values 16 half16 .. + 15 of the block
+        uint32_t out[8];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const uint32_t lo = (r.w[4 * jj + i] >> (4 * half16)) & 0x0f0f0f0fu;
+          code4<kExact, true>(lo | high4(r.qh[jj], 16 * half16 + 4 * i), d, 0.f, -m, out[2 * i], out[2 * i + 1]);
+        }
         emit(jj * 16 + half16 * 8, out);
       }
     }

@@ -205,6 +205,135 @@ struct QuarterRegs<QType::Q8_0> {
   }
 };
 
+template <>
+struct QuarterRegs<QType::Q5_K> {
+  uint32_t hd[4];     // d | dmin << 16, then the 12 packed scale bytes
+  uint32_t qh[8];     // the 32 high-bit bytes
+  uint32_t w[2][8];   // nibble bytes of sub-blocks 4h + 2g and 4h + 2g + 1 (32 bytes)
+  __device__ __forceinline__ void load(const uint8_t* tile, int row, int g) {
+    const uint4 v = lds128(tile + row * 16);
+    hd[0] = v.x;
+    hd[1] = v.y;
+    hd[2] = v.z;
+    hd[3] = v.w;
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      const uint4 u = lds128(tile + ((1 + c) * kTileRows + row) * 16);
+      qh[4 * c] = u.x;
+      qh[4 * c + 1] = u.y;
+      qh[4 * c + 2] = u.z;
+      qh[4 * c + 3] = u.w;
+    }
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const uint4 u = lds128(tile + ((3 + 4 * h + 2 * g + c) * kTileRows + row) * 16);
+        w[h][4 * c] = u.x;
+        w[h][4 * c + 1] = u.y;
+        w[h][4 * c + 2] = u.z;
+        w[h][4 * c + 3] = u.w;
+      }
+  }
+  __device__ __forceinline__ void clear() {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) hd[i] = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) qh[i] = 0;
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) w[h][i] = 0;
+  }
+  __device__ __forceinline__ int scale_byte(int i) const {
+    return static_cast<int>((hd[1 + (i >> 2)] >> (8 * (i & 3))) & 0xffu);
+  }
+  template <int h, typename Emit>
+  __device__ __forceinline__ void decode(int g, Emit&& emit) const {
+    const float d = f16_to_f32(static_cast<uint16_t>(hd[0] & 0xffffu));
+    const float dmin = f16_to_f32(static_cast<uint16_t>(hd[0] >> 16));
+#pragma unroll
+    for (int s = 0; s < 2; ++s) {
+      const int j = 4 * h + 2 * g + s;  // sub-block of 32 values (gguf_quant.py:118-151)
+      int sc, m;
+      if (j < 4) {
+        sc = scale_byte(j) & 63;
+        m = scale_byte(j + 4) & 63;
+      } else {
+        sc = (scale_byte(j + 4) & 15) | ((scale_byte(j - 4) >> 6) << 4);
+        m = (scale_byte(j + 4) >> 4) | ((scale_byte(j) >> 6) << 4);
+      }
+      const float ds = __fmul_rn(d, static_cast<float>(sc));
+      const float dm = __fmul_rn(dmin, static_cast<float>(m));
+#pragma unroll
+      for (int half16 = 0; half16 < 2; ++half16) {
+        uint32_t out[8];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int wi = 4 * half16 + i;
+          const uint32_t lo = (w[h][wi] >> (4 * s)) & 0x0f0f0f0fu;
+          const uint32_t hi = ((qh[wi] >> j) & 0x01010101u) << 4;
+          code4<false, true>(lo | hi, ds, 0.f, dm, out[2 * i], out[2 * i + 1]);
+        }
+        emit(32 * s + 16 * half16, out);
+      }
+    }
+  }
+};
+
+template <>
+struct QuarterRegs<QType::Q5_1> {
+  uint32_t dm[2][2];   // d | m << 16 of GGUF blocks 4h + 2g, 4h + 2g + 1
+  uint32_t qh[2][2];   // their high-bit words
+  uint32_t w[2][8];    // their nibble bytes
+  __device__ __forceinline__ void load(const uint8_t* tile, int row, int g) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const uint2 a = *reinterpret_cast<const uint2*>(tile + (h * kTileRows + row) * 16 + 8 * g);
+      const uint2 b = *reinterpret_cast<const uint2*>(tile + ((2 + h) * kTileRows + row) * 16 + 8 * g);
+      dm[h][0] = a.x;
+      dm[h][1] = a.y;
+      qh[h][0] = b.x;
+      qh[h][1] = b.y;
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const uint4 u = lds128(tile + ((4 + 4 * h + 2 * g + c) * kTileRows + row) * 16);
+        w[h][4 * c] = u.x;
+        w[h][4 * c + 1] = u.y;
+        w[h][4 * c + 2] = u.z;
+        w[h][4 * c + 3] = u.w;
+      }
+    }
+  }
+  __device__ __forceinline__ void clear() {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      dm[h][0] = dm[h][1] = qh[h][0] = qh[h][1] = 0;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) w[h][i] = 0;
+    }
+  }
+  template <int h, typename Emit>
+  __device__ __forceinline__ void decode(int g, Emit&& emit) const {
+#pragma unroll
+    for (int s = 0; s < 2; ++s) {  // GGUF block 4h + 2g + s (quant.py:31-55)
+      const float d = f16_to_f32(static_cast<uint16_t>(dm[h][s] & 0xffffu));
+      const float m = f16_to_f32(static_cast<uint16_t>(dm[h][s] >> 16));
+#pragma unroll
+      for (int half16 = 0; half16 < 2; ++half16) {
+        uint32_t out[8];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const uint32_t lo = (w[h][4 * s + i] >> (4 * half16)) & 0x0f0f0f0fu;
+          code4<false, true>(lo | HalfTile<QType::Q5_1>::high4(qh[h][s], 16 * half16 + 4 * i), d, 0.f, -m,
+                             out[2 * i], out[2 * i + 1]);
+        }
+        emit(32 * s + 16 * half16, out);
+      }
+    }
+  }
+};
+
 template <QType QT>
 struct PCfg {
   static constexpr int kTile = HalfTile<QT>::kBytes;   // one 64-row tile of one K block

@@ -228,12 +228,13 @@ def expert_parallel(
         if dist.get_world_size(group) % tensor_parallel:
             raise ValueError("Tensor parallel size must divide the device count")
     types = tuple(normalize_qtype(t) for t in (gate_type, up_type, down_type))
-    if types[0] != types[1] or types[0] not in ("Q6_K", "Q4_K") or types[2] not in ("Q6_K", "Q4_K", "Q8_0"):
-        raise ValueError("expert kernels take gate and up both Q6_K or both Q4_K, down Q6_K, Q4_K or Q8_0")
+    if (types[0] != types[1] or types[0] not in ("Q6_K", "Q4_K", "Q5_K")
+            or types[2] not in ("Q6_K", "Q4_K", "Q8_0", "Q5_1")):
+        raise ValueError("expert kernels take gate and up both Q6_K, Q4_K or Q5_K, down Q6_K, Q4_K, Q8_0 or Q5_1")
     if compute == "int8_q8" and types[2] == "Q8_0":
         raise ValueError("the int8_q8 expert policy (W8A8 Q8_0 dot) is not built; use compute='bf16'")
     # the down projection reads whole GGUF blocks of intermediate (gate/up tiles pad rows to 64)
-    step = 32 if types[2] == "Q8_0" else 256
+    step = 32 if types[2] in ("Q8_0", "Q5_1") else 256
     if tensor_parallel > 1 and ((intermediate // tensor_parallel) % step or intermediate % tensor_parallel):
         raise ValueError("Tensor slices must contain whole down quantization blocks")
     if hidden % 256 or intermediate % step:

@@ -3,7 +3,7 @@
 Mirrors ``kaggle/packed_q6``: ``pack_q6``/``unpack_q6`` (``layout.py:49-108``) and
 ``q6_matmul`` (``kernel.py:98-148``), with this build's tile layout (64 rows x 256
 values per tile, see ``csrc/rowtile.cuh``) instead of the TPU SoA tiles. ``pack_rows``
-and ``quant_matmul`` are the type-generic forms (Q6_K, Q4_K, Q8_0).
+and ``quant_matmul`` are the type-generic forms (Q6_K, Q4_K, Q5_K, Q8_0, Q5_1).
 """
 
 from dataclasses import dataclass
@@ -14,7 +14,7 @@ import torch
 from . import _lib
 from .quant import BLOCK_LAYOUTS, GGML_TYPE, normalize_qtype
 
-TILED_TYPES = ("Q6_K", "Q4_K", "Q8_0")
+TILED_TYPES = ("Q6_K", "Q4_K", "Q5_K", "Q8_0", "Q5_1")
 
 
 @dataclass(frozen=True)
@@ -26,7 +26,7 @@ class PackedWeights:
 
     @property
     def input_blocks(self):
-        """GGUF blocks per row (256 values for the k-quants, 32 for Q8_0)."""
+        """GGUF blocks per row (256 values for the k-quants, 32 for Q8_0 and Q5_1)."""
         values = BLOCK_LAYOUTS[self.qtype][0]
         return (self.input_features + values - 1) // values
 

@@ -11,7 +11,8 @@ import numpy as np
 import torch
 
 from . import _lib
-from .packed import TILED_TYPES, tiled_bytes
+from .packed import TILED_TYPES as EXPERT_TYPES  # gate/up: the k-quants; down: Q6_K, Q4_K, Q8_0, Q5_1
+from .packed import tiled_bytes
 from .quant import BLOCK_LAYOUTS, GGML_TYPE, normalize_qtype
 
 
@@ -72,8 +73,8 @@ def put_expert_bytes(raw, kind, qtype, hidden, intermediate, *, rank=0, world=1,
     ``tensor_rank``'s slice of the intermediate channels (``tensor_slice``), tiled as a
     matrix of ``intermediate / tensor_parallel`` channels."""
     name = normalize_qtype(qtype)
-    if name not in TILED_TYPES:
-        raise ValueError(f"expert kernels take {TILED_TYPES}; got {name}")
+    if name not in EXPERT_TYPES:
+        raise ValueError(f"expert kernels take {EXPERT_TYPES}; got {name}")
     values, size = BLOCK_LAYOUTS[name]
     first, count = local_range(len(raw), rank, world)
     device = torch.device(device or "cuda")

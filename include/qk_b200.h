@@ -74,8 +74,8 @@ int qk_dequantize_rows(const uint8_t* raw, int qtype, int64_t rows, int64_t row_
 /* ---- tiled repack (lossless) -------------------------------------------------
  * Replaces packed_q6/layout.py:49-108 pack_q6 / unpack_q6: a byte-only repack of raw
  * GGUF rows into the B200 tile layout (64 rows x 256 values per tile, rows padded to
- * 64) read by qk_quant_gemm and qk_moe_forward. Q6_K, Q4_K and Q8_0 (eight 32-value
- * blocks per 256-value tile column).
+ * 64) read by qk_quant_gemm and qk_moe_forward. Q6_K, Q4_K, Q5_K, and Q8_0 and Q5_1
+ * (eight 32-value blocks per 256-value tile column).
  * bad_scales (device int32, may be NULL): receives the count of non-finite FP16 block
  * scales (pack_q6 rejects those, layout.py:67-69); the host wrapper raises on > 0. */
 int64_t qk_tiled_bytes(int qtype, int64_t rows, int64_t row_width);
@@ -98,7 +98,7 @@ int qk_dequantize_tiled(const uint8_t* tiled, int qtype, int64_t rows, int64_t r
 /* ---- packed projection -------------------------------------------------------
  * Replaces packed_q6/kernel.py:98-148 q6_matmul(x, packed, scales, output_features):
  * out[M, N] (FP32) = bf16 x[M, K] @ bf16(decode(W))[N, K]^T, FP32 accumulation on the
- * tcgen05 tensor core. w_tiled: qk_repack_rows output for W (Q6_K, Q4_K or Q8_0). Ragged M, N
+ * tcgen05 tensor core. w_tiled: qk_repack_rows output for W (any tiled type). Ragged M, N
  * and K allowed. The workspace holds x repacked into the tensor core's operand tiles and
  * the FP32 partial sum of every 256-value K block, added in K order at the end. */
 size_t qk_quant_gemm_workspace_bytes(int64_t M, int64_t K, int64_t N);
@@ -129,10 +129,11 @@ int qk_router_topk_logits(const float* logits, const uint8_t* active, int T, int
  * out: BF16 [B, hidden] (out_dtype QK_OUT_BF16), or the FP32 sum over this rank's
  * experts (QK_OUT_F32) that an expert-parallel all-reduce adds (experts.py:130-131). */
 typedef struct qk_moe_desc {
-  int gate_type, up_type, down_type; /* gate == up: Q6_K or Q4_K; down: Q6_K, Q4_K
-                                        or Q8_0 (the reference checkpoints' down) */
+  int gate_type, up_type, down_type; /* gate == up: Q6_K, Q4_K or Q5_K; down: Q6_K,
+                                        Q4_K, Q8_0 or Q5_1 (the reference
+                                        checkpoints' types, checkpoints/q4.json, q6.json) */
   int hidden;                        /* multiple of 256                          */
-  int intermediate;                  /* multiple of the down block: 256, 32 (Q8_0) */
+  int intermediate;                  /* multiple of the down block: 256, or 32 (Q8_0, Q5_1) */
   int num_experts;                   /* experts held by this rank                */
   int first_expert;                  /* global id of this rank's first expert    */
   int top_k;                         /* routes per token                         */

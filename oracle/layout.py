@@ -12,7 +12,12 @@ tensor-core kernels reads chunk ``c`` of its row ``r`` at ``(c*64 + r)*16``.
 Q4_K blocks keep their GGUF bytes. Q8_0 (32-value blocks of an FP16 scale and 32 int8
 codes) groups the 8 blocks of a 256-value column into one 272-byte super-block: chunk 0 is
 the 8 scales (``[block][2 B]``), chunks 1..16 the 256 codes in position order; blocks past
-the row's end are zero. Q6_K blocks re-pack the 6-bit codes losslessly: sub-block
+the row's end are zero. Q5_K blocks keep their GGUF bytes (11 chunks: d, dmin and scales;
+the 32 high-bit bytes; the 128 nibble bytes). Q5_1 (32-value blocks of FP16 d and m, a 32-bit
+high-bit word and 16 nibble bytes) groups 8 blocks into one 192-byte super-block: chunks 0-1
+the (d, m) pairs of blocks 0-3 and 4-7, chunks 2-3 their high-bit words, chunks 4..11 the
+blocks' nibble bytes; blocks past the row's end are zero. Q6_K blocks re-pack the 6-bit
+codes losslessly: sub-block
 ``j`` (values ``16j .. 16j+15``) becomes three little-endian words ``W0, W1, W2`` at bytes
 ``12j .. 12j+11``; byte ``i`` of ``Wn`` holds code ``4n + i`` in bits 0..5 and bits
 ``2n .. 2n+1`` of code ``12 + i`` in bits 6..7. Bytes 192..207 are the sub-scales.
@@ -21,8 +26,9 @@ the row's end are zero. Q6_K blocks re-pack the 6-bit codes losslessly: sub-bloc
 import numpy as np
 
 TILE_ROWS = 64
-BLOCK_BYTES = {"Q6_K": 210, "Q4_K": 144, "Q8_0": 272}  # Q8_0: the 8-block super-block
-CHUNKS = {"Q6_K": 13, "Q4_K": 9, "Q8_0": 17}
+# Q8_0 and Q5_1: the 8-block super-block
+BLOCK_BYTES = {"Q6_K": 210, "Q4_K": 144, "Q8_0": 272, "Q5_K": 176, "Q5_1": 192}
+CHUNKS = {"Q6_K": 13, "Q4_K": 9, "Q8_0": 17, "Q5_K": 11, "Q5_1": 12}
 TILE_BYTES = {q: TILE_ROWS * b for q, b in BLOCK_BYTES.items()}
 
 
@@ -101,13 +107,39 @@ def _q8_blocks(sup, nblk32):
     return out.reshape(rows, nsup * 8, 34)[:, :nblk32]
 
 
+def _q51_super(raw):
+    """Q5_1 ``uint8[rows, nblk32, 24]`` -> super-blocks ``uint8[rows, ceil(nblk32 / 8), 192]``."""
+    rows, nblk32, _ = raw.shape
+    nsup = (nblk32 + 7) // 8
+    full = np.zeros((rows, nsup * 8, 24), np.uint8)
+    full[:, :nblk32] = raw
+    full = full.reshape(rows, nsup, 8, 24)
+    return np.concatenate([full[..., :4].reshape(rows, nsup, 32), full[..., 4:8].reshape(rows, nsup, 32),
+                           full[..., 8:].reshape(rows, nsup, 128)], -1)
+
+
+def _q51_blocks(sup, nblk32):
+    """Inverse of :func:`_q51_super`."""
+    rows, nsup, _ = sup.shape
+    out = np.zeros((rows, nsup, 8, 24), np.uint8)
+    out[..., :4] = sup[..., :32].reshape(rows, nsup, 8, 4)
+    out[..., 4:8] = sup[..., 32:64].reshape(rows, nsup, 8, 4)
+    out[..., 8:] = sup[..., 64:].reshape(rows, nsup, 8, 16)
+    return out.reshape(rows, nsup * 8, 24)[:, :nblk32]
+
+
 def tile(raw, qtype):
-    """``uint8[rows, nblk, bpb]`` (Q8_0: ``[rows, nblk32, 34]``) -> flat tiled bytes."""
+    """``uint8[rows, nblk, bpb]`` (Q8_0: ``[rows, nblk32, 34]``, Q5_1: ``[rows, nblk32, 24]``)
+    -> flat tiled bytes."""
     raw = np.asarray(raw, np.uint8)
     if qtype == "Q8_0":
         if raw.shape[-1] != 34:
             raise ValueError("Q8_0 blocks contain 34 bytes")
         raw = _q8_super(raw)
+    elif qtype == "Q5_1":
+        if raw.shape[-1] != 24:
+            raise ValueError("Q5_1 blocks contain 24 bytes")
+        raw = _q51_super(raw)
     rows, nblk, size = raw.shape
     if size != BLOCK_BYTES[qtype]:
         raise ValueError(f"{qtype} blocks contain {BLOCK_BYTES[qtype]} bytes")
@@ -139,6 +171,8 @@ def untile(tiled, qtype, rows, row_width):
     raw = out.transpose(0, 2, 1, 3).reshape(-1, nblk, size)[:rows]
     if qtype == "Q8_0":
         return _q8_blocks(raw, (row_width + 31) // 32)
+    if qtype == "Q5_1":
+        return _q51_blocks(raw, (row_width + 31) // 32)
     return unrepack_q6_codes(raw) if qtype == "Q6_K" else raw
 
 

@@ -37,10 +37,10 @@ def test_tiled_sizes_match_layout_statement():
     from qk_b200 import _lib
 
     lib = _lib.load()
-    for qtype, code in (("Q6_K", 14), ("Q4_K", 12), ("Q8_0", 8)):
+    for qtype, code in (("Q6_K", 14), ("Q4_K", 12), ("Q8_0", 8), ("Q5_K", 13), ("Q5_1", 7)):
         for rows, width in ((1, 1), (17, 263), (512, 2048), (2048, 512)):
             assert lib.qk_tiled_bytes(code, rows, width) == layout.tiled_bytes(qtype, rows, width)
-    assert lib.qk_tiled_bytes(13, 16, 256) == -1  # Q5_K: no tiled layout
+    assert lib.qk_tiled_bytes(6, 16, 256) == -1  # Q5_0: no tiled layout
 
 
 def test_argument_validation_happens_before_any_launch():
@@ -51,7 +51,7 @@ def test_argument_validation_happens_before_any_launch():
     assert lib.qk_dequantize_rows(null, 99, 1, 256, 0, null, null) == _lib.QK_ERR_UNSUPPORTED_TYPE
     assert "unsupported" in _lib.last_error()
     assert lib.qk_dequantize_rows(null, 14, 1, 0, 0, null, null) == _lib.QK_ERR_INVALID_ARGUMENT
-    assert lib.qk_quant_gemm(null, 1, 256, null, 13, 16, null, null, 0, null) == _lib.QK_ERR_UNSUPPORTED_TYPE
+    assert lib.qk_quant_gemm(null, 1, 256, null, 6, 16, null, null, 0, null) == _lib.QK_ERR_UNSUPPORTED_TYPE
     assert lib.qk_quant_gemm(ctypes.c_void_p(16), 4, 256, ctypes.c_void_p(16), 14, 16, ctypes.c_void_p(16), null, 0, null) == _lib.QK_ERR_WORKSPACE
     assert lib.qk_quant_gemm_workspace_bytes(65, 263, 7) == 80 * 512 * 2 + 2 * 65 * 7 * 4
     assert lib.qk_router_topk_logits(null, null, 1, 4, 5, null, null, null, null) == _lib.QK_ERR_INVALID_ARGUMENT
@@ -59,6 +59,12 @@ def test_argument_validation_happens_before_any_launch():
     assert lib.qk_moe_forward(ctypes.byref(desc), *([null] * 6), 1, 1, null, null, 0, null) == _lib.QK_ERR_UNSUPPORTED_TYPE
     desc = _lib.MoeDesc(14, 14, 13, 2048, 512, 64, 0, 4)  # Q5_K down
     assert lib.qk_moe_forward(ctypes.byref(desc), *([null] * 6), 1, 1, null, null, 0, null) == _lib.QK_ERR_UNSUPPORTED_TYPE
+    desc = _lib.MoeDesc(7, 7, 7, 2048, 512, 64, 0, 4)  # Q5_1 gate/up
+    assert lib.qk_moe_forward(ctypes.byref(desc), *([null] * 6), 1, 1, null, null, 0, null) == _lib.QK_ERR_UNSUPPORTED_TYPE
+    desc = _lib.MoeDesc(13, 13, 7, 2560, 640, 64, 0, 4)  # the Q4 checkpoint's Q5_K / Q5_1 mix
+    assert lib.qk_moe_workspace_bytes(ctypes.byref(desc), 8) > 0
+    assert lib.qk_moe_forward(ctypes.byref(desc), *([ctypes.c_void_p(16)] * 6), 1, 1,
+                              ctypes.c_void_p(16), null, 0, null) == _lib.QK_ERR_WORKSPACE
     desc = _lib.MoeDesc(14, 14, 14, 2048, 96, 64, 0, 4)  # a k-quant down needs I % 256
     assert lib.qk_moe_forward(ctypes.byref(desc), *([null] * 6), 1, 1, null, null, 0, null) == _lib.QK_ERR_INVALID_ARGUMENT
     desc = _lib.MoeDesc(14, 14, 8, 2048, 96, 64, 0, 4)   # a Q8_0 down takes I % 32

@@ -7,7 +7,7 @@ import pytest
 
 from oracle import gguf, layout, moe
 from oracle.precision import bf16_round
-from util import bf16_tensor, to_f32
+from util import bf16_tensor, random_blocks, to_f32
 
 pytestmark = pytest.mark.gpu
 
@@ -92,6 +92,43 @@ def test_q8_0_repack_is_lossless_and_fragment_decode_is_bit_exact(cuda_device, r
         got = to_f32(dequantize_packed(packed, dtype))
         np.testing.assert_array_equal(got.view(np.uint32), expected.view(np.uint32))
         np.testing.assert_array_equal(to_f32(dequantize_packed(packed, dtype, fused=True)), expected)
+
+
+@pytest.mark.parametrize("qtype,rows,width", [
+    ("Q5_K", 1, 256), ("Q5_K", 17, 512), ("Q5_K", 65, 263), ("Q5_K", 512, 2048),
+    ("Q5_1", 1, 32), ("Q5_1", 17, 96), ("Q5_1", 65, 263), ("Q5_1", 130, 2048), ("Q5_1", 64, 640)])
+def test_q5_repack_is_lossless_and_fragment_decode_is_bit_exact(cuda_device, qtype, rows, width):
+    """Q5_K (GGUF bytes, 11 chunks) and Q5_1 (8-block super-blocks, ragged last columns zero)
+    tiles: byte-equal to the oracle's layout, lossless, and decoded bit-exactly by the
+    fragment decoders the expert kernels run."""
+    import torch
+
+    from qk_b200.packed import dequantize_packed, pack_rows, unpack_rows
+
+    raw = random_blocks(np.random.default_rng(rows * 3 + width), rows, width, qtype)
+    packed = pack_rows(raw, width, qtype, cuda_device)
+    assert packed.data.numel() == layout.tiled_bytes(qtype, rows, width)
+    np.testing.assert_array_equal(packed.data.cpu().numpy(), layout.tile(raw, qtype))
+    np.testing.assert_array_equal(unpack_rows(packed).cpu().numpy(), raw)
+    expected = bf16_round(gguf.dequantize_rows(raw, qtype, width))
+    for dtype in (torch.bfloat16, torch.float32):
+        got = to_f32(dequantize_packed(packed, dtype))
+        np.testing.assert_array_equal(got.view(np.uint32), expected.view(np.uint32))
+        np.testing.assert_array_equal(to_f32(dequantize_packed(packed, dtype, fused=True)), expected)
+
+
+@pytest.mark.parametrize("qtype,n,k", [("Q5_K", 200, 512), ("Q5_1", 130, 640)])
+def test_q5_packed_projection(cuda_device, qtype, n, k):
+    """The dense packed projection over Q5_K / Q5_1 tiles against an FP64 dot of the decoded
+    BF16 weights (the projection tolerance of test_packed_q6.py:77-81)."""
+    from qk_b200.packed import pack_rows, quant_matmul
+
+    rng = np.random.default_rng(n + k)
+    raw = random_blocks(rng, n, k, qtype)
+    x = bf16_round(rng.normal(size=(9, k)).astype(np.float32))
+    got = quant_matmul(bf16_tensor(x, cuda_device), pack_rows(raw, k, qtype, cuda_device)).cpu().numpy()
+    w = bf16_round(gguf.dequantize_rows(raw, qtype, k)).astype(np.float64)
+    np.testing.assert_allclose(got, x.astype(np.float64) @ w.T, rtol=2e-5, atol=2e-4)
 
 
 @pytest.mark.parametrize("scale", [np.inf, -np.inf, np.nan])

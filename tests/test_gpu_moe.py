@@ -5,7 +5,7 @@ import pytest
 
 from oracle import gguf, moe
 from oracle.precision import bf16_round
-from util import bf16_tensor, rel_err, to_f32
+from util import bf16_tensor, random_blocks, rel_err, to_f32
 
 pytestmark = pytest.mark.gpu
 
@@ -14,11 +14,17 @@ LAYER_TOL = 1e-2
 
 
 def make_experts(rng, count, hidden, intermediate, qtype, down_type=None):
+    """Expert bytes: N(0, 0.02) weights encoded to Q6_K / Q4_K / Q8_0, or random blocks with
+    finite scales for Q5_K / Q5_1 (no encoder of those types is needed)."""
     raw = {}
     for kind, (rows, width) in (("gate", (intermediate, hidden)), ("up", (intermediate, hidden)),
                                 ("down", (hidden, intermediate))):
+        t = (down_type or qtype) if kind == "down" else qtype
+        if t in ("Q5_K", "Q5_1"):
+            raw[kind] = random_blocks(rng, count * rows, width, t).reshape(count, -1)
+            continue
         w = rng.normal(0, 0.02, (count, rows, width)).astype(np.float32)
-        raw[kind] = gguf.encode(w, (down_type or qtype) if kind == "down" else qtype).reshape(count, -1)
+        raw[kind] = gguf.encode(w, t).reshape(count, -1)
     return raw
 
 
@@ -151,6 +157,59 @@ def test_prefill_form_chunks_of_256_tokens(cuda_device, qtype, down_type, hidden
     np.testing.assert_array_equal(got[5::11], 0)
 
 
+@pytest.mark.parametrize("batch", [300, 1200])
+def test_top1_routes_zero_rows_and_fp32_output(cuda_device, batch):
+    """Top-1 routes (config 2's routing): rows of tokens with a zero weight or an expert of
+    another rank are zero; 300 tokens on 8 experts take the narrow form, 1200 the wide one.
+    The FP32 output (the expert-parallel partial) rounds to the BF16 one bit for bit."""
+    import torch
+
+    hidden, intermediate, count = 512, 256, 8
+    rng = np.random.default_rng(batch)
+    raw = make_experts(rng, count, hidden, intermediate, "Q6_K")
+    ids = rng.integers(0, count, (batch, 1)).astype(np.int32)
+    ids[7::17, 0] = count + 2        # another rank's expert
+    weights = bf16_round(rng.uniform(0.05, 1.0, (batch, 1)).astype(np.float32))
+    weights[3::19] = 0
+    x = rng.normal(size=(batch, hidden)).astype(np.float32)
+    got, fn, dev = run_layer(cuda_device, raw, "Q6_K", hidden, intermediate, x, ids, weights)
+    expected = moe.expert_ffn(raw["gate"], raw["up"], raw["down"], x, ids, weights, gate_type="Q6_K",
+                              up_type="Q6_K", down_type="Q6_K", hidden=hidden, intermediate=intermediate)
+    mx, l2 = rel_err(got, expected)
+    assert mx < LAYER_TOL and l2 < 2e-3, (mx, l2)
+    np.testing.assert_array_equal(got[7::17], 0)
+    np.testing.assert_array_equal(got[3::19], 0)
+    ids_t = torch.from_numpy(ids).to(cuda_device)
+    f32 = fn._run(dev["gate"], dev["up"], dev["down"], bf16_tensor(x, cuda_device), ids_t,
+                  bf16_tensor(weights, cuda_device), 0, torch.float32)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(bf16_round(f32.cpu().numpy()), got)
+
+
+@pytest.mark.parametrize("count,k,batch", [(6, 3, 6000), (512, 8, 2100)])
+def test_many_routes_metadata_over_many_ctas(cuda_device, count, k, batch):
+    """More than 16384 routes: the routing metadata comes from the count, tables and place
+    kernels over many CTAs instead of one CTA. 6 experts x 3000 routes take the prefill form,
+    512 experts x about 33 routes the narrow one; merged duplicate routes, zero weights and ids
+    outside the rank's experts are in the same call."""
+    hidden, intermediate = 256, 256
+    rng = np.random.default_rng(count + batch)
+    raw = make_experts(rng, count, hidden, intermediate, "Q6_K")
+    ids = np.argsort(rng.random((batch, count)), axis=1)[:, :k].astype(np.int32)
+    ids[1:40, 1] = ids[1:40, 0]      # duplicate routes merge
+    ids[50:60, 2] = count + 3        # not an expert of this rank
+    weights = bf16_round(rng.uniform(0.05, 1.0, (batch, k)).astype(np.float32))
+    weights[5::13] = 0
+    x = rng.normal(size=(batch, hidden)).astype(np.float32)
+    assert batch * k > 16384
+    got, _, _ = run_layer(cuda_device, raw, "Q6_K", hidden, intermediate, x, ids, weights)
+    expected = moe.expert_ffn(raw["gate"], raw["up"], raw["down"], x, ids, weights, gate_type="Q6_K",
+                              up_type="Q6_K", down_type="Q6_K", hidden=hidden, intermediate=intermediate)
+    mx, l2 = rel_err(got, expected)
+    assert mx < LAYER_TOL and l2 < 2e-3, (mx, l2)
+    np.testing.assert_array_equal(got[5::13], 0)
+
+
 @pytest.mark.parametrize("qtype,intermediate,batch", [
     ("Q6_K", 512, 8), ("Q6_K", 640, 8), ("Q4_K", 96, 5), ("Q6_K", 640, 700)])
 def test_q8_0_down_projection(cuda_device, qtype, intermediate, batch):
@@ -166,6 +225,26 @@ def test_q8_0_down_projection(cuda_device, qtype, intermediate, batch):
     got, _, _ = run_layer(cuda_device, raw, qtype, hidden, intermediate, x, ids, weights, down_type="Q8_0")
     expected = moe.expert_ffn(raw["gate"], raw["up"], raw["down"], x, ids, weights, gate_type=qtype,
                               up_type=qtype, down_type="Q8_0", hidden=hidden, intermediate=intermediate)
+    mx, l2 = rel_err(got, expected)
+    assert mx < LAYER_TOL and l2 < 2e-3, (mx, l2)
+
+
+@pytest.mark.parametrize("qtype,down_type,hidden,intermediate,batch", [
+    ("Q4_K", "Q5_1", 512, 640, 8), ("Q5_K", "Q5_1", 512, 640, 8), ("Q5_K", "Q6_K", 512, 512, 300),
+    ("Q4_K", "Q5_1", 256, 96, 700), ("Q5_K", "Q5_1", 512, 640, 1600)])
+def test_q5_expert_types(cuda_device, qtype, down_type, hidden, intermediate, batch):
+    """The reference Q4 checkpoint's expert types (checkpoints/q4.json: gate/up Q4_K or Q5_K,
+    down Q5_1, intermediate 640): 8 tokens (narrow form), 300 and 700 (wide), 1600 on 8 experts
+    top-2 (prefill form); I = 96 pads the gate/up tile and the down's K block."""
+    count, k = 8, 2
+    rng = np.random.default_rng(intermediate + batch)
+    raw = make_experts(rng, count, hidden, intermediate, qtype, down_type)
+    ids = np.argsort(rng.random((batch, count)), axis=1)[:, :k].astype(np.int32)
+    weights = bf16_round(rng.uniform(0.05, 1.0, (batch, k)).astype(np.float32))
+    x = rng.normal(size=(batch, hidden)).astype(np.float32)
+    got, _, _ = run_layer(cuda_device, raw, qtype, hidden, intermediate, x, ids, weights, down_type=down_type)
+    expected = moe.expert_ffn(raw["gate"], raw["up"], raw["down"], x, ids, weights, gate_type=qtype,
+                              up_type=qtype, down_type=down_type, hidden=hidden, intermediate=intermediate)
     mx, l2 = rel_err(got, expected)
     assert mx < LAYER_TOL and l2 < 2e-3, (mx, l2)
 

@@ -167,6 +167,31 @@ def test_q8_0_tiles_round_trip_and_place_codes_in_position_order(rows, width):
     np.testing.assert_array_equal(codes, raw[r, j, 2:])
 
 
+@pytest.mark.parametrize("qtype,rows,width", [("Q5_K", 48, 512), ("Q5_K", 70, 300), ("Q5_1", 1, 32),
+                                             ("Q5_1", 70, 288), ("Q5_1", 64, 640)])
+def test_q5_tiles_round_trip_and_place_chunks(qtype, rows, width):
+    """Q5_K tiles hold the GGUF bytes as [chunk][row][16 B]; Q5_1 super-blocks put each block's
+    (d, m), high-bit word and nibbles into chunks h, 2 + h and 4 + block of its half h."""
+    from util import random_blocks
+
+    raw = random_blocks(np.random.default_rng(rows + width), rows, width, qtype)
+    tiled = layout.tile(raw, qtype)
+    assert tiled.size == layout.tiled_bytes(qtype, rows, width)
+    np.testing.assert_array_equal(layout.untile(tiled, qtype, rows, width), raw)
+    nsup = (width + 255) // 256
+    c = layout.CHUNKS[qtype]
+    body = tiled.reshape(-1, nsup, c, 64, 16)  # [row tile][column][chunk][row][16 B]
+    r, j = rows - 1, raw.shape[1] - 1
+    if qtype == "Q5_K":
+        np.testing.assert_array_equal(body[r // 64, j, :, r % 64].reshape(-1), raw[r, j])
+    else:
+        blk, h = j % 8, (j % 8) // 4
+        col = body[r // 64, j // 8, :, r % 64]
+        np.testing.assert_array_equal(col[h, 4 * (blk % 4) : 4 * (blk % 4) + 4], raw[r, j, :4])
+        np.testing.assert_array_equal(col[2 + h, 4 * (blk % 4) : 4 * (blk % 4) + 4], raw[r, j, 4:8])
+        np.testing.assert_array_equal(col[4 + blk], raw[r, j, 8:])
+
+
 def test_soa_restatement_inverts_the_reference_pack_q6(golden):
     """``oracle.layout.soa_to_rows`` against the reference's own ``pack_q6`` planes."""
     from oracle.layout import soa_to_rows

@@ -26,3 +26,24 @@ def rel_err(actual, expected):
     e = np.asarray(expected, np.float64)
     scale = max(np.max(np.abs(e)), 1e-30)
     return float(np.max(np.abs(a - e)) / scale), float(np.linalg.norm(a - e) / max(np.linalg.norm(e), 1e-30))
+
+
+def random_blocks(rng, rows, width, qtype):
+    """Random GGUF blocks ``uint8[rows, blocks, bytes]`` of a Q5_K or Q5_1 row of ``width``
+    values with finite FP16 scales (no encoder of these types is needed: any code bytes are
+    legal). Q5_K: d in [1e-4, 2e-4), dmin in [0, 1e-4); Q5_1: d in [1e-3, 2e-3), m in
+    [-0.03, 0)."""
+    values, size = {"Q5_K": (256, 176), "Q5_1": (32, 24)}[qtype]
+    blocks = (width + values - 1) // values
+    raw = rng.integers(0, 256, (rows, blocks, size), dtype=np.uint8)
+
+    def f16(lo, hi):
+        return rng.uniform(lo, hi, (rows, blocks)).astype("<f2").view(np.uint8).reshape(rows, blocks, 2)
+
+    if qtype == "Q5_K":
+        raw[..., 0:2] = f16(1e-4, 2e-4)
+        raw[..., 2:4] = f16(0, 1e-4)
+    else:
+        raw[..., 0:2] = f16(1e-3, 2e-3)
+        raw[..., 2:4] = f16(-0.03, 0)
+    return raw
