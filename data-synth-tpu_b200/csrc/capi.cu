@@ -67,6 +67,18 @@ int allow_smem(const void* kernel, size_t bytes) {
   return QK_OK;
 }
 
+void* tensor_map_encoder() {
+  static void* fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      p = nullptr;
+    return p;
+  }();
+  return fn;
+}
+
 }  // namespace qk
 
 extern "C" {

@@ -57,6 +57,8 @@ cudaError_t launch_dependent(void (*kernel)(KArgs...), dim3 grid, dim3 block, si
 }
 
 int sm_count();  // SMs of the current device (cached per device)
+// The driver's cuTensorMapEncodeTiled, looked up once through the runtime (NULL if absent).
+void* tensor_map_encoder();
 // Opt a kernel into `bytes` of dynamic shared memory on the current device (once).
 int allow_smem(const void* kernel, size_t bytes);
 

@@ -7,6 +7,7 @@
 // 32 rows, zero padding for ragged M and K, as the reference zero-pads, kernel.py:139-140);
 // rows at or beyond N are not stored.
 #include "common.cuh"
+#include "umma_i8.cuh"
 #include "umma_proj.cuh"
 
 namespace qk {
@@ -129,6 +130,64 @@ int qk_quant_gemm(const uint16_t* x, int64_t M, int64_t K, const uint8_t* w_tile
   if (e != cudaSuccess) return cuda_error(e, "reduce_blocks_kernel");
   count_launch(1);
   return QK_OK;
+}
+
+// ---- W8A8 projection (qwen38_tpu/compute.py:20-34, q8_matmul) ----
+// Workspace: the BF16 activation tiles of x, the int8 codes [chunks x 32 rows x K256] and the
+// FP32 scales [chunks x 32 rows x K256 / 32] (K256: K rounded up to 256).
+static size_t q8mm_parts(int64_t M, int64_t K, size_t* codes_off, size_t* scales_off) {
+  const int64_t rows = (M + kMaxTok - 1) / kMaxTok * kMaxTok, k256 = (K + 255) / 256 * 256;
+  const size_t xt = (xt_bytes(M, K) + 255) & ~size_t(255);
+  const size_t codes = (static_cast<size_t>(rows * k256) + 255) & ~size_t(255);
+  *codes_off = xt;
+  *scales_off = xt + codes;
+  return xt + codes + static_cast<size_t>(rows * (k256 / 32)) * 4;
+}
+
+size_t qk_q8_matmul_workspace_bytes(int64_t M, int64_t K, int64_t N) {
+  if (M <= 0 || K <= 0 || N <= 0) return 0;
+  size_t c, s;
+  return q8mm_parts(M, K, &c, &s);
+}
+
+int qk_q8_matmul(const uint16_t* x, int64_t M, int64_t K, const uint8_t* w_tiled, int64_t N, int out_dtype,
+                 void* out, void* workspace, size_t workspace_bytes, qk_stream_t stream) {
+  QK_REQUIRE(M >= 0 && K > 0 && N > 0, "x must be a nonempty [M,K] BF16 array");
+  QK_REQUIRE(K % 32 == 0, "Q8_0 input features must be a multiple of 32");
+  QK_REQUIRE(M < (1 << 30) && K < (1 << 20) && N < (1 << 24), "dimension too large");
+  QK_REQUIRE(out_dtype == QK_OUT_F32 || out_dtype == QK_OUT_BF16, "out_dtype must be F32 or BF16");
+  if (M == 0) return QK_OK;
+  QK_REQUIRE(x && w_tiled && out, "null pointer");
+  size_t codes_off, scales_off;
+  const size_t need = q8mm_parts(M, K, &codes_off, &scales_off);
+  if (!workspace || workspace_bytes < need)
+    return set_error(QK_ERR_WORKSPACE, "workspace needs %zu bytes, got %zu", need, workspace_bytes);
+  QK_REQUIRE((reinterpret_cast<uintptr_t>(workspace) & 255) == 0, "workspace must be 256-byte aligned");
+  QK_REQUIRE((reinterpret_cast<uintptr_t>(w_tiled) & 15) == 0, "tiled weights must be 16-byte aligned");
+  cudaStream_t st = as_stream(stream);
+  const int sms = sm_count();
+  const int nkb = static_cast<int>((K + 255) / 256);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  {
+    const int64_t total = dense_tile_rows(M) * nkb * 32;
+    int64_t g = (total + 255) / 256;
+    if (g > sms * 8) g = sms * 8;
+    pack_x_kernel<<<static_cast<unsigned>(g), 256, 0, st>>>(x, static_cast<int>(M), static_cast<int>(K), nkb, ws);
+    QK_LAUNCHED("pack_x_kernel");
+  }
+  I8Args a{};
+  a.ht = ws;
+  a.qx = reinterpret_cast<int8_t*>(ws + codes_off);
+  a.qs = reinterpret_cast<float*>(ws + scales_off);
+  a.nkb = nkb;
+  a.ngroups = static_cast<int>(K / 32);
+  a.items_per_chunk = static_cast<int>((N + 127) / 128);
+  a.tiles64 = 0;  // one matrix: tile 2p of item p
+  a.nrows = static_cast<int>(N);
+  a.dense_m = static_cast<int>(M);
+  a.out = out;
+  a.out_bf16 = out_dtype == QK_OUT_BF16;
+  return launch_w8a8(a, w_tiled, (N + kTileRows - 1) / kTileRows, sms, st);
 }
 
 }  // extern "C"

@@ -18,10 +18,12 @@
 //  5. combine  - per token, FP32 sum of f32(y) * f32(route) over its experts in ascending
 //                expert order (the reference's accumulation order, experts.py:129), then
 //                BF16 (experts.py:131), or the FP32 partial sum for an EP all-reduce.
+#include <cstring>
 #include <type_traits>
 
 #include "common.cuh"
 #include "ep_p2p.cuh"
+#include "umma_i8.cuh"
 #include "umma_prefill.cuh"
 #include "umma_proj.cuh"
 
@@ -53,6 +55,8 @@ struct Workspace {
   uint8_t* ht;            // down activation tiles [rows_max x I bf16]
   uint16_t* y;            // [B k, H]
   int32_t* hist;          // [kRouteCtas][E] entries per (route CTA, expert), many-route calls only
+  int8_t* qx;             // int8_q8 down: activation codes [rows_max x I] (W8A8 calls only)
+  float* qs;              // int8_q8 down: activation scales [rows_max x I / 32]
 };
 
 inline size_t align256(size_t n) { return (n + 255) & ~size_t(255); }
@@ -103,6 +107,10 @@ size_t layout(const qk_moe_desc& d, int max_tokens, uint8_t* base, Workspace* ws
   uint8_t* ht = take(rows * ((d.intermediate + 255) / 256 * 256) * 2);  // whole 256-value K blocks
   uint8_t* y = take(R * d.hidden * 2);
   uint8_t* hist = take(R > kManyRoutes ? kRouteCtas * E * 4 : 0);
+  const bool w8a8 = d.compute == QK_COMPUTE_INT8_Q8 && d.down_type == QK_TYPE_Q8_0;
+  const size_t ipad = (d.intermediate + 255) / 256 * 256;
+  uint8_t* qx = take(w8a8 ? rows * ipad : 0);
+  uint8_t* qs = take(w8a8 ? rows * (ipad / 32) * 4 : 0);
   if (ws) {
     ws->meta = reinterpret_cast<MoeMeta*>(meta);
     ws->counts = reinterpret_cast<int32_t*>(counts);
@@ -119,6 +127,8 @@ size_t layout(const qk_moe_desc& d, int max_tokens, uint8_t* base, Workspace* ws
     ws->ht = ht;
     ws->y = reinterpret_cast<uint16_t*>(y);
     ws->hist = reinterpret_cast<int32_t*>(hist);
+    ws->qx = reinterpret_cast<int8_t*>(qx);
+    ws->qs = reinterpret_cast<float*>(qs);
   }
   return off;
 }
@@ -637,6 +647,28 @@ int launch_pass(int qtype, int form, const UArgs& a, int sms, cudaStream_t st) {
   return set_error(QK_ERR_UNSUPPORTED_TYPE, "no projection pass for type %d", qtype);
 }
 
+// The int8_q8 down pass (umma_i8.cuh): `dn` carries the chunk tables and outputs of the BF16
+// down pass it replaces.
+int launch_w8a8_down(const qk_moe_desc& d, const UArgs& dn, const Workspace& ws, const uint8_t* down, int sms,
+                     cudaStream_t st) {
+  I8Args a{};
+  a.ht = dn.xt;
+  a.qx = ws.qx;
+  a.qs = ws.qs;
+  a.nkb = dn.nkb;
+  a.ngroups = d.intermediate / 32;
+  a.items_per_chunk = d.hidden / 128;
+  a.tiles64 = dn.tiles64;
+  a.n_chunks_p = dn.n_chunks_p;
+  a.chunk_rec = dn.chunk_rec;
+  a.y = dn.y;
+  a.yr = dn.yr;
+  a.entry_route = dn.entry_route;
+  a.nrows = d.hidden;
+  a.status = dn.status;
+  return launch_w8a8(a, down, static_cast<int64_t>(d.num_experts) * dn.tiles64, sms, st);
+}
+
 }  // namespace
 }  // namespace qk
 
@@ -682,6 +714,7 @@ static int moe_forward_impl(const qk_moe_desc* desc, const uint8_t* gate, const 
              "intermediate must be a positive multiple of the down type's block (256, or 32 for Q8_0 and Q5_1)");
   QK_REQUIRE(d.num_experts > 0 && d.num_experts <= 4096, "num_experts must be in [1, 4096]");
   QK_REQUIRE(d.top_k > 0 && d.top_k <= kMaxTopK, "top_k must be in [1, %d]", kMaxTopK);
+  QK_REQUIRE(d.compute == QK_COMPUTE_BF16 || d.compute == QK_COMPUTE_INT8_Q8, "Unknown expert compute policy");
   QK_REQUIRE(B >= 0, "batch must be non-negative");
   QK_REQUIRE(out_dtype == QK_OUT_F32 || out_dtype == QK_OUT_BF16, "out_dtype must be F32 or BF16");
   if (B == 0) return QK_OK;
@@ -731,8 +764,10 @@ static int moe_forward_impl(const qk_moe_desc* desc, const uint8_t* gate, const 
 #ifndef QK_PREFILL_MIN_TOKENS
 #define QK_PREFILL_MIN_TOKENS 192
 #endif
-  const bool prefill = routes >= QK_PREFILL_MIN_TOKENS * static_cast<size_t>(d.num_experts);
-  const bool wide = !prefill && routes >= QK_WIDE_MIN_TOKENS * static_cast<size_t>(d.num_experts);
+  // The int8_q8 policy's W8A8 down pass takes token chunks of at most 32 (the narrow form).
+  const bool w8a8 = d.compute == QK_COMPUTE_INT8_Q8 && d.down_type == QK_TYPE_Q8_0;
+  const bool prefill = !w8a8 && routes >= QK_PREFILL_MIN_TOKENS * static_cast<size_t>(d.num_experts);
+  const bool wide = !w8a8 && !prefill && routes >= QK_WIDE_MIN_TOKENS * static_cast<size_t>(d.num_experts);
   const int ctok = prefill ? kPTok : wide ? kWideTok : kMaxTok;
   const size_t all_routes = static_cast<size_t>(B) * d.top_k;
   const int E = d.num_experts;
@@ -820,7 +855,7 @@ static int moe_forward_impl(const qk_moe_desc* desc, const uint8_t* gate, const 
   rc = launch_pass<kModeGateUp>(d.gate_type, form, gu, sms, st);
   if (rc) return rc;
   mark(2);
-  rc = launch_pass<kModeDown>(d.down_type, form, dn, sms, st);
+  rc = w8a8 ? launch_w8a8_down(d, dn, ws, down, sms, st) : launch_pass<kModeDown>(d.down_type, form, dn, sms, st);
   if (rc) return rc;
   mark(3);
   if (phase == kPartial) return QK_OK;

@@ -45,7 +45,11 @@ class MoeDesc(ctypes.Structure):
         ("num_experts", _i),
         ("first_expert", _i),
         ("top_k", _i),
+        ("compute", _i),
     ]
+
+
+QK_COMPUTE_BF16, QK_COMPUTE_INT8_Q8 = 0, 1
 
 
 # name -> (restype, argtypes)
@@ -61,6 +65,8 @@ SIGNATURES = {
     "qk_q6_soa_to_rows": (_i, [_p, _p, _i64, _i64, _p, _p]),
     "qk_quant_gemm_workspace_bytes": (_sz, [_i64, _i64, _i64]),
     "qk_quant_gemm": (_i, [_p, _i64, _i64, _p, _i, _i64, _p, _p, _sz, _p]),
+    "qk_q8_matmul_workspace_bytes": (_sz, [_i64, _i64, _i64]),
+    "qk_q8_matmul": (_i, [_p, _i64, _i64, _p, _i64, _i, _p, _p, _sz, _p]),
     "qk_router_topk": (_i, [_p, _p, _p, _i, _i, _i, _i, _p, _p, _p, _p]),
     "qk_router_topk_logits": (_i, [_p, _p, _i, _i, _i, _p, _p, _p, _p]),
     "qk_moe_workspace_bytes": (_sz, [ctypes.POINTER(MoeDesc), _i]),

@@ -23,12 +23,14 @@ EXPERT_ROW_TILE = 128
 
 
 class ExpertFFN:
-    def __init__(self, group, gate_type, up_type, down_type, hidden, intermediate, tensor_parallel=1):
+    def __init__(self, group, gate_type, up_type, down_type, hidden, intermediate, tensor_parallel=1,
+                 compute="bf16"):
         self.group = group
         self.types = tuple(normalize_qtype(t) for t in (gate_type, up_type, down_type))
         self.hidden = hidden
         self.intermediate = intermediate
         self.tensor_parallel = tensor_parallel
+        self.compute = compute
         self._workspace = {}
         self.tensor_group = self.expert_group = None
         self.expert_rank = 0
@@ -70,11 +72,12 @@ class ExpertFFN:
         return _lib.MoeDesc(
             GGML_TYPE[self.types[0]], GGML_TYPE[self.types[1]], GGML_TYPE[self.types[2]],
             self.hidden, self.intermediate // self.tensor_parallel, num_experts, first_expert, top_k,
+            _lib.QK_COMPUTE_INT8_Q8 if self.compute == "int8_q8" else _lib.QK_COMPUTE_BF16,
         )
 
     def workspace(self, desc, batch, device):
         need = int(_lib.load().qk_moe_workspace_bytes(desc, batch))
-        key = (device.index, desc.num_experts, desc.top_k)
+        key = (device.index, desc.num_experts, desc.top_k, desc.compute)
         buf = self._workspace.get(key)
         if buf is None or buf.numel() < need:
             buf = torch.empty(max(need, 1), dtype=torch.uint8, device=device)
@@ -202,10 +205,11 @@ def expert_parallel(
 ):
     """Return the routed FFN for this process's experts; see the module docstring.
 
-    ``compute`` "int8_q8" only changes Q8_0 projections in the reference (its W8A8 dot,
-    qwen38_tpu/compute.py:20-34); with Q6_K/Q4_K projections it computes exactly like
-    "bf16". A Q8_0 down projection runs the "bf16" form (dequantise, BF16 dot); "int8_q8"
-    with a Q8_0 down is refused rather than computed differently. ``row_tile`` and
+    ``compute`` "int8_q8" only changes Q8_0 projections, as in the reference
+    (qwen38_tpu/experts.py:85-99): a Q8_0 down projection becomes the W8A8 integer dot of
+    qwen38_tpu/compute.py:20-34 (activations quantised per 32 values, tcgen05 kind::i8 MMAs,
+    FP32 scaled sum over the groups; the call then uses 32-token chunks); the k-quant gate
+    and up projections compute exactly like "bf16". ``row_tile`` and
     ``group_size`` shape the reference's XLA loops and do not change results; they are
     validated and otherwise unused (the kernels tile rows by 32 and stream experts).
     """
@@ -231,15 +235,13 @@ def expert_parallel(
     if (types[0] != types[1] or types[0] not in ("Q6_K", "Q4_K", "Q5_K")
             or types[2] not in ("Q6_K", "Q4_K", "Q8_0", "Q5_1")):
         raise ValueError("expert kernels take gate and up both Q6_K, Q4_K or Q5_K, down Q6_K, Q4_K, Q8_0 or Q5_1")
-    if compute == "int8_q8" and types[2] == "Q8_0":
-        raise ValueError("the int8_q8 expert policy (W8A8 Q8_0 dot) is not built; use compute='bf16'")
     # the down projection reads whole GGUF blocks of intermediate (gate/up tiles pad rows to 64)
     step = 32 if types[2] in ("Q8_0", "Q5_1") else 256
     if tensor_parallel > 1 and ((intermediate // tensor_parallel) % step or intermediate % tensor_parallel):
         raise ValueError("Tensor slices must contain whole down quantization blocks")
     if hidden % 256 or intermediate % step:
         raise ValueError(f"hidden must be a multiple of 256 and intermediate a multiple of {step}")
-    return ExpertFFN(group, *types, hidden, intermediate, tensor_parallel)
+    return ExpertFFN(group, *types, hidden, intermediate, tensor_parallel, compute)
 
 
 __all__ = ["ExpertFFN", "expert_parallel", "expert_shape", "EXPERT_ROW_TILE"]

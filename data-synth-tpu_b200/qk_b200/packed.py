@@ -213,6 +213,28 @@ def quant_matmul(x, packed):
     return out
 
 
+def q8_matmul(x, packed, *, output_dtype=None):
+    """``qwen38_tpu/compute.py:20-34`` ``q8_matmul(x, packed, *, output_dtype=None)``: the W8A8
+    integer dot over Q8_0 weights (tiles of :func:`pack_rows`), on the tcgen05 tensor core
+    (kind::i8). Returns ``[M, N]`` in ``output_dtype`` (default: x's dtype, BF16)."""
+    if not isinstance(x, torch.Tensor) or x.dim() != 2 or min(x.shape) < 1 or x.dtype != torch.bfloat16:
+        raise ValueError("x must be a nonempty [M,K] BF16 array")
+    if packed.qtype != "Q8_0" or x.shape[1] != packed.input_features:
+        raise ValueError("Packed dtype/shape does not match projection dimensions")
+    dtype = torch.bfloat16 if output_dtype is None else output_dtype
+    if dtype not in (torch.bfloat16, torch.float32):
+        raise ValueError("output_dtype must be BF16 or FP32")
+    x = x.contiguous()
+    out = torch.empty((x.shape[0], packed.output_features), dtype=dtype, device=x.device)
+    need = int(_lib.load().qk_q8_matmul_workspace_bytes(x.shape[0], x.shape[1], packed.output_features))
+    ws = _workspace(x.device, need)
+    with torch.cuda.device(x.device):
+        _lib.call("qk_q8_matmul", _lib.ptr(x), x.shape[0], x.shape[1], _lib.ptr(packed.data),
+                  packed.output_features, _lib.QK_OUT_BF16 if dtype == torch.bfloat16 else _lib.QK_OUT_F32,
+                  _lib.ptr(out), _lib.ptr(ws), ws.numel(), _lib.stream_handle(x.device))
+    return out
+
+
 def q6_matmul(x, packed, scales=None, *, output_features, batch_tile=8):
     """``packed_q6.kernel.q6_matmul`` contract: FP32 ``[M, N]``; validates like the reference.
 

@@ -106,6 +106,19 @@ int qk_quant_gemm(const uint16_t* x, int64_t M, int64_t K, const uint8_t* w_tile
                   int64_t N, float* out, void* workspace, size_t workspace_bytes,
                   qk_stream_t stream);
 
+/* ---- W8A8 projection ------------------------------------------------------------
+ * Replaces qwen38_tpu/compute.py:20-34 q8_matmul(x, packed, output_dtype): the int8_q8
+ * policy's integer dot over Q8_0 weights. Per row of x and 32-value group the activations
+ * are quantised to int8 (scale max|x| / 127, rint, clip +-127), the int32 dot with the
+ * weight codes runs on the tcgen05 tensor core (kind::i8), and the groups are added in order
+ * as (f32(partial) * act_scale) * weight_scale (compute.py:52-65). x: BF16 [M, K], K a
+ * multiple of 32; w_tiled: qk_repack_rows output of Q8_0 W [N, K]; out: [M, N] FP32 or BF16
+ * (out_dtype). The workspace (256-byte aligned) holds x's operand tiles, codes and scales. */
+size_t qk_q8_matmul_workspace_bytes(int64_t M, int64_t K, int64_t N);
+int qk_q8_matmul(const uint16_t* x, int64_t M, int64_t K, const uint8_t* w_tiled, int64_t N,
+                 int out_dtype, void* out, void* workspace, size_t workspace_bytes,
+                 qk_stream_t stream);
+
 /* ---- router ------------------------------------------------------------------
  * Replaces the router of qwen38_tpu/math.py:277-281 (routes_and_shared):
  * probs = softmax(f32(x) @ f32(Wr)^T); (w, ids) = top_k(probs, k) (ties: lower index);
@@ -137,7 +150,12 @@ typedef struct qk_moe_desc {
   int num_experts;                   /* experts held by this rank                */
   int first_expert;                  /* global id of this rank's first expert    */
   int top_k;                         /* routes per token                         */
+  int compute;                       /* QK_COMPUTE_BF16 (0), or QK_COMPUTE_INT8_Q8: a
+                                        Q8_0 down projection as the W8A8 integer dot of
+                                        qwen38_tpu/compute.py:20-34 (tcgen05 kind::i8);
+                                        other types compute as BF16 (experts.py:85-99) */
 } qk_moe_desc;
+enum { QK_COMPUTE_BF16 = 0, QK_COMPUTE_INT8_Q8 = 1 };
 
 size_t qk_moe_workspace_bytes(const qk_moe_desc* desc, int max_tokens);
 int qk_moe_forward(const qk_moe_desc* desc, const uint8_t* gate, const uint8_t* up,

@@ -8,6 +8,9 @@
   ascending expert order, ``y = bf16(bf16(silu(bf16(x Wg^T)) * bf16(x Wu^T)) Wd^T)``,
   ``out += f32(y) * f32(route)``; finally ``bf16(out)``.
 * ``projection`` restates ``packed_q6/reference.py:44-48`` (``projection_reference``).
+* ``q8_matmul`` restates the W8A8 integer dot ``numpy_q8_matmul``
+  (``kaggle/qwen38_tpu/compute.py:52-65``), the ``int8_q8`` expert policy's Q8_0 projection
+  (``compute.py:20-34``, used by ``experts.py:85-99``).
 """
 
 import numpy as np
@@ -66,11 +69,38 @@ def _bpb(qtype):
     return BLOCK_LAYOUTS[qtype][1]
 
 
-def expert_forward(x, wg, wu, wd, accumulate="f64"):
-    """One expert's SwiGLU on BF16-valued rows; returns BF16-valued ``y``."""
+def q8_matmul(x, packed):
+    """``compute.py:52-65`` (``numpy_q8_matmul``): FP32 ``[rows, outputs]`` of a W8A8 dot.
+
+    ``x``: FP32-valued ``[rows, K]``; ``packed``: Q8_0 blocks ``uint8[outputs, K / 32, 34]``.
+    Per 32-value group g the activations are quantised to int8 with the FP32 scale
+    ``max|x| / 127`` (``x / scale`` rounded half to even, clipped to +-127; a zero scale
+    divides by 1), the int32 dot with the weight codes is taken exactly, and the groups are
+    added in order: ``out += (f32(partial) * act_scale) * weight_scale``."""
+    packed = np.asarray(packed, np.uint8)
+    scale = np.ascontiguousarray(packed[..., :2]).view("<f2").reshape(packed.shape[:2]).astype(np.float32)
+    weights = np.ascontiguousarray(packed[..., 2:]).view(np.int8).astype(np.int64)
+    grouped = np.asarray(x, np.float32).reshape(x.shape[0], -1, 32)
+    act_scale = (np.max(np.abs(grouped), -1) / np.float32(127)).astype(np.float32)
+    codes = np.clip(np.rint(grouped / np.where(act_scale == 0, np.float32(1), act_scale)[..., None]),
+                    -127, 127).astype(np.int64)
+    out = np.zeros((x.shape[0], packed.shape[0]), np.float32)
+    for group in range(weights.shape[1]):
+        partial = (codes[:, group] @ weights[:, group].T).astype(np.float32)
+        out = (out + (partial * act_scale[:, group, None]).astype(np.float32) * scale[:, group][None, :]).astype(
+            np.float32)
+    return out
+
+
+def expert_forward(x, wg, wu, wd, accumulate="f64", down_q8=None):
+    """One expert's SwiGLU on BF16-valued rows; returns BF16-valued ``y``. With ``down_q8``
+    (the expert's raw Q8_0 down blocks ``[hidden, I / 32, 34]``) the down projection is the
+    ``int8_q8`` policy's W8A8 dot (``experts.py:96-107``) instead of the BF16 one."""
     g = bf16_round(_dot(x, wg, accumulate))
     u = bf16_round(_dot(x, wu, accumulate))
     act = bf16_round((bf16_round(g * sigmoid(g)) * u).astype(np.float32))
+    if down_q8 is not None:
+        return bf16_round(q8_matmul(act, down_q8))
     return bf16_round(_dot(act, wd, accumulate))
 
 
@@ -90,6 +120,7 @@ def expert_ffn(
     first_expert=0,
     accumulate="f64",
     partial=False,
+    compute="bf16",
 ):
     """Routed FFN over this rank's experts ``[first_expert, first_expert + E_local)``.
 
@@ -97,6 +128,7 @@ def expert_ffn(
     ``down``: ``[E_local, hidden * row_bytes(intermediate)]``. ``x``: BF16-valued
     ``[B, hidden]``; ``ids``/``weights``: ``[B, k]``. Returns BF16-valued ``[B, hidden]``,
     or the FP32 partial sum when ``partial`` (the value the EP all-reduce adds).
+    ``compute="int8_q8"`` computes a Q8_0 down projection as the W8A8 dot (``q8_matmul``).
     """
     x = bf16_round(np.asarray(x, np.float32))
     count = np.asarray(gate).shape[0]
@@ -108,8 +140,10 @@ def expert_ffn(
             continue
         wg = expert_weights(gate[e], gate_type, intermediate, hidden)
         wu = expert_weights(up[e], up_type, intermediate, hidden)
-        wd = expert_weights(down[e], down_type, hidden, intermediate)
-        y = expert_forward(x[rows], wg, wu, wd, accumulate)
+        w8 = compute == "int8_q8" and down_type == "Q8_0"
+        wd = None if w8 else expert_weights(down[e], down_type, hidden, intermediate)
+        q8 = np.asarray(down[e]).reshape(hidden, -1, 34) if w8 else None
+        y = expert_forward(x[rows], wg, wu, wd, accumulate, down_q8=q8)
         contribution = (y * route[e, rows][:, None]).astype(np.float32)
         out[rows] = (out[rows] + contribution).astype(np.float32)
     return out if partial else bf16_round(out)

@@ -13,6 +13,8 @@ The fixtures are committed; tests never read the reference at run time. Sources:
   - the packed-Q6 projection golden (``tests/test_packed_q6.py:51-81`` cases);
 * ``packed_q6/layout.py`` ``pack_q6`` - the reference's SoA planes of fixture rows
   (``soa_q6.npz``), the input form ``qk_q6_soa_to_rows`` restores;
+* ``compute.numpy_q8_matmul`` on ``compute.pack_q8`` weights - the W8A8 golden
+  (``w8a8.npz``) of the ``int8_q8`` expert policy;
 * pure-NumPy functions that live in modules importing JAX are executed from their own
   source text (extracted with ``ast``, no JAX needed): ``compute.pack_q8``,
   ``compute.numpy_q8_matmul`` and the test oracle ``scale_oracle``
@@ -318,6 +320,30 @@ def soa_golden(q6ref, funcs):
     np.savez_compressed(HERE / "soa_q6.npz", **out)
 
 
+W8A8_CASES = ((8, 256, 64, 837), (24, 640, 256, 5))
+
+
+def w8a8_golden(funcs):
+    """The reference's W8A8 dot ``numpy_q8_matmul`` (``compute.py:52-65``) on weights packed by
+    its ``pack_q8`` (``compute.py:41-49``): the integer-dot test of
+    ``tests/test_qwen38_compute.py:81-100`` (seed 837: a zero row, x20 outliers on every 32nd
+    value, a row of 127s), and a down-projection shape (I = 640, 20 groups)."""
+    out = {"cases": np.array(W8A8_CASES, np.int64)}
+    for rows, width, outputs, seed in W8A8_CASES:
+        rng = np.random.default_rng(seed)
+        x = rng.normal(size=(rows, width)).astype(np.float32)
+        x[0] = 0
+        x[1, ::32] *= 20
+        x[2] = 127
+        x = x.astype(BF16).astype(np.float32)  # the kernels take BF16 activations
+        raw = funcs["pack_q8"](rng.normal(size=(outputs, width)).astype(np.float32))
+        key = f"{rows}_{width}_{outputs}"
+        out[f"x_{key}"] = x
+        out[f"raw_{key}"] = raw.reshape(outputs, width // 32, 34)
+        out[f"expected_{key}"] = funcs["numpy_q8_matmul"](x, raw.reshape(outputs, width // 32, 34))
+    np.savez_compressed(HERE / "w8a8.npz", **out)
+
+
 def main():
     args = [a for a in sys.argv[1:] if not a.startswith("--only=")]
     only = [a.split("=", 1)[1] for a in sys.argv[1:] if a.startswith("--only=")]
@@ -332,6 +358,7 @@ def main():
         "q8": lambda: q8_golden(funcs),
         "split": lambda: split_golden(quant, funcs),
         "soa": lambda: soa_golden(q6ref, funcs),
+        "w8a8": lambda: w8a8_golden(funcs),
     }
     for name, step in steps.items():
         if not only or name in only:

@@ -249,6 +249,71 @@ def test_q5_expert_types(cuda_device, qtype, down_type, hidden, intermediate, ba
     assert mx < LAYER_TOL and l2 < 2e-3, (mx, l2)
 
 
+@pytest.mark.parametrize("qtype,hidden,intermediate,batch,k", [
+    ("Q6_K", 512, 512, 8, 2), ("Q4_K", 512, 640, 40, 2), ("Q6_K", 256, 96, 300, 4), ("Q4_K", 2048, 512, 64, 4)])
+def test_int8_q8_policy_w8a8_down(cuda_device, qtype, hidden, intermediate, batch, k):
+    """compute="int8_q8" with a Q8_0 down (experts.py:85-107): the down projection is the W8A8
+    integer dot (compute.py:20-34; tcgen05 kind::i8), checked against the oracle's restatement
+    of the reference's numpy_q8_matmul inside the routed FFN. I = 640 and 96 leave a partial
+    last K block (its padded groups are skipped); 300 tokens take several 32-token chunks per
+    expert. The BF16 policy on the same experts differs from it by the activation rounding."""
+    rng = np.random.default_rng(intermediate + batch + k)
+    count = 8
+    raw = make_experts(rng, count, hidden, intermediate, qtype, "Q8_0")
+    ids = np.argsort(rng.random((batch, count)), axis=1)[:, :k].astype(np.int32)
+    weights = bf16_round(rng.uniform(0.05, 1.0, (batch, k)).astype(np.float32))
+    weights[3::7] = 0
+    x = rng.normal(size=(batch, hidden)).astype(np.float32)
+    import torch
+
+    from qk_b200.experts import expert_parallel
+    from qk_b200.parallel import put_expert_bytes
+
+    dev = {n: put_expert_bytes(v, n, "Q8_0" if n == "down" else qtype, hidden, intermediate, device=cuda_device)
+           for n, v in raw.items()}
+    args = (dev["gate"], dev["up"], dev["down"], bf16_tensor(x, cuda_device),
+            torch.from_numpy(ids).to(cuda_device), bf16_tensor(weights, cuda_device))
+    fn = expert_parallel(gate_type=qtype, up_type=qtype, down_type="Q8_0", hidden=hidden,
+                         intermediate=intermediate, compute="int8_q8")
+    got = to_f32(fn(*args))
+    fn.check_status()
+    expected = moe.expert_ffn(raw["gate"], raw["up"], raw["down"], x, ids, weights, gate_type=qtype,
+                              up_type=qtype, down_type="Q8_0", hidden=hidden, intermediate=intermediate,
+                              compute="int8_q8")
+    mx, l2 = rel_err(got, expected)
+    assert mx < LAYER_TOL and l2 < 2e-3, (mx, l2)
+    np.testing.assert_array_equal(got[3::7], 0)
+    bf16 = expert_parallel(gate_type=qtype, up_type=qtype, down_type="Q8_0", hidden=hidden,
+                           intermediate=intermediate)
+    other = to_f32(bf16(*args))
+    assert not np.array_equal(other, got)  # a different arithmetic ran
+    assert rel_err(other, got)[1] < 0.05
+
+
+def test_int8_q8_w8a8_dot_matches_reference_golden(golden, cuda_device):
+    """The W8A8 projection (compute.py:20-34, q8_matmul) on the reference's integer-dot test
+    (tests/test_qwen38_compute.py:81-100: a zero row, x20 outliers, a row of 127s) and a
+    down-projection shape (K = 640, 20 groups), against the reference's own numpy_q8_matmul on
+    its pack_q8 weights: FP32 within the reference's FP32 tolerance (atol 5e-4, rtol 2e-6), BF16
+    within its BF16 tolerance (atol 0.5, rtol 0.004); the zero row stays zero."""
+    import torch
+
+    from qk_b200.packed import pack_rows, q8_matmul
+
+    data = golden("w8a8.npz")
+    for rows, width, outputs, _ in data["cases"]:
+        key = f"{rows}_{width}_{outputs}"
+        x, raw, expected = data[f"x_{key}"], data[f"raw_{key}"], data[f"expected_{key}"]
+        packed = pack_rows(raw, int(width), "Q8_0", cuda_device)
+        xd = bf16_tensor(x, cuda_device)
+        got = q8_matmul(xd, packed, output_dtype=torch.float32).cpu().numpy()
+        np.testing.assert_allclose(got, expected, atol=5e-4, rtol=2e-6)
+        np.testing.assert_array_equal(got[0], 0)
+        got16 = to_f32(q8_matmul(xd, packed))
+        np.testing.assert_allclose(got16, bf16_round(expected), atol=0.5, rtol=0.004)
+        np.testing.assert_array_equal(got16, bf16_round(got))
+
+
 def test_zero_weights_give_zero_and_ids_outside_rank_are_ignored(cuda_device):
     hidden, intermediate, count = 256, 256, 4
     rng = np.random.default_rng(3)
@@ -340,9 +405,6 @@ def test_contract_errors(cuda_device):
     with pytest.raises(ValueError, match="row tile"):
         expert_parallel(gate_type="Q6_K", up_type="Q6_K", down_type="Q6_K", hidden=256,
                         intermediate=256, row_tile=0)
-    with pytest.raises(ValueError, match="int8_q8"):
-        expert_parallel(gate_type="Q6_K", up_type="Q6_K", down_type="Q8_0", hidden=256,
-                        intermediate=256, compute="int8_q8")
     with pytest.raises(ValueError, match="gate and up"):
         expert_parallel(gate_type="Q6_K", up_type="Q4_K", down_type="Q6_K", hidden=256,
                         intermediate=256)

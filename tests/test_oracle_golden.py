@@ -192,6 +192,17 @@ def test_q5_tiles_round_trip_and_place_chunks(qtype, rows, width):
         np.testing.assert_array_equal(col[4 + blk], raw[r, j, 8:])
 
 
+def test_w8a8_dot_matches_reference_numpy_q8_matmul(golden):
+    """``compute.py:52-65`` restated: bit-equal to the reference's own ``numpy_q8_matmul`` on
+    its ``pack_q8`` weights, a zero row staying zero."""
+    data = golden("w8a8.npz")
+    for rows, width, outputs, _ in data["cases"]:
+        key = f"{rows}_{width}_{outputs}"
+        got = moe.q8_matmul(data[f"x_{key}"], data[f"raw_{key}"])
+        np.testing.assert_array_equal(got.view(np.uint32), data[f"expected_{key}"].view(np.uint32))
+        np.testing.assert_array_equal(got[0], 0)
+
+
 def test_soa_restatement_inverts_the_reference_pack_q6(golden):
     """``oracle.layout.soa_to_rows`` against the reference's own ``pack_q6`` planes."""
     from oracle.layout import soa_to_rows
