@@ -269,6 +269,10 @@ constexpr uint32_t kWaitHintNs = 1000;
 
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
   if (mbar_try_wait(bar, parity)) return true;
+  // Not unrolled: the loop is inlined at every wait of a kernel, and unrolled copies of it
+  // made the projection kernels' code several times larger than their hot loops (a kernel
+  // whose warps run different roles then misses in the instruction cache).
+#pragma unroll 1
   for (uint32_t i = 0; i < kWaitLimit; ++i)
     if (mbar_try_wait_suspend(bar, parity, kWaitHintNs)) return true;
   return false;

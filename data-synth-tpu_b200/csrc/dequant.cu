@@ -354,11 +354,11 @@ __global__ void __launch_bounds__(2 * kTileRows) dequant_tiled_kernel(const uint
   };
   typename HT::Regs regs;
   if (h == 0) {
-    HT::template load<0>(regs, t, r);
-    HT::template decode<kExact, 0>(regs, [&](int col, const uint32_t(&o)[8]) { store(kb * 256 + 2 * col, o); });
+    HT::load(regs, t, r, 0);
+    HT::template decode<kExact>(regs, 0, [&](int col, const uint32_t(&o)[8]) { store(kb * 256 + 2 * col, o); });
   } else {
-    HT::template load<1>(regs, t, r);
-    HT::template decode<kExact, 1>(regs, [&](int col, const uint32_t(&o)[8]) { store(kb * 256 + 128 + 2 * col, o); });
+    HT::load(regs, t, r, 1);
+    HT::template decode<kExact>(regs, 1, [&](int col, const uint32_t(&o)[8]) { store(kb * 256 + 128 + 2 * col, o); });
   }
 }
 

@@ -118,8 +118,7 @@ struct HalfTile<QType::Q6_K> {
     r.d = 0.f;
   }
 
-  template <int h>
-  __device__ __forceinline__ static void load(Regs& r, const uint8_t* tile, int row) {
+  __device__ __forceinline__ static void load(Regs& r, const uint8_t* tile, int row, int h) {
 #pragma unroll
     for (int c = 0; c < 6; ++c) {
       const uint4 v = lds128(tile + ((6 * h + c) * kTileRows + row) * 16);
@@ -136,8 +135,8 @@ struct HalfTile<QType::Q6_K> {
 
   // emit(col, regs[8]) receives the 8 packed BF16 pairs of the 16 positions starting at
   // column `col` of the half (column = position / 2 inside the half).
-  template <bool kExact, int h, typename Emit>
-  __device__ __forceinline__ static void decode(const Regs& r, Emit&& emit) {
+  template <bool kExact, typename Emit>
+  __device__ __forceinline__ static void decode(const Regs& r, int h, Emit&& emit) {
 #pragma unroll
     for (int jj = 0; jj < 8; ++jj) {
       const int sc = static_cast<int8_t>((r.sc[jj >> 2] >> (8 * (jj & 3))) & 0xffu);
@@ -173,8 +172,7 @@ struct HalfTile<QType::Q4_K> {
     for (int i = 0; i < 16; ++i) r.w[i] = 0;
   }
 
-  template <int h>
-  __device__ __forceinline__ static void load(Regs& r, const uint8_t* tile, int row) {
+  __device__ __forceinline__ static void load(Regs& r, const uint8_t* tile, int row, int h) {
     const uint4 v = lds128(tile + row * 16);
     r.hd[0] = v.x;
     r.hd[1] = v.y;
@@ -194,21 +192,28 @@ struct HalfTile<QType::Q4_K> {
     return static_cast<int>((r.hd[1 + (i >> 2)] >> (8 * (i & 3))) & 0xffu);
   }
 
-  template <bool kExact, int h, typename Emit>
-  __device__ __forceinline__ static void decode(const Regs& r, Emit&& emit) {
+  // 6-bit scale and min of sub-block j = 4 h + jj (jj a compile-time index, h the half, which
+  // may be a run-time value: the register indices stay constant either way).
+  __device__ __forceinline__ static void scales_of(const Regs& r, int h, int jj, int& sc, int& m) {
+    const int b0 = scale_byte(r, jj), b4 = scale_byte(r, jj + 4), b8 = scale_byte(r, jj + 8);
+    if (h == 0) {
+      sc = b0 & 63;
+      m = b4 & 63;
+    } else {
+      sc = (b8 & 15) | ((b0 >> 6) << 4);
+      m = (b8 >> 4) | ((b4 >> 6) << 4);
+    }
+  }
+
+  template <bool kExact, typename Emit>
+  __device__ __forceinline__ static void decode(const Regs& r, int h, Emit&& emit) {
     const float d = f16_to_f32(static_cast<uint16_t>(r.hd[0] & 0xffffu));
     const float dmin = f16_to_f32(static_cast<uint16_t>(r.hd[0] >> 16));
 #pragma unroll
     for (int jj = 0; jj < 4; ++jj) {
       const int j = 4 * h + jj;  // sub-block of 32 positions (gguf_quant.py:118-135)
       int sc, m;
-      if (j < 4) {
-        sc = scale_byte(r, j) & 63;
-        m = scale_byte(r, j + 4) & 63;
-      } else {
-        sc = (scale_byte(r, j + 4) & 15) | ((scale_byte(r, j - 4) >> 6) << 4);
-        m = (scale_byte(r, j + 4) >> 4) | ((scale_byte(r, j) >> 6) << 4);
-      }
+      scales_of(r, h, jj, sc, m);
       const float ds = __fmul_rn(d, static_cast<float>(sc));
       const float dm = __fmul_rn(dmin, static_cast<float>(m));
 #pragma unroll
@@ -248,8 +253,7 @@ struct HalfTile<QType::Q8_0> {
     for (int i = 0; i < 32; ++i) r.w[i] = 0;
   }
 
-  template <int h>
-  __device__ __forceinline__ static void load(Regs& r, const uint8_t* tile, int row) {
+  __device__ __forceinline__ static void load(Regs& r, const uint8_t* tile, int row, int h) {
     const uint2 s = *reinterpret_cast<const uint2*>(tile + row * 16 + 8 * h);
     r.d[0] = s.x;
     r.d[1] = s.y;
@@ -265,8 +269,8 @@ struct HalfTile<QType::Q8_0> {
 
   // Codes are signed; flipping their sign bits gives code + 128 in [1, 255], decoded with
   // offset 128: (1024 + code + 128) d - 1152 d = code d, exact in FP32 (19 significant bits).
-  template <bool kExact, int h, typename Emit>
-  __device__ __forceinline__ static void decode(const Regs& r, Emit&& emit) {
+  template <bool kExact, typename Emit>
+  __device__ __forceinline__ static void decode(const Regs& r, int h, Emit&& emit) {
 #pragma unroll
     for (int jj = 0; jj < 4; ++jj) {  // GGUF block 4h + jj of the super-block
       const float d = f16_to_f32(static_cast<uint16_t>(r.d[jj >> 1] >> (16 * (jj & 1))));
@@ -308,8 +312,7 @@ struct HalfTile<QType::Q5_K> {
     for (int i = 0; i < 16; ++i) r.w[i] = 0;
   }
 
-  template <int h>
-  __device__ __forceinline__ static void load(Regs& r, const uint8_t* tile, int row) {
+  __device__ __forceinline__ static void load(Regs& r, const uint8_t* tile, int row, int h) {
     const uint4 v = lds128(tile + row * 16);
     r.hd[0] = v.x;
     r.hd[1] = v.y;
@@ -337,21 +340,28 @@ struct HalfTile<QType::Q5_K> {
     return static_cast<int>((r.hd[1 + (i >> 2)] >> (8 * (i & 3))) & 0xffu);
   }
 
-  template <bool kExact, int h, typename Emit>
-  __device__ __forceinline__ static void decode(const Regs& r, Emit&& emit) {
+  // 6-bit scale and min of sub-block j = 4 h + jj (jj a compile-time index, h the half, which
+  // may be a run-time value: the register indices stay constant either way).
+  __device__ __forceinline__ static void scales_of(const Regs& r, int h, int jj, int& sc, int& m) {
+    const int b0 = scale_byte(r, jj), b4 = scale_byte(r, jj + 4), b8 = scale_byte(r, jj + 8);
+    if (h == 0) {
+      sc = b0 & 63;
+      m = b4 & 63;
+    } else {
+      sc = (b8 & 15) | ((b0 >> 6) << 4);
+      m = (b8 >> 4) | ((b4 >> 6) << 4);
+    }
+  }
+
+  template <bool kExact, typename Emit>
+  __device__ __forceinline__ static void decode(const Regs& r, int h, Emit&& emit) {
     const float d = f16_to_f32(static_cast<uint16_t>(r.hd[0] & 0xffffu));
     const float dmin = f16_to_f32(static_cast<uint16_t>(r.hd[0] >> 16));
 #pragma unroll
     for (int jj = 0; jj < 4; ++jj) {
       const int j = 4 * h + jj;  // sub-block of 32 values
       int sc, m;
-      if (j < 4) {
-        sc = scale_byte(r, j) & 63;
-        m = scale_byte(r, j + 4) & 63;
-      } else {
-        sc = (scale_byte(r, j + 4) & 15) | ((scale_byte(r, j - 4) >> 6) << 4);
-        m = (scale_byte(r, j + 4) >> 4) | ((scale_byte(r, j) >> 6) << 4);
-      }
+      scales_of(r, h, jj, sc, m);
       const float ds = __fmul_rn(d, static_cast<float>(sc));
       const float dm = __fmul_rn(dmin, static_cast<float>(m));
 #pragma unroll
@@ -395,8 +405,7 @@ struct HalfTile<QType::Q5_1> {
     for (int i = 0; i < 16; ++i) r.w[i] = 0;
   }
 
-  template <int h>
-  __device__ __forceinline__ static void load(Regs& r, const uint8_t* tile, int row) {
+  __device__ __forceinline__ static void load(Regs& r, const uint8_t* tile, int row, int h) {
     const uint4 a = lds128(tile + (h * kTileRows + row) * 16);
     const uint4 b = lds128(tile + ((2 + h) * kTileRows + row) * 16);
     r.dm[0] = a.x;
@@ -425,8 +434,8 @@ struct HalfTile<QType::Q5_1> {
 
   // v = d * q + m: fma(1024 + q, d, -1024 d) is d * q exactly (both factors have at most 11
   // significant bits), then one FP32 addition of m, as the reference rounds it.
-  template <bool kExact, int h, typename Emit>
-  __device__ __forceinline__ static void decode(const Regs& r, Emit&& emit) {
+  template <bool kExact, typename Emit>
+  __device__ __forceinline__ static void decode(const Regs& r, int h, Emit&& emit) {
 #pragma unroll
     for (int jj = 0; jj < 4; ++jj) {  // GGUF block 4h + jj of the super-block
       const float d = f16_to_f32(static_cast<uint16_t>(r.dm[jj] & 0xffffu));

@@ -34,7 +34,10 @@
 //   warps 21-24 epilogue: read the four accumulators (tcgen05.ld), add them, release them,
 //               and write h = SwiGLU (gate/up), y (down) or the FP32 output (dense).
 // TMEM: A buffers [0, 384) (3 x 128 columns = 256 BF16 of K per lane; three, so a decode
-// group never waits for the MMA of the stage it decoded last), accumulators [384, 512)
+// group never waits for the MMA of the stage it decoded last; each half of a buffer - values
+// 0..127 and 128..255 of the block - has its own full/empty barrier pair, so the issuers of
+// K atoms 0-1 start when the 4 warps of half 0 are done and half 0's warps reuse the buffer
+// as soon as those issuers' MMAs complete), accumulators [384, 512)
 // (4 issuers x 32 columns; the wide form: 1 issuer x 128 columns, the epilogue reading them
 // 32 columns at a time). Every wait is bounded; on give-up the CTA records QK_ERR_TIMEOUT in
 // `status` and leaves its loops.
@@ -289,6 +292,7 @@ __global__ void __launch_bounds__(Form<W>::kThreads, 1) umma_proj_kernel(const U
   constexpr int DB = Form<W>::kDBuf;          // accumulator buffers
   constexpr uint32_t kAccCol = Form<W>::kAccCol;
   constexpr int TB = Cfg::kTile;
+  static_assert((2 * SW + 2 * kXSlots + 4 * AB + 2 * DB) * 8 + kXSlots * 4 + 4 <= 512, "barrier region");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* xring = smem;
@@ -297,9 +301,11 @@ __global__ void __launch_bounds__(Form<W>::kThreads, 1) umma_proj_kernel(const U
   uint64_t* wempty = wfull + SW;
   uint64_t* xfull = wempty + SW;
   uint64_t* xempty = xfull + kXSlots;
+  // A buffer b, half h (values 128 h .. 128 h + 127 of the block): afull[2 b + h] when its
+  // 4 decode warps have stored it, aempty[2 b + h] when the MMAs reading it have completed.
   uint64_t* afull = xempty + kXSlots;
-  uint64_t* aempty = afull + AB;
-  uint64_t* dfull = aempty + AB;
+  uint64_t* aempty = afull + 2 * AB;
+  uint64_t* dfull = aempty + 2 * AB;
   uint64_t* dempty = dfull + DB;
   volatile uint32_t* xoff = reinterpret_cast<volatile uint32_t*>(dempty + DB);  // [kXSlots] granule of each stage
   uint32_t* tmem_sh = const_cast<uint32_t*>(xoff + kXSlots);
@@ -319,8 +325,10 @@ __global__ void __launch_bounds__(Form<W>::kThreads, 1) umma_proj_kernel(const U
       mbar_init(&xempty[s], NI);  // the MMA commits
     }
     for (int i = 0; i < AB; ++i) {
-      mbar_init(&afull[i], kDecodeWarps / 2);
-      mbar_init(&aempty[i], NI);
+      for (int h = 0; h < 2; ++h) {
+        mbar_init(&afull[2 * i + h], kDecodeWarps / 4);
+        mbar_init(&aempty[2 * i + h], NI >= 2 ? NI / 2 : 1);
+      }
     }
     for (int i = 0; i < DB; ++i) {
       mbar_init(&dfull[i], NI);
@@ -407,7 +415,11 @@ __global__ void __launch_bounds__(Form<W>::kThreads, 1) umma_proj_kernel(const U
         tc_fence_after();
         for (int i = 0; i < it.kb1 - it.kb0; ++i, ++sc) {
           const uint32_t j = sc % kXSlots, b = sc % AB;
-          if (!mbar_wait_bounded(&xfull[j], (sc / kXSlots) & 1) || !mbar_wait_bounded(&afull[b], (sc / AB) & 1)) {
+          // the halves of the block this issuer's K atoms lie in
+          constexpr int kAtoms = 16 / NI / 4;
+          const uint32_t h0 = (mi * kAtoms) / 2, h1 = (mi * kAtoms + kAtoms - 1) / 2;
+          if (!mbar_wait_bounded(&xfull[j], (sc / kXSlots) & 1) || !mbar_wait_bounded(&afull[2 * b + h0], (sc / AB) & 1) ||
+              (h1 != h0 && !mbar_wait_bounded(&afull[2 * b + h1], (sc / AB) & 1))) {
             ok = false;
             break;
           }
@@ -419,7 +431,8 @@ __global__ void __launch_bounds__(Form<W>::kThreads, 1) umma_proj_kernel(const U
 #pragma unroll
           for (int ks = 0; ks < kSteps; ++ks)
             umma_ts(dcol, acol + ks * 8, bd + (((ks >> 2) * atom) >> 4) + (ks & 3) * 2, idesc, (i != 0) || (ks != 0));
-          umma_commit(&aempty[b]);
+          umma_commit(&aempty[2 * b + h0]);
+          if (h1 != h0) umma_commit(&aempty[2 * b + h1]);
           umma_commit(&xempty[j]);
         }
         if (!ok) break;
@@ -522,8 +535,9 @@ __global__ void __launch_bounds__(Form<W>::kThreads, 1) umma_proj_kernel(const U
     // ---------------- decode warps ----------------
     const int g = warp >> 3, q = warp & 3, L = 32 * q + lane;
     const int t = L & 1, r = L >> 1;
-    auto run = [&](auto hc) {
-      constexpr int h = decltype(hc)::value;
+    // One copy of the loop for both halves (h a run-time value): a copy per half doubled the
+    // decode warps' code, and the instruction-cache misses of that showed as no_instruction stalls.
+    auto run = [&](int h) {
       uint32_t sc = 0;
 #ifdef QK_STAGGER_NS
       if (g == 1) __nanosleep(QK_STAGGER_NS);  // start the second decode group half a stage later
@@ -547,21 +561,21 @@ __global__ void __launch_bounds__(Form<W>::kThreads, 1) umma_proj_kernel(const U
           // wait for the A buffer first, then load and decode in one stretch (the shared-memory
           // loads of later sub-blocks overlap the decode of earlier ones); the weight slot is
           // released after the decode
-          if (sc >= AB && !mbar_wait_bounded(&aempty[b], ((sc / AB) - 1) & 1)) {
+          if (sc >= AB && !mbar_wait_bounded(&aempty[2 * b + h], ((sc / AB) - 1) & 1)) {
             ok = false;
             break;
           }
           tc_fence_after();
           typename HT::Regs regs;
-          if (mine) HT::template load<h>(regs, wring + static_cast<size_t>(s) * Cfg::kWStageBytes + t * Cfg::kTile1, r);
+          if (mine) HT::load(regs, wring + static_cast<size_t>(s) * Cfg::kWStageBytes + t * Cfg::kTile1, r, h);
           else HT::clear(regs);
 #else
           typename HT::Regs regs;
-          if (mine) HT::template load<h>(regs, wring + static_cast<size_t>(s) * Cfg::kWStageBytes + t * Cfg::kTile1, r);
+          if (mine) HT::load(regs, wring + static_cast<size_t>(s) * Cfg::kWStageBytes + t * Cfg::kTile1, r, h);
           else HT::clear(regs);
           __syncwarp();
           if (lane == 0) mbar_arrive(&wempty[s]);
-          if (sc >= AB && !mbar_wait_bounded(&aempty[b], ((sc / AB) - 1) & 1)) {
+          if (sc >= AB && !mbar_wait_bounded(&aempty[2 * b + h], ((sc / AB) - 1) & 1)) {
             ok = false;
             break;
           }
@@ -573,13 +587,13 @@ __global__ void __launch_bounds__(Form<W>::kThreads, 1) umma_proj_kernel(const U
           // tcgen05.st takes them (the registers of an 8-column store are not free for the next
           // step's results until the store has read them)
           uint32_t sbuf[32];
-          HT::template decode<false, h>(regs, [&](int col, const uint32_t(&o)[8]) {
+          HT::template decode<false>(regs, h, [&](int col, const uint32_t(&o)[8]) {
 #pragma unroll
             for (int i = 0; i < 8; ++i) sbuf[(col & 31) + i] = o[i];
             if ((col & 31) == 24) tmem_st32(col0 + (col & ~31), sbuf);
           });
 #else
-          HT::template decode<false, h>(regs, [&](int col, const uint32_t(&o)[8]) { tmem_st8(col0 + col, o); });
+          HT::template decode<false>(regs, h, [&](int col, const uint32_t(&o)[8]) { tmem_st8(col0 + col, o); });
 #endif
           tmem_wait_st();
           tc_fence_before();
@@ -588,13 +602,12 @@ __global__ void __launch_bounds__(Form<W>::kThreads, 1) umma_proj_kernel(const U
 #if QK_LATE_RELEASE
             mbar_arrive(&wempty[s]);
 #endif
-            mbar_arrive(&afull[b]);
+            mbar_arrive(&afull[2 * b + h]);
           }
         }
       }
     };
-    if (((warp >> 2) & 1) == 0) run(std::integral_constant<int, 0>{});
-    else run(std::integral_constant<int, 1>{});
+    run((warp >> 2) & 1);
   }
 
   if (!ok && lane == 0 && A.status) atomicExch(A.status, QK_ERR_TIMEOUT);
