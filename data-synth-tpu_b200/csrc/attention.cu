@@ -434,6 +434,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_mbar_init();
   }
   __syncthreads();
+  // Launched as a programmatic dependent: the set-up above overlaps the previous kernel (the
+  // cache append); the cache, q and the lengths are read only after it has finished.
+  pdl_wait();
   pdl_trigger();  // the merge kernel may take its place now; it waits for this grid to end
 
   const int cta = blockIdx.x;
@@ -1003,11 +1006,16 @@ int launch_attention(const uint16_t* q, const int8_t* k_codes, const int8_t* v_c
   if (nregs < kLaunchRegs)
     return set_error(QK_ERR_CUDA, "attention kernel built with %d registers per thread, the split needs %d",
                      nregs, kLaunchRegs);
-  if (head_dim == 256)
-    attn_stream_kernel<256><<<a.ctas, kThreads, smem, st>>>(maps[0], maps[1], maps[2], maps[3], a);
-  else
-    attn_stream_kernel<128><<<a.ctas, kThreads, smem, st>>>(maps[0], maps[1], maps[2], maps[3], a);
-  QK_LAUNCHED("attn_stream_kernel");
+  {
+    const cudaError_t e =
+        head_dim == 256
+            ? launch_dependent(attn_stream_kernel<256>, dim3(a.ctas), dim3(kThreads), smem, st, maps[0], maps[1], maps[2],
+                               maps[3], a)
+            : launch_dependent(attn_stream_kernel<128>, dim3(a.ctas), dim3(kThreads), smem, st, maps[0], maps[1], maps[2],
+                               maps[3], a);
+    if (e != cudaSuccess) return cuda_error(e, "attn_stream_kernel");
+    count_launch();
+  }
   if (a.ctas > 1) {
     // partials per cut segment: about nch / (units / ctas) + 1; wider merges split d further
     const long long per = a.units / a.ctas;

@@ -282,6 +282,20 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
 // small loads
 // ---------------------------------------------------------------------------------
 
+// Block-wide FP32 sum (all threads get the result): a warp butterfly, then the warps' sums
+// added in warp order. `red` holds blockDim.x / 32 floats.
+__device__ __forceinline__ float block_sum(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  __syncthreads();  // `red` may still be read by a previous call
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float s = 0.f;
+  for (int w = 0; w < nw; ++w) s += red[w];
+  return s;
+}
+
 __device__ __forceinline__ uint4 ld_nc_v4(const void* p) {
   uint4 r;
   asm("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];"

@@ -55,6 +55,8 @@ __global__ void append_kernel(const void* __restrict__ key, const void* __restri
                               const int32_t* __restrict__ time, const uint8_t* __restrict__ active,
                               int8_t* k_codes, int8_t* v_codes, uint16_t* k_scale, uint16_t* v_scale,
                               int B, int T, int D, int group, int W = 1) {
+  pdl_wait();  // launched as a programmatic dependent: the keys' and values' producer first
+  pdl_trigger();
   const int64_t total = static_cast<int64_t>(B) * W * 2 * D;
   const int G = D / group;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
@@ -151,9 +153,11 @@ int qk_kv_q8_append(const void* key, const void* value, int in_dtype, const int3
   if (B == 0) return QK_OK;
   QK_REQUIRE(key && value && time && k_codes && v_codes && k_scale && v_scale, "null pointer");
   const int D = kv_heads * head_dim;
-  append_kernel<<<grid_for(static_cast<int64_t>(B) * 2 * D, 256), 256, 0, as_stream(stream)>>>(
-      key, value, in_dtype == QK_OUT_BF16, time, active, k_codes, v_codes, k_scale, v_scale, B, T, D, group);
-  QK_LAUNCHED("append_kernel");
+  const cudaError_t e = launch_dependent(append_kernel, dim3(grid_for(static_cast<int64_t>(B) * 2 * D, 256)), dim3(256),
+                                         0, as_stream(stream), key, value, static_cast<int>(in_dtype == QK_OUT_BF16),
+                                         time, active, k_codes, v_codes, k_scale, v_scale, B, T, D, group, 1);
+  if (e != cudaSuccess) return cuda_error(e, "append_kernel");
+  count_launch();
   return QK_OK;
 }
 

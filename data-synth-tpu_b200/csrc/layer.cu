@@ -11,19 +11,6 @@ namespace {
 
 constexpr int kRowThreads = 256;
 
-// Block-wide FP32 sum (all threads get the result). `red` holds kRowThreads / 32 floats.
-__device__ __forceinline__ float block_sum(float v, float* red) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-  __syncthreads();  // `red` may still be read by a previous call
-  if (lane == 0) red[warp] = v;
-  __syncthreads();
-  float s = 0.f;
-  for (int w = 0; w < nw; ++w) s += red[w];
-  return s;
-}
-
 // math.py:27-31 rms: bf16(xf * rsqrt(mean(xf^2) + eps) * gamma), one block per row.
 __global__ void __launch_bounds__(kRowThreads) rms_norm_kernel(const uint16_t* __restrict__ x,
                                                                const uint16_t* __restrict__ gamma, int width,
@@ -41,6 +28,30 @@ __global__ void __launch_bounds__(kRowThreads) rms_norm_kernel(const uint16_t* _
   const float r = rsqrtf(__fadd_rn(__fdiv_rn(block_sum(ss, red), static_cast<float>(width)), eps));
   for (int i = threadIdx.x; i < width; i += blockDim.x)
     out[row * width + i] = bf16_bits_rne(__fmul_rn(__fmul_rn(bf16_to_f32(xr[i]), r), bf16_to_f32(gamma[i])));
+}
+
+// The residual add and the RMSNorm that follows it, one block per row: xo = bf16(x + y)
+// (stored; xo may alias x), then out = rms(xo) as rms_norm_kernel computes it (the same
+// thread layout and reduction over the stored BF16 values), so one launch gives the bits of
+// qk_residual_add + qk_rms_norm.
+__global__ void __launch_bounds__(kRowThreads) residual_rms_norm_kernel(const uint16_t* x, const uint16_t* __restrict__ y,
+                                                                        const uint16_t* __restrict__ gamma, int width,
+                                                                        float eps, uint16_t* xo,
+                                                                        uint16_t* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
+  __shared__ float red[kRowThreads / 32];
+  const int64_t row = blockIdx.x;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < width; i += blockDim.x) {
+    const uint16_t b = bf16_bits_rne(__fadd_rn(bf16_to_f32(x[row * width + i]), bf16_to_f32(y[row * width + i])));
+    xo[row * width + i] = b;
+    const float v = bf16_to_f32(b);
+    ss = fmaf(v, v, ss);
+  }
+  const float r = rsqrtf(__fadd_rn(__fdiv_rn(block_sum(ss, red), static_cast<float>(width)), eps));
+  for (int i = threadIdx.x; i < width; i += blockDim.x)
+    out[row * width + i] = bf16_bits_rne(__fmul_rn(__fmul_rn(bf16_to_f32(xo[row * width + i]), r), bf16_to_f32(gamma[i])));
 }
 
 // attention_cache.py:129-135: the fused projection output of one row is
@@ -144,6 +155,18 @@ int qk_rms_norm(const uint16_t* x, const uint16_t* gamma, int rows, int width, f
   const cudaError_t e = launch_dependent(rms_norm_kernel, dim3(rows), dim3(kRowThreads), 0, as_stream(stream), x, gamma,
                                          width, eps, out);
   if (e != cudaSuccess) return cuda_error(e, "rms_norm_kernel");
+  count_launch();
+  return QK_OK;
+}
+
+int qk_residual_rms_norm(const uint16_t* x, const uint16_t* y, const uint16_t* gamma, int rows, int width, float eps,
+                         uint16_t* x_out, uint16_t* out, qk_stream_t stream) {
+  QK_REQUIRE(rows >= 0 && width > 0, "invalid rms geometry");
+  if (rows == 0) return QK_OK;
+  QK_REQUIRE(x && y && gamma && x_out && out, "null pointer");
+  const cudaError_t e = launch_dependent(residual_rms_norm_kernel, dim3(rows), dim3(kRowThreads), 0, as_stream(stream),
+                                         x, y, gamma, width, eps, x_out, out);
+  if (e != cudaSuccess) return cuda_error(e, "residual_rms_norm_kernel");
   count_launch();
   return QK_OK;
 }

@@ -355,16 +355,6 @@ __device__ __forceinline__ uint32_t a_offset(uint32_t row, uint32_t k) {
   return (row >> 3) * 1024u + (row & 7) * 128u + ((chunk ^ (row & 7)) << 4) + (k & 7) * 2u;
 }
 
-// D[tmem] (+)= A[smem] * B[smem], M = 128, N from the descriptor, K = 16. One thread issues.
-__device__ __forceinline__ void umma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
-                                        uint32_t accumulate) {
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
 template <QType QT, int MODE>
 __global__ void __launch_bounds__(kPThreads, 1) umma_prefill_kernel(const UArgs A) {
   using Cfg = PCfg<QT>;

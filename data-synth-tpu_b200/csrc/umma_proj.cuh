@@ -86,22 +86,31 @@ enum { kModeGateUp = 0, kModeDown = 1, kModeDense = 2 };
 // of <= 128 tokens, so an expert's weights are decoded once per 128 tokens instead of once
 // per 32, one issuer (an M=128, N=128 MMA keeps the tensor pipe busy for its issue time),
 // and a 128 KB activation ring (two stages of 128 tokens).
-template <bool W>
+// The down pass of the narrow form: 2 MMA issuers (one per half block) and two accumulator
+// buffers, so the MMAs of the next item do not wait for the epilogue to read the last one
+// (an item has only I / 256 K blocks there; 43.3 vs 44.9 us at M = 16, 128 experts).
+#ifndef QK_DOWN_ISSUERS
+#define QK_DOWN_ISSUERS 2
+#endif
+#ifndef QK_DOWN_DBUF
+#define QK_DOWN_DBUF 2
+#endif
+template <bool W, int MODE = kModeGateUp>
 struct Form {
+  static constexpr bool kDown = MODE == kModeDown;
   static constexpr int kTok = W ? kWideTok : kMaxTok;
-  static constexpr int kIssuers = W ? 1 : kMmaIssuers;
+  static constexpr int kIssuers = W ? 1 : kDown ? QK_DOWN_ISSUERS : kMmaIssuers;
   static constexpr int kXGranules = W ? 16 : 8;
   // TMEM: A buffers of 128 columns, then the accumulators. (Two A and two accumulator
   // buffers for the wide form measured the same as three and one.)
   static constexpr int kABuf = W ? 3 : kABuffers;
-  static constexpr int kDBuf = W ? 1 : kDBuffers;
+  static constexpr int kDBuf = W ? 1 : kDown ? QK_DOWN_DBUF : kDBuffers;
   static constexpr uint32_t kAccCol = kABuf * 128;
   static constexpr int kEpilogueWarp0 = kMmaWarp0 + kIssuers;
   static constexpr int kThreads = (kEpilogueWarp0 + 4) * 32;
   static_assert(16 % kIssuers == 0 && 16 / kIssuers >= 4, "issuers take whole 64-value K atoms");
   static_assert(kABuf * 128 + kDBuf * kIssuers * kTok <= 512, "TMEM columns");
 };
-constexpr int kUmmaThreads = Form<false>::kThreads;
 
 template <QType QT, bool W = false>
 struct UCfg {
@@ -280,17 +289,17 @@ __device__ __forceinline__ void store_y8(const float (&acc)[8], int lane, uint16
 }
 
 template <QType QT, int MODE, bool W = false>
-__global__ void __launch_bounds__(Form<W>::kThreads, 1) umma_proj_kernel(const UArgs A) {
+__global__ void __launch_bounds__(Form<W, MODE>::kThreads, 1) umma_proj_kernel(const UArgs A) {
   using Cfg = UCfg<QT, W>;
   using HT = HalfTile<QT>;
   constexpr int SW = Cfg::kWStages;
-  constexpr int NI = Form<W>::kIssuers;       // MMA-issuing warps
-  constexpr int TOK = Form<W>::kTok;          // tokens per chunk (accumulator columns per issuer)
-  constexpr int XG = Form<W>::kXGranules;     // activation ring granules
-  constexpr int EW0 = Form<W>::kEpilogueWarp0;
-  constexpr int AB = Form<W>::kABuf;          // A buffers
-  constexpr int DB = Form<W>::kDBuf;          // accumulator buffers
-  constexpr uint32_t kAccCol = Form<W>::kAccCol;
+  constexpr int NI = Form<W, MODE>::kIssuers;       // MMA-issuing warps
+  constexpr int TOK = Form<W, MODE>::kTok;          // tokens per chunk (accumulator columns per issuer)
+  constexpr int XG = Form<W, MODE>::kXGranules;     // activation ring granules
+  constexpr int EW0 = Form<W, MODE>::kEpilogueWarp0;
+  constexpr int AB = Form<W, MODE>::kABuf;          // A buffers
+  constexpr int DB = Form<W, MODE>::kDBuf;          // accumulator buffers
+  constexpr uint32_t kAccCol = Form<W, MODE>::kAccCol;
   constexpr int TB = Cfg::kTile;
   static_assert((2 * SW + 2 * kXSlots + 4 * AB + 2 * DB) * 8 + kXSlots * 4 + 4 <= 512, "barrier region");
   extern __shared__ uint8_t smem_raw[];
@@ -624,7 +633,7 @@ int launch_umma(const UArgs& A, int grid, cudaStream_t st) {
   using Cfg = UCfg<QT, W>;
   int rc = allow_smem(reinterpret_cast<const void*>(umma_proj_kernel<QT, MODE, W>), Cfg::kSmem);
   if (rc) return rc;
-  const cudaError_t e = launch_dependent(umma_proj_kernel<QT, MODE, W>, dim3(grid), dim3(Form<W>::kThreads), Cfg::kSmem,
+  const cudaError_t e = launch_dependent(umma_proj_kernel<QT, MODE, W>, dim3(grid), dim3(Form<W, MODE>::kThreads), Cfg::kSmem,
                                          st, A);
   if (e != cudaSuccess) return cuda_error(e, "umma_proj_kernel");
   count_launch(1);

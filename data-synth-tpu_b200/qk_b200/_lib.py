@@ -69,6 +69,11 @@ SIGNATURES = {
     "qk_q8_matmul": (_i, [_p, _i64, _i64, _p, _i64, _i, _p, _p, _sz, _p]),
     "qk_router_topk": (_i, [_p, _p, _p, _i, _i, _i, _i, _p, _p, _p, _p]),
     "qk_router_topk_logits": (_i, [_p, _p, _i, _i, _i, _p, _p, _p, _p]),
+    "qk_router_logits": (_i, [_p, _p, _i, _i, _i, _p, _p]),
+    "qk_linear_bf16_workspace_bytes": (_sz, [_i64, _i64, _i64]),
+    "qk_linear_bf16": (_i, [_p, _i64, _i64, _p, _i64, _p, _p, _sz, _p]),
+    "qk_linear_bf16_check": (_i, [_p, _p]),
+    "qk_router_select_shared": (_i, [_p, _p, _i, _i, _i, _p, _p, _i, _i, _i, _p, _p, _p]),
     "qk_moe_workspace_bytes": (_sz, [ctypes.POINTER(MoeDesc), _i]),
     "qk_moe_forward": (
         _i,
@@ -114,6 +119,7 @@ SIGNATURES = {
         [_p, _p, _p, _p, _p, _i, _i, _i, _i, _i, ctypes.c_float, _p, _p, _p, _p, _p],
     ),
     "qk_residual_add": (_i, [_p, _p, _i64, _p, _p]),
+    "qk_residual_rms_norm": (_i, [_p, _p, _p, _i, _i, ctypes.c_float, _p, _p, _p]),
     "qk_append_shared_route": (_i, [_p, _p, _i, _i, _p, _p, _i, _i, _p, _p, _p]),
     "qk_append_shared_route_ep": (_i, [_p, _p, _i, _i, _p, _p, _i, _i, _i, _p, _p, _p]),
     "qk_ep_plan": (_i, [_p, _p, _i, _i, _i, _i, _p, _p, _p, _p, _p, _p]),

@@ -7,13 +7,13 @@ layer, following the reference's layer order (attention_cache.py:128-172 then
 math.py:277-284 and the routed FFN, engine.py:193-204), with a plain pre-norm residual:
 
     h  = rms(x, attn_norm)
-    q | gate, k, v = h @ [Wq; Wk; Wv]^T                       (cuBLAS, BF16)
+    q | gate, k, v = h @ [Wq; Wk; Wv]^T                       (qk_linear_bf16)
     q, k = rope(rms(q, q_norm)), rope(rms(k, k_norm))          (qk_qk_norm_rope)
     cache <- Q8(k, v) at time positions[b]                      (qk_kv_q8_append)
     o  = decode attention over the cache with the gate         (qk_kv_q8_decode_attention)
-    x  = x + o @ Wo^T                                           (cuBLAS + qk_residual_add)
+    x  = x + o @ Wo^T                     (qk_linear_bf16 + qk_residual_rms_norm)
     h2 = rms(x, ffn_norm)
-    ids, w = router top-k(h2)                                   (qk_router_topk)
+    ids, w = router top-k(h2)              (qk_router_logits + qk_router_topk_logits)
     ids, w += (shared, sigmoid(h2 . w_shared_router))            (qk_append_shared_route)
     x  = x + experts(h2, ids, w)                                (qk_moe_forward, routed + shared)
 
@@ -209,8 +209,15 @@ class DecodeState:
         self.a = torch.empty((batch, H), **bf)
         self.y = torch.empty((batch, H), **bf)
         k = cfg.top_k
-        self.ids = torch.empty((batch, k), dtype=torch.int32, device=dev)
-        self.w = torch.empty((batch, k), **bf)
+        self.logits = torch.empty((batch, cfg.experts), dtype=torch.float32, device=dev)
+        # the attention projections: this library's tcgen05 pass up to 256 rows, a library GEMM
+        # beyond (their zeroed workspaces are reused by every call)
+        self.own_linear = batch <= 256
+        if self.own_linear:
+            from .packed import linear_workspace
+
+            self.lin_qkv = (self.qkv.shape[1], linear_workspace(batch, H, self.qkv.shape[1], dev))
+            self.lin_o = (H, linear_workspace(batch, hq * hd, H, dev))
         self.ids_all = [torch.empty((batch, k + 1), dtype=torch.int32, device=dev) for _ in range(cfg.layers)]
         self.w_all = torch.empty((batch, k + 1), **bf)
         lib = _lib.load()
@@ -235,10 +242,16 @@ class DecodeState:
         P = _lib.ptr
         B, H, hq, kv, hd = self.batch, cfg.hidden, cfg.query_heads, cfg.kv_heads, cfg.head_dim
         T = cfg.context
+        nl = len(m.layers)
+        # the first layer's attention norm; every later one runs with the residual add before it
+        _lib.check(lib.qk_rms_norm(P(self.x), P(m.layers[0].attn_norm), B, H, cfg.eps, P(self.h), st))
         for li, L in enumerate(m.layers):
             cache = self.caches[li]
-            _lib.check(lib.qk_rms_norm(P(self.x), P(L.attn_norm), B, H, cfg.eps, P(self.h), st))
-            torch.matmul(self.h, L.w_qkv.t(), out=self.qkv)
+            if self.own_linear:
+                n, ws = self.lin_qkv
+                _lib.check(lib.qk_linear_bf16(P(self.h), B, H, P(L.w_qkv), n, P(self.qkv), P(ws), ws.numel(), st))
+            else:
+                torch.matmul(self.h, L.w_qkv.t(), out=self.qkv)
             _lib.check(lib.qk_qk_norm_rope(P(self.qkv), P(L.q_norm), P(L.k_norm), P(m.inv_freq), P(self.positions),
                                            B, hq, kv, hd, cfg.rotary_dim, cfg.eps, P(self.q), P(self.gate), P(self.k),
                                            P(self.v), st))
@@ -249,36 +262,48 @@ class DecodeState:
                 P(self.q), P(cache["k"]), P(cache["v"]), P(cache["k_scale"]), P(cache["v_scale"]), P(self.indices),
                 None, P(self.positions), P(self.gate), B, T, T, hq, kv, hd, P(self.o),
                 P(self.attn_ws) if self.attn_ws_bytes else None, self.attn_ws_bytes, st))
-            torch.matmul(self.o.view(B, hq * hd), L.w_o.t(), out=self.a)
-            _lib.check(lib.qk_residual_add(P(self.x), P(self.a), B * H, P(self.x), st))
-            _lib.check(lib.qk_rms_norm(P(self.x), P(L.ffn_norm), B, H, cfg.eps, P(self.h), st))
-            _lib.check(lib.qk_router_topk(P(self.h), P(L.router), None, B, H, cfg.experts, cfg.top_k, P(self.ids),
-                                          P(self.w), None, st))
+            if self.own_linear:
+                n, ws = self.lin_o
+                _lib.check(lib.qk_linear_bf16(P(self.o), B, hq * hd, P(L.w_o), n, P(self.a), P(ws), ws.numel(), st))
+            else:
+                torch.matmul(self.o.view(B, hq * hd), L.w_o.t(), out=self.a)
+            _lib.check(lib.qk_residual_rms_norm(P(self.x), P(self.a), P(L.ffn_norm), B, H, cfg.eps, P(self.x),
+                                                P(self.h), st))
+            # the router's logits over ~E / 4 CTAs, then one CTA per token for the selection and
+            # the shared expert's route: the ids and weights of qk_router_topk +
+            # qk_append_shared_route, whose 8-CTA clusters read the whole FP32 router matrix per
+            # 8 tokens
+            _lib.check(lib.qk_router_logits(P(self.h), P(L.router), B, H, cfg.experts, P(self.logits), st))
             ids_all = self.ids_all[li]
+            shared_id, per = (cfg.experts, 0) if self.ep is None else (m.rank * (m.per + 1) + m.per, m.per)
+            _lib.check(lib.qk_router_select_shared(P(self.logits), None, B, cfg.experts, cfg.top_k, P(self.h),
+                                                   P(L.shared_router), H, shared_id, per, P(ids_all),
+                                                   P(self.w_all), st))
             if self.ep is None:
-                _lib.check(lib.qk_append_shared_route(P(self.ids), P(self.w), B, cfg.top_k, P(self.h),
-                                                      P(L.shared_router), H, cfg.experts, P(ids_all), P(self.w_all),
-                                                      st))
                 _lib.check(lib.qk_moe_forward(m.desc, P(L.experts["gate"]), P(L.experts["up"]),
                                               P(L.experts["down"]), P(self.h), P(ids_all), P(self.w_all), B,
                                               _lib.QK_OUT_BF16, P(self.y), P(self.moe_ws), self.moe_ws_bytes, st))
             else:
-                _lib.check(lib.qk_append_shared_route_ep(P(self.ids), P(self.w), B, cfg.top_k, P(self.h),
-                                                         P(L.shared_router), H, m.per, m.rank, P(ids_all),
-                                                         P(self.w_all), st))
                 self.ep(L.experts["gate"], L.experts["up"], L.experts["down"], self.h, ids_all, self.w_all,
                         out=self.y)
-            _lib.check(lib.qk_residual_add(P(self.x), P(self.y), B * H, P(self.x), st))
+            if li + 1 < nl:  # the residual add and the next layer's attention norm
+                _lib.check(lib.qk_residual_rms_norm(P(self.x), P(self.y), P(m.layers[li + 1].attn_norm), B, H,
+                                                    cfg.eps, P(self.x), P(self.h), st))
+            else:
+                _lib.check(lib.qk_residual_add(P(self.x), P(self.y), B * H, P(self.x), st))
         return self.x
 
     def launches_per_step(self):
-        # rms, norm/rope, append, attention (split + merge when split), residual, rms, router,
-        # shared route, MoE (route, dispatch, gate/up, down, combine; expert parallel: dispatch,
-        # wait, route, dispatch, gate/up, down, combine-and-return, final combine), residual;
-        # plus 2 GEMMs
+        # per layer: norm/rope, append, attention (split + merge when split), residual + FFN
+        # norm, router logits, router selection + shared route, MoE (route, dispatch, gate/up,
+        # down, combine; expert parallel: dispatch, wait, route, dispatch, gate/up, down,
+        # combine-and-return, final combine), residual (+ the next layer's attention norm);
+        # the first layer's attention norm; the 2 projections per layer (this library's, or
+        # library GEMMs above 256 rows)
         attn = 2 if self.attn_ws_bytes else 1
         moe = 5 if self.ep is None else 8
-        return self.model.cfg.layers * (9 + attn + moe), self.model.cfg.layers * 2
+        own = 2 if self.own_linear else 0
+        return self.model.cfg.layers * (6 + attn + moe + own) + 1, self.model.cfg.layers * (2 - own)
 
     def close(self):
         if self.ep is not None:

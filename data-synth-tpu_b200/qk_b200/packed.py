@@ -255,3 +255,33 @@ def q6_matmul(x, packed, scales=None, *, output_features, batch_tile=8):
     ):
         raise ValueError("Packed Q6 dtype/shape does not match projection dimensions")
     return quant_matmul(x, packed)
+
+
+def linear_workspace(M, K, N, device):
+    """A zeroed workspace for ``qk_linear_bf16`` at these sizes (zeroed once; every call leaves
+    it ready for the next)."""
+    nbytes = int(_lib.load().qk_linear_bf16_workspace_bytes(M, K, N))
+    if nbytes == 0:
+        raise ValueError("linear_bf16 takes 1 <= M <= 256 rows and K a multiple of 64")
+    return torch.zeros(nbytes, dtype=torch.uint8, device=device)
+
+
+def linear_bf16(x, weight, out=None, workspace=None):
+    """``linear(x, weight)`` of ``qwen38_tpu/math.py:10-16`` for BF16 operands at decode batch
+    sizes: ``bf16(x @ weight^T)`` with FP32 accumulation on the tensor core (x: BF16 [M, K],
+    1 <= M <= 256; weight: BF16 [N, K])."""
+    if x.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16 or x.dim() != 2 or weight.dim() != 2:
+        raise TypeError("x and weight must be BF16 matrices")
+    M, K = x.shape
+    N = weight.shape[0]
+    if weight.shape[1] != K:
+        raise ValueError("weight must be [N, K] for x [M, K]")
+    x, weight = x.contiguous(), weight.contiguous()
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.bfloat16, device=x.device)
+    if workspace is None:
+        workspace = linear_workspace(M, K, N, x.device)
+    with torch.cuda.device(x.device):
+        _lib.call("qk_linear_bf16", _lib.ptr(x), M, K, _lib.ptr(weight), N, _lib.ptr(out), _lib.ptr(workspace),
+                  workspace.numel(), _lib.stream_handle(x.device))
+    return out

@@ -36,6 +36,26 @@ def routes(x, router_weight, top_k, active=None, *, return_probs=False):
     return (ids, weights, probs) if return_probs else (ids, weights)
 
 
+def router_logits(x, router_weight, out=None):
+    """FP32 logits ``x @ Wr^T`` ``[T, E]`` (the linear of ``math.py:277-281``) over many CTAs,
+    with the same values ``routes`` selects from; ``routes_from_logits(router_logits(x, w), k)``
+    equals ``routes(x, w, k)``."""
+    if x.dtype != torch.bfloat16 or x.dim() != 2:
+        raise TypeError("x must be a BF16 [T, H] tensor")
+    router_weight = router_weight.to(device=x.device, dtype=torch.float32).contiguous()
+    T, H = x.shape
+    E = router_weight.shape[0]
+    if router_weight.shape[1] != H:
+        raise ValueError("router weight must be [E, hidden]")
+    x = x.contiguous()
+    if out is None:
+        out = torch.empty((T, E), dtype=torch.float32, device=x.device)
+    with torch.cuda.device(x.device):
+        _lib.call("qk_router_logits", _lib.ptr(x), _lib.ptr(router_weight), T, H, E, _lib.ptr(out),
+                  _lib.stream_handle(x.device))
+    return out
+
+
 def routes_from_logits(logits, top_k, active=None, *, return_probs=False):
     """The same selection from precomputed FP32 logits ``[T, E]``."""
     logits = logits.to(torch.float32).contiguous()

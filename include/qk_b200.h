@@ -119,6 +119,22 @@ int qk_q8_matmul(const uint16_t* x, int64_t M, int64_t K, const uint8_t* w_tiled
                  int out_dtype, void* out, void* workspace, size_t workspace_bytes,
                  qk_stream_t stream);
 
+/* ---- dense BF16 projection (decode batches) -------------------------------------
+ * Replaces qwen38_tpu/math.py:10-16 linear(x, weight) for BF16 operands, as the decoder's
+ * attention projections call it (attention_cache.py:131-134 q|gate, k, v; :171 out):
+ * y = bf16(x @ w^T) with FP32 accumulation. x: BF16 [M, K] (1 <= M <= 256, K a multiple of
+ * 64); w: BF16 [N, K]; y: BF16 [M, N]. A tcgen05 pass that streams w once, its K dimension
+ * split over the SMs with FP32 partials added in a fixed order. The workspace (256-byte
+ * aligned, qk_linear_bf16_workspace_bytes) must be zeroed once before its first call; every
+ * call leaves it ready for the next. Calls sharing a workspace must not overlap. */
+size_t qk_linear_bf16_workspace_bytes(int64_t M, int64_t K, int64_t N);
+int qk_linear_bf16(const uint16_t* x, int64_t M, int64_t K, const uint16_t* w, int64_t N,
+                   uint16_t* y, void* workspace, size_t workspace_bytes, qk_stream_t stream);
+/* No counterpart in the reference. QK_ERR_TIMEOUT if a bounded device wait of an earlier
+ * qk_linear_bf16 call on this workspace gave up (its output is then not valid), else QK_OK;
+ * clears the flag. Synchronises `stream`. */
+int qk_linear_bf16_check(const void* workspace, qk_stream_t stream);
+
 /* ---- router ------------------------------------------------------------------
  * Replaces the router of qwen38_tpu/math.py:277-281 (routes_and_shared):
  * probs = softmax(f32(x) @ f32(Wr)^T); (w, ids) = top_k(probs, k) (ties: lower index);
@@ -127,9 +143,28 @@ int qk_q8_matmul(const uint16_t* x, int64_t M, int64_t K, const uint8_t* w_tiled
  * ids: int32 [T, k]; weights: BF16 [T, k]; probs (FP32 [T, E], may be NULL). */
 int qk_router_topk(const uint16_t* x, const float* router_w, const uint8_t* active, int T, int H,
                    int E, int k, int32_t* ids, uint16_t* weights, float* probs, qk_stream_t stream);
-/* Same selection from precomputed FP32 logits [T, E]. */
+/* Same selection from precomputed FP32 logits [T, E] (one warp per token). */
 int qk_router_topk_logits(const float* logits, const uint8_t* active, int T, int E, int k,
                           int32_t* ids, uint16_t* weights, float* probs, qk_stream_t stream);
+/* The router's FP32 logits alone (math.py:277-281's linear(f32(x), f32(Wr)), HIGHEST
+ * precision): logits [T, E] = x @ router_w^T, spread over ceil(E / 4) x ceil(T / 8) CTAs with
+ * the per-row summation order of qk_router_topk, so the values are identical to the ones it
+ * selects from. Followed by qk_router_topk_logits it is qk_router_topk in two launches for
+ * callers that own a [T, E] FP32 buffer (the router matrix is then read by ~E / 4 SMs instead
+ * of one 8-CTA cluster per 8 tokens). */
+int qk_router_logits(const uint16_t* x, const float* router_w, int T, int H, int E, float* logits,
+                     qk_stream_t stream);
+/* qk_router_topk_logits followed by the shared expert's route (math.py:282-283) in one launch:
+ * ids_out / weights_out [T, k + 1] hold each token's k routes, then (shared_id,
+ * bf16(sigmoid(bf16(h . shared_router)))); h: BF16 [T, H], shared_router: BF16 [H]. With
+ * experts_per_rank > 0 routed expert e is written as (e / experts_per_rank) *
+ * (experts_per_rank + 1) + e % experts_per_rank (the numbering of
+ * qk_append_shared_route_ep). Bit-identical to qk_router_topk_logits followed by
+ * qk_append_shared_route[_ep]. */
+int qk_router_select_shared(const float* logits, const uint8_t* active, int T, int E, int k,
+                            const uint16_t* h, const uint16_t* shared_router, int H,
+                            int shared_id, int experts_per_rank, int32_t* ids_out,
+                            uint16_t* weights_out, qk_stream_t stream);
 
 /* ---- routed expert FFN -------------------------------------------------------
  * Replaces the function returned by qwen38_tpu/experts.py:17-140 expert_parallel(mesh,
@@ -379,6 +414,12 @@ int qk_qk_norm_rope(const uint16_t* qkv, const uint16_t* q_norm, const uint16_t*
                     const float* inv_freq, const int32_t* positions, int B, int hq, int kv,
                     int head_dim, int rotary_dim, float eps, uint16_t* q_out,
                     uint16_t* gate_out, uint16_t* k_out, uint16_t* v_out, qk_stream_t stream);
+/* The residual add followed by the next RMSNorm (math.py:27-31), one launch: x_out =
+ * bf16(x + y) [rows, width] (x_out may alias x), out = rms(x_out, gamma, eps). Bit-identical
+ * to qk_residual_add then qk_rms_norm. */
+int qk_residual_rms_norm(const uint16_t* x, const uint16_t* y, const uint16_t* gamma, int rows,
+                         int width, float eps, uint16_t* x_out, uint16_t* out,
+                         qk_stream_t stream);
 /* out = bf16(x + y) over n BF16 values (out may alias x): the residual add. */
 int qk_residual_add(const uint16_t* x, const uint16_t* y, int64_t n, uint16_t* out,
                     qk_stream_t stream);

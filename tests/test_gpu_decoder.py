@@ -233,6 +233,65 @@ def test_expert_parallel_shared_route_renumbers_the_routed_experts(cuda_device):
     np.testing.assert_array_equal(w_ep, outs["plain"][1])
 
 
+def test_residual_rms_norm_is_residual_add_then_rms_norm(cuda_device):
+    """The fused launch gives the bits of qk_residual_add followed by qk_rms_norm, with x_out
+    aliasing x as the decoder step uses it."""
+    import torch
+
+    from qk_b200 import _lib
+
+    rng = np.random.default_rng(21)
+    rows, width = 7, 2048
+    x = bf16_round(rng.normal(size=(rows, width)).astype(np.float32))
+    y = bf16_round(rng.normal(size=(rows, width)).astype(np.float32))
+    g = bf16_round(rng.normal(1, 0.1, width).astype(np.float32))
+    st = _lib.stream_handle(cuda_device)
+    x1, yd, gd = bf16_tensor(x, cuda_device), bf16_tensor(y, cuda_device), bf16_tensor(g, cuda_device)
+    h1 = torch.empty((rows, width), dtype=torch.bfloat16, device=cuda_device)
+    _lib.call("qk_residual_add", _lib.ptr(x1), _lib.ptr(yd), rows * width, _lib.ptr(x1), st)
+    _lib.call("qk_rms_norm", _lib.ptr(x1), _lib.ptr(gd), rows, width, 1e-6, _lib.ptr(h1), st)
+    x2 = bf16_tensor(x, cuda_device)
+    h2 = torch.empty_like(h1)
+    _lib.call("qk_residual_rms_norm", _lib.ptr(x2), _lib.ptr(yd), _lib.ptr(gd), rows, width, 1e-6, _lib.ptr(x2),
+              _lib.ptr(h2), st)
+    assert torch.equal(x1.view(torch.int16), x2.view(torch.int16))
+    assert torch.equal(h1.view(torch.int16), h2.view(torch.int16))
+
+
+@pytest.mark.parametrize("per", [0, 64])
+def test_router_select_shared_is_topk_then_shared_route(cuda_device, per):
+    """qk_router_select_shared gives the bits of qk_router_topk_logits followed by
+    qk_append_shared_route (per = 0) or its expert-parallel form (per > 0)."""
+    import torch
+
+    from qk_b200 import _lib
+
+    rng = np.random.default_rng(22 + per)
+    B, E, k, H, rank = 11, 512, 10, 2048, 3
+    logits = torch.from_numpy(rng.normal(0, 1, (B, E)).astype(np.float32)).to(cuda_device)
+    h = bf16_tensor(rng.normal(size=(B, H)).astype(np.float32), cuda_device)
+    wsr = bf16_tensor(rng.normal(0, 0.02, H).astype(np.float32), cuda_device)
+    st = _lib.stream_handle(cuda_device)
+    ids = torch.empty((B, k), dtype=torch.int32, device=cuda_device)
+    w = torch.empty((B, k), dtype=torch.bfloat16, device=cuda_device)
+    _lib.call("qk_router_topk_logits", _lib.ptr(logits), None, B, E, k, _lib.ptr(ids), _lib.ptr(w), None, st)
+    ref_ids = torch.empty((B, k + 1), dtype=torch.int32, device=cuda_device)
+    ref_w = torch.empty((B, k + 1), dtype=torch.bfloat16, device=cuda_device)
+    shared_id = E if per == 0 else rank * (per + 1) + per
+    if per == 0:
+        _lib.call("qk_append_shared_route", _lib.ptr(ids), _lib.ptr(w), B, k, _lib.ptr(h), _lib.ptr(wsr), H, E,
+                  _lib.ptr(ref_ids), _lib.ptr(ref_w), st)
+    else:
+        _lib.call("qk_append_shared_route_ep", _lib.ptr(ids), _lib.ptr(w), B, k, _lib.ptr(h), _lib.ptr(wsr), H, per,
+                  rank, _lib.ptr(ref_ids), _lib.ptr(ref_w), st)
+    got_ids = torch.empty_like(ref_ids)
+    got_w = torch.empty_like(ref_w)
+    _lib.call("qk_router_select_shared", _lib.ptr(logits), None, B, E, k, _lib.ptr(h), _lib.ptr(wsr), H, shared_id,
+              per, _lib.ptr(got_ids), _lib.ptr(got_w), st)
+    assert torch.equal(got_ids, ref_ids)
+    assert torch.equal(got_w.view(torch.int16), ref_w.view(torch.int16))
+
+
 def _two_gpu_stack_rank(rank, world, port, path):
     import datetime
     import os

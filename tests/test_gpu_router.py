@@ -52,3 +52,23 @@ def test_router_ties_go_to_lower_index(cuda_device):
     ids_o, w_o, _ = moe.routes(None, None, 3, logits=logits)
     np.testing.assert_array_equal(ids.cpu().numpy(), ids_o)
     np.testing.assert_array_equal(to_f32(weights), w_o)
+
+
+@pytest.mark.parametrize("T,E,k", [(1, 512, 10), (8, 512, 10), (13, 64, 4), (64, 512, 10), (37, 256, 1)])
+def test_two_launch_router_equals_the_one_launch_router(cuda_device, T, E, k):
+    """router_logits (many CTAs) + routes_from_logits (a warp per token) give the ids, weights
+    and probabilities of the one-launch cluster router bit for bit."""
+    import torch
+
+    from qk_b200.routing import router_logits, routes, routes_from_logits
+
+    rng = np.random.default_rng(T * 7 + E)
+    x = bf16_tensor(rng.normal(size=(T, 2048)).astype(np.float32), cuda_device)
+    w = torch.from_numpy(rng.normal(0, 0.02, (E, 2048)).astype(np.float32)).to(cuda_device)
+    active = torch.from_numpy(np.arange(T) % 5 != 2).to(cuda_device)
+    ids1, w1, p1 = routes(x, w, k, active, return_probs=True)
+    logits = router_logits(x, w)
+    ids2, w2, p2 = routes_from_logits(logits, k, active, return_probs=True)
+    assert torch.equal(ids1, ids2)
+    assert torch.equal(w1.view(torch.int16), w2.view(torch.int16))
+    assert torch.equal(p1.view(torch.int32), p2.view(torch.int32))
