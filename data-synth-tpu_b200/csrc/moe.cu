@@ -420,23 +420,28 @@ __global__ void __launch_bounds__(256) moe_dispatch_kernel(const uint16_t* __res
 // ------------------------------------------------------------------------------------
 constexpr int kMaxTopK = 32;
 
-// One warp per token: lane j < k holds route j's entry, and its rank among the token's
-// entries by expert id gives the reference's ascending-expert accumulation order
-// (experts.py:129); lane i then learns which lane holds rank i. Each lane owns 8 columns of
-// every 256-column block and walks the row in groups of 4 blocks: for two routes at a time it
-// loads all 8 of its 16-byte pieces before adding them, in rank order, into FP32 sums, so the
-// loads of a warp are in flight together and the route metadata is read once per token.
+// One warp per (token, group of KG 256-column blocks): lane j < k holds route j's entry, and
+// its rank among the token's entries by expert id gives the reference's ascending-expert
+// accumulation order (experts.py:129); lane i then learns which lane holds rank i. Each lane
+// owns 8 columns of each block of the group: for KR routes at a time it loads all KR x KG of
+// its 16-byte pieces before adding them, in rank order, into FP32 sums, so the loads of a warp
+// are in flight together. Many tokens: KG = 4, KR = 2 (the route metadata is read twice per
+// token at H = 2048); few tokens (a decode batch): KG = 1, KR = 8, so the warps of a small
+// batch are eight times as many and each waits for fewer rounds of loads. The sums do not
+// depend on KG or KR.
 // With `yr` (tensor parallel: the FP32 down projection of each route, summed over the tensor
 // ranks) the expert output of route (b, j) is bf16(yr[b * k + j]) (grouped_experts.py:
 // 113-119: psum before the BF16 rounding); otherwise the entry's BF16 y.
+template <int kG, int kR>
 __global__ void __launch_bounds__(256) moe_combine_kernel(const int32_t* __restrict__ ids, int B,
                                                           int k, int H, int out_bf16, void* out,
                                                           const float* __restrict__ yr, Workspace ws) {
-  constexpr int kG = 4;  // 256-column blocks per group
   pdl_wait();
   const int lane = threadIdx.x & 31;
-  const int b = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  if (b >= B) return;
+  const int blocks = H / 256, ngroups = (blocks + kG - 1) / kG;
+  const int wi_ = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (wi_ >= B * ngroups) return;
+  const int b = wi_ / ngroups, g0 = (wi_ - b * ngroups) * kG;
   const int entry = lane < k ? ws.route_entry[b * k + lane] : -1;
   const int eid = entry >= 0 ? ids[b * k + lane] : 0x7fffffff;
   const float w = entry >= 0 ? ws.entry_weight[entry] : 0.f;
@@ -452,18 +457,17 @@ __global__ void __launch_bounds__(256) moe_combine_kernel(const int32_t* __restr
     const int vj = __shfl_sync(0xffffffffu, entry, j) >= 0;
     if (vj && rj == lane) src_of_rank = j;
   }
-  const int blocks = H / 256;
-  for (int g0 = 0; g0 < blocks; g0 += kG) {
+  {
     float acc[kG][8];
 #pragma unroll
     for (int q = 0; q < kG; ++q)
 #pragma unroll
       for (int t = 0; t < 8; ++t) acc[q][t] = 0.f;
-    for (int i0 = 0; i0 < n; i0 += 2) {
-      uint4 v[2][kG];
-      float wi[2];
+    for (int i0 = 0; i0 < n; i0 += kR) {
+      uint4 v[kR][kG];
+      float wi[kR];
 #pragma unroll
-      for (int u = 0; u < 2; ++u) {
+      for (int u = 0; u < kR; ++u) {
         const int i = i0 + u;
         const int src = __shfl_sync(0xffffffffu, src_of_rank, i < n ? i : 0);
         const int ent = __shfl_sync(0xffffffffu, entry, src);
@@ -486,7 +490,7 @@ __global__ void __launch_bounds__(256) moe_combine_kernel(const int32_t* __restr
         }
       }
 #pragma unroll
-      for (int u = 0; u < 2; ++u) {
+      for (int u = 0; u < kR; ++u) {
         if (i0 + u >= n) break;
 #pragma unroll
         for (int q = 0; q < kG; ++q) {
@@ -517,6 +521,19 @@ __global__ void __launch_bounds__(256) moe_combine_kernel(const int32_t* __restr
       }
     }
   }
+}
+
+// The combine's form: a warp per (token, 4 blocks) with 2 routes in flight for many tokens,
+// a warp per (token, block) with 8 routes in flight for a decode batch.
+template <typename... Args>
+cudaError_t launch_combine(int B, int H, cudaStream_t st, Args... args) {
+  const int blocks = H / 256;
+  if (static_cast<int64_t>(B) * blocks <= 2048) {
+    const int warps = B * blocks;
+    return launch_dependent(moe_combine_kernel<1, 8>, dim3((warps + 7) / 8), dim3(256), 0, st, args...);
+  }
+  const int warps = B * ((blocks + 3) / 4);
+  return launch_dependent(moe_combine_kernel<4, 2>, dim3((warps + 7) / 8), dim3(256), 0, st, args...);
 }
 
 __global__ void cast_kernel(const float* __restrict__ in, uint16_t* __restrict__ out, int64_t n) {
@@ -736,7 +753,7 @@ static int moe_forward_impl(const qk_moe_desc* desc, const uint8_t* gate, const 
   };
 
   if (phase == kCombine) {
-    const cudaError_t e = launch_dependent(moe_combine_kernel, dim3((B + 7) / 8), dim3(256), 0, st, ids, B, d.top_k,
+    const cudaError_t e = launch_combine(B, d.hidden, st, ids, B, d.top_k,
                                            d.hidden, static_cast<int>(out_dtype == QK_OUT_BF16), out,
                                            static_cast<const float*>(yr), ws);
     if (e != cudaSuccess) return cuda_error(e, "moe_combine_kernel");
@@ -871,7 +888,7 @@ static int moe_forward_impl(const qk_moe_desc* desc, const uint8_t* gate, const 
     return QK_OK;
   }
   {
-    const cudaError_t e = launch_dependent(moe_combine_kernel, dim3((B + 7) / 8), dim3(256), 0, st, ids, B, d.top_k,
+    const cudaError_t e = launch_combine(B, d.hidden, st, ids, B, d.top_k,
                                            d.hidden, static_cast<int>(out_dtype == QK_OUT_BF16), out,
                                            static_cast<const float*>(nullptr), ws);
     if (e != cudaSuccess) return cuda_error(e, "moe_combine_kernel");
