@@ -296,6 +296,48 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
   return s;
 }
 
+// One-block-per-row kernels (256 threads) hold a BF16 row of up to kRowChunks x 256 x 8
+// values in registers, 8 values per 16-byte chunk: thread t takes chunks t, t + 256, ...,
+// issues all its loads before using them and accumulates chunk by chunk in value order;
+// block_sum then adds the threads. Kernels that share this layout give the same bits.
+constexpr int kRowBlock = 256;
+constexpr int kRowChunks = 4;
+constexpr int kMaxRowWidth = kRowChunks * kRowBlock * 8;  // 8192 values
+
+__device__ __forceinline__ void unpack8(const uint4& v, float (&f)[8]) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int t = 0; t < 4; ++t) {
+    f[2 * t] = __uint_as_float(w[t] << 16);
+    f[2 * t + 1] = __uint_as_float(w[t] & 0xffff0000u);
+  }
+}
+
+// Dot product of a BF16 row of H values with a BF16 vector in the row layout (FP32 fused
+// multiply-adds), rounded to BF16: the shared expert's gate logit bf16(h . wsr)
+// (math.py:282-283). Every thread of the 256-thread block calls it.
+__device__ __forceinline__ float row_dot_bf16(const uint16_t* hrow, const uint16_t* wsr, int H, float* red) {
+  const int nch = H / 8;
+  uint4 a[kRowChunks], b[kRowChunks];
+#pragma unroll
+  for (int c = 0; c < kRowChunks; ++c) {
+    const int i = threadIdx.x + c * kRowBlock;
+    a[c] = i < nch ? reinterpret_cast<const uint4*>(hrow)[i] : make_uint4(0, 0, 0, 0);
+    b[c] = i < nch ? reinterpret_cast<const uint4*>(wsr)[i] : make_uint4(0, 0, 0, 0);
+  }
+  float s = 0.f;
+#pragma unroll
+  for (int c = 0; c < kRowChunks; ++c) {
+    if (threadIdx.x + c * kRowBlock >= nch) break;
+    float f[8], g[8];
+    unpack8(a[c], f);
+    unpack8(b[c], g);
+#pragma unroll
+    for (int t = 0; t < 8; ++t) s = fmaf(f[t], g[t], s);
+  }
+  return bf16_round(block_sum(s, red));
+}
+
 __device__ __forceinline__ uint4 ld_nc_v4(const void* p) {
   uint4 r;
   asm("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];"

@@ -11,7 +11,43 @@ namespace {
 
 constexpr int kRowThreads = 256;
 
-// math.py:27-31 rms: bf16(xf * rsqrt(mean(xf^2) + eps) * gamma), one block per row.
+static_assert(kRowThreads == kRowBlock, "the row kernels use the common row layout");
+
+__device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
+  uint32_t w[4];
+#pragma unroll
+  for (int t = 0; t < 4; ++t)
+    w[t] = static_cast<uint32_t>(bf16_bits_rne(f[2 * t])) | (static_cast<uint32_t>(bf16_bits_rne(f[2 * t + 1])) << 16);
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// out = bf16(v * r * gamma) for the row's chunks held in registers, r = rsqrt(mean(v^2) + eps)
+// from the threads' sums of squares `ss` (math.py:27-31).
+__device__ __forceinline__ void rms_finish(const uint4 (&v)[kRowChunks], float ss, float* red, const uint16_t* gamma,
+                                           int width, float eps, uint16_t* orow) {
+  const int nch = width / 8;
+  const float r = rsqrtf(__fadd_rn(__fdiv_rn(block_sum(ss, red), static_cast<float>(width)), eps));
+  uint4 g[kRowChunks];
+#pragma unroll
+  for (int c = 0; c < kRowChunks; ++c) {
+    const int i = threadIdx.x + c * kRowThreads;
+    g[c] = i < nch ? reinterpret_cast<const uint4*>(gamma)[i] : make_uint4(0, 0, 0, 0);
+  }
+#pragma unroll
+  for (int c = 0; c < kRowChunks; ++c) {
+    const int i = threadIdx.x + c * kRowThreads;
+    if (i >= nch) break;
+    float f[8], gf[8];
+    unpack8(v[c], f);
+    unpack8(g[c], gf);
+#pragma unroll
+    for (int t = 0; t < 8; ++t) f[t] = __fmul_rn(__fmul_rn(f[t], r), gf[t]);
+    reinterpret_cast<uint4*>(orow)[i] = pack8(f);
+  }
+}
+
+// math.py:27-31 rms: bf16(xf * rsqrt(mean(xf^2) + eps) * gamma), one block per row, the row
+// held in registers (one round of loads instead of one per 256 values).
 __global__ void __launch_bounds__(kRowThreads) rms_norm_kernel(const uint16_t* __restrict__ x,
                                                                const uint16_t* __restrict__ gamma, int width,
                                                                float eps, uint16_t* __restrict__ out) {
@@ -19,20 +55,29 @@ __global__ void __launch_bounds__(kRowThreads) rms_norm_kernel(const uint16_t* _
   pdl_trigger();
   __shared__ float red[kRowThreads / 32];
   const int64_t row = blockIdx.x;
-  const uint16_t* xr = x + row * width;
-  float ss = 0.f;
-  for (int i = threadIdx.x; i < width; i += blockDim.x) {
-    const float v = bf16_to_f32(xr[i]);
-    ss = fmaf(v, v, ss);
+  const uint4* xr = reinterpret_cast<const uint4*>(x + row * width);
+  const int nch = width / 8;
+  uint4 v[kRowChunks];
+#pragma unroll
+  for (int c = 0; c < kRowChunks; ++c) {
+    const int i = threadIdx.x + c * kRowThreads;
+    v[c] = i < nch ? xr[i] : make_uint4(0, 0, 0, 0);
   }
-  const float r = rsqrtf(__fadd_rn(__fdiv_rn(block_sum(ss, red), static_cast<float>(width)), eps));
-  for (int i = threadIdx.x; i < width; i += blockDim.x)
-    out[row * width + i] = bf16_bits_rne(__fmul_rn(__fmul_rn(bf16_to_f32(xr[i]), r), bf16_to_f32(gamma[i])));
+  float ss = 0.f;
+#pragma unroll
+  for (int c = 0; c < kRowChunks; ++c) {
+    if (threadIdx.x + c * kRowThreads >= nch) break;
+    float f[8];
+    unpack8(v[c], f);
+#pragma unroll
+    for (int t = 0; t < 8; ++t) ss = fmaf(f[t], f[t], ss);
+  }
+  rms_finish(v, ss, red, gamma, width, eps, out + row * width);
 }
 
 // The residual add and the RMSNorm that follows it, one block per row: xo = bf16(x + y)
 // (stored; xo may alias x), then out = rms(xo) as rms_norm_kernel computes it (the same
-// thread layout and reduction over the stored BF16 values), so one launch gives the bits of
+// chunk layout and reduction over the BF16 sums), so one launch gives the bits of
 // qk_residual_add + qk_rms_norm.
 __global__ void __launch_bounds__(kRowThreads) residual_rms_norm_kernel(const uint16_t* x, const uint16_t* __restrict__ y,
                                                                         const uint16_t* __restrict__ gamma, int width,
@@ -42,16 +87,33 @@ __global__ void __launch_bounds__(kRowThreads) residual_rms_norm_kernel(const ui
   pdl_trigger();
   __shared__ float red[kRowThreads / 32];
   const int64_t row = blockIdx.x;
-  float ss = 0.f;
-  for (int i = threadIdx.x; i < width; i += blockDim.x) {
-    const uint16_t b = bf16_bits_rne(__fadd_rn(bf16_to_f32(x[row * width + i]), bf16_to_f32(y[row * width + i])));
-    xo[row * width + i] = b;
-    const float v = bf16_to_f32(b);
-    ss = fmaf(v, v, ss);
+  const uint4* xr = reinterpret_cast<const uint4*>(x + row * width);
+  const uint4* yr = reinterpret_cast<const uint4*>(y + row * width);
+  const int nch = width / 8;
+  uint4 v[kRowChunks], u[kRowChunks];
+#pragma unroll
+  for (int c = 0; c < kRowChunks; ++c) {
+    const int i = threadIdx.x + c * kRowThreads;
+    v[c] = i < nch ? xr[i] : make_uint4(0, 0, 0, 0);
+    u[c] = i < nch ? yr[i] : make_uint4(0, 0, 0, 0);
   }
-  const float r = rsqrtf(__fadd_rn(__fdiv_rn(block_sum(ss, red), static_cast<float>(width)), eps));
-  for (int i = threadIdx.x; i < width; i += blockDim.x)
-    out[row * width + i] = bf16_bits_rne(__fmul_rn(__fmul_rn(bf16_to_f32(xo[row * width + i]), r), bf16_to_f32(gamma[i])));
+  float ss = 0.f;
+#pragma unroll
+  for (int c = 0; c < kRowChunks; ++c) {
+    const int i = threadIdx.x + c * kRowThreads;
+    if (i >= nch) break;
+    float f[8], g[8];
+    unpack8(v[c], f);
+    unpack8(u[c], g);
+#pragma unroll
+    for (int t = 0; t < 8; ++t) f[t] = __fadd_rn(f[t], g[t]);
+    v[c] = pack8(f);  // the BF16 sum: stored, and the RMSNorm's input
+    reinterpret_cast<uint4*>(xo + row * width)[i] = v[c];
+    unpack8(v[c], f);
+#pragma unroll
+    for (int t = 0; t < 8; ++t) ss = fmaf(f[t], f[t], ss);
+  }
+  rms_finish(v, ss, red, gamma, width, eps, out + row * width);
 }
 
 // attention_cache.py:129-135: the fused projection output of one row is
@@ -126,9 +188,7 @@ __global__ void __launch_bounds__(kRowThreads) append_shared_route_kernel(
   pdl_trigger();
   __shared__ float red[kRowThreads / 32];
   const int64_t b = blockIdx.x;
-  float s = 0.f;
-  for (int i = threadIdx.x; i < H; i += blockDim.x) s = fmaf(bf16_to_f32(h[b * H + i]), bf16_to_f32(wsr[i]), s);
-  const float dot = bf16_round(block_sum(s, red));
+  const float dot = row_dot_bf16(h + b * H, wsr, H, red);
   if (threadIdx.x < k) {
     const int e = ids[b * k + threadIdx.x];
     ids_out[b * (k + 1) + threadIdx.x] = per > 0 && e >= 0 ? (e / per) * (per + 1) + e % per : e;
@@ -149,9 +209,12 @@ extern "C" {
 
 int qk_rms_norm(const uint16_t* x, const uint16_t* gamma, int rows, int width, float eps, uint16_t* out,
                 qk_stream_t stream) {
-  QK_REQUIRE(rows >= 0 && width > 0, "invalid rms geometry");
+  QK_REQUIRE(rows >= 0 && width > 0 && width % 8 == 0 && width <= kMaxRowWidth,
+             "rms width must be a positive multiple of 8 up to %d", kMaxRowWidth);
   if (rows == 0) return QK_OK;
   QK_REQUIRE(x && gamma && out, "null pointer");
+  QK_REQUIRE(((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(gamma) | reinterpret_cast<uintptr_t>(out)) & 15) == 0,
+             "x, gamma and out must be 16-byte aligned");
   const cudaError_t e = launch_dependent(rms_norm_kernel, dim3(rows), dim3(kRowThreads), 0, as_stream(stream), x, gamma,
                                          width, eps, out);
   if (e != cudaSuccess) return cuda_error(e, "rms_norm_kernel");
@@ -161,9 +224,13 @@ int qk_rms_norm(const uint16_t* x, const uint16_t* gamma, int rows, int width, f
 
 int qk_residual_rms_norm(const uint16_t* x, const uint16_t* y, const uint16_t* gamma, int rows, int width, float eps,
                          uint16_t* x_out, uint16_t* out, qk_stream_t stream) {
-  QK_REQUIRE(rows >= 0 && width > 0, "invalid rms geometry");
+  QK_REQUIRE(rows >= 0 && width > 0 && width % 8 == 0 && width <= kMaxRowWidth,
+             "rms width must be a positive multiple of 8 up to %d", kMaxRowWidth);
   if (rows == 0) return QK_OK;
   QK_REQUIRE(x && y && gamma && x_out && out, "null pointer");
+  QK_REQUIRE(((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y) | reinterpret_cast<uintptr_t>(gamma) |
+               reinterpret_cast<uintptr_t>(x_out) | reinterpret_cast<uintptr_t>(out)) & 15) == 0,
+             "x, y, gamma, x_out and out must be 16-byte aligned");
   const cudaError_t e = launch_dependent(residual_rms_norm_kernel, dim3(rows), dim3(kRowThreads), 0, as_stream(stream),
                                          x, y, gamma, width, eps, x_out, out);
   if (e != cudaSuccess) return cuda_error(e, "residual_rms_norm_kernel");
@@ -203,9 +270,12 @@ int qk_residual_add(const uint16_t* x, const uint16_t* y, int64_t n, uint16_t* o
 int qk_append_shared_route(const int32_t* ids, const uint16_t* weights, int B, int k, const uint16_t* h,
                            const uint16_t* shared_router, int H, int shared_id, int32_t* ids_out,
                            uint16_t* weights_out, qk_stream_t stream) {
-  QK_REQUIRE(B >= 0 && k > 0 && k < kRowThreads && H > 0, "invalid route geometry");
+  QK_REQUIRE(B >= 0 && k > 0 && k < kRowThreads && H > 0 && H % 8 == 0 && H <= kMaxRowWidth,
+             "invalid route geometry");
   if (B == 0) return QK_OK;
   QK_REQUIRE(ids && weights && h && shared_router && ids_out && weights_out, "null pointer");
+  QK_REQUIRE(((reinterpret_cast<uintptr_t>(h) | reinterpret_cast<uintptr_t>(shared_router)) & 15) == 0,
+             "h and shared_router must be 16-byte aligned");
   const cudaError_t e = launch_dependent(append_shared_route_kernel, dim3(B), dim3(kRowThreads), 0, as_stream(stream),
                                          ids, weights, k, h, shared_router, H, shared_id, 0, ids_out, weights_out);
   if (e != cudaSuccess) return cuda_error(e, "append_shared_route_kernel");
@@ -216,10 +286,13 @@ int qk_append_shared_route(const int32_t* ids, const uint16_t* weights, int B, i
 int qk_append_shared_route_ep(const int32_t* ids, const uint16_t* weights, int B, int k, const uint16_t* h,
                               const uint16_t* shared_router, int H, int experts_per_rank, int rank,
                               int32_t* ids_out, uint16_t* weights_out, qk_stream_t stream) {
-  QK_REQUIRE(B >= 0 && k > 0 && k < kRowThreads && H > 0, "invalid route geometry");
+  QK_REQUIRE(B >= 0 && k > 0 && k < kRowThreads && H > 0 && H % 8 == 0 && H <= kMaxRowWidth,
+             "invalid route geometry");
   QK_REQUIRE(experts_per_rank > 0 && rank >= 0, "invalid expert partition");
   if (B == 0) return QK_OK;
   QK_REQUIRE(ids && weights && h && shared_router && ids_out && weights_out, "null pointer");
+  QK_REQUIRE(((reinterpret_cast<uintptr_t>(h) | reinterpret_cast<uintptr_t>(shared_router)) & 15) == 0,
+             "h and shared_router must be 16-byte aligned");
   const int shared_id = rank * (experts_per_rank + 1) + experts_per_rank;
   const cudaError_t e = launch_dependent(append_shared_route_kernel, dim3(B), dim3(kRowThreads), 0, as_stream(stream),
                                          ids, weights, k, h, shared_router, H, shared_id, experts_per_rank, ids_out,

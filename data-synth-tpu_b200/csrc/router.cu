@@ -241,9 +241,9 @@ __global__ void __launch_bounds__(kSelectWarps * 32)
 
 // Selection plus the shared expert's route (math.py:282-283), one 256-thread CTA per token:
 // ids_out / w_out [T, k + 1] hold the k routes and then (shared_id, bf16(sigmoid(bf16(h . wsr)))).
-// The dot product has the thread layout and block reduction of qk_append_shared_route, so
-// this launch replaces qk_router_topk_logits + qk_append_shared_route with the same bits.
-constexpr int kSharedThreads = 256;
+// The dot product is qk_append_shared_route's (row_dot_bf16), so this launch replaces
+// qk_router_topk_logits + qk_append_shared_route with the same bits.
+constexpr int kSharedThreads = kRowBlock;
 
 __global__ void __launch_bounds__(kSharedThreads)
     router_select_shared_kernel(const float* __restrict__ logits, const uint8_t* __restrict__ active, int E, int k,
@@ -256,10 +256,7 @@ __global__ void __launch_bounds__(kSharedThreads)
   const int t = blockIdx.x, lane = threadIdx.x & 31;
   if (threadIdx.x < 32)
     for (int e = lane; e < E; e += 32) row_s[e] = logits[static_cast<int64_t>(t) * E + e];
-  float s = 0.f;
-  for (int i = threadIdx.x; i < H; i += blockDim.x)
-    s = fmaf(bf16_to_f32(h[static_cast<int64_t>(t) * H + i]), bf16_to_f32(wsr[i]), s);
-  const float dot = bf16_round(block_sum(s, red));
+  const float dot = row_dot_bf16(h + static_cast<int64_t>(t) * H, wsr, H, red);
   if (threadIdx.x < 32) select_row(row_s, t, E, k, lane, active, ids_out, w_out, nullptr, k + 1, per);
   if (threadIdx.x == 0) {
     ids_out[static_cast<int64_t>(t) * (k + 1) + k] = shared_id;
@@ -342,9 +339,11 @@ int qk_router_select_shared(const float* logits, const uint8_t* active, int T, i
                             const uint16_t* shared_router, int H, int shared_id, int experts_per_rank,
                             int32_t* ids_out, uint16_t* weights_out, qk_stream_t stream) {
   QK_REQUIRE(T >= 0 && E > 0 && k > 0 && k <= E && k <= 32, "Invalid expert top-k");
-  QK_REQUIRE(H > 0 && experts_per_rank >= 0, "invalid route geometry");
+  QK_REQUIRE(H > 0 && H % 8 == 0 && H <= kMaxRowWidth && experts_per_rank >= 0, "invalid route geometry");
   if (T == 0) return QK_OK;
   QK_REQUIRE(logits && h && shared_router && ids_out && weights_out, "null pointer");
+  QK_REQUIRE(((reinterpret_cast<uintptr_t>(h) | reinterpret_cast<uintptr_t>(shared_router)) & 15) == 0,
+             "h and shared_router must be 16-byte aligned");
   const size_t smem = static_cast<size_t>(E) * 4;
   QK_REQUIRE(smem <= 200 * 1024, "too many experts for the router selection kernel (4 E bytes within 200 KB)");
   int rc = allow_smem(reinterpret_cast<const void*>(router_select_shared_kernel), smem);
