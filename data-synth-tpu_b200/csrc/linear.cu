@@ -20,6 +20,12 @@
 // Launched as a programmatic dependent: the W boxes of the first stages are requested before
 // griddepcontrol.wait (no earlier kernel writes W), the x boxes after it. No multicast. Every
 // wait is bounded; on give-up the CTA records QK_ERR_TIMEOUT in the workspace status word.
+//
+// Up to kGemvMaxM rows of x (a decode step of one to four sequences) take linear_gemv_kernel
+// instead: a warp per output column, the row of W streamed with 16-byte loads (eight per lane
+// in flight) against x held in shared memory, FP32 fused multiply-adds and a warp butterfly.
+// An MMA of N = 16 tokens would waste 15/16 of its columns there, and the per-CTA MMA chain,
+// the split-K partials and their ordered sum were most of that pass's time.
 #include <cuda.h>  // CUtensorMap and its enums; the encoder is looked up at run time
 
 #include "umma.cuh"
@@ -52,6 +58,77 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
 }
 
 __device__ __forceinline__ void epilogue_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+constexpr int kGemvMaxM = 4;
+constexpr int kGemvThreads = 256;
+constexpr int kGemvChunks = 8;  // 16-byte chunks of a W row per lane per pass (256 per warp)
+
+// y[m, n] = bf16(sum_k x[m, k] w[n, k]) for m < MM: warp per column n (grid-strided), lane l
+// adding the chunks l, l + 32, ... of the row in order, then a butterfly over the lanes.
+template <int MM>
+__global__ void __launch_bounds__(kGemvThreads) linear_gemv_kernel(const uint16_t* x, const uint16_t* __restrict__ w,
+                                                                   int N, int K, uint16_t* __restrict__ y) {
+  extern __shared__ uint4 xs[];  // x [MM][K / 8 chunks]
+  const int lane = threadIdx.x & 31;
+  const int nw = gridDim.x * (kGemvThreads / 32);
+  const int kc = K / 8;
+  const uint4* w4 = reinterpret_cast<const uint4*>(w);
+  uint4 wv[kGemvChunks];
+  auto load_pass = [&](int r, int c0) {
+#pragma unroll
+    for (int j = 0; j < kGemvChunks; ++j) {
+      const int c = c0 + lane + 32 * j;
+      wv[j] = c < kc ? w4[static_cast<int64_t>(r) * kc + c] : make_uint4(0, 0, 0, 0);
+    }
+  };
+  int row = blockIdx.x * (kGemvThreads / 32) + (threadIdx.x >> 5);
+  if (row < N) load_pass(row, 0);  // W is no earlier kernel's output: fetched before the wait
+  pdl_wait();
+  pdl_trigger();
+  for (int i = threadIdx.x; i < MM * kc; i += kGemvThreads) xs[i] = reinterpret_cast<const uint4*>(x)[i];
+  __syncthreads();
+  for (; row < N; row += nw) {
+    float acc[MM];
+#pragma unroll
+    for (int m = 0; m < MM; ++m) acc[m] = 0.f;
+    for (int c0 = 0; c0 < kc; c0 += 32 * kGemvChunks) {
+      if (c0 > 0) load_pass(row, c0);
+#pragma unroll
+      for (int j = 0; j < kGemvChunks; ++j) {
+        const int c = c0 + lane + 32 * j;
+        if (c >= kc) break;
+        float f[8];
+        unpack8(wv[j], f);
+#pragma unroll
+        for (int m = 0; m < MM; ++m) {
+          float g[8];
+          unpack8(xs[m * kc + c], g);
+#pragma unroll
+          for (int t = 0; t < 8; ++t) acc[m] = fmaf(f[t], g[t], acc[m]);
+        }
+      }
+    }
+    if (row + nw < N) load_pass(row + nw, 0);  // the next column's loads overlap this one's sums
+#pragma unroll
+    for (int m = 0; m < MM; ++m) {
+      float v = acc[m];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      if (lane == 0) y[static_cast<int64_t>(m) * N + row] = bf16_bits_rne(v);
+    }
+  }
+}
+
+template <int MM>
+cudaError_t launch_gemv(const uint16_t* x, const uint16_t* w, int N, int K, uint16_t* y, cudaStream_t st) {
+  const size_t smem = static_cast<size_t>(MM) * K * 2;
+  int rc = allow_smem(reinterpret_cast<const void*>(linear_gemv_kernel<MM>), smem);
+  if (rc) return cudaErrorInvalidValue;
+  int64_t grid = (static_cast<int64_t>(N) + kGemvThreads / 32 - 1) / (kGemvThreads / 32);
+  if (grid > 4 * sm_count()) grid = 4 * sm_count();
+  return launch_dependent(linear_gemv_kernel<MM>, dim3(static_cast<unsigned>(grid)), dim3(kGemvThreads), smem, st, x, w,
+                          N, K, y);
+}
 
 __global__ void __launch_bounds__(kLinThreads, 1)
     linear_bf16_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap tx, LinArgs a) {
@@ -273,6 +350,17 @@ int qk_linear_bf16(const uint16_t* x, int64_t M, int64_t K, const uint16_t* w, i
   if (!workspace || workspace_bytes < need)
     return set_error(QK_ERR_WORKSPACE, "linear workspace needs %zu bytes, got %zu", need, workspace_bytes);
   QK_REQUIRE((reinterpret_cast<uintptr_t>(workspace) & 255) == 0, "workspace must be 256-byte aligned");
+  if (M <= kGemvMaxM && K <= 16384) {
+    cudaStream_t st = as_stream(stream);
+    const int n = static_cast<int>(N), k = static_cast<int>(K);
+    const cudaError_t e = M == 1   ? launch_gemv<1>(x, w, n, k, y, st)
+                          : M == 2 ? launch_gemv<2>(x, w, n, k, y, st)
+                          : M == 3 ? launch_gemv<3>(x, w, n, k, y, st)
+                                   : launch_gemv<4>(x, w, n, k, y, st);
+    if (e != cudaSuccess) return cuda_error(e, "linear_gemv_kernel");
+    count_launch();
+    return QK_OK;
+  }
   LinArgs a{};
   a.M = static_cast<int>(M);
   a.N = static_cast<int>(N);
