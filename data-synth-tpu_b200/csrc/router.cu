@@ -221,6 +221,30 @@ __global__ void __launch_bounds__(kLogitRows * 32)
   }
 }
 
+// Token t's logits row into shared memory by one warp: all its 16-byte loads are issued
+// before the stores when the row is 16-byte aligned (E % 4 == 0), else one float at a time.
+__device__ __forceinline__ void stage_row(float* row, const float* __restrict__ logits, int t, int E, int lane) {
+  const float* src = logits + static_cast<int64_t>(t) * E;
+  if ((E & 3) == 0 && (reinterpret_cast<uintptr_t>(src) & 15) == 0) {
+    const int n4 = E / 4;
+    for (int i0 = 0; i0 < n4; i0 += 32 * 8) {
+      float4 v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int i = i0 + lane + 32 * j;
+        v[j] = i < n4 ? reinterpret_cast<const float4*>(src)[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int i = i0 + lane + 32 * j;
+        if (i < n4) reinterpret_cast<float4*>(row)[i] = v[j];
+      }
+    }
+  } else {
+    for (int e = lane; e < E; e += 32) row[e] = src[e];
+  }
+}
+
 // Selection from FP32 logits [T, E]: one warp per token, its row staged in shared memory.
 constexpr int kSelectWarps = 8;
 
@@ -234,7 +258,7 @@ __global__ void __launch_bounds__(kSelectWarps * 32)
   const int t = blockIdx.x * kSelectWarps + warp;
   if (t >= T) return;
   float* row = rows + warp * E;
-  for (int e = lane; e < E; e += 32) row[e] = logits[static_cast<int64_t>(t) * E + e];
+  stage_row(row, logits, t, E, lane);
   __syncwarp();
   select_row(row, t, E, k, lane, active, ids, weights, probs_out, k, 0);
 }
@@ -255,7 +279,7 @@ __global__ void __launch_bounds__(kSharedThreads)
   pdl_trigger();
   const int t = blockIdx.x, lane = threadIdx.x & 31;
   if (threadIdx.x < 32)
-    for (int e = lane; e < E; e += 32) row_s[e] = logits[static_cast<int64_t>(t) * E + e];
+    stage_row(row_s, logits, t, E, lane);
   const float dot = row_dot_bf16(h + static_cast<int64_t>(t) * H, wsr, H, red);
   if (threadIdx.x < 32) select_row(row_s, t, E, k, lane, active, ids_out, w_out, nullptr, k + 1, per);
   if (threadIdx.x == 0) {
