@@ -468,11 +468,36 @@ __global__ void __launch_bounds__(kThreads, 1)
   int k = 0;
   for (int sg = s_first; sg <= s_last; ++sg) {
     const int b = sg / a.groups, hg = sg - b * a.groups;
-    // q of the segment's heads: q_s[hl][r][d] (padded blocks), zero rows for r >= a.r
-    for (int i = tid; i < kg * kHeads * HD; i += kAttnWarps * 32) {
-      const int hl = i / (kHeads * HD), r = (i / HD) % kHeads, d = i % HD;
-      q_s[G::qi(hl * kHeads + r, d)] =
-          r < a.r ? a.q[(static_cast<int64_t>(b) * a.hq + (hg * kg + hl) * a.r + r) * HD + d] : 0;
+    // q of the segment's heads: q_s[hl][r][d] (padded blocks), zero rows for r >= a.r. With
+    // an aligned q every thread issues its 16-byte loads (at most 4) before storing any: a
+    // 2-byte load per store put one global round trip per 256 values on every segment start.
+    if ((reinterpret_cast<uintptr_t>(a.q) & 15) == 0) {
+      constexpr int kQChunks = (Geo<HD>::kKgMax * kHeads * HD / 8 + kAttnWarps * 32 - 1) / (kAttnWarps * 32);
+      const int nq = kg * kHeads * HD / 8;
+      uint4 qv[kQChunks];
+#pragma unroll
+      for (int c = 0; c < kQChunks; ++c) {
+        const int i = tid + c * kAttnWarps * 32, e = 8 * i;
+        const int hl = e / (kHeads * HD), r = (e / HD) % kHeads, d = e % HD;
+        qv[c] = i < nq && r < a.r ? *reinterpret_cast<const uint4*>(
+                                        a.q + (static_cast<int64_t>(b) * a.hq + (hg * kg + hl) * a.r + r) * HD + d)
+                                  : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int c = 0; c < kQChunks; ++c) {
+        const int i = tid + c * kAttnWarps * 32, e = 8 * i;
+        if (i >= nq) break;
+        const int hl = e / (kHeads * HD), r = (e / HD) % kHeads, d = e % HD;
+        uint2* dst = reinterpret_cast<uint2*>(q_s + G::qi(hl * kHeads + r, d));  // 8-byte aligned
+        dst[0] = make_uint2(qv[c].x, qv[c].y);
+        dst[1] = make_uint2(qv[c].z, qv[c].w);
+      }
+    } else {
+      for (int i = tid; i < kg * kHeads * HD; i += kAttnWarps * 32) {
+        const int hl = i / (kHeads * HD), r = (i / HD) % kHeads, d = i % HD;
+        q_s[G::qi(hl * kHeads + r, d)] =
+            r < a.r ? a.q[(static_cast<int64_t>(b) * a.hq + (hg * kg + hl) * a.r + r) * HD + d] : 0;
+      }
     }
     const int len = a.valid ? 0 : a.lengths[b];
     consumer_sync();
