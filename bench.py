@@ -428,6 +428,7 @@ def b200_arm(args):
         if dist and sync:
             dist.barrier()
         ms = t0.elapsed_time(t1) / steps
+        fn.check_status()  # every bounded wait of the last timed call completed
         stage_ms = None
         if profile:  # per-kernel times from events recorded between the launches
             acc = [0.0] * 4

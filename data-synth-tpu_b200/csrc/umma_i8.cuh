@@ -220,9 +220,9 @@ __global__ void __launch_bounds__(kI8Threads, 1) umma_i8_down_kernel(const __gri
                    &full[s]);
         }
       }
-      // after a give-up, wait (bounded) for this CTA's copies still in flight before leaving
-      if (!ok)
-        for (uint32_t i = sc > kI8Stages ? sc - kI8Stages : 0; i < sc; ++i)
+      // every copy issued must have landed before the CTA leaves: instant when the consumers
+      // took them all, bounded after a give-up here or in another role
+      for (uint32_t i = sc > kI8Stages ? sc - kI8Stages : 0; i < sc; ++i)
           mbar_wait_bounded(&full[i % kI8Stages], (i / kI8Stages) & 1);
     }
   } else if (warp == 1) {

@@ -464,6 +464,11 @@ __global__ void __launch_bounds__(kPThreads, 1) umma_prefill_kernel(const UArgs 
           }
         }
       }
+      // every copy issued must have landed before the CTA leaves (instant unless another role
+      // gave up a wait; bounded otherwise)
+      if (kc > 0) mbar_wait_bounded(raw_full, (kc - 1) & 1);
+      for (uint32_t t = 0; t < static_cast<uint32_t>(NB) && t < ac; ++t)
+        mbar_wait_bounded(&b_full[t], ((ac - t + NB - 1) / NB - 1) & 1);
     }
   } else if (warp == kPMmaWarp) {
     if (lane == 0) {

@@ -15,6 +15,12 @@
 //               32 (w % 4) .. + 31: it reads its row's half block from the shared-memory
 //               weight ring into registers, frees the slot, decodes 128 values into BF16
 //               and stores them with tcgen05.st into its lane (64 columns).
+//               Each weight slot has a full barrier per group. With an odd number of slots
+//               the uses of a slot alternate between the groups, and a group's previous wait
+//               on one shared barrier would be two phases back: the copy of the other
+//               group's use can still be in flight (copies land out of order), and a parity
+//               wait would then take that incomplete phase for its own completed one. On its
+//               own barrier a group waits on every phase in order.
 //   warp 16     producer: one lane issues, per stage, the activation tile (already in the
 //               128-byte-swizzled K-major layout) and then the two weight tiles as 1-D bulk
 //               copies (TMA engine, no multicast). Issued together they land together: the
@@ -288,6 +294,14 @@ __device__ __forceinline__ void store_y8(const float (&acc)[8], int lane, uint16
   __syncwarp();
 }
 
+// Phase of stage sc on its group's full barrier wfull[2 (sc % SW) + sc % 2]: the number of
+// earlier stages of the same slot and group. With SW even every use of a slot is one group's
+// (use u = sc / SW); with SW odd the uses alternate, and the group's own are every other one.
+template <int SW>
+__device__ __forceinline__ uint32_t wfull_phase(uint32_t sc) {
+  return SW % 2 == 0 ? sc / SW : (sc / SW) >> 1;
+}
+
 template <QType QT, int MODE, bool W = false>
 __global__ void __launch_bounds__(Form<W, MODE>::kThreads, 1) umma_proj_kernel(const UArgs A) {
   using Cfg = UCfg<QT, W>;
@@ -301,13 +315,15 @@ __global__ void __launch_bounds__(Form<W, MODE>::kThreads, 1) umma_proj_kernel(c
   constexpr int DB = Form<W, MODE>::kDBuf;          // accumulator buffers
   constexpr uint32_t kAccCol = Form<W, MODE>::kAccCol;
   constexpr int TB = Cfg::kTile;
-  static_assert((2 * SW + 2 * kXSlots + 4 * AB + 2 * DB) * 8 + kXSlots * 4 + 4 <= 512, "barrier region");
+  static_assert((3 * SW + 2 * kXSlots + 4 * AB + 2 * DB) * 8 + kXSlots * 4 + 4 <= 512, "barrier region");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* xring = smem;
   uint8_t* wring = smem + Cfg::kWOff;
+  // weight slot s: wfull[2 s + g] when the copies of a stage of decode group g have landed
+  // (stage sc is group sc % 2's), wempty[s] when its group has taken it into registers
   uint64_t* wfull = reinterpret_cast<uint64_t*>(smem + Cfg::kBarOff);
-  uint64_t* wempty = wfull + SW;
+  uint64_t* wempty = wfull + 2 * SW;
   uint64_t* xfull = wempty + SW;
   uint64_t* xempty = xfull + kXSlots;
   // A buffer b, half h (values 128 h .. 128 h + 127 of the block): afull[2 b + h] when its
@@ -326,7 +342,8 @@ __global__ void __launch_bounds__(Form<W, MODE>::kThreads, 1) umma_proj_kernel(c
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < SW; ++s) {
-      mbar_init(&wfull[s], 1);
+      mbar_init(&wfull[2 * s], 1);
+      mbar_init(&wfull[2 * s + 1], 1);
       mbar_init(&wempty[s], kDecodeWarps / 2);  // the stage's decode group
     }
     for (int s = 0; s < kXSlots; ++s) {
@@ -399,12 +416,24 @@ __global__ void __launch_bounds__(Form<W, MODE>::kThreads, 1) umma_proj_kernel(c
           mbar_expect_tx(&xfull[j], xbytes);
           bulk_g2s_hint(xring + off * kXGranule, xsrc + static_cast<int64_t>(kb) * xbytes, xbytes, &xfull[j], xpol);
           uint8_t* st = wring + static_cast<size_t>(s) * Cfg::kWStageBytes;
-          mbar_expect_tx(&wfull[s], static_cast<uint32_t>(TB * nt));
-          bulk_g2s_hint(st, w0 + (static_cast<int64_t>(rt0) * A.nkb + kb) * TB, TB, &wfull[s], wpol);
+          uint64_t* wf = &wfull[2 * s + (sc & 1)];
+          mbar_expect_tx(wf, static_cast<uint32_t>(TB * nt));
+          bulk_g2s_hint(st, w0 + (static_cast<int64_t>(rt0) * A.nkb + kb) * TB, TB, wf, wpol);
           if (nt == 2)
-            bulk_g2s_hint(st + Cfg::kTile1, w1 + (static_cast<int64_t>(rt1) * A.nkb + kb) * TB, TB, &wfull[s], wpol);
+            bulk_g2s_hint(st + Cfg::kTile1, w1 + (static_cast<int64_t>(rt1) * A.nkb + kb) * TB, TB, wf, wpol);
         }
       }
+      // Every copy issued must have landed before the CTA leaves: instant when the consumers
+      // took them all, and otherwise (another role gave up a wait) a bounded wait for the last
+      // phase of each slot, so that no copy writes into the shared memory of a CTA that ended.
+      // (Only a slot's last use can be in flight: the one before it was decoded before the
+      // slot was refilled.)
+      for (uint32_t t = 0; t < SW && t < sc; ++t) {
+        const uint32_t last = t + (sc - 1 - t) / SW * SW;
+        mbar_wait_bounded(&wfull[2 * t + (last & 1)], wfull_phase<SW>(last) & 1);
+      }
+      for (uint32_t t = 0; t < kXSlots && t < sc; ++t)
+        mbar_wait_bounded(&xfull[t], ((sc - t + kXSlots - 1) / kXSlots - 1) & 1);
     }
   } else if (warp >= kMmaWarp0 && warp < EW0) {
     if (lane == 0) {
@@ -558,7 +587,7 @@ __global__ void __launch_bounds__(Form<W, MODE>::kThreads, 1) umma_proj_kernel(c
         for (int i = 0; i < it.kb1 - it.kb0; ++i, ++sc) {
           if ((sc & 1) != static_cast<uint32_t>(g)) continue;
           const int s = sc % SW;
-          if (!mbar_wait_bounded(&wfull[s], (sc / SW) & 1)) {
+          if (!mbar_wait_bounded(&wfull[2 * s + g], wfull_phase<SW>(sc) & 1)) {
             ok = false;
             break;
           }
