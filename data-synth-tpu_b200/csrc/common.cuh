@@ -315,27 +315,41 @@ __device__ __forceinline__ void unpack8(const uint4& v, float (&f)[8]) {
 
 // Dot product of a BF16 row of H values with a BF16 vector in the row layout (FP32 fused
 // multiply-adds), rounded to BF16: the shared expert's gate logit bf16(h . wsr)
-// (math.py:282-283). Every thread of the 256-thread block calls it.
-__device__ __forceinline__ float row_dot_bf16(const uint16_t* hrow, const uint16_t* wsr, int H, float* red) {
-  const int nch = H / 8;
+// (math.py:282-283). Every thread of the 256-thread block calls it, or row_dot_load and
+// later row_dot_finish (the loads in flight meanwhile).
+struct RowDot {
   uint4 a[kRowChunks], b[kRowChunks];
+};
+
+__device__ __forceinline__ void row_dot_load(RowDot& r, const uint16_t* hrow, const uint16_t* wsr, int H) {
+  const int nch = H / 8;
 #pragma unroll
   for (int c = 0; c < kRowChunks; ++c) {
     const int i = threadIdx.x + c * kRowBlock;
-    a[c] = i < nch ? reinterpret_cast<const uint4*>(hrow)[i] : make_uint4(0, 0, 0, 0);
-    b[c] = i < nch ? reinterpret_cast<const uint4*>(wsr)[i] : make_uint4(0, 0, 0, 0);
+    r.a[c] = i < nch ? reinterpret_cast<const uint4*>(hrow)[i] : make_uint4(0, 0, 0, 0);
+    r.b[c] = i < nch ? reinterpret_cast<const uint4*>(wsr)[i] : make_uint4(0, 0, 0, 0);
   }
+}
+
+__device__ __forceinline__ float row_dot_finish(const RowDot& r, int H, float* red) {
+  const int nch = H / 8;
   float s = 0.f;
 #pragma unroll
   for (int c = 0; c < kRowChunks; ++c) {
     if (threadIdx.x + c * kRowBlock >= nch) break;
     float f[8], g[8];
-    unpack8(a[c], f);
-    unpack8(b[c], g);
+    unpack8(r.a[c], f);
+    unpack8(r.b[c], g);
 #pragma unroll
     for (int t = 0; t < 8; ++t) s = fmaf(f[t], g[t], s);
   }
   return bf16_round(block_sum(s, red));
+}
+
+__device__ __forceinline__ float row_dot_bf16(const uint16_t* hrow, const uint16_t* wsr, int H, float* red) {
+  RowDot r;
+  row_dot_load(r, hrow, wsr, H);
+  return row_dot_finish(r, H, red);
 }
 
 __device__ __forceinline__ uint4 ld_nc_v4(const void* p) {

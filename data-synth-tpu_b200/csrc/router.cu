@@ -41,12 +41,15 @@ __device__ __forceinline__ void select_row(float* row, int t, int E, int k, int 
   if (probs_out)
     for (int e = lane; e < E; e += 32) probs_out[static_cast<int64_t>(t) * E + e] = row[e];
 
-  // top-k: k rounds of warp argmax; ties go to the lower expert index (lax.top_k).
-  float mine = 0.f;  // lane j keeps the j-th selected probability
-  int mine_id = 0;
-  for (int j = 0; j < k; ++j) {
-    float bv = -INFINITY;
-    int bi = 0x7fffffff;
+  // top-k: k rounds of a warp argmax; ties go to the lower expert index (lax.top_k). Each
+  // lane keeps the best of its own entries e = lane + 32 i. A round takes the warp's maximum
+  // with two reductions (probabilities are >= 0, so their bit patterns order like their
+  // values; taken entries are -1), and only the lane that held the winner rescans.
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+  auto lane_best = [&]() {
+    bv = -INFINITY;
+    bi = 0x7fffffff;
     for (int e = lane; e < E; e += 32) {
       const float v = row[e];
       if (v > bv || (v == bv && e < bi)) {
@@ -54,21 +57,25 @@ __device__ __forceinline__ void select_row(float* row, int t, int E, int k, int 
         bi = e;
       }
     }
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-      if (ov > bv || (ov == bv && oi < bi)) {
-        bv = ov;
-        bi = oi;
-      }
-    }
+  };
+  lane_best();
+  float mine = 0.f;  // lane j keeps the j-th selected probability
+  int mine_id = 0;
+  for (int j = 0; j < k; ++j) {
+    const bool cand = bv >= 0.f;
+    const uint32_t key = cand ? __float_as_uint(bv) : 0u;
+    const uint32_t top = __reduce_max_sync(0xffffffffu, key);
+    const uint32_t id = __reduce_min_sync(0xffffffffu, cand && key == top ? static_cast<uint32_t>(bi) : 0xffffffffu);
     if (lane == j) {
-      mine = bv;
-      mine_id = bi;
+      mine = __uint_as_float(top);
+      mine_id = static_cast<int>(id);
     }
-    if (lane == (bi & 31)) row[bi] = -1.f;  // probabilities are >= 0: excluded from later rounds
-    __syncwarp();
+    if (id < static_cast<uint32_t>(E) && lane == static_cast<int>(id & 31)) {
+      row[id] = -1.f;  // excluded from later rounds
+      lane_best();
+    }
   }
+  __syncwarp();
   // renormalise with a sequential FP32 sum over j (the oracle uses the same order)
   float total = 0.f;
   for (int j = 0; j < k; ++j) total = __fadd_rn(total, __shfl_sync(0xffffffffu, mine, j));
@@ -176,28 +183,48 @@ __global__ void __launch_bounds__(kLogitRows * 32)
     router_logits_kernel(const uint16_t* __restrict__ x, const float* __restrict__ w, int T, int H, int E,
                          float* __restrict__ logits) {
   extern __shared__ __align__(16) uint16_t xs_l[];  // x rows [kTok][H] (BF16)
-  pdl_wait();
-  pdl_trigger();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int t0 = blockIdx.y * kTok, nt = min(kTok, T - t0);
-  const int pieces = nt * H / 8;
-  for (int i = threadIdx.x; i < pieces; i += blockDim.x)
-    reinterpret_cast<uint4*>(xs_l)[i] = reinterpret_cast<const uint4*>(x + static_cast<int64_t>(t0) * H)[i];
-  __syncthreads();
-  const int e = blockIdx.x * kLogitRows + warp;
-  if (e >= E) return;
   constexpr int kU = 16;  // a whole 2048-value row's loads in flight per lane (the order of the sums is the same)
-  float acc[kTok];
-#pragma unroll
-  for (int t = 0; t < kTok; ++t) acc[t] = 0.f;
-  const float* wr = w + static_cast<int64_t>(e) * H;
-  for (int h0 = lane * 4; h0 < H; h0 += 128 * kU) {
-    float4 v[kU];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int e = blockIdx.x * kLogitRows + warp;
+  const float* wr = w + static_cast<int64_t>(e < E ? e : 0) * H;
+  float4 v[kU];
+  auto load_w = [&](int h0) {
 #pragma unroll
     for (int u = 0; u < kU; ++u) {
       const int h = h0 + 128 * u;
       v[u] = h < H ? *reinterpret_cast<const float4*>(wr + h) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
+  };
+  // The router matrix is no earlier kernel's output: its first loads go out before the wait.
+  load_w(lane * 4);
+  pdl_wait();
+  pdl_trigger();
+  const int t0 = blockIdx.y * kTok, nt = min(kTok, T - t0);
+  {
+    // the token rows, 8 loads per thread in flight before the stores
+    const int pieces = nt * H / 8;
+    const uint4* src = reinterpret_cast<const uint4*>(x + static_cast<int64_t>(t0) * H);
+    for (int i0 = 0; i0 < pieces; i0 += kLogitRows * 32 * 8) {
+      uint4 xv[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int i = i0 + threadIdx.x + kLogitRows * 32 * j;
+        xv[j] = i < pieces ? src[i] : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int i = i0 + threadIdx.x + kLogitRows * 32 * j;
+        if (i < pieces) reinterpret_cast<uint4*>(xs_l)[i] = xv[j];
+      }
+    }
+  }
+  __syncthreads();
+  if (e >= E) return;
+  float acc[kTok];
+#pragma unroll
+  for (int t = 0; t < kTok; ++t) acc[t] = 0.f;
+  for (int h0 = lane * 4; h0 < H; h0 += 128 * kU) {
+    if (h0 != lane * 4) load_w(h0);
 #pragma unroll
     for (int u = 0; u < kU; ++u) {
       const int h = h0 + 128 * u;
@@ -278,10 +305,15 @@ __global__ void __launch_bounds__(kSharedThreads)
   pdl_wait();
   pdl_trigger();
   const int t = blockIdx.x, lane = threadIdx.x & 31;
-  if (threadIdx.x < 32)
+  // the shared-expert dot's loads are in flight while warp 0 selects
+  RowDot rd;
+  row_dot_load(rd, h + static_cast<int64_t>(t) * H, wsr, H);
+  if (threadIdx.x < 32) {
     stage_row(row_s, logits, t, E, lane);
-  const float dot = row_dot_bf16(h + static_cast<int64_t>(t) * H, wsr, H, red);
-  if (threadIdx.x < 32) select_row(row_s, t, E, k, lane, active, ids_out, w_out, nullptr, k + 1, per);
+    __syncwarp();
+    select_row(row_s, t, E, k, lane, active, ids_out, w_out, nullptr, k + 1, per);
+  }
+  const float dot = row_dot_finish(rd, H, red);
   if (threadIdx.x == 0) {
     ids_out[static_cast<int64_t>(t) * (k + 1) + k] = shared_id;
     w_out[static_cast<int64_t>(t) * (k + 1) + k] = bf16_bits_rne(sigmoid_ref(dot));
