@@ -124,9 +124,12 @@ int qk_q8_matmul(const uint16_t* x, int64_t M, int64_t K, const uint8_t* w_tiled
  * attention projections call it (attention_cache.py:131-134 q|gate, k, v; :171 out):
  * y = bf16(x @ w^T) with FP32 accumulation. x: BF16 [M, K] (1 <= M <= 256, K a multiple of
  * 64); w: BF16 [N, K]; y: BF16 [M, N]. A tcgen05 pass that streams w once, its K dimension
- * split over the SMs with FP32 partials added in a fixed order. The workspace (256-byte
- * aligned, qk_linear_bf16_workspace_bytes) must be zeroed once before its first call; every
- * call leaves it ready for the next. Calls sharing a workspace must not overlap. */
+ * split over the SMs with FP32 partials added in a fixed order; for 1 <= M <= 4 a GEMV (a warp
+ * per output column, FP32 fused multiply-adds and a butterfly), which checks the workspace
+ * argument but does not touch it. Both are tested against FP64 within one BF16 ulp plus the
+ * FP32 accumulation bound. The workspace (256-byte aligned, qk_linear_bf16_workspace_bytes)
+ * must be zeroed once before its first call; every call leaves it ready for the next. Calls
+ * sharing a workspace must not overlap. */
 size_t qk_linear_bf16_workspace_bytes(int64_t M, int64_t K, int64_t N);
 int qk_linear_bf16(const uint16_t* x, int64_t M, int64_t K, const uint16_t* w, int64_t N,
                    uint16_t* y, void* workspace, size_t workspace_bytes, qk_stream_t stream);
