@@ -19,8 +19,10 @@
 //               the uses of a slot alternate between the groups, and a group's previous wait
 //               on one shared barrier would be two phases back: the copy of the other
 //               group's use can still be in flight (copies land out of order), and a parity
-//               wait would then take that incomplete phase for its own completed one. On its
-//               own barrier a group waits on every phase in order.
+//               wait would then take that incomplete phase for its own completed one. (With
+//               three A buffers only a three-slot ring reaches that: the A-buffer waits order
+//               the other group's use of a five- or seven-slot ring first.) On its own barrier
+//               a group waits on every phase in order, whatever the A buffers order.
 //   warp 16     producer: one lane issues, per stage, the activation tile (already in the
 //               128-byte-swizzled K-major layout) and then the two weight tiles as 1-D bulk
 //               copies (TMA engine, no multicast). Issued together they land together: the
