@@ -17,7 +17,9 @@ full barrier per (slot, decode group), `wfull[2 s + sc % 2]`, waited at phase
 it is caught at ring size 3 with three A buffers, and at 5, 7 and 9 once the A buffers are
 many. (With three, a group's A-buffer wait at stage sc - 2 needs the MMA of sc - 5 and so
 the other group's decode of it: from five slots up that orders the slot's previous copy
-before the group's next use, which is why only the three-slot rings could alias.)"""
+before the group's next use, which is why only the three-slot rings could alias.) A second
+model runs the kernel's full form: a decode warp per actor, per-half A-buffer barriers with
+the kernel's arrival counts, and one, two or four MMA issuers with their own commits."""
 
 import random
 
@@ -152,6 +154,86 @@ def test_one_full_barrier_per_slot_holds_where_the_uses_are_ordered(sw, ab):
     # three A buffers order the stages from five slots up; an even ring gives every use of a
     # slot to one group
     assert _caught(sw, ab, seeds=60) == 0
+
+
+def run_kernel_model(sw, ab, ni, stages, seed, warps_per_half=2, plant=None):
+    """The kernel's full form: every decode warp its own actor (group g = sc % 2, half h of the
+    block), per-half A-buffer barriers afull / aempty[2 b + h] with the kernel's counts (the
+    half's warps; the commits of the ni / 2 issuers whose K atoms lie in that half, or 1),
+    and ni MMA issuers, each with its own in-order commits."""
+    rng = random.Random(seed)
+    wfull = [Bar(f"wfull[{i}]", 1) for i in range(2 * sw)]
+    wempty = [Bar(f"wempty[{s}]", 2 * warps_per_half) for s in range(sw)]
+    afull_count = 2 * warps_per_half if plant == "afull_whole_group" else warps_per_half
+    aempty_count = ni if plant == "aempty_all_issuers" else (ni // 2 if ni >= 2 else 1)
+    afull = [Bar(f"afull[{i}]", afull_count) for i in range(2 * ab)]
+    aempty = [Bar(f"aempty[{i}]", aempty_count) for i in range(2 * ab)]
+    atoms = 16 // ni // 4  # 64-value K atoms per issuer
+    copies, commits = [], [[] for _ in range(ni)]
+
+    def producer():
+        for sc in range(stages):
+            s = sc % sw
+            if sc >= sw:
+                yield lambda b=wempty[s], k=sc // sw - 1: b.passes(k)
+            bar = wfull[2 * s + (sc & 1)]
+            bar.expect_tx(2)
+            copies.extend([bar, bar])
+
+    def decode_warp(g, h):
+        for sc in range(g, stages, 2):
+            s, b = sc % sw, sc % ab
+            yield lambda bar=wfull[2 * s + g], k=wfull_phase(sw, sc): bar.passes(k)
+            wempty[s].arrive()
+            if sc >= ab:
+                yield lambda bb=aempty[2 * b + h], k=sc // ab - 1: bb.passes(k)
+            afull[2 * b + h].arrive()
+
+    def issuer(mi):
+        h0, h1 = (mi * atoms) // 2, (mi * atoms + atoms - 1) // 2
+        for sc in range(stages):
+            b = sc % ab
+            yield lambda bb=afull[2 * b + h0], k=sc // ab: bb.passes(k)
+            if h1 != h0:
+                yield lambda bb=afull[2 * b + h1], k=sc // ab: bb.passes(k)
+            commits[mi].append(aempty[2 * b + h0])
+            if h1 != h0:
+                commits[mi].append(aempty[2 * b + h1])
+
+    actors = [producer()]
+    actors += [decode_warp(g, h) for g in range(2) for h in range(2) for _ in range(warps_per_half)]
+    actors += [issuer(mi) for mi in range(ni)]
+    conds = [next(a, None) for a in actors]
+    while True:
+        runnable = [i for i, c in enumerate(conds) if c is not None and c()]
+        choices = runnable + (["copy"] if copies else []) + [("commit", m) for m in range(ni) if commits[m]]
+        if not choices:
+            if any(c is not None for c in conds):
+                raise Alias("deadlock: every actor waits and nothing is in flight")
+            return
+        pick = rng.choice(choices)
+        if pick == "copy":
+            copies.pop(rng.randrange(len(copies))).complete_tx(1)
+        elif isinstance(pick, tuple):
+            commits[pick[1]].pop(0).arrive()
+        else:
+            conds[pick] = next(actors[pick], None)
+
+
+@pytest.mark.parametrize("ni", [1, 2, 4])
+@pytest.mark.parametrize("sw", [3, 4, 5, 6, 7, 8])
+def test_kernel_form_with_per_half_a_buffers_and_several_issuers(sw, ni):
+    # ni = 4: the narrow gate/up pass; 2: the narrow down pass; 1: the wide form
+    for seed in range(12):
+        run_kernel_model(sw, ab=3, ni=ni, stages=36, seed=seed)
+
+
+@pytest.mark.parametrize("plant,ni", [("afull_whole_group", 4), ("aempty_all_issuers", 4),
+                                      ("aempty_all_issuers", 2)])
+def test_kernel_model_catches_wrong_per_half_counts(plant, ni):
+    # the counts of one barrier per whole A buffer, planted on the per-half barriers
+    with pytest.raises(Alias):
+        run_kernel_model(6, ab=3, ni=ni, stages=36, seed=0, plant=plant)
 
 
 @pytest.mark.parametrize("sw", range(2, 10))
